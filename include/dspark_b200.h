@@ -1,0 +1,244 @@
+/*
+ * dspark_b200.h — C ABI of libdspark_b200.so, the sm_100a kernels under the speculative
+ * verify step of mlx-dspark (Qwen3 targets with W8 affine group-64 weights, DSpark and
+ * DFlash drafters).
+ *
+ * Conventions shared by every entry point:
+ *   - Pointers are device pointers unless a parameter says "host". Shapes are explicit
+ *     ints; leading dimensions are in elements. No torch types cross this boundary.
+ *   - Calls are stream-ordered and asynchronous; nothing is allocated inside the library.
+ *     Scratch memory is passed in by the caller (sizes from the *_workspace_bytes queries).
+ *   - The return value is a status code (DSPARK_OK = 0). On failure the thread-local
+ *     message from dspark_last_error() says what was wrong.
+ *   - Kernels that wait on the device (pipeline barriers, grid barriers) give up after a
+ *     bounded time and write DSPARK_ERR_TIMEOUT into the caller's device status word
+ *     (`int* status`, may be NULL); the host reads it at its next synchronisation point.
+ *
+ * Reference interfaces replaced (paths inside regeter/mlx-dspark):
+ *   the mlx-lm Qwen3 forward called by src/mlx_dspark/target.py:58-75 and
+ *   src/mlx_dspark/batch_engine.py:184-206; the DSpark drafter src/mlx_dspark/model.py:241-437;
+ *   the DFlash drafter src/mlx_dspark/dflash_model.py:100-208; greedy acceptance
+ *   src/mlx_dspark/generate.py:905-921 and batch_engine.py:573-595; speculative-sampling
+ *   acceptance src/mlx_dspark/generate.py:659-688 with src/mlx_dspark/sampling.py:18-49.
+ */
+#ifndef DSPARK_B200_H_
+#define DSPARK_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+/* opaque stream handle (a cudaStream_t); NULL means the legacy default stream */
+typedef void* dspark_stream_t;
+
+enum {
+  DSPARK_OK = 0,
+  DSPARK_ERR_INVALID = 1,     /* bad shape, pointer or argument */
+  DSPARK_ERR_ALIGN = 2,       /* pointer or leading dimension not aligned as required */
+  DSPARK_ERR_LAUNCH = 3,      /* kernel launch failed */
+  DSPARK_ERR_TIMEOUT = 4,     /* a bounded device-side wait gave up */
+  DSPARK_ERR_UNSUPPORTED = 5, /* configuration not compiled in */
+  DSPARK_ERR_CUDA = 6,        /* CUDA runtime / driver call failed */
+  DSPARK_ERR_WORKSPACE = 7    /* workspace missing or too small */
+};
+
+/* W8A16 GEMM epilogues */
+enum {
+  DSPARK_EPI_STORE_BF16 = 0,    /* y[m,n] = bf16(acc)                                      */
+  DSPARK_EPI_RESIDUAL_BF16 = 1, /* y[m,n] = bf16(r[m,n] + bf16(acc)); y may alias r          */
+  DSPARK_EPI_SILU_MUL_F16 = 2,  /* gate/up interleaved in 64-row halves of each 128-row tile;
+                                   y[m,j] = fp16(bf16(bf16(silu(g)) * u)), y has N/2 columns */
+  DSPARK_EPI_STORE_F32 = 3      /* y[m,n] = acc (fp32)                                       */
+};
+
+/* library identity */
+int dspark_version(void);
+const char* dspark_last_error(void);
+
+/* -------------------------------------------------------------------------------------
+ * K1 — W8A16 group-64 dequant GEMM for the small-M verify shape.
+ * Replaces: mlx nn.QuantizedLinear (bits 8, group 64, affine) inside the mlx-lm Qwen3
+ * layers (called from src/mlx_dspark/target.py:67, batch_engine.py:200) and the drafter's
+ * quantized linears (src/mlx_dspark/load.py:204-206).
+ *
+ *   Y[M,N] = X[M,K] . W[N,K]^T,   W[n,k] = scale[n,k/64] * q[n,k] + bias[n,k/64]
+ *
+ * x   : fp16 [M, ldx] activations (bf16-rounded values stored as fp16, |x| < 65504)
+ * wq  : uint8 [N, K] row-major
+ * wsb : uint32 [K/64, N]; low half = fp16 scale, high half = fp16 bias of group (n, g)
+ * M <= 64, N % 128 == 0, K % 128 == 0, ldx % 8 == 0, 16-byte aligned x / wq / wsb.
+ * workspace: dspark_w8a16_gemm_workspace_bytes(M, N, K) bytes, zero-filled once before the
+ * first call; every call leaves its counter words at zero again.
+ * ------------------------------------------------------------------------------------- */
+size_t dspark_w8a16_gemm_workspace_bytes(int M, int N, int K);
+int dspark_w8a16_gemm(const void* x, int ldx, const uint8_t* wq, const uint32_t* wsb, int M,
+                      int N, int K, void* y, int ldy, const void* residual, int ldr, int epilogue,
+                      void* workspace, size_t workspace_bytes, int* status,
+                      dspark_stream_t stream);
+
+/* -------------------------------------------------------------------------------------
+ * K13 — embedding dequant-gather. Replaces mlx QuantizedEmbedding (embed_tokens,
+ * src/mlx_dspark/target.py:63; drafter embed src/mlx_dspark/model.py:372-373).
+ *   out[m, :] = bf16(scale * q[ids[m], :] + bias) * embed_scale (embed_scale 1 for Qwen3)
+ * ids is a device array of M token ids (read on the device, so the call can sit in a
+ * CUDA graph whose ids change between replays).
+ * ------------------------------------------------------------------------------------- */
+int dspark_embed_w8(const int32_t* ids, int M, const uint8_t* wq, const uint32_t* wsb, int V,
+                    int H, void* out, int ldo, dspark_stream_t stream);
+
+/* -------------------------------------------------------------------------------------
+ * K6 — RMSNorm over rows, mlx.fast.rms_norm semantics (fp32 math, one bf16 rounding).
+ * Replaces the input/post-attention/final norms of the Qwen3 layers and the drafter's
+ * hidden_norm / norm (src/mlx_dspark/model.py:375-376,386-390).
+ *   y = bf16(x * rsqrt(mean(x^2) + eps) * w). y_bf16 and y_f16 (bf16 value stored as fp16,
+ *   the GEMM input format) are both optional.
+ * ------------------------------------------------------------------------------------- */
+int dspark_rmsnorm(const void* x, int ldx, const void* w, int M, int H, float eps, void* y_bf16,
+                   int ldy, void* y_f16, int ldy16, dspark_stream_t stream);
+
+/* paged KV cache layout of one layer.
+ * Page p holds `page_size` tokens of every kv head:
+ *   bf16 pages: K[Hkv][page_size][head_dim] bf16 then V[Hkv][page_size][head_dim] bf16
+ *   8-bit pages: Kq[Hkv][page_size][head_dim] u8, Vq[...] u8, then
+ *                Ksb[Hkv][page_size][head_dim/64] u32, Vsb[...] u32 (bf16 scale | bf16 bias<<16)
+ * block_table[b * max_pages + i] = physical page of token positions [i*page_size, ...). */
+typedef struct dspark_kv_layout {
+  void* pool;                 /* this layer's page pool */
+  const int32_t* block_table; /* [batch, max_pages] */
+  int max_pages;
+  int page_size;
+  int num_kv_heads;
+  int head_dim;
+  int kv8;                    /* 0 = bf16 pages, 1 = 8-bit affine group-64 pages */
+  int reserved;
+  long long page_bytes;       /* bytes per page (the stride between pages) */
+} dspark_kv_layout;
+
+long long dspark_kv_page_bytes(int page_size, int num_kv_heads, int head_dim, int kv8);
+
+/* -------------------------------------------------------------------------------------
+ * K6+K7+K3 — per-head q/k RMSNorm, non-interleaved RoPE at per-row positions, and the
+ * write of the new K/V rows into the paged cache (quantize-on-write for 8-bit pages).
+ * Replaces: Qwen3 attention pre-SDPA (mlx-lm qwen3; q_norm/k_norm then rope at
+ * cache.offset) with KVCache.update_and_fetch / QuantizedKVCache (target.py:44-46),
+ * BatchCache.update_and_fetch (batch_engine.py:132-147), DSparkAttention._kv/update_ctx
+ * (model.py:241-256).
+ *
+ * qkv  : bf16 [B*T, ldqkv]; columns [0, Hq*hd) = q, then Hkv*hd of k, then Hkv*hd of v
+ *        (Hq may be 0: then only k and v are present)
+ * pos0 : [B] device array; token t of row b sits at position pos0[b] + t, and its K/V go
+ *        to that position in the paged cache
+ * inv_freq : fp32 [hd/2] device array, theta^(-2i/hd)
+ * q_out: bf16 [B*T, Hq*hd] (ignored when Hq == 0)
+ * ------------------------------------------------------------------------------------- */
+int dspark_qkv_rope_kv_write(const void* qkv, int ldqkv, int B, int T, int Hq, int Hkv, int hd,
+                             const void* q_norm_w, const void* k_norm_w, float eps,
+                             const float* inv_freq, const int32_t* pos0, void* q_out,
+                             const dspark_kv_layout* kv, dspark_stream_t stream);
+
+/* -------------------------------------------------------------------------------------
+ * K2/K4/K5 — GQA attention of T block queries per row over the paged cache, split-KV with
+ * an in-kernel last-arriver combine. Keys of row b are positions [0, kv_len[b] + T).
+ *   causal = 1: query t sees keys j <= kv_len[b] + t   (target verify, mlx-lm mask /
+ *               build_batch_mask batch_engine.py:170-178)
+ *   causal = 0: every query sees every key              (drafter block attention,
+ *               model.py:258-283, dflash_model.py:100-134)
+ * q   : bf16 [B*T, Hq*hd]; out: fp16 [B*T, ldo] (bf16-rounded, the o_proj GEMM input)
+ * workspace: dspark_attention_workspace_bytes(...), zero-filled once before first use.
+ * ------------------------------------------------------------------------------------- */
+size_t dspark_attention_workspace_bytes(int B, int T, int Hq, int Hkv, int hd, int max_splits);
+int dspark_attention(const void* q, int B, int T, int Hq, const dspark_kv_layout* kv,
+                     const int32_t* kv_len, int causal, float scale, void* out, int ldo,
+                     int max_splits, void* workspace, size_t workspace_bytes, int* status,
+                     dspark_stream_t stream);
+
+/* -------------------------------------------------------------------------------------
+ * K8 — fused greedy acceptance. Row-wise argmax of bf16 logits (first index on ties, the
+ * mx.argmax rule), accepted-prefix length n, bonus token, and the in-place KV commit /
+ * rollback (kv_len[b] += n + 1; the rejected tail is dropped by the length alone).
+ * Replaces src/mlx_dspark/generate.py:910-933 and batch_engine.py:573-595.
+ *
+ * logits   : bf16 [B*T, ld]; verify_ids: [B, T] (column 0 = pending, then the T-1 drafts)
+ * argmax   : out [B*T] argmax per row
+ * kv_len   : [B] in/out (updated only when commit != 0)
+ * pending  : out [B] next pending token (= committed[n])
+ * plan     : out [B, T + 2]: {n, count, committed tokens...}; count = n + 1
+ * workspace: dspark_accept_workspace_bytes(B*T, V), zero-filled once before first use.
+ * ------------------------------------------------------------------------------------- */
+size_t dspark_accept_workspace_bytes(int rows, int V);
+int dspark_accept_greedy(const void* logits, int ld, int B, int T, int V,
+                         const int32_t* verify_ids, int32_t* argmax, int32_t* kv_len,
+                         int commit, int32_t* pending, int32_t* plan, void* workspace,
+                         size_t workspace_bytes, dspark_stream_t stream);
+
+/* -------------------------------------------------------------------------------------
+ * K10 — DSpark Markov head + greedy block sampling: sequential over cap positions,
+ *   logits_i = base_i + w2 . w1[prev];  prev = argmax(logits_i)   (first index on ties)
+ * Replaces DSparkDrafter.sample_block (src/mlx_dspark/model.py:398-409) and the batched
+ * _batched_sample_block (batch_engine.py:414-428).
+ * base : bf16 base logits; position i of row b is row (b * rows_per_b + i), i < cap
+ * first_prev: [B] (the pending token of each row)
+ * w1   : W8 [V, R] Markov embedding, w2: W8 [V, R] (rank R = 256)
+ * draft: out [B, cap]; verify_ids (optional): out [B, cap+1] = {first_prev, draft...}
+ * workspace: dspark_markov_workspace_bytes(B, V), zero-filled once before first use.
+ * ------------------------------------------------------------------------------------- */
+size_t dspark_markov_workspace_bytes(int B, int V);
+int dspark_markov_sample_block(const void* base, int ld, int rows_per_b, int B, int cap, int V,
+                               int R,
+                               const uint8_t* w1q, const uint32_t* w1sb, const uint8_t* w2q,
+                               const uint32_t* w2sb, const int32_t* first_prev, int32_t* draft,
+                               int32_t* verify_ids, void* workspace, size_t workspace_bytes,
+                               int* status, dspark_stream_t stream);
+
+/* -------------------------------------------------------------------------------------
+ * Length-only commit: len_a[b] += plan[b*plan_stride + 1] (and len_b, if given). Used after
+ * the drafter context update so both consumers read the pre-commit length first.
+ * Replaces the trims of src/mlx_dspark/generate.py:929-938 (target KV) and the
+ * n_cached bookkeeping of :938.
+ * ------------------------------------------------------------------------------------- */
+int dspark_commit_lengths(const int32_t* plan, int plan_stride, int B, int32_t* len_a,
+                          int32_t* len_b, dspark_stream_t stream);
+
+/* -------------------------------------------------------------------------------------
+ * Benchmark draft override (BASELINE configs with a Bernoulli(0.7) agree mask): draft slot i
+ * of row b becomes ref[b][j] where agree[b][round][i] != 0, else (ref[b][j] + 1) mod V, with
+ * j = kv_len[b] - prompt_len[b] + 1 + i; round_ctr[b] is incremented on the device.
+ * No reference counterpart (benchmark harness only); writes verify_ids[b, 1 + i].
+ * ------------------------------------------------------------------------------------- */
+int dspark_draft_override(int B, int cap, int V, const int32_t* ref, int ref_len,
+                          const uint8_t* agree, int rounds, int32_t* round_ctr,
+                          const int32_t* kv_len, const int32_t* prompt_len, int32_t* verify_ids,
+                          dspark_stream_t stream);
+
+/* drafter block embedding: row b*k + i embeds pending[b] if i == 0 else mask_id
+ * (src/mlx_dspark/generate.py:848-849, batch_engine.py:548-549); ids_out optional [B*k] */
+int dspark_embed_block_w8(const int32_t* pending, int B, int k, int mask_id, const uint8_t* wq,
+                          const uint32_t* wsb, int V, int H, void* out, int ldo, int32_t* ids_out,
+                          dspark_stream_t stream);
+
+/* bf16 -> fp16 copy of a [rows, cols] block: the target hidden-state tap written into the
+ * fp16 fused-context GEMM input (src/mlx_dspark/target.py:66-69,75) */
+int dspark_bf16_to_f16(const void* src, int lds, void* dst, int ldd, int rows, int cols,
+                       dspark_stream_t stream);
+
+/* diagnostic: the W8A16 product on CUDA cores (fp32 dequant); epilogues 0, 1, 3 only */
+int dspark_w8a16_gemm_simt(const void* x, int ldx, const uint8_t* wq, const uint32_t* wsb, int M,
+                           int N, int K, void* y, int ldy, const void* residual, int ldr,
+                           int epilogue, dspark_stream_t stream);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DSPARK_B200_H_ */

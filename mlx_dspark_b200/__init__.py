@@ -1,0 +1,20 @@
+"""mlx_dspark_b200 — the speculative verify step of mlx-dspark on B200 (sm_100a).
+
+PyTorch on the host drives hand-written sm_100a kernels through the C ABI of
+libdspark_b200.so (include/dspark_b200.h): W8A16 tcgen05 GEMMs, paged GQA attention,
+fused greedy acceptance with in-place KV commit, and the DSpark drafter. The public names
+follow the reference package (src/mlx_dspark/__init__.py:54-116).
+"""
+__version__ = "0.1.0"
+
+from .config import DFlashConfig, DSparkConfig, TargetConfig, WORKLOADS, TARGETS
+from .generate import GenResult, greedy_generate, speculative_generate
+from .load import load_drafter, load_pair, load_target
+from .model import DSparkDrafter
+from .target import Target
+
+__all__ = [
+    "DSparkConfig", "DFlashConfig", "TargetConfig", "Target", "DSparkDrafter",
+    "load_drafter", "load_target", "load_pair", "speculative_generate", "greedy_generate",
+    "GenResult", "WORKLOADS", "TARGETS",
+]

@@ -1,0 +1,92 @@
+"""ctypes binding of libdspark_b200.so (the C ABI declared in include/dspark_b200.h).
+
+The library is required: there is no CPU or PyTorch fallback. Importing this module
+without the built library raises with the build command to run.
+"""
+from __future__ import annotations
+
+import ctypes
+from ctypes import POINTER, c_float, c_int, c_longlong, c_size_t, c_void_p, c_char_p
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().with_name("libdspark_b200.so")
+
+DSPARK_OK = 0
+ERR_NAMES = {1: "invalid argument", 2: "alignment", 3: "launch failed", 4: "device wait timed out",
+             5: "unsupported", 6: "CUDA error", 7: "workspace"}
+
+EPI_STORE_BF16, EPI_RESIDUAL_BF16, EPI_SILU_MUL_F16, EPI_STORE_F32 = 0, 1, 2, 3
+
+
+class DsparkError(RuntimeError):
+    def __init__(self, what: str, code: int, msg: str):
+        super().__init__(f"{what}: {ERR_NAMES.get(code, code)}: {msg}")
+        self.code = code
+
+
+class KvLayout(ctypes.Structure):
+    """dspark_kv_layout"""
+    _fields_ = [("pool", c_void_p), ("block_table", c_void_p), ("max_pages", c_int),
+                ("page_size", c_int), ("num_kv_heads", c_int), ("head_dim", c_int),
+                ("kv8", c_int), ("reserved", c_int), ("page_bytes", c_longlong)]
+
+
+P = c_void_p
+I = c_int
+# name -> (restype, argtypes); mirrors include/dspark_b200.h
+SIGNATURES = {
+    "dspark_version": (I, []),
+    "dspark_last_error": (c_char_p, []),
+    "dspark_w8a16_gemm_workspace_bytes": (c_size_t, [I, I, I]),
+    "dspark_w8a16_gemm": (I, [P, I, P, P, I, I, I, P, I, P, I, I, P, c_size_t, P, P]),
+    "dspark_w8a16_gemm_simt": (I, [P, I, P, P, I, I, I, P, I, P, I, I, P]),
+    "dspark_embed_w8": (I, [P, I, P, P, I, I, P, I, P]),
+    "dspark_embed_block_w8": (I, [P, I, I, I, P, P, I, I, P, I, P, P]),
+    "dspark_rmsnorm": (I, [P, I, P, I, I, c_float, P, I, P, I, P]),
+    "dspark_kv_page_bytes": (c_longlong, [I, I, I, I]),
+    "dspark_qkv_rope_kv_write": (I, [P, I, I, I, I, I, I, P, P, c_float, P, P, P,
+                                     POINTER(KvLayout), P]),
+    "dspark_attention_workspace_bytes": (c_size_t, [I, I, I, I, I, I]),
+    "dspark_attention": (I, [P, I, I, I, POINTER(KvLayout), P, I, c_float, P, I, I, P,
+                             c_size_t, P, P]),
+    "dspark_accept_workspace_bytes": (c_size_t, [I, I]),
+    "dspark_accept_greedy": (I, [P, I, I, I, I, P, P, P, I, P, P, P, c_size_t, P]),
+    "dspark_commit_lengths": (I, [P, I, I, P, P, P]),
+    "dspark_draft_override": (I, [I, I, I, P, I, P, I, P, P, P, P, P]),
+    "dspark_markov_workspace_bytes": (c_size_t, [I, I]),
+    "dspark_markov_sample_block": (I, [P, I, I, I, I, I, I, P, P, P, P, P, P, P, P, c_size_t, P, P]),
+    "dspark_bf16_to_f16": (I, [P, I, P, I, I, I, P]),
+}
+
+_lib = None
+
+
+def lib():
+    """Load the library once and attach the signatures."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise RuntimeError(f"{LIB_PATH.name} is not built; run `python -m mlx_dspark_b200.build` "
+                           f"(there is no fallback path)")
+    L = ctypes.CDLL(str(LIB_PATH))
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+def check(rc: int, what: str) -> None:
+    if rc != DSPARK_OK:
+        msg = lib().dspark_last_error()
+        raise DsparkError(what, rc, msg.decode() if msg else "")
+
+
+def call(name: str, *args) -> None:
+    check(getattr(lib(), name)(*args), name)
+
+
+def exported_symbols() -> list[str]:
+    return list(SIGNATURES)

@@ -1,0 +1,211 @@
+// K8 — greedy acceptance fused with the row argmax, and the length-only KV commit.
+//
+// Reference semantics (src/mlx_dspark/generate.py:910-933, batch_engine.py:573-595):
+//   tt = argmax(v_logits)  (mx.argmax: first index of the maximum)
+//   n  = sum(cumprod(draft == tt[:cap]))
+//   committed = draft[:n] + [tt[n]];  cache.trim(len(draft) - n)
+// The verify block already wrote K/V for all T positions; keeping n + 1 of them is a length
+// update (kv_len += n + 1), so commit and rollback are O(1) on the device.
+#include "common.cuh"
+
+namespace dspark {
+namespace acc {
+
+constexpr int kThreads = 256;
+
+struct Best {
+  float v;
+  int i;
+};
+__device__ __forceinline__ Best better(Best a, Best b) {
+  // larger value wins; equal values: smaller index (first occurrence)
+  if (b.v > a.v || (b.v == a.v && b.i < a.i)) return b;
+  return a;
+}
+__device__ __forceinline__ Best warp_best(Best x) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    Best y;
+    y.v = __shfl_xor_sync(0xffffffffu, x.v, o);
+    y.i = __shfl_xor_sync(0xffffffffu, x.i, o);
+    x = better(x, y);
+  }
+  return x;
+}
+
+// Each CTA scans a contiguous vocabulary slice of every row; the last CTA to finish
+// reduces the per-CTA partials (in CTA order) and runs the acceptance.
+__global__ void __launch_bounds__(kThreads) accept_greedy_kernel(
+    const __nv_bfloat16* __restrict__ logits, int ld, int B, int T, int V,
+    const int32_t* __restrict__ verify_ids, int32_t* __restrict__ argmax_out,
+    int32_t* __restrict__ kv_len, int commit, int32_t* __restrict__ pending,
+    int32_t* __restrict__ plan, float* __restrict__ part_v, int* __restrict__ part_i,
+    int* __restrict__ counter) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int rows = B * T;
+  const int chunk = ((V + gridDim.x - 1) / gridDim.x + 7) & ~7;
+  const int v0 = blockIdx.x * chunk;
+  const int v1 = min(V, v0 + chunk);
+  __shared__ Best red[kThreads / 32];
+  __shared__ int is_last;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int r = 0; r < rows; ++r) {
+    const __nv_bfloat16* row = logits + (size_t)r * ld;
+    Best b{-INFINITY, 0x7fffffff};
+    for (int v = v0 + threadIdx.x * 8; v < v1; v += kThreads * 8) {
+      if (v + 8 <= v1 && ((ld & 7) == 0)) {
+        const uint4 u = *reinterpret_cast<const uint4*>(row + v);
+        const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) b = better(b, Best{__bfloat162float(e[j]), v + j});
+      } else {
+        for (int j = v; j < min(v + 8, v1); ++j) b = better(b, Best{__bfloat162float(row[j]), j});
+      }
+    }
+    b = warp_best(b);
+    if (lane == 0) red[warp] = b;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      Best t = red[0];
+      for (int w = 1; w < kThreads / 32; ++w) t = better(t, red[w]);
+      part_v[(size_t)blockIdx.x * rows + r] = t.v;
+      part_i[(size_t)blockIdx.x * rows + r] = t.i;
+    }
+    __syncthreads();
+  }
+  __threadfence();
+  if (threadIdx.x == 0) is_last = (atomicAdd(counter, 1) == (int)gridDim.x - 1);
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  __shared__ int tt[64];
+  for (int r = threadIdx.x; r < rows; r += kThreads) {
+    Best t{-INFINITY, 0x7fffffff};
+    for (int c = 0; c < (int)gridDim.x; ++c)
+      t = better(t, Best{__ldcg(part_v + (size_t)c * rows + r), __ldcg(part_i + (size_t)c * rows + r)});
+    if (t.i == 0x7fffffff) t.i = 0;  // all-NaN row
+    tt[r] = t.i;
+    argmax_out[r] = t.i;
+  }
+  __syncthreads();
+  for (int b = threadIdx.x; b < B; b += kThreads) {
+    int n = 0;
+    while (n < T - 1 && verify_ids[b * T + n + 1] == tt[b * T + n]) ++n;
+    int32_t* pl = plan + (size_t)b * (T + 2);
+    pl[0] = n;
+    pl[1] = n + 1;
+    for (int i = 0; i < n; ++i) pl[2 + i] = verify_ids[b * T + i + 1];
+    pl[2 + n] = tt[b * T + n];
+    for (int i = n + 1; i < T; ++i) pl[2 + i] = -1;
+    pending[b] = tt[b * T + n];
+    if (commit) kv_len[b] += n + 1;
+  }
+  if (threadIdx.x == 0) *counter = 0;
+}
+
+// kv_len[b] += plan[b * stride + 1] for every length array given
+__global__ void commit_lengths_kernel(const int32_t* __restrict__ plan, int stride, int B,
+                                      int32_t* __restrict__ a, int32_t* __restrict__ b2) {
+  pdl_wait();
+  pdl_launch_dependents();
+  for (int b = threadIdx.x; b < B; b += blockDim.x) {
+    const int add = plan[(size_t)b * stride + 1];
+    if (a) a[b] += add;
+    if (b2) b2[b] += add;
+  }
+}
+
+// Benchmark draft override (greedy configs with a Bernoulli agree mask): draft position i of
+// row b proposes ref[b][j] when agree[b][round][i] is set, else (ref[b][j] + 1) mod V, where
+// j = kv_len[b] - prompt_len[b] + 1 + i indexes the row's reference greedy continuation.
+__global__ void draft_override_kernel(int B, int cap, int V, const int32_t* __restrict__ ref,
+                                      int ref_len, const uint8_t* __restrict__ agree,
+                                      int rounds, const int32_t* __restrict__ round_ctr,
+                                      const int32_t* __restrict__ kv_len,
+                                      const int32_t* __restrict__ prompt_len,
+                                      int32_t* __restrict__ verify_ids) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int b = blockIdx.x;
+  const int rnd = min(round_ctr[b], rounds - 1);
+  for (int i = threadIdx.x; i < cap; i += blockDim.x) {
+    int j = kv_len[b] - prompt_len[b] + 1 + i;
+    j = j < 0 ? 0 : (j >= ref_len ? ref_len - 1 : j);
+    const int g = ref[(size_t)b * ref_len + j];
+    const bool ok = agree[((size_t)b * rounds + rnd) * cap + i] != 0;
+    verify_ids[(size_t)b * (cap + 1) + 1 + i] = ok ? g : (g + 1) % V;
+  }
+}
+
+__global__ void bump_kernel(int32_t* __restrict__ ctr, int B) {
+  pdl_wait();
+  pdl_launch_dependents();
+  for (int b = threadIdx.x; b < B; b += blockDim.x) ctr[b] += 1;
+}
+
+static size_t ws(int rows, int V, int* grid_out, size_t* off_i, size_t* off_c) {
+  int grid = 148;
+  if (V / grid < 1024) grid = (V + 1023) / 1024;
+  if (grid < 1) grid = 1;
+  if (grid_out) *grid_out = grid;
+  // counter word first (fixed offset for every shape), then the two partial arrays
+  const size_t pv = (((size_t)grid * rows * 4) + 255) & ~(size_t)255;
+  if (off_c) *off_c = 256;
+  if (off_i) *off_i = 256 + pv;
+  return 256 + 2 * pv;
+}
+
+}  // namespace acc
+}  // namespace dspark
+
+using namespace dspark;
+
+extern "C" size_t dspark_accept_workspace_bytes(int rows, int V) {
+  if (rows <= 0 || V <= 0) return 0;
+  return acc::ws(rows, V, nullptr, nullptr, nullptr);
+}
+
+extern "C" int dspark_accept_greedy(const void* logits, int ld, int B, int T, int V,
+                                    const int32_t* verify_ids, int32_t* argmax, int32_t* kv_len,
+                                    int commit, int32_t* pending, int32_t* plan, void* workspace,
+                                    size_t workspace_bytes, dspark_stream_t stream) {
+  if (!logits || !verify_ids || !argmax || !pending || !plan || B <= 0 || T <= 0 || V <= 0 || ld < V)
+    return set_error(DSPARK_ERR_INVALID, "accept_greedy: bad arguments");
+  if (commit && !kv_len) return set_error(DSPARK_ERR_INVALID, "accept_greedy: commit without kv_len");
+  if (B * T > 64) return set_error(DSPARK_ERR_UNSUPPORTED, "accept_greedy: more than 64 rows");
+  int grid;
+  size_t off_i, off_c;
+  const size_t need = acc::ws(B * T, V, &grid, &off_i, &off_c);
+  if (!workspace || workspace_bytes < need)
+    return set_error(DSPARK_ERR_WORKSPACE, "accept_greedy: workspace %zu < %zu", workspace_bytes, need);
+  uint8_t* w = static_cast<uint8_t*>(workspace);
+  return launch_pdl("accept_greedy", acc::accept_greedy_kernel, dim3(grid), dim3(acc::kThreads), 0,
+                    static_cast<cudaStream_t>(stream), static_cast<const __nv_bfloat16*>(logits),
+                    ld, B, T, V, verify_ids, argmax, kv_len, commit, pending, plan,
+                    reinterpret_cast<float*>(w + off_c), reinterpret_cast<int*>(w + off_i),
+                    reinterpret_cast<int*>(w));
+}
+
+extern "C" int dspark_commit_lengths(const int32_t* plan, int plan_stride, int B, int32_t* len_a,
+                                     int32_t* len_b, dspark_stream_t stream) {
+  if (!plan || B <= 0 || (!len_a && !len_b))
+    return set_error(DSPARK_ERR_INVALID, "commit_lengths: bad arguments");
+  return launch_pdl("commit_lengths", acc::commit_lengths_kernel, dim3(1), dim3(128), 0,
+                    static_cast<cudaStream_t>(stream), plan, plan_stride, B, len_a, len_b);
+}
+
+extern "C" int dspark_draft_override(int B, int cap, int V, const int32_t* ref, int ref_len,
+                                     const uint8_t* agree, int rounds, int32_t* round_ctr,
+                                     const int32_t* kv_len, const int32_t* prompt_len,
+                                     int32_t* verify_ids, dspark_stream_t stream) {
+  if (!ref || !agree || !round_ctr || !kv_len || !prompt_len || !verify_ids || B <= 0 || cap <= 0 ||
+      ref_len <= 0 || rounds <= 0)
+    return set_error(DSPARK_ERR_INVALID, "draft_override: bad arguments");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int rc = launch_pdl("draft_override", acc::draft_override_kernel, dim3(B), dim3(32), 0, st, B,
+                      cap, V, ref, ref_len, agree, rounds, (const int32_t*)round_ctr, kv_len,
+                      prompt_len, verify_ids);
+  if (rc) return rc;
+  return launch_pdl("draft_override.bump", acc::bump_kernel, dim3(1), dim3(32), 0, st, round_ctr, B);
+}

@@ -1,0 +1,344 @@
+"""Decode loops on the device: speculative (DSpark, greedy) and plain greedy.
+
+Reference: src/mlx_dspark/generate.py — GenResult (:27-46), greedy_generate (:373-465),
+_prefill_tapped (:632-656), speculative_generate (:691-978).
+
+One speculative round is a fixed sequence of launches on one stream, with every varying
+quantity (positions, lengths, pending token, draft ids) in device memory:
+
+  draft  : block embed -> drafter layer(s) over [ctx; block] -> head on cap rows -> Markov argmax
+           (writes verify_ids = [pending, d_1..d_cap])
+  verify : target forward over verify_ids with the hidden-state tap
+  accept : fused argmax + accepted prefix + bonus token -> plan, pending
+  context: fc + hidden_norm + k/v of the verified rows written at the drafter's context length
+  commit : seq_len += n + 1 for the target KV and the drafter context (rollback = not counting)
+
+so it is captured once into a CUDA graph and replayed; the host reads one small plan per
+round (the reference also synchronises once per round, generate.py:917).
+"""
+from __future__ import annotations
+
+import time
+from dataclasses import dataclass
+
+import torch
+
+from . import ops
+from .kvcache import CacheState, RowView
+
+PREFILL_CHUNK = 2048  # reference knob (generate.py:613); the device chunk is min(this, chunk_len)
+
+
+@dataclass
+class GenResult:
+    text: str
+    token_ids: list[int]
+    num_tokens: int
+    num_rounds: int
+    accept_lengths: list[int]
+    target_forwards: int
+    seconds: float
+    finish_reason: str = "stop"
+    lookup_rounds: int = 0
+    logprobs: list | None = None
+    decode_seconds: float = 0.0  # time of the decode loop alone (after prefill)
+
+    @property
+    def mean_accept_len(self) -> float:
+        return self.num_tokens / max(self.num_rounds, 1)
+
+    @property
+    def tokens_per_sec(self) -> float:
+        return self.num_tokens / max(self.seconds, 1e-9)
+
+
+def eos_token_ids(tokenizer) -> set[int]:
+    """eos ids of a tokenizer (generate.py:111-132, reduced to the id attributes)."""
+    ids: set[int] = set()
+    if tokenizer is None:
+        return ids
+    e = getattr(tokenizer, "eos_token_ids", None)
+    if isinstance(e, int):
+        ids.add(e)
+    elif e:
+        ids.update(int(x) for x in e)
+    e1 = getattr(tokenizer, "eos_token_id", None)
+    if isinstance(e1, int):
+        ids.add(e1)
+    return ids
+
+
+def _decode(tokenizer, ids):
+    if tokenizer is None or not hasattr(tokenizer, "decode"):
+        return ""
+    return tokenizer.decode(ids)
+
+
+def _finish_reason(out_ids, max_new_tokens, last_tok, eos_ids) -> str:
+    if last_tok in eos_ids:
+        return "stop"
+    return "length" if len(out_ids) >= max_new_tokens else "stop"
+
+
+# ----------------------------------------------------------------------------------------
+def prefill_rows(target, ids: list[int], tstate, tap=(), drafter=None, cstate=None,
+                 dbuf_key=None):
+    """Chunked prefill of one row with the tap feeding the drafter context per chunk
+    (_prefill_tapped, generate.py:632-656). `tstate`/`cstate` are one-row views whose
+    lengths advance on the device. Returns the last chunk's logits row (bf16, device)."""
+    T = min(target.chunk_len(1), PREFILL_CHUNK)
+    n = len(ids)
+    ids_dev = torch.as_tensor(ids, dtype=torch.int32).to(target.device)
+    last = None
+    pos = 0
+    while pos < n:
+        t = min(T, n - pos)
+        buf = target.buffers(1, t, len(tap))
+        buf.ids.copy_(ids_dev[pos:pos + t])
+        target.forward(buf, tstate, tap, with_logits=(pos + t == n))
+        if drafter is not None:
+            dbuf = drafter.buffers(1, drafter.block_size, t)
+            drafter.update_context_dev(buf.fused16, 1, t, cstate, dbuf)
+            cstate.seq_len.add_(t)
+        tstate.seq_len.add_(t)
+        pos += t
+        if pos == n:
+            last = buf.logits[t - 1].clone()
+    return last
+
+
+class SpecSession:
+    """Static state and buffers of a B-row speculative decode with `cap` drafts per round."""
+
+    def __init__(self, target, drafter, B: int, cap: int, max_tokens: int, *,
+                 override: dict | None = None):
+        self.target, self.drafter = target, drafter
+        self.B, self.cap = B, cap
+        self.k = drafter.block_size
+        self.T = cap + 1
+        self.tap = list(drafter.config.target_layer_ids)
+        dev = target.device
+        # pages for the whole request budget, plus one drafted block past the end
+        cap_tokens = max_tokens + self.k + self.T + 64
+        self.tstate = CacheState(target.new_pool(cap_tokens, B), B, cap_tokens, dev)
+        self.cstate = CacheState(drafter.new_pool(cap_tokens, B), B, cap_tokens, dev)
+        for b in range(B):
+            self.tstate.ensure(b, cap_tokens)
+            self.cstate.ensure(b, cap_tokens)
+        self.vbuf = target.buffers(B, self.T, len(self.tap))
+        self.dbuf = drafter.buffers(B, self.k, B * self.T)
+        self.pending = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.draft = torch.zeros(B, cap, dtype=torch.int32, device=dev)
+        self.argmax = torch.zeros(B * self.T, dtype=torch.int32, device=dev)
+        self.plan = torch.zeros(B, self.T + 2, dtype=torch.int32, device=dev)
+        self.plan_host = torch.zeros(B, self.T + 2, dtype=torch.int32, pin_memory=True)
+        self.splits_t = target.attn_splits(B, self.tstate.max_pages)
+        self.splits_c = target.attn_splits(B, self.cstate.max_pages)
+        self.override = None
+        if override is not None:
+            o = override
+            self.override = {
+                "ref": o["ref"].to(dev, torch.int32).contiguous(),        # [B, ref_len]
+                "agree": o["agree"].to(dev, torch.uint8).contiguous(),    # [B, rounds, cap]
+                "round": torch.zeros(B, dtype=torch.int32, device=dev),
+                "prompt_len": torch.as_tensor(o["prompt_len"], dtype=torch.int32).to(dev),
+            }
+        self.graph = None
+        self.done = torch.cuda.Event()
+
+    def release(self):
+        self.graph = None
+        self.tstate.release()
+        self.cstate.release()
+
+    def launch_round(self) -> None:
+        d, t, sc = self.drafter, self.target, self.target.scratch
+        B, T, cap = self.B, self.T, self.cap
+        d.draft_dev(self.pending, B, cap, self.cstate, self.dbuf, self.draft, self.vbuf.ids,
+                    self.splits_c)
+        if self.override is not None:
+            o = self.override
+            ops.draft_override(B, cap, t.cfg.vocab_size, o["ref"], o["agree"], o["round"],
+                               self.tstate.seq_len, o["prompt_len"], self.vbuf.ids)
+        t.forward(self.vbuf, self.tstate, self.tap, splits=self.splits_t)
+        ops.accept_greedy(self.vbuf.logits, B, T, self.vbuf.ids, self.argmax, None, False,
+                          self.pending, self.plan, sc)
+        d.update_context_dev(self.vbuf.fused16, B, T, self.cstate, self.dbuf)
+        ops.commit_lengths(self.plan, B, self.tstate.seq_len, self.cstate.seq_len)
+        self.plan_host.copy_(self.plan, non_blocking=True)
+
+    def capture(self) -> None:
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                self.launch_round()
+        torch.cuda.current_stream().wait_stream(s)
+        self.graph = g
+
+    def step(self, use_graph: bool = True):
+        """Run one round; returns the plan rows [B, T+2] as python lists."""
+        if use_graph and self.graph is not None:
+            self.graph.replay()
+        else:
+            self.launch_round()
+        self.done.record()
+        self.done.synchronize()
+        return self.plan_host.tolist()
+
+
+def speculative_generate(target, tokenizer, drafter, prompt: str = "", *,
+                         prompt_ids: list[int] | None = None, cache=None, ctx_caches=None,
+                         reuse_len: int = 0, max_new_tokens: int = 128,
+                         confidence_threshold: float = 0.0, max_draft_tokens: int | None = 2,
+                         cap_controller=None, lookup_drafts: bool = False,
+                         lookup_max_draft: int = 6, temperature: float = 0.0, top_p: float = 1.0,
+                         top_k: int = 0, presence_penalty: float = 0.0,
+                         frequency_penalty: float = 0.0, logprobs: int | None = None,
+                         seed: int | None = None, apply_chat_template: bool = True,
+                         stop: list[str] | None = None, on_text=None, verbose: bool = False,
+                         use_graph: bool = True, draft_override: dict | None = None) -> GenResult:
+    """Speculative decoding, batch 1 (generate.py:691-978). Greedy (temperature 0): the output
+    is the target's greedy decoding; drafter quality only changes accept lengths."""
+    if temperature > 0.0:
+        raise NotImplementedError("sampled speculative decoding goes through the sampler path")
+    if presence_penalty or frequency_penalty or logprobs is not None or confidence_threshold > 0:
+        raise NotImplementedError("penalties / logprobs / confidence truncation are not built")
+    if lookup_drafts:
+        raise NotImplementedError("hybrid n-gram drafts are not built on the device loop yet")
+    cfg = drafter.config
+    k = cfg.block_size
+    cap = k if max_draft_tokens is None else max(1, min(int(max_draft_tokens), k))
+    eos_ids = eos_token_ids(tokenizer)
+    if prompt_ids is None:
+        prompt_ids = list(tokenizer.encode(prompt))
+    ids = list(prompt_ids)
+    budget = len(ids) + max_new_tokens + cap + 1
+    sess = SpecSession(target, drafter, 1, cap, budget, override=draft_override)
+    try:
+        t0 = time.time()
+        last = prefill_rows(target, ids, sess.tstate, sess.tap, drafter, sess.cstate)
+        pending = int(last.float().argmax())
+        sess.pending.fill_(pending)
+        torch.cuda.synchronize()
+        t1 = time.time()
+        out = [pending]
+        accept = []
+        rounds = 0
+        while len(out) < max_new_tokens and pending not in eos_ids:
+            plan = sess.step(use_graph)[0]
+            if use_graph and sess.graph is None:
+                sess.capture()
+            n = plan[0]
+            committed = plan[2:3 + n]
+            accept.append(len(committed))
+            for tok in committed:
+                out.append(tok)
+                if tok in eos_ids:
+                    break
+            pending = out[-1]
+            rounds += 1
+            if verbose:
+                print(f"  round {rounds:3d}: drafted {cap}, accepted {n}, committed {len(committed)}")
+        t2 = time.time()
+        text = _decode(tokenizer, [t for t in out if t not in eos_ids])
+        return GenResult(text=text, token_ids=out, num_tokens=len(out), num_rounds=len(accept),
+                         accept_lengths=accept, target_forwards=len(accept) + 1,
+                         seconds=t2 - t0, decode_seconds=t2 - t1,
+                         finish_reason=_finish_reason(out, max_new_tokens, pending, eos_ids))
+    finally:
+        sess.release()
+
+
+class GreedySession:
+    """Plain greedy decode of B rows, one token per step (generate.py:373-465)."""
+
+    def __init__(self, target, B: int, max_tokens: int):
+        self.target, self.B = target, B
+        dev = target.device
+        cap_tokens = max_tokens + 64
+        self.tstate = CacheState(target.new_pool(cap_tokens, B), B, cap_tokens, dev)
+        for b in range(B):
+            self.tstate.ensure(b, cap_tokens)
+        self.buf = target.buffers(B, 1, 0)
+        self.argmax = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.plan = torch.zeros(B, 3, dtype=torch.int32, device=dev)
+        self.plan_host = torch.zeros(B, 3, dtype=torch.int32, pin_memory=True)
+        self.splits = target.attn_splits(B, self.tstate.max_pages)
+        self.graph = None
+        self.done = torch.cuda.Event()
+
+    def release(self):
+        self.graph = None
+        self.tstate.release()
+
+    def launch_step(self):
+        t = self.target
+        t.forward(self.buf, self.tstate, (), splits=self.splits)
+        # T = 1: n = 0, bonus = argmax; the next input id is written in place
+        ops.accept_greedy(self.buf.logits, self.B, 1, self.buf.ids, self.argmax, self.tstate.seq_len,
+                          True, self.buf.ids, self.plan, t.scratch)
+        self.plan_host.copy_(self.plan, non_blocking=True)
+
+    def capture(self):
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                self.launch_step()
+        torch.cuda.current_stream().wait_stream(s)
+        self.graph = g
+
+    def step(self, use_graph=True):
+        if use_graph and self.graph is not None:
+            self.graph.replay()
+        else:
+            self.launch_step()
+        self.done.record()
+        self.done.synchronize()
+        return self.plan_host.tolist()
+
+
+def greedy_generate(target, tokenizer, prompt: str = "", *, prompt_ids: list[int] | None = None,
+                    cache=None, reuse_len: int = 0, max_new_tokens: int = 128,
+                    temperature: float = 0.0, top_p: float = 1.0, top_k: int = 0,
+                    presence_penalty: float = 0.0, frequency_penalty: float = 0.0,
+                    logprobs: int | None = None, seed: int | None = None,
+                    apply_chat_template: bool = True, stop=None, on_text=None,
+                    use_graph: bool = True) -> GenResult:
+    """Plain greedy decoding of the target (the baseline the speedup is measured against)."""
+    if temperature > 0.0:
+        raise NotImplementedError("sampled plain decoding goes through the sampler path")
+    eos_ids = eos_token_ids(tokenizer)
+    if prompt_ids is None:
+        prompt_ids = list(tokenizer.encode(prompt))
+    ids = list(prompt_ids)
+    sess = GreedySession(target, 1, len(ids) + max_new_tokens + 1)
+    try:
+        t0 = time.time()
+        last = prefill_rows(target, ids, sess.tstate, ())
+        nxt = int(last.float().argmax())
+        sess.buf.ids.fill_(nxt)
+        torch.cuda.synchronize()
+        t1 = time.time()
+        out = [nxt]
+        while len(out) < max_new_tokens and nxt not in eos_ids:
+            plan = sess.step(use_graph)[0]
+            if use_graph and sess.graph is None:
+                sess.capture()
+            nxt = plan[2]
+            out.append(nxt)
+        t2 = time.time()
+        text = _decode(tokenizer, [t for t in out if t not in eos_ids])
+        return GenResult(text=text, token_ids=out, num_tokens=len(out), num_rounds=len(out),
+                         accept_lengths=[1] * len(out), target_forwards=len(out),
+                         seconds=t2 - t0, decode_seconds=t2 - t1,
+                         finish_reason=_finish_reason(out, max_new_tokens, nxt, eos_ids))
+    finally:
+        sess.release()
+
+
+__all__ = ["GenResult", "SpecSession", "GreedySession", "speculative_generate",
+           "greedy_generate", "prefill_rows", "eos_token_ids", "RowView"]

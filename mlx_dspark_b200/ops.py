@@ -1,0 +1,172 @@
+"""Typed wrappers over the C ABI: torch tensors in, device pointers and shapes out.
+
+Every wrapper launches on the current torch CUDA stream and raises ``DsparkError`` on a
+nonzero status. ``Scratch`` owns the caller-side workspaces (one per kernel family, since
+each family keeps self-resetting counters at the start of its buffer) and the device
+status word that bounded device waits report into.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._lib import KvLayout, call, lib
+from .weights import PackedLinear
+
+
+def _p(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _require_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("dspark_b200 kernels take CUDA tensors only (no CPU fallback)")
+
+
+class Scratch:
+    """Zero-filled, grow-only workspaces per kernel family plus a device status word."""
+
+    FAMILIES = ("gemm", "attention", "accept", "markov")
+
+    def __init__(self, device="cuda"):
+        self.device = torch.device(device)
+        self.bufs: dict[str, torch.Tensor] = {}
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+
+    def get(self, family: str, nbytes: int) -> torch.Tensor:
+        b = self.bufs.get(family)
+        if b is None or b.numel() < nbytes:
+            b = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=self.device)
+            self.bufs[family] = b
+        return b
+
+    def reserve(self, family: str, nbytes: int) -> None:
+        self.get(family, nbytes)
+
+    def check_status(self) -> None:
+        s = int(self.status.item())
+        if s != 0:
+            self.status.zero_()
+            for b in self.bufs.values():  # counters may be left mid-count after a timeout
+                b.zero_()
+            raise _lib.DsparkError("device", s, "a kernel reported an error on the device")
+
+
+# ----------------------------------------------------------------------------------------
+def gemm_workspace_bytes(M: int, N: int, K: int) -> int:
+    return int(lib().dspark_w8a16_gemm_workspace_bytes(M, N, K))
+
+
+def gemm(x16: torch.Tensor, w: PackedLinear, y: torch.Tensor, *, epilogue=_lib.EPI_STORE_BF16,
+         residual: torch.Tensor | None = None, scratch: Scratch, M: int | None = None) -> torch.Tensor:
+    """y = x16 @ W^T with the chosen epilogue (see include/dspark_b200.h)."""
+    _require_cuda(x16, y)
+    M = x16.shape[0] if M is None else M
+    K = w.K
+    assert x16.dtype == torch.float16 and x16.shape[-1] >= K
+    ws = scratch.get("gemm", gemm_workspace_bytes(M, w.N, K))
+    call("dspark_w8a16_gemm", _p(x16), x16.stride(0), _p(w.q), _p(w.sb), M, w.N, K, _p(y),
+         y.stride(0), _p(residual), residual.stride(0) if residual is not None else 0, epilogue,
+         _p(ws), ws.numel(), _p(scratch.status), _stream())
+    return y
+
+
+def gemm_simt(x16, w: PackedLinear, y, *, epilogue=_lib.EPI_STORE_BF16, residual=None, M=None):
+    M = x16.shape[0] if M is None else M
+    call("dspark_w8a16_gemm_simt", _p(x16), x16.stride(0), _p(w.q), _p(w.sb), M, w.N, w.K, _p(y),
+         y.stride(0), _p(residual), residual.stride(0) if residual is not None else 0, epilogue,
+         _stream())
+    return y
+
+
+def embed(ids: torch.Tensor, w: PackedLinear, out: torch.Tensor, M: int | None = None) -> torch.Tensor:
+    _require_cuda(ids, out)
+    M = ids.numel() if M is None else M
+    call("dspark_embed_w8", _p(ids), M, _p(w.q), _p(w.sb), w.N, w.K, _p(out), out.stride(0), _stream())
+    return out
+
+
+def embed_block(pending: torch.Tensor, B: int, k: int, mask_id: int, w: PackedLinear,
+                out: torch.Tensor, ids_out: torch.Tensor | None = None) -> torch.Tensor:
+    call("dspark_embed_block_w8", _p(pending), B, k, mask_id, _p(w.q), _p(w.sb), w.N, w.K,
+         _p(out), out.stride(0), _p(ids_out), _stream())
+    return out
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, y: torch.Tensor | None = None,
+            y16: torch.Tensor | None = None, M: int | None = None) -> None:
+    _require_cuda(x, w)
+    M = x.shape[0] if M is None else M
+    H = w.numel()
+    call("dspark_rmsnorm", _p(x), x.stride(0), _p(w), M, H, float(eps), _p(y),
+         y.stride(0) if y is not None else 0, _p(y16), y16.stride(0) if y16 is not None else 0,
+         _stream())
+
+
+def kv_page_bytes(page_size: int, num_kv_heads: int, head_dim: int, kv8: bool) -> int:
+    return int(lib().dspark_kv_page_bytes(page_size, num_kv_heads, head_dim, int(kv8)))
+
+
+def kv_layout(pool: torch.Tensor, block_table: torch.Tensor, page_size: int, num_kv_heads: int,
+              head_dim: int, kv8: bool) -> KvLayout:
+    return KvLayout(pool.data_ptr(), block_table.data_ptr(), block_table.shape[1], page_size,
+                    num_kv_heads, head_dim, int(kv8), 0,
+                    kv_page_bytes(page_size, num_kv_heads, head_dim, kv8))
+
+
+def qkv_rope_kv_write(qkv: torch.Tensor, B: int, T: int, Hq: int, Hkv: int, hd: int,
+                      q_norm: torch.Tensor | None, k_norm: torch.Tensor, eps: float,
+                      inv_freq: torch.Tensor, pos0: torch.Tensor, q_out: torch.Tensor | None,
+                      kv: KvLayout) -> None:
+    call("dspark_qkv_rope_kv_write", _p(qkv), qkv.stride(0), B, T, Hq, Hkv, hd, _p(q_norm),
+         _p(k_norm), float(eps), _p(inv_freq), _p(pos0), _p(q_out), kv, _stream())
+
+
+def attention_workspace_bytes(B, T, Hq, Hkv, hd, splits) -> int:
+    return int(lib().dspark_attention_workspace_bytes(B, T, Hq, Hkv, hd, splits))
+
+
+def attention(q: torch.Tensor, B: int, T: int, Hq: int, kv: KvLayout, kv_len: torch.Tensor,
+              causal: bool, scale: float, out: torch.Tensor, splits: int, scratch: Scratch) -> None:
+    ws = scratch.get("attention", attention_workspace_bytes(B, T, Hq, kv.num_kv_heads,
+                                                            kv.head_dim, splits))
+    call("dspark_attention", _p(q), B, T, Hq, kv, _p(kv_len), int(causal), float(scale), _p(out),
+         out.stride(0), splits, _p(ws), ws.numel(), _p(scratch.status), _stream())
+
+
+def accept_greedy(logits: torch.Tensor, B: int, T: int, verify_ids: torch.Tensor,
+                  argmax: torch.Tensor, kv_len: torch.Tensor | None, commit: bool,
+                  pending: torch.Tensor, plan: torch.Tensor, scratch: Scratch) -> None:
+    V = logits.shape[-1]
+    ws = scratch.get("accept", int(lib().dspark_accept_workspace_bytes(B * T, V)))
+    call("dspark_accept_greedy", _p(logits), logits.stride(0), B, T, V, _p(verify_ids),
+         _p(argmax), _p(kv_len), int(commit), _p(pending), _p(plan), _p(ws), ws.numel(), _stream())
+
+
+def commit_lengths(plan: torch.Tensor, B: int, a: torch.Tensor, b: torch.Tensor | None = None):
+    call("dspark_commit_lengths", _p(plan), plan.stride(0), B, _p(a), _p(b), _stream())
+
+
+def draft_override(B, cap, V, ref, agree, round_ctr, kv_len, prompt_len, verify_ids):
+    call("dspark_draft_override", B, cap, V, _p(ref), ref.shape[-1], _p(agree), agree.shape[1],
+         _p(round_ctr), _p(kv_len), _p(prompt_len), _p(verify_ids), _stream())
+
+
+def markov_sample_block(base: torch.Tensor, rows_per_b: int, B: int, cap: int, w1: PackedLinear,
+                        w2: PackedLinear,
+                        first_prev: torch.Tensor, draft: torch.Tensor,
+                        verify_ids: torch.Tensor | None, scratch: Scratch) -> None:
+    V = w2.N
+    ws = scratch.get("markov", int(lib().dspark_markov_workspace_bytes(B, V)))
+    call("dspark_markov_sample_block", _p(base), base.stride(0), rows_per_b, B, cap, V, w2.K, _p(w1.q),
+         _p(w1.sb), _p(w2.q), _p(w2.sb), _p(first_prev), _p(draft), _p(verify_ids), _p(ws),
+         ws.numel(), _p(scratch.status), _stream())
+
+
+def bf16_to_f16(src: torch.Tensor, dst: torch.Tensor, rows: int, cols: int) -> None:
+    call("dspark_bf16_to_f16", _p(src), src.stride(0), _p(dst), dst.stride(0), rows, cols, _stream())

@@ -1,0 +1,204 @@
+"""GPU Qwen3 target: make_cache / run (hidden-state tap) / plain, on the sm_100a kernels.
+
+Drop-in for src/mlx_dspark/target.py:16-81 (Target.make_cache, run(ids, cache, tap) ->
+(logits, fused), plain(ids, cache) -> logits; attributes model/tokenizer/kv_bits/is_vlm/
+_tied). A forward over T tokens of B rows runs, per layer:
+
+  rmsnorm -> W8 GEMM (q|k|v) -> q/k norm + RoPE + paged KV write -> paged GQA attention
+  -> W8 GEMM (o, + residual) -> rmsnorm -> W8 GEMM (gate|up, SiLU*up) -> W8 GEMM (down, + residual)
+  [-> bf16->fp16 copy of the residual stream into the fused tap buffer]
+
+then the final norm and the W8 head. All launches go to the current stream with
+programmatic dependent launch, from static per-(B, T) buffers, so the sequence can be
+captured into a CUDA graph by the decode loops.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import ops
+from ._lib import EPI_RESIDUAL_BF16, EPI_SILU_MUL_F16, EPI_STORE_BF16
+from .config import TargetConfig
+from .kvcache import PAGE, CacheState, PagePool, TargetCache
+from .weights import PackedLinear, TargetWeights, pack
+
+MAX_M = 64          # rows per W8A16 GEMM launch
+MAX_ATTN_ROWS = 128  # query rows per kv head per attention CTA
+
+
+def rope_inv_freq(head_dim: int, theta: float, device) -> torch.Tensor:
+    i = torch.arange(0, head_dim, 2, dtype=torch.float64)
+    return (theta ** (-i / head_dim)).to(torch.float32).to(device)
+
+
+class PackedLayer:
+    def __init__(self, lw, device):
+        self.input_ln = lw.input_ln.to(device)
+        self.post_ln = lw.post_ln.to(device)
+        self.q_norm = lw.q_norm.to(device)
+        self.k_norm = lw.k_norm.to(device)
+        self.qkv = pack(lw.wq, lw.wk, lw.wv, device=device)
+        self.kv = None  # drafters pack k|v separately for the context update
+        self.o = pack(lw.wo, device=device)
+        self.gu = pack(lw.gate, lw.up, interleave64=True, device=device)
+        self.down = pack(lw.down, device=device)
+
+
+class Buffers:
+    """Static activations of one (B, T) forward shape."""
+
+    def __init__(self, cfg: TargetConfig, B: int, T: int, n_tap: int, device, logits=True):
+        M = B * T
+        H, I = cfg.hidden_size, cfg.intermediate_size
+        self.B, self.T, self.M = B, T, M
+        self.ids = torch.zeros(M, dtype=torch.int32, device=device)
+        self.h = torch.zeros(M, H, dtype=torch.bfloat16, device=device)
+        self.xn16 = torch.zeros(M, H, dtype=torch.float16, device=device)
+        self.qkv = torch.zeros(M, cfg.qkv_dim, dtype=torch.bfloat16, device=device)
+        self.q = torch.zeros(M, cfg.q_dim, dtype=torch.bfloat16, device=device)
+        self.attn16 = torch.zeros(M, cfg.q_dim, dtype=torch.float16, device=device)
+        self.act16 = torch.zeros(M, I, dtype=torch.float16, device=device)
+        self.fused16 = (torch.zeros(M, n_tap * H, dtype=torch.float16, device=device)
+                        if n_tap else None)
+        self.logits = (torch.zeros(M, cfg.vocab_size, dtype=torch.bfloat16, device=device)
+                       if logits else None)
+
+
+class Target:
+    """GPU W8 Qwen3 target with a hidden-state tap (see module docstring)."""
+
+    def __init__(self, weights: TargetWeights, tokenizer=None, *, kv_bits: int | None = None,
+                 device="cuda", scratch: ops.Scratch | None = None):
+        if kv_bits not in (None, 8):
+            raise ValueError("kv_bits must be None (bf16 KV) or 8")
+        self.cfg: TargetConfig = weights.cfg
+        self.tokenizer = tokenizer
+        self.kv_bits = kv_bits
+        self.kv_group_size = 64
+        self.is_vlm = False
+        self.family = "qwen3"
+        self._tied = weights.lm_head is None
+        self.device = torch.device(device)
+        c = self.cfg
+        if c.head_dim not in (64, 128):
+            raise ValueError("head_dim must be 64 or 128")
+        self.embed = pack(weights.embed, device=device)
+        self.layers = [PackedLayer(l, device) for l in weights.layers]
+        self.norm = weights.norm.to(device)
+        self.head = self.embed if self._tied else pack(weights.lm_head, device=device)
+        self.inv_freq = rope_inv_freq(c.head_dim, c.rope_theta, device)
+        self.scale = c.head_dim ** -0.5
+        self.scratch = scratch or ops.Scratch(device)
+        self._bufs: dict[tuple, Buffers] = {}
+        self.model = self  # reference code reaches target.model for embed/lm_head binding
+        self.group = c.num_attention_heads // c.num_key_value_heads
+
+    # ------------------------------------------------------------------ caches
+    def new_pool(self, max_tokens: int, rows: int = 1, extra_pages: int = 0) -> PagePool:
+        pages = rows * ((max_tokens + PAGE - 1) // PAGE) + extra_pages
+        return PagePool(self.cfg.num_hidden_layers, pages, self.cfg.num_key_value_heads,
+                        self.cfg.head_dim, self.kv_bits == 8, self.device)
+
+    def make_cache(self, max_tokens: int = 4096) -> TargetCache:
+        """Per-layer cache views over a fresh page pool (mlx-lm make_prompt_cache shape;
+        QuantizedKVCache semantics when kv_bits == 8)."""
+        pool = self.new_pool(max_tokens)
+        state = CacheState(pool, 1, max_tokens, self.device)
+        kind = "QuantizedKVCache" if self.kv_bits == 8 else "KVCache"
+        return TargetCache(state, self.cfg.num_hidden_layers, kind)
+
+    # ------------------------------------------------------------------ buffers
+    def buffers(self, B: int, T: int, n_tap: int, logits: bool = True) -> Buffers:
+        key = (B, T, n_tap, logits)
+        b = self._bufs.get(key)
+        if b is None:
+            b = Buffers(self.cfg, B, T, n_tap, self.device, logits)
+            self._bufs[key] = b
+        return b
+
+    def attn_splits(self, B: int, max_pages: int) -> int:
+        s = max(1, (2 * 148) // (B * self.cfg.num_key_value_heads))
+        return max(1, min(s, max_pages))
+
+    def chunk_len(self, B: int = 1) -> int:
+        """Largest T with B*T <= 64 GEMM rows and G*T <= 128 attention rows."""
+        return max(1, min(MAX_M // B, MAX_ATTN_ROWS // self.group))
+
+    # ------------------------------------------------------------------ the forward
+    def forward(self, buf: Buffers, state: CacheState, tap=(), *, splits: int | None = None,
+                with_logits: bool = True) -> None:
+        """Run B x T tokens (ids already in buf.ids) at positions state.seq_len[b] + t.
+        Writes KV for all T positions; does not advance seq_len."""
+        c, sc = self.cfg, self.scratch
+        B, T, M = buf.B, buf.T, buf.M
+        splits = splits or self.attn_splits(B, state.max_pages)
+        tap_idx = {l: j for j, l in enumerate(tap)}
+        H = c.hidden_size
+        ops.embed(buf.ids, self.embed, buf.h, M)
+        for l, L in enumerate(self.layers):
+            kv = state.layout(l)
+            ops.rmsnorm(buf.h, L.input_ln, c.rms_norm_eps, y16=buf.xn16, M=M)
+            ops.gemm(buf.xn16, L.qkv, buf.qkv, epilogue=EPI_STORE_BF16, scratch=sc, M=M)
+            ops.qkv_rope_kv_write(buf.qkv, B, T, c.num_attention_heads, c.num_key_value_heads,
+                                  c.head_dim, L.q_norm, L.k_norm, c.rms_norm_eps, self.inv_freq,
+                                  state.seq_len, buf.q, kv)
+            ops.attention(buf.q, B, T, c.num_attention_heads, kv, state.seq_len, True,
+                          self.scale, buf.attn16, splits, sc)
+            ops.gemm(buf.attn16, L.o, buf.h, epilogue=EPI_RESIDUAL_BF16, residual=buf.h,
+                     scratch=sc, M=M)
+            ops.rmsnorm(buf.h, L.post_ln, c.rms_norm_eps, y16=buf.xn16, M=M)
+            ops.gemm(buf.xn16, L.gu, buf.act16, epilogue=EPI_SILU_MUL_F16, scratch=sc, M=M)
+            ops.gemm(buf.act16, L.down, buf.h, epilogue=EPI_RESIDUAL_BF16, residual=buf.h,
+                     scratch=sc, M=M)
+            if l in tap_idx:
+                j = tap_idx[l]
+                ops.bf16_to_f16(buf.h, buf.fused16[:, j * H:(j + 1) * H], M, H)
+        if with_logits:
+            ops.rmsnorm(buf.h, self.norm, c.rms_norm_eps, y16=buf.xn16, M=M)
+            ops.gemm(buf.xn16, self.head, buf.logits, epilogue=EPI_STORE_BF16, scratch=sc, M=M)
+
+    # ------------------------------------------------------------------ reference API
+    def run(self, ids, cache: TargetCache, tap):
+        """ids [1, L] -> (logits [1, L, V] bf16, fused [1, L, n_tap*H] bf16)."""
+        return self._run(ids, cache, list(tap))
+
+    def plain(self, ids, cache: TargetCache):
+        return self._run(ids, cache, [])[0]
+
+    def _run(self, ids, cache: TargetCache, tap: list[int]):
+        ids = torch.as_tensor(ids, dtype=torch.int32).reshape(-1).to(self.device)
+        Ltot = ids.numel()
+        st = cache.state
+        off = cache.sync_to_device()
+        st.ensure(0, off + Ltot)
+        T = self.chunk_len(1)
+        V, H = self.cfg.vocab_size, self.cfg.hidden_size
+        logits = torch.empty(Ltot, V, dtype=torch.bfloat16, device=self.device)
+        fused = (torch.empty(Ltot, len(tap) * H, dtype=torch.bfloat16, device=self.device)
+                 if tap else None)
+        pos = 0
+        while pos < Ltot:
+            t = min(T, Ltot - pos)
+            buf = self.buffers(1, t, len(tap))
+            buf.ids.copy_(ids[pos:pos + t])
+            self.forward(buf, st, tap)
+            logits[pos:pos + t].copy_(buf.logits)
+            if tap:
+                fused[pos:pos + t].copy_(buf.fused16)
+            pos += t
+            st.seq_len.add_(t)
+        cache.advance(Ltot)
+        return logits[None], (None if fused is None else fused[None])
+
+    def weight_bytes(self) -> int:
+        n = self.embed.nbytes() + (0 if self._tied else self.head.nbytes())
+        for L in self.layers:
+            n += L.qkv.nbytes() + L.o.nbytes() + L.gu.nbytes() + L.down.nbytes()
+        return n
+
+    def verify_tap(self) -> None:
+        """The tap is computed inside the same forward as the logits (no replicated loop
+        to validate, unlike target.py:84-128); nothing to probe."""
+        return None

@@ -1,0 +1,67 @@
+"""Host-side checks that need no GPU: the C-ABI library loads, exports and binds every
+entry point of include/dspark_b200.h, rejects bad arguments with a message, and the host
+packing / layout helpers are right."""
+import os
+import re
+
+import pytest
+import torch
+
+from mlx_dspark_b200 import _lib
+from mlx_dspark_b200.weights import pack, quantize_w8g64
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(__file__)), "include", "dspark_b200.h")
+
+
+def declared_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(dspark_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    L = _lib.lib()
+    names = declared_functions()
+    assert len(names) >= 15
+    for n in names:
+        assert hasattr(L, n), n
+    assert sorted(names) == sorted(_lib.SIGNATURES), set(names) ^ set(_lib.SIGNATURES)
+    assert L.dspark_version() >= 10000
+
+
+def test_bad_arguments_return_codes_and_messages():
+    L = _lib.lib()
+    rc = L.dspark_w8a16_gemm(None, 0, None, None, 0, 128, 128, None, 0, None, 0, 0, None, 0,
+                             None, None)
+    assert rc == 1
+    assert b"null pointer" in L.dspark_last_error()
+    with pytest.raises(_lib.DsparkError) as e:
+        _lib.call("dspark_rmsnorm", None, 0, None, 0, 0, 1e-6, None, 0, None, 0, None)
+    assert "rmsnorm" in str(e.value)
+
+
+def test_kv_page_bytes():
+    L = _lib.lib()
+    assert L.dspark_kv_page_bytes(64, 8, 128, 0) == 2 * 8 * 64 * 128 * 2
+    assert L.dspark_kv_page_bytes(64, 8, 128, 1) == 2 * 8 * 64 * 128 + 2 * 8 * 64 * 2 * 4
+
+
+def test_pack_layout_and_interleave():
+    g = quantize_w8g64(torch.randn(128, 256) * 0.02)
+    u = quantize_w8g64(torch.randn(128, 256) * 0.02)
+    p = pack(g, u, interleave64=True, device="cpu")
+    assert p.N == 256 and p.K == 256 and p.sb.shape == (4, 256)
+    # packed tile t = [gate rows 64t..64t+63; up rows 64t..64t+63]
+    assert torch.equal(p.q[0:64], g.q[0:64]) and torch.equal(p.q[64:128], u.q[0:64])
+    assert torch.equal(p.q[128:192], g.q[64:128]) and torch.equal(p.q[192:256], u.q[64:128])
+    # sb[g, n] = fp16 scale (low) | fp16 bias (high)
+    s = (p.sb[1, 65] & 0xFFFF).to(torch.int16).view(torch.float16).float()
+    b = (p.sb[1, 65] >> 16).to(torch.int16).view(torch.float16).float()
+    assert s == u.scales[1, 1].float() and b == u.biases[1, 1].float()
+
+
+def test_pack_rejects_values_fp16_cannot_hold():
+    qt = quantize_w8g64(torch.randn(128, 128) * 0.02)
+    qt.scales[0, 0] = torch.tensor(1e-7).to(torch.bfloat16)
+    with pytest.raises(ValueError):
+        pack(qt, device="cpu")
