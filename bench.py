@@ -1,0 +1,458 @@
+#!/usr/bin/env python
+"""Benchmark of the speculative verify step (BASELINE.json metric: accepted tok/s on
+Qwen3-8B W8 with a DSpark drafter; verify-step us; HBM GB/s).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: Qwen3-8B-arch target, random-init W8 g64 weights (seed 1),
+1-layer DSpark drafter with block 8, batch 1, a 1024-token random prompt, greedy decoding,
+draft tokens overridden from a seeded Bernoulli(0.7) agree mask over the target's own
+greedy continuation (so the mean accept length is set by the mask, as the config asks).
+
+A step is one speculative round: draft (drafter forward + Markov head) -> verify (target
+forward over 9 tokens) -> fused acceptance -> drafter context update -> KV commit, replayed
+from one CUDA graph. `value` = committed tokens / device time over exactly K rounds with
+everything resident in HBM. `e2e` = the same metric through the public
+speculative_generate() call, whose host loop copies each round's input token host->device
+and reads each round's commit plan device->host. Multi-GPU: one process per GPU, each an
+independent replica of the request (request-parallel, no collective), value = sum of
+tokens / max over ranks of the device time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "source": "measured"}
+    return dict(PEAKS_FALLBACK, source="fallback")
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="C2")
+    ap.add_argument("--prompt-len", type=int, default=None)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="small run for ncu: short prompt, random reference tokens, no extras")
+    ap.add_argument("--cpu-budget", type=float, default=20.0)
+    ap.add_argument("--layers", type=int, default=None,
+                    help="depth-reduced target (same widths) for profiling captures")
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------------------------------
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def allreduce_max(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def allreduce_sum(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+# ----------------------------------------------------------------------------------------
+def build_models(wl, seed, layers=None, keep_cpu=True):
+    from mlx_dspark_b200.config import TARGETS, dspark_for, with_layers
+    from mlx_dspark_b200.model import DSparkDrafter
+    from mlx_dspark_b200.target import Target
+    from mlx_dspark_b200.weights import generate_dspark, generate_target
+
+    tcfg = TARGETS[wl.target]
+    if layers:
+        tcfg = with_layers(tcfg, layers)
+    dcfg = dspark_for(tcfg, block_size=wl.block_size)
+    tw = generate_target(tcfg, seed, "cuda")
+    dw = generate_dspark(dcfg, seed, "cuda")
+    target = Target(tw, kv_bits=wl.kv_bits)
+    drafter = DSparkDrafter(dw, target)
+    # the kernels hold packed copies; keep the canonical tensors on the host only
+    tw_cpu = tw.to("cpu") if keep_cpu else None
+    del tw, dw
+    torch.cuda.empty_cache()
+    return tw_cpu, target, drafter, dcfg
+
+
+def gemm_roofline(target, M, reps=5):
+    """Time the verify's W8 GEMMs alone (every layer's qkv, o, gate/up, down and the head at
+    M rows) with CUDA events; returns (GB/s, algorithmic bytes per pass, us per pass, launches)."""
+    from mlx_dspark_b200 import ops
+    from mlx_dspark_b200._lib import EPI_RESIDUAL_BF16, EPI_SILU_MUL_F16, EPI_STORE_BF16
+
+    c = target.cfg
+    dev = target.device
+    x = torch.randn(M, max(c.hidden_size, c.intermediate_size, c.q_dim), device=dev).to(torch.float16)
+    h = torch.zeros(M, c.hidden_size, dtype=torch.bfloat16, device=dev)
+    qkv = torch.zeros(M, c.qkv_dim, dtype=torch.bfloat16, device=dev)
+    act = torch.zeros(M, c.intermediate_size, dtype=torch.float16, device=dev)
+    logits = torch.zeros(M, c.vocab_size, dtype=torch.bfloat16, device=dev)
+    sc = target.scratch
+    H, I = c.hidden_size, c.intermediate_size
+
+    def one_pass():
+        for L in target.layers:
+            ops.gemm(x[:, :H], L.qkv, qkv, epilogue=EPI_STORE_BF16, scratch=sc, M=M)
+            ops.gemm(x[:, :c.q_dim], L.o, h, epilogue=EPI_RESIDUAL_BF16, residual=h, scratch=sc, M=M)
+            ops.gemm(x[:, :H], L.gu, act, epilogue=EPI_SILU_MUL_F16, scratch=sc, M=M)
+            ops.gemm(x[:, :I], L.down, h, epilogue=EPI_RESIDUAL_BF16, residual=h, scratch=sc, M=M)
+        ops.gemm(x[:, :H], target.head, logits, epilogue=EPI_STORE_BF16, scratch=sc, M=M)
+
+    wbytes = sum(L.qkv.nbytes() + L.o.nbytes() + L.gu.nbytes() + L.down.nbytes()
+                 for L in target.layers) + target.head.nbytes()
+    act_bytes = 0
+    for L in target.layers:
+        act_bytes += M * (H * 2 + c.qkv_dim * 2)            # x in, qkv out
+        act_bytes += M * (c.q_dim * 2 + H * 2 * 2)          # x in, residual in + out
+        act_bytes += M * (H * 2 + I * 2)                    # x in, act out
+        act_bytes += M * (I * 2 + H * 2 * 2)
+    act_bytes += M * (H * 2 + c.vocab_size * 2)
+    one_pass()
+    torch.cuda.synchronize()
+    s = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(reps):
+        one_pass()
+    e.record()
+    torch.cuda.synchronize()
+    us = s.elapsed_time(e) * 1000.0 / reps
+    total = wbytes + act_bytes
+    return total / (us * 1e-6) / 1e9, total, us, 4 * len(target.layers) + 1
+
+
+def verify_step_us(target, sess, reps=30):
+    """Device time of the verify forward + fused acceptance alone (one CUDA graph)."""
+    from mlx_dspark_b200 import ops
+
+    t = target
+    B, T = sess.B, sess.T
+
+    def launch():
+        t.forward(sess.vbuf, sess.tstate, sess.tap, splits=sess.splits_t)
+        ops.accept_greedy(sess.vbuf.logits, B, T, sess.vbuf.ids, sess.argmax, None, False,
+                          sess.pending, sess.plan, t.scratch)
+
+    launch()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    st = torch.cuda.Stream()
+    st.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(st):
+        with torch.cuda.graph(g, stream=st):
+            launch()
+    torch.cuda.current_stream().wait_stream(st)
+    g.replay()
+    torch.cuda.synchronize()
+    s = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(reps):
+        g.replay()
+    e.record()
+    torch.cuda.synchronize()
+    del g
+    return s.elapsed_time(e) * 1000.0 / reps
+
+
+def read_traffic():
+    """Per-launch DRAM traffic of the W8 GEMM from the committed ncu summary, if present."""
+    p = os.path.join(ROOT, "profiles", "w8a16_gemm_qwen3_8b_verify.md")
+    if not os.path.exists(p):
+        return None
+    with open(p) as f:
+        for line in f:
+            if line.strip().startswith("traffic_bytes_per_pass_scaled:"):
+                try:
+                    return float(line.split(":", 1)[1].strip().split()[0])
+                except ValueError:
+                    return None
+    return None
+
+
+def cpu_baseline(tw, prompt_len, budget):
+    from oracle.cpu_baseline import time_greedy_decode
+
+    cw = tw.to("cpu")
+    tps, n, dt, threads = time_greedy_decode(cw, prompt_len, budget_s=budget)
+    return {"value": round(tps, 4), "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"{n} plain greedy decode steps of the Qwen3-8B W8 target at a "
+                      f"{prompt_len}-token context (oracle port, fp32 math, int8 weights "
+                      f"dequantized per step; KV of the context filled synthetically), "
+                      f"{dt:.1f} s"}
+
+
+# ----------------------------------------------------------------------------------------
+def run_ours(args, world, rank):
+    from mlx_dspark_b200 import _lib
+    from mlx_dspark_b200.config import WORKLOADS
+    from mlx_dspark_b200.generate import SpecSession, greedy_generate, prefill_rows, speculative_generate
+
+    wl = WORKLOADS[args.workload]
+    K, W = args.steps, args.warmup
+    prompt_len = args.prompt_len or (128 if args.profile else wl.prompt_len)
+    cap = wl.block_size
+    want_cpu = rank == 0 and world == 1 and not args.no_cpu_baseline and not args.profile
+    tw, target, drafter, dcfg = build_models(wl, wl.seed, args.layers, keep_cpu=want_cpu)
+    V = target.cfg.vocab_size
+    g = torch.Generator().manual_seed(wl.seed)
+    prompt = torch.randint(0, V, (prompt_len,), generator=g).tolist()
+    rounds = K + W + 2
+    ref_len = (K + W + 2) * (cap + 1) + 16
+    if args.profile:
+        ref = torch.randint(0, V, (ref_len,), generator=g).tolist()
+    else:
+        ref = greedy_generate(target, None, prompt_ids=prompt, max_new_tokens=ref_len).token_ids
+    agree = (torch.rand(1, rounds, cap, generator=torch.Generator().manual_seed(7)) < (wl.accept_p or 0.7)).to(torch.uint8)
+    override = {"ref": torch.tensor([ref]), "agree": agree, "prompt_len": [prompt_len]}
+    budget = prompt_len + ref_len + 64
+    sess = SpecSession(target, drafter, 1, cap, budget, override=override)
+    last = prefill_rows(target, prompt, sess.tstate, sess.tap, drafter, sess.cstate)
+    sess.pending.fill_(int(last.float().argmax()))
+    torch.cuda.synchronize()
+    # one eager round (counts launches, sizes every workspace), then capture
+    n0 = _lib.LAUNCHES["n"]
+    sess.step(use_graph=False)
+    launches_per_round = _lib.LAUNCHES["n"] - n0
+    sess.capture()
+    clocks = ClockSampler(torch.cuda.current_device())
+    clocks.start()
+    for _ in range(max(0, W - 1)):
+        sess.graph.replay()
+    torch.cuda.synchronize()
+    len0 = int(sess.tstate.seq_len[0])
+    barrier(world)
+    torch.cuda.synchronize()
+    ev_s = torch.cuda.Event(enable_timing=True)
+    ev_e = torch.cuda.Event(enable_timing=True)
+    ev_s.record()
+    for _ in range(K):
+        sess.graph.replay()
+    ev_e.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = ev_s.elapsed_time(ev_e)
+    len1 = int(sess.tstate.seq_len[0])
+    target.scratch.check_status()
+    tokens = len1 - len0
+    # verify-step and GEMM roofline (same process, same clocks window)
+    vus = verify_step_us(target, sess)
+    gbs, gemm_bytes, gemm_us, gemm_launches = gemm_roofline(target, sess.T)
+    clk = clocks.stop()
+    sess.release()
+    max_ms = allreduce_max(ms, world)
+    all_tokens = allreduce_sum(float(tokens), world)
+    value = all_tokens / (max_ms / 1000.0)
+    peaks = load_peaks()
+    out = {
+        "metric": "accepted tok/s Qwen3-8B W8 DSpark (1/N GPU); verify-step us; HBM GB/s",
+        "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": round(max_ms / K, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "w8a16 (int8 weights, fp16 MMA, fp32 accumulate, bf16 activations)",
+        "data": "synthetic: random-init W8 g64 weights (seed 1), random prompt ids, "
+                "Bernoulli(0.7) draft-agree mask over the target's own greedy continuation",
+        "config": {"workload": wl.name, "model": "Qwen3-8B-arch W8 g64 + DSpark 1-layer block 8",
+                   "global_batch": world, "batch_per_gpu": 1, "prompt_len": prompt_len,
+                   "draft_cap": cap, "parallelism": f"request-parallel x{world} (replicas)",
+                   "l2": "inputs larger than L2 (8 GB of weights streamed per round)"},
+        "mean_accept_len": round(tokens / K, 3),
+        "verify_step_us": round(vus, 1),
+        "round_us": round(max_ms * 1000.0 / K, 1),
+        "verify_hbm_gbs": round(target.weight_bytes() / (vus * 1e-6) / 1e9, 1),
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
+                     "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4),
+                     "traffic": read_traffic(), "kernel": "w8a16_tc_kernel (all verify GEMMs, M=9)",
+                     "bytes_per_pass": gemm_bytes, "us_per_pass": round(gemm_us, 1),
+                     "launches_per_pass": gemm_launches,
+                     "peak_source": peaks["source"] + " (MEASURED_PEAKS.json hbm_gbs)"},
+        "gpu_launches": launches_per_round * K,
+        "clocks": clk,
+    }
+    if not args.no_e2e and not args.profile:
+        res = speculative_generate(target, None, drafter, prompt_ids=prompt,
+                                   max_new_tokens=min(512, ref_len - 16), max_draft_tokens=cap,
+                                   draft_override=override)
+        e2e_tps = (res.num_tokens - 1) / res.decode_seconds
+        e2e_all = allreduce_sum(e2e_tps, world)
+        out["e2e"] = {"value": round(e2e_all, 2), "unit": "tok/s",
+                      "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4 * (cap + 3),
+                      "api": "mlx_dspark_b200.speculative_generate (host loop, one sync per round)",
+                      "rounds": res.num_rounds, "mean_accept_len": round(res.mean_accept_len, 3),
+                      "prefill_s": round(res.seconds - res.decode_seconds, 3)}
+    if want_cpu:
+        out["cpu_baseline"] = cpu_baseline(tw, prompt_len, args.cpu_budget)
+    return out
+
+
+def run_reference(args, world, rank):
+    """The reference arm: the reference's CPU implementation of this path on the host cores.
+    MLX cannot be installed here, so it is the oracle port (plain greedy decode, the
+    north-star's 'plain MLX-CPU decode' baseline); each step is one decode token."""
+    if rank != 0:
+        return None
+    from mlx_dspark_b200.config import TARGETS, WORKLOADS
+    from mlx_dspark_b200.weights import generate_target
+    from oracle.cpu_baseline import StreamingDecoder
+
+    wl = WORKLOADS[args.workload]
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    tw = generate_target(TARGETS[wl.target], wl.seed, dev).to("cpu")
+    if dev == "cuda":
+        torch.cuda.empty_cache()
+    K = args.steps
+    W = min(args.warmup, 1)
+    dec = StreamingDecoder(tw, wl.prompt_len + K + W + 2)
+    dec.fill_random_context(wl.prompt_len)
+    tok = 1
+    for _ in range(W):
+        tok = dec.step(tok)
+    budget = 150.0
+    t0 = time.perf_counter()
+    n = 0
+    while n < K and time.perf_counter() - t0 < budget:
+        tok = dec.step(tok)
+        n += 1
+    dt = time.perf_counter() - t0
+    v = n / dt
+    return {
+        "impl": "reference", "metric": "accepted tok/s Qwen3-8B W8 DSpark (1/N GPU); verify-step us; HBM GB/s",
+        "value": round(v, 4), "unit": "tok/s", "n_gpus": world, "steps": n, "steps_requested": K,
+        "warmup": W, "ms_per_step": round(dt * 1000 / max(n, 1), 2), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32 math over int8 + bf16 weights",
+        "data": "synthetic (same weights and context length as the GPU arm)",
+        "config": {"workload": wl.name, "model": "Qwen3-8B-arch W8 g64 (plain greedy decode)",
+                   "global_batch": 1, "prompt_len": wl.prompt_len, "parallelism": "host cores"},
+        "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": dec.threads, "kind": "port",
+                         "sample": f"{n} greedy decode steps at a {wl.prompt_len}-token context "
+                                   f"(mlx absent: oracle port of greedy_generate), {dt:.1f} s"},
+        "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        out = run_reference(args, world, rank)
+        if out is not None:
+            print(json.dumps(out), flush=True)
+        return 0
+    world, rank, _ = dist_setup(args.gpus)
+    try:
+        out = run_ours(args, world, rank)
+        if rank == 0:
+            print(json.dumps(out), flush=True)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

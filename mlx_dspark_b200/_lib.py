@@ -84,8 +84,16 @@ def check(rc: int, what: str) -> None:
         raise DsparkError(what, rc, msg.decode() if msg else "")
 
 
+# kernel launches issued through call() (graph replays re-run them without Python)
+LAUNCHES = {"n": 0}
+_KERNELS_PER_CALL = {"dspark_markov_sample_block": lambda a: int(a[4]),
+                     "dspark_draft_override": lambda a: 2}
+
+
 def call(name: str, *args) -> None:
     check(getattr(lib(), name)(*args), name)
+    f = _KERNELS_PER_CALL.get(name)
+    LAUNCHES["n"] += f(args) if f else 1
 
 
 def exported_symbols() -> list[str]:

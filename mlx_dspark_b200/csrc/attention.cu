@@ -20,6 +20,7 @@ namespace dspark {
 namespace attn {
 
 constexpr int KT = 64;  // keys per tile == page size
+constexpr int kMinPagesPerSplit = 4;
 
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
@@ -149,7 +150,11 @@ __global__ void __launch_bounds__(256) attn_kernel(const Args a) {
   const int kvlen = a.kv_len[b];
   const int Ltot = kvlen + a.T;
   const int npages = (Ltot + KT - 1) / KT;
-  const int pps = (npages + a.nsplit - 1) / a.nsplit;
+  // Splits actually used for this context: at least kMinPagesPerSplit pages each, so the
+  // merge stays cheap at short contexts; CTAs past them leave before touching the counter.
+  const int nsplit = min(a.nsplit, (npages + kMinPagesPerSplit - 1) / kMinPagesPerSplit);
+  if (split >= nsplit) return;
+  const int pps = (npages + nsplit - 1) / nsplit;
   const int p_lo = split * pps;
   const int p_hi = min(p_lo + pps, npages);
 
@@ -298,7 +303,7 @@ __global__ void __launch_bounds__(256) attn_kernel(const Args a) {
   int* flag = reinterpret_cast<int*>(smem + 2 * L::kBuf);
   if (threadIdx.x == 0) {
     const int old = atomicAdd(a.counters + bh, 1);
-    *flag = (old == a.nsplit - 1);
+    *flag = (old == nsplit - 1);
   }
   __syncthreads();
   if (!*flag) return;
@@ -308,9 +313,9 @@ __global__ void __launch_bounds__(256) attn_kernel(const Args a) {
   const size_t base0 = (size_t)bh * a.nsplit * a.R;
   for (int r = threadIdx.x; r < a.R; r += blockDim.x) {
     float M = -INFINITY;
-    for (int sp = 0; sp < a.nsplit; ++sp) M = fmaxf(M, __ldcg(a.ws_ml + (base0 + (size_t)sp * a.R + r) * 2));
+    for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, __ldcg(a.ws_ml + (base0 + (size_t)sp * a.R + r) * 2));
     float Ls = 0.0f;
-    for (int sp = 0; sp < a.nsplit; ++sp) {
+    for (int sp = 0; sp < nsplit; ++sp) {
       const float ms = __ldcg(a.ws_ml + (base0 + (size_t)sp * a.R + r) * 2);
       const float ls = __ldcg(a.ws_ml + (base0 + (size_t)sp * a.R + r) * 2 + 1);
       const float e = (ms == -INFINITY) ? 0.0f : exp2f(ms - M);
@@ -318,13 +323,13 @@ __global__ void __launch_bounds__(256) attn_kernel(const Args a) {
       Ls += ls * e;
     }
     const float inv = Ls > 0.0f ? 1.0f / Ls : 0.0f;
-    for (int sp = 0; sp < a.nsplit; ++sp) wgt[sp * a.R + r] *= inv;
+    for (int sp = 0; sp < nsplit; ++sp) wgt[sp * a.R + r] *= inv;
   }
   __syncthreads();
   for (int i = threadIdx.x; i < a.R * (HD / 4); i += blockDim.x) {
     const int r = i / (HD / 4), d = (i - r * (HD / 4)) * 4;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int sp = 0; sp < a.nsplit; ++sp) {
+    for (int sp = 0; sp < nsplit; ++sp) {
       const float w = wgt[sp * a.R + r];
       if (w == 0.0f) continue;
       const float4 v = __ldcg(reinterpret_cast<const float4*>(a.ws_o + (base0 + (size_t)sp * a.R + r) * HD + d));

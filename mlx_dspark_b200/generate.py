@@ -132,6 +132,7 @@ class SpecSession:
         self.argmax = torch.zeros(B * self.T, dtype=torch.int32, device=dev)
         self.plan = torch.zeros(B, self.T + 2, dtype=torch.int32, device=dev)
         self.plan_host = torch.zeros(B, self.T + 2, dtype=torch.int32, pin_memory=True)
+        self.pending_host = torch.zeros(B, dtype=torch.int32, pin_memory=True)
         self.splits_t = target.attn_splits(B, self.tstate.max_pages)
         self.splits_c = target.attn_splits(B, self.cstate.max_pages)
         self.override = None
@@ -177,8 +178,12 @@ class SpecSession:
         torch.cuda.current_stream().wait_stream(s)
         self.graph = g
 
-    def step(self, use_graph: bool = True):
-        """Run one round; returns the plan rows [B, T+2] as python lists."""
+    def step(self, use_graph: bool = True, feed_pending: bool = False):
+        """Run one round; returns the plan rows [B, T+2] as python lists. With feed_pending
+        the round's input token comes from pending_host (pinned) by one H2D copy, as in a
+        host-driven loop where the host owns the committed sequence."""
+        if feed_pending:
+            self.pending.copy_(self.pending_host, non_blocking=True)
         if use_graph and self.graph is not None:
             self.graph.replay()
         else:
@@ -227,7 +232,8 @@ def speculative_generate(target, tokenizer, drafter, prompt: str = "", *,
         accept = []
         rounds = 0
         while len(out) < max_new_tokens and pending not in eos_ids:
-            plan = sess.step(use_graph)[0]
+            sess.pending_host[0] = pending
+            plan = sess.step(use_graph, feed_pending=True)[0]
             if use_graph and sess.graph is None:
                 sess.capture()
             n = plan[0]

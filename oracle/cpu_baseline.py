@@ -1,0 +1,97 @@
+"""Timed CPU baseline: plain greedy decode of the W8 Qwen3 target on the host cores.
+TEST / BENCHMARK INFRASTRUCTURE ONLY (bench.py's cpu_baseline leg and --impl reference).
+
+The reference's MLX CPU backend cannot run here (mlx is not installed), so this is the
+oracle port of greedy_generate's per-token work (src/mlx_dspark/generate.py:433-450: one
+target forward of one token over the KV cache, then argmax), written for speed on CPU:
+weights stay int8 + bf16 scale/bias and are dequantized on the fly per linear, in row
+chunks that stay in cache; math is fp32 with the oracle's bf16 rounding points.
+"""
+from __future__ import annotations
+
+import os
+import time
+
+import torch
+
+from .qwen3 import F32, bf, inv_freq, rms_norm, rope, silu
+
+
+class StreamingDecoder:
+    """One-token decode of a TargetWeights on the CPU with a dense per-layer KV cache."""
+
+    def __init__(self, w, max_ctx: int, threads: int | None = None, chunk_rows: int = 2048):
+        self.w, self.cfg = w, w.cfg
+        self.threads = threads or os.cpu_count() or 1
+        torch.set_num_threads(self.threads)
+        c = self.cfg
+        self.freqs = inv_freq(c.head_dim, c.rope_theta)
+        self.chunk = chunk_rows
+        L, Hkv, hd = c.num_hidden_layers, c.num_key_value_heads, c.head_dim
+        self.K = torch.zeros(L, Hkv, max_ctx, hd)
+        self.V = torch.zeros(L, Hkv, max_ctx, hd)
+        self.len = 0
+
+    def fill_random_context(self, n: int, seed: int = 0) -> None:
+        """Stand-in context of n positions (timing sample: the attention work of a real
+        context of that length, without paying for a CPU prefill)."""
+        g = torch.Generator().manual_seed(seed)
+        self.K[:, :, :n].normal_(0, 1, generator=g)
+        self.V[:, :, :n].normal_(0, 1, generator=g)
+        self.len = n
+
+    def _lin(self, x, qt):
+        N, K = qt.q.shape
+        out = torch.empty(N, dtype=F32)
+        for r0 in range(0, N, self.chunk):
+            r1 = min(N, r0 + self.chunk)
+            w = qt.q[r0:r1].to(F32).view(r1 - r0, K // 64, 64)
+            w.mul_(qt.scales[r0:r1].to(F32)[..., None]).add_(qt.biases[r0:r1].to(F32)[..., None])
+            out[r0:r1] = w.view(r1 - r0, K) @ x
+        return bf(out)
+
+    def step(self, token: int) -> int:
+        c, W = self.cfg, self.w
+        e = W.embed
+        h = bf(e.scales[token].to(F32).repeat_interleave(64) * e.q[token].to(F32)
+               + e.biases[token].to(F32).repeat_interleave(64))
+        pos = self.len
+        p = torch.tensor([pos])
+        for i, L in enumerate(W.layers):
+            x = rms_norm(h, L.input_ln, c.rms_norm_eps)
+            q = self._lin(x, L.wq).view(c.num_attention_heads, 1, c.head_dim)
+            k = self._lin(x, L.wk).view(c.num_key_value_heads, 1, c.head_dim)
+            v = self._lin(x, L.wv).view(c.num_key_value_heads, 1, c.head_dim)
+            q = rope(rms_norm(q, L.q_norm, c.rms_norm_eps), p, self.freqs)
+            k = rope(rms_norm(k, L.k_norm, c.rms_norm_eps), p, self.freqs)
+            self.K[i, :, pos] = k[:, 0]
+            self.V[i, :, pos] = v[:, 0]
+            rep = c.num_attention_heads // c.num_key_value_heads
+            Kc = self.K[i, :, :pos + 1].repeat_interleave(rep, 0)
+            Vc = self.V[i, :, :pos + 1].repeat_interleave(rep, 0)
+            s = (q @ Kc.transpose(1, 2)) * c.head_dim ** -0.5
+            a = bf(torch.softmax(s, -1) @ Vc).reshape(-1)
+            h = bf(h + self._lin(a, L.wo))
+            x = rms_norm(h, L.post_ln, c.rms_norm_eps)
+            act = bf(bf(silu(self._lin(x, L.gate))) * self._lin(x, L.up))
+            h = bf(h + self._lin(act, L.down))
+        hn = rms_norm(h, W.norm, c.rms_norm_eps)
+        logits = self._lin(hn, W.head)
+        self.len += 1
+        return int(logits.argmax())
+
+
+def time_greedy_decode(w, context: int, budget_s: float = 20.0, min_steps: int = 1,
+                       max_steps: int = 64, threads: int | None = None):
+    """Decode until the time budget is spent; returns (tokens_per_s, steps, seconds, threads)."""
+    dec = StreamingDecoder(w, context + max_steps + 1, threads)
+    dec.fill_random_context(context)
+    tok = 1
+    tok = dec.step(tok)  # untimed warm-up (allocator, thread pool)
+    t0 = time.perf_counter()
+    n = 0
+    while n < max_steps and (n < min_steps or time.perf_counter() - t0 < budget_s):
+        tok = dec.step(tok)
+        n += 1
+    dt = time.perf_counter() - t0
+    return n / dt, n, dt, dec.threads
