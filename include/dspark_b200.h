@@ -151,7 +151,9 @@ int dspark_qkv_rope_kv_write(const void* qkv, int ldqkv, int B, int T, int Hq, i
  *   causal = 0: every query sees every key              (drafter block attention,
  *               model.py:258-283, dflash_model.py:100-134)
  * q   : bf16 [B*T, Hq*hd]; out: fp16 [B*T, ldo] (bf16-rounded, the o_proj GEMM input)
- * workspace: dspark_attention_workspace_bytes(...), zero-filled once before first use.
+ * workspace: dspark_attention_workspace_bytes(...) bytes for the split partials. When the
+ * context spans more than one page (one page per split, at most max_splits) a second
+ * launch merges the partials; with one split the first launch writes the output directly.
  * ------------------------------------------------------------------------------------- */
 size_t dspark_attention_workspace_bytes(int B, int T, int Hq, int Hkv, int hd, int max_splits);
 int dspark_attention(const void* q, int B, int T, int Hq, const dspark_kv_layout* kv,

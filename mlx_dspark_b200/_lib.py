@@ -87,7 +87,8 @@ def check(rc: int, what: str) -> None:
 # kernel launches issued through call() (graph replays re-run them without Python)
 LAUNCHES = {"n": 0}
 _KERNELS_PER_CALL = {"dspark_markov_sample_block": lambda a: int(a[4]),
-                     "dspark_draft_override": lambda a: 2}
+                     "dspark_draft_override": lambda a: 2,
+                     "dspark_attention": lambda a: 2 if int(a[10]) > 1 else 1}
 
 
 def call(name: str, *args) -> None:

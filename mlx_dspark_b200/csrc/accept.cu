@@ -47,15 +47,17 @@ __global__ void __launch_bounds__(kThreads) accept_greedy_kernel(
   const int chunk = ((V + gridDim.x - 1) / gridDim.x + 7) & ~7;
   const int v0 = blockIdx.x * chunk;
   const int v1 = min(V, v0 + chunk);
-  __shared__ Best red[kThreads / 32];
   __shared__ int is_last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int r = 0; r < rows; ++r) {
+  constexpr int kWarps = kThreads / 32;
+  // one warp per row (rows strided over the warps), no block barrier in the scan: every
+  // lane's loads of a row are independent, so a row costs about one memory round trip
+  for (int r = warp; r < rows; r += kWarps) {
     const __nv_bfloat16* row = logits + (size_t)r * ld;
     Best b{-INFINITY, 0x7fffffff};
-    for (int v = v0 + threadIdx.x * 8; v < v1; v += kThreads * 8) {
+    for (int v = v0 + lane * 8; v < v1; v += 32 * 8) {
       if (v + 8 <= v1 && ((ld & 7) == 0)) {
-        const uint4 u = *reinterpret_cast<const uint4*>(row + v);
+        const uint4 u = __ldg(reinterpret_cast<const uint4*>(row + v));
         const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
 #pragma unroll
         for (int j = 0; j < 8; ++j) b = better(b, Best{__bfloat162float(e[j]), v + j});
@@ -64,29 +66,29 @@ __global__ void __launch_bounds__(kThreads) accept_greedy_kernel(
       }
     }
     b = warp_best(b);
-    if (lane == 0) red[warp] = b;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      Best t = red[0];
-      for (int w = 1; w < kThreads / 32; ++w) t = better(t, red[w]);
-      part_v[(size_t)blockIdx.x * rows + r] = t.v;
-      part_i[(size_t)blockIdx.x * rows + r] = t.i;
+    if (lane == 0) {
+      part_v[(size_t)blockIdx.x * rows + r] = b.v;
+      part_i[(size_t)blockIdx.x * rows + r] = b.i;
     }
-    __syncthreads();
   }
   __threadfence();
+  __syncthreads();
   if (threadIdx.x == 0) is_last = (atomicAdd(counter, 1) == (int)gridDim.x - 1);
   __syncthreads();
   if (!is_last) return;
   __threadfence();
   __shared__ int tt[64];
-  for (int r = threadIdx.x; r < rows; r += kThreads) {
+  // final reduction: a warp per row, lanes over the CTAs' partials (all loads in flight)
+  for (int r = warp; r < rows; r += kWarps) {
     Best t{-INFINITY, 0x7fffffff};
-    for (int c = 0; c < (int)gridDim.x; ++c)
+    for (int c = lane; c < (int)gridDim.x; c += 32)
       t = better(t, Best{__ldcg(part_v + (size_t)c * rows + r), __ldcg(part_i + (size_t)c * rows + r)});
-    if (t.i == 0x7fffffff) t.i = 0;  // all-NaN row
-    tt[r] = t.i;
-    argmax_out[r] = t.i;
+    t = warp_best(t);
+    if (lane == 0) {
+      if (t.i == 0x7fffffff) t.i = 0;  // all-NaN row
+      tt[r] = t.i;
+      argmax_out[r] = t.i;
+    }
   }
   __syncthreads();
   for (int b = threadIdx.x; b < B; b += kThreads) {

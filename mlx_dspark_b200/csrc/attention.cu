@@ -20,7 +20,7 @@ namespace dspark {
 namespace attn {
 
 constexpr int KT = 64;  // keys per tile == page size
-constexpr int kMinPagesPerSplit = 4;
+constexpr int kMinPagesPerSplit = 1;  // a split is at least this many pages
 
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
@@ -281,11 +281,24 @@ __global__ void __launch_bounds__(256) attn_kernel(const Args a) {
   }
   cp_wait<0>();
 
-  // per-split partials
   l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
   l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
   l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
   l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  if (nsplit == 1) {
+    // the whole context in one CTA: normalise and write the output directly
+    const float inv0 = l0 > 0.0f ? 1.0f / l0 : 0.0f, inv1 = l1 > 0.0f ? 1.0f / l1 : 0.0f;
+    __half* d0 = r0 < a.R ? a.out + (size_t)(b * a.T + r0 % a.T) * a.ldo + (size_t)(h * a.G + r0 / a.T) * HD : nullptr;
+    __half* d1 = r1 < a.R ? a.out + (size_t)(b * a.T + r1 % a.T) * a.ldo + (size_t)(h * a.G + r1 / a.T) * HD : nullptr;
+#pragma unroll
+    for (int j = 0; j < HD / 8; ++j) {
+      const int d = j * 8 + (lane & 3) * 2;
+      if (d0) *reinterpret_cast<__half2*>(d0 + d) = __floats2half2_rn(bf16_round(o[j][0] * inv0), bf16_round(o[j][1] * inv0));
+      if (d1) *reinterpret_cast<__half2*>(d1 + d) = __floats2half2_rn(bf16_round(o[j][2] * inv1), bf16_round(o[j][3] * inv1));
+    }
+    return;
+  }
+  // per-split partials (unnormalised O, running max, running sum); attn_combine_kernel merges
   const int bh = b * Hkv + h;
   const size_t sbase = ((size_t)bh * a.nsplit + split) * a.R;
   if ((lane & 3) == 0) {
@@ -298,51 +311,63 @@ __global__ void __launch_bounds__(256) attn_kernel(const Args a) {
     if (r0 < a.R) *reinterpret_cast<float2*>(a.ws_o + (sbase + r0) * HD + d) = make_float2(o[j][0], o[j][1]);
     if (r1 < a.R) *reinterpret_cast<float2*>(a.ws_o + (sbase + r1) * HD + d) = make_float2(o[j][2], o[j][3]);
   }
-  __threadfence();
-  __syncthreads();
-  int* flag = reinterpret_cast<int*>(smem + 2 * L::kBuf);
-  if (threadIdx.x == 0) {
-    const int old = atomicAdd(a.counters + bh, 1);
-    *flag = (old == nsplit - 1);
-  }
-  __syncthreads();
-  if (!*flag) return;
-  __threadfence();
-  // merge: weights w[s][r] = exp2(m_s - M_r) / sum_s l_s exp2(m_s - M_r)
-  float* wgt = reinterpret_cast<float*>(smem);  // [nsplit][R] (tiles are free now)
+}
+
+// Merge of the split partials: one warp per query row (8 rows per CTA), every (row, kv head,
+// batch row) in parallel. Lanes range over the splits for the max and the softmax sum, and
+// over the head dimension for O, whose splits are summed in split order.
+template <int HD>
+__global__ void __launch_bounds__(256) attn_combine_kernel(const Args a) {
+  pdl_wait();
+  pdl_launch_dependents();
+  constexpr int E = HD / 32;  // output dims per lane
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int kvlen = a.kv_len[b];
+  const int npages = (kvlen + a.T + KT - 1) / KT;
+  const int nsplit = min(a.nsplit, (npages + kMinPagesPerSplit - 1) / kMinPagesPerSplit);
+  if (nsplit <= 1) return;  // the attention kernel already wrote this output
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = blockIdx.x * 8 + warp;
+  if (r >= a.R) return;
+  const int bh = b * a.kv.num_kv_heads + h;
   const size_t base0 = (size_t)bh * a.nsplit * a.R;
-  for (int r = threadIdx.x; r < a.R; r += blockDim.x) {
-    float M = -INFINITY;
-    for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, __ldcg(a.ws_ml + (base0 + (size_t)sp * a.R + r) * 2));
-    float Ls = 0.0f;
-    for (int sp = 0; sp < nsplit; ++sp) {
-      const float ms = __ldcg(a.ws_ml + (base0 + (size_t)sp * a.R + r) * 2);
-      const float ls = __ldcg(a.ws_ml + (base0 + (size_t)sp * a.R + r) * 2 + 1);
-      const float e = (ms == -INFINITY) ? 0.0f : exp2f(ms - M);
-      wgt[sp * a.R + r] = e;
-      Ls += ls * e;
-    }
-    const float inv = Ls > 0.0f ? 1.0f / Ls : 0.0f;
-    for (int sp = 0; sp < nsplit; ++sp) wgt[sp * a.R + r] *= inv;
+  float M = -INFINITY;
+  for (int sp = lane; sp < nsplit; sp += 32)
+    M = fmaxf(M, __ldcg(a.ws_ml + (base0 + (size_t)sp * a.R + r) * 2));
+  M = warp_max(M);
+  float Ls = 0.0f;
+  for (int sp = lane; sp < nsplit; sp += 32) {
+    const float ms = __ldcg(a.ws_ml + (base0 + (size_t)sp * a.R + r) * 2);
+    if (ms != -INFINITY) Ls += __ldcg(a.ws_ml + (base0 + (size_t)sp * a.R + r) * 2 + 1) * exp2f(ms - M);
   }
-  __syncthreads();
-  for (int i = threadIdx.x; i < a.R * (HD / 4); i += blockDim.x) {
-    const int r = i / (HD / 4), d = (i - r * (HD / 4)) * 4;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int sp = 0; sp < nsplit; ++sp) {
-      const float w = wgt[sp * a.R + r];
-      if (w == 0.0f) continue;
-      const float4 v = __ldcg(reinterpret_cast<const float4*>(a.ws_o + (base0 + (size_t)sp * a.R + r) * HD + d));
-      acc.x += w * v.x; acc.y += w * v.y; acc.z += w * v.z; acc.w += w * v.w;
+  Ls = warp_sum(Ls);
+  float acc[E];
+#pragma unroll
+  for (int k = 0; k < E; ++k) acc[k] = 0.0f;
+#pragma unroll 4
+  for (int sp = 0; sp < nsplit; ++sp) {
+    const size_t row = base0 + (size_t)sp * a.R + r;
+    const float ms = __ldcg(a.ws_ml + row * 2);
+    const float e = ms == -INFINITY ? 0.0f : exp2f(ms - M);  // empty splits hold zeros
+    const float* src = a.ws_o + row * HD + lane * E;
+    float v[E];
+    if constexpr (E == 4) {
+      const float4 t = __ldcg(reinterpret_cast<const float4*>(src));
+      v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+    } else {
+      const float2 t = __ldcg(reinterpret_cast<const float2*>(src));
+      v[0] = t.x; v[1] = t.y;
     }
-    const int t = r % a.T, g = r / a.T;
-    __half* dst = a.out + (size_t)(b * a.T + t) * a.ldo + (size_t)(h * a.G + g) * HD + d;
-    dst[0] = __float2half_rn(bf16_round(acc.x));
-    dst[1] = __float2half_rn(bf16_round(acc.y));
-    dst[2] = __float2half_rn(bf16_round(acc.z));
-    dst[3] = __float2half_rn(bf16_round(acc.w));
+#pragma unroll
+    for (int k = 0; k < E; ++k) acc[k] = fmaf(e, v[k], acc[k]);
   }
-  if (threadIdx.x == 0) a.counters[bh] = 0;
+  const float inv = Ls > 0.0f ? 1.0f / Ls : 0.0f;
+  const int t = r % a.T, g = r / a.T;
+  __half* dst = a.out + (size_t)(b * a.T + t) * a.ldo + (size_t)(h * a.G + g) * HD + lane * E;
+#pragma unroll
+  for (int k = 0; k < E; k += 2)
+    *reinterpret_cast<__half2*>(dst + k) =
+        __floats2half2_rn(bf16_round(acc[k] * inv), bf16_round(acc[k + 1] * inv));
 }
 
 static size_t ws_layout(int B, int T, int Hq, int Hkv, int hd, int nsplit, size_t* off_ml,
@@ -405,19 +430,18 @@ extern "C" int dspark_attention(const void* q, int B, int T, int Hq, const dspar
   const int warps = (R + 15) / 16;
   const dim3 grid(max_splits, Hkv, B), block(warps * 32);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  auto go = [&](auto kern, int smem) {
-    static thread_local int configured_for = -1;
-    (void)configured_for;
+  auto go = [&](auto kern, auto combine, int smem) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
       return set_error(DSPARK_ERR_CUDA, "attention: cudaFuncSetAttribute failed");
-    return launch_pdl("attention", kern, grid, block, (size_t)smem, st, a);
+    int rc = launch_pdl("attention", kern, grid, block, (size_t)smem, st, a);
+    if (rc || max_splits == 1) return rc;
+    return launch_pdl("attention.combine", combine, dim3((R + 7) / 8, Hkv, B), dim3(256), 0, st, a);
   };
-  // merge scratch reuses the tile buffers: nsplit * R floats must fit
-  auto need_smem = [&](int tile_bytes) { return std::max(tile_bytes, max_splits * R * 4 + 16); };
+  using namespace attn;
   if (hd == 128) {
-    if (kv->kv8) return go(attn::attn_kernel<128, true>, need_smem(attn::Layout<128, true>::kBytes));
-    return go(attn::attn_kernel<128, false>, need_smem(attn::Layout<128, false>::kBytes));
+    if (kv->kv8) return go(attn_kernel<128, true>, attn_combine_kernel<128>, Layout<128, true>::kBytes);
+    return go(attn_kernel<128, false>, attn_combine_kernel<128>, Layout<128, false>::kBytes);
   }
-  if (kv->kv8) return go(attn::attn_kernel<64, true>, need_smem(attn::Layout<64, true>::kBytes));
-  return go(attn::attn_kernel<64, false>, need_smem(attn::Layout<64, false>::kBytes));
+  if (kv->kv8) return go(attn_kernel<64, true>, attn_combine_kernel<64>, Layout<64, true>::kBytes);
+  return go(attn_kernel<64, false>, attn_combine_kernel<64>, Layout<64, false>::kBytes);
 }

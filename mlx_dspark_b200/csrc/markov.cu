@@ -4,10 +4,12 @@
 // _batched_sample_block (src/mlx_dspark/batch_engine.py:414-428), VanillaMarkov
 // (model.py:324-336):
 //   for i in range(cap): logits_i = base_i + w2(w1[prev]); prev = argmax(logits_i)
-// One launch per position i: every CTA computes the Markov bias over a vocabulary slice for
-// all rows (one pass over the W8 w2 matrix, which stays L2-resident across the cap steps),
-// adds the base logits and keeps a per-slice argmax; the last CTA to finish reduces the
-// slices in CTA order and publishes the token that the next launch conditions on.
+// One launch per position i. Each thread owns vocabulary rows: it issues the row's 256 W8
+// bytes as 16 independent 16-byte loads before any arithmetic (memory-level parallelism; the
+// W8 w2 matrix, 41 MB at V = 151936, stays L2-resident across the cap steps), forms the
+// Markov bias for every batch row, adds the base logits and keeps a running argmax. The last
+// CTA to finish reduces the per-CTA results in CTA order and publishes the token that the
+// next launch conditions on.
 // Rounding follows a bf16 model: e = bf16(dequant w1[prev]); bias = bf16(w2 . e);
 // logit = bf16(base + bias); argmax takes the first index of the maximum.
 #include "common.cuh"
@@ -18,6 +20,7 @@ namespace mk {
 constexpr int kThreads = 256;
 constexpr int kMaxB = 8;
 constexpr int kR = 256;  // Markov rank
+constexpr int kG = kR / 64;
 
 struct Best {
   float v;
@@ -28,8 +31,10 @@ __device__ __forceinline__ Best better(Best a, Best b) {
   return a;
 }
 
+// NB == B: the batch width is a template parameter so every per-row loop is exact.
+template <int NB>
 __global__ void __launch_bounds__(kThreads) markov_step_kernel(
-    const __nv_bfloat16* __restrict__ base, int ld, int rows_per_b, int B, int cap, int V, int step,
+    const __nv_bfloat16* __restrict__ base, int ld, int rows_per_b, int cap, int V, int step,
     const uint8_t* __restrict__ w1q, const uint32_t* __restrict__ w1sb,
     const uint8_t* __restrict__ w2q, const uint32_t* __restrict__ w2sb,
     const int32_t* __restrict__ first_prev, int32_t* __restrict__ draft,
@@ -37,12 +42,13 @@ __global__ void __launch_bounds__(kThreads) markov_step_kernel(
     int* __restrict__ counter) {
   pdl_wait();
   pdl_launch_dependents();
-  __shared__ float e[kMaxB][kR];
-  __shared__ Best red[kMaxB][kThreads / 32];
+  __shared__ __align__(16) float e[NB][kR];
+  __shared__ float esum[NB][kG];
+  __shared__ Best red[NB][kThreads / 32];
   __shared__ int is_last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // e_b = bf16(dequant w1[prev_b])
-  for (int idx = threadIdx.x; idx < B * kR; idx += kThreads) {
+  for (int idx = threadIdx.x; idx < NB * kR; idx += kThreads) {
     const int b = idx / kR, r = idx - b * kR;
     int prev = step == 0 ? first_prev[b] : draft[b * cap + step - 1];
     prev = prev < 0 ? 0 : (prev >= V ? V - 1 : prev);
@@ -51,44 +57,87 @@ __global__ void __launch_bounds__(kThreads) markov_step_kernel(
     e[b][r] = bf16_round(fmaf(__low2float(sb), (float)w1q[(size_t)prev * kR + r], __high2float(sb)));
   }
   __syncthreads();
-  const int chunk = (V + gridDim.x - 1) / gridDim.x;
-  const int v0 = blockIdx.x * chunk, v1 = min(V, v0 + chunk);
-  Best best[kMaxB];
+  // w2 . e = sum_g (s_g * sum_{r in g} q_r e_r + b_g * sum_{r in g} e_r)
+  if (threadIdx.x < NB * kG) {
+    const int b = threadIdx.x / kG, g = threadIdx.x % kG;
+    float s = 0.0f;
+    for (int r = 0; r < 64; ++r) s += e[b][g * 64 + r];
+    esum[b][g] = s;
+  }
+  __syncthreads();
+  Best best[NB];
 #pragma unroll
-  for (int b = 0; b < kMaxB; ++b) best[b] = Best{-INFINITY, 0x7fffffff};
-  // one warp per vocabulary row: lane l covers dims [8l, 8l+8) (group l/8)
-  for (int v = v0 + warp; v < v1; v += kThreads / 32) {
-    const uint2 q8 = *reinterpret_cast<const uint2*>(w2q + (size_t)v * kR + lane * 8);
-    const uint32_t sbv = w2sb[(size_t)(lane >> 3) * V + v];
-    const __half2 sb = *reinterpret_cast<const __half2*>(&sbv);
-    const float s = __low2float(sb), bb = __high2float(sb);
-    float w[8];
+  for (int b = 0; b < NB; ++b) best[b] = Best{-INFINITY, 0x7fffffff};
+  const int nthr = gridDim.x * kThreads;
+  for (int v = blockIdx.x * kThreads + threadIdx.x; v < V; v += nthr) {
+    const uint4* rowp = reinterpret_cast<const uint4*>(w2q + (size_t)v * kR);
+    uint4 q[kR / 16];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) w[j] = fmaf(s, (float)(((j < 4 ? q8.x : q8.y) >> (8 * (j & 3))) & 0xFF), bb);
+    for (int j = 0; j < kR / 16; ++j) q[j] = __ldg(rowp + j);
+    uint32_t sbv[kG];
 #pragma unroll
-    for (int b = 0; b < kMaxB; ++b) {
-      if (b >= B) break;
-      float d = 0.0f;
+    for (int g = 0; g < kG; ++g) sbv[g] = __ldg(w2sb + (size_t)g * V + v);
+    float d[NB];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) d += w[j] * e[b][lane * 8 + j];
-      d = warp_sum(d);
+    for (int b = 0; b < NB; ++b) d[b] = 0.0f;
+#pragma unroll
+    for (int g = 0; g < kG; ++g) {
+      float qd[NB];
+#pragma unroll
+      for (int b = 0; b < NB; ++b) qd[b] = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t words[4] = {q[g * 4 + j].x, q[g * 4 + j].y, q[g * 4 + j].z, q[g * 4 + j].w};
+#pragma unroll
+        for (int wi = 0; wi < 4; ++wi) {
+          const int r0 = g * 64 + j * 16 + wi * 4;
+          float ev[NB][4];
+#pragma unroll
+          for (int b = 0; b < NB; ++b) {
+            const float4 t = *reinterpret_cast<const float4*>(&e[b][r0]);
+            ev[b][0] = t.x; ev[b][1] = t.y; ev[b][2] = t.z; ev[b][3] = t.w;
+          }
+#pragma unroll
+          for (int by = 0; by < 4; ++by) {
+            // exact byte -> float: the fp32 bit pattern of 2^23 + q, minus 2^23
+            const float qf =
+                __uint_as_float(__byte_perm(words[wi], 0x4B000000u, 0x7650 + by)) - 8388608.0f;
+#pragma unroll
+            for (int b = 0; b < NB; ++b) qd[b] = fmaf(qf, ev[b][by], qd[b]);
+          }
+        }
+      }
+      const __half2 sb = *reinterpret_cast<const __half2*>(&sbv[g]);
+      const float s = __low2float(sb), bb = __high2float(sb);
+#pragma unroll
+      for (int b = 0; b < NB; ++b) d[b] = fmaf(s, qd[b], fmaf(bb, esum[b][g], d[b]));
+    }
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
       const float logit =
-          bf16_round(__bfloat162float(base[(size_t)(b * rows_per_b + step) * ld + v]) + bf16_round(d));
+          bf16_round(__bfloat162float(base[(size_t)(b * rows_per_b + step) * ld + v]) + bf16_round(d[b]));
       best[b] = better(best[b], Best{logit, v});
     }
   }
 #pragma unroll
-  for (int b = 0; b < kMaxB; ++b) {
-    if (b >= B) break;
-    if (lane == 0) red[b][warp] = best[b];
+  for (int b = 0; b < NB; ++b) {
+    Best t = best[b];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      Best y;
+      y.v = __shfl_xor_sync(0xffffffffu, t.v, o);
+      y.i = __shfl_xor_sync(0xffffffffu, t.i, o);
+      t = better(t, y);
+    }
+    if (lane == 0) red[b][warp] = t;
   }
   __syncthreads();
-  if (threadIdx.x < B) {
+  if (threadIdx.x < NB) {
     const int b = threadIdx.x;
     Best t = red[b][0];
     for (int w = 1; w < kThreads / 32; ++w) t = better(t, red[b][w]);
-    part_v[(size_t)blockIdx.x * B + b] = t.v;
-    part_i[(size_t)blockIdx.x * B + b] = t.i;
+    part_v[(size_t)blockIdx.x * NB + b] = t.v;
+    part_i[(size_t)blockIdx.x * NB + b] = t.i;
   }
   __threadfence();
   __syncthreads();
@@ -96,24 +145,36 @@ __global__ void __launch_bounds__(kThreads) markov_step_kernel(
   __syncthreads();
   if (!is_last) return;
   __threadfence();
-  if (threadIdx.x < B) {
-    const int b = threadIdx.x;
+  // final reduction: warp b per batch row, lanes over the CTAs' partials (loads in flight
+  // together); the (max value, min index) order makes the result independent of grouping
+  if (warp < NB) {
+    const int b = warp;
     Best t{-INFINITY, 0x7fffffff};
-    for (int c = 0; c < (int)gridDim.x; ++c)
-      t = better(t, Best{__ldcg(part_v + (size_t)c * B + b), __ldcg(part_i + (size_t)c * B + b)});
-    if (t.i == 0x7fffffff) t.i = 0;
-    draft[b * cap + step] = t.i;
-    if (verify_ids) {
-      if (step == 0) verify_ids[b * (cap + 1)] = first_prev[b];
-      verify_ids[b * (cap + 1) + 1 + step] = t.i;
+    for (int c = lane; c < (int)gridDim.x; c += 32)
+      t = better(t, Best{__ldcg(part_v + (size_t)c * NB + b), __ldcg(part_i + (size_t)c * NB + b)});
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      Best y;
+      y.v = __shfl_xor_sync(0xffffffffu, t.v, o);
+      y.i = __shfl_xor_sync(0xffffffffu, t.i, o);
+      t = better(t, y);
+    }
+    if (lane == 0) {
+      if (t.i == 0x7fffffff) t.i = 0;
+      draft[b * cap + step] = t.i;
+      if (verify_ids) {
+        if (step == 0) verify_ids[b * (cap + 1)] = first_prev[b];
+        verify_ids[b * (cap + 1) + 1 + step] = t.i;
+      }
     }
   }
   if (threadIdx.x == 0) *counter = 0;
 }
 
 static size_t ws(int B, int V, int* grid_out, size_t* off_i, size_t* off_c) {
-  int grid = 2 * 148;
-  if (V / grid < 64) grid = (V + 63) / 64;
+  // one thread per vocabulary row, two rows per thread
+  int grid = (V + 2 * kThreads - 1) / (2 * kThreads);
+  if (grid < 1) grid = 1;
   if (grid_out) *grid_out = grid;
   // counter word first (fixed offset for every shape), then the two partial arrays
   const size_t pv = (((size_t)grid * B * 4) + 255) & ~(size_t)255;
@@ -153,12 +214,25 @@ extern "C" int dspark_markov_sample_block(const void* base, int ld, int rows_per
     return set_error(DSPARK_ERR_WORKSPACE, "markov_sample_block: workspace %zu < %zu", workspace_bytes, need);
   uint8_t* w = static_cast<uint8_t*>(workspace);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  for (int i = 0; i < cap; ++i) {
-    int rc = launch_pdl("markov_step", mk::markov_step_kernel, dim3(grid), dim3(mk::kThreads), 0, st,
-                        static_cast<const __nv_bfloat16*>(base), ld, rows_per_b, B, cap, V, i, w1q, w1sb, w2q,
-                        w2sb, first_prev, draft, verify_ids, reinterpret_cast<float*>(w + off_c),
-                        reinterpret_cast<int*>(w + off_i), reinterpret_cast<int*>(w));
-    if (rc) return rc;
+  auto run = [&](auto kern) {
+    for (int i = 0; i < cap; ++i) {
+      int rc = launch_pdl("markov_step", kern, dim3(grid), dim3(mk::kThreads), 0, st,
+                          static_cast<const __nv_bfloat16*>(base), ld, rows_per_b, cap, V, i,
+                          w1q, w1sb, w2q, w2sb, first_prev, draft, verify_ids,
+                          reinterpret_cast<float*>(w + off_c), reinterpret_cast<int*>(w + off_i),
+                          reinterpret_cast<int*>(w));
+      if (rc) return rc;
+    }
+    return (int)DSPARK_OK;
+  };
+  switch (B) {
+    case 1: return run(mk::markov_step_kernel<1>);
+    case 2: return run(mk::markov_step_kernel<2>);
+    case 3: return run(mk::markov_step_kernel<3>);
+    case 4: return run(mk::markov_step_kernel<4>);
+    case 5: return run(mk::markov_step_kernel<5>);
+    case 6: return run(mk::markov_step_kernel<6>);
+    case 7: return run(mk::markov_step_kernel<7>);
+    default: return run(mk::markov_step_kernel<8>);
   }
-  return DSPARK_OK;
 }

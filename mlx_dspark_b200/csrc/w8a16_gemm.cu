@@ -387,33 +387,60 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 ? 2 : 1))
       if (whole) {
         epilogue_store<BN>(p, tile, er, acc, xch);
       } else {
+        // partial of this CTA: row er's BN values contiguous, so the finishing CTA reads one
+        // run of BN floats per contributor with 16-byte loads
         const int slot = (int)blockIdx.x * 2 + (seg == 0 ? 0 : 1);
-        float* part = p.partials + (size_t)slot * BN * BM;
+        float4* part = reinterpret_cast<float4*>(p.partials + (size_t)slot * BN * BM + er * BN);
 #pragma unroll
-        for (int m = 0; m < BN; ++m)
-          if (m < p.M) part[m * BM + er] = acc[m];
-        __threadfence();
+        for (int j = 0; j < BN / 4; ++j)
+          part[j] = make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
         asm volatile("bar.sync 1, 128;" ::: "memory");
         const long long c_lo = range_owner(tile_lo, total, G);
         const long long c_hi = range_owner(tile_lo + KB - 1, total, G);
         if (er == 0) {
           const int contributors = (int)(c_hi - c_lo + 1);
-          const int old = atomicAdd(p.counters + tile, 1);
+          // One acq_rel gpu-scope atomic per CTA. Release: the partials of all 128 threads
+          // (ordered before it by the barrier; release is cumulative) are visible to whoever
+          // reads the final count. Acquire: the last arriver sees every partial.
+          int old;
+          asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;"
+                       : "=r"(old)
+                       : "l"(p.counters + tile)
+                       : "memory");
           *last_flag = (old == contributors - 1) ? 1 : 0;
         }
         asm volatile("bar.sync 1, 128;" ::: "memory");
         const int is_last = *last_flag;
         if (is_last) {
-          __threadfence();
           float sum[BN];
 #pragma unroll
           for (int m = 0; m < BN; ++m) sum[m] = 0.0f;
-          for (long long c = c_lo; c <= c_hi; ++c) {
-            const int cj = (range_start(c, total, G) >= tile_lo) ? 0 : 1;
-            const float* cp = p.partials + ((size_t)c * 2 + cj) * BN * BM;
+          // U contributors' loads in flight at once; the sum stays in contributor order
+          constexpr int U = BN <= 16 ? 2 : 1;
+          for (long long c = c_lo; c <= c_hi; c += U) {
+            float4 t[U][BN / 4];
 #pragma unroll
-            for (int m = 0; m < BN; ++m)
-              if (m < p.M) sum[m] += __ldcg(cp + m * BM + er);
+            for (int u = 0; u < U; ++u) {
+              if (c + u <= c_hi) {
+                const int cj = (range_start(c + u, total, G) >= tile_lo) ? 0 : 1;
+                const float4* cp = reinterpret_cast<const float4*>(
+                    p.partials + ((size_t)(c + u) * 2 + cj) * BN * BM + er * BN);
+#pragma unroll
+                for (int j = 0; j < BN / 4; ++j) t[u][j] = __ldcg(cp + j);
+              }
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+              if (c + u <= c_hi) {
+#pragma unroll
+                for (int j = 0; j < BN / 4; ++j) {
+                  sum[4 * j] += t[u][j].x;
+                  sum[4 * j + 1] += t[u][j].y;
+                  sum[4 * j + 2] += t[u][j].z;
+                  sum[4 * j + 3] += t[u][j].w;
+                }
+              }
+            }
           }
           if (er == 0) p.counters[tile] = 0;
           epilogue_store<BN>(p, tile, er, sum, xch);
@@ -520,9 +547,12 @@ static int make_map_2d(CUtensorMap* map, CUtensorMapDataType dt, int elem_bytes,
 }
 
 static int sm_count() {
+  static int cached = 0;
+  if (cached) return cached;
   int dev = 0, n = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  if (n > 0) cached = n;
   return n > 0 ? n : 148;
 }
 
