@@ -180,6 +180,23 @@ int dspark_accept_greedy(const void* logits, int ld, int B, int T, int V,
                          int commit, int32_t* pending, int32_t* plan, void* workspace,
                          size_t workspace_bytes, dspark_stream_t stream);
 
+/* The same greedy acceptance for callers that may not allocate device memory: hosts that
+ * hand the library only their input and output buffers, such as a serving process whose
+ * device memory pool is fixed at start-up or a binding from another language with no handle
+ * on the process's allocator. It has no counterpart in the reference (the reference never
+ * manages device memory itself). The kernel's scratch lives in a fixed array inside the
+ * library (about 74 KB per GPU that loads the library, held until the process exits), so:
+ *   - at most 64 rows (B * T <= 64); larger calls return DSPARK_ERR_UNSUPPORTED;
+ *   - every call on a device shares that array: calls that overlap on the GPU (on two
+ *     streams at once) race, so order them on one stream;
+ *   - the first call on a device looks the array's address up (cudaGetSymbolAddress); make
+ *     that first call before any stream capture.
+ * It allocates nothing; arguments and results are those of dspark_accept_greedy. */
+int dspark_accept_greedy_noalloc(const void* logits, int ld, int B, int T, int V,
+                                 const int32_t* verify_ids, int32_t* argmax, int32_t* kv_len,
+                                 int commit, int32_t* pending, int32_t* plan,
+                                 dspark_stream_t stream);
+
 /* -------------------------------------------------------------------------------------
  * K10 — DSpark Markov head + greedy block sampling: sequential over cap positions,
  *   logits_i = base_i + w2 . w1[prev];  prev = argmax(logits_i)   (first index on ties)

@@ -51,6 +51,7 @@ SIGNATURES = {
                              c_size_t, P, P]),
     "dspark_accept_workspace_bytes": (c_size_t, [I, I]),
     "dspark_accept_greedy": (I, [P, I, I, I, I, P, P, P, I, P, P, P, c_size_t, P]),
+    "dspark_accept_greedy_noalloc": (I, [P, I, I, I, I, P, P, P, I, P, P, P]),
     "dspark_commit_lengths": (I, [P, I, I, P, P, P]),
     "dspark_draft_override": (I, [I, I, I, P, I, P, I, P, P, P, P, P]),
     "dspark_markov_workspace_bytes": (c_size_t, [I, I]),

@@ -6,6 +6,8 @@
 //   committed = draft[:n] + [tt[n]];  cache.trim(len(draft) - n)
 // The verify block already wrote K/V for all T positions; keeping n + 1 of them is a length
 // update (kv_len += n + 1), so commit and rollback are O(1) on the device.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace dspark {
@@ -185,6 +187,89 @@ extern "C" int dspark_accept_greedy(const void* logits, int ld, int B, int T, in
   return launch_pdl("accept_greedy", acc::accept_greedy_kernel, dim3(grid), dim3(acc::kThreads), 0,
                     static_cast<cudaStream_t>(stream), static_cast<const __nv_bfloat16*>(logits),
                     ld, B, T, V, verify_ids, argmax, kv_len, commit, pending, plan,
+                    reinterpret_cast<float*>(w + off_c), reinterpret_cast<int*>(w + off_i),
+                    reinterpret_cast<int*>(w));
+}
+
+// ------------------------------------------------------------------------------------------
+// Allocation-free variant of dspark_accept_greedy.
+//
+// For callers that are handed only their input and output buffers and may not allocate
+// device memory themselves: a serving process whose device memory pool is fixed when it
+// starts, or a binding from another language that has no handle on the process's allocator.
+// The kernel's scratch (one counter word and the per-CTA partial argmaxes) lives in a
+// file-scope device array instead of a caller-provided workspace. Its size serves up to
+// kStaticRows verify rows with the kStaticGrid-CTA vocabulary split, about 74 KB, held by
+// every GPU that loads this library until the process exits.
+//
+// The array is shared by every call on a device and keeps the last call's contents: the
+// counter is cleared on the stream before each launch, and calls that overlap on the GPU (two
+// streams at once) race on it. The first call on a device looks the array's device address
+// up with cudaGetSymbolAddress (in host code the array's name is only a host-side stand-in),
+// so that first call should come before any stream capture.
+namespace dspark {
+namespace acc {
+constexpr int kStaticRows = 64;   // same row limit as the workspace entry point
+constexpr int kStaticGrid = 148;  // ws() never splits the vocabulary over more CTAs
+constexpr size_t kStaticScratchBytes =
+    256 + 2 * ((((size_t)kStaticGrid * kStaticRows * 4) + 255) & ~(size_t)255);
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+}  // namespace acc
+}  // namespace dspark
+
+static std::mutex g_static_scratch_mu;
+static void* g_static_scratch_ptr[128] = {};
+
+static int static_scratch_address(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess)
+    return set_error(DSPARK_ERR_CUDA, "accept_greedy_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= 128) return set_error(DSPARK_ERR_UNSUPPORTED, "accept_greedy_noalloc: device %d", dev);
+  std::lock_guard<std::mutex> lock(g_static_scratch_mu);
+  if (!g_static_scratch_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, acc::g_static_scratch);
+    if (e != cudaSuccess || !p)
+      return set_error(DSPARK_ERR_CUDA, "accept_greedy_noalloc: cudaGetSymbolAddress: %s",
+                       cudaGetErrorString(e));
+    g_static_scratch_ptr[dev] = p;
+  }
+  *out = g_static_scratch_ptr[dev];
+  return DSPARK_OK;
+}
+
+extern "C" int dspark_accept_greedy_noalloc(const void* logits, int ld, int B, int T, int V,
+                                            const int32_t* verify_ids, int32_t* argmax,
+                                            int32_t* kv_len, int commit, int32_t* pending,
+                                            int32_t* plan, dspark_stream_t stream) {
+  if (!logits || !verify_ids || !argmax || !pending || !plan || B <= 0 || T <= 0 || V <= 0 || ld < V)
+    return set_error(DSPARK_ERR_INVALID, "accept_greedy_noalloc: bad arguments");
+  if (commit && !kv_len)
+    return set_error(DSPARK_ERR_INVALID, "accept_greedy_noalloc: commit without kv_len");
+  if (B * T > acc::kStaticRows)
+    return set_error(DSPARK_ERR_UNSUPPORTED,
+                     "accept_greedy_noalloc: %d rows exceed the fixed scratch limit of %d rows",
+                     B * T, acc::kStaticRows);
+  int grid;
+  size_t off_i, off_c;
+  const size_t need = acc::ws(B * T, V, &grid, &off_i, &off_c);
+  if (grid > acc::kStaticGrid || need > acc::kStaticScratchBytes)
+    return set_error(DSPARK_ERR_UNSUPPORTED,
+                     "accept_greedy_noalloc: needs %zu scratch bytes, the fixed scratch holds %zu",
+                     need, acc::kStaticScratchBytes);
+  void* base = nullptr;
+  int rc = static_scratch_address(&base);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(base, 0, sizeof(int), st);  // the arrival counter
+  if (e != cudaSuccess)
+    return set_error(DSPARK_ERR_CUDA, "accept_greedy_noalloc: clearing the counter: %s",
+                     cudaGetErrorString(e));
+  uint8_t* w = static_cast<uint8_t*>(base);
+  return launch_pdl("accept_greedy_noalloc", acc::accept_greedy_kernel, dim3(grid),
+                    dim3(acc::kThreads), 0, st, static_cast<const __nv_bfloat16*>(logits), ld, B,
+                    T, V, verify_ids, argmax, kv_len, commit, pending, plan,
                     reinterpret_cast<float*>(w + off_c), reinterpret_cast<int*>(w + off_i),
                     reinterpret_cast<int*>(w));
 }
