@@ -217,6 +217,67 @@ int dspark_markov_sample_block(const void* base, int ld, int rows_per_b, int B, 
                                int* status, dspark_stream_t stream);
 
 /* -------------------------------------------------------------------------------------
+ * K9 — lossless speculative sampling.
+ *
+ * Distribution of a row: p = truncate(softmax(x)), x = bf16(logits / bf16(T)) (temp_mode 0,
+ * the `v_logits / temperature` of generate.py:673,543) or bf16(logits * bf16(1/T))
+ * (temp_mode 1, the `logits * inv_t` of model.py:300). Top-k keeps values >= the k-th largest
+ * (ties kept); the nucleus keeps values >= the smallest value whose strictly-larger mass is
+ * below top_p (src/mlx_dspark/sampling.py:18-44). top_k = 0 and top_p = 1 disable the cuts.
+ * Weights are 2^-40 fixed point of a documented exp2 polynomial; every draw is an inverse-CDF
+ * draw in vocabulary order from a Philox4x32-10 word, so a CPU restatement reproduces each
+ * token exactly.
+ * rng: device {seed, offset} pair per group (per request); counter = {offset, row, stream}.
+ * ------------------------------------------------------------------------------------- */
+
+/* Draw one token per row from p (sample_probs, sampling.py:47-49; the first token _pick,
+ * generate.py:144-146; the DFlash draft, generate.py:541-545).
+ * logits: bf16 rows; row r of group g is row (g * rows + r) at stride ld
+ * probs (optional): fp32 out, the truncated distribution of each row (the q the accept
+ *   test needs), row (g * rows + r) at stride ld_probs
+ * tokens: out, row (g * rows + r) at tokens[(g * rows + r) * tok_stride]; tokens2 an
+ *   optional second copy. Philox counter row = row_base + r, stream = stream_id. */
+int dspark_sample_rows(const void* logits, long long ld, int groups, int rows, int V,
+                       float temperature, int temp_mode, double top_p, int top_k,
+                       const unsigned long long* rng, int stream_id, int row_base, float* probs,
+                       long long ld_probs, int32_t* tokens, int tok_stride, int32_t* tokens2,
+                       int tok2_stride, dspark_stream_t stream);
+
+/* Speculative-sampling acceptance (Leviathan / Chen 2023) of B verify blocks; replaces
+ * _spec_sample_accept (src/mlx_dspark/generate.py:659-688). Row i < T-1 of block b accepts
+ * draft x = verify_ids[b, i+1] iff u < min(1, p_i[x] / max(q_i[x], 1e-9)); the first reject
+ * n draws the replacement from norm(max(p_n - q_n, 0)) (uniform over the vocabulary if that is
+ * all zero), all accepted draws the bonus from p_{T-1}. Outputs are those of
+ * dspark_accept_greedy (plan, pending, kv_len commit) and the call advances rng[b].offset.
+ * q_probs: fp32 [B, T-1, ld_q], the distributions the drafts were drawn from (probs of
+ *   dspark_sample_rows); q_onehot = 1 takes q_i = one-hot(x_i) instead (lookup drafts,
+ *   generate.py:815-824) and q_probs may be NULL.
+ * T <= 32, V <= 262144. workspace: dspark_accept_sample_workspace_bytes(B, T), zero-filled
+ * once before first use (the call leaves its counters at zero). */
+size_t dspark_accept_sample_workspace_bytes(int B, int T);
+int dspark_accept_sample(const void* logits, long long ld, int B, int T, int V,
+                         const int32_t* verify_ids, const float* q_probs, long long ld_q,
+                         int q_onehot, float temperature, int temp_mode, double top_p, int top_k,
+                         unsigned long long* rng, int32_t* kv_len, int commit, int32_t* pending,
+                         int32_t* plan, void* workspace, size_t workspace_bytes,
+                         dspark_stream_t stream);
+
+/* DSpark temperature draft: DSparkDrafter.sample_block_probs (src/mlx_dspark/model.py:283-309).
+ * Sequential over cap positions: logits_i = base_i + w2 . w1[prev] (as in K10), then token i
+ * drawn from truncate(softmax(logits_i * bf16(1/T))) with Philox row = i, stream 1.
+ * q_probs: out fp32 [B, cap, ld_q] (q_i of each row); draft / verify_ids as in K10.
+ * workspace: dspark_markov_probs_workspace_bytes(B, V) (the logits row of each step). */
+size_t dspark_markov_probs_workspace_bytes(int B, int V);
+int dspark_markov_sample_block_probs(const void* base, int ld, int rows_per_b, int B, int cap,
+                                     int V, int R, const uint8_t* w1q, const uint32_t* w1sb,
+                                     const uint8_t* w2q, const uint32_t* w2sb,
+                                     const int32_t* first_prev, int32_t* draft,
+                                     int32_t* verify_ids, float temperature, double top_p,
+                                     int top_k, const unsigned long long* rng, float* q_probs,
+                                     long long ld_q, void* workspace, size_t workspace_bytes,
+                                     dspark_stream_t stream);
+
+/* -------------------------------------------------------------------------------------
  * Length-only commit: len_a[b] += plan[b*plan_stride + 1] (and len_b, if given). Used after
  * the drafter context update so both consumers read the pre-commit length first.
  * Replaces the trims of src/mlx_dspark/generate.py:929-938 (target KV) and the

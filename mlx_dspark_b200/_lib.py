@@ -6,7 +6,7 @@ without the built library raises with the build command to run.
 from __future__ import annotations
 
 import ctypes
-from ctypes import POINTER, c_float, c_int, c_longlong, c_size_t, c_void_p, c_char_p
+from ctypes import POINTER, c_char_p, c_double, c_float, c_int, c_longlong, c_size_t, c_void_p
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().with_name("libdspark_b200.so")
@@ -57,6 +57,14 @@ SIGNATURES = {
     "dspark_markov_workspace_bytes": (c_size_t, [I, I]),
     "dspark_markov_sample_block": (I, [P, I, I, I, I, I, I, P, P, P, P, P, P, P, P, c_size_t, P, P]),
     "dspark_bf16_to_f16": (I, [P, I, P, I, I, I, P]),
+    "dspark_sample_rows": (I, [P, c_longlong, I, I, I, c_float, I, c_double, I, P, I, I, P,
+                               c_longlong, P, I, P, I, P]),
+    "dspark_accept_sample_workspace_bytes": (c_size_t, [I, I]),
+    "dspark_accept_sample": (I, [P, c_longlong, I, I, I, P, P, c_longlong, I, c_float, I,
+                                 c_double, I, P, P, I, P, P, P, c_size_t, P]),
+    "dspark_markov_probs_workspace_bytes": (c_size_t, [I, I]),
+    "dspark_markov_sample_block_probs": (I, [P, I, I, I, I, I, I, P, P, P, P, P, P, P, c_float,
+                                             c_double, I, P, P, c_longlong, P, c_size_t, P]),
 }
 
 _lib = None
@@ -88,6 +96,7 @@ def check(rc: int, what: str) -> None:
 # kernel launches issued through call() (graph replays re-run them without Python)
 LAUNCHES = {"n": 0}
 _KERNELS_PER_CALL = {"dspark_markov_sample_block": lambda a: int(a[4]),
+                     "dspark_markov_sample_block_probs": lambda a: 2 * int(a[4]),
                      "dspark_draft_override": lambda a: 2,
                      "dspark_attention": lambda a: 2 if int(a[10]) > 1 else 1}
 

@@ -12,6 +12,10 @@
 // next launch conditions on.
 // Rounding follows a bf16 model: e = bf16(dequant w1[prev]); bias = bf16(w2 . e);
 // logit = bf16(base + bias); argmax takes the first index of the maximum.
+//
+// Temperature drafts (sample_block_probs, model.py:283-309) use the same step kernel in its
+// SAMPLE form: it writes the biased logits row and the next launch (dspark_sample_rows) draws
+// token i from truncate(softmax(logits_i / T)), keeping q_i for the acceptance test.
 #include "common.cuh"
 
 namespace dspark {
@@ -32,16 +36,19 @@ __device__ __forceinline__ Best better(Best a, Best b) {
 }
 
 // NB == B: the batch width is a template parameter so every per-row loop is exact.
-template <int NB>
+// SAMPLE: write logits_i of batch row b to out[b * ld_out + v] instead of the argmax.
+template <int NB, bool SAMPLE>
 __global__ void __launch_bounds__(kThreads) markov_step_kernel(
     const __nv_bfloat16* __restrict__ base, int ld, int rows_per_b, int cap, int V, int step,
     const uint8_t* __restrict__ w1q, const uint32_t* __restrict__ w1sb,
     const uint8_t* __restrict__ w2q, const uint32_t* __restrict__ w2sb,
     const int32_t* __restrict__ first_prev, int32_t* __restrict__ draft,
     int32_t* __restrict__ verify_ids, float* __restrict__ part_v, int* __restrict__ part_i,
-    int* __restrict__ counter) {
+    int* __restrict__ counter, __nv_bfloat16* __restrict__ out, int ld_out) {
   pdl_wait();
   pdl_launch_dependents();
+  if (SAMPLE && step == 0 && verify_ids && blockIdx.x == 0 && threadIdx.x < NB)
+    verify_ids[threadIdx.x * (cap + 1)] = first_prev[threadIdx.x];
   __shared__ __align__(16) float e[NB][kR];
   __shared__ float esum[NB][kG];
   __shared__ Best red[NB][kThreads / 32];
@@ -116,9 +123,13 @@ __global__ void __launch_bounds__(kThreads) markov_step_kernel(
     for (int b = 0; b < NB; ++b) {
       const float logit =
           bf16_round(__bfloat162float(base[(size_t)(b * rows_per_b + step) * ld + v]) + bf16_round(d[b]));
-      best[b] = better(best[b], Best{logit, v});
+      if (SAMPLE)
+        out[(size_t)b * ld_out + v] = __float2bfloat16_rn(logit);
+      else
+        best[b] = better(best[b], Best{logit, v});
     }
   }
+  if (SAMPLE) return;
 #pragma unroll
   for (int b = 0; b < NB; ++b) {
     Best t = best[b];
@@ -220,19 +231,77 @@ extern "C" int dspark_markov_sample_block(const void* base, int ld, int rows_per
                           static_cast<const __nv_bfloat16*>(base), ld, rows_per_b, cap, V, i,
                           w1q, w1sb, w2q, w2sb, first_prev, draft, verify_ids,
                           reinterpret_cast<float*>(w + off_c), reinterpret_cast<int*>(w + off_i),
-                          reinterpret_cast<int*>(w));
+                          reinterpret_cast<int*>(w), (__nv_bfloat16*)nullptr, 0);
       if (rc) return rc;
     }
     return (int)DSPARK_OK;
   };
   switch (B) {
-    case 1: return run(mk::markov_step_kernel<1>);
-    case 2: return run(mk::markov_step_kernel<2>);
-    case 3: return run(mk::markov_step_kernel<3>);
-    case 4: return run(mk::markov_step_kernel<4>);
-    case 5: return run(mk::markov_step_kernel<5>);
-    case 6: return run(mk::markov_step_kernel<6>);
-    case 7: return run(mk::markov_step_kernel<7>);
-    default: return run(mk::markov_step_kernel<8>);
+    case 1: return run(mk::markov_step_kernel<1, false>);
+    case 2: return run(mk::markov_step_kernel<2, false>);
+    case 3: return run(mk::markov_step_kernel<3, false>);
+    case 4: return run(mk::markov_step_kernel<4, false>);
+    case 5: return run(mk::markov_step_kernel<5, false>);
+    case 6: return run(mk::markov_step_kernel<6, false>);
+    case 7: return run(mk::markov_step_kernel<7, false>);
+    default: return run(mk::markov_step_kernel<8, false>);
+  }
+}
+
+extern "C" int dspark_sample_rows(const void* logits, long long ld, int groups, int rows, int V,
+                                  float temperature, int temp_mode, double top_p, int top_k,
+                                  const unsigned long long* rng, int stream_id, int row_base,
+                                  float* probs, long long ld_probs, int32_t* tokens, int tok_stride,
+                                  int32_t* tokens2, int tok2_stride, dspark_stream_t stream);
+
+extern "C" size_t dspark_markov_probs_workspace_bytes(int B, int V) {
+  if (B <= 0 || V <= 0) return 0;
+  return (size_t)B * (size_t)((V + 7) & ~7) * 2;
+}
+
+extern "C" int dspark_markov_sample_block_probs(
+    const void* base, int ld, int rows_per_b, int B, int cap, int V, int R, const uint8_t* w1q,
+    const uint32_t* w1sb, const uint8_t* w2q, const uint32_t* w2sb, const int32_t* first_prev,
+    int32_t* draft, int32_t* verify_ids, float temperature, double top_p, int top_k,
+    const unsigned long long* rng, float* q_probs, long long ld_q, void* workspace,
+    size_t workspace_bytes, dspark_stream_t stream) {
+  if (!base || !w1q || !w1sb || !w2q || !w2sb || !first_prev || !draft || !rng || !q_probs ||
+      B <= 0 || cap <= 0 || V <= 0 || ld < V || ld_q < V)
+    return set_error(DSPARK_ERR_INVALID, "markov_sample_block_probs: bad arguments");
+  if (R != mk::kR) return set_error(DSPARK_ERR_UNSUPPORTED, "markov_sample_block_probs: rank %d != 256", R);
+  if (B > mk::kMaxB) return set_error(DSPARK_ERR_UNSUPPORTED, "markov_sample_block_probs: B > %d", mk::kMaxB);
+  const size_t need = dspark_markov_probs_workspace_bytes(B, V);
+  if (!workspace || workspace_bytes < need)
+    return set_error(DSPARK_ERR_WORKSPACE, "markov_sample_block_probs: workspace %zu < %zu",
+                     workspace_bytes, need);
+  const int ld_out = (V + 7) & ~7;
+  __nv_bfloat16* out = static_cast<__nv_bfloat16*>(workspace);
+  const int grid = (V + 2 * mk::kThreads - 1) / (2 * mk::kThreads);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto run = [&](auto kern) {
+    for (int i = 0; i < cap; ++i) {
+      int rc = launch_pdl("markov_step_sample", kern, dim3(grid), dim3(mk::kThreads), 0, st,
+                          static_cast<const __nv_bfloat16*>(base), ld, rows_per_b, cap, V, i,
+                          w1q, w1sb, w2q, w2sb, first_prev, draft, verify_ids, (float*)nullptr,
+                          (int*)nullptr, (int*)nullptr, out, ld_out);
+      if (rc) return rc;
+      // token i of batch row b -> draft[b * cap + i] and verify_ids[b * (cap + 1) + 1 + i];
+      // q_i of row b -> q_probs[(b * cap + i) * ld_q]
+      rc = dspark_sample_rows(out, ld_out, B, 1, V, temperature, 1, top_p, top_k, rng, 1, i,
+                              q_probs + (size_t)i * ld_q, (long long)cap * ld_q, draft + i, cap,
+                              verify_ids ? verify_ids + 1 + i : nullptr, cap + 1, stream);
+      if (rc) return rc;
+    }
+    return (int)DSPARK_OK;
+  };
+  switch (B) {
+    case 1: return run(mk::markov_step_kernel<1, true>);
+    case 2: return run(mk::markov_step_kernel<2, true>);
+    case 3: return run(mk::markov_step_kernel<3, true>);
+    case 4: return run(mk::markov_step_kernel<4, true>);
+    case 5: return run(mk::markov_step_kernel<5, true>);
+    case 6: return run(mk::markov_step_kernel<6, true>);
+    case 7: return run(mk::markov_step_kernel<7, true>);
+    default: return run(mk::markov_step_kernel<8, true>);
   }
 }

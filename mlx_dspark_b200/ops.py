@@ -31,7 +31,7 @@ def _require_cuda(*ts):
 class Scratch:
     """Zero-filled, grow-only workspaces per kernel family plus a device status word."""
 
-    FAMILIES = ("gemm", "attention", "accept", "markov")
+    FAMILIES = ("gemm", "attention", "accept", "markov", "accept_sample", "markov_probs")
 
     def __init__(self, device="cuda"):
         self.device = torch.device(device)
@@ -170,3 +170,60 @@ def markov_sample_block(base: torch.Tensor, rows_per_b: int, B: int, cap: int, w
 
 def bf16_to_f16(src: torch.Tensor, dst: torch.Tensor, rows: int, cols: int) -> None:
     call("dspark_bf16_to_f16", _p(src), src.stride(0), _p(dst), dst.stride(0), rows, cols, _stream())
+
+
+# ----------------------------------------------------------------------------------------
+# lossless speculative sampling (K9)
+def rng_state(seeds, device="cuda") -> torch.Tensor:
+    """Device {seed, offset} pairs, one per request (int64 storage of the u64 words)."""
+    seeds = [seeds] if isinstance(seeds, int) else list(seeds)
+    words = [((int(s) & 0xFFFFFFFFFFFFFFFF) ^ (1 << 63)) - (1 << 63) for s in seeds]
+    t = torch.zeros(len(words), 2, dtype=torch.int64)
+    t[:, 0] = torch.tensor(words, dtype=torch.int64)
+    return t.to(device)
+
+
+def sample_rows(logits: torch.Tensor, groups: int, rows: int, temperature: float, top_p: float,
+                top_k: int, rng: torch.Tensor, tokens: torch.Tensor, *, stream_id: int = 2,
+                row_base: int = 0, tok_stride: int = 1, probs: torch.Tensor | None = None,
+                tokens2: torch.Tensor | None = None, tok2_stride: int = 1,
+                temp_mode: int = 0) -> torch.Tensor:
+    """Draw one token per row of truncate(softmax(logits / T)) (dspark_sample_rows)."""
+    _require_cuda(logits, rng, tokens)
+    assert logits.dtype == torch.bfloat16
+    V = logits.shape[-1]
+    call("dspark_sample_rows", _p(logits), logits.stride(0), groups, rows, V, float(temperature),
+         int(temp_mode), float(top_p), int(top_k or 0), _p(rng), int(stream_id), int(row_base),
+         _p(probs), probs.stride(0) if probs is not None else 0, _p(tokens), int(tok_stride),
+         _p(tokens2), int(tok2_stride), _stream())
+    return tokens
+
+
+def accept_sample(logits: torch.Tensor, B: int, T: int, verify_ids: torch.Tensor,
+                  q_probs: torch.Tensor | None, temperature: float, top_p: float, top_k: int,
+                  rng: torch.Tensor, kv_len: torch.Tensor | None, commit: bool,
+                  pending: torch.Tensor, plan: torch.Tensor, scratch: Scratch, *,
+                  q_onehot: bool = False, temp_mode: int = 0) -> None:
+    """Rejection-sampling acceptance of B blocks (dspark_accept_sample); advances rng offsets."""
+    _require_cuda(logits, verify_ids, rng, pending, plan)
+    V = logits.shape[-1]
+    ws = scratch.get("accept_sample", int(lib().dspark_accept_sample_workspace_bytes(B, T)))
+    ld_q = q_probs.shape[-1] if q_probs is not None else 0
+    call("dspark_accept_sample", _p(logits), logits.stride(0), B, T, V, _p(verify_ids),
+         _p(q_probs), ld_q, int(q_onehot), float(temperature), int(temp_mode), float(top_p),
+         int(top_k or 0), _p(rng), _p(kv_len), int(commit), _p(pending), _p(plan), _p(ws),
+         ws.numel(), _stream())
+
+
+def markov_sample_block_probs(base: torch.Tensor, rows_per_b: int, B: int, cap: int,
+                              w1: PackedLinear, w2: PackedLinear, first_prev: torch.Tensor,
+                              draft: torch.Tensor, verify_ids: torch.Tensor | None,
+                              temperature: float, top_p: float, top_k: int, rng: torch.Tensor,
+                              q_probs: torch.Tensor, scratch: Scratch) -> None:
+    """DSpark temperature draft: Markov step + draw per position (model.py:283-309)."""
+    V = w2.N
+    ws = scratch.get("markov_probs", int(lib().dspark_markov_probs_workspace_bytes(B, V)))
+    call("dspark_markov_sample_block_probs", _p(base), base.stride(0), rows_per_b, B, cap, V,
+         w2.K, _p(w1.q), _p(w1.sb), _p(w2.q), _p(w2.sb), _p(first_prev), _p(draft),
+         _p(verify_ids), float(temperature), float(top_p), int(top_k or 0), _p(rng), _p(q_probs),
+         q_probs.shape[-1], _p(ws), ws.numel(), _stream())
