@@ -297,6 +297,13 @@ int dspark_draft_override(int B, int cap, int V, const int32_t* ref, int ref_len
                           const int32_t* kv_len, const int32_t* prompt_len, int32_t* verify_ids,
                           dspark_stream_t stream);
 
+/* Row argmax, first index of the maximum (mx.argmax): the greedy draft of a block drafter
+ * without a sequential head — DFlash (src/mlx_dspark/generate.py:564) and sample_block without
+ * a Markov head (model.py:272-273). Token of row r -> tokens[r * tok_stride] and, if given,
+ * tokens2[r * tok2_stride]. */
+int dspark_argmax_rows(const void* logits, long long ld, int rows, int V, int32_t* tokens,
+                       int tok_stride, int32_t* tokens2, int tok2_stride, dspark_stream_t stream);
+
 /* drafter block embedding: row b*k + i embeds pending[b] if i == 0 else mask_id
  * (src/mlx_dspark/generate.py:848-849, batch_engine.py:548-549); ids_out optional [B*k] */
 int dspark_embed_block_w8(const int32_t* pending, int B, int k, int mask_id, const uint8_t* wq,

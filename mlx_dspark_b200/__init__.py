@@ -2,19 +2,21 @@
 
 PyTorch on the host drives hand-written sm_100a kernels through the C ABI of
 libdspark_b200.so (include/dspark_b200.h): W8A16 tcgen05 GEMMs, paged GQA attention,
-fused greedy acceptance with in-place KV commit, and the DSpark drafter. The public names
+fused greedy and rejection-sampling acceptance with in-place KV commit, and the DSpark and
+DFlash drafters. The public names
 follow the reference package (src/mlx_dspark/__init__.py:54-116).
 """
 __version__ = "0.1.0"
 
 from .config import DFlashConfig, DSparkConfig, TargetConfig, WORKLOADS, TARGETS
-from .generate import GenResult, greedy_generate, speculative_generate
-from .load import load_drafter, load_pair, load_target
-from .model import DSparkDrafter
+from .generate import GenResult, dflash_generate, greedy_generate, speculative_generate
+from .load import load_dflash_drafter, load_drafter, load_pair, load_target
+from .model import DFlashDrafter, DSparkDrafter, Sampling
 from .target import Target
 
 __all__ = [
-    "DSparkConfig", "DFlashConfig", "TargetConfig", "Target", "DSparkDrafter",
-    "load_drafter", "load_target", "load_pair", "speculative_generate", "greedy_generate",
-    "GenResult", "WORKLOADS", "TARGETS",
+    "DSparkConfig", "DFlashConfig", "TargetConfig", "Target", "DSparkDrafter", "DFlashDrafter",
+    "Sampling", "load_drafter", "load_dflash_drafter", "load_target", "load_pair",
+    "speculative_generate", "dflash_generate", "greedy_generate", "GenResult", "WORKLOADS",
+    "TARGETS",
 ]

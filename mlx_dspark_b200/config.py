@@ -170,6 +170,11 @@ class DFlashConfig:
         if not self.layer_types:
             self.layer_types = ("full_attention",) * self.num_hidden_layers
 
+    @property
+    def scaling(self) -> float:
+        """SDPA scale head_dim^-0.5 (dflash_model.py:89)."""
+        return self.head_dim ** -0.5
+
 
 # ----------------------------------------------------------------------------------------
 # the BASELINE workloads

@@ -142,6 +142,45 @@ __global__ void draft_override_kernel(int B, int cap, int V, const int32_t* __re
   }
 }
 
+// Row argmax (first index of the maximum), one CTA per row: the greedy block draft of a
+// drafter without a sequential head (DFlash, generate.py:564; sample_block without a Markov
+// head, model.py:272-273). Token of row r -> tokens[r * s1] (and tokens2[r * s2]).
+constexpr int kArgThreads = 1024;
+__global__ void __launch_bounds__(kArgThreads) argmax_rows_kernel(
+    const __nv_bfloat16* __restrict__ logits, long long ld, int V, int32_t* __restrict__ tokens,
+    int s1, int32_t* __restrict__ tokens2, int s2) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int r = blockIdx.x;
+  const __nv_bfloat16* row = logits + (size_t)r * ld;
+  Best b{-INFINITY, 0x7fffffff};
+  const bool vec = ((ld & 7) == 0) && ((reinterpret_cast<uintptr_t>(logits) & 15) == 0);
+  for (int v = threadIdx.x * 8; v < V; v += kArgThreads * 8) {
+    if (vec && v + 8 <= V) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(row + v));
+      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) b = better(b, Best{__bfloat162float(e[j]), v + j});
+    } else {
+      for (int j = v; j < min(v + 8, V); ++j) b = better(b, Best{__bfloat162float(row[j]), j});
+    }
+  }
+  b = warp_best(b);
+  __shared__ Best red[kArgThreads / 32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = b;
+  __syncthreads();
+  if (warp == 0) {
+    b = red[lane];
+    b = warp_best(b);
+    if (lane == 0) {
+      const int t = b.i == 0x7fffffff ? 0 : b.i;
+      tokens[(size_t)r * s1] = t;
+      if (tokens2) tokens2[(size_t)r * s2] = t;
+    }
+  }
+}
+
 __global__ void bump_kernel(int32_t* __restrict__ ctr, int B) {
   pdl_wait();
   pdl_launch_dependents();
@@ -295,4 +334,16 @@ extern "C" int dspark_draft_override(int B, int cap, int V, const int32_t* ref, 
                       prompt_len, verify_ids);
   if (rc) return rc;
   return launch_pdl("draft_override.bump", acc::bump_kernel, dim3(1), dim3(32), 0, st, round_ctr, B);
+}
+
+extern "C" int dspark_argmax_rows(const void* logits, long long ld, int rows, int V, int32_t* tokens,
+                                  int tok_stride, int32_t* tokens2, int tok2_stride,
+                                  dspark_stream_t stream) {
+  if (!logits || !tokens || rows <= 0 || V <= 0 || ld < V || tok_stride < 1 ||
+      (tokens2 && tok2_stride < 1))
+    return set_error(DSPARK_ERR_INVALID, "argmax_rows: bad arguments");
+  if (rows > 65535) return set_error(DSPARK_ERR_UNSUPPORTED, "argmax_rows: too many rows");
+  return launch_pdl("argmax_rows", acc::argmax_rows_kernel, dim3(rows), dim3(acc::kArgThreads), 0,
+                    static_cast<cudaStream_t>(stream), static_cast<const __nv_bfloat16*>(logits),
+                    ld, V, tokens, tok_stride, tokens2, tok2_stride);
 }

@@ -1,7 +1,9 @@
-"""Decode loops on the device: speculative (DSpark, greedy) and plain greedy.
+"""Decode loops on the device: speculative (DSpark or DFlash drafter; greedy or sampled) and
+plain decoding.
 
 Reference: src/mlx_dspark/generate.py — GenResult (:27-46), greedy_generate (:373-465),
-_prefill_tapped (:632-656), speculative_generate (:691-978).
+dflash_generate (:468-601), _prefill_tapped (:632-656), _spec_sample_accept (:659-688),
+speculative_generate (:691-978).
 
 One speculative round is a fixed sequence of launches on one stream, with every varying
 quantity (positions, lengths, pending token, draft ids) in device memory:
@@ -9,7 +11,10 @@ quantity (positions, lengths, pending token, draft ids) in device memory:
   draft  : block embed -> drafter layer(s) over [ctx; block] -> head on cap rows -> Markov argmax
            (writes verify_ids = [pending, d_1..d_cap])
   verify : target forward over verify_ids with the hidden-state tap
-  accept : fused argmax + accepted prefix + bonus token -> plan, pending
+  accept : fused argmax + accepted prefix + bonus token -> plan, pending (greedy), or the
+           rejection-sampling acceptance with residual draw (temperature > 0; the drafts and
+           their q distributions come from the drafter's draw kernels, all randomness from a
+           per-request Philox stream on the device whose offset the acceptance advances)
   context: fc + hidden_norm + k/v of the verified rows written at the drafter's context length
   commit : seq_len += n + 1 for the target KV and the drafter context (rollback = not counting)
 
@@ -25,6 +30,7 @@ import torch
 
 from . import ops
 from .kvcache import CacheState, RowView
+from .model import Sampling
 
 PREFILL_CHUNK = 2048  # reference knob (generate.py:613); the device chunk is min(this, chunk_len)
 
@@ -111,9 +117,11 @@ class SpecSession:
     """Static state and buffers of a B-row speculative decode with `cap` drafts per round."""
 
     def __init__(self, target, drafter, B: int, cap: int, max_tokens: int, *,
-                 override: dict | None = None):
+                 override: dict | None = None, sampling: Sampling | None = None,
+                 seeds=None):
         self.target, self.drafter = target, drafter
         self.B, self.cap = B, cap
+        self.sampling = sampling if (sampling is not None and sampling.active) else None
         self.k = drafter.block_size
         self.T = cap + 1
         self.tap = list(drafter.config.target_layer_ids)
@@ -135,8 +143,14 @@ class SpecSession:
         self.pending_host = torch.zeros(B, dtype=torch.int32, pin_memory=True)
         self.splits_t = target.attn_splits(B, self.tstate.max_pages)
         self.splits_c = target.attn_splits(B, self.cstate.max_pages)
+        self.rng = ops.rng_state(list(seeds) if seeds is not None else [0] * B, dev)
+        self.q = None
+        if self.sampling is not None:
+            self.q = torch.zeros(B * cap, target.cfg.vocab_size, dtype=torch.float32, device=dev)
         self.override = None
         if override is not None:
+            if self.sampling is not None:
+                raise ValueError("the draft override is a greedy benchmark harness")
             o = override
             self.override = {
                 "ref": o["ref"].to(dev, torch.int32).contiguous(),        # [B, ref_len]
@@ -155,15 +169,21 @@ class SpecSession:
     def launch_round(self) -> None:
         d, t, sc = self.drafter, self.target, self.target.scratch
         B, T, cap = self.B, self.T, self.cap
+        sm = self.sampling
         d.draft_dev(self.pending, B, cap, self.cstate, self.dbuf, self.draft, self.vbuf.ids,
-                    self.splits_c)
+                    self.splits_c, sampling=sm, rng=self.rng, q_probs=self.q)
         if self.override is not None:
             o = self.override
             ops.draft_override(B, cap, t.cfg.vocab_size, o["ref"], o["agree"], o["round"],
                                self.tstate.seq_len, o["prompt_len"], self.vbuf.ids)
         t.forward(self.vbuf, self.tstate, self.tap, splits=self.splits_t)
-        ops.accept_greedy(self.vbuf.logits, B, T, self.vbuf.ids, self.argmax, None, False,
-                          self.pending, self.plan, sc)
+        if sm is None:
+            ops.accept_greedy(self.vbuf.logits, B, T, self.vbuf.ids, self.argmax, None, False,
+                              self.pending, self.plan, sc)
+        else:
+            ops.accept_sample(self.vbuf.logits, B, T, self.vbuf.ids, self.q, sm.temperature,
+                              sm.top_p, sm.top_k, self.rng, None, False, self.pending, self.plan,
+                              sc)
         d.update_context_dev(self.vbuf.fused16, B, T, self.cstate, self.dbuf)
         ops.commit_lengths(self.plan, B, self.tstate.seq_len, self.cstate.seq_len)
         self.plan_host.copy_(self.plan, non_blocking=True)
@@ -193,38 +213,28 @@ class SpecSession:
         return self.plan_host.tolist()
 
 
-def speculative_generate(target, tokenizer, drafter, prompt: str = "", *,
-                         prompt_ids: list[int] | None = None, cache=None, ctx_caches=None,
-                         reuse_len: int = 0, max_new_tokens: int = 128,
-                         confidence_threshold: float = 0.0, max_draft_tokens: int | None = 2,
-                         cap_controller=None, lookup_drafts: bool = False,
-                         lookup_max_draft: int = 6, temperature: float = 0.0, top_p: float = 1.0,
-                         top_k: int = 0, presence_penalty: float = 0.0,
-                         frequency_penalty: float = 0.0, logprobs: int | None = None,
-                         seed: int | None = None, apply_chat_template: bool = True,
-                         stop: list[str] | None = None, on_text=None, verbose: bool = False,
-                         use_graph: bool = True, draft_override: dict | None = None) -> GenResult:
-    """Speculative decoding, batch 1 (generate.py:691-978). Greedy (temperature 0): the output
-    is the target's greedy decoding; drafter quality only changes accept lengths."""
-    if temperature > 0.0:
-        raise NotImplementedError("sampled speculative decoding goes through the sampler path")
-    if presence_penalty or frequency_penalty or logprobs is not None or confidence_threshold > 0:
-        raise NotImplementedError("penalties / logprobs / confidence truncation are not built")
-    if lookup_drafts:
-        raise NotImplementedError("hybrid n-gram drafts are not built on the device loop yet")
-    cfg = drafter.config
-    k = cfg.block_size
-    cap = k if max_draft_tokens is None else max(1, min(int(max_draft_tokens), k))
+def _pick_first(target, last_row: torch.Tensor, sampling: Sampling | None, rng: torch.Tensor) -> int:
+    """First committed token from the prefill's last logits (_pick, generate.py:144-146):
+    argmax, or a draw with Philox {offset 0, row 0, stream 2}."""
+    if sampling is None:
+        return int(last_row.float().argmax())
+    tok = torch.zeros(1, dtype=torch.int32, device=target.device)
+    ops.sample_rows(last_row.view(1, -1), 1, 1, sampling.temperature, sampling.top_p,
+                    sampling.top_k, rng[:1], tok, stream_id=2)
+    return int(tok.item())
+
+
+def _spec_loop(target, tokenizer, drafter, ids, cap, max_new_tokens, sampling, seed, use_graph,
+               draft_override, verbose) -> GenResult:
     eos_ids = eos_token_ids(tokenizer)
-    if prompt_ids is None:
-        prompt_ids = list(tokenizer.encode(prompt))
-    ids = list(prompt_ids)
     budget = len(ids) + max_new_tokens + cap + 1
-    sess = SpecSession(target, drafter, 1, cap, budget, override=draft_override)
+    sampling = sampling if (sampling is not None and sampling.active) else None
+    sess = SpecSession(target, drafter, 1, cap, budget, override=draft_override,
+                       sampling=sampling, seeds=[0 if seed is None else int(seed)])
     try:
         t0 = time.time()
         last = prefill_rows(target, ids, sess.tstate, sess.tap, drafter, sess.cstate)
-        pending = int(last.float().argmax())
+        pending = _pick_first(target, last, sampling, sess.rng)
         sess.pending.fill_(pending)
         torch.cuda.synchronize()
         t1 = time.time()
@@ -257,11 +267,62 @@ def speculative_generate(target, tokenizer, drafter, prompt: str = "", *,
         sess.release()
 
 
-class GreedySession:
-    """Plain greedy decode of B rows, one token per step (generate.py:373-465)."""
+def speculative_generate(target, tokenizer, drafter, prompt: str = "", *,
+                         prompt_ids: list[int] | None = None, cache=None, ctx_caches=None,
+                         reuse_len: int = 0, max_new_tokens: int = 128,
+                         confidence_threshold: float = 0.0, max_draft_tokens: int | None = 2,
+                         cap_controller=None, lookup_drafts: bool = False,
+                         lookup_max_draft: int = 6, temperature: float = 0.0, top_p: float = 1.0,
+                         top_k: int = 0, presence_penalty: float = 0.0,
+                         frequency_penalty: float = 0.0, logprobs: int | None = None,
+                         seed: int | None = None, apply_chat_template: bool = True,
+                         stop: list[str] | None = None, on_text=None, verbose: bool = False,
+                         use_graph: bool = True, draft_override: dict | None = None) -> GenResult:
+    """Speculative decoding with the DSpark drafter, batch 1 (generate.py:691-978).
+    temperature 0: the output is the target's greedy decoding. temperature > 0: drafts are drawn
+    from the drafter's truncated distributions and accepted by rejection sampling, so the output
+    is a sample of top-p/top-k(softmax(target / T)) (lossless); `seed` seeds the Philox stream."""
+    if presence_penalty or frequency_penalty or logprobs is not None or confidence_threshold > 0:
+        raise NotImplementedError("penalties / logprobs / confidence truncation are not built")
+    if lookup_drafts:
+        raise NotImplementedError("hybrid n-gram drafts are not built on the device loop yet")
+    k = drafter.config.block_size
+    cap = k if max_draft_tokens is None else max(1, min(int(max_draft_tokens), k))
+    if prompt_ids is None:
+        prompt_ids = list(tokenizer.encode(prompt))
+    return _spec_loop(target, tokenizer, drafter, list(prompt_ids), cap, max_new_tokens,
+                      Sampling(temperature, top_p, top_k), seed, use_graph, draft_override,
+                      verbose)
 
-    def __init__(self, target, B: int, max_tokens: int):
+
+def dflash_generate(target_model, tokenizer, drafter, prompt: str = "", *,
+                    prompt_ids: list[int] | None = None, max_new_tokens: int = 128,
+                    max_draft_tokens: int | None = None, cap_controller=None,
+                    temperature: float = 0.0, top_p: float = 1.0, top_k: int = 0,
+                    apply_chat_template: bool = True, seed: int | None = None,
+                    stop: list[str] | None = None, on_text=None, use_graph: bool = True,
+                    verbose: bool = False) -> GenResult:
+    """Speculative decoding with the DFlash block-diffusion drafter (generate.py:468-601). The
+    backbone drafts the full block; `max_draft_tokens` bounds how many drafted tokens are
+    verified (None = block - 1, DFlash's native operating point)."""
+    kdraft = drafter.config.block_size - 1
+    cap = kdraft if max_draft_tokens is None else max(1, min(int(max_draft_tokens), kdraft))
+    if prompt_ids is None:
+        prompt_ids = list(tokenizer.encode(prompt))
+    return _spec_loop(target_model, tokenizer, drafter, list(prompt_ids), cap, max_new_tokens,
+                      Sampling(temperature, top_p, top_k), seed, use_graph, None, verbose)
+
+
+class GreedySession:
+    """Plain decode of B rows, one token per step (generate.py:373-465): argmax, or with
+    temperature > 0 a draw from top-p/top-k(softmax(logits / T)) whose Philox offset the
+    draw kernel advances on the device (so the step stays one CUDA graph)."""
+
+    def __init__(self, target, B: int, max_tokens: int, sampling: Sampling | None = None,
+                 seeds=None):
         self.target, self.B = target, B
+        self.sampling = sampling if (sampling is not None and sampling.active) else None
+        self.rng = ops.rng_state(list(seeds) if seeds is not None else [0] * B, target.device)
         dev = target.device
         cap_tokens = max_tokens + 64
         self.tstate = CacheState(target.new_pool(cap_tokens, B), B, cap_tokens, dev)
@@ -282,9 +343,15 @@ class GreedySession:
     def launch_step(self):
         t = self.target
         t.forward(self.buf, self.tstate, (), splits=self.splits)
-        # T = 1: n = 0, bonus = argmax; the next input id is written in place
-        ops.accept_greedy(self.buf.logits, self.B, 1, self.buf.ids, self.argmax, self.tstate.seq_len,
-                          True, self.buf.ids, self.plan, t.scratch)
+        # T = 1: n = 0, bonus = argmax (or a draw); the next input id is written in place
+        sm = self.sampling
+        if sm is None:
+            ops.accept_greedy(self.buf.logits, self.B, 1, self.buf.ids, self.argmax,
+                              self.tstate.seq_len, True, self.buf.ids, self.plan, t.scratch)
+        else:
+            ops.accept_sample(self.buf.logits, self.B, 1, self.buf.ids, None, sm.temperature,
+                              sm.top_p, sm.top_k, self.rng, self.tstate.seq_len, True,
+                              self.buf.ids, self.plan, t.scratch)
         self.plan_host.copy_(self.plan, non_blocking=True)
 
     def capture(self):
@@ -314,18 +381,21 @@ def greedy_generate(target, tokenizer, prompt: str = "", *, prompt_ids: list[int
                     logprobs: int | None = None, seed: int | None = None,
                     apply_chat_template: bool = True, stop=None, on_text=None,
                     use_graph: bool = True) -> GenResult:
-    """Plain greedy decoding of the target (the baseline the speedup is measured against)."""
-    if temperature > 0.0:
-        raise NotImplementedError("sampled plain decoding goes through the sampler path")
+    """Plain decoding of the target (the baseline the speedup is measured against): greedy, or
+    sampled with temperature / top-p / top-k from a Philox stream seeded by `seed`."""
+    if presence_penalty or frequency_penalty or logprobs is not None:
+        raise NotImplementedError("penalties / logprobs are not built")
     eos_ids = eos_token_ids(tokenizer)
     if prompt_ids is None:
         prompt_ids = list(tokenizer.encode(prompt))
     ids = list(prompt_ids)
-    sess = GreedySession(target, 1, len(ids) + max_new_tokens + 1)
+    sampling = Sampling(temperature, top_p, top_k)
+    sess = GreedySession(target, 1, len(ids) + max_new_tokens + 1, sampling,
+                         [0 if seed is None else int(seed)])
     try:
         t0 = time.time()
         last = prefill_rows(target, ids, sess.tstate, ())
-        nxt = int(last.float().argmax())
+        nxt = _pick_first(target, last, sess.sampling, sess.rng)
         sess.buf.ids.fill_(nxt)
         torch.cuda.synchronize()
         t1 = time.time()
@@ -347,4 +417,4 @@ def greedy_generate(target, tokenizer, prompt: str = "", *, prompt_ids: list[int
 
 
 __all__ = ["GenResult", "SpecSession", "GreedySession", "speculative_generate",
-           "greedy_generate", "prefill_rows", "eos_token_ids", "RowView"]
+           "dflash_generate", "greedy_generate", "prefill_rows", "eos_token_ids", "RowView"]

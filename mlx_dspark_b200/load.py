@@ -9,10 +9,10 @@ from __future__ import annotations
 
 import torch
 
-from .config import TARGETS, DSparkConfig, TargetConfig, dspark_for
-from .model import DSparkDrafter
+from .config import TARGETS, DFlashConfig, DSparkConfig, TargetConfig, dflash_for, dspark_for
+from .model import DFlashDrafter, DSparkDrafter
 from .target import Target
-from .weights import generate_dspark, generate_target
+from .weights import generate_dflash, generate_dspark, generate_target
 
 
 class IdTokenizer:
@@ -55,8 +55,25 @@ def load_drafter(target: Target, config: DSparkConfig | None = None, *, seed: in
     return DSparkDrafter(weights, target, device=device), cfg
 
 
-def load_pair(model: str = "tiny", *, drafter: DSparkConfig | None = None, seed: int = 0,
-              kv_bits: int | None = None, device="cuda"):
+def load_dflash_drafter(target: Target, config: DFlashConfig | None = None, *, seed: int = 0,
+                        device="cuda", gen_device: str | None = None, weights=None):
+    """(DFlashDrafter, config) bound to `target` (2 layers, block 16 by default;
+    load.py:224-289 loads z-lab DFlash checkpoints the same way, bound to the target)."""
+    cfg = config or dflash_for(target.cfg)
+    if weights is None:
+        weights = generate_dflash(cfg, seed, gen_device or _gen_device(device))
+    return DFlashDrafter(weights, target, device=device), cfg
+
+
+def load_pair(model: str = "tiny", *, drafter: DSparkConfig | DFlashConfig | str | None = None,
+              seed: int = 0, kv_bits: int | None = None, device="cuda"):
+    """(target, tokenizer, drafter, config); drafter "dflash" (or a DFlashConfig) selects the
+    block-diffusion drafter, anything else the DSpark drafter."""
     target, tok = load_target(model, require_tap=True, kv_bits=kv_bits, seed=seed, device=device)
-    d, cfg = load_drafter(target, drafter, seed=seed, device=device)
+    if drafter == "dflash" or isinstance(drafter, DFlashConfig):
+        d, cfg = load_dflash_drafter(target, None if drafter == "dflash" else drafter, seed=seed,
+                                     device=device)
+    else:
+        d, cfg = load_drafter(target, None if drafter == "dspark" else drafter, seed=seed,
+                              device=device)
     return target, tok, d, cfg

@@ -1,23 +1,48 @@
-"""GPU DSpark drafter (qwen3 family) on the sm_100a kernels.
+"""GPU block drafters on the sm_100a kernels: DSpark (semi-autoregressive, Markov head) and
+DFlash (block diffusion), both conditioned on target hidden states.
 
-Drop-in for DSparkDrafter (src/mlx_dspark/model.py:348-437): embed, fuse_target,
-make_ctx_cache, update_context, backbone, compute_logits, sample_block, config,
-block_size, mask_token_id, markov_head, confidence_head. The drafter context (the
-per-layer K/V of the fused target hidden states, model.py:176-208) lives in a paged pool of
-its own; the block K/V are written after the committed context for the duration of one
-draft (the attention of model.py:258-283 reads [ctx; block] with no mask), and the context
-update of the accepted rows overwrites them.
+Both follow the same device path (BlockDrafter):
+  context : fused target hidden [rows, n_tap*H] -> fc -> hidden_norm -> per layer
+            k_norm/RoPE K and V written into the drafter's paged context cache
+            (DSpark update_context, src/mlx_dspark/model.py:381-384 and :254-256;
+            DFlash KV injection, src/mlx_dspark/dflash_model.py:100-124)
+  block   : [pending, mask x (k-1)] -> embed -> layers (q from the block, K/V = [ctx; block],
+            no mask) -> final norm (model.py:258-283,386-390; dflash_model.py:125-134,197-205)
+The block K/V are written after the committed context for the duration of one draft; the
+context update of the accepted rows overwrites them.
+
+DSparkDrafter — drop-in for DSparkDrafter (model.py:348-437): own or shared embedding / head,
+head over the first cap rows, then the sequential Markov head (greedy, or temperature drafts
+with the q distributions kept for the acceptance test).
+DFlashDrafter — drop-in for DFlashDraftModel (dflash_model.py:167-208) bound to a target: the
+target's embedding and head, logits read from block row 1 on (logits_start = 1), greedy
+argmax or temperature drafts; batch 1 like the reference's dflash_generate.
 """
 from __future__ import annotations
+
+from dataclasses import dataclass
 
 import torch
 
 from . import ops
 from ._lib import EPI_RESIDUAL_BF16, EPI_SILU_MUL_F16, EPI_STORE_BF16
-from .config import DSparkConfig, TargetConfig
+from .config import DFlashConfig, DSparkConfig
 from .kvcache import PAGE, CacheState, PagePool
 from .target import PackedLayer, Target, rope_inv_freq
-from .weights import DSparkWeights, pack
+from .weights import DFlashWeights, DSparkWeights, pack
+
+
+@dataclass
+class Sampling:
+    """Temperature / nucleus / top-k parameters of a sampled decode (temperature > 0)."""
+
+    temperature: float
+    top_p: float = 1.0
+    top_k: int = 0
+
+    @property
+    def active(self) -> bool:
+        return self.temperature > 0.0
 
 
 class _Markov:
@@ -28,7 +53,7 @@ class _Markov:
 
 
 class DraftBuffers:
-    def __init__(self, cfg: DSparkConfig, B: int, k: int, ctx_rows: int, n_tap: int, device):
+    def __init__(self, cfg, B: int, k: int, ctx_rows: int, device):
         H, I = cfg.hidden_size, cfg.intermediate_size
         q_dim = cfg.num_attention_heads * cfg.head_dim
         kv_dim = cfg.num_key_value_heads * cfg.head_dim
@@ -48,37 +73,35 @@ class DraftBuffers:
         self.ctx_kv = torch.zeros(ctx_rows, 2 * kv_dim, dtype=torch.bfloat16, device=device)
 
 
-class DSparkDrafter:
-    def __init__(self, weights: DSparkWeights, target: Target, device="cuda"):
-        cfg = weights.cfg
+class BlockDrafter:
+    """Context update and block backbone shared by the DSpark and DFlash drafters."""
+
+    logits_start = 0
+
+    def __init__(self, cfg, fc, hidden_norm, norm, layer_weights, target: Target, embed_w, head_w,
+                 device):
         self.config = cfg
         self.block_size = cfg.block_size
         self.mask_token_id = cfg.mask_token_id
-        self.softcap = cfg.final_logit_softcapping
-        if self.softcap is not None:
-            raise NotImplementedError("logit softcapping (gemma4 drafters) is not built")
-        if cfg.norm_style != "qwen":
-            raise NotImplementedError("only the qwen3 drafter family is built")
         self.device = torch.device(device)
         self.target = target
-        self.embed_w = target.embed if weights.embed is None else pack(weights.embed, device=device)
-        self.head_w = target.head if weights.lm_head is None else pack(weights.lm_head, device=device)
-        self.fc = pack(weights.fc, device=device)
-        self.hidden_norm = weights.hidden_norm.to(device)
-        self.norm = weights.norm.to(device)
+        self.embed_w, self.head_w = embed_w, head_w
+        self.fc = pack(fc, device=device)
+        self.hidden_norm = hidden_norm.to(device)
+        self.norm = norm.to(device)
         self.layers = []
-        for lw in weights.layers:
+        for lw in layer_weights:
             pl = PackedLayer(lw, device)
             pl.kv = pack(lw.wk, lw.wv, device=device)
             self.layers.append(pl)
-        self.markov_head = None
-        if weights.markov_w1 is not None:
-            self.markov_head = _Markov(pack(weights.markov_w1, device=device),
-                                       pack(weights.markov_w2, device=device), cfg.markov_rank)
-        self.confidence_head = None
         self.inv_freq = rope_inv_freq(cfg.head_dim, cfg.rope_theta, device)
         self.scratch = target.scratch
         self._bufs = {}
+        self.rng = ops.rng_state(0, self.device)
+
+    def seed(self, seed: int) -> None:
+        """Seed the device Philox stream used by host-API draws (mx.random.seed)."""
+        self.rng.copy_(ops.rng_state(int(seed), self.device))
 
     # ------------------------------------------------------------------ caches / buffers
     def new_pool(self, max_tokens: int, rows: int = 1) -> PagePool:
@@ -94,8 +117,7 @@ class DSparkDrafter:
         key = (B, k, ctx_rows)
         b = self._bufs.get(key)
         if b is None:
-            b = DraftBuffers(self.config, B, k, ctx_rows, len(self.config.target_layer_ids),
-                             self.device)
+            b = DraftBuffers(self.config, B, k, ctx_rows, self.device)
             self._bufs[key] = b
         return b
 
@@ -103,7 +125,7 @@ class DSparkDrafter:
     def update_context_dev(self, fused16: torch.Tensor, B: int, T: int, ctx: CacheState,
                            buf: DraftBuffers) -> None:
         """fused [B*T, n_tap*H] (fp16) -> fc -> hidden_norm -> per layer k_norm/RoPE K and V
-        written at ctx positions seq_len[b] + t (model.py:381-384, update_ctx :254-256)."""
+        written at ctx positions seq_len[b] + t."""
         c, sc = self.config, self.scratch
         M = B * T
         ops.gemm(fused16, self.fc, buf.ctx_h, epilogue=EPI_STORE_BF16, scratch=sc, M=M)
@@ -114,11 +136,10 @@ class DSparkDrafter:
                                   L.k_norm, c.rms_norm_eps, self.inv_freq, ctx.seq_len, None,
                                   ctx.layout(l))
 
-    def draft_dev(self, pending: torch.Tensor, B: int, cap: int, ctx: CacheState,
-                  buf: DraftBuffers, draft: torch.Tensor, verify_ids: torch.Tensor | None,
-                  splits: int) -> None:
-        """Block [pending, mask x (k-1)] -> backbone over [ctx; block] -> head over the first
-        cap positions -> Markov sequential argmax (generate.py:846-852,910; model.py:386-409)."""
+    def backbone_dev(self, pending: torch.Tensor, B: int, ctx: CacheState, buf: DraftBuffers,
+                     splits: int) -> None:
+        """Block [pending, mask x (k-1)] of each row at positions seq_len[b] + i -> layers over
+        [ctx; block] -> final norm into buf.xn16 (fp16, the head GEMM input)."""
         c, sc = self.config, self.scratch
         k = self.block_size
         M = B * k
@@ -139,25 +160,8 @@ class DSparkDrafter:
             ops.gemm(buf.act16, L.down, buf.h, epilogue=EPI_RESIDUAL_BF16, residual=buf.h,
                      scratch=sc, M=M)
         ops.rmsnorm(buf.h, self.norm, c.rms_norm_eps, y16=buf.xn16, M=M)
-        head_rows = cap if B == 1 else M
-        ops.gemm(buf.xn16, self.head_w, buf.base, epilogue=EPI_STORE_BF16, scratch=sc,
-                 M=head_rows)
-        rows_per_b = cap if B == 1 else k
-        if self.markov_head is not None:
-            ops.markov_sample_block(buf.base, rows_per_b, B, cap, self.markov_head.w1,
-                                    self.markov_head.w2, pending, draft, verify_ids, sc)
-        else:
-            raise NotImplementedError("drafters without a Markov head use markov_rank > 0 here")
 
     # ------------------------------------------------------------------ reference API
-    def embed(self, ids):
-        """ids [1, L] -> [1, L, H] bf16 (model.py:372-373)."""
-        ids = torch.as_tensor(ids, dtype=torch.int32).reshape(-1).to(self.device)
-        out = torch.empty(ids.numel(), self.config.hidden_size, dtype=torch.bfloat16,
-                          device=self.device)
-        ops.embed(ids, self.embed_w, out)
-        return out[None]
-
     def update_context(self, target_hidden_cat, ctx_offset, ctx_caches: CacheState) -> None:
         """fused [1, n, n_tap*H] at context positions ctx_offset.. (model.py:381-384)."""
         fused = target_hidden_cat.reshape(-1, target_hidden_cat.shape[-1])
@@ -174,17 +178,103 @@ class DSparkDrafter:
             pos += t
         ctx_caches.set_len(0, ctx_offset + n)
 
+    def embed(self, ids):
+        """ids [1, L] -> [1, L, H] bf16 (model.py:372-373)."""
+        ids = torch.as_tensor(ids, dtype=torch.int32).reshape(-1).to(self.device)
+        out = torch.empty(ids.numel(), self.config.hidden_size, dtype=torch.bfloat16,
+                          device=self.device)
+        ops.embed(ids, self.embed_w, out)
+        return out[None]
+
+
+class DSparkDrafter(BlockDrafter):
+    def __init__(self, weights: DSparkWeights, target: Target, device="cuda"):
+        cfg = weights.cfg
+        self.softcap = cfg.final_logit_softcapping
+        if self.softcap is not None:
+            raise NotImplementedError("logit softcapping (gemma4 drafters) is not built")
+        if cfg.norm_style != "qwen":
+            raise NotImplementedError("only the qwen3 drafter family is built")
+        embed_w = target.embed if weights.embed is None else pack(weights.embed, device=device)
+        head_w = target.head if weights.lm_head is None else pack(weights.lm_head, device=device)
+        super().__init__(cfg, weights.fc, weights.hidden_norm, weights.norm, weights.layers,
+                         target, embed_w, head_w, device)
+        self.markov_head = None
+        if weights.markov_w1 is not None:
+            self.markov_head = _Markov(pack(weights.markov_w1, device=device),
+                                       pack(weights.markov_w2, device=device), cfg.markov_rank)
+        self.confidence_head = None
+
+    def draft_dev(self, pending: torch.Tensor, B: int, cap: int, ctx: CacheState,
+                  buf: DraftBuffers, draft: torch.Tensor, verify_ids: torch.Tensor | None,
+                  splits: int, sampling: Sampling | None = None, rng: torch.Tensor | None = None,
+                  q_probs: torch.Tensor | None = None) -> None:
+        """Block -> backbone -> head over the first cap positions -> Markov head, greedy
+        (generate.py:846-852,910) or a temperature draft keeping q (model.py:283-309)."""
+        sc = self.scratch
+        k = self.block_size
+        self.backbone_dev(pending, B, ctx, buf, splits)
+        head_rows = cap if B == 1 else B * k
+        ops.gemm(buf.xn16, self.head_w, buf.base, epilogue=EPI_STORE_BF16, scratch=sc,
+                 M=head_rows)
+        rows_per_b = cap if B == 1 else k
+        sampled = sampling is not None and sampling.active
+        m = self.markov_head
+        if m is not None and not sampled:
+            ops.markov_sample_block(buf.base, rows_per_b, B, cap, m.w1, m.w2, pending, draft,
+                                    verify_ids, sc)
+        elif m is not None:
+            ops.markov_sample_block_probs(buf.base, rows_per_b, B, cap, m.w1, m.w2, pending, draft,
+                                          verify_ids, sampling.temperature, sampling.top_p,
+                                          sampling.top_k, rng, q_probs, sc)
+        else:
+            # no sequential head: every position is an independent argmax / draw
+            vids = None if verify_ids is None else verify_ids.view(B, cap + 1)
+            if vids is not None:
+                vids[:, 0].copy_(pending[:B])
+            for b in range(B):
+                base_b = buf.base[b * rows_per_b:b * rows_per_b + cap]
+                v2 = None if vids is None else vids[b, 1:]
+                if sampled:
+                    ops.sample_rows(base_b, 1, cap, sampling.temperature, sampling.top_p,
+                                    sampling.top_k, rng[b:b + 1], draft.view(B, cap)[b],
+                                    stream_id=1, probs=q_probs[b * cap:(b + 1) * cap],
+                                    tokens2=v2, temp_mode=1)
+                else:
+                    ops.argmax_rows(base_b, cap, draft.view(B, cap)[b], 1, v2, 1)
+
+    # ------------------------------------------------------------------ reference API
     def sample_block(self, base_logits, first_prev_token: int):
-        """base [cap, V] -> [cap] greedy tokens with the Markov head (model.py:398-409)."""
+        """base [cap, V] -> [cap] greedy tokens with the Markov head (model.py:270-281)."""
         base = base_logits.reshape(-1, base_logits.shape[-1]).to(torch.bfloat16).contiguous()
         cap = base.shape[0]
-        prev = torch.tensor([int(first_prev_token)], dtype=torch.int32, device=self.device)
-        draft = torch.empty(cap, dtype=torch.int32, device=self.device)
         if self.markov_head is None:
             return base.float().argmax(-1)
+        prev = torch.tensor([int(first_prev_token)], dtype=torch.int32, device=self.device)
+        draft = torch.empty(cap, dtype=torch.int32, device=self.device)
         ops.markov_sample_block(base, cap, 1, cap, self.markov_head.w1, self.markov_head.w2,
                                 prev, draft, None, self.scratch)
         return draft
+
+    def sample_block_probs(self, base_logits, first_prev_token: int, temperature: float,
+                           top_p: float = 1.0, top_k: int = 0):
+        """Temperature draft (model.py:283-309): (tokens [cap], probs [cap, V]). Draws come from
+        this drafter's Philox stream (seed()); the stream does not advance (the acceptance
+        step advances it in a decode loop)."""
+        base = base_logits.reshape(-1, base_logits.shape[-1]).to(torch.bfloat16).contiguous()
+        cap, V = base.shape
+        draft = torch.empty(cap, dtype=torch.int32, device=self.device)
+        probs = torch.zeros(cap, V, dtype=torch.float32, device=self.device)
+        prev = torch.tensor([int(first_prev_token)], dtype=torch.int32, device=self.device)
+        s = Sampling(temperature, top_p, top_k)
+        if self.markov_head is not None:
+            ops.markov_sample_block_probs(base, cap, 1, cap, self.markov_head.w1,
+                                          self.markov_head.w2, prev, draft, None, temperature,
+                                          top_p, top_k, self.rng, probs, self.scratch)
+        else:
+            ops.sample_rows(base, 1, cap, s.temperature, s.top_p, s.top_k, self.rng, draft,
+                            stream_id=1, probs=probs, temp_mode=1)
+        return draft, probs
 
     def weight_bytes_per_draft(self, cap: int) -> int:
         n = self.fc.nbytes()
@@ -194,3 +284,69 @@ class DSparkDrafter:
         if self.markov_head is not None:
             n += cap * self.markov_head.w2.nbytes()
         return n
+
+
+class DFlashDrafter(BlockDrafter):
+    """DFlash block-diffusion drafter bound to a target (dflash_model.py:167-208)."""
+
+    logits_start = 1
+
+    def __init__(self, weights: DFlashWeights, target: Target, device="cuda"):
+        cfg: DFlashConfig = weights.cfg
+        if any(t != "full_attention" for t in cfg.layer_types):
+            raise NotImplementedError("sliding-window DFlash layers are not built")
+        if cfg.final_logit_softcapping is not None:
+            raise NotImplementedError("logit softcapping is not built")
+        super().__init__(cfg, weights.fc, weights.hidden_norm, weights.norm, weights.layers,
+                         target, target.embed, target.head, device)
+        self.markov_head = None
+        self.confidence_head = None
+
+    def bind(self, target_model=None):
+        """The embedding and head are the target's from construction (dflash_model.py:171-186)."""
+        return self
+
+    def make_cache(self, max_tokens: int = 4096) -> CacheState:
+        return self.make_ctx_cache(max_tokens)
+
+    def draft_dev(self, pending: torch.Tensor, B: int, cap: int, ctx: CacheState,
+                  buf: DraftBuffers, draft: torch.Tensor, verify_ids: torch.Tensor | None,
+                  splits: int, sampling: Sampling | None = None, rng: torch.Tensor | None = None,
+                  q_probs: torch.Tensor | None = None) -> None:
+        """Block -> backbone -> target head over block rows 1..cap -> argmax or draws
+        (generate.py:537-549,561-565)."""
+        if B != 1:
+            raise NotImplementedError("DFlash drafts one request at a time (as dflash_generate)")
+        assert cap <= self.block_size - 1
+        self.backbone_dev(pending, 1, ctx, buf, splits)
+        x = buf.xn16[self.logits_start:self.logits_start + cap]
+        ops.gemm(x, self.head_w, buf.base, epilogue=EPI_STORE_BF16, scratch=self.scratch, M=cap)
+        base = buf.base[:cap]
+        v2 = None
+        if verify_ids is not None:
+            verify_ids.view(-1)[:1].copy_(pending[:1])
+            v2 = verify_ids.view(-1)[1:]
+        if sampling is not None and sampling.active:
+            ops.sample_rows(base, 1, cap, sampling.temperature, sampling.top_p, sampling.top_k,
+                            rng, draft.view(-1), stream_id=1, probs=q_probs[:cap], tokens2=v2,
+                            temp_mode=0)
+        else:
+            ops.argmax_rows(base, cap, draft.view(-1), 1, v2, 1)
+
+    def __call__(self, inputs, target_hidden, cache: CacheState, logits_start: int = 0):
+        """Reference forward: inputs [1, L] block ids, target_hidden [1, S, n_tap*H] new context
+        rows appended at the cache's length; returns logits [1, L - logits_start, V]."""
+        ids = torch.as_tensor(inputs, dtype=torch.int32).reshape(-1).to(self.device)
+        L = ids.numel()
+        assert L == self.block_size and int(ids[1:].eq(self.mask_token_id).all())
+        if target_hidden is not None and target_hidden.numel():
+            n0 = int(cache.seq_len[0])
+            self.update_context(target_hidden, n0, cache)
+        cache.ensure(0, int(cache.seq_len[0]) + self.block_size)
+        buf = self.buffers(1, self.block_size, 1)
+        self.backbone_dev(ids[:1], 1, cache, buf, self.target.attn_splits(1, cache.max_pages))
+        rows = L - logits_start
+        out = torch.zeros(rows, self.config.vocab_size, dtype=torch.bfloat16, device=self.device)
+        ops.gemm(buf.xn16[logits_start:], self.head_w, out, epilogue=EPI_STORE_BF16,
+                 scratch=self.scratch, M=rows)
+        return out[None]

@@ -172,6 +172,15 @@ def bf16_to_f16(src: torch.Tensor, dst: torch.Tensor, rows: int, cols: int) -> N
     call("dspark_bf16_to_f16", _p(src), src.stride(0), _p(dst), dst.stride(0), rows, cols, _stream())
 
 
+def argmax_rows(logits: torch.Tensor, rows: int, tokens: torch.Tensor, tok_stride: int = 1,
+                tokens2: torch.Tensor | None = None, tok2_stride: int = 1) -> torch.Tensor:
+    """First-index argmax of each row (the greedy draft of a head-less block drafter)."""
+    _require_cuda(logits, tokens)
+    call("dspark_argmax_rows", _p(logits), logits.stride(0), rows, logits.shape[-1], _p(tokens),
+         int(tok_stride), _p(tokens2), int(tok2_stride), _stream())
+    return tokens
+
+
 # ----------------------------------------------------------------------------------------
 # lossless speculative sampling (K9)
 def rng_state(seeds, device="cuda") -> torch.Tensor:
