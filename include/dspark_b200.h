@@ -278,6 +278,20 @@ int dspark_markov_sample_block_probs(const void* base, int ld, int rows_per_b, i
                                      dspark_stream_t stream);
 
 /* -------------------------------------------------------------------------------------
+ * R8 — OpenAI presence / frequency penalties (_Penalizer, src/mlx_dspark/generate.py:179-228).
+ * dspark_apply_penalties subtracts, in place, from row i of each verify block b (bf16 logits
+ * [B*T, ld]) the penalty of the completion counts counts[b, V] plus the block's draft prefix
+ * verify_ids[b, 1..i]: presence once per token, frequency per occurrence, in MLX's bf16
+ * arithmetic (block_penalty / apply, generate.py:202-228). verify_ids may be NULL when T == 1.
+ * dspark_penalty_counts_add adds the committed tokens plan[b, 2 .. 2 + plan[b, 1]) to
+ * counts[b] (pen.add, generate.py:941-949). T <= 64. */
+int dspark_apply_penalties(void* logits, long long ld, int B, int T, int V, const int32_t* counts,
+                           const int32_t* verify_ids, double presence, double frequency,
+                           dspark_stream_t stream);
+int dspark_penalty_counts_add(int32_t* counts, int B, int V, const int32_t* plan, int plan_stride,
+                              dspark_stream_t stream);
+
+/* -------------------------------------------------------------------------------------
  * Length-only commit: len_a[b] += plan[b*plan_stride + 1] (and len_b, if given). Used after
  * the drafter context update so both consumers read the pre-commit length first.
  * Replaces the trims of src/mlx_dspark/generate.py:929-938 (target KV) and the

@@ -57,6 +57,8 @@ SIGNATURES = {
     "dspark_markov_workspace_bytes": (c_size_t, [I, I]),
     "dspark_markov_sample_block": (I, [P, I, I, I, I, I, I, P, P, P, P, P, P, P, P, c_size_t, P, P]),
     "dspark_bf16_to_f16": (I, [P, I, P, I, I, I, P]),
+    "dspark_apply_penalties": (I, [P, c_longlong, I, I, I, P, P, c_double, c_double, P]),
+    "dspark_penalty_counts_add": (I, [P, I, I, P, I, P]),
     "dspark_argmax_rows": (I, [P, c_longlong, I, I, P, I, P, I, P]),
     "dspark_sample_rows": (I, [P, c_longlong, I, I, I, c_float, I, c_double, I, P, I, I, P,
                                c_longlong, P, I, P, I, P]),

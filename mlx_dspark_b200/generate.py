@@ -118,10 +118,17 @@ class SpecSession:
 
     def __init__(self, target, drafter, B: int, cap: int, max_tokens: int, *,
                  override: dict | None = None, sampling: Sampling | None = None,
-                 seeds=None):
+                 seeds=None, penalties: tuple[float, float] = (0.0, 0.0)):
         self.target, self.drafter = target, drafter
         self.B, self.cap = B, cap
         self.sampling = sampling if (sampling is not None and sampling.active) else None
+        # OpenAI presence / frequency penalties on the target rows (_Penalizer,
+        # generate.py:179-228): completion-token counts per row live on the device
+        self.penalties = (float(penalties[0] or 0.0), float(penalties[1] or 0.0))
+        self.counts = None
+        if any(self.penalties):
+            self.counts = torch.zeros(B, target.cfg.vocab_size, dtype=torch.int32,
+                                      device=target.device)
         self.k = drafter.block_size
         self.T = cap + 1
         self.tap = list(drafter.config.target_layer_ids)
@@ -177,6 +184,9 @@ class SpecSession:
             ops.draft_override(B, cap, t.cfg.vocab_size, o["ref"], o["agree"], o["round"],
                                self.tstate.seq_len, o["prompt_len"], self.vbuf.ids)
         t.forward(self.vbuf, self.tstate, self.tap, splits=self.splits_t)
+        if self.counts is not None:
+            ops.apply_penalties(self.vbuf.logits, B, T, self.counts, self.vbuf.ids,
+                                *self.penalties)
         if sm is None:
             ops.accept_greedy(self.vbuf.logits, B, T, self.vbuf.ids, self.argmax, None, False,
                               self.pending, self.plan, sc)
@@ -184,6 +194,8 @@ class SpecSession:
             ops.accept_sample(self.vbuf.logits, B, T, self.vbuf.ids, self.q, sm.temperature,
                               sm.top_p, sm.top_k, self.rng, None, False, self.pending, self.plan,
                               sc)
+        if self.counts is not None:
+            ops.penalty_counts_add(self.counts, self.plan, B)
         d.update_context_dev(self.vbuf.fused16, B, T, self.cstate, self.dbuf)
         ops.commit_lengths(self.plan, B, self.tstate.seq_len, self.cstate.seq_len)
         self.plan_host.copy_(self.plan, non_blocking=True)
@@ -225,17 +237,20 @@ def _pick_first(target, last_row: torch.Tensor, sampling: Sampling | None, rng: 
 
 
 def _spec_loop(target, tokenizer, drafter, ids, cap, max_new_tokens, sampling, seed, use_graph,
-               draft_override, verbose) -> GenResult:
+               draft_override, verbose, penalties=(0.0, 0.0)) -> GenResult:
     eos_ids = eos_token_ids(tokenizer)
     budget = len(ids) + max_new_tokens + cap + 1
     sampling = sampling if (sampling is not None and sampling.active) else None
     sess = SpecSession(target, drafter, 1, cap, budget, override=draft_override,
-                       sampling=sampling, seeds=[0 if seed is None else int(seed)])
+                       sampling=sampling, seeds=[0 if seed is None else int(seed)],
+                       penalties=penalties)
     try:
         t0 = time.time()
         last = prefill_rows(target, ids, sess.tstate, sess.tap, drafter, sess.cstate)
         pending = _pick_first(target, last, sampling, sess.rng)
         sess.pending.fill_(pending)
+        if sess.counts is not None:
+            sess.counts[0, pending] += 1          # pen.add([pending]) (generate.py:784)
         torch.cuda.synchronize()
         t1 = time.time()
         out = [pending]
@@ -282,8 +297,8 @@ def speculative_generate(target, tokenizer, drafter, prompt: str = "", *,
     temperature 0: the output is the target's greedy decoding. temperature > 0: drafts are drawn
     from the drafter's truncated distributions and accepted by rejection sampling, so the output
     is a sample of top-p/top-k(softmax(target / T)) (lossless); `seed` seeds the Philox stream."""
-    if presence_penalty or frequency_penalty or logprobs is not None or confidence_threshold > 0:
-        raise NotImplementedError("penalties / logprobs / confidence truncation are not built")
+    if logprobs is not None or confidence_threshold > 0:
+        raise NotImplementedError("logprobs / confidence truncation are not built")
     if lookup_drafts:
         raise NotImplementedError("hybrid n-gram drafts are not built on the device loop yet")
     k = drafter.config.block_size
@@ -292,7 +307,7 @@ def speculative_generate(target, tokenizer, drafter, prompt: str = "", *,
         prompt_ids = list(tokenizer.encode(prompt))
     return _spec_loop(target, tokenizer, drafter, list(prompt_ids), cap, max_new_tokens,
                       Sampling(temperature, top_p, top_k), seed, use_graph, draft_override,
-                      verbose)
+                      verbose, (presence_penalty, frequency_penalty))
 
 
 def dflash_generate(target_model, tokenizer, drafter, prompt: str = "", *,
@@ -319,8 +334,13 @@ class GreedySession:
     draw kernel advances on the device (so the step stays one CUDA graph)."""
 
     def __init__(self, target, B: int, max_tokens: int, sampling: Sampling | None = None,
-                 seeds=None):
+                 seeds=None, penalties: tuple[float, float] = (0.0, 0.0)):
         self.target, self.B = target, B
+        self.penalties = (float(penalties[0] or 0.0), float(penalties[1] or 0.0))
+        self.counts = None
+        if any(self.penalties):
+            self.counts = torch.zeros(B, target.cfg.vocab_size, dtype=torch.int32,
+                                      device=target.device)
         self.sampling = sampling if (sampling is not None and sampling.active) else None
         self.rng = ops.rng_state(list(seeds) if seeds is not None else [0] * B, target.device)
         dev = target.device
@@ -345,6 +365,8 @@ class GreedySession:
         t.forward(self.buf, self.tstate, (), splits=self.splits)
         # T = 1: n = 0, bonus = argmax (or a draw); the next input id is written in place
         sm = self.sampling
+        if self.counts is not None:
+            ops.apply_penalties(self.buf.logits, self.B, 1, self.counts, None, *self.penalties)
         if sm is None:
             ops.accept_greedy(self.buf.logits, self.B, 1, self.buf.ids, self.argmax,
                               self.tstate.seq_len, True, self.buf.ids, self.plan, t.scratch)
@@ -352,6 +374,8 @@ class GreedySession:
             ops.accept_sample(self.buf.logits, self.B, 1, self.buf.ids, None, sm.temperature,
                               sm.top_p, sm.top_k, self.rng, self.tstate.seq_len, True,
                               self.buf.ids, self.plan, t.scratch)
+        if self.counts is not None:
+            ops.penalty_counts_add(self.counts, self.plan, self.B)
         self.plan_host.copy_(self.plan, non_blocking=True)
 
     def capture(self):
@@ -383,19 +407,22 @@ def greedy_generate(target, tokenizer, prompt: str = "", *, prompt_ids: list[int
                     use_graph: bool = True) -> GenResult:
     """Plain decoding of the target (the baseline the speedup is measured against): greedy, or
     sampled with temperature / top-p / top-k from a Philox stream seeded by `seed`."""
-    if presence_penalty or frequency_penalty or logprobs is not None:
-        raise NotImplementedError("penalties / logprobs are not built")
+    if logprobs is not None:
+        raise NotImplementedError("logprobs are not built")
     eos_ids = eos_token_ids(tokenizer)
     if prompt_ids is None:
         prompt_ids = list(tokenizer.encode(prompt))
     ids = list(prompt_ids)
     sampling = Sampling(temperature, top_p, top_k)
     sess = GreedySession(target, 1, len(ids) + max_new_tokens + 1, sampling,
-                         [0 if seed is None else int(seed)])
+                         [0 if seed is None else int(seed)],
+                         (presence_penalty, frequency_penalty))
     try:
         t0 = time.time()
         last = prefill_rows(target, ids, sess.tstate, ())
         nxt = _pick_first(target, last, sess.sampling, sess.rng)
+        if sess.counts is not None:
+            sess.counts[0, nxt] += 1             # pen.add([nxt]) (generate.py:427)
         sess.buf.ids.fill_(nxt)
         torch.cuda.synchronize()
         t1 = time.time()

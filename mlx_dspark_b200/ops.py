@@ -172,6 +172,20 @@ def bf16_to_f16(src: torch.Tensor, dst: torch.Tensor, rows: int, cols: int) -> N
     call("dspark_bf16_to_f16", _p(src), src.stride(0), _p(dst), dst.stride(0), rows, cols, _stream())
 
 
+def apply_penalties(logits: torch.Tensor, B: int, T: int, counts: torch.Tensor,
+                    verify_ids: torch.Tensor | None, presence: float, frequency: float) -> None:
+    """In-place presence / frequency penalties on B verify blocks of T rows (_Penalizer)."""
+    _require_cuda(logits, counts)
+    call("dspark_apply_penalties", _p(logits), logits.stride(0), B, T, logits.shape[-1],
+         _p(counts), _p(verify_ids), float(presence), float(frequency), _stream())
+
+
+def penalty_counts_add(counts: torch.Tensor, plan: torch.Tensor, B: int) -> None:
+    """counts[b] += the committed tokens of plan row b."""
+    call("dspark_penalty_counts_add", _p(counts), B, counts.shape[-1], _p(plan), plan.stride(0),
+         _stream())
+
+
 def argmax_rows(logits: torch.Tensor, rows: int, tokens: torch.Tensor, tok_stride: int = 1,
                 tokens2: torch.Tensor | None = None, tok2_stride: int = 1) -> torch.Tensor:
     """First-index argmax of each row (the greedy draft of a head-less block drafter)."""

@@ -173,3 +173,41 @@ def test_sampled_plain_decode_replays_exactly(pair):
     res = greedy_generate(target, None, prompt_ids=prompt, max_new_tokens=24, temperature=0.7,
                           top_k=20, seed=seed)
     assert res.num_tokens == 24
+
+
+def _penalized_teacher_forced(ref_t, prompt, tokens, P, F):
+    from oracle.penalties import Penalizer
+    from test_gpu_e2e import _gap_tol
+    cache = ref_t.make_cache()
+    seq = list(prompt) + list(tokens[:-1])
+    rows, pos = [], 0
+    while pos < len(seq):
+        lg, _ = ref_t.run(seq[pos:pos + 64], cache, ())
+        rows.append(lg)
+        pos += 64
+    rows = torch.cat(rows, 0)[len(prompt) - 1:]
+    excused = 0
+    for i, t in enumerate(tokens):
+        pen = Penalizer(P, F)
+        pen.add(tokens[:i])
+        r = pen.apply(rows[i].to(torch.bfloat16)[None], [])[0].float()
+        top = int(r.argmax())
+        if t != top:
+            gap = float(r[top] - r[t])
+            assert gap <= _gap_tol(float(r[top])), (i, t, top, gap)
+            excused += 1
+    return excused
+
+
+def test_penalized_greedy_decoding_matches_oracle(pair):
+    P, F = 0.6, 0.4
+    spec = speculative_generate(pair["target"], None, pair["dspark"], prompt_ids=pair["prompt"],
+                                max_new_tokens=48, max_draft_tokens=None, presence_penalty=P,
+                                frequency_penalty=F)
+    plain = greedy_generate(pair["target"], None, prompt_ids=pair["prompt"], max_new_tokens=48,
+                            presence_penalty=P, frequency_penalty=F)
+    for res in (spec, plain):
+        assert _penalized_teacher_forced(pair["ref_t"], pair["prompt"], res.token_ids[:48], P, F) <= 3
+    # penalties change the output of this repetitive random-init model
+    base = greedy_generate(pair["target"], None, prompt_ids=pair["prompt"], max_new_tokens=48)
+    assert base.token_ids != plain.token_ids

@@ -217,3 +217,37 @@ def test_markov_sample_block_probs_matches_oracle(cuda):
             assert np.array_equal(q[b, i].cpu().numpy(), qi), (b, i)
             prev = t
         assert vids[b].tolist() == [first[b]] + draft[b].tolist()
+
+
+def test_apply_penalties_matches_oracle(cuda):
+    from oracle.penalties import Penalizer
+    B, T, V = 2, 9, 32768
+    g = torch.Generator().manual_seed(3)
+    logits = (torch.randn(B * T, V, generator=g) * 4).to(torch.bfloat16)
+    hist = [[5, 5, 9, 100, 31000] + [7] * 300, [1, 2, 3, 3]]
+    drafts = [[5, 5, 11, 11, 9, 8, 7, 6], [3, 4, 4, 4, 2, 30000, 1, 1]]
+    counts = torch.zeros(B, V, dtype=torch.int32)
+    vid = torch.zeros(B, T, dtype=torch.int32)
+    for b in range(B):
+        for t in hist[b]:
+            counts[b, t] += 1
+        vid[b, 1:] = torch.tensor(drafts[b])
+    out = logits.clone().to(cuda)
+    ops.apply_penalties(out, B, T, counts.to(cuda), vid.to(cuda), 0.4, 0.3)
+    torch.cuda.synchronize()
+    for b in range(B):
+        p = Penalizer(0.4, 0.3)
+        p.add(hist[b])
+        exp = p.apply(logits[b * T:(b + 1) * T], drafts[b])
+        assert torch.equal(out[b * T:(b + 1) * T].cpu(), exp), b
+    # counts advance by a plan's committed tokens
+    plan = torch.tensor([[2, 3, 5, 5, 17, -1, -1, -1, -1, -1, -1],
+                         [0, 1, 4, -1, -1, -1, -1, -1, -1, -1, -1]], dtype=torch.int32)
+    c = counts.to(cuda)
+    ops.penalty_counts_add(c, plan.to(cuda), B)
+    torch.cuda.synchronize()
+    exp = counts.clone()
+    exp[0, 5] += 2
+    exp[0, 17] += 1
+    exp[1, 4] += 1
+    assert torch.equal(c.cpu(), exp)
