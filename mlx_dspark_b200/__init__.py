@@ -11,12 +11,13 @@ __version__ = "0.1.0"
 from .config import DFlashConfig, DSparkConfig, TargetConfig, WORKLOADS, TARGETS
 from .generate import GenResult, dflash_generate, greedy_generate, speculative_generate
 from .load import load_dflash_drafter, load_drafter, load_pair, load_target
+from .lookup import NGramIndex, lookup_generate
 from .model import DFlashDrafter, DSparkDrafter, Sampling
 from .target import Target
 
 __all__ = [
     "DSparkConfig", "DFlashConfig", "TargetConfig", "Target", "DSparkDrafter", "DFlashDrafter",
     "Sampling", "load_drafter", "load_dflash_drafter", "load_target", "load_pair",
-    "speculative_generate", "dflash_generate", "greedy_generate", "GenResult", "WORKLOADS",
-    "TARGETS",
+    "speculative_generate", "dflash_generate", "greedy_generate", "lookup_generate",
+    "NGramIndex", "GenResult", "WORKLOADS", "TARGETS",
 ]

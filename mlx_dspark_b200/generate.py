@@ -210,6 +210,24 @@ class SpecSession:
         torch.cuda.current_stream().wait_stream(s)
         self.graph = g
 
+    def lookup_round(self, pending: int, draft: list[int]) -> list[int]:
+        """A hybrid round that verifies an n-gram lookup draft instead of drafting
+        (generate.py:807-837): verify [pending] + draft with the tap, accept (greedy, or the
+        one-hot proposal when sampling), write the drafter context from the verified rows,
+        then commit both lengths. Runs eagerly: its width follows the match length."""
+        from .lookup import BlockVerifier  # lookup imports this module
+        if self.B != 1:
+            raise NotImplementedError("hybrid lookup rounds are batch 1 (as the reference)")
+        if getattr(self, "_verifier", None) is None:
+            self._verifier = BlockVerifier(self.target, self.tstate, self.tap, self.sampling,
+                                           self.rng, self.counts, self.penalties, self.pending)
+        T = len(draft) + 1
+        buf, plan, plan_host = self._verifier.launch(pending, draft, commit=False)
+        self.drafter.update_context_dev(buf.fused16, 1, T, self.cstate,
+                                        self.drafter.buffers(1, self.k, T))
+        ops.commit_lengths(plan, 1, self.tstate.seq_len, self.cstate.seq_len)
+        return self._verifier.finish(plan, plan_host)
+
     def step(self, use_graph: bool = True, feed_pending: bool = False):
         """Run one round; returns the plan rows [B, T+2] as python lists. With feed_pending
         the round's input token comes from pending_host (pinned) by one H2D copy, as in a
@@ -237,7 +255,7 @@ def _pick_first(target, last_row: torch.Tensor, sampling: Sampling | None, rng: 
 
 
 def _spec_loop(target, tokenizer, drafter, ids, cap, max_new_tokens, sampling, seed, use_graph,
-               draft_override, verbose, penalties=(0.0, 0.0)) -> GenResult:
+               draft_override, verbose, penalties=(0.0, 0.0), lookup_max_draft=0) -> GenResult:
     eos_ids = eos_token_ids(tokenizer)
     budget = len(ids) + max_new_tokens + cap + 1
     sampling = sampling if (sampling is not None and sampling.active) else None
@@ -251,32 +269,49 @@ def _spec_loop(target, tokenizer, drafter, ids, cap, max_new_tokens, sampling, s
         sess.pending.fill_(pending)
         if sess.counts is not None:
             sess.counts[0, pending] += 1          # pen.add([pending]) (generate.py:784)
+        index = None
+        if lookup_max_draft:
+            from .lookup import NGramIndex  # lookup imports this module
+            # hybrid mode: a stricter 4-gram minimum than pure lookup (generate.py:789-798)
+            index = NGramIndex(min_n=4, max_n=5, max_draft=lookup_max_draft)
+            index.extend(ids + [pending])
         torch.cuda.synchronize()
         t1 = time.time()
         out = [pending]
         accept = []
-        rounds = 0
+        rounds = lookup_rounds = 0
         while len(out) < max_new_tokens and pending not in eos_ids:
-            sess.pending_host[0] = pending
-            plan = sess.step(use_graph, feed_pending=True)[0]
-            if use_graph and sess.graph is None:
-                sess.capture()
+            lk = index.propose() if index is not None else []
+            if lk:
+                lookup_rounds += 1
+                plan = sess.lookup_round(pending, lk)
+            else:
+                sess.pending_host[0] = pending
+                plan = sess.step(use_graph, feed_pending=True)[0]
+                if use_graph and sess.graph is None:
+                    sess.capture()
             n = plan[0]
             committed = plan[2:3 + n]
             accept.append(len(committed))
+            appended = []
             for tok in committed:
                 out.append(tok)
+                appended.append(tok)
                 if tok in eos_ids:
                     break
+            if index is not None:
+                index.extend(appended)
             pending = out[-1]
             rounds += 1
             if verbose:
-                print(f"  round {rounds:3d}: drafted {cap}, accepted {n}, committed {len(committed)}")
+                src = "lookup" if lk else "drafter"
+                print(f"  round {rounds:3d}: {src} drafted {len(lk) if lk else cap}, accepted {n}, "
+                      f"committed {len(committed)}")
         t2 = time.time()
         text = _decode(tokenizer, [t for t in out if t not in eos_ids])
         return GenResult(text=text, token_ids=out, num_tokens=len(out), num_rounds=len(accept),
                          accept_lengths=accept, target_forwards=len(accept) + 1,
-                         seconds=t2 - t0, decode_seconds=t2 - t1,
+                         seconds=t2 - t0, decode_seconds=t2 - t1, lookup_rounds=lookup_rounds,
                          finish_reason=_finish_reason(out, max_new_tokens, pending, eos_ids))
     finally:
         sess.release()
@@ -299,15 +334,14 @@ def speculative_generate(target, tokenizer, drafter, prompt: str = "", *,
     is a sample of top-p/top-k(softmax(target / T)) (lossless); `seed` seeds the Philox stream."""
     if logprobs is not None or confidence_threshold > 0:
         raise NotImplementedError("logprobs / confidence truncation are not built")
-    if lookup_drafts:
-        raise NotImplementedError("hybrid n-gram drafts are not built on the device loop yet")
     k = drafter.config.block_size
     cap = k if max_draft_tokens is None else max(1, min(int(max_draft_tokens), k))
     if prompt_ids is None:
         prompt_ids = list(tokenizer.encode(prompt))
     return _spec_loop(target, tokenizer, drafter, list(prompt_ids), cap, max_new_tokens,
                       Sampling(temperature, top_p, top_k), seed, use_graph, draft_override,
-                      verbose, (presence_penalty, frequency_penalty))
+                      verbose, (presence_penalty, frequency_penalty),
+                      max(1, int(lookup_max_draft)) if lookup_drafts else 0)
 
 
 def dflash_generate(target_model, tokenizer, drafter, prompt: str = "", *,
