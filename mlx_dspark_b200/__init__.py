@@ -12,6 +12,8 @@ from .config import DFlashConfig, DSparkConfig, TargetConfig, WORKLOADS, TARGETS
 from .generate import GenResult, dflash_generate, greedy_generate, speculative_generate
 from .load import load_dflash_drafter, load_drafter, load_pair, load_target
 from .lookup import NGramIndex, lookup_generate
+from .batch_engine import SpecSlots, batch_generate_baseline, batch_spec_generate, serve_requests
+from .prefix_cache import PrefixBlocks, PrefixCache
 from .model import DFlashDrafter, DSparkDrafter, Sampling
 from .target import Target
 
@@ -19,5 +21,6 @@ __all__ = [
     "DSparkConfig", "DFlashConfig", "TargetConfig", "Target", "DSparkDrafter", "DFlashDrafter",
     "Sampling", "load_drafter", "load_dflash_drafter", "load_target", "load_pair",
     "speculative_generate", "dflash_generate", "greedy_generate", "lookup_generate",
-    "NGramIndex", "GenResult", "WORKLOADS", "TARGETS",
+    "NGramIndex", "SpecSlots", "batch_spec_generate", "batch_generate_baseline",
+    "serve_requests", "PrefixCache", "PrefixBlocks", "GenResult", "WORKLOADS", "TARGETS",
 ]

@@ -118,7 +118,7 @@ class SpecSession:
 
     def __init__(self, target, drafter, B: int, cap: int, max_tokens: int, *,
                  override: dict | None = None, sampling: Sampling | None = None,
-                 seeds=None, penalties: tuple[float, float] = (0.0, 0.0)):
+                 seeds=None, penalties: tuple[float, float] = (0.0, 0.0), states=None):
         self.target, self.drafter = target, drafter
         self.B, self.cap = B, cap
         self.sampling = sampling if (sampling is not None and sampling.active) else None
@@ -135,11 +135,16 @@ class SpecSession:
         dev = target.device
         # pages for the whole request budget, plus one drafted block past the end
         cap_tokens = max_tokens + self.k + self.T + 64
-        self.tstate = CacheState(target.new_pool(cap_tokens, B), B, cap_tokens, dev)
-        self.cstate = CacheState(drafter.new_pool(cap_tokens, B), B, cap_tokens, dev)
-        for b in range(B):
-            self.tstate.ensure(b, cap_tokens)
-            self.cstate.ensure(b, cap_tokens)
+        self._owns_states = states is None
+        if states is None:
+            self.tstate = CacheState(target.new_pool(cap_tokens, B), B, cap_tokens, dev)
+            self.cstate = CacheState(drafter.new_pool(cap_tokens, B), B, cap_tokens, dev)
+            for b in range(B):
+                self.tstate.ensure(b, cap_tokens)
+                self.cstate.ensure(b, cap_tokens)
+        else:
+            # caller-owned rows (prefix reuse, the batch engine): the caller provides pages
+            self.tstate, self.cstate = states
         self.vbuf = target.buffers(B, self.T, len(self.tap))
         self.dbuf = drafter.buffers(B, self.k, B * self.T)
         self.pending = torch.zeros(B, dtype=torch.int32, device=dev)
@@ -170,8 +175,9 @@ class SpecSession:
 
     def release(self):
         self.graph = None
-        self.tstate.release()
-        self.cstate.release()
+        if self._owns_states:
+            self.tstate.release()
+            self.cstate.release()
 
     def launch_round(self) -> None:
         d, t, sc = self.drafter, self.target, self.target.scratch
@@ -200,6 +206,10 @@ class SpecSession:
         ops.commit_lengths(self.plan, B, self.tstate.seq_len, self.cstate.seq_len)
         self.plan_host.copy_(self.plan, non_blocking=True)
 
+    def _versions(self):
+        return (self.tstate.pool.version, self.cstate.pool.version,
+                self.target.scratch.version, self.tstate.max_pages, self.cstate.max_pages)
+
     def capture(self) -> None:
         g = torch.cuda.CUDAGraph()
         s = torch.cuda.Stream()
@@ -209,6 +219,7 @@ class SpecSession:
                 self.launch_round()
         torch.cuda.current_stream().wait_stream(s)
         self.graph = g
+        self._graph_versions = self._versions()
 
     def lookup_round(self, pending: int, draft: list[int]) -> list[int]:
         """A hybrid round that verifies an n-gram lookup draft instead of drafting
@@ -234,6 +245,8 @@ class SpecSession:
         host-driven loop where the host owns the committed sequence."""
         if feed_pending:
             self.pending.copy_(self.pending_host, non_blocking=True)
+        if self.graph is not None and self._graph_versions != self._versions():
+            self.graph = None  # a pool, block table or workspace moved: capture again
         if use_graph and self.graph is not None:
             self.graph.replay()
         else:
@@ -254,17 +267,42 @@ def _pick_first(target, last_row: torch.Tensor, sampling: Sampling | None, rng: 
     return int(tok.item())
 
 
+def _caller_states(drafter, cache, ctx_caches, reuse_len: int, tokens: int):
+    """The CacheStates of caller-provided caches, widened and paged for `tokens` positions and
+    trimmed to the reused prefix (the reference trims its caches to reuse_len the same way)."""
+    if ctx_caches is None:
+        ctx_caches = drafter.make_ctx_cache(tokens)
+        if reuse_len:
+            raise ValueError("reuse_len needs the drafter context caches of the reused prefix")
+    tstate, cstate = cache.state, ctx_caches.state
+    for st in (tstate, cstate):
+        st.grow(tokens)
+        st.ensure(0, tokens)
+        st.set_len(0, reuse_len)
+    return tstate, cstate, ctx_caches
+
+
 def _spec_loop(target, tokenizer, drafter, ids, cap, max_new_tokens, sampling, seed, use_graph,
-               draft_override, verbose, penalties=(0.0, 0.0), lookup_max_draft=0) -> GenResult:
+               draft_override, verbose, penalties=(0.0, 0.0), lookup_max_draft=0, cache=None,
+               ctx_caches=None, reuse_len: int = 0) -> GenResult:
     eos_ids = eos_token_ids(tokenizer)
     budget = len(ids) + max_new_tokens + cap + 1
     sampling = sampling if (sampling is not None and sampling.active) else None
+    states = None
+    if cache is not None:
+        tokens = budget + drafter.block_size + cap + 1 + 64
+        tstate, cstate, ctx_caches = _caller_states(drafter, cache, ctx_caches, int(reuse_len),
+                                                    tokens)
+        states = (tstate, cstate)
+    else:
+        reuse_len = 0
     sess = SpecSession(target, drafter, 1, cap, budget, override=draft_override,
                        sampling=sampling, seeds=[0 if seed is None else int(seed)],
-                       penalties=penalties)
+                       penalties=penalties, states=states)
     try:
         t0 = time.time()
-        last = prefill_rows(target, ids, sess.tstate, sess.tap, drafter, sess.cstate)
+        # prefill only the part of the prompt past the reused prefix (generate.py:640-650)
+        last = prefill_rows(target, ids[reuse_len:], sess.tstate, sess.tap, drafter, sess.cstate)
         pending = _pick_first(target, last, sampling, sess.rng)
         sess.pending.fill_(pending)
         if sess.counts is not None:
@@ -315,6 +353,11 @@ def _spec_loop(target, tokenizer, drafter, ids, cap, max_new_tokens, sampling, s
                          finish_reason=_finish_reason(out, max_new_tokens, pending, eos_ids))
     finally:
         sess.release()
+        if cache is not None:
+            # the caller's caches now hold prompt + every committed token but the pending one
+            n = sess.tstate.sync_from_device()[0]
+            cache.set_offset(n)
+            sess.cstate.sync_from_device()
 
 
 def speculative_generate(target, tokenizer, drafter, prompt: str = "", *,
@@ -341,7 +384,8 @@ def speculative_generate(target, tokenizer, drafter, prompt: str = "", *,
     return _spec_loop(target, tokenizer, drafter, list(prompt_ids), cap, max_new_tokens,
                       Sampling(temperature, top_p, top_k), seed, use_graph, draft_override,
                       verbose, (presence_penalty, frequency_penalty),
-                      max(1, int(lookup_max_draft)) if lookup_drafts else 0)
+                      max(1, int(lookup_max_draft)) if lookup_drafts else 0, cache, ctx_caches,
+                      reuse_len)
 
 
 def dflash_generate(target_model, tokenizer, drafter, prompt: str = "", *,

@@ -39,8 +39,25 @@ class PagePool:
                                 device=device)
         self.free = list(range(num_pages - 1, -1, -1))
         self.refs = [0] * num_pages
+        self.version = 0          # bumped when `data` moves (layouts hold its address)
+        self.growable = True
+
+    def grow(self, num_pages: int) -> None:
+        """Reallocate to `num_pages` pages, copying the old ones (page ids stay valid)."""
+        if num_pages <= self.num_pages:
+            return
+        data = torch.zeros(self.n_layers, num_pages, self.page_bytes, dtype=torch.uint8,
+                           device=self.data.device)
+        data[:, :self.num_pages].copy_(self.data)
+        self.data = data
+        self.free = list(range(num_pages - 1, self.num_pages - 1, -1)) + self.free
+        self.refs += [0] * (num_pages - self.num_pages)
+        self.num_pages = num_pages
+        self.version += 1
 
     def alloc(self, n: int) -> list[int]:
+        if n > len(self.free) and self.growable:
+            self.grow(self.num_pages + max(n - len(self.free), self.num_pages // 2))
         if n > len(self.free):
             raise MemoryError(f"KV page pool exhausted ({n} pages wanted, {len(self.free)} free)")
         out = [self.free.pop() for _ in range(n)]
@@ -78,8 +95,20 @@ class CacheState:
         self.pages: list[list[int]] = [[] for _ in range(rows)]
         self.host_len = [0] * rows
         self._layouts = None
+        self._layout_version = -1
 
     # -- pages --
+    def grow(self, max_tokens: int) -> None:
+        """Widen the block table so rows can hold `max_tokens` positions (pages stay put)."""
+        need = (max_tokens + PAGE - 1) // PAGE
+        if need <= self.max_pages:
+            return
+        bt = torch.zeros(self.rows, need, dtype=torch.int32, device=self.block_table.device)
+        bt[:, :self.max_pages] = self.block_table
+        self.block_table = bt
+        self.max_pages = need
+        self._layouts = None
+
     def ensure(self, row: int, tokens: int) -> None:
         """Make sure positions [0, tokens) of `row` have pages."""
         need = (tokens + PAGE - 1) // PAGE
@@ -128,9 +157,21 @@ class CacheState:
         self.host_len = [int(x) for x in self.seq_len.tolist()]
         return self.host_len
 
+    def move_row(self, src: int, dst: int) -> None:
+        """Row dst takes over row src's pages and length (batch compaction: a block-table row
+        copy, no KV bytes move); row src is left empty. dst's old pages must be released."""
+        assert not self.pages[dst], "move_row: release the destination row first"
+        self.pages[dst] = self.pages[src]
+        self.pages[src] = []
+        self.block_table[dst].copy_(self.block_table[src])
+        self.seq_len[dst] = self.seq_len[src]
+        self.host_len[dst] = self.host_len[src]
+        self.set_len(src, 0)
+
     def layout(self, layer: int) -> ops.KvLayout:
-        if self._layouts is None:
+        if self._layouts is None or self._layout_version != self.pool.version:
             self._layouts = [self.pool.layout(l, self.block_table) for l in range(self.pool.n_layers)]
+            self._layout_version = self.pool.version
         return self._layouts[layer]
 
 
@@ -145,10 +186,12 @@ class RowView:
         self.block_table = state.block_table[row:row + 1]
         self.seq_len = state.seq_len[row:row + 1]
         self._layouts = None
+        self._layout_version = -1
 
     def layout(self, layer: int) -> ops.KvLayout:
-        if self._layouts is None:
+        if self._layouts is None or self._layout_version != self.pool.version:
             self._layouts = [self.pool.layout(l, self.block_table) for l in range(self.pool.n_layers)]
+            self._layout_version = self.pool.version
         return self._layouts[layer]
 
 
@@ -214,6 +257,38 @@ class TargetCache(list):
         for c in self:
             c.offset = n
         self.state.host_len[0] = n
+
+    def release(self) -> None:
+        self.state.release()
+
+
+class _CtxLayer:
+    """One layer's view of a drafter context cache (reference CtxCache duck type,
+    src/mlx_dspark/model.py:176-208): every layer shares the cache's single length."""
+
+    def __init__(self, parent: "CtxCaches"):
+        self._parent = parent
+
+    @property
+    def length(self) -> int:
+        return self._parent.state.host_len[0]
+
+    def trim_to(self, length: int) -> None:
+        st = self._parent.state
+        if length < st.host_len[0]:
+            st.set_len(0, max(0, int(length)))
+
+
+class CtxCaches(list):
+    """make_ctx_cache() result for one sequence: per-layer views over one CacheState."""
+
+    def __init__(self, state: CacheState, n_layers: int):
+        super().__init__(_CtxLayer(self) for _ in range(n_layers))
+        self.state = state
+
+    @property
+    def length(self) -> int:
+        return self.state.host_len[0]
 
     def release(self) -> None:
         self.state.release()

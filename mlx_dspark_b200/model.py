@@ -27,7 +27,7 @@ import torch
 from . import ops
 from ._lib import EPI_RESIDUAL_BF16, EPI_SILU_MUL_F16, EPI_STORE_BF16
 from .config import DFlashConfig, DSparkConfig
-from .kvcache import PAGE, CacheState, PagePool
+from .kvcache import PAGE, CacheState, CtxCaches, PagePool
 from .target import PackedLayer, Target, rope_inv_freq
 from .weights import DFlashWeights, DSparkWeights, pack
 
@@ -110,8 +110,10 @@ class BlockDrafter:
         return PagePool(len(self.layers), pages, c.num_key_value_heads, c.head_dim, False,
                         self.device)
 
-    def make_ctx_cache(self, max_tokens: int = 4096) -> CacheState:
-        return CacheState(self.new_pool(max_tokens), 1, max_tokens, self.device)
+    def make_ctx_cache(self, max_tokens: int = 4096) -> CtxCaches:
+        """Per-layer context caches of one sequence (model.py:250-251) over a paged pool."""
+        return CtxCaches(CacheState(self.new_pool(max_tokens), 1, max_tokens, self.device),
+                         len(self.layers))
 
     def buffers(self, B: int, k: int, ctx_rows: int) -> DraftBuffers:
         key = (B, k, ctx_rows)
@@ -162,10 +164,12 @@ class BlockDrafter:
         ops.rmsnorm(buf.h, self.norm, c.rms_norm_eps, y16=buf.xn16, M=M)
 
     # ------------------------------------------------------------------ reference API
-    def update_context(self, target_hidden_cat, ctx_offset, ctx_caches: CacheState) -> None:
+    def update_context(self, target_hidden_cat, ctx_offset, ctx_caches) -> None:
         """fused [1, n, n_tap*H] at context positions ctx_offset.. (model.py:381-384)."""
+        ctx_caches = getattr(ctx_caches, "state", ctx_caches)
         fused = target_hidden_cat.reshape(-1, target_hidden_cat.shape[-1])
         n = fused.shape[0]
+        ctx_caches.grow(ctx_offset + n + self.block_size)
         ctx_caches.ensure(0, ctx_offset + n + self.block_size)
         pos = 0
         T = self.target.chunk_len(1)
@@ -306,7 +310,7 @@ class DFlashDrafter(BlockDrafter):
         """The embedding and head are the target's from construction (dflash_model.py:171-186)."""
         return self
 
-    def make_cache(self, max_tokens: int = 4096) -> CacheState:
+    def make_cache(self, max_tokens: int = 4096) -> CtxCaches:
         return self.make_ctx_cache(max_tokens)
 
     def draft_dev(self, pending: torch.Tensor, B: int, cap: int, ctx: CacheState,
@@ -333,9 +337,10 @@ class DFlashDrafter(BlockDrafter):
         else:
             ops.argmax_rows(base, cap, draft.view(-1), 1, v2, 1)
 
-    def __call__(self, inputs, target_hidden, cache: CacheState, logits_start: int = 0):
+    def __call__(self, inputs, target_hidden, cache, logits_start: int = 0):
         """Reference forward: inputs [1, L] block ids, target_hidden [1, S, n_tap*H] new context
         rows appended at the cache's length; returns logits [1, L - logits_start, V]."""
+        cache = getattr(cache, "state", cache)
         ids = torch.as_tensor(inputs, dtype=torch.int32).reshape(-1).to(self.device)
         L = ids.numel()
         assert L == self.block_size and int(ids[1:].eq(self.mask_token_id).all())

@@ -37,12 +37,14 @@ class Scratch:
         self.device = torch.device(device)
         self.bufs: dict[str, torch.Tensor] = {}
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.version = 0  # bumped when a buffer moves (captured graphs hold the addresses)
 
     def get(self, family: str, nbytes: int) -> torch.Tensor:
         b = self.bufs.get(family)
         if b is None or b.numel() < nbytes:
             b = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=self.device)
             self.bufs[family] = b
+            self.version += 1
         return b
 
     def reserve(self, family: str, nbytes: int) -> None:
