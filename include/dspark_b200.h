@@ -316,7 +316,23 @@ int dspark_draft_override(int B, int cap, int V, const int32_t* ref, int ref_len
  * a Markov head (model.py:272-273). Token of row r -> tokens[r * tok_stride] and, if given,
  * tokens2[r * tok2_stride]. */
 int dspark_argmax_rows(const void* logits, long long ld, int rows, int V, int32_t* tokens,
-                       int tok_stride, int32_t* tokens2, int tok2_stride, dspark_stream_t stream);
+                       int tok_stride, int32_t* tokens2, int tok2_stride, float* values,
+                       int index_offset, dspark_stream_t stream);
+
+/* Tensor-parallel pieces (BASELINE C5: Qwen3-32B at TP 2/4/8; NCCL all-reduce after o_proj
+ * and down_proj). The reference runs on one device and has no counterpart; they stand in for
+ * its single-device o_proj / down_proj residual adds and the lm_head argmax.
+ * dspark_residual_add_f32: h = bf16(h + bf16(sum)) — the RESIDUAL_BF16 epilogue applied after
+ *   the fp32 partials of a row-split projection were all-reduced.
+ * dspark_accept_greedy_sharded: greedy acceptance when each of `shards` ranks holds a vocabulary
+ *   slice: values / indices [shards, B*T] are every shard's row maximum and its global index
+ *   (dspark_argmax_rows with values and index_offset); the row argmax is the largest value,
+ *   ties to the smallest index; outputs as dspark_accept_greedy. T <= 64. */
+int dspark_residual_add_f32(void* h, int ldh, const float* sum, int lds, int M, int N,
+                            dspark_stream_t stream);
+int dspark_accept_greedy_sharded(const float* values, const int32_t* indices, int shards, int B,
+                                 int T, const int32_t* verify_ids, int32_t* kv_len, int commit,
+                                 int32_t* pending, int32_t* plan, dspark_stream_t stream);
 
 /* drafter block embedding: row b*k + i embeds pending[b] if i == 0 else mask_id
  * (src/mlx_dspark/generate.py:848-849, batch_engine.py:548-549); ids_out optional [B*k] */

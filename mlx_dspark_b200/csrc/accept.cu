@@ -148,7 +148,7 @@ __global__ void draft_override_kernel(int B, int cap, int V, const int32_t* __re
 constexpr int kArgThreads = 1024;
 __global__ void __launch_bounds__(kArgThreads) argmax_rows_kernel(
     const __nv_bfloat16* __restrict__ logits, long long ld, int V, int32_t* __restrict__ tokens,
-    int s1, int32_t* __restrict__ tokens2, int s2) {
+    int s1, int32_t* __restrict__ tokens2, int s2, float* __restrict__ values, int index_offset) {
   pdl_wait();
   pdl_launch_dependents();
   const int r = blockIdx.x;
@@ -174,10 +174,44 @@ __global__ void __launch_bounds__(kArgThreads) argmax_rows_kernel(
     b = red[lane];
     b = warp_best(b);
     if (lane == 0) {
-      const int t = b.i == 0x7fffffff ? 0 : b.i;
+      const int t = (b.i == 0x7fffffff ? 0 : b.i) + index_offset;
       tokens[(size_t)r * s1] = t;
       if (tokens2) tokens2[(size_t)r * s2] = t;
+      if (values) values[r] = b.v;
     }
+  }
+}
+
+// Greedy acceptance over a vocabulary split across `shards` ranks: row r's argmax is the
+// largest of the shards' (value, global index) pairs, ties to the smallest index (the
+// mx.argmax rule over the whole row). Then the accepted prefix, plan, pending and commit of
+// accept_greedy_kernel. One thread per batch row.
+__global__ void accept_sharded_kernel(const float* __restrict__ vals, const int32_t* __restrict__ idx,
+                                      int shards, int B, int T, const int32_t* __restrict__ verify_ids,
+                                      int32_t* __restrict__ kv_len, int commit,
+                                      int32_t* __restrict__ pending, int32_t* __restrict__ plan) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int rows = B * T;
+  for (int b = threadIdx.x; b < B; b += blockDim.x) {
+    int tt[64];
+    for (int t = 0; t < T; ++t) {
+      const int r = b * T + t;
+      Best best{-INFINITY, 0x7fffffff};
+      for (int s = 0; s < shards; ++s)
+        best = better(best, Best{vals[(size_t)s * rows + r], idx[(size_t)s * rows + r]});
+      tt[t] = best.i == 0x7fffffff ? 0 : best.i;
+    }
+    int n = 0;
+    while (n < T - 1 && verify_ids[b * T + n + 1] == tt[n]) ++n;
+    int32_t* pl = plan + (size_t)b * (T + 2);
+    pl[0] = n;
+    pl[1] = n + 1;
+    for (int i = 0; i < n; ++i) pl[2 + i] = verify_ids[b * T + i + 1];
+    pl[2 + n] = tt[n];
+    for (int i = n + 1; i < T; ++i) pl[2 + i] = -1;
+    pending[b] = tt[n];
+    if (commit) kv_len[b] += n + 1;
   }
 }
 
@@ -338,12 +372,25 @@ extern "C" int dspark_draft_override(int B, int cap, int V, const int32_t* ref, 
 
 extern "C" int dspark_argmax_rows(const void* logits, long long ld, int rows, int V, int32_t* tokens,
                                   int tok_stride, int32_t* tokens2, int tok2_stride,
-                                  dspark_stream_t stream) {
+                                  float* values, int index_offset, dspark_stream_t stream) {
   if (!logits || !tokens || rows <= 0 || V <= 0 || ld < V || tok_stride < 1 ||
-      (tokens2 && tok2_stride < 1))
+      (tokens2 && tok2_stride < 1) || index_offset < 0)
     return set_error(DSPARK_ERR_INVALID, "argmax_rows: bad arguments");
   if (rows > 65535) return set_error(DSPARK_ERR_UNSUPPORTED, "argmax_rows: too many rows");
   return launch_pdl("argmax_rows", acc::argmax_rows_kernel, dim3(rows), dim3(acc::kArgThreads), 0,
                     static_cast<cudaStream_t>(stream), static_cast<const __nv_bfloat16*>(logits),
-                    ld, V, tokens, tok_stride, tokens2, tok2_stride);
+                    ld, V, tokens, tok_stride, tokens2, tok2_stride, values, index_offset);
+}
+
+extern "C" int dspark_accept_greedy_sharded(const float* values, const int32_t* indices, int shards,
+                                            int B, int T, const int32_t* verify_ids,
+                                            int32_t* kv_len, int commit, int32_t* pending,
+                                            int32_t* plan, dspark_stream_t stream) {
+  if (!values || !indices || !verify_ids || !pending || !plan || shards <= 0 || B <= 0 || T <= 0)
+    return set_error(DSPARK_ERR_INVALID, "accept_greedy_sharded: bad arguments");
+  if (commit && !kv_len) return set_error(DSPARK_ERR_INVALID, "accept_greedy_sharded: commit without kv_len");
+  if (T > 64) return set_error(DSPARK_ERR_UNSUPPORTED, "accept_greedy_sharded: T > 64");
+  return launch_pdl("accept_greedy_sharded", acc::accept_sharded_kernel, dim3(1), dim3(128), 0,
+                    static_cast<cudaStream_t>(stream), values, indices, shards, B, T, verify_ids,
+                    kv_len, commit, pending, plan);
 }

@@ -296,3 +296,31 @@ extern "C" int dspark_bf16_to_f16(const void* src, int lds, void* dst, int ldd, 
                     static_cast<cudaStream_t>(stream), static_cast<const __nv_bfloat16*>(src), lds,
                     static_cast<__half*>(dst), ldd, cols);
 }
+
+// h = bf16(h + bf16(sum)): the residual epilogue of a row-split projection whose fp32
+// partials were summed across tensor-parallel ranks (the RESIDUAL_BF16 epilogue of the
+// W8 GEMM, applied after the all-reduce).
+__global__ void residual_add_f32_kernel(__nv_bfloat16* __restrict__ h, int ldh,
+                                        const float* __restrict__ sum, int lds, int M, int N) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const long long total = (long long)M * N;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int m = (int)(i / N), n = (int)(i % N);
+    __nv_bfloat16* p = h + (size_t)m * ldh + n;
+    *p = __float2bfloat16_rn(__bfloat162float(*p) + bf16_round(sum[(size_t)m * lds + n]));
+  }
+}
+
+extern "C" int dspark_residual_add_f32(void* h, int ldh, const float* sum, int lds, int M, int N,
+                                       dspark_stream_t stream) {
+  if (!h || !sum || M <= 0 || N <= 0 || ldh < N || lds < N)
+    return set_error(DSPARK_ERR_INVALID, "residual_add_f32: bad arguments");
+  const long long total = (long long)M * N;
+  int grid = (int)((total + 255) / 256);
+  if (grid > 4 * 148) grid = 4 * 148;
+  return launch_pdl("residual_add_f32", residual_add_f32_kernel, dim3(grid), dim3(256), 0,
+                    static_cast<cudaStream_t>(stream), static_cast<__nv_bfloat16*>(h), ldh, sum,
+                    lds, M, N);
+}

@@ -122,6 +122,8 @@ class SpecSession:
         self.target, self.drafter = target, drafter
         self.B, self.cap = B, cap
         self.sampling = sampling if (sampling is not None and sampling.active) else None
+        if self.sampling is not None and not target.capturable:
+            raise NotImplementedError("sampled decoding of a tensor-parallel target is not built")
         # OpenAI presence / frequency penalties on the target rows (_Penalizer,
         # generate.py:179-228): completion-token counts per row live on the device
         self.penalties = (float(penalties[0] or 0.0), float(penalties[1] or 0.0))
@@ -194,8 +196,8 @@ class SpecSession:
             ops.apply_penalties(self.vbuf.logits, B, T, self.counts, self.vbuf.ids,
                                 *self.penalties)
         if sm is None:
-            ops.accept_greedy(self.vbuf.logits, B, T, self.vbuf.ids, self.argmax, None, False,
-                              self.pending, self.plan, sc)
+            t.greedy_accept(self.vbuf.logits, B, T, self.vbuf.ids, self.argmax, None, False,
+                            self.pending, self.plan)
         else:
             ops.accept_sample(self.vbuf.logits, B, T, self.vbuf.ids, self.q, sm.temperature,
                               sm.top_p, sm.top_k, self.rng, None, False, self.pending, self.plan,
@@ -211,6 +213,8 @@ class SpecSession:
                 self.target.scratch.version, self.tstate.max_pages, self.cstate.max_pages)
 
     def capture(self) -> None:
+        if not self.target.capturable:
+            return
         g = torch.cuda.CUDAGraph()
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
@@ -247,7 +251,7 @@ class SpecSession:
             self.pending.copy_(self.pending_host, non_blocking=True)
         if self.graph is not None and self._graph_versions != self._versions():
             self.graph = None  # a pool, block table or workspace moved: capture again
-        if use_graph and self.graph is not None:
+        if use_graph and self.graph is not None and self.target.capturable:
             self.graph.replay()
         else:
             self.launch_round()
@@ -260,7 +264,7 @@ def _pick_first(target, last_row: torch.Tensor, sampling: Sampling | None, rng: 
     """First committed token from the prefill's last logits (_pick, generate.py:144-146):
     argmax, or a draw with Philox {offset 0, row 0, stream 2}."""
     if sampling is None:
-        return int(last_row.float().argmax())
+        return target.argmax_row(last_row)
     tok = torch.zeros(1, dtype=torch.int32, device=target.device)
     ops.sample_rows(last_row.view(1, -1), 1, 1, sampling.temperature, sampling.top_p,
                     sampling.top_k, rng[:1], tok, stream_id=2)
@@ -446,8 +450,8 @@ class GreedySession:
         if self.counts is not None:
             ops.apply_penalties(self.buf.logits, self.B, 1, self.counts, None, *self.penalties)
         if sm is None:
-            ops.accept_greedy(self.buf.logits, self.B, 1, self.buf.ids, self.argmax,
-                              self.tstate.seq_len, True, self.buf.ids, self.plan, t.scratch)
+            t.greedy_accept(self.buf.logits, self.B, 1, self.buf.ids, self.argmax,
+                            self.tstate.seq_len, True, self.buf.ids, self.plan)
         else:
             ops.accept_sample(self.buf.logits, self.B, 1, self.buf.ids, None, sm.temperature,
                               sm.top_p, sm.top_k, self.rng, self.tstate.seq_len, True,
@@ -457,6 +461,8 @@ class GreedySession:
         self.plan_host.copy_(self.plan, non_blocking=True)
 
     def capture(self):
+        if not self.target.capturable:
+            return
         g = torch.cuda.CUDAGraph()
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
@@ -467,7 +473,7 @@ class GreedySession:
         self.graph = g
 
     def step(self, use_graph=True):
-        if use_graph and self.graph is not None:
+        if use_graph and self.graph is not None and self.target.capturable:
             self.graph.replay()
         else:
             self.launch_step()

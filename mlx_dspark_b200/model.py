@@ -200,7 +200,8 @@ class DSparkDrafter(BlockDrafter):
         if cfg.norm_style != "qwen":
             raise NotImplementedError("only the qwen3 drafter family is built")
         embed_w = target.embed if weights.embed is None else pack(weights.embed, device=device)
-        head_w = target.head if weights.lm_head is None else pack(weights.lm_head, device=device)
+        head_w = target.draft_head if weights.lm_head is None else pack(weights.lm_head,
+                                                                         device=device)
         super().__init__(cfg, weights.fc, weights.hidden_norm, weights.norm, weights.layers,
                          target, embed_w, head_w, device)
         self.markov_head = None
@@ -302,7 +303,7 @@ class DFlashDrafter(BlockDrafter):
         if cfg.final_logit_softcapping is not None:
             raise NotImplementedError("logit softcapping is not built")
         super().__init__(cfg, weights.fc, weights.hidden_norm, weights.norm, weights.layers,
-                         target, target.embed, target.head, device)
+                         target, target.embed, target.draft_head, device)
         self.markov_head = None
         self.confidence_head = None
 

@@ -189,12 +189,30 @@ def penalty_counts_add(counts: torch.Tensor, plan: torch.Tensor, B: int) -> None
 
 
 def argmax_rows(logits: torch.Tensor, rows: int, tokens: torch.Tensor, tok_stride: int = 1,
-                tokens2: torch.Tensor | None = None, tok2_stride: int = 1) -> torch.Tensor:
-    """First-index argmax of each row (the greedy draft of a head-less block drafter)."""
+                tokens2: torch.Tensor | None = None, tok2_stride: int = 1, *,
+                values: torch.Tensor | None = None, index_offset: int = 0,
+                V: int | None = None) -> torch.Tensor:
+    """First-index argmax of each row over its first V columns (the greedy draft of a head-less
+    block drafter; with values/index_offset, one vocabulary shard's maxima)."""
     _require_cuda(logits, tokens)
-    call("dspark_argmax_rows", _p(logits), logits.stride(0), rows, logits.shape[-1], _p(tokens),
-         int(tok_stride), _p(tokens2), int(tok2_stride), _stream())
+    call("dspark_argmax_rows", _p(logits), logits.stride(0), rows,
+         logits.shape[-1] if V is None else int(V), _p(tokens), int(tok_stride), _p(tokens2),
+         int(tok2_stride), _p(values), int(index_offset), _stream())
     return tokens
+
+
+def residual_add_f32(h: torch.Tensor, summed: torch.Tensor, M: int) -> None:
+    """h[:M] = bf16(h + bf16(summed)) (row-split projection after its all-reduce)."""
+    call("dspark_residual_add_f32", _p(h), h.stride(0), _p(summed), summed.stride(0), M,
+         h.shape[-1], _stream())
+
+
+def accept_greedy_sharded(values: torch.Tensor, indices: torch.Tensor, B: int, T: int,
+                          verify_ids: torch.Tensor, kv_len: torch.Tensor | None, commit: bool,
+                          pending: torch.Tensor, plan: torch.Tensor) -> None:
+    """Greedy acceptance from every vocabulary shard's (max, global argmax) per row."""
+    call("dspark_accept_greedy_sharded", _p(values), _p(indices), values.shape[0], B, T,
+         _p(verify_ids), _p(kv_len), int(commit), _p(pending), _p(plan), _stream())
 
 
 # ----------------------------------------------------------------------------------------

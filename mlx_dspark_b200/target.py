@@ -94,6 +94,17 @@ class Target:
         self._bufs: dict[tuple, Buffers] = {}
         self.model = self  # reference code reaches target.model for embed/lm_head binding
         self.group = c.num_attention_heads // c.num_key_value_heads
+        self.draft_head = self.head  # the head a drafter shares (full vocabulary)
+
+    capturable = True  # a round of this target can be captured into one CUDA graph
+
+    def greedy_accept(self, logits, B, T, verify_ids, argmax, kv_len, commit, pending, plan):
+        """Greedy acceptance of B verify blocks (dspark_accept_greedy)."""
+        ops.accept_greedy(logits, B, T, verify_ids, argmax, kv_len, commit, pending, plan,
+                          self.scratch)
+
+    def argmax_row(self, row: torch.Tensor) -> int:
+        return int(row.float().argmax())
 
     # ------------------------------------------------------------------ caches
     def new_pool(self, max_tokens: int, rows: int = 1, extra_pages: int = 0) -> PagePool:

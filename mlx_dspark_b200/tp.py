@@ -1,0 +1,214 @@
+"""Tensor parallelism of the verify forward for targets past one GPU's budget (BASELINE C5:
+Qwen3-32B at TP 2/4/8). The reference runs on one device; this is the B200 counterpart of its
+target forward (src/mlx_dspark/target.py:58-75) spread over `world` ranks, one process per
+GPU, NCCL over NVLink for the exchanges.
+
+Split (Megatron-style, by head and by MLP slice):
+  q/k/v      column-split by head: rank r owns q heads [r*Hq/w, (r+1)*Hq/w) and kv heads
+             [r*Hkv/w, (r+1)*Hkv/w) (GQA groups stay whole), its slice of the paged KV cache
+  o_proj     row-split over the same q heads -> fp32 partial [M, H] -> all-reduce -> residual
+  gate/up    column-split over the intermediate dimension (I/w per rank)
+  down_proj  row-split over I/w -> fp32 partial -> all-reduce -> residual
+  lm_head    vocabulary-parallel: rank r owns rows [r*Vs, (r+1)*Vs) (padded to 128-row tiles);
+             greedy acceptance all-gathers each rank's (row max, global argmax) pair — 8 bytes
+             per row per rank — and merges them (ties to the smallest index, the mx.argmax rule)
+  embedding, norms, the drafter: replicated (the drafter reads the replicated hidden taps and a
+             replicated copy of the head)
+The residual epilogue rounds once after the sum, bf16(h + bf16(sum of partials)), the same
+rounding point as the single-device RESIDUAL_BF16 epilogue; only the fp32 summation order of
+the partials differs from TP = 1.
+"""
+from __future__ import annotations
+
+from dataclasses import replace
+
+import torch
+import torch.distributed as dist
+
+from . import ops
+from ._lib import EPI_SILU_MUL_F16, EPI_STORE_BF16, EPI_STORE_F32
+from .target import Target
+from .weights import GROUP, LayerWeights, QTensor, TargetWeights, pack
+
+TILE = 128
+
+
+def shard_rows(qt: QTensor, r0: int, r1: int) -> QTensor:
+    return QTensor(qt.q[r0:r1].contiguous(), qt.scales[r0:r1].contiguous(),
+                   qt.biases[r0:r1].contiguous())
+
+
+def shard_cols(qt: QTensor, k0: int, k1: int) -> QTensor:
+    assert k0 % GROUP == 0 and k1 % GROUP == 0
+    return QTensor(qt.q[:, k0:k1].contiguous(), qt.scales[:, k0 // GROUP:k1 // GROUP].contiguous(),
+                   qt.biases[:, k0 // GROUP:k1 // GROUP].contiguous())
+
+
+def pad_rows(qt: QTensor, n: int) -> QTensor:
+    """Append zero rows (q = 0, scale = 0, bias = 0) up to n rows."""
+    extra = n - qt.q.shape[0]
+    if extra <= 0:
+        return qt
+    z = lambda t: torch.zeros((extra,) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)  # noqa: E731
+    return QTensor(torch.cat([qt.q, z(qt.q)]), torch.cat([qt.scales, z(qt.scales)]),
+                   torch.cat([qt.biases, z(qt.biases)]))
+
+
+def vocab_shard(V: int, world: int) -> tuple[int, int]:
+    """(rows per rank, rows per rank padded to whole 128-row GEMM tiles)."""
+    vs = (V + world - 1) // world
+    return vs, (vs + TILE - 1) // TILE * TILE
+
+
+def check_divisible(cfg, world: int) -> None:
+    H, I = cfg.hidden_size, cfg.intermediate_size
+    if cfg.num_key_value_heads % world or cfg.num_attention_heads % world:
+        raise ValueError(f"TP {world}: heads {cfg.num_attention_heads}/{cfg.num_key_value_heads} "
+                         "do not split evenly")
+    if (I // world) % TILE or I % world:
+        raise ValueError(f"TP {world}: intermediate {I} does not split into 128-row tiles")
+    if ((cfg.num_attention_heads + 2 * cfg.num_key_value_heads) // world * cfg.head_dim) % TILE:
+        raise ValueError(f"TP {world}: the per-rank q|k|v width is not a multiple of 128")
+    if (cfg.num_attention_heads // world * cfg.head_dim) % TILE:
+        raise ValueError(f"TP {world}: the per-rank o_proj depth is not a multiple of 128")
+    if H % TILE:
+        raise ValueError("hidden size must be a multiple of 128")
+
+
+def shard_target(tw: TargetWeights, rank: int, world: int):
+    """Rank `rank`'s weights: (TargetWeights with the per-rank config, vocab offset, valid
+    vocabulary rows of the head shard)."""
+    cfg = tw.cfg
+    check_divisible(cfg, world)
+    hd = cfg.head_dim
+    qh, kvh, I = cfg.num_attention_heads // world, cfg.num_key_value_heads // world, \
+        cfg.intermediate_size // world
+    q0, kv0, i0 = rank * qh * hd, rank * kvh * hd, rank * I
+    layers = []
+    for L in tw.layers:
+        layers.append(LayerWeights(
+            L.input_ln, L.post_ln, L.q_norm, L.k_norm,
+            shard_rows(L.wq, q0, q0 + qh * hd), shard_rows(L.wk, kv0, kv0 + kvh * hd),
+            shard_rows(L.wv, kv0, kv0 + kvh * hd), shard_cols(L.wo, q0, q0 + qh * hd),
+            shard_rows(L.gate, i0, i0 + I), shard_rows(L.up, i0, i0 + I),
+            shard_cols(L.down, i0, i0 + I)))
+    V = cfg.vocab_size
+    vs, vpad = vocab_shard(V, world)
+    v0 = rank * vs
+    valid = max(0, min(vs, V - v0))
+    head = pad_rows(shard_rows(tw.head, v0, v0 + valid), vpad)
+    rcfg = replace(cfg, num_attention_heads=qh, num_key_value_heads=kvh, intermediate_size=I,
+                   vocab_size=vpad, tie_word_embeddings=False)
+    return TargetWeights(rcfg, tw.embed, layers, tw.norm, head), v0, valid
+
+
+class TPTarget(Target):
+    """One rank's share of a tensor-parallel target. The process group must be NCCL (one
+    process per GPU) for device tensors; every rank runs the same decode loop."""
+
+    capturable = False  # rounds with collectives run eagerly
+
+    def __init__(self, weights: TargetWeights, rank: int, world: int, group=None, tokenizer=None,
+                 *, kv_bits: int | None = None, device="cuda"):
+        shard, self.vocab_offset, self.vocab_valid = shard_target(weights, rank, world)
+        super().__init__(shard, tokenizer, kv_bits=kv_bits, device=device)
+        self.full_cfg = weights.cfg
+        self.rank, self.world, self.pg = rank, world, group  # (self.group is the GQA group)
+        # the drafters index the whole vocabulary: a replicated copy of the full head
+        self.draft_head = self.embed if weights.lm_head is None else pack(weights.lm_head,
+                                                                          device=device)
+        self._partials: dict[int, torch.Tensor] = {}
+        self._shard: dict[int, tuple] = {}
+
+    def _partial(self, M: int) -> torch.Tensor:
+        p = self._partials.get(M)
+        if p is None:
+            p = torch.zeros(M, self.cfg.hidden_size, dtype=torch.float32, device=self.device)
+            self._partials[M] = p
+        return p
+
+    def _all_reduce(self, t: torch.Tensor) -> None:
+        dist.all_reduce(t, group=self.pg)
+
+    def forward(self, buf, state, tap=(), *, splits: int | None = None,
+                with_logits: bool = True) -> None:
+        c, sc = self.cfg, self.scratch
+        B, T, M = buf.B, buf.T, buf.M
+        splits = splits or self.attn_splits(B, state.max_pages)
+        tap_idx = {l: j for j, l in enumerate(tap)}
+        H = c.hidden_size
+        part = self._partial(M)
+        ops.embed(buf.ids, self.embed, buf.h, M)
+        for l, L in enumerate(self.layers):
+            kv = state.layout(l)
+            ops.rmsnorm(buf.h, L.input_ln, c.rms_norm_eps, y16=buf.xn16, M=M)
+            ops.gemm(buf.xn16, L.qkv, buf.qkv, epilogue=EPI_STORE_BF16, scratch=sc, M=M)
+            ops.qkv_rope_kv_write(buf.qkv, B, T, c.num_attention_heads, c.num_key_value_heads,
+                                  c.head_dim, L.q_norm, L.k_norm, c.rms_norm_eps, self.inv_freq,
+                                  state.seq_len, buf.q, kv)
+            ops.attention(buf.q, B, T, c.num_attention_heads, kv, state.seq_len, True,
+                          self.scale, buf.attn16, splits, sc)
+            ops.gemm(buf.attn16, L.o, part, epilogue=EPI_STORE_F32, scratch=sc, M=M)
+            self._all_reduce(part)
+            ops.residual_add_f32(buf.h, part, M)
+            ops.rmsnorm(buf.h, L.post_ln, c.rms_norm_eps, y16=buf.xn16, M=M)
+            ops.gemm(buf.xn16, L.gu, buf.act16, epilogue=EPI_SILU_MUL_F16, scratch=sc, M=M)
+            ops.gemm(buf.act16, L.down, part, epilogue=EPI_STORE_F32, scratch=sc, M=M)
+            self._all_reduce(part)
+            ops.residual_add_f32(buf.h, part, M)
+            if l in tap_idx:
+                j = tap_idx[l]
+                ops.bf16_to_f16(buf.h, buf.fused16[:, j * H:(j + 1) * H], M, H)
+        if with_logits:
+            ops.rmsnorm(buf.h, self.norm, c.rms_norm_eps, y16=buf.xn16, M=M)
+            ops.gemm(buf.xn16, self.head, buf.logits, epilogue=EPI_STORE_BF16, scratch=sc, M=M)
+
+    # ------------------------------------------------------------------ vocab-parallel argmax
+    def _shard_bufs(self, rows: int):
+        b = self._shard.get(rows)
+        if b is None:
+            dev = self.device
+            b = (torch.zeros(rows, dtype=torch.float32, device=dev),
+                 torch.zeros(rows, dtype=torch.int32, device=dev),
+                 torch.zeros(self.world, rows, dtype=torch.float32, device=dev),
+                 torch.zeros(self.world, rows, dtype=torch.int32, device=dev))
+            self._shard[rows] = b
+        return b
+
+    def _gather_maxima(self, logits: torch.Tensor, rows: int):
+        v, i, va, ia = self._shard_bufs(rows)
+        ops.argmax_rows(logits, rows, i, values=v, index_offset=self.vocab_offset,
+                        V=self.vocab_valid)
+        dist.all_gather_into_tensor(va, v, group=self.pg)
+        dist.all_gather_into_tensor(ia, i, group=self.pg)
+        return va, ia
+
+    def greedy_accept(self, logits, B, T, verify_ids, argmax, kv_len, commit, pending, plan):
+        va, ia = self._gather_maxima(logits, B * T)
+        ops.accept_greedy_sharded(va, ia, B, T, verify_ids, kv_len, commit, pending, plan)
+
+    def argmax_row(self, row: torch.Tensor) -> int:
+        va, ia = self._gather_maxima(row.view(1, -1), 1)
+        vals, idx = va[:, 0].tolist(), ia[:, 0].tolist()
+        best = max(range(self.world), key=lambda s: (vals[s], -idx[s]))
+        return int(idx[best])
+
+
+def init_process_group(backend: str = "nccl", timeout_s: int = 120):
+    """One process per GPU from torchrun's environment; returns (rank, world, device)."""
+    import datetime
+    import os
+    rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    dev = torch.device("cuda", local) if backend == "nccl" else torch.device("cpu")
+    if backend == "nccl":
+        torch.cuda.set_device(dev)
+    if not dist.is_initialized():
+        dist.init_process_group(backend, rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=timeout_s),
+                                **({"device_id": dev} if backend == "nccl" else {}))
+    return rank, world, dev
+
+
+__all__ = ["TPTarget", "shard_target", "shard_rows", "shard_cols", "vocab_shard",
+           "init_process_group"]

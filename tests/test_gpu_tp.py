@@ -1,0 +1,121 @@
+"""Tensor-parallel verify on 2 GPUs (NCCL, one process per GPU; skipped with fewer GPUs).
+
+The TP=2 tiny target's gathered logits match the CPU oracle (bf16 rtol 2e-2 of the row scale,
+as test_gpu_e2e), every rank commits the same tokens, and greedy speculative and plain decoding
+at TP=2 emit the target's greedy decoding (teacher-forced oracle check, near-ties excused)."""
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _rank_main(rank, world, port, q, logdir):
+    import faulthandler
+    import sys
+    import traceback
+    log = open(os.path.join(logdir, f"tp_rank{rank}.log"), "w", buffering=1)
+    sys.stdout = sys.stderr = log
+    faulthandler.enable(file=log)
+    faulthandler.dump_traceback_later(90, repeat=True, file=log)
+    try:
+        _rank_body(rank, world, port, q, log)
+    except BaseException:
+        traceback.print_exc(file=log)
+        q.put(("error", rank, traceback.format_exc()))
+        raise
+
+
+def _rank_body(rank, world, port, q, log):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world), LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+    from mlx_dspark_b200.config import TINY, dspark_for
+    from mlx_dspark_b200.generate import greedy_generate, speculative_generate
+    from mlx_dspark_b200.load import load_drafter
+    from mlx_dspark_b200.tp import TPTarget, init_process_group
+    from mlx_dspark_b200.weights import generate_dspark, generate_target
+    rank, world, dev = init_process_group("nccl", timeout_s=60)
+    print("initialised", flush=True)
+    try:
+        tw = generate_target(TINY, 0, "cpu")
+        target = TPTarget(tw, rank, world, device=dev)
+        dcfg = dspark_for(TINY)
+        drafter, _ = load_drafter(target, dcfg, weights=generate_dspark(dcfg, 0, "cpu"), device=dev)
+        g = torch.Generator().manual_seed(0)
+        prompt = torch.randint(0, TINY.vocab_size, (96,), generator=g).tolist()
+        print("loaded", flush=True)
+        logits, _ = target.run([prompt], target.make_cache(256), ())
+        print("forward done", flush=True)
+        local = logits[0, :, :target.vocab_valid].contiguous()
+        parts = [torch.zeros_like(local) for _ in range(world)]
+        dist.all_gather(parts, local)
+        spec = speculative_generate(target, None, drafter, prompt_ids=prompt, max_new_tokens=48,
+                                    max_draft_tokens=None)
+        print("spec done", flush=True)
+        plain = greedy_generate(target, None, prompt_ids=prompt, max_new_tokens=32)
+        print("plain done", flush=True)
+        toks = torch.tensor(spec.token_ids[:48], device=dev)
+        all_toks = [torch.zeros_like(toks) for _ in range(world)]
+        dist.all_gather(all_toks, toks)
+        if rank == 0:
+            q.put(("ok", torch.cat(parts, 1).float().cpu(), prompt, spec.token_ids[:48],
+                   plain.token_ids[:32], all(torch.equal(t, all_toks[0]) for t in all_toks)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp2_matches_oracle():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    from mlx_dspark_b200.config import TINY
+    from mlx_dspark_b200.weights import generate_target
+    from oracle.qwen3 import Qwen3Ref
+    from test_gpu_e2e import teacher_forced_check
+    import queue
+    import time
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    logdir = os.environ.get("DSPARK_TEST_LOGDIR", "gpurun_out")
+    os.makedirs(logdir, exist_ok=True)
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, q, logdir)) for r in range(2)]
+    for p in procs:
+        p.start()
+    msg, deadline = None, time.time() + 240
+    try:
+        while msg is None and time.time() < deadline:
+            try:
+                msg = q.get(timeout=5)
+            except queue.Empty:
+                if any(p.exitcode not in (None, 0) for p in procs):
+                    break
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.terminate()
+                p.join(timeout=30)
+    assert msg is not None, "no result from the ranks (see gpurun_out/tp_rank*.log)"
+    assert msg[0] == "ok", msg
+    _, gl, prompt, spec, plain, same = msg
+    assert all(p.exitcode == 0 for p in procs)
+    assert same
+    ref = Qwen3Ref(generate_target(TINY, 0, "cpu"))
+    rl, _ = ref.run(prompt, ref.make_cache())
+    scale = rl.abs().amax(-1, keepdim=True)
+    assert ((gl - rl).abs() <= 2e-2 * scale).all(), float(((gl - rl).abs() / scale).max())
+    for toks in (spec, plain):
+        excused, worst = teacher_forced_check(ref, prompt, toks)
+        assert excused <= 3, (excused, worst)
