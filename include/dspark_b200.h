@@ -82,6 +82,16 @@ int dspark_w8a16_gemm(const void* x, int ldx, const uint8_t* wq, const uint32_t*
                       int N, int K, void* y, int ldy, const void* residual, int ldr, int epilogue,
                       void* workspace, size_t workspace_bytes, int* status,
                       dspark_stream_t stream);
+/* The same GEMM, which also warms L2 with up to two byte ranges a later kernel reads (the next
+ * projection's weights): each CTA prefetches its slice after issuing its last load, so HBM keeps
+ * streaming through the GEMM's tail and the small kernels that follow. Ranges are 16-byte
+ * aligned; sizes are rounded down to multiples of 16; NULL / 0 means none. The result is that of
+ * dspark_w8a16_gemm. (No reference counterpart: MLX schedules its own memory traffic.) */
+int dspark_w8a16_gemm_pf(const void* x, int ldx, const uint8_t* wq, const uint32_t* wsb, int M,
+                         int N, int K, void* y, int ldy, const void* residual, int ldr,
+                         int epilogue, void* workspace, size_t workspace_bytes, const void* pf0,
+                         size_t pf0_bytes, const void* pf1, size_t pf1_bytes, int* status,
+                         dspark_stream_t stream);
 
 /* -------------------------------------------------------------------------------------
  * K13 — embedding dequant-gather. Replaces mlx QuantizedEmbedding (embed_tokens,
@@ -122,6 +132,56 @@ typedef struct dspark_kv_layout {
 } dspark_kv_layout;
 
 long long dspark_kv_page_bytes(int page_size, int num_kv_heads, int head_dim, int kv8);
+
+/* -------------------------------------------------------------------------------------
+ * K1c — layer chain: the work between two attention kernels of the verify forward as the
+ * phases of ONE persistent launch, in order (the per-layer arithmetic of mlx-lm's Qwen3
+ * decoder layer under src/mlx_dspark/target.py:58-75, with the same rounding points as the
+ * separate kernels):
+ *   GEMM     y = x . W^T with an epilogue (dspark_w8a16_gemm: fp16 x [M, K], W8 weights)
+ *   NORM     y16[m] = fp16(bf16(x[m] * rsqrt(mean(x[m]^2) + eps) * w))  (dspark_rmsnorm)
+ *   ROPE_KV  per-head q/k RMSNorm + RoPE + paged KV write of a q|k|v block
+ *            (dspark_qkv_rope_kv_write)
+ *   COPY_F16 y16[m] = fp16(x[m]) over H columns (the hidden-state tap, dspark_bf16_to_f16)
+ * Phase i reads what phase i-1 wrote (phase 0: what the previous kernel wrote): every CTA
+ * arrives on phase i's counter after its share of phase i, and a phase's inputs are read
+ * only once that counter is full. The weights of every GEMM phase stream without waiting,
+ * so the next projection's weights are in flight while the previous phase finishes. The
+ * launch is cooperative (every CTA resident); grid-wide waits are bounded like every other
+ * device wait (DSPARK_ERR_TIMEOUT in *status). At most 10 phases, 4 of them GEMMs; M <= 64.
+ * workspace: dspark_chain_workspace_bytes(...), zero-filled once; every call leaves it zeroed.
+ * (No reference counterpart as a unit: MLX dispatches each op as its own kernel.) */
+enum { DSPARK_PHASE_GEMM = 0, DSPARK_PHASE_NORM = 1, DSPARK_PHASE_ROPE_KV = 2,
+       DSPARK_PHASE_COPY_F16 = 3 };
+typedef struct dspark_chain_phase {
+  int kind;
+  int epilogue;                 /* GEMM: DSPARK_EPI_* */
+  const void* x;                /* GEMM: fp16 [M, K]; NORM / COPY_F16: bf16 rows */
+  int ldx;
+  const uint8_t* wq;            /* GEMM weights, dspark_w8a16_gemm layout */
+  const uint32_t* wsb;
+  int N, K;
+  void* y;                      /* GEMM output; NORM / COPY_F16: fp16 output rows */
+  int ldy;
+  const void* residual;         /* GEMM residual (DSPARK_EPI_RESIDUAL_BF16) */
+  int ldr;
+  const void* w;                /* NORM: bf16 weight [H] */
+  int H;                        /* NORM / COPY_F16: columns */
+  float eps;                    /* NORM / ROPE_KV */
+  const void* qkv;              /* ROPE_KV: bf16 [B*T, ldqkv] q|k|v */
+  int ldqkv, T, Hq, Hkv, hd;
+  const void* q_norm;           /* ROPE_KV: bf16 [hd] */
+  const void* k_norm;
+  const float* inv_freq;
+  const int32_t* pos0;          /* ROPE_KV: [B] positions of row t = 0 */
+  void* q_out;                  /* ROPE_KV: bf16 [B*T, Hq*hd] */
+  dspark_kv_layout kv;
+} dspark_chain_phase;
+size_t dspark_chain_phase_size(void); /* sizeof(dspark_chain_phase), for bindings to check */
+size_t dspark_chain_workspace_bytes(int M, const dspark_chain_phase* phases, int n_phases);
+int dspark_run_chain(int M, const dspark_chain_phase* phases, int n_phases, void* workspace,
+                     size_t workspace_bytes, int* status, dspark_stream_t stream);
+
 
 /* -------------------------------------------------------------------------------------
  * K6+K7+K3 — per-head q/k RMSNorm, non-interleaved RoPE at per-row positions, and the

@@ -31,6 +31,20 @@ class KvLayout(ctypes.Structure):
                 ("kv8", c_int), ("reserved", c_int), ("page_bytes", c_longlong)]
 
 
+class ChainPhase(ctypes.Structure):
+    """dspark_chain_phase"""
+    _fields_ = [("kind", c_int), ("epilogue", c_int), ("x", c_void_p), ("ldx", c_int),
+                ("wq", c_void_p), ("wsb", c_void_p), ("N", c_int), ("K", c_int),
+                ("y", c_void_p), ("ldy", c_int), ("residual", c_void_p), ("ldr", c_int),
+                ("w", c_void_p), ("H", c_int), ("eps", c_float),
+                ("qkv", c_void_p), ("ldqkv", c_int), ("T", c_int), ("Hq", c_int),
+                ("Hkv", c_int), ("hd", c_int), ("q_norm", c_void_p), ("k_norm", c_void_p),
+                ("inv_freq", c_void_p), ("pos0", c_void_p), ("q_out", c_void_p),
+                ("kv", KvLayout)]
+
+
+PHASE_GEMM, PHASE_NORM, PHASE_ROPE_KV, PHASE_COPY_F16 = 0, 1, 2, 3
+
 P = c_void_p
 I = c_int
 # name -> (restype, argtypes); mirrors include/dspark_b200.h
@@ -39,6 +53,8 @@ SIGNATURES = {
     "dspark_last_error": (c_char_p, []),
     "dspark_w8a16_gemm_workspace_bytes": (c_size_t, [I, I, I]),
     "dspark_w8a16_gemm": (I, [P, I, P, P, I, I, I, P, I, P, I, I, P, c_size_t, P, P]),
+    "dspark_w8a16_gemm_pf": (I, [P, I, P, P, I, I, I, P, I, P, I, I, P, c_size_t, P, c_size_t, P,
+                                 c_size_t, P, P]),
     "dspark_w8a16_gemm_simt": (I, [P, I, P, P, I, I, I, P, I, P, I, I, P]),
     "dspark_embed_w8": (I, [P, I, P, P, I, I, P, I, P]),
     "dspark_embed_block_w8": (I, [P, I, I, I, P, P, I, I, P, I, P, P]),
@@ -57,6 +73,9 @@ SIGNATURES = {
     "dspark_markov_workspace_bytes": (c_size_t, [I, I]),
     "dspark_markov_sample_block": (I, [P, I, I, I, I, I, I, P, P, P, P, P, P, P, P, c_size_t, P, P]),
     "dspark_bf16_to_f16": (I, [P, I, P, I, I, I, P]),
+    "dspark_chain_phase_size": (c_size_t, []),
+    "dspark_chain_workspace_bytes": (c_size_t, [I, P, I]),
+    "dspark_run_chain": (I, [I, P, I, P, c_size_t, P, P]),
     "dspark_apply_penalties": (I, [P, c_longlong, I, I, I, P, P, c_double, c_double, P]),
     "dspark_penalty_counts_add": (I, [P, I, I, P, I, P]),
     "dspark_argmax_rows": (I, [P, c_longlong, I, I, P, I, P, I, P, I, P]),

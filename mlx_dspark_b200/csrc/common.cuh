@@ -71,6 +71,13 @@ __device__ __forceinline__ void pdl_launch_dependents() {
 }
 
 // ------------------------------------------------------------------------------------------
+// bulk L2 prefetch (fire and forget): warm L2 with bytes a later kernel will read.
+// Address 16-byte aligned, size a multiple of 16.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// ------------------------------------------------------------------------------------------
 // mbarrier
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");

@@ -3,6 +3,7 @@
 // one CTA per token row; they honour programmatic dependent launch so they can be queued
 // behind a GEMM without a launch gap.
 #include "common.cuh"
+#include "rope_kv.cuh"
 
 namespace dspark {
 
@@ -112,23 +113,7 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* __res
   }
 }
 
-// ------------------------------------------------------------------------------------------
-// paged cache addressing
-struct KvAddr {
-  uint8_t* page;  // base of the page holding `pos`
-  int slot;       // token slot inside the page
-};
-__device__ __forceinline__ KvAddr kv_locate(const dspark_kv_layout& kv, int b, int pos) {
-  const int pi = pos / kv.page_size;
-  const int phys = kv.block_table[(size_t)b * kv.max_pages + pi];
-  KvAddr a;
-  a.page = static_cast<uint8_t*>(kv.pool) + (size_t)phys * (size_t)kv.page_bytes;
-  a.slot = pos - pi * kv.page_size;
-  return a;
-}
-
-// One warp per (token, head). E = head_dim / 32 contiguous elements per lane; lanes l and
-// l + 16 hold the two halves that non-interleaved RoPE rotates against each other.
+// One warp per (token, head) (rope_kv_item).
 template <int E>
 __global__ void __launch_bounds__(256) qkv_rope_kv_kernel(
     const __nv_bfloat16* __restrict__ qkv, int ldqkv, int T, int Hq, int Hkv,
@@ -143,78 +128,9 @@ __global__ void __launch_bounds__(256) qkv_rope_kv_kernel(
   const int pos = pos0[b] + t;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nheads = Hq + 2 * Hkv;
-  for (int h = warp; h < nheads; h += blockDim.x >> 5) {
-    const __nv_bfloat16* src = qkv + (size_t)m * ldqkv + (size_t)h * HD + lane * E;
-    float x[E];
-#pragma unroll
-    for (int e = 0; e < E; ++e) x[e] = __bfloat162float(src[e]);
-    const bool is_v = h >= Hq + Hkv;
-    if (!is_v) {
-      const __nv_bfloat16* nw = h < Hq ? qnw : knw;
-      float ss = 0.0f;
-#pragma unroll
-      for (int e = 0; e < E; ++e) ss += x[e] * x[e];
-      ss = warp_sum(ss);
-      const float r = rsqrtf(ss / (float)HD + eps);
-#pragma unroll
-      for (int e = 0; e < E; ++e) x[e] = bf16_round(x[e] * r * __bfloat162float(nw[lane * E + e]));
-      // RoPE (rotate-half): pair element i with i + HD/2
-      float other[E];
-#pragma unroll
-      for (int e = 0; e < E; ++e) other[e] = __shfl_xor_sync(0xffffffffu, x[e], 16);
-      const bool upper = lane >= 16;
-#pragma unroll
-      for (int e = 0; e < E; ++e) {
-        const int fi = (lane & 15) * E + e;
-        float sn, cs;
-        sincosf((float)pos * inv_freq[fi], &sn, &cs);
-        x[e] = upper ? bf16_round(x[e] * cs + other[e] * sn) : bf16_round(x[e] * cs - other[e] * sn);
-      }
-    }
-    if (h < Hq) {
-      __nv_bfloat16* dst = q_out + (size_t)m * Hq * HD + (size_t)h * HD + lane * E;
-#pragma unroll
-      for (int e = 0; e < E; ++e) dst[e] = __float2bfloat16_rn(x[e]);
-      continue;
-    }
-    const int kvh = is_v ? h - Hq - Hkv : h - Hq;
-    const int which = is_v ? 1 : 0;
-    const KvAddr a = kv_locate(kv, b, pos);
-    const size_t row = ((size_t)which * Hkv + kvh) * kv.page_size + a.slot;
-    if (!kv.kv8) {
-      __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.page) + row * HD + lane * E;
-#pragma unroll
-      for (int e = 0; e < E; ++e) dst[e] = __float2bfloat16_rn(x[e]);
-    } else {
-      // affine 8-bit, group 64 along head_dim: scale = (max-min)/255, bias = min (bf16),
-      // q = clamp(rint((x - bias) / scale), 0, 255)
-      constexpr int LPG = 64 / E;  // lanes per group
-      float mn = x[0], mx = x[0];
-#pragma unroll
-      for (int e = 1; e < E; ++e) { mn = fminf(mn, x[e]); mx = fmaxf(mx, x[e]); }
-#pragma unroll
-      for (int o = LPG / 2; o > 0; o >>= 1) {
-        mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      }
-      const float sc = bf16_round((mx - mn) / 255.0f);
-      const float bi = bf16_round(mn);
-      uint8_t* qdst = a.page + row * HD + lane * E;
-#pragma unroll
-      for (int e = 0; e < E; ++e) {
-        float qv = sc > 0.0f ? rintf((x[e] - bi) / sc) : 0.0f;
-        qv = fminf(fmaxf(qv, 0.0f), 255.0f);
-        qdst[e] = (uint8_t)qv;
-      }
-      if ((lane % LPG) == 0) {
-        uint32_t* sbdst = reinterpret_cast<uint32_t*>(a.page + (size_t)2 * Hkv * kv.page_size * HD) +
-                          row * (HD / 64) + (lane * E) / 64;
-        const __nv_bfloat16 s16 = __float2bfloat16_rn(sc), b16 = __float2bfloat16_rn(bi);
-        *sbdst = (uint32_t)(*reinterpret_cast<const uint16_t*>(&s16)) |
-                 ((uint32_t)(*reinterpret_cast<const uint16_t*>(&b16)) << 16);
-      }
-    }
-  }
+  for (int h = warp; h < nheads; h += blockDim.x >> 5)
+    rope_kv_item<E>(qkv + (size_t)m * ldqkv, Hq, Hkv, h, qnw, knw, eps, inv_freq, b, pos,
+                    q_out + (size_t)m * Hq * HD, kv, lane);
 }
 
 }  // namespace dspark

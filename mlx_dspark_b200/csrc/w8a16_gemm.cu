@@ -31,6 +31,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "rope_kv.cuh"
 
 namespace dspark {
 namespace w8 {
@@ -64,6 +65,10 @@ struct Params {
   float* partials;  // [grid][2][BN][128]
   int* counters;    // [tiles]
   int* status;
+  // L2 prefetch of the next kernel's operands: CTA b warms bytes [b*chunk, (b+1)*chunk) of each
+  // range after issuing its last load (16-byte aligned, sizes multiples of 16)
+  const char* pf_ptr[2];
+  unsigned long long pf_bytes[2];
 };
 
 __device__ __forceinline__ long long range_start(long long b, long long total, long long G) {
@@ -251,6 +256,21 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 ? 2 : 1))
         tma_load_2d(x_s + s * L::kXBytes, &tm_x, xfull(s), kb * BK, 0, pol_x);
         tma_load_2d(x_s + s * L::kXBytes + BN * 128, &tm_x, xfull(s), kb * BK + 64, 0, pol_x);
         issued = i + 1;
+      }
+      // this CTA's loads are all issued: while they land and the tail runs, warm L2 with its
+      // slice of the next GEMM's weights so HBM does not idle through the tail and the small
+      // kernels in between
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const unsigned long long nb = p.pf_bytes[r];
+        if (nb == 0) continue;
+        const unsigned long long chunk = ((nb + (unsigned long long)G - 1) / (unsigned long long)G + 15ull) & ~15ull;
+        unsigned long long off = (unsigned long long)blockIdx.x * chunk;
+        const unsigned long long stop = off + chunk < nb ? off + chunk : nb;
+        for (; off < stop; off += 65536ull) {
+          const unsigned long long left = stop - off;
+          prefetch_l2_bulk(p.pf_ptr[r] + off, (uint32_t)(left < 65536ull ? left : 65536ull));
+        }
       }
       // drain: no bulk copy may still be writing into this CTA's shared memory at exit
       const int first = issued > STAGES ? issued - STAGES : 0;
@@ -511,6 +531,538 @@ __global__ void __launch_bounds__(256) w8a16_simt_kernel(const __half* __restric
 }
 
 // ------------------------------------------------------------------------------------------
+// Layer chain: the GEMMs and small ops between two attention kernels as phases of ONE
+// persistent launch (cooperative: every CTA resident, so grid-wide waits are safe):
+//   o_proj (+residual) -> RMSNorm -> gate|up (SiLU*up) -> down (+residual) [-> tap copy]
+//   -> next layer's RMSNorm -> next q|k|v -> q/k norm + RoPE + paged KV write
+// The per-launch ramp and tail (~6-9 us a GEMM) are paid once per layer. Warp roles are the
+// GEMM's; the producer warp splits in two lanes: lane 0 streams every phase's weight tiles
+// without waiting for anything but free ring slots (so the next projection's weights are in
+// flight while the previous phase finishes), lane 1 issues a GEMM phase's activation loads
+// only once the grid-wide counter of the phase before it is full. The epilogue warps finish
+// the GEMM tiles, run the elementwise phases, and arrive on each phase's counter.
+constexpr int kChainMaxPhases = 10;
+constexpr int kChainMaxGemm = 4;
+enum { kPhGemm = 0, kPhNorm = 1, kPhRope = 2, kPhCopy = 3 };
+// Grid barriers follow GEMM and NORM phases. A barrier may spread its arrivals over kBarSlots
+// counters on separate 128-byte lines (CTA c adds to slot c % kBarSlots; a waiter sums them);
+// one slot measured fastest on B200 (16 slots: polling 16 lines costs more than the contention
+// it removes).
+constexpr int kBarSlots = 1;
+constexpr int kBarStride = 32;  // ints between slots (128 bytes)
+constexpr int kChainMaxBars = kChainMaxPhases;
+constexpr size_t kBarRegion = (((size_t)(kChainMaxBars * kBarSlots + 1) * kBarStride * 4) + 255) & ~(size_t)255;
+
+struct ChainGemm {
+  int N, K, tiles, kb;
+  long long total;
+  int epilogue;
+  void* y;
+  int ldy;
+  const void* residual;
+  int ldr;
+  int* counters;
+  float* partials;
+};
+struct ChainPhase {
+  int kind;
+  int gemm;        // GEMM phases: index into ChainParams::g and ChainMaps
+  int wait_bar;    // grid barrier to acquire before reading inputs (-1: the previous kernel)
+  int arrive_bar;  // grid barrier to arrive on afterwards (-1: none)
+  int local_norm;  // GEMM: NORM phase (run by this CTA) whose output is X (-1: none)
+  // NORM: x (bf16) -> y16 (fp16) ; COPY: x (bf16) -> y16 (fp16), cols = H
+  const __nv_bfloat16* x;
+  int ldx;
+  const __nv_bfloat16* w;
+  int H;
+  float eps;
+  __half* y16;
+  int ldy16;
+  // ROPE
+  const __nv_bfloat16* qkv;
+  int ldqkv, T, Hq, Hkv, hd;
+  const __nv_bfloat16* qnw;
+  const __nv_bfloat16* knw;
+  const float* inv_freq;
+  const int32_t* pos0;
+  __nv_bfloat16* q_out;
+  dspark_kv_layout kv;
+};
+struct ChainParams {
+  int M, nphases, ngemm;
+  ChainPhase ph[kChainMaxPhases];
+  ChainGemm g[kChainMaxGemm];
+  int* bars;  // one arrival counter per phase, then a done counter
+  int* status;
+};
+struct ChainMaps {
+  CUtensorMap w[kChainMaxGemm], sb[kChainMaxGemm], x[kChainMaxGemm];
+};
+
+__device__ __forceinline__ int bar_count(const int* bar) {
+  int sum = 0;
+#pragma unroll
+  for (int k = 0; k < kBarSlots; ++k) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(bar + k * kBarStride) : "memory");
+    sum += v;
+  }
+  return sum;
+}
+__device__ __forceinline__ bool grid_wait(const int* bar, int target, volatile int* abort_flag,
+                                          int* status) {
+  if (bar_count(bar) >= target) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  while (true) {
+    __nanosleep(32);
+    if (bar_count(bar) >= target) return true;
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > kSpinLimitNs) {
+      *abort_flag = 1;
+      report_error(status, DSPARK_ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ void grid_arrive(int* bar) {
+  int* slot = bar + (int)(blockIdx.x % kBarSlots) * kBarStride;
+  asm volatile("fence.acq_rel.gpu;\n\tred.release.gpu.global.add.s32 [%0], 1;" ::"l"(slot) : "memory");
+}
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(kThreads, (BN <= 32 ? 2 : 1))
+    chain_kernel(const __grid_constant__ ChainMaps maps, const __grid_constant__ ChainParams p) {
+  using L = Smem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* sbase = smem_raw + (base - raw);
+
+  const uint32_t w_s = base;
+  const uint32_t x_s = base + STAGES * kWBytes;
+  const uint32_t sb_s = x_s + STAGES * L::kXBytes;
+  float* xch = reinterpret_cast<float*>(sbase + STAGES * L::kStageBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sbase + STAGES * L::kStageBytes + L::kXchBytes);
+  auto full = [&](int s) { return smem_u32(bars + s); };
+  auto xfull = [&](int s) { return smem_u32(bars + STAGES + s); };
+  auto empty = [&](int s) { return smem_u32(bars + 2 * STAGES + s); };
+  auto afull = [&](int a) { return smem_u32(bars + 3 * STAGES + a); };
+  auto aempty = [&](int a) { return smem_u32(bars + 3 * STAGES + kABufs + a); };
+  auto accfull = [&](int b) { return smem_u32(bars + 3 * STAGES + 2 * kABufs + b); };
+  auto accempty = [&](int b) { return smem_u32(bars + 3 * STAGES + 2 * kABufs + 2 + b); };
+  const uint32_t done_bar = smem_u32(bars + 3 * STAGES + 2 * kABufs + 4);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 3 * STAGES + 2 * kABufs + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_holder + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const long long G = gridDim.x;
+  const int Gi = (int)gridDim.x;
+  // NORM phases run redundantly in every CTA; this CTA's activation producer waits for its
+  // own epilogue warps to finish the rows (one use per launch: parity 0)
+  __shared__ uint64_t local_done[kChainMaxPhases];
+  auto bar_at = [&](int b) { return p.bars + b * kBarSlots * kBarStride; };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full(s), 1);
+      mbar_init(xfull(s), 1);
+      mbar_init(empty(s), kConvWarps + 1);
+    }
+    for (int a = 0; a < kABufs; ++a) {
+      mbar_init(afull(a), kConvWarps);
+      mbar_init(aempty(a), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(accfull(b), 1);
+      mbar_init(accempty(b), kEpiWarps);
+    }
+    mbar_init(done_bar, 1);
+    for (int q = 0; q < kChainMaxPhases; ++q) mbar_init(smem_u32(&local_done[q]), 1);
+    *abort_flag = 0;
+    *last_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == kProducerWarp) {
+    if (lane == 0) {
+      for (int j = 0; j < p.ngemm; ++j) {
+        tma_prefetch_desc(&maps.w[j]);
+        tma_prefetch_desc(&maps.sb[j]);
+        tma_prefetch_desc(&maps.x[j]);
+      }
+    }
+    __syncwarp();
+    tmem_alloc(smem_u32(tmem_holder), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  pdl_launch_dependents();
+
+  // A GEMM phase spreads over Gj = min(G, units) CTAs, so every CTA that owns a range owns at
+  // least one unit (the stream-K fixup counts contributors by range); the rest sit it out.
+  auto phase_range = [&](const ChainGemm& gj, long long& st, long long& en) {
+    const long long Gj = gj.total < G ? gj.total : G;
+    if ((long long)blockIdx.x < Gj) {
+      st = range_start(blockIdx.x, gj.total, Gj);
+      en = range_start(blockIdx.x + 1, gj.total, Gj);
+    } else {
+      st = en = 0;
+    }
+  };
+  // total units of this CTA over all GEMM phases (phase order)
+  int n_units = 0;
+  for (int j = 0; j < p.ngemm; ++j) {
+    long long st, en;
+    phase_range(p.g[j], st, en);
+    n_units += (int)(en - st);
+  }
+
+  if (warp == kProducerWarp) {
+    if (lane == 0) {
+      // weights and (scale, bias): depend on nothing, streamed through every phase
+      const uint64_t pol_w = policy_evict_first();
+      int u = 0;
+      bool ok = true;
+      for (int j = 0; j < p.ngemm && ok; ++j) {
+        const ChainGemm& gj = p.g[j];
+        long long st, en;
+        phase_range(gj, st, en);
+        for (long long g = st; g < en; ++g, ++u) {
+          const int s = u % STAGES;
+          const uint32_t ph = (uint32_t)(u / STAGES) & 1u;
+          if (u >= STAGES && !mbar_wait(empty(s), ph ^ 1u, abort_flag, p.status)) { ok = false; break; }
+          const int tile = (int)(g / gj.kb), kb = (int)(g % gj.kb);
+          mbar_arrive_expect_tx(full(s), kWBytes + kSBBytes);
+          tma_load_2d(w_s + s * kWBytes, &maps.w[j], full(s), kb * BK, tile * BM, pol_w);
+          tma_load_2d(sb_s + s * kSBBytes, &maps.sb[j], full(s), tile * BM, kb * 2, pol_w);
+        }
+      }
+      const int issued = u;
+      const int first = issued > STAGES ? issued - STAGES : 0;
+      for (int i = first; i < issued; ++i) {
+        volatile int never = 0;
+        mbar_wait(full(i % STAGES), (uint32_t)(i / STAGES) & 1u, &never, p.status);
+      }
+    } else if (lane == 1) {
+      // activations: a GEMM phase's X is complete once the counter of the phase before it is
+      // full (the first phase's X comes from the previous kernel)
+      const uint64_t pol_x = policy_evict_last();
+      int u = 0;
+      bool ok = true;
+      for (int q = 0; q < p.nphases && ok; ++q) {
+        if (p.ph[q].kind != kPhGemm) continue;
+        const int j = p.ph[q].gemm;
+        const ChainGemm& gj = p.g[j];
+        long long st, en;
+        phase_range(gj, st, en);
+        if (st == en) continue;
+        if (p.ph[q].wait_bar < 0) pdl_wait();
+        else if (!grid_wait(bar_at(p.ph[q].wait_bar), Gi, abort_flag, p.status)) { ok = false; break; }
+        if (p.ph[q].local_norm >= 0 &&
+            !mbar_wait(smem_u32(&local_done[p.ph[q].local_norm]), 0, abort_flag, p.status)) { ok = false; break; }
+        // the phase before wrote X with generic stores; these loads go through the async proxy
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        for (long long g = st; g < en; ++g, ++u) {
+          const int s = u % STAGES;
+          const uint32_t ph = (uint32_t)(u / STAGES) & 1u;
+          if (u >= STAGES && !mbar_wait(empty(s), ph ^ 1u, abort_flag, p.status)) { ok = false; break; }
+          const int kb = (int)(g % gj.kb);
+          mbar_arrive_expect_tx(xfull(s), L::kXBytes);
+          tma_load_2d(x_s + s * L::kXBytes, &maps.x[j], xfull(s), kb * BK, 0, pol_x);
+          tma_load_2d(x_s + s * L::kXBytes + BN * 128, &maps.x[j], xfull(s), kb * BK + 64, 0, pol_x);
+        }
+      }
+      const int issued = u;
+      const int first = issued > STAGES ? issued - STAGES : 0;
+      for (int i = first; i < issued; ++i) {
+        volatile int never = 0;
+        mbar_wait(xfull(i % STAGES), (uint32_t)(i / STAGES) & 1u, &never, p.status);
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_f16(BM, BN);
+      int seg = 0, u = 0;
+      bool ok = true;
+      for (int j = 0; j < p.ngemm && ok; ++j) {
+        const ChainGemm& gj = p.g[j];
+        long long st, en;
+        phase_range(gj, st, en);
+        for (long long g = st; g < en; ++g, ++u) {
+          const int kb = (int)(g % gj.kb);
+          const bool seg_first = (g == st) || (kb == 0);
+          const bool seg_last = (g == en - 1) || (kb == gj.kb - 1);
+          const int s = u % STAGES;
+          const uint32_t ph = (uint32_t)(u / STAGES) & 1u;
+          const int a = u % kABufs;
+          const uint32_t aph = (uint32_t)(u / kABufs) & 1u;
+          const int ab = seg & 1;
+          const uint32_t abph = (uint32_t)(seg >> 1) & 1u;
+          if (seg_first && !mbar_wait(accempty(ab), abph ^ 1u, abort_flag, p.status)) { ok = false; break; }
+          if (!mbar_wait(afull(a), aph, abort_flag, p.status)) { ok = false; break; }
+          if (!mbar_wait(xfull(s), ph, abort_flag, p.status)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t d_tmem = tmem_base + 128u + (uint32_t)ab * 64u;
+#pragma unroll
+          for (int jj = 0; jj < BK / 16; ++jj) {
+            const uint32_t a_tmem = tmem_base + (uint32_t)a * 64u + (uint32_t)jj * 8u;
+            const uint32_t b_addr = x_s + s * L::kXBytes + (jj >> 2) * (BN * 128) + (jj & 3) * 32;
+            tc_mma_ts(d_tmem, a_tmem, umma_desc_sw128_kmajor(b_addr), idesc,
+                      (seg_first && jj == 0) ? 0u : 1u);
+          }
+          tc_commit(empty(s));
+          tc_commit(aempty(a));
+          if (seg_last) {
+            tc_commit(accfull(ab));
+            ++seg;
+          }
+        }
+      }
+      tc_commit(done_bar);
+      volatile int never = 0;
+      mbar_wait(done_bar, 0, &never, p.status);
+    }
+  } else if (warp < kConvWarps) {
+    const int r = threadIdx.x;
+    const uint32_t lane_base = tmem_base + ((uint32_t)(warp * 32) << 16);
+    const uint32_t k1024 = 0x64006400u;
+    for (int i = 0; i < n_units; ++i) {
+      const int s = i % STAGES;
+      const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
+      const int a = i % kABufs;
+      const uint32_t aph = (uint32_t)(i / kABufs) & 1u;
+      if (!mbar_wait(full(s), ph, abort_flag, p.status)) break;
+      if (!mbar_wait(aempty(a), aph ^ 1u, abort_flag, p.status)) break;
+      tc_fence_after();
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t sbv;
+        asm volatile("ld.shared.b32 %0, [%1];" : "=r"(sbv) : "r"(sb_s + s * kSBBytes + (h * BM + r) * 4));
+        const uint32_t sc2 = __byte_perm(sbv, 0, 0x1010);
+        const uint32_t bi2 = __byte_perm(sbv, 0, 0x3232);
+        uint32_t out[32];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int chunk = h * 4 + j;
+          const uint32_t addr = w_s + s * kWBytes + r * 128 + ((chunk ^ (r & 7)) << 4);
+          uint32_t v0, v1, v2, v3;
+          asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                       : "=r"(v0), "=r"(v1), "=r"(v2), "=r"(v3)
+                       : "r"(addr));
+          const uint32_t vv[4] = {v0, v1, v2, v3};
+#pragma unroll
+          for (int w = 0; w < 4; ++w) {
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              const uint32_t q2 = __byte_perm(vv[w], 0x64646464u, hh ? 0x4342u : 0x4140u);
+              __half2 qh = *reinterpret_cast<const __half2*>(&q2);
+              qh = __hsub2(qh, *reinterpret_cast<const __half2*>(&k1024));
+              const __half2 wv = __hfma2(qh, *reinterpret_cast<const __half2*>(&sc2),
+                                         *reinterpret_cast<const __half2*>(&bi2));
+              out[j * 8 + w * 2 + hh] = *reinterpret_cast<const uint32_t*>(&wv);
+            }
+          }
+        }
+        tmem_st32(lane_base + (uint32_t)a * 64u + (uint32_t)h * 32u, out);
+      }
+      tc_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(empty(s));
+        mbar_arrive(afull(a));
+      }
+    }
+  } else if (warp < kConvWarps + kEpiWarps) {
+    const int er = threadIdx.x - kConvWarps * 32;
+    const int quad = warp & 3;
+    const int ew = warp - kConvWarps;  // 0..3
+    pdl_wait();
+    int seg = 0;
+    bool ok = true;
+    for (int q = 0; q < p.nphases && ok; ++q) {
+      const ChainPhase& P = p.ph[q];
+      if (P.kind == kPhGemm) {
+        if (P.wait_bar >= 0) {
+          // acquire what earlier phases wrote (the residual of down is written by o's epilogue)
+          if (er == 0) *last_flag = grid_wait(bar_at(P.wait_bar), Gi, abort_flag, p.status) ? 1 : 0;
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          if (!*last_flag) { ok = false; break; }
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+        }
+        const int j = P.gemm;
+        const ChainGemm& gj = p.g[j];
+        Params pp{};
+        pp.M = p.M;
+        pp.epilogue = gj.epilogue;
+        pp.y = gj.y;
+        pp.ldy = gj.ldy;
+        pp.residual = gj.residual;
+        pp.ldr = gj.ldr;
+        const int KB = gj.kb;
+        const long long total = gj.total;
+        const long long Gj = total < G ? total : G;
+        long long start, end;
+        phase_range(gj, start, end);
+        int lseg = 0;
+        long long g = start;
+        while (g < end) {
+          const int tile = (int)(g / KB);
+          const long long tile_lo = (long long)tile * KB;
+          const long long seg_end = (end < tile_lo + KB) ? end : tile_lo + KB;
+          const bool whole = (g == tile_lo) && (seg_end == tile_lo + KB);
+          const int ab = seg & 1;
+          const uint32_t abph = (uint32_t)(seg >> 1) & 1u;
+          if (!mbar_wait(accfull(ab), abph, abort_flag, p.status)) { ok = false; break; }
+          tc_fence_after();
+          float acc[BN];
+#pragma unroll
+          for (int c = 0; c < BN / 16; ++c) {
+            uint32_t rr[16];
+            tmem_ld16(tmem_base + ((uint32_t)(quad * 32) << 16) + 128u + (uint32_t)ab * 64u + (uint32_t)c * 16u, rr);
+            tc_wait_ld();
+#pragma unroll
+            for (int t = 0; t < 16; ++t) acc[c * 16 + t] = __uint_as_float(rr[t]);
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(accempty(ab));
+          if (whole) {
+            epilogue_store<BN>(pp, tile, er, acc, xch);
+          } else {
+            const int slot = (int)blockIdx.x * 2 + (lseg == 0 ? 0 : 1);
+            float4* part = reinterpret_cast<float4*>(gj.partials + (size_t)slot * BN * BM + er * BN);
+#pragma unroll
+            for (int jj = 0; jj < BN / 4; ++jj)
+              part[jj] = make_float4(acc[4 * jj], acc[4 * jj + 1], acc[4 * jj + 2], acc[4 * jj + 3]);
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            const long long c_lo = range_owner(tile_lo, total, Gj);
+            const long long c_hi = range_owner(tile_lo + KB - 1, total, Gj);
+            if (er == 0) {
+              const int contributors = (int)(c_hi - c_lo + 1);
+              int old;
+              asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;"
+                           : "=r"(old)
+                           : "l"(gj.counters + tile)
+                           : "memory");
+              *last_flag = (old == contributors - 1) ? 1 : 0;
+            }
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            if (*last_flag) {
+              float sum[BN];
+#pragma unroll
+              for (int m = 0; m < BN; ++m) sum[m] = 0.0f;
+              for (long long c = c_lo; c <= c_hi; ++c) {
+                const int cj = (range_start(c, total, Gj) >= tile_lo) ? 0 : 1;
+                const float4* cp = reinterpret_cast<const float4*>(
+                    gj.partials + ((size_t)c * 2 + cj) * BN * BM + er * BN);
+#pragma unroll
+                for (int jj = 0; jj < BN / 4; ++jj) {
+                  const float4 t = __ldcg(cp + jj);
+                  sum[4 * jj] += t.x;
+                  sum[4 * jj + 1] += t.y;
+                  sum[4 * jj + 2] += t.z;
+                  sum[4 * jj + 3] += t.w;
+                }
+              }
+              if (er == 0) gj.counters[tile] = 0;
+              epilogue_store<BN>(pp, tile, er, sum, xch);
+            }
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+          }
+          ++seg;
+          ++lseg;
+          g = seg_end;
+        }
+      } else {
+        if (P.wait_bar >= 0) {
+          if (er == 0) *last_flag = grid_wait(bar_at(P.wait_bar), Gi, abort_flag, p.status) ? 1 : 0;
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          if (!*last_flag) { ok = false; break; }
+        }
+        if (P.kind == kPhNorm) {
+          // rows m = blockIdx.x, blockIdx.x + G, ...: y16 = fp16(bf16(x * rsqrt(mean x^2 + eps) * w))
+          for (int m = blockIdx.x; m < p.M; m += Gi) {
+            const __nv_bfloat16* xr = P.x + (size_t)m * P.ldx;
+            float ss = 0.0f;
+            for (int k = er * 2; k < P.H; k += 256) {
+              const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(xr + k));
+              ss += v.x * v.x + v.y * v.y;
+            }
+            ss = warp_sum(ss);
+            if (lane == 0) xch[ew] = ss;
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            const float tot = (xch[0] + xch[1]) + (xch[2] + xch[3]);
+            const float rr = rsqrtf(tot / (float)P.H + P.eps);
+            for (int k = er * 2; k < P.H; k += 256) {
+              const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(xr + k));
+              const float2 wv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(P.w + k));
+              const __nv_bfloat162 o = __floats2bfloat162_rn(v.x * rr * wv.x, v.y * rr * wv.y);
+              const float2 of = __bfloat1622float2(o);
+              *reinterpret_cast<__half2*>(P.y16 + (size_t)m * P.ldy16 + k) = __floats2half2_rn(of.x, of.y);
+            }
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+          }
+        } else if (P.kind == kPhCopy) {
+          const long long n2 = (long long)p.M * (P.H / 2);
+          for (long long i = (long long)blockIdx.x * 128 + er; i < n2; i += (long long)Gi * 128) {
+            const int m = (int)(i / (P.H / 2)), k = (int)(i % (P.H / 2)) * 2;
+            const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(P.x + (size_t)m * P.ldx + k));
+            *reinterpret_cast<__half2*>(P.y16 + (size_t)m * P.ldy16 + k) = __floats2half2_rn(v.x, v.y);
+          }
+        } else if (P.kind == kPhRope) {
+          const int nheads = P.Hq + 2 * P.Hkv;
+          const int items = p.M * nheads;
+          for (int it = blockIdx.x * kEpiWarps + ew; it < items; it += Gi * kEpiWarps) {
+            const int m = it / nheads, h = it - m * nheads;
+            const int b = m / P.T, t = m - b * P.T;
+            const int pos = P.pos0[b] + t;
+            if (P.hd == 128)
+              rope_kv_item<4>(P.qkv + (size_t)m * P.ldqkv, P.Hq, P.Hkv, h, P.qnw, P.knw, P.eps,
+                              P.inv_freq, b, pos, P.q_out + (size_t)m * P.Hq * 128, P.kv, lane);
+            else
+              rope_kv_item<2>(P.qkv + (size_t)m * P.ldqkv, P.Hq, P.Hkv, h, P.qnw, P.knw, P.eps,
+                              P.inv_freq, b, pos, P.q_out + (size_t)m * P.Hq * 64, P.kv, lane);
+          }
+        }
+      }
+      // this CTA's share of phase q is written: make it visible to later TMA (async proxy)
+      // reads, then one release arrival per CTA
+      if (P.arrive_bar >= 0) {
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (er == 0) grid_arrive(bar_at(P.arrive_bar));
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kProducerWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+  // every thread of every CTA is past its last grid wait once `done` reaches G: the last CTA
+  // resets the phase counters for the next launch
+  if (threadIdx.x == 0) {
+    int old;
+    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;"
+                 : "=r"(old)
+                 : "l"(p.bars + kChainMaxBars * kBarSlots * kBarStride)
+                 : "memory");
+    if (old == Gi - 1) {
+      for (int k = 0; k < kChainMaxBars * kBarSlots; ++k) p.bars[k * kBarStride] = 0;
+      p.bars[kChainMaxBars * kBarSlots * kBarStride] = 0;
+      __threadfence();
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------
 // host side
 static PFN_cuTensorMapEncodeTiled_v12000 get_encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -616,6 +1168,56 @@ static int launch_tc(const void* x, int ldx, const uint8_t* wq, const uint32_t* 
   return DSPARK_OK;
 }
 
+// ---- layer chain host side
+template <int BN>
+static int launch_chain(const ChainMaps& maps, const ChainParams& p, cudaStream_t st) {
+  constexpr int S = Cfg<BN>::kStages;
+  using L = Smem<BN, S>;
+  auto kern = chain_kernel<BN, S>;
+  static bool configured = false;
+  if (!configured) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kTotal) !=
+        cudaSuccess)
+      return set_error(DSPARK_ERR_CUDA, "chain: cudaFuncSetAttribute(smem=%u) failed", L::kTotal);
+    configured = true;
+  }
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, L::kTotal) != cudaSuccess ||
+      per_sm < 1)
+    return set_error(DSPARK_ERR_LAUNCH, "chain: no resident CTA fits");
+  const int grid = sm_count() * std::min(per_sm, Cfg<BN>::kCtasPerSm);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = L::kTotal;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, maps, p);
+  if (e != cudaSuccess) return set_error(DSPARK_ERR_LAUNCH, "chain launch failed: %s", cudaGetErrorString(e));
+  return DSPARK_OK;
+}
+
+static int chain_grid(int M) {
+  const int bn = pick_bn(M);
+  return sm_count() * (bn <= 32 ? 2 : 1);
+}
+
+// workspace: [phase counters + done (256 B)] [stream-K tile counters, a FIXED region of
+// kMaxTiles ints for every phase list] [2 partial regions]. The fixed region keeps one chain's
+// partials from landing where another chain (a different phase list sharing the workspace)
+// keeps its counters.
+static size_t chain_ws(int M, const dspark_chain_phase* ph, int n, size_t* off_part) {
+  (void)ph;
+  (void)n;
+  const size_t part = (size_t)chain_grid(M) * 2 * pick_bn(M) * BM * sizeof(float);
+  if (off_part) *off_part = kBarRegion + kCounterBytes;
+  return kBarRegion + kCounterBytes + 2 * part;
+}
+
 static size_t ws_bytes(int M, int N, int K) {
   const int bn = pick_bn(M);
   const int cps = bn <= 32 ? 2 : 1;
@@ -649,10 +1251,11 @@ static int gemm_common_checks(const void* x, int ldx, const uint8_t* wq, const u
   return DSPARK_OK;
 }
 
-extern "C" int dspark_w8a16_gemm(const void* x, int ldx, const uint8_t* wq, const uint32_t* wsb,
-                                 int M, int N, int K, void* y, int ldy, const void* residual,
-                                 int ldr, int epilogue, void* workspace, size_t workspace_bytes,
-                                 int* status, dspark_stream_t stream) {
+extern "C" int dspark_w8a16_gemm_pf(const void* x, int ldx, const uint8_t* wq, const uint32_t* wsb,
+                                    int M, int N, int K, void* y, int ldy, const void* residual,
+                                    int ldr, int epilogue, void* workspace, size_t workspace_bytes,
+                                    const void* pf0, size_t pf0_bytes, const void* pf1,
+                                    size_t pf1_bytes, int* status, dspark_stream_t stream) {
   int rc = gemm_common_checks(x, ldx, wq, wsb, M, N, K, y, epilogue, residual);
   if (rc) return rc;
   const size_t need = w8::ws_bytes(M, N, K);
@@ -671,12 +1274,137 @@ extern "C" int dspark_w8a16_gemm(const void* x, int ldx, const uint8_t* wq, cons
   p.counters = static_cast<int*>(workspace);
   p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + counters);
   p.status = status;
+  const void* pf[2] = {pf0, pf1};
+  const size_t pfb[2] = {pf0_bytes, pf1_bytes};
+  for (int r = 0; r < 2; ++r) {
+    if (pf[r] && pfb[r] && (reinterpret_cast<uintptr_t>(pf[r]) & 15))
+      return set_error(DSPARK_ERR_ALIGN, "w8a16_gemm_pf: prefetch range %d not 16-byte aligned", r);
+    p.pf_ptr[r] = static_cast<const char*>(pf[r]);
+    p.pf_bytes[r] = pf[r] ? (unsigned long long)(pfb[r] & ~(size_t)15) : 0ull;
+  }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   switch (w8::pick_bn(M)) {
     case 16: return w8::launch_tc<16>(x, ldx, wq, wsb, p, st);
     case 32: return w8::launch_tc<32>(x, ldx, wq, wsb, p, st);
     case 48: return w8::launch_tc<48>(x, ldx, wq, wsb, p, st);
     default: return w8::launch_tc<64>(x, ldx, wq, wsb, p, st);
+  }
+}
+
+extern "C" int dspark_w8a16_gemm(const void* x, int ldx, const uint8_t* wq, const uint32_t* wsb,
+                                 int M, int N, int K, void* y, int ldy, const void* residual,
+                                 int ldr, int epilogue, void* workspace, size_t workspace_bytes,
+                                 int* status, dspark_stream_t stream) {
+  return dspark_w8a16_gemm_pf(x, ldx, wq, wsb, M, N, K, y, ldy, residual, ldr, epilogue, workspace,
+                              workspace_bytes, nullptr, 0, nullptr, 0, status, stream);
+}
+
+extern "C" size_t dspark_chain_phase_size(void) { return sizeof(dspark_chain_phase); }
+
+extern "C" size_t dspark_chain_workspace_bytes(int M, const dspark_chain_phase* phases, int n) {
+  if (M <= 0 || M > 64 || !phases || n <= 0) return 0;
+  return w8::chain_ws(M, phases, n, nullptr);
+}
+
+extern "C" int dspark_run_chain(int M, const dspark_chain_phase* ph, int n, void* workspace,
+                                size_t workspace_bytes, int* status, dspark_stream_t stream) {
+  using namespace w8;
+  if (!ph || n <= 0 || n > kChainMaxPhases) return set_error(DSPARK_ERR_INVALID, "chain: %d phases", n);
+  if (M < 1 || M > 64) return set_error(DSPARK_ERR_INVALID, "chain: M=%d not in [1,64]", M);
+  size_t off_part = 0;
+  const size_t need = chain_ws(M, ph, n, &off_part);
+  if (!workspace || workspace_bytes < need)
+    return set_error(DSPARK_ERR_WORKSPACE, "chain: workspace %zu < %zu bytes", workspace_bytes, need);
+  const int BNv = pick_bn(M);
+  {
+    long long tiles = 0;
+    for (int i = 0; i < n; ++i)
+      if (ph[i].kind == DSPARK_PHASE_GEMM) tiles += ph[i].N / BM;
+    if (tiles > kMaxTiles) return set_error(DSPARK_ERR_UNSUPPORTED, "chain: %lld tiles > %d", tiles, kMaxTiles);
+  }
+  ChainMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  ChainParams p;
+  memset(&p, 0, sizeof(p));
+  p.M = M;
+  p.nphases = n;
+  p.status = status;
+  uint8_t* w = static_cast<uint8_t*>(workspace);
+  p.bars = reinterpret_cast<int*>(w);
+  int* counters = reinterpret_cast<int*>(w + kBarRegion);
+  const size_t part_bytes = (size_t)chain_grid(M) * 2 * BNv * BM * sizeof(float);
+  int ng = 0;
+  // dependencies: a grid barrier after every GEMM and NORM phase but the last phase; every
+  // phase reads what was written before the latest barrier
+  int nbar = 0, last_bar = -1, last_norm = -1;
+  for (int i = 0; i < n; ++i) {
+    const dspark_chain_phase& q = ph[i];
+    ChainPhase& P = p.ph[i];
+    P.kind = q.kind;
+    P.wait_bar = last_bar;
+    P.arrive_bar = -1;
+    P.local_norm = -1;
+    (void)last_norm;
+    if ((q.kind == DSPARK_PHASE_GEMM || q.kind == DSPARK_PHASE_NORM) && i < n - 1) {
+      P.arrive_bar = nbar++;
+      last_bar = P.arrive_bar;
+    }
+    switch (q.kind) {
+      case DSPARK_PHASE_GEMM: {
+        if (ng >= kChainMaxGemm) return set_error(DSPARK_ERR_UNSUPPORTED, "chain: more than %d GEMMs", kChainMaxGemm);
+        int rc = gemm_common_checks(q.x, q.ldx, q.wq, q.wsb, M, q.N, q.K, q.y, q.epilogue, q.residual);
+        if (rc) return rc;
+        ChainGemm& g = p.g[ng];
+        g.N = q.N; g.K = q.K; g.tiles = q.N / BM; g.kb = q.K / BK;
+        g.total = (long long)g.tiles * g.kb;
+        g.epilogue = q.epilogue; g.y = q.y; g.ldy = q.ldy; g.residual = q.residual; g.ldr = q.ldr;
+        g.counters = counters;
+        counters += g.tiles;
+        g.partials = reinterpret_cast<float*>(w + off_part + (size_t)(ng & 1) * part_bytes);
+        if ((rc = make_map_2d(&maps.w[ng], CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, q.wq, (uint64_t)q.K,
+                              (uint64_t)q.N, (uint64_t)q.K, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B)))
+          return rc;
+        if ((rc = make_map_2d(&maps.sb[ng], CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, q.wsb, (uint64_t)q.N,
+                              (uint64_t)(q.K / 64), (uint64_t)q.N * 4, BM, 2, CU_TENSOR_MAP_SWIZZLE_NONE)))
+          return rc;
+        if ((rc = make_map_2d(&maps.x[ng], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, q.x, (uint64_t)q.K,
+                              (uint64_t)M, (uint64_t)q.ldx * 2, 64, BNv, CU_TENSOR_MAP_SWIZZLE_128B)))
+          return rc;
+        P.gemm = ng++;
+        break;
+      }
+      case DSPARK_PHASE_NORM:
+      case DSPARK_PHASE_COPY_F16:
+        if (!q.x || !q.y || q.H <= 0 || q.H % 2 || q.ldx < q.H || q.ldy < q.H || q.ldx % 2 || q.ldy % 2 ||
+            (q.kind == DSPARK_PHASE_NORM && !q.w))
+          return set_error(DSPARK_ERR_INVALID, "chain: bad norm/copy phase %d", i);
+        P.x = static_cast<const __nv_bfloat16*>(q.x); P.ldx = q.ldx;
+        P.w = static_cast<const __nv_bfloat16*>(q.w); P.H = q.H; P.eps = q.eps;
+        P.y16 = static_cast<__half*>(q.y); P.ldy16 = q.ldy;
+        break;
+      case DSPARK_PHASE_ROPE_KV:
+        if (!q.qkv || !q.k_norm || !q.inv_freq || !q.pos0 || (q.Hq > 0 && (!q.q_out || !q.q_norm)) ||
+            (q.hd != 64 && q.hd != 128) || q.T <= 0 || M % q.T || q.kv.head_dim != q.hd ||
+            q.kv.num_kv_heads != q.Hkv || !q.kv.pool || !q.kv.block_table)
+          return set_error(DSPARK_ERR_INVALID, "chain: bad rope phase %d", i);
+        P.qkv = static_cast<const __nv_bfloat16*>(q.qkv); P.ldqkv = q.ldqkv; P.T = q.T;
+        P.Hq = q.Hq; P.Hkv = q.Hkv; P.hd = q.hd;
+        P.qnw = static_cast<const __nv_bfloat16*>(q.q_norm);
+        P.knw = static_cast<const __nv_bfloat16*>(q.k_norm);
+        P.eps = q.eps; P.inv_freq = q.inv_freq; P.pos0 = q.pos0;
+        P.q_out = static_cast<__nv_bfloat16*>(q.q_out); P.kv = q.kv;
+        break;
+      default:
+        return set_error(DSPARK_ERR_INVALID, "chain: phase %d kind %d", i, q.kind);
+    }
+  }
+  p.ngemm = ng;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (BNv) {
+    case 16: return launch_chain<16>(maps, p, st);
+    case 32: return launch_chain<32>(maps, p, st);
+    case 48: return launch_chain<48>(maps, p, st);
+    default: return launch_chain<64>(maps, p, st);
   }
 }
 

@@ -10,7 +10,7 @@ from __future__ import annotations
 import torch
 
 from . import _lib
-from ._lib import KvLayout, call, lib
+from ._lib import ChainPhase, KvLayout, call, lib
 from .weights import PackedLinear
 
 
@@ -31,7 +31,7 @@ def _require_cuda(*ts):
 class Scratch:
     """Zero-filled, grow-only workspaces per kernel family plus a device status word."""
 
-    FAMILIES = ("gemm", "attention", "accept", "markov", "accept_sample", "markov_probs")
+    FAMILIES = ("gemm", "attention", "accept", "markov", "accept_sample", "markov_probs", "chain")
 
     def __init__(self, device="cuda"):
         self.device = torch.device(device)
@@ -64,17 +64,32 @@ def gemm_workspace_bytes(M: int, N: int, K: int) -> int:
     return int(lib().dspark_w8a16_gemm_workspace_bytes(M, N, K))
 
 
+PREFETCH_LIMIT = 16 << 20  # bytes of the next weights warmed in L2 (16 MB measured best on C2)
+
+
 def gemm(x16: torch.Tensor, w: PackedLinear, y: torch.Tensor, *, epilogue=_lib.EPI_STORE_BF16,
-         residual: torch.Tensor | None = None, scratch: Scratch, M: int | None = None) -> torch.Tensor:
-    """y = x16 @ W^T with the chosen epilogue (see include/dspark_b200.h)."""
+         residual: torch.Tensor | None = None, scratch: Scratch, M: int | None = None,
+         prefetch: PackedLinear | None = None) -> torch.Tensor:
+    """y = x16 @ W^T with the chosen epilogue (see include/dspark_b200.h). `prefetch`: the next
+    projection's weights, warmed in L2 (up to PREFETCH_LIMIT bytes) during this GEMM's tail."""
     _require_cuda(x16, y)
     M = x16.shape[0] if M is None else M
     K = w.K
     assert x16.dtype == torch.float16 and x16.shape[-1] >= K
     ws = scratch.get("gemm", gemm_workspace_bytes(M, w.N, K))
-    call("dspark_w8a16_gemm", _p(x16), x16.stride(0), _p(w.q), _p(w.sb), M, w.N, K, _p(y),
+    if prefetch is None or PREFETCH_LIMIT <= 0:
+        call("dspark_w8a16_gemm", _p(x16), x16.stride(0), _p(w.q), _p(w.sb), M, w.N, K, _p(y),
+             y.stride(0), _p(residual), residual.stride(0) if residual is not None else 0,
+             epilogue, _p(ws), ws.numel(), _p(scratch.status), _stream())
+        return y
+    # q is row-major [N, K]: a prefix of it is whole 128-row tiles. sb is [K/64, N] (1/16 of q's
+    # bytes), so any prefix covers a few groups of every row: warm all of it, up to limit / 8.
+    qb = min(prefetch.q.numel(), PREFETCH_LIMIT)
+    sbb = min(prefetch.sb.numel() * 4, PREFETCH_LIMIT // 8)
+    call("dspark_w8a16_gemm_pf", _p(x16), x16.stride(0), _p(w.q), _p(w.sb), M, w.N, K, _p(y),
          y.stride(0), _p(residual), residual.stride(0) if residual is not None else 0, epilogue,
-         _p(ws), ws.numel(), _p(scratch.status), _stream())
+         _p(ws), ws.numel(), _p(prefetch.q), qb, _p(prefetch.sb), sbb, _p(scratch.status),
+         _stream())
     return y
 
 
@@ -270,3 +285,37 @@ def markov_sample_block_probs(base: torch.Tensor, rows_per_b: int, B: int, cap: 
          w2.K, _p(w1.q), _p(w1.sb), _p(w2.q), _p(w2.sb), _p(first_prev), _p(draft),
          _p(verify_ids), float(temperature), float(top_p), int(top_k or 0), _p(rng), _p(q_probs),
          q_probs.shape[-1], _p(ws), ws.numel(), _stream())
+
+
+# ----------------------------------------------------------------------------------------
+# layer chain (dspark_run_chain): the phases between two attention kernels in one launch
+def gemm_phase(x16: torch.Tensor, w: PackedLinear, y: torch.Tensor, epilogue: int,
+               residual: torch.Tensor | None = None) -> ChainPhase:
+    return ChainPhase(kind=_lib.PHASE_GEMM, epilogue=epilogue, x=_p(x16), ldx=x16.stride(0),
+                      wq=_p(w.q), wsb=_p(w.sb), N=w.N, K=w.K, y=_p(y), ldy=y.stride(0),
+                      residual=_p(residual), ldr=residual.stride(0) if residual is not None else 0)
+
+
+def norm_phase(x: torch.Tensor, w: torch.Tensor, eps: float, y16: torch.Tensor) -> ChainPhase:
+    return ChainPhase(kind=_lib.PHASE_NORM, x=_p(x), ldx=x.stride(0), w=_p(w), H=w.numel(),
+                      eps=float(eps), y=_p(y16), ldy=y16.stride(0))
+
+
+def copy_phase(src: torch.Tensor, dst: torch.Tensor, cols: int) -> ChainPhase:
+    return ChainPhase(kind=_lib.PHASE_COPY_F16, x=_p(src), ldx=src.stride(0), H=int(cols),
+                      y=_p(dst), ldy=dst.stride(0))
+
+
+def rope_phase(qkv: torch.Tensor, T: int, Hq: int, Hkv: int, hd: int, q_norm, k_norm, eps: float,
+               inv_freq: torch.Tensor, pos0: torch.Tensor, q_out, kv: KvLayout) -> ChainPhase:
+    return ChainPhase(kind=_lib.PHASE_ROPE_KV, qkv=_p(qkv), ldqkv=qkv.stride(0), T=int(T),
+                      Hq=int(Hq), Hkv=int(Hkv), hd=int(hd), q_norm=_p(q_norm), k_norm=_p(k_norm),
+                      eps=float(eps), inv_freq=_p(inv_freq), pos0=_p(pos0), q_out=_p(q_out), kv=kv)
+
+
+def run_chain(M: int, phases: list, scratch: Scratch) -> None:
+    """One launch running `phases` in order (see include/dspark_b200.h, K1c)."""
+    arr = (ChainPhase * len(phases))(*phases)
+    need = int(lib().dspark_chain_workspace_bytes(M, arr, len(phases)))
+    ws = scratch.get("chain", need)
+    call("dspark_run_chain", M, arr, len(phases), _p(ws), ws.numel(), _p(scratch.status), _stream())

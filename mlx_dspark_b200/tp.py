@@ -107,6 +107,7 @@ class TPTarget(Target):
     process per GPU) for device tensors; every rank runs the same decode loop."""
 
     capturable = False  # rounds with collectives run eagerly
+    use_chain = False   # the all-reduces sit between the projections
 
     def __init__(self, weights: TargetWeights, rank: int, world: int, group=None, tokenizer=None,
                  *, kv_bits: int | None = None, device="cuda"):

@@ -65,3 +65,9 @@ def test_pack_rejects_values_fp16_cannot_hold():
     qt.scales[0, 0] = torch.tensor(1e-7).to(torch.bfloat16)
     with pytest.raises(ValueError):
         pack(qt, device="cpu")
+
+
+def test_chain_phase_struct_matches_the_c_layout():
+    import ctypes
+    from mlx_dspark_b200 import _lib
+    assert ctypes.sizeof(_lib.ChainPhase) == _lib.lib().dspark_chain_phase_size()
