@@ -194,11 +194,17 @@ def gemm_roofline(target, M, reps=5):
     H, I = c.hidden_size, c.intermediate_size
 
     def one_pass():
-        for L in target.layers:
-            ops.gemm(x[:, :H], L.qkv, qkv, epilogue=EPI_STORE_BF16, scratch=sc, M=M)
-            ops.gemm(x[:, :c.q_dim], L.o, h, epilogue=EPI_RESIDUAL_BF16, residual=h, scratch=sc, M=M)
-            ops.gemm(x[:, :H], L.gu, act, epilogue=EPI_SILU_MUL_F16, scratch=sc, M=M)
-            ops.gemm(x[:, :I], L.down, h, epilogue=EPI_RESIDUAL_BF16, residual=h, scratch=sc, M=M)
+        # the verify forward's GEMM sequence, each warming L2 with the next one's weights
+        n = len(target.layers)
+        for l, L in enumerate(target.layers):
+            nxt = target.layers[l + 1].qkv if l + 1 < n else target.head
+            ops.gemm(x[:, :H], L.qkv, qkv, epilogue=EPI_STORE_BF16, scratch=sc, M=M, prefetch=L.o)
+            ops.gemm(x[:, :c.q_dim], L.o, h, epilogue=EPI_RESIDUAL_BF16, residual=h, scratch=sc,
+                     M=M, prefetch=L.gu)
+            ops.gemm(x[:, :H], L.gu, act, epilogue=EPI_SILU_MUL_F16, scratch=sc, M=M,
+                     prefetch=L.down)
+            ops.gemm(x[:, :I], L.down, h, epilogue=EPI_RESIDUAL_BF16, residual=h, scratch=sc, M=M,
+                     prefetch=nxt)
         ops.gemm(x[:, :H], target.head, logits, epilogue=EPI_STORE_BF16, scratch=sc, M=M)
 
     wbytes = sum(L.qkv.nbytes() + L.o.nbytes() + L.gu.nbytes() + L.down.nbytes()
