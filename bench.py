@@ -233,6 +233,7 @@ def gemm_roofline(target, M, reps=5):
 def verify_step_us(target, sess, reps=30):
     """Device time of the verify forward + fused acceptance alone (one CUDA graph)."""
     from mlx_dspark_b200 import ops
+    from mlx_dspark_b200.generate import capture_graph
 
     t = target
     B, T = sess.B, sess.T
@@ -244,13 +245,7 @@ def verify_step_us(target, sess, reps=30):
 
     launch()
     torch.cuda.synchronize()
-    g = torch.cuda.CUDAGraph()
-    st = torch.cuda.Stream()
-    st.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.stream(st):
-        with torch.cuda.graph(g, stream=st):
-            launch()
-    torch.cuda.current_stream().wait_stream(st)
+    g = capture_graph(launch)
     g.replay()
     torch.cuda.synchronize()
     s = torch.cuda.Event(enable_timing=True)

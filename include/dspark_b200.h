@@ -92,6 +92,20 @@ int dspark_w8a16_gemm_pf(const void* x, int ldx, const uint8_t* wq, const uint32
                          int epilogue, void* workspace, size_t workspace_bytes, const void* pf0,
                          size_t pf0_bytes, const void* pf1, size_t pf1_bytes, int* status,
                          dspark_stream_t stream);
+/* How the K dimension is split across CTAs (process-wide; no reference counterpart):
+ *   0 (default) — stream-K for every GEMM: equal contiguous ranges of (tile, k-block) units,
+ *                 split tiles finished by the last CTA to arrive, in CTA order;
+ *   1           — GEMMs with few 128-row tiles (N/128 at most half the SMs, e.g. q|k|v, o and
+ *                 down at Qwen3 widths) cut each tile's K into c <= 8 slices that run as one
+ *                 thread-block cluster, one CTA per SM, and sum their fp32 partials through
+ *                 distributed shared memory in slice order; other GEMMs stay stream-K.
+ *                 Slower than mode 0 on B200 in a launch chain; kept as an option.
+ * Both are deterministic; they differ only in the fp32 summation order of split tiles. */
+int dspark_w8a16_gemm_split_mode(int mode);
+/* The launch a GEMM of this shape gets under the current split mode: *grid CTAs, *cluster =
+ * the cluster size of the split-K form (0 = stream-K), *max_active (optional) = how many
+ * clusters of the preferred size the device keeps resident (-1 if none or not queried). */
+int dspark_w8a16_gemm_plan(int M, int N, int K, int* grid, int* cluster, int* max_active);
 
 /* -------------------------------------------------------------------------------------
  * K13 — embedding dequant-gather. Replaces mlx QuantizedEmbedding (embed_tokens,

@@ -43,8 +43,7 @@ __global__ void __launch_bounds__(kThreads) accept_greedy_kernel(
     int32_t* __restrict__ kv_len, int commit, int32_t* __restrict__ pending,
     int32_t* __restrict__ plan, float* __restrict__ part_v, int* __restrict__ part_i,
     int* __restrict__ counter) {
-  pdl_wait();
-  pdl_launch_dependents();
+  pdl_enter();
   const int rows = B * T;
   const int chunk = ((V + gridDim.x - 1) / gridDim.x + 7) & ~7;
   const int v0 = blockIdx.x * chunk;
@@ -111,8 +110,7 @@ __global__ void __launch_bounds__(kThreads) accept_greedy_kernel(
 // kv_len[b] += plan[b * stride + 1] for every length array given
 __global__ void commit_lengths_kernel(const int32_t* __restrict__ plan, int stride, int B,
                                       int32_t* __restrict__ a, int32_t* __restrict__ b2) {
-  pdl_wait();
-  pdl_launch_dependents();
+  pdl_enter();
   for (int b = threadIdx.x; b < B; b += blockDim.x) {
     const int add = plan[(size_t)b * stride + 1];
     if (a) a[b] += add;
@@ -129,8 +127,7 @@ __global__ void draft_override_kernel(int B, int cap, int V, const int32_t* __re
                                       const int32_t* __restrict__ kv_len,
                                       const int32_t* __restrict__ prompt_len,
                                       int32_t* __restrict__ verify_ids) {
-  pdl_wait();
-  pdl_launch_dependents();
+  pdl_enter();
   const int b = blockIdx.x;
   const int rnd = min(round_ctr[b], rounds - 1);
   for (int i = threadIdx.x; i < cap; i += blockDim.x) {
@@ -149,8 +146,7 @@ constexpr int kArgThreads = 1024;
 __global__ void __launch_bounds__(kArgThreads) argmax_rows_kernel(
     const __nv_bfloat16* __restrict__ logits, long long ld, int V, int32_t* __restrict__ tokens,
     int s1, int32_t* __restrict__ tokens2, int s2, float* __restrict__ values, int index_offset) {
-  pdl_wait();
-  pdl_launch_dependents();
+  pdl_enter();
   const int r = blockIdx.x;
   const __nv_bfloat16* row = logits + (size_t)r * ld;
   Best b{-INFINITY, 0x7fffffff};
@@ -190,8 +186,7 @@ __global__ void accept_sharded_kernel(const float* __restrict__ vals, const int3
                                       int shards, int B, int T, const int32_t* __restrict__ verify_ids,
                                       int32_t* __restrict__ kv_len, int commit,
                                       int32_t* __restrict__ pending, int32_t* __restrict__ plan) {
-  pdl_wait();
-  pdl_launch_dependents();
+  pdl_enter();
   const int rows = B * T;
   for (int b = threadIdx.x; b < B; b += blockDim.x) {
     int tt[64];
@@ -216,8 +211,7 @@ __global__ void accept_sharded_kernel(const float* __restrict__ vals, const int3
 }
 
 __global__ void bump_kernel(int32_t* __restrict__ ctr, int B) {
-  pdl_wait();
-  pdl_launch_dependents();
+  pdl_enter();
   for (int b = threadIdx.x; b < B; b += blockDim.x) ctr[b] += 1;
 }
 

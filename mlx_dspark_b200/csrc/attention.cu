@@ -141,8 +141,7 @@ template <int HD, bool KV8>
 __global__ void __launch_bounds__(256) attn_kernel(const Args a) {
   using L = Layout<HD, KV8>;
   extern __shared__ __align__(16) uint8_t smem[];
-  pdl_wait();
-  pdl_launch_dependents();
+  pdl_enter();
 
   const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int Hkv = a.kv.num_kv_heads;
@@ -318,8 +317,7 @@ __global__ void __launch_bounds__(256) attn_kernel(const Args a) {
 // over the head dimension for O, whose splits are summed in split order.
 template <int HD>
 __global__ void __launch_bounds__(256) attn_combine_kernel(const Args a) {
-  pdl_wait();
-  pdl_launch_dependents();
+  pdl_enter();
   constexpr int E = HD / 32;  // output dims per lane
   const int h = blockIdx.y, b = blockIdx.z;
   const int kvlen = a.kv_len[b];

@@ -69,6 +69,31 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
+// Entry of the small kernels: wait for the previous kernel, then let the next one launch.
+// (Triggering before the wait lets the next kernel's CTAs take SM slots even earlier; on B200 that
+// left the verify pass unchanged and slowed the drafter's chain of Markov steps by ~110 us.)
+__device__ __forceinline__ void pdl_enter() {
+  pdl_wait();
+  pdl_launch_dependents();
+}
+
+// ------------------------------------------------------------------------------------------
+// thread-block clusters: a full cluster barrier (every thread of every CTA arrives; release on
+// arrive, acquire on wait), the shared::cluster address of the same shared-memory offset in
+// CTA `rank` of the cluster, and a load through it.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float ld_shared_cluster_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
 
 // ------------------------------------------------------------------------------------------
 // bulk L2 prefetch (fire and forget): warm L2 with bytes a later kernel will read.
@@ -131,6 +156,20 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar), "l"(policy)
       : "memory");
+}
+// Untiled bulk copy global -> this CTA's shared memory (no multicast): dst and src 16-byte
+// aligned, bytes a multiple of 16; completion is counted on `bar` in bytes.
+__device__ __forceinline__ void bulk_load_g2s(uint32_t dst, const void* src, uint32_t bytes,
+                                              uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+      : "memory");
+}
+// Orders this thread's earlier generic-proxy accesses (and what it acquired) before its later
+// async-proxy (bulk copy / TMA) accesses of global memory.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

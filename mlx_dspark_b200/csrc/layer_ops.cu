@@ -14,8 +14,7 @@ __global__ void __launch_bounds__(256) embed_w8_kernel(const int32_t* __restrict
                                                        const uint32_t* __restrict__ wsb, int V,
                                                        int H, __nv_bfloat16* __restrict__ out,
                                                        int ldo) {
-  pdl_wait();
-  pdl_launch_dependents();
+  pdl_enter();
   const int m = blockIdx.x;
   int id = ids[m];
   id = id < 0 ? 0 : (id >= V ? V - 1 : id);
@@ -41,8 +40,7 @@ __global__ void __launch_bounds__(256) embed_block_w8_kernel(const int32_t* __re
                                                              int V, int H,
                                                              __nv_bfloat16* __restrict__ out,
                                                              int ldo, int32_t* __restrict__ ids_out) {
-  pdl_wait();
-  pdl_launch_dependents();
+  pdl_enter();
   const int m = blockIdx.x;
   const int b = m / k, i = m - b * k;
   int id = i == 0 ? pending[b] : mask_id;
@@ -65,8 +63,7 @@ __global__ void __launch_bounds__(256) embed_block_w8_kernel(const int32_t* __re
 __global__ void __launch_bounds__(256) bf16_to_f16_kernel(const __nv_bfloat16* __restrict__ src,
                                                           int lds, __half* __restrict__ dst,
                                                           int ldd, int cols) {
-  pdl_wait();
-  pdl_launch_dependents();
+  pdl_enter();
   const int r = blockIdx.x;
   for (int c = threadIdx.x * 2; c < cols; c += blockDim.x * 2) {
     const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + (size_t)r * lds + c));
@@ -81,8 +78,7 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* __res
                                                       float eps, __nv_bfloat16* __restrict__ y,
                                                       int ldy, __half* __restrict__ y16,
                                                       int ldy16) {
-  pdl_wait();
-  pdl_launch_dependents();
+  pdl_enter();
   const int m = blockIdx.x;
   const __nv_bfloat16* xr = x + (size_t)m * ldx;
   float ss = 0.0f;
@@ -121,8 +117,7 @@ __global__ void __launch_bounds__(256) qkv_rope_kv_kernel(
     const float* __restrict__ inv_freq, const int32_t* __restrict__ pos0,
     __nv_bfloat16* __restrict__ q_out, dspark_kv_layout kv) {
   constexpr int HD = E * 32;
-  pdl_wait();
-  pdl_launch_dependents();
+  pdl_enter();
   const int m = blockIdx.x;
   const int b = m / T, t = m - b * T;
   const int pos = pos0[b] + t;
@@ -218,8 +213,7 @@ extern "C" int dspark_bf16_to_f16(const void* src, int lds, void* dst, int ldd, 
 // W8 GEMM, applied after the all-reduce).
 __global__ void residual_add_f32_kernel(__nv_bfloat16* __restrict__ h, int ldh,
                                         const float* __restrict__ sum, int lds, int M, int N) {
-  pdl_wait();
-  pdl_launch_dependents();
+  pdl_enter();
   const long long total = (long long)M * N;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {

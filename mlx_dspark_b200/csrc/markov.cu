@@ -45,8 +45,7 @@ __global__ void __launch_bounds__(kThreads) markov_step_kernel(
     const int32_t* __restrict__ first_prev, int32_t* __restrict__ draft,
     int32_t* __restrict__ verify_ids, float* __restrict__ part_v, int* __restrict__ part_i,
     int* __restrict__ counter, __nv_bfloat16* __restrict__ out, int ld_out) {
-  pdl_wait();
-  pdl_launch_dependents();
+  pdl_enter();
   if (SAMPLE && step == 0 && verify_ids && blockIdx.x == 0 && threadIdx.x < NB)
     verify_ids[threadIdx.x * (cap + 1)] = first_prev[threadIdx.x];
   __shared__ __align__(16) float e[NB][kR];

@@ -22,8 +22,7 @@ __global__ void __launch_bounds__(kThreads) apply_kernel(
     __nv_bfloat16* __restrict__ logits, long long ld, int T, int V,
     const int32_t* __restrict__ counts, const int32_t* __restrict__ verify_ids, float P, float F,
     float inc_new, float inc_seen) {
-  pdl_wait();
-  pdl_launch_dependents();
+  pdl_enter();
   const int b = blockIdx.y;
   __shared__ int draft[kMaxT];
   for (int i = threadIdx.x; i < T - 1; i += kThreads) draft[i] = verify_ids[(size_t)b * T + 1 + i];
@@ -53,8 +52,7 @@ __global__ void __launch_bounds__(kThreads) apply_kernel(
 // counts[b][tok] += 1 for the committed tokens plan[b][2 .. 2 + plan[b][1])
 __global__ void counts_add_kernel(int32_t* __restrict__ counts, int V,
                                   const int32_t* __restrict__ plan, int plan_stride) {
-  pdl_wait();
-  pdl_launch_dependents();
+  pdl_enter();
   const int b = blockIdx.x;
   const int32_t* pl = plan + (size_t)b * plan_stride;
   const int cnt = pl[1];

@@ -434,8 +434,7 @@ __global__ void __launch_bounds__(kThreads, 1) row_kernel(const Args a) {
   const int n = v1 - v0;
   int slot = 0;
 
-  pdl_wait();
-  pdl_launch_dependents();
+  pdl_enter();
 
   for (int i = tid; i < kSub * kBins; i += kThreads) {
     (&s.sub_cnt[0][0])[i] = 0;

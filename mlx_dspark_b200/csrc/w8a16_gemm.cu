@@ -65,6 +65,10 @@ struct Params {
   float* partials;  // [grid][2][BN][128]
   int* counters;    // [tiles]
   int* status;
+  // > 1: cluster split-K. CTA b works on tile b / csplit, k-slice b % csplit; the csplit CTAs
+  // of a tile form one thread-block cluster and sum their partials through distributed shared
+  // memory. 0: stream-K over the whole grid.
+  int csplit;
   // L2 prefetch of the next kernel's operands: CTA b warms bytes [b*chunk, (b+1)*chunk) of each
   // range after issuing its last load (16-byte aligned, sizes multiples of 16)
   const char* pf_ptr[2];
@@ -101,14 +105,22 @@ __device__ __forceinline__ void epilogue_store(const Params& p, int tile, int er
       break;
     }
     case DSPARK_EPI_RESIDUAL_BF16: {
+      // y may be the residual itself (in place): read every row first, then store, so the
+      // loads are not ordered one by one behind the stores they might alias
       __nv_bfloat16* y = static_cast<__nv_bfloat16*>(p.y);
       const __nv_bfloat16* r = static_cast<const __nv_bfloat16*>(p.residual);
 #pragma unroll
-      for (int m = 0; m < BN; ++m)
-        if (m < p.M) {
-          const float rv = __bfloat162float(r[(size_t)m * p.ldr + n]);
-          y[(size_t)m * p.ldy + n] = __float2bfloat16_rn(rv + bf16_round(acc[m]));
-        }
+      for (int c0 = 0; c0 < BN; c0 += 16) {  // 16 rows at a time bounds the registers held
+        __nv_bfloat16 rv[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          rv[j] = c0 + j < p.M ? r[(size_t)(c0 + j) * p.ldr + n] : __float2bfloat16_rn(0.0f);
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          if (c0 + j < p.M)
+            y[(size_t)(c0 + j) * p.ldy + n] =
+                __float2bfloat16_rn(__bfloat162float(rv[j]) + bf16_round(acc[c0 + j]));
+      }
       break;
     }
     case DSPARK_EPI_SILU_MUL_F16: {
@@ -122,15 +134,52 @@ __device__ __forceinline__ void epilogue_store(const Params& p, int tile, int er
         __half* y = static_cast<__half*>(p.y);
         const int col = tile * 64 + er;
 #pragma unroll
-        for (int m = 0; m < BN; ++m)
-          if (m < p.M) {
-            const float g = bf16_round(acc[m]);
-            const float u = bf16_round(xch[er * BN + m]);
-            const float s = bf16_round(silu_f(g));
-            y[(size_t)m * p.ldy + col] = __float2half_rn(bf16_round(s * u));
-          }
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          // the exchanged values first (xch is a generic pointer the stores may alias)
+          float up[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) up[j] = xch[er * BN + c0 + j];
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (c0 + j < p.M) {
+              const float g = bf16_round(acc[c0 + j]);
+              const float u = bf16_round(up[j]);
+              const float s = bf16_round(silu_f(g));
+              y[(size_t)(c0 + j) * p.ldy + col] = __float2half_rn(bf16_round(s * u));
+            }
+        }
       }
       asm volatile("bar.sync 1, 128;" ::: "memory");
+      break;
+    }
+    default:
+      break;
+  }
+}
+
+// One output of the tile from its accumulated value v (and, for SILU_MUL, the matching up-row
+// value vu): the same arithmetic as epilogue_store, element by element. `row` is the tile row
+// (for SILU_MUL a gate row < 64), m the activation row.
+__device__ __forceinline__ void epilogue_one(const Params& p, int tile, int row, int m, float v,
+                                             float vu) {
+  switch (p.epilogue) {
+    case DSPARK_EPI_STORE_BF16:
+      static_cast<__nv_bfloat16*>(p.y)[(size_t)m * p.ldy + tile * BM + row] = __float2bfloat16_rn(v);
+      break;
+    case DSPARK_EPI_STORE_F32:
+      static_cast<float*>(p.y)[(size_t)m * p.ldy + tile * BM + row] = v;
+      break;
+    case DSPARK_EPI_RESIDUAL_BF16: {
+      const size_t n = (size_t)tile * BM + row;
+      const float rv = __bfloat162float(static_cast<const __nv_bfloat16*>(p.residual)[(size_t)m * p.ldr + n]);
+      static_cast<__nv_bfloat16*>(p.y)[(size_t)m * p.ldy + n] = __float2bfloat16_rn(rv + bf16_round(v));
+      break;
+    }
+    case DSPARK_EPI_SILU_MUL_F16: {
+      const float g = bf16_round(v);
+      const float u = bf16_round(vu);
+      const float sg = bf16_round(silu_f(g));
+      static_cast<__half*>(p.y)[(size_t)m * p.ldy + tile * 64 + row] = __float2half_rn(bf16_round(sg * u));
       break;
     }
     default:
@@ -143,16 +192,27 @@ struct Smem {
   static constexpr uint32_t kXBytes = 2u * BN * 128u;
   static constexpr uint32_t kStageBytes = kWBytes + kXBytes + kSBBytes;
   static constexpr uint32_t kXchBytes = 64u * BN * 4u;
-  static constexpr uint32_t kBarBytes = 256;
+  static constexpr uint32_t kBarBytes = 512;
   static constexpr uint32_t kTotal = 1024 + STAGES * kStageBytes + kXchBytes + kBarBytes;
 };
 
-template <int BN, int STAGES>
-__global__ void __launch_bounds__(kThreads, (BN <= 32 ? 2 : 1))
+template <int BN, int STAGES, bool CS>
+__global__ void __launch_bounds__(kThreads, (BN <= 32 && !CS ? 2 : 1))
     w8a16_tc_kernel(const __grid_constant__ CUtensorMap tm_w,
                     const __grid_constant__ CUtensorMap tm_sb,
                     const __grid_constant__ CUtensorMap tm_x, const Params p) {
   using L = Smem<BN, STAGES>;
+  // TMEM: [0, AB*64) the converted-weight ring (64 columns = 128 fp16 per lane each), then two
+  // fp32 accumulators of ACCS columns. Two CTAs per SM share the 512 columns; one CTA per SM
+  // takes all of them for a deeper ring (the ring depth bounds how far conversion runs ahead
+  // of MMA completion).
+  constexpr bool kTwoPerSm = BN <= 32 && !CS;
+  constexpr int AB = kTwoPerSm ? 3 : 6;
+  constexpr uint32_t ACCS = BN <= 32 ? 32u : 64u;
+  constexpr uint32_t ACC0 = (uint32_t)AB * 64u;
+  constexpr uint32_t TC = kTwoPerSm ? 256u : 512u;
+  static_assert(ACC0 + 2 * ACCS <= TC, "TMEM layout");
+  static_assert(3 * STAGES + 2 * AB + 8 <= (int)(L::kBarBytes / 8), "barrier region");
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -168,13 +228,14 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 ? 2 : 1))
   auto xfull = [&](int s) { return smem_u32(bars + STAGES + s); };
   auto empty = [&](int s) { return smem_u32(bars + 2 * STAGES + s); };
   auto afull = [&](int a) { return smem_u32(bars + 3 * STAGES + a); };
-  auto aempty = [&](int a) { return smem_u32(bars + 3 * STAGES + kABufs + a); };
-  auto accfull = [&](int b) { return smem_u32(bars + 3 * STAGES + 2 * kABufs + b); };
-  auto accempty = [&](int b) { return smem_u32(bars + 3 * STAGES + 2 * kABufs + 2 + b); };
-  const uint32_t done_bar = smem_u32(bars + 3 * STAGES + 2 * kABufs + 4);
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 3 * STAGES + 2 * kABufs + 5);
+  auto aempty = [&](int a) { return smem_u32(bars + 3 * STAGES + AB + a); };
+  auto accfull = [&](int b) { return smem_u32(bars + 3 * STAGES + 2 * AB + b); };
+  auto accempty = [&](int b) { return smem_u32(bars + 3 * STAGES + 2 * AB + 2 + b); };
+  const uint32_t done_bar = smem_u32(bars + 3 * STAGES + 2 * AB + 4);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 3 * STAGES + 2 * AB + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_holder + 2);
+  const uint32_t fix_bar = smem_u32(bars + 3 * STAGES + 2 * AB + 7);  // stream-K fixup copies
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -185,7 +246,7 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 ? 2 : 1))
       mbar_init(xfull(s), 1);
       mbar_init(empty(s), kConvWarps + 1);
     }
-    for (int a = 0; a < kABufs; ++a) {
+    for (int a = 0; a < AB; ++a) {
       mbar_init(afull(a), kConvWarps);
       mbar_init(aempty(a), 1);
     }
@@ -194,6 +255,7 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 ? 2 : 1))
       mbar_init(accempty(b), kEpiWarps);
     }
     mbar_init(done_bar, 1);
+    mbar_init(fix_bar, 1);
     *abort_flag = 0;
     *last_flag = 0;
     fence_mbar_init();
@@ -205,7 +267,7 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 ? 2 : 1))
       tma_prefetch_desc(&tm_x);
     }
     __syncwarp();
-    tmem_alloc(smem_u32(tmem_holder), kTmemCols);
+    tmem_alloc(smem_u32(tmem_holder), TC);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -216,10 +278,17 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 ? 2 : 1))
 
   const long long G = gridDim.x;
   const long long total = p.total;
-  const long long start = range_start(blockIdx.x, total, G);
-  const long long end = range_start(blockIdx.x + 1, total, G);
-  const int n_iter = (int)(end - start);
   const int KB = p.kb;
+  long long start, end;
+  if constexpr (CS) {
+    const int tile = (int)(blockIdx.x / p.csplit), r = (int)(blockIdx.x % p.csplit);
+    start = (long long)tile * KB + (long long)r * KB / p.csplit;
+    end = (long long)tile * KB + (long long)(r + 1) * KB / p.csplit;
+  } else {
+    start = range_start(blockIdx.x, total, G);
+    end = range_start(blockIdx.x + 1, total, G);
+  }
+  const int n_iter = (int)(end - start);
 
   if (warp == kProducerWarp) {
     if (lane == 0) {
@@ -293,15 +362,15 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 ? 2 : 1))
         const bool seg_last = (i == n_iter - 1) || (kb == KB - 1);
         const int s = i % STAGES;
         const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
-        const int a = i % kABufs;
-        const uint32_t aph = (uint32_t)(i / kABufs) & 1u;
+        const int a = i % AB;
+        const uint32_t aph = (uint32_t)(i / AB) & 1u;
         const int ab = seg & 1;
         const uint32_t abph = (uint32_t)(seg >> 1) & 1u;
         if (seg_first && !mbar_wait(accempty(ab), abph ^ 1u, abort_flag, p.status)) break;
         if (!mbar_wait(afull(a), aph, abort_flag, p.status)) break;
         if (!mbar_wait(xfull(s), ph, abort_flag, p.status)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + 128u + (uint32_t)ab * 64u;
+        const uint32_t d_tmem = tmem_base + ACC0 + (uint32_t)ab * ACCS;
 #pragma unroll
         for (int j = 0; j < BK / 16; ++j) {
           const uint32_t a_tmem = tmem_base + (uint32_t)a * 64u + (uint32_t)j * 8u;
@@ -329,8 +398,8 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 ? 2 : 1))
     for (int i = 0; i < n_iter; ++i) {
       const int s = i % STAGES;
       const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
-      const int a = i % kABufs;
-      const uint32_t aph = (uint32_t)(i / kABufs) & 1u;
+      const int a = i % AB;
+      const uint32_t aph = (uint32_t)(i / AB) & 1u;
       if (!mbar_wait(full(s), ph, abort_flag, p.status)) break;
       if (!mbar_wait(aempty(a), aph ^ 1u, abort_flag, p.status)) break;
       tc_fence_after();
@@ -379,6 +448,7 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 ? 2 : 1))
     const int quad = warp & 3;
     pdl_wait();
     int seg = 0;
+    uint32_t fix_phase = 0;
     long long g = start;
     while (g < end) {
       const int tile = (int)(g / KB);
@@ -393,7 +463,7 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 ? 2 : 1))
 #pragma unroll
       for (int c = 0; c < BN / 16; ++c) {
         uint32_t rr[16];
-        tmem_ld16(tmem_base + ((uint32_t)(quad * 32) << 16) + 128u + (uint32_t)ab * 64u +
+        tmem_ld16(tmem_base + ((uint32_t)(quad * 32) << 16) + ACC0 + (uint32_t)ab * ACCS +
                       (uint32_t)c * 16u,
                   rr);
         tc_wait_ld();
@@ -404,21 +474,45 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 ? 2 : 1))
       __syncwarp();
       if (lane == 0) mbar_arrive(accempty(ab));
 
-      if (whole) {
-        epilogue_store<BN>(p, tile, er, acc, xch);
-      } else {
-        // partial of this CTA: row er's BN values contiguous, so the finishing CTA reads one
-        // run of BN floats per contributor with 16-byte loads
-        const int slot = (int)blockIdx.x * 2 + (seg == 0 ? 0 : 1);
-        float4* part = reinterpret_cast<float4*>(p.partials + (size_t)slot * BN * BM + er * BN);
+      if constexpr (CS) {
+        // cluster split-K: this CTA's only segment. Every MMA of the CTA has completed, so no
+        // copy or MMA touches the stage ring any more: the partial goes to its start, row er's
+        // BN values contiguous, and the cluster sums them after the role loops.
+        float4* part = reinterpret_cast<float4*>(reinterpret_cast<float*>(sbase) + er * BN);
 #pragma unroll
         for (int j = 0; j < BN / 4; ++j)
           part[j] = make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
+        (void)whole;
+      } else if (whole) {
+        epilogue_store<BN>(p, tile, er, acc, xch);
+      } else {
+        // partial of this CTA, column-major [m][128] and only the M real activation rows: the
+        // stores are coalesced, and each contributor's partial is one contiguous M*512-byte block
+        const int slot = (int)blockIdx.x * 2 + (seg == 0 ? 0 : 1);
+        float* part = p.partials + (size_t)slot * BN * BM + er;
+#pragma unroll
+        for (int m = 0; m < BN; ++m)
+          if (m < p.M) part[m * BM] = acc[m];
+        if (p.epilogue == DSPARK_EPI_RESIDUAL_BF16) {
+          // the finishing CTA reads the residual rows of this tile last: warm L1 with them now,
+          // so that read overlaps the arrival round trip instead of following it
+          const __nv_bfloat16* rp = static_cast<const __nv_bfloat16*>(p.residual) + tile * BM + er;
+#pragma unroll
+          for (int m = 0; m < BN; ++m)
+            if (m < p.M) asm volatile("prefetch.global.L1 [%0];" ::"l"(rp + (size_t)m * p.ldr));
+        }
         asm volatile("bar.sync 1, 128;" ::: "memory");
         const long long c_lo = range_owner(tile_lo, total, G);
         const long long c_hi = range_owner(tile_lo + KB - 1, total, G);
+        const int nctr = (int)(c_hi - c_lo + 1);
+        // contributor c keeps this tile in its partial slot 2c + 1 only if the tile is its second
+        // segment, which only the first contributor's range can make it (ranges are contiguous)
+        const int cj_lo = range_start(c_lo, total, G) >= tile_lo ? 0 : 1;
+        const uint32_t blk = (uint32_t)p.M * BM * 4u;
+        // the stage ring is idle once this CTA's last segment is accumulated (every copy into
+        // it has landed and been consumed), so the finishing CTA can stage the partials there
+        const bool ring_free = seg_end == end && (uint32_t)nctr * blk <= (uint32_t)STAGES * L::kStageBytes;
         if (er == 0) {
-          const int contributors = (int)(c_hi - c_lo + 1);
           // One acq_rel gpu-scope atomic per CTA. Release: the partials of all 128 threads
           // (ordered before it by the barrier; release is cumulative) are visible to whoever
           // reads the final count. Acquire: the last arriver sees every partial.
@@ -427,7 +521,20 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 ? 2 : 1))
                        : "=r"(old)
                        : "l"(p.counters + tile)
                        : "memory");
-          *last_flag = (old == contributors - 1) ? 1 : 0;
+          const bool last = old == nctr - 1;
+          *last_flag = last ? 1 : 0;
+          if (last && ring_free) {
+            // every contributor's block in flight at once: one bulk copy each into the ring
+            fence_proxy_async_global();
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            mbar_arrive_expect_tx(fix_bar, (uint32_t)nctr * blk);
+            for (int ci = 0; ci < nctr; ++ci) {
+              const long long c = c_lo + ci;
+              const int cj = ci == 0 ? cj_lo : 0;
+              bulk_load_g2s(base + (uint32_t)ci * blk, p.partials + ((size_t)c * 2 + cj) * BN * BM,
+                            blk, fix_bar);
+            }
+          }
         }
         asm volatile("bar.sync 1, 128;" ::: "memory");
         const int is_last = *last_flag;
@@ -435,31 +542,41 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 ? 2 : 1))
           float sum[BN];
 #pragma unroll
           for (int m = 0; m < BN; ++m) sum[m] = 0.0f;
-          // U contributors' loads in flight at once; the sum stays in contributor order
-          constexpr int U = BN <= 16 ? 2 : 1;
-          for (long long c = c_lo; c <= c_hi; c += U) {
-            float4 t[U][BN / 4];
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-              if (c + u <= c_hi) {
-                const int cj = (range_start(c + u, total, G) >= tile_lo) ? 0 : 1;
-                const float4* cp = reinterpret_cast<const float4*>(
-                    p.partials + ((size_t)(c + u) * 2 + cj) * BN * BM + er * BN);
-#pragma unroll
-                for (int j = 0; j < BN / 4; ++j) t[u][j] = __ldcg(cp + j);
-              }
+          if (ring_free) {
+            if (!mbar_wait(fix_bar, fix_phase, abort_flag, p.status)) {
+              // no copy may still be writing into shared memory when the CTA leaves
+              volatile int never = 0;
+              mbar_wait(fix_bar, fix_phase, &never, p.status);
             }
+            fix_phase ^= 1u;
+            // contributor order, as in the register path below; four contributors' values are
+            // loaded before they are added so the shared-memory loads overlap
+            const float* st = reinterpret_cast<const float*>(sbase) + er;
+            const int stride = (int)(blk / 4);
+            int ci = 0;
+            for (; ci + 4 <= nctr; ci += 4) {
 #pragma unroll
-            for (int u = 0; u < U; ++u) {
-              if (c + u <= c_hi) {
-#pragma unroll
-                for (int j = 0; j < BN / 4; ++j) {
-                  sum[4 * j] += t[u][j].x;
-                  sum[4 * j + 1] += t[u][j].y;
-                  sum[4 * j + 2] += t[u][j].z;
-                  sum[4 * j + 3] += t[u][j].w;
+              for (int m = 0; m < BN; ++m)
+                if (m < p.M) {
+                  const float* q = st + ci * stride + m * BM;
+                  const float v0 = q[0], v1 = q[stride], v2 = q[2 * stride], v3 = q[3 * stride];
+                  sum[m] = (((sum[m] + v0) + v1) + v2) + v3;
                 }
-              }
+            }
+            for (; ci < nctr; ++ci) {
+#pragma unroll
+              for (int m = 0; m < BN; ++m)
+                if (m < p.M) sum[m] += st[ci * stride + m * BM];
+            }
+          } else {
+            for (long long c = c_lo; c <= c_hi; ++c) {
+              const int cj = c == c_lo ? cj_lo : 0;
+              const float* cp = p.partials + ((size_t)c * 2 + cj) * BN * BM + er;
+              float t[BN];
+#pragma unroll
+              for (int m = 0; m < BN; ++m) t[m] = m < p.M ? __ldcg(cp + m * BM) : 0.0f;
+#pragma unroll
+              for (int m = 0; m < BN; ++m) sum[m] += t[m];
             }
           }
           if (er == 0) p.counters[tile] = 0;
@@ -472,11 +589,50 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 ? 2 : 1))
     }
   }
 
+  if constexpr (CS) {
+    // Every thread of every CTA of the cluster takes both cluster barriers (no early exits
+    // above, and each role loop ends after its bounded waits), so both barriers complete.
+    cluster_sync_all();  // release/acquire: every CTA's partial is visible cluster-wide
+    if (warp >= kConvWarps && warp < kConvWarps + kEpiWarps && !*abort_flag) {
+      // CTA rank r finishes tile rows [r0, r1) for every activation row, summing the csplit
+      // partials in rank order (the same order whichever CTA finishes first)
+      const int t = threadIdx.x - kConvWarps * 32;
+      const int c = p.csplit;
+      const int rank = (int)(blockIdx.x % c);  // == %cluster_ctarank: clusters are (c, 1, 1)
+      const int tile = (int)(blockIdx.x / c);
+      const bool silu = p.epilogue == DSPARK_EPI_SILU_MUL_F16;
+      const int rows = silu ? BM / 2 : BM;
+      const int r0 = rank * rows / c, r1 = (rank + 1) * rows / c;
+      const int nr = r1 - r0;
+      uint32_t peer[8];  // shared::cluster address of each slice's partial
+#pragma unroll
+      for (int q = 0; q < 8; ++q) peer[q] = q < c ? mapa_shared(base, (uint32_t)q) : 0u;
+      auto slice_sum = [&](uint32_t off) {
+        float v[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          if (q < c) v[q] = ld_shared_cluster_f32(peer[q] + off);
+        float sum = 0.0f;
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          if (q < c) sum += v[q];
+        return sum;
+      };
+      for (int o = t; o < nr * p.M; o += kEpiWarps * 32) {
+        const int m = o / nr, row = r0 + (o - m * nr);
+        const float sv = slice_sum((uint32_t)(row * BN + m) * 4u);
+        const float su = silu ? slice_sum((uint32_t)((row + BM / 2) * BN + m) * 4u) : 0.0f;
+        epilogue_one(p, tile, row, m, sv, su);
+      }
+    }
+    cluster_sync_all();  // no CTA leaves while a peer still reads its shared memory
+  }
+
   tc_fence_before();
   __syncthreads();
   if (warp == kProducerWarp) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, kTmemCols);
+    tmem_dealloc(tmem_base, TC);
   }
 }
 
@@ -1120,10 +1276,84 @@ template <>
 struct Cfg<48> { static constexpr int kStages = 5; static constexpr int kCtasPerSm = 1; };
 template <>
 struct Cfg<64> { static constexpr int kStages = 5; static constexpr int kCtasPerSm = 1; };
+// stage ring of the cluster split-K form (one CTA per SM)
+template <int BN>
+struct CfgCs { static constexpr int kStages = BN <= 32 ? 8 : 6; };
+
+// Split mode of the small-M GEMM: 0 stream-K for every shape (default), 1 cluster split-K for
+// shapes with few tiles where one wave of clusters fits. Measured on B200 in a chain of C2 verify
+// GEMMs (us per launch, stream-K vs cluster): q|k|v 12.2 vs 17.6, o 12.3 vs 13.1, down 19.0 vs
+// 25.1. The cluster form runs one CTA per SM, and its CTAs cannot start until the previous
+// kernel's CTAs have left their SM, so it loses more at the launch boundary than it saves in the
+// reduction.
+static int g_split_mode = 0;
+
+// Cluster split-K for GEMMs with few 128-row tiles (q|k|v, o, down at Qwen3 widths): every
+// tile's K is cut into c slices of one cluster, so no single CTA sums ~10 partials at the end.
+// The device keeps about one CTA of a cluster kernel per SM resident, so the cluster form runs
+// one CTA per SM with a deeper stage ring (the same bytes in flight per SM as two CTAs of the
+// stream-K form). Candidates: tiles <= SMs / 2, the largest c <= 8 with tiles * c <= SMs, at
+// least 3/5 of the SMs busy; otherwise stream-K.
+static int pick_csplit(int tiles, int kb, int c_max) {
+  if (g_split_mode != 1) return 0;
+  const int sms = sm_count();
+  if (tiles <= 0 || tiles * 2 > sms) return 0;
+  int c = std::min(std::min(c_max, kb), sms / tiles);
+  if (c < 2 || tiles * c * 5 < sms * 3) return 0;
+  return c;
+}
 
 static long long grid_for(long long total, int ctas_per_sm) {
   const long long g = (long long)sm_count() * ctas_per_sm;
   return std::min<long long>(g, total);
+}
+
+// Max active clusters of c CTAs of the cluster-split kernel (cached per c; a failed query is
+// retried on the next call and meanwhile reads as "does not fit"). -1: query failed.
+template <int BN>
+static int max_clusters(int c) {
+  constexpr int S = CfgCs<BN>::kStages;
+  using L = Smem<BN, S>;
+  static int cache[9] = {0};  // max active clusters + 1
+  if (c < 2 || c > 8) return -1;
+  if (cache[c]) return cache[c] - 1;
+  auto kern_cs = w8a16_tc_kernel<BN, S, true>;
+  if (cudaFuncSetAttribute(kern_cs, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kTotal) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    return -1;
+  }
+  cudaLaunchConfig_t q = {};
+  q.blockDim = dim3(kThreads);
+  q.dynamicSmemBytes = L::kTotal;
+  q.gridDim = dim3((unsigned)(c * 64));
+  cudaLaunchAttribute qa[1];
+  qa[0].id = cudaLaunchAttributeClusterDimension;
+  qa[0].val.clusterDim.x = (unsigned)c;
+  qa[0].val.clusterDim.y = 1;
+  qa[0].val.clusterDim.z = 1;
+  q.attrs = qa;
+  q.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern_cs, &q) != cudaSuccess) {
+    cudaGetLastError();
+    return -1;
+  }
+  cache[c] = n + 1;
+  return n;
+}
+
+// cluster size for this GEMM: pick_csplit's choice if one wave of its clusters is resident
+// at once, else 0 (stream-K)
+template <int BN>
+static int plan_csplit(int tiles, int kb) {
+  for (int c_max = 8; c_max >= 2;) {
+    const int c = pick_csplit(tiles, kb, c_max);
+    if (c < 2) return 0;
+    if (max_clusters<BN>(c) >= tiles) return c;
+    c_max = c - 1;  // fewer, wider slices
+  }
+  return 0;
 }
 
 template <int BN>
@@ -1143,26 +1373,44 @@ static int launch_tc(const void* x, int ldx, const uint8_t* wq, const uint32_t* 
   if ((rc = make_map_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x, (uint64_t)p.K, (uint64_t)p.M,
                         (uint64_t)ldx * 2, 64, BN, CU_TENSOR_MAP_SWIZZLE_128B)))
     return rc;
-  auto kern = w8a16_tc_kernel<BN, S>;
+  constexpr int SC = CfgCs<BN>::kStages;
+  using LC = Smem<BN, SC>;
+  auto kern = w8a16_tc_kernel<BN, S, false>;
+  auto kern_cs = w8a16_tc_kernel<BN, SC, true>;
   static bool configured = false;
   if (!configured) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kTotal) !=
-        cudaSuccess)
-      return set_error(DSPARK_ERR_CUDA, "cudaFuncSetAttribute(smem=%u) failed", L::kTotal);
+            cudaSuccess ||
+        cudaFuncSetAttribute(kern_cs, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)LC::kTotal) !=
+            cudaSuccess)
+      return set_error(DSPARK_ERR_CUDA, "cudaFuncSetAttribute(smem=%u/%u) failed", L::kTotal, LC::kTotal);
     configured = true;
   }
-  const long long grid = grid_for(p.total, Cfg<BN>::kCtasPerSm);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)grid);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = L::kTotal;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tw, tsb, tx, p);
+  p.csplit = plan_csplit<BN>(p.tiles, p.kb);
+  long long grid;
+  if (p.csplit > 1) {
+    grid = (long long)p.tiles * p.csplit;
+    cfg.dynamicSmemBytes = LC::kTotal;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = (unsigned)p.csplit;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.numAttrs = 2;
+  } else {
+    grid = grid_for(p.total, Cfg<BN>::kCtasPerSm);
+  }
+  cfg.gridDim = dim3((unsigned)grid);
+  cudaError_t e = p.csplit > 1 ? cudaLaunchKernelEx(&cfg, kern_cs, tw, tsb, tx, p)
+                               : cudaLaunchKernelEx(&cfg, kern, tw, tsb, tx, p);
   if (e != cudaSuccess)
     return set_error(DSPARK_ERR_LAUNCH, "w8a16 tc launch failed: %s", cudaGetErrorString(e));
   return DSPARK_OK;
@@ -1297,6 +1545,37 @@ extern "C" int dspark_w8a16_gemm(const void* x, int ldx, const uint8_t* wq, cons
                                  int* status, dspark_stream_t stream) {
   return dspark_w8a16_gemm_pf(x, ldx, wq, wsb, M, N, K, y, ldy, residual, ldr, epilogue, workspace,
                               workspace_bytes, nullptr, 0, nullptr, 0, status, stream);
+}
+
+extern "C" int dspark_w8a16_gemm_plan(int M, int N, int K, int* grid, int* cluster,
+                                      int* max_active) {
+  using namespace w8;
+  if (M < 1 || M > 64 || N <= 0 || K <= 0 || N % BM || K % BK || !grid || !cluster)
+    return set_error(DSPARK_ERR_INVALID, "w8a16_gemm_plan: bad arguments");
+  const int tiles = N / BM, kb = K / BK;
+  const int bn = pick_bn(M);
+  const int cps = bn <= 32 ? 2 : 1;
+  int c = 0, mc = 0;
+  const int saved = g_split_mode;
+  g_split_mode = 1;
+  const int c0 = pick_csplit(tiles, kb, 8);  // the cluster size mode 1 would try first
+  g_split_mode = saved;
+  switch (bn) {
+    case 16: c = plan_csplit<16>(tiles, kb); mc = max_clusters<16>(c0); break;
+    case 32: c = plan_csplit<32>(tiles, kb); mc = max_clusters<32>(c0); break;
+    case 48: c = plan_csplit<48>(tiles, kb); mc = max_clusters<48>(c0); break;
+    default: c = plan_csplit<64>(tiles, kb); mc = max_clusters<64>(c0); break;
+  }
+  *cluster = c;
+  *grid = c > 1 ? tiles * c : (int)grid_for((long long)tiles * kb, cps);
+  if (max_active) *max_active = mc;
+  return DSPARK_OK;
+}
+
+extern "C" int dspark_w8a16_gemm_split_mode(int mode) {
+  if (mode < 0 || mode > 1) return set_error(DSPARK_ERR_INVALID, "w8a16_gemm_split_mode: %d", mode);
+  w8::g_split_mode = mode;
+  return DSPARK_OK;
 }
 
 extern "C" size_t dspark_chain_phase_size(void) { return sizeof(dspark_chain_phase); }

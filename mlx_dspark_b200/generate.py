@@ -74,6 +74,24 @@ def eos_token_ids(tokenizer) -> set[int]:
     return ids
 
 
+def capture_graph(fn) -> torch.cuda.CUDAGraph:
+    """Record fn()'s launches into a CUDA graph on a side stream. capture_begin/capture_end
+    directly: the torch.cuda.graph context also empties the caching allocator on entry, which
+    frees every cached block (seconds after a large session is released) and would land inside
+    the first decode round."""
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        g.capture_begin()
+        try:
+            fn()
+        finally:
+            g.capture_end()
+    torch.cuda.current_stream().wait_stream(s)
+    return g
+
+
 def _decode(tokenizer, ids):
     if tokenizer is None or not hasattr(tokenizer, "decode"):
         return ""
@@ -215,14 +233,7 @@ class SpecSession:
     def capture(self) -> None:
         if not self.target.capturable:
             return
-        g = torch.cuda.CUDAGraph()
-        s = torch.cuda.Stream()
-        s.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(s):
-            with torch.cuda.graph(g, stream=s):
-                self.launch_round()
-        torch.cuda.current_stream().wait_stream(s)
-        self.graph = g
+        self.graph = capture_graph(self.launch_round)
         self._graph_versions = self._versions()
 
     def lookup_round(self, pending: int, draft: list[int]) -> list[int]:
@@ -463,14 +474,7 @@ class GreedySession:
     def capture(self):
         if not self.target.capturable:
             return
-        g = torch.cuda.CUDAGraph()
-        s = torch.cuda.Stream()
-        s.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(s):
-            with torch.cuda.graph(g, stream=s):
-                self.launch_step()
-        torch.cuda.current_stream().wait_stream(s)
-        self.graph = g
+        self.graph = capture_graph(self.launch_step)
 
     def step(self, use_graph=True):
         if use_graph and self.graph is not None and self.target.capturable:

@@ -67,6 +67,22 @@ def gemm_workspace_bytes(M: int, N: int, K: int) -> int:
 PREFETCH_LIMIT = 16 << 20  # bytes of the next weights warmed in L2 (16 MB measured best on C2)
 
 
+def gemm_split_mode(mode: int) -> None:
+    """0: stream-K for every GEMM (default); 1: cluster split-K for GEMMs with few tiles.
+    Process-wide; graphs captured earlier keep the mode they were captured with."""
+    _lib.check(_lib.lib().dspark_w8a16_gemm_split_mode(int(mode)), "w8a16_gemm_split_mode")
+
+
+def gemm_plan(M: int, N: int, K: int) -> dict:
+    """How a GEMM of this shape launches under the current split mode: grid size, cluster
+    size (0 = stream-K) and the device's max resident clusters of the preferred size."""
+    import ctypes
+    g, c, mc = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    _lib.check(_lib.lib().dspark_w8a16_gemm_plan(M, N, K, ctypes.byref(g), ctypes.byref(c),
+                                                 ctypes.byref(mc)), "w8a16_gemm_plan")
+    return {"grid": g.value, "cluster": c.value, "max_clusters": mc.value}
+
+
 def gemm(x16: torch.Tensor, w: PackedLinear, y: torch.Tensor, *, epilogue=_lib.EPI_STORE_BF16,
          residual: torch.Tensor | None = None, scratch: Scratch, M: int | None = None,
          prefetch: PackedLinear | None = None) -> torch.Tensor:

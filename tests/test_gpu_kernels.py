@@ -83,7 +83,46 @@ def test_w8a16_gemm_kmap_diagnostic(cuda):
     assert (err <= exp.abs().max() * 2 ** -10 + 1e-6).all(), f"per-k max err {err.tolist()}"
 
 
-@pytest.mark.parametrize("M,H,I", [(9, 512, 1536), (36, 1024, 2048), (1, 256, 384)])
+@pytest.mark.parametrize("M,N,K", [(9, 4096, 4096), (9, 6144, 4096), (9, 4096, 12288),
+                                   (16, 2048, 2048), (32, 4096, 1024), (1, 4096, 4096)])
+def test_gemm_cluster_split_matches_stream_k(cuda, M, N, K):
+    """Stream-K (default) and cluster split-K (split mode 1, for GEMMs with few tiles: q|k|v,
+    o, down) both stay inside the fp16-weight bound, each is deterministic, and they differ only
+    by the fp32 summation order of the split tiles."""
+    qt = _qrand(N, K, seed=M + N + 3 * K)
+    w = pack(qt, device=cuda)
+    x = _x16(M, K, seed=K)
+    ref = x @ qt.dequant().t()
+    bound = (x.abs() @ qt.dequant().abs().t()) * 2.0 ** -10 + 1e-5
+    sc = ops.Scratch(cuda)
+    out = {}
+    assert ops.gemm_plan(M, N, K)["cluster"] == 0  # stream-K by default
+    try:
+        for mode in (0, 1):
+            ops.gemm_split_mode(mode)
+            if mode == 1 and (N, K) in ((4096, 4096), (4096, 12288)) and M <= 32:
+                # the Qwen3-8B o / down shapes take the cluster form on a B200 (148 SMs)
+                assert ops.gemm_plan(M, N, K)["cluster"] > 1, ops.gemm_plan(M, N, K)
+            ys = []
+            for _ in range(2):
+                y = torch.zeros(M, N, dtype=torch.float32, device=cuda)
+                ops.gemm(x.to(torch.float16).to(cuda), w, y, epilogue=EPI_STORE_F32, scratch=sc)
+                ys.append(y)
+            torch.cuda.synchronize()
+            sc.check_status()
+            assert torch.equal(ys[0], ys[1]), f"split mode {mode} not deterministic"
+            err = (ys[0].cpu() - ref).abs()
+            assert (err <= bound).all(), f"mode {mode}: {int((err > bound).sum())} outside bound"
+            out[mode] = ys[0].cpu()
+    finally:
+        ops.gemm_split_mode(0)
+    # the two orders agree to fp32 summation error
+    tol = (x.abs() @ qt.dequant().abs().t()) * 2.0 ** -18 + 1e-7
+    assert ((out[0] - out[1]).abs() <= tol).all()
+
+
+@pytest.mark.parametrize("M,H,I", [(9, 512, 1536), (36, 1024, 2048), (1, 256, 384),
+                                   (9, 4096, 2048)])
 def test_gemm_residual_and_silu_epilogues(cuda, M, H, I):
     sc = ops.Scratch(cuda)
     g, u, d = _qrand(I, H, 1), _qrand(I, H, 2), _qrand(H, I, 3)
