@@ -61,6 +61,9 @@ enum {
 /* library identity */
 int dspark_version(void);
 const char* dspark_last_error(void);
+/* Kernels this thread has launched through the library so far (monotonic; the difference
+ * around a call is what the call launched, e.g. 1 or 2 for dspark_attention). */
+long long dspark_launch_count(void);
 
 /* -------------------------------------------------------------------------------------
  * K1 — W8A16 group-64 dequant GEMM for the small-M verify shape.
@@ -218,18 +221,28 @@ int dspark_qkv_rope_kv_write(const void* qkv, int ldqkv, int B, int T, int Hq, i
                              const dspark_kv_layout* kv, dspark_stream_t stream);
 
 /* -------------------------------------------------------------------------------------
- * K2/K4/K5 — GQA attention of T block queries per row over the paged cache, split-KV with
- * an in-kernel last-arriver combine. Keys of row b are positions [0, kv_len[b] + T).
+ * K2/K4/K5 — GQA attention of T block queries per row over the paged cache, split-KV.
+ * Keys of row b are positions [0, kv_len[b] + T).
  *   causal = 1: query t sees keys j <= kv_len[b] + t   (target verify, mlx-lm mask /
  *               build_batch_mask batch_engine.py:170-178)
  *   causal = 0: every query sees every key              (drafter block attention,
  *               model.py:258-283, dflash_model.py:100-134)
  * q   : bf16 [B*T, Hq*hd]; out: fp16 [B*T, ldo] (bf16-rounded, the o_proj GEMM input)
- * workspace: dspark_attention_workspace_bytes(...) bytes for the split partials. When the
- * context spans more than one page (one page per split, at most max_splits) a second
- * launch merges the partials; with one split the first launch writes the output directly.
+ * workspace: dspark_attention_workspace_bytes(...) bytes for the split partials.
+ * Splits (at most max_splits, at least one page each) are merged in split order in one of
+ * two forms:
+ *   - two launches (default): partials in the workspace, merged by a second kernel; with one
+ *     split the first launch writes the output directly;
+ *   - one launch, cluster form (merge mode 1): the S splits of a (row, kv head) run as one
+ *     thread-block cluster (S a power of two <= 16) and merge through distributed shared
+ *     memory; used when the block table has at most 4 pages per split and B*Hkv clusters are
+ *     resident at once, else the two-launch form. Slower on B200 (clusters cannot start on SMs
+ *     as the previous kernel drains).
  * ------------------------------------------------------------------------------------- */
 size_t dspark_attention_workspace_bytes(int B, int T, int Hq, int Hkv, int hd, int max_splits);
+/* Process-wide choice of the merge form: 0 (default) two launches, 1 cluster form where it
+ * applies (no reference counterpart; for A/B parity tests and measurements). */
+int dspark_attention_merge_mode(int mode);
 int dspark_attention(const void* q, int B, int T, int Hq, const dspark_kv_layout* kv,
                      const int32_t* kv_len, int causal, float scale, void* out, int ldo,
                      int max_splits, void* workspace, size_t workspace_bytes, int* status,

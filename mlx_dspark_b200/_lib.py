@@ -51,6 +51,7 @@ I = c_int
 SIGNATURES = {
     "dspark_version": (I, []),
     "dspark_last_error": (c_char_p, []),
+    "dspark_launch_count": (c_longlong, []),
     "dspark_w8a16_gemm_workspace_bytes": (c_size_t, [I, I, I]),
     "dspark_w8a16_gemm": (I, [P, I, P, P, I, I, I, P, I, P, I, I, P, c_size_t, P, P]),
     "dspark_w8a16_gemm_pf": (I, [P, I, P, P, I, I, I, P, I, P, I, I, P, c_size_t, P, c_size_t, P,
@@ -65,6 +66,7 @@ SIGNATURES = {
     "dspark_qkv_rope_kv_write": (I, [P, I, I, I, I, I, I, P, P, c_float, P, P, P,
                                      POINTER(KvLayout), P]),
     "dspark_attention_workspace_bytes": (c_size_t, [I, I, I, I, I, I]),
+    "dspark_attention_merge_mode": (I, [I]),
     "dspark_attention": (I, [P, I, I, I, POINTER(KvLayout), P, I, c_float, P, I, I, P,
                              c_size_t, P, P]),
     "dspark_accept_workspace_bytes": (c_size_t, [I, I]),
@@ -119,18 +121,16 @@ def check(rc: int, what: str) -> None:
         raise DsparkError(what, rc, msg.decode() if msg else "")
 
 
-# kernel launches issued through call() (graph replays re-run them without Python)
+# kernel launches issued through call() (graph replays re-run them without Python), as
+# counted by the library itself
 LAUNCHES = {"n": 0}
-_KERNELS_PER_CALL = {"dspark_markov_sample_block": lambda a: int(a[4]),
-                     "dspark_markov_sample_block_probs": lambda a: 2 * int(a[4]),
-                     "dspark_draft_override": lambda a: 2,
-                     "dspark_attention": lambda a: 2 if int(a[10]) > 1 else 1}
 
 
 def call(name: str, *args) -> None:
-    check(getattr(lib(), name)(*args), name)
-    f = _KERNELS_PER_CALL.get(name)
-    LAUNCHES["n"] += f(args) if f else 1
+    L = lib()
+    n0 = L.dspark_launch_count()
+    check(getattr(L, name)(*args), name)
+    LAUNCHES["n"] += L.dspark_launch_count() - n0
 
 
 def exported_symbols() -> list[str]:

@@ -21,6 +21,7 @@ namespace dspark {
 
 // ------------------------------------------------------------------------------------------
 // host-side error plumbing (defined in status.cpp)
+void note_launch();  // one more kernel launched by this thread (dspark_launch_count)
 int set_error(int code, const char* fmt, ...);
 int check_launch(const char* what);
 
@@ -298,6 +299,7 @@ inline int launch_pdl(const char* what, K kern, dim3 grid, dim3 block, size_t sm
   cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, args...);
   if (e != cudaSuccess) return set_error(DSPARK_ERR_LAUNCH, "%s: %s", what, cudaGetErrorString(e));
+  note_launch();
   return DSPARK_OK;
 }
 

@@ -841,6 +841,7 @@ int launch(const char* what, const Args& a, int groups, cudaStream_t st) {
   cfg.numAttrs = 2;
   e = cudaLaunchKernelEx(&cfg, kern, a);
   if (e != cudaSuccess) return set_error(DSPARK_ERR_LAUNCH, "%s: %s", what, cudaGetErrorString(e));
+  note_launch();
   return DSPARK_OK;
 }
 

@@ -18,6 +18,10 @@ int set_error(int code, const char* fmt, ...) {
   return code;
 }
 
+// kernels launched by this thread through the library (dspark_launch_count)
+static thread_local long long g_launches = 0;
+void note_launch() { ++g_launches; }
+
 int check_launch(const char* what) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
@@ -31,3 +35,5 @@ int check_launch(const char* what) {
 extern "C" int dspark_version(void) { return 10000; /* 1.0.0 */ }
 
 extern "C" const char* dspark_last_error(void) { return dspark::g_last_error; }
+
+extern "C" long long dspark_launch_count(void) { return dspark::g_launches; }

@@ -1413,6 +1413,7 @@ static int launch_tc(const void* x, int ldx, const uint8_t* wq, const uint32_t* 
                                : cudaLaunchKernelEx(&cfg, kern, tw, tsb, tx, p);
   if (e != cudaSuccess)
     return set_error(DSPARK_ERR_LAUNCH, "w8a16 tc launch failed: %s", cudaGetErrorString(e));
+  note_launch();
   return DSPARK_OK;
 }
 
@@ -1446,6 +1447,7 @@ static int launch_chain(const ChainMaps& maps, const ChainParams& p, cudaStream_
   cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, maps, p);
   if (e != cudaSuccess) return set_error(DSPARK_ERR_LAUNCH, "chain launch failed: %s", cudaGetErrorString(e));
+  note_launch();
   return DSPARK_OK;
 }
 
@@ -1615,7 +1617,7 @@ extern "C" int dspark_run_chain(int M, const dspark_chain_phase* ph, int n, void
   int ng = 0;
   // dependencies: a grid barrier after every GEMM and NORM phase but the last phase; every
   // phase reads what was written before the latest barrier
-  int nbar = 0, last_bar = -1, last_norm = -1;
+  int nbar = 0, last_bar = -1;
   for (int i = 0; i < n; ++i) {
     const dspark_chain_phase& q = ph[i];
     ChainPhase& P = p.ph[i];
@@ -1623,7 +1625,6 @@ extern "C" int dspark_run_chain(int M, const dspark_chain_phase* ph, int n, void
     P.wait_bar = last_bar;
     P.arrive_bar = -1;
     P.local_norm = -1;
-    (void)last_norm;
     if ((q.kind == DSPARK_PHASE_GEMM || q.kind == DSPARK_PHASE_NORM) && i < n - 1) {
       P.arrive_bar = nbar++;
       last_bar = P.arrive_bar;
@@ -1703,5 +1704,7 @@ extern "C" int dspark_w8a16_gemm_simt(const void* x, int ldx, const uint8_t* wq,
   const int blocks = (N * 32 + 255) / 256;
   w8::w8a16_simt_kernel<64><<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __half*>(x), ldx, wq, wsb, p);
-  return check_launch("w8a16_gemm_simt");
+  const int lrc = check_launch("w8a16_gemm_simt");
+  if (lrc == DSPARK_OK) note_launch();
+  return lrc;
 }

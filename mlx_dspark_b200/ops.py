@@ -73,6 +73,12 @@ def gemm_split_mode(mode: int) -> None:
     _lib.check(_lib.lib().dspark_w8a16_gemm_split_mode(int(mode)), "w8a16_gemm_split_mode")
 
 
+def attention_merge_mode(mode: int) -> None:
+    """0: split-KV partials merged by a second launch (default); 1: inside one cluster launch
+    where it applies. Process-wide; captured graphs keep their form."""
+    _lib.check(_lib.lib().dspark_attention_merge_mode(int(mode)), "attention_merge_mode")
+
+
 def gemm_plan(M: int, N: int, K: int) -> dict:
     """How a GEMM of this shape launches under the current split mode: grid size, cluster
     size (0 = stream-K) and the device's max resident clusters of the preferred size."""
