@@ -219,6 +219,19 @@ int dspark_qkv_rope_kv_write(const void* qkv, int ldqkv, int B, int T, int Hq, i
                              const void* q_norm_w, const void* k_norm_w, float eps,
                              const float* inv_freq, const int32_t* pos0, void* q_out,
                              const dspark_kv_layout* kv, dspark_stream_t stream);
+/* The q|k|v projection and the step above in ONE launch: the W8 GEMM of the fused q|k|v
+ * weights (N = (Hq + 2*Hkv)*hd, a multiple of 128) whose epilogue, per finished 128-row tile
+ * (one head at hd 128, two at hd 64), stages the tile's bf16 outputs in shared memory and runs
+ * the same per-head norm + RoPE + q / K/V writes as dspark_qkv_rope_kv_write. Outputs equal
+ * dspark_w8a16_gemm (STORE_BF16) followed by dspark_qkv_rope_kv_write bit for bit; the raw q|k|v
+ * row is never stored. M = B*T rows; workspace and prefetch ranges as dspark_w8a16_gemm_pf. */
+int dspark_w8a16_gemm_qkv_rope(const void* x, int ldx, const uint8_t* wq, const uint32_t* wsb,
+                               int M, int K, int T, int Hq, int Hkv, int hd, const void* q_norm_w,
+                               const void* k_norm_w, float eps, const float* inv_freq,
+                               const int32_t* pos0, void* q_out, const dspark_kv_layout* kv,
+                               void* workspace, size_t workspace_bytes, const void* pf0,
+                               size_t pf0_bytes, const void* pf1, size_t pf1_bytes, int* status,
+                               dspark_stream_t stream);
 
 /* -------------------------------------------------------------------------------------
  * K2/K4/K5 — GQA attention of T block queries per row over the paged cache, split-KV.

@@ -65,6 +65,9 @@ SIGNATURES = {
     "dspark_kv_page_bytes": (c_longlong, [I, I, I, I]),
     "dspark_qkv_rope_kv_write": (I, [P, I, I, I, I, I, I, P, P, c_float, P, P, P,
                                      POINTER(KvLayout), P]),
+    "dspark_w8a16_gemm_qkv_rope": (I, [P, I, P, P, I, I, I, I, I, I, P, P, c_float, P, P, P,
+                                       POINTER(KvLayout), P, c_size_t, P, c_size_t, P, c_size_t,
+                                       P, P]),
     "dspark_attention_workspace_bytes": (c_size_t, [I, I, I, I, I, I]),
     "dspark_attention_merge_mode": (I, [I]),
     "dspark_attention": (I, [P, I, I, I, POINTER(KvLayout), P, I, c_float, P, I, I, P,

@@ -1,5 +1,5 @@
-// Shared by the standalone q/k-norm + RoPE + KV-write kernel (layer_ops.cu) and the rope
-// phase of the fused layer chain (w8a16_gemm.cu).
+// Shared by the standalone q/k-norm + RoPE + KV-write kernel (layer_ops.cu), the q|k|v GEMM's
+// fused RoPE epilogue and the rope phase of the fused layer chain (w8a16_gemm.cu).
 #pragma once
 
 #include "common.cuh"
@@ -25,15 +25,17 @@ __device__ __forceinline__ KvAddr kv_locate(const dspark_kv_layout& kv, int b, i
 // per-head RMSNorm of q and k, non-interleaved RoPE, then q to q_row or K/V into the paged
 // cache (bf16, or affine 8-bit group 64 quantized on write). E = head_dim / 32 contiguous
 // elements per lane; lanes l and l + 16 hold the halves RoPE rotates against each other.
+// `head` points at the head's HD bf16 inputs, in global or shared memory (the W8 GEMM's fused
+// epilogue passes a tile it staged in shared memory).
 template <int E>
-__device__ __forceinline__ void rope_kv_item(const __nv_bfloat16* __restrict__ qkv_row, int Hq,
-                                             int Hkv, int h, const __nv_bfloat16* __restrict__ qnw,
+__device__ __forceinline__ void rope_kv_head(const __nv_bfloat16* head, int Hq, int Hkv, int h,
+                                             const __nv_bfloat16* __restrict__ qnw,
                                              const __nv_bfloat16* __restrict__ knw, float eps,
                                              const float* __restrict__ inv_freq, int b, int pos,
                                              __nv_bfloat16* __restrict__ q_row,
                                              const dspark_kv_layout& kv, int lane) {
   constexpr int HD = E * 32;
-  const __nv_bfloat16* src = qkv_row + (size_t)h * HD + lane * E;
+  const __nv_bfloat16* src = head + lane * E;
   float x[E];
 #pragma unroll
   for (int e = 0; e < E; ++e) x[e] = __bfloat162float(src[e]);
@@ -103,6 +105,18 @@ __device__ __forceinline__ void rope_kv_item(const __nv_bfloat16* __restrict__ q
                ((uint32_t)(*reinterpret_cast<const uint16_t*>(&b16)) << 16);
     }
   }
+}
+
+// head h of a packed [q|k|v] row in global memory
+template <int E>
+__device__ __forceinline__ void rope_kv_item(const __nv_bfloat16* __restrict__ qkv_row, int Hq,
+                                             int Hkv, int h, const __nv_bfloat16* __restrict__ qnw,
+                                             const __nv_bfloat16* __restrict__ knw, float eps,
+                                             const float* __restrict__ inv_freq, int b, int pos,
+                                             __nv_bfloat16* __restrict__ q_row,
+                                             const dspark_kv_layout& kv, int lane) {
+  rope_kv_head<E>(qkv_row + (size_t)h * (E * 32), Hq, Hkv, h, qnw, knw, eps, inv_freq, b, pos,
+                  q_row, kv, lane);
 }
 
 }  // namespace dspark

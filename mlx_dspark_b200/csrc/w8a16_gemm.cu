@@ -53,6 +53,19 @@ constexpr uint32_t kSBBytes = 2 * BM * 4;  // 1 KB
 constexpr int kMaxTiles = 16384;
 constexpr size_t kCounterBytes = kMaxTiles * sizeof(int);
 
+// Fused q|k|v epilogue (dspark_w8a16_gemm_qkv_rope): per-head RMSNorm of q and k, RoPE, q to
+// q_out and K/V into the paged cache, instead of storing the raw q|k|v row.
+struct RopeEpi {
+  const __nv_bfloat16* qnw;
+  const __nv_bfloat16* knw;
+  const float* inv_freq;
+  const int32_t* pos0;  // [B] position of each batch row's first token
+  __nv_bfloat16* q_out; // [M, Hq*hd]
+  dspark_kv_layout kv;
+  float eps;
+  int T, Hq, Hkv, hd;
+};
+
 struct Params {
   int M, N, K;
   int tiles;  // N / 128
@@ -69,6 +82,7 @@ struct Params {
   // of a tile form one thread-block cluster and sum their partials through distributed shared
   // memory. 0: stream-K over the whole grid.
   int csplit;
+  RopeEpi rope;
   // L2 prefetch of the next kernel's operands: CTA b warms bytes [b*chunk, (b+1)*chunk) of each
   // range after issuing its last load (16-byte aligned, sizes multiples of 16)
   const char* pf_ptr[2];
@@ -187,6 +201,36 @@ __device__ __forceinline__ void epilogue_one(const Params& p, int tile, int row,
   }
 }
 
+// The fused q|k|v epilogue of a finished tile: stage the tile's bf16 outputs (the values the
+// separate q|k|v GEMM would store) in shared memory as [m][128], then one warp per (token, head
+// in the tile) runs the same norm + RoPE + KV write as the standalone kernel. The staging fits
+// the exchange buffer: BN x 128 bf16 = 64 x BN fp32.
+template <int BN>
+__device__ __forceinline__ void rope_epilogue(const Params& p, int tile, int er, const float* acc,
+                                              float* xch) {
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(xch);
+#pragma unroll
+  for (int m = 0; m < BN; ++m)
+    if (m < p.M) xs[m * BM + er] = __float2bfloat16_rn(acc[m]);
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+  const RopeEpi& r = p.rope;
+  const int warp = er >> 5, lane = er & 31;
+  const int hpt = BM / r.hd;  // heads per tile
+  for (int it = warp; it < p.M * hpt; it += kEpiWarps) {
+    const int m = it / hpt, j = it - m * hpt;
+    const int h = tile * hpt + j;
+    const int b = m / r.T;
+    const int pos = r.pos0[b] + (m - b * r.T);
+    const __nv_bfloat16* head = xs + m * BM + j * r.hd;
+    __nv_bfloat16* q_row = r.q_out + (size_t)m * r.Hq * r.hd;
+    if (r.hd == 128)
+      rope_kv_head<4>(head, r.Hq, r.Hkv, h, r.qnw, r.knw, r.eps, r.inv_freq, b, pos, q_row, r.kv, lane);
+    else
+      rope_kv_head<2>(head, r.Hq, r.Hkv, h, r.qnw, r.knw, r.eps, r.inv_freq, b, pos, q_row, r.kv, lane);
+  }
+  asm volatile("bar.sync 1, 128;" ::: "memory");  // xch is reused by this CTA's next tile
+}
+
 template <int BN, int STAGES>
 struct Smem {
   static constexpr uint32_t kXBytes = 2u * BN * 128u;
@@ -196,7 +240,7 @@ struct Smem {
   static constexpr uint32_t kTotal = 1024 + STAGES * kStageBytes + kXchBytes + kBarBytes;
 };
 
-template <int BN, int STAGES, bool CS>
+template <int BN, int STAGES, bool CS, bool ROPE>
 __global__ void __launch_bounds__(kThreads, (BN <= 32 && !CS ? 2 : 1))
     w8a16_tc_kernel(const __grid_constant__ CUtensorMap tm_w,
                     const __grid_constant__ CUtensorMap tm_sb,
@@ -484,7 +528,10 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 && !CS ? 2 : 1))
           part[j] = make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
         (void)whole;
       } else if (whole) {
-        epilogue_store<BN>(p, tile, er, acc, xch);
+        if constexpr (ROPE)
+          rope_epilogue<BN>(p, tile, er, acc, xch);
+        else
+          epilogue_store<BN>(p, tile, er, acc, xch);
       } else {
         // partial of this CTA, column-major [m][128] and only the M real activation rows: the
         // stores are coalesced, and each contributor's partial is one contiguous M*512-byte block
@@ -580,7 +627,10 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 && !CS ? 2 : 1))
             }
           }
           if (er == 0) p.counters[tile] = 0;
-          epilogue_store<BN>(p, tile, er, sum, xch);
+          if constexpr (ROPE)
+            rope_epilogue<BN>(p, tile, er, sum, xch);
+          else
+            epilogue_store<BN>(p, tile, er, sum, xch);
         }
         asm volatile("bar.sync 1, 128;" ::: "memory");
       }
@@ -1317,7 +1367,7 @@ static int max_clusters(int c) {
   static int cache[9] = {0};  // max active clusters + 1
   if (c < 2 || c > 8) return -1;
   if (cache[c]) return cache[c] - 1;
-  auto kern_cs = w8a16_tc_kernel<BN, S, true>;
+  auto kern_cs = w8a16_tc_kernel<BN, S, true, false>;
   if (cudaFuncSetAttribute(kern_cs, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kTotal) !=
       cudaSuccess) {
     cudaGetLastError();
@@ -1356,7 +1406,7 @@ static int plan_csplit(int tiles, int kb) {
   return 0;
 }
 
-template <int BN>
+template <int BN, bool ROPE = false>
 static int launch_tc(const void* x, int ldx, const uint8_t* wq, const uint32_t* wsb, Params p,
                      cudaStream_t st) {
   constexpr int S = Cfg<BN>::kStages;
@@ -1375,8 +1425,8 @@ static int launch_tc(const void* x, int ldx, const uint8_t* wq, const uint32_t* 
     return rc;
   constexpr int SC = CfgCs<BN>::kStages;
   using LC = Smem<BN, SC>;
-  auto kern = w8a16_tc_kernel<BN, S, false>;
-  auto kern_cs = w8a16_tc_kernel<BN, SC, true>;
+  auto kern = w8a16_tc_kernel<BN, S, false, ROPE>;
+  auto kern_cs = w8a16_tc_kernel<BN, SC, true, false>;
   static bool configured = false;
   if (!configured) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kTotal) !=
@@ -1395,7 +1445,7 @@ static int launch_tc(const void* x, int ldx, const uint8_t* wq, const uint32_t* 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  p.csplit = plan_csplit<BN>(p.tiles, p.kb);
+  p.csplit = ROPE ? 0 : plan_csplit<BN>(p.tiles, p.kb);  // the fused epilogue is stream-K only
   long long grid;
   if (p.csplit > 1) {
     grid = (long long)p.tiles * p.csplit;
@@ -1501,13 +1551,13 @@ static int gemm_common_checks(const void* x, int ldx, const uint8_t* wq, const u
   return DSPARK_OK;
 }
 
-extern "C" int dspark_w8a16_gemm_pf(const void* x, int ldx, const uint8_t* wq, const uint32_t* wsb,
-                                    int M, int N, int K, void* y, int ldy, const void* residual,
-                                    int ldr, int epilogue, void* workspace, size_t workspace_bytes,
-                                    const void* pf0, size_t pf0_bytes, const void* pf1,
-                                    size_t pf1_bytes, int* status, dspark_stream_t stream) {
-  int rc = gemm_common_checks(x, ldx, wq, wsb, M, N, K, y, epilogue, residual);
-  if (rc) return rc;
+// Shared launch path of the W8 GEMM entry points: rope != nullptr selects the fused q|k|v
+// epilogue (y unused).
+static int gemm_launch(const void* x, int ldx, const uint8_t* wq, const uint32_t* wsb, int M, int N,
+                       int K, void* y, int ldy, const void* residual, int ldr, int epilogue,
+                       void* workspace, size_t workspace_bytes, const void* pf0, size_t pf0_bytes,
+                       const void* pf1, size_t pf1_bytes, const w8::RopeEpi* rope, int* status,
+                       dspark_stream_t stream) {
   const size_t need = w8::ws_bytes(M, N, K);
   if (!workspace || workspace_bytes < need)
     return set_error(DSPARK_ERR_WORKSPACE, "w8a16_gemm: workspace %zu < %zu bytes", workspace_bytes, need);
@@ -1524,6 +1574,7 @@ extern "C" int dspark_w8a16_gemm_pf(const void* x, int ldx, const uint8_t* wq, c
   p.counters = static_cast<int*>(workspace);
   p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + counters);
   p.status = status;
+  if (rope) p.rope = *rope;
   const void* pf[2] = {pf0, pf1};
   const size_t pfb[2] = {pf0_bytes, pf1_bytes};
   for (int r = 0; r < 2; ++r) {
@@ -1533,12 +1584,66 @@ extern "C" int dspark_w8a16_gemm_pf(const void* x, int ldx, const uint8_t* wq, c
     p.pf_bytes[r] = pf[r] ? (unsigned long long)(pfb[r] & ~(size_t)15) : 0ull;
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (rope) {
+    switch (w8::pick_bn(M)) {
+      case 16: return w8::launch_tc<16, true>(x, ldx, wq, wsb, p, st);
+      case 32: return w8::launch_tc<32, true>(x, ldx, wq, wsb, p, st);
+      case 48: return w8::launch_tc<48, true>(x, ldx, wq, wsb, p, st);
+      default: return w8::launch_tc<64, true>(x, ldx, wq, wsb, p, st);
+    }
+  }
   switch (w8::pick_bn(M)) {
     case 16: return w8::launch_tc<16>(x, ldx, wq, wsb, p, st);
     case 32: return w8::launch_tc<32>(x, ldx, wq, wsb, p, st);
     case 48: return w8::launch_tc<48>(x, ldx, wq, wsb, p, st);
     default: return w8::launch_tc<64>(x, ldx, wq, wsb, p, st);
   }
+}
+
+extern "C" int dspark_w8a16_gemm_pf(const void* x, int ldx, const uint8_t* wq, const uint32_t* wsb,
+                                    int M, int N, int K, void* y, int ldy, const void* residual,
+                                    int ldr, int epilogue, void* workspace, size_t workspace_bytes,
+                                    const void* pf0, size_t pf0_bytes, const void* pf1,
+                                    size_t pf1_bytes, int* status, dspark_stream_t stream) {
+  int rc = gemm_common_checks(x, ldx, wq, wsb, M, N, K, y, epilogue, residual);
+  if (rc) return rc;
+  return gemm_launch(x, ldx, wq, wsb, M, N, K, y, ldy, residual, ldr, epilogue, workspace,
+                     workspace_bytes, pf0, pf0_bytes, pf1, pf1_bytes, nullptr, status, stream);
+}
+
+extern "C" int dspark_w8a16_gemm_qkv_rope(const void* x, int ldx, const uint8_t* wq,
+                                          const uint32_t* wsb, int M, int K, int T, int Hq,
+                                          int Hkv, int hd, const void* q_norm_w,
+                                          const void* k_norm_w, float eps, const float* inv_freq,
+                                          const int32_t* pos0, void* q_out,
+                                          const dspark_kv_layout* kv, void* workspace,
+                                          size_t workspace_bytes, const void* pf0,
+                                          size_t pf0_bytes, const void* pf1, size_t pf1_bytes,
+                                          int* status, dspark_stream_t stream) {
+  if (hd != 64 && hd != 128)
+    return set_error(DSPARK_ERR_UNSUPPORTED, "w8a16_gemm_qkv_rope: head_dim %d", hd);
+  if (T <= 0 || M % T || Hkv <= 0 || Hq < 0 || !k_norm_w || !inv_freq || !pos0 || !kv ||
+      !kv->pool || !kv->block_table || (Hq > 0 && (!q_out || !q_norm_w)))
+    return set_error(DSPARK_ERR_INVALID, "w8a16_gemm_qkv_rope: bad arguments");
+  if (kv->head_dim != hd || kv->num_kv_heads != Hkv || kv->page_size <= 0 ||
+      kv->page_bytes != dspark_kv_page_bytes(kv->page_size, Hkv, hd, kv->kv8))
+    return set_error(DSPARK_ERR_INVALID, "w8a16_gemm_qkv_rope: kv layout does not match");
+  const int N = (Hq + 2 * Hkv) * hd;
+  // the row output pointer only feeds the shared checks: the fused epilogue writes q_out / cache
+  int rc = gemm_common_checks(x, ldx, wq, wsb, M, N, K, q_out ? q_out : kv->pool,
+                              DSPARK_EPI_STORE_BF16, nullptr);
+  if (rc) return rc;
+  w8::RopeEpi r{};
+  r.qnw = static_cast<const __nv_bfloat16*>(q_norm_w);
+  r.knw = static_cast<const __nv_bfloat16*>(k_norm_w);
+  r.inv_freq = inv_freq;
+  r.pos0 = pos0;
+  r.q_out = static_cast<__nv_bfloat16*>(q_out);
+  r.kv = *kv;
+  r.eps = eps;
+  r.T = T; r.Hq = Hq; r.Hkv = Hkv; r.hd = hd;
+  return gemm_launch(x, ldx, wq, wsb, M, N, K, nullptr, 0, nullptr, 0, -1, workspace,
+                     workspace_bytes, pf0, pf0_bytes, pf1, pf1_bytes, &r, status, stream);
 }
 
 extern "C" int dspark_w8a16_gemm(const void* x, int ldx, const uint8_t* wq, const uint32_t* wsb,

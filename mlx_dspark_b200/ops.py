@@ -115,6 +115,29 @@ def gemm(x16: torch.Tensor, w: PackedLinear, y: torch.Tensor, *, epilogue=_lib.E
     return y
 
 
+def gemm_qkv_rope(x16: torch.Tensor, w: PackedLinear, *, T: int, Hq: int, Hkv: int, hd: int,
+                  q_norm: torch.Tensor | None, k_norm: torch.Tensor, eps: float,
+                  inv_freq: torch.Tensor, pos0: torch.Tensor, q_out: torch.Tensor | None,
+                  kv: KvLayout, scratch: Scratch, M: int | None = None,
+                  prefetch: PackedLinear | None = None) -> None:
+    """The q|k|v GEMM with the per-head norm + RoPE + q / paged K/V writes in its epilogue
+    (one launch; equals gemm(STORE_BF16) + qkv_rope_kv_write)."""
+    _require_cuda(x16)
+    M = x16.shape[0] if M is None else M
+    K = w.K
+    assert x16.dtype == torch.float16 and x16.shape[-1] >= K and w.N == (Hq + 2 * Hkv) * hd
+    ws = scratch.get("gemm", gemm_workspace_bytes(M, w.N, K))
+    pq = psb = None
+    qb = sbb = 0
+    if prefetch is not None and PREFETCH_LIMIT > 0:
+        pq, psb = prefetch.q, prefetch.sb
+        qb = min(prefetch.q.numel(), PREFETCH_LIMIT)
+        sbb = min(prefetch.sb.numel() * 4, PREFETCH_LIMIT // 8)
+    call("dspark_w8a16_gemm_qkv_rope", _p(x16), x16.stride(0), _p(w.q), _p(w.sb), M, K, T, Hq,
+         Hkv, hd, _p(q_norm), _p(k_norm), float(eps), _p(inv_freq), _p(pos0), _p(q_out), kv,
+         _p(ws), ws.numel(), _p(pq), qb, _p(psb), sbb, _p(scratch.status), _stream())
+
+
 def gemm_simt(x16, w: PackedLinear, y, *, epilogue=_lib.EPI_STORE_BF16, residual=None, M=None):
     M = x16.shape[0] if M is None else M
     call("dspark_w8a16_gemm_simt", _p(x16), x16.stride(0), _p(w.q), _p(w.sb), M, w.N, w.K, _p(y),

@@ -142,6 +142,9 @@ class Target:
     # B200 the chain's software grid barriers and its row-split norm cost more than the PDL
     # kernel boundaries they replace (C2 verify 4.99-5.87 ms chained vs 4.18 ms separate).
     use_chain = False
+    # the q|k|v GEMM runs the per-head norm + RoPE + KV write in its epilogue (one launch
+    # instead of two; bit-identical outputs)
+    fuse_qkv_rope = True
 
     def forward(self, buf: Buffers, state: CacheState, tap=(), *, splits: int | None = None,
                 with_logits: bool = True) -> None:
@@ -161,11 +164,7 @@ class Target:
             # each GEMM warms L2 with the next GEMM's weights (the head after the last layer)
             nxt = self.layers[l + 1].qkv if l + 1 < n_layers else (self.head if with_logits else None)
             ops.rmsnorm(buf.h, L.input_ln, c.rms_norm_eps, y16=buf.xn16, M=M)
-            ops.gemm(buf.xn16, L.qkv, buf.qkv, epilogue=EPI_STORE_BF16, scratch=sc, M=M,
-                     prefetch=L.o)
-            ops.qkv_rope_kv_write(buf.qkv, B, T, c.num_attention_heads, c.num_key_value_heads,
-                                  c.head_dim, L.q_norm, L.k_norm, c.rms_norm_eps, self.inv_freq,
-                                  state.seq_len, buf.q, kv)
+            self._qkv_rope(buf, L, kv, state, B, T, M)
             ops.attention(buf.q, B, T, c.num_attention_heads, kv, state.seq_len, True,
                           self.scale, buf.attn16, splits, sc)
             ops.gemm(buf.attn16, L.o, buf.h, epilogue=EPI_RESIDUAL_BF16, residual=buf.h,
@@ -181,6 +180,22 @@ class Target:
         if with_logits:
             ops.rmsnorm(buf.h, self.norm, c.rms_norm_eps, y16=buf.xn16, M=M)
             ops.gemm(buf.xn16, self.head, buf.logits, epilogue=EPI_STORE_BF16, scratch=sc, M=M)
+
+    def _qkv_rope(self, buf: Buffers, L, kv, state: CacheState, B: int, T: int, M: int) -> None:
+        """q|k|v projection of buf.xn16, per-head q/k norm + RoPE at state.seq_len, q into
+        buf.q and K/V into the layer's paged cache."""
+        c, sc = self.cfg, self.scratch
+        if self.fuse_qkv_rope:
+            ops.gemm_qkv_rope(buf.xn16, L.qkv, T=T, Hq=c.num_attention_heads,
+                              Hkv=c.num_key_value_heads, hd=c.head_dim, q_norm=L.q_norm,
+                              k_norm=L.k_norm, eps=c.rms_norm_eps, inv_freq=self.inv_freq,
+                              pos0=state.seq_len, q_out=buf.q, kv=kv, scratch=sc, M=M,
+                              prefetch=L.o)
+            return
+        ops.gemm(buf.xn16, L.qkv, buf.qkv, epilogue=EPI_STORE_BF16, scratch=sc, M=M, prefetch=L.o)
+        ops.qkv_rope_kv_write(buf.qkv, B, T, c.num_attention_heads, c.num_key_value_heads,
+                              c.head_dim, L.q_norm, L.k_norm, c.rms_norm_eps, self.inv_freq,
+                              state.seq_len, buf.q, kv)
 
     def _forward_chain(self, buf: Buffers, state: CacheState, tap=(), *,
                        splits: int | None = None, with_logits: bool = True) -> None:

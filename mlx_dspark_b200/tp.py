@@ -143,10 +143,7 @@ class TPTarget(Target):
         for l, L in enumerate(self.layers):
             kv = state.layout(l)
             ops.rmsnorm(buf.h, L.input_ln, c.rms_norm_eps, y16=buf.xn16, M=M)
-            ops.gemm(buf.xn16, L.qkv, buf.qkv, epilogue=EPI_STORE_BF16, scratch=sc, M=M)
-            ops.qkv_rope_kv_write(buf.qkv, B, T, c.num_attention_heads, c.num_key_value_heads,
-                                  c.head_dim, L.q_norm, L.k_norm, c.rms_norm_eps, self.inv_freq,
-                                  state.seq_len, buf.q, kv)
+            self._qkv_rope(buf, L, kv, state, B, T, M)
             ops.attention(buf.q, B, T, c.num_attention_heads, kv, state.seq_len, True,
                           self.scale, buf.attn16, splits, sc)
             ops.gemm(buf.attn16, L.o, part, epilogue=EPI_STORE_F32, scratch=sc, M=M)

@@ -244,6 +244,47 @@ def test_qkv_rope_kv_write(cuda, hd, kv8):
             assert torch.equal(Vn, v)
 
 
+@pytest.mark.parametrize("hd,kv8,B,T,Hq,Hkv", [(128, False, 1, 9, 32, 8), (128, True, 2, 5, 8, 2),
+                                             (64, False, 3, 1, 8, 2), (64, True, 1, 16, 6, 2),
+                                             (128, False, 4, 9, 16, 4)])
+def test_gemm_qkv_rope_fused_matches_separate(cuda, hd, kv8, B, T, Hq, Hkv):
+    """The q|k|v GEMM with the RoPE/KV-write epilogue equals the GEMM followed by the
+    standalone RoPE/KV-write kernel bit for bit (q rows and every written cache byte)."""
+    H, eps = 1024, 1e-6
+    M = B * T
+    N = (Hq + 2 * Hkv) * hd
+    qt = _qrand(N, H, seed=N + T)
+    w = pack(qt, device=cuda)
+    x = _x16(M, H, seed=7 + B).to(torch.float16).to(cuda)
+    qn = (1 + 0.1 * torch.randn(hd, generator=torch.Generator().manual_seed(1))).to(torch.bfloat16).to(cuda)
+    kn = (1 + 0.1 * torch.randn(hd, generator=torch.Generator().manual_seed(2))).to(torch.bfloat16).to(cuda)
+    freqs = oq.inv_freq(hd, 1e6).to(cuda)
+    pos0 = torch.tensor([60, 3, 127, 0][:B], dtype=torch.int32)  # page-straddling rows
+    outs = []
+    for fused in (False, True):
+        pool, st = _pool_and_state(cuda, Hkv, hd, kv8, B, 256)
+        st.seq_len.copy_(pos0.to(cuda))
+        sc = ops.Scratch(cuda)
+        q_out = torch.zeros(M, Hq * hd, dtype=torch.bfloat16, device=cuda)
+        if fused:
+            ops.gemm_qkv_rope(x, w, T=T, Hq=Hq, Hkv=Hkv, hd=hd, q_norm=qn, k_norm=kn, eps=eps,
+                              inv_freq=freqs, pos0=st.seq_len, q_out=q_out, kv=st.layout(0),
+                              scratch=sc, M=M)
+        else:
+            qkv = torch.zeros(M, N, dtype=torch.bfloat16, device=cuda)
+            ops.gemm(x, w, qkv, epilogue=EPI_STORE_BF16, scratch=sc, M=M)
+            ops.qkv_rope_kv_write(qkv, B, T, Hq, Hkv, hd, qn, kn, eps, freqs, st.seq_len, q_out,
+                                  st.layout(0))
+        torch.cuda.synchronize()
+        sc.check_status()
+        pages = torch.stack([pool.data[0][int(st.block_table[b, p])]
+                             for b in range(B) for p in range(st.max_pages)])
+        outs.append((q_out.cpu(), pages.cpu()))
+    assert torch.equal(outs[0][0], outs[1][0]), "q rows differ"
+    assert torch.equal(outs[0][1], outs[1][1]), "cache pages differ"
+    assert outs[1][0].float().abs().sum() > 0
+
+
 @pytest.mark.parametrize("hd,kv8,causal,T,lens", [
     (128, False, True, 9, [1535, 7]),
     (128, False, False, 8, [200, 0]),
