@@ -192,20 +192,28 @@ def gemm_roofline(target, M, reps=5):
     logits = torch.zeros(M, c.vocab_size, dtype=torch.bfloat16, device=dev)
     sc = target.scratch
     H, I = c.hidden_size, c.intermediate_size
+    # the residual stream the norm-fused GEMMs read, and its per-tile row sums of squares
+    hin = torch.randn(M, H, device=dev).to(torch.bfloat16)
+    ss = torch.full((H // 128, M), 128.0, dtype=torch.float32, device=dev)
+    eps = c.rms_norm_eps
 
     def one_pass():
-        # the verify forward's GEMM sequence, each warming L2 with the next one's weights
+        # the verify forward's GEMM sequence and variants (input RMSNorm fused into q|k|v,
+        # gate|up and the head; row sums of squares out of o and down), each warming L2 with the
+        # next one's weights
         n = len(target.layers)
         for l, L in enumerate(target.layers):
             nxt = target.layers[l + 1].qkv if l + 1 < n else target.head
-            ops.gemm(x[:, :H], L.qkv, qkv, epilogue=EPI_STORE_BF16, scratch=sc, M=M, prefetch=L.o)
+            ops.gemm(hin, L.qkv, qkv, epilogue=EPI_STORE_BF16, scratch=sc, M=M, prefetch=L.o,
+                     norm=ops.RowNorm(L.input_ln, eps, ss))
             ops.gemm(x[:, :c.q_dim], L.o, h, epilogue=EPI_RESIDUAL_BF16, residual=h, scratch=sc,
-                     M=M, prefetch=L.gu)
-            ops.gemm(x[:, :H], L.gu, act, epilogue=EPI_SILU_MUL_F16, scratch=sc, M=M,
-                     prefetch=L.down)
+                     M=M, prefetch=L.gu, sumsq_out=ss)
+            ops.gemm(hin, L.gu, act, epilogue=EPI_SILU_MUL_F16, scratch=sc, M=M,
+                     prefetch=L.down, norm=ops.RowNorm(L.post_ln, eps, ss))
             ops.gemm(x[:, :I], L.down, h, epilogue=EPI_RESIDUAL_BF16, residual=h, scratch=sc, M=M,
-                     prefetch=nxt)
-        ops.gemm(x[:, :H], target.head, logits, epilogue=EPI_STORE_BF16, scratch=sc, M=M)
+                     prefetch=nxt, sumsq_out=ss)
+        ops.gemm(hin, target.head, logits, epilogue=EPI_STORE_BF16, scratch=sc, M=M,
+                 norm=ops.RowNorm(target.norm, eps, ss))
 
     wbytes = sum(L.qkv.nbytes() + L.o.nbytes() + L.gu.nbytes() + L.down.nbytes()
                  for L in target.layers) + target.head.nbytes()

@@ -95,6 +95,32 @@ int dspark_w8a16_gemm_pf(const void* x, int ldx, const uint8_t* wq, const uint32
                          int epilogue, void* workspace, size_t workspace_bytes, const void* pf0,
                          size_t pf0_bytes, const void* pf1, size_t pf1_bytes, int* status,
                          dspark_stream_t stream);
+/* Options of dspark_w8a16_gemm_ex (zero-initialise; NULL pointers switch a feature off).
+ *   prefetch[2], prefetch_bytes[2]: as dspark_w8a16_gemm_pf.
+ *   row_sumsq (RESIDUAL_BF16 epilogue only): fp32 [N/128, M] output; entry (t, m) is the sum of
+ *     the squares of the bf16 outputs y[m, 128t .. 128t+127] this call writes, summed in a fixed
+ *     order — the pieces of the next RMSNorm of the residual stream.
+ *   norm_w, norm_sumsq, norm_tiles, norm_eps: fuse the RMSNorm of the GEMM input (mlx.fast.rms_norm,
+ *     the input/post-attention/final norms of the Qwen3 layers). x is then the bf16 residual stream
+ *     [M, K] itself; the GEMM consumes bf16(x[m,k] * r[m] * w[k]) (as dspark_rmsnorm's output)
+ *     with r[m] = rsqrt(sum_t norm_sumsq[t, m] / K + eps) from the row_sumsq of the GEMM that
+ *     wrote x (norm_tiles = its N/128). The only difference from dspark_rmsnorm + this GEMM is the
+ *     fp32 summation order of the squares. */
+typedef struct dspark_gemm_opts {
+  const void* prefetch[2];
+  size_t prefetch_bytes[2];
+  float* row_sumsq;
+  const float* norm_sumsq;
+  const void* norm_w;
+  int norm_tiles;
+  float norm_eps;
+} dspark_gemm_opts;
+int dspark_w8a16_gemm_ex(const void* x, int ldx, const uint8_t* wq, const uint32_t* wsb, int M,
+                         int N, int K, void* y, int ldy, const void* residual, int ldr,
+                         int epilogue, const dspark_gemm_opts* opts, void* workspace,
+                         size_t workspace_bytes, int* status, dspark_stream_t stream);
+size_t dspark_gemm_opts_size(void); /* sizeof(dspark_gemm_opts), for bindings to check */
+
 /* How the K dimension is split across CTAs (process-wide; no reference counterpart):
  *   0 (default) — stream-K for every GEMM: equal contiguous ranges of (tile, k-block) units,
  *                 split tiles finished by the last CTA to arrive, in CTA order;
@@ -224,14 +250,14 @@ int dspark_qkv_rope_kv_write(const void* qkv, int ldqkv, int B, int T, int Hq, i
  * (one head at hd 128, two at hd 64), stages the tile's bf16 outputs in shared memory and runs
  * the same per-head norm + RoPE + q / K/V writes as dspark_qkv_rope_kv_write. Outputs equal
  * dspark_w8a16_gemm (STORE_BF16) followed by dspark_qkv_rope_kv_write bit for bit; the raw q|k|v
- * row is never stored. M = B*T rows; workspace and prefetch ranges as dspark_w8a16_gemm_pf. */
+ * row is never stored. M = B*T rows; workspace as dspark_w8a16_gemm; opts as dspark_w8a16_gemm_ex
+ * (its input norm is the layer's input RMSNorm; row_sumsq must be NULL). */
 int dspark_w8a16_gemm_qkv_rope(const void* x, int ldx, const uint8_t* wq, const uint32_t* wsb,
                                int M, int K, int T, int Hq, int Hkv, int hd, const void* q_norm_w,
                                const void* k_norm_w, float eps, const float* inv_freq,
                                const int32_t* pos0, void* q_out, const dspark_kv_layout* kv,
-                               void* workspace, size_t workspace_bytes, const void* pf0,
-                               size_t pf0_bytes, const void* pf1, size_t pf1_bytes, int* status,
-                               dspark_stream_t stream);
+                               const dspark_gemm_opts* opts, void* workspace,
+                               size_t workspace_bytes, int* status, dspark_stream_t stream);
 
 /* -------------------------------------------------------------------------------------
  * K2/K4/K5 — GQA attention of T block queries per row over the paged cache, split-KV.

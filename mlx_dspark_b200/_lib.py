@@ -47,6 +47,13 @@ PHASE_GEMM, PHASE_NORM, PHASE_ROPE_KV, PHASE_COPY_F16 = 0, 1, 2, 3
 
 P = c_void_p
 I = c_int
+class GemmOpts(ctypes.Structure):
+    """dspark_gemm_opts (include/dspark_b200.h)."""
+    _fields_ = [("prefetch", c_void_p * 2), ("prefetch_bytes", c_size_t * 2),
+                ("row_sumsq", c_void_p), ("norm_sumsq", c_void_p), ("norm_w", c_void_p),
+                ("norm_tiles", c_int), ("norm_eps", c_float)]
+
+
 # name -> (restype, argtypes); mirrors include/dspark_b200.h
 SIGNATURES = {
     "dspark_version": (I, []),
@@ -66,8 +73,10 @@ SIGNATURES = {
     "dspark_qkv_rope_kv_write": (I, [P, I, I, I, I, I, I, P, P, c_float, P, P, P,
                                      POINTER(KvLayout), P]),
     "dspark_w8a16_gemm_qkv_rope": (I, [P, I, P, P, I, I, I, I, I, I, P, P, c_float, P, P, P,
-                                       POINTER(KvLayout), P, c_size_t, P, c_size_t, P, c_size_t,
-                                       P, P]),
+                                       POINTER(KvLayout), POINTER(GemmOpts), P, c_size_t, P, P]),
+    "dspark_w8a16_gemm_ex": (I, [P, I, P, P, I, I, I, P, I, P, I, I, POINTER(GemmOpts), P,
+                                 c_size_t, P, P]),
+    "dspark_gemm_opts_size": (c_size_t, []),
     "dspark_attention_workspace_bytes": (c_size_t, [I, I, I, I, I, I]),
     "dspark_attention_merge_mode": (I, [I]),
     "dspark_attention": (I, [P, I, I, I, POINTER(KvLayout), P, I, c_float, P, I, I, P,

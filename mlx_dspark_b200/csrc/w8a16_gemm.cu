@@ -83,6 +83,15 @@ struct Params {
   // memory. 0: stream-K over the whole grid.
   int csplit;
   RopeEpi rope;
+  // RMSNorm plumbing between GEMMs (dspark_gemm_opts): the RESIDUAL_BF16 epilogue writes per-tile
+  // sums of squares of its bf16 outputs to ss_out [tiles][M]; a GEMM with norm_w set reads the raw
+  // bf16 residual stream as x and normalises each activation tile in shared memory before the MMA,
+  // with r[m] = rsqrt(sum_t ss_in[t][m] / K + eps)
+  float* ss_out;
+  const float* ss_in;
+  const __nv_bfloat16* norm_w;
+  int ss_tiles;
+  float norm_eps;
   // L2 prefetch of the next kernel's operands: CTA b warms bytes [b*chunk, (b+1)*chunk) of each
   // range after issuing its last load (16-byte aligned, sizes multiples of 16)
   const char* pf_ptr[2];
@@ -123,6 +132,7 @@ __device__ __forceinline__ void epilogue_store(const Params& p, int tile, int er
       // loads are not ordered one by one behind the stores they might alias
       __nv_bfloat16* y = static_cast<__nv_bfloat16*>(p.y);
       const __nv_bfloat16* r = static_cast<const __nv_bfloat16*>(p.residual);
+      const int lane = er & 31, ew = er >> 5;
 #pragma unroll
       for (int c0 = 0; c0 < BN; c0 += 16) {  // 16 rows at a time bounds the registers held
         __nv_bfloat16 rv[16];
@@ -131,9 +141,23 @@ __device__ __forceinline__ void epilogue_store(const Params& p, int tile, int er
           rv[j] = c0 + j < p.M ? r[(size_t)(c0 + j) * p.ldr + n] : __float2bfloat16_rn(0.0f);
 #pragma unroll
         for (int j = 0; j < 16; ++j)
-          if (c0 + j < p.M)
-            y[(size_t)(c0 + j) * p.ldy + n] =
-                __float2bfloat16_rn(__bfloat162float(rv[j]) + bf16_round(acc[c0 + j]));
+          if (c0 + j < p.M) {
+            const __nv_bfloat16 o = __float2bfloat16_rn(__bfloat162float(rv[j]) + bf16_round(acc[c0 + j]));
+            y[(size_t)(c0 + j) * p.ldy + n] = o;
+            if (p.ss_out) {
+              // this row's share of the next RMSNorm: warp sum, then the 4 warps in order
+              const float v = __bfloat162float(o);
+              const float w = warp_sum(v * v);
+              if (lane == 0) xch[ew * BN + c0 + j] = w;
+            }
+          }
+      }
+      if (p.ss_out) {
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (er < p.M)
+          p.ss_out[(size_t)tile * p.M + er] =
+              ((xch[er] + xch[BN + er]) + xch[2 * BN + er]) + xch[3 * BN + er];
+        asm volatile("bar.sync 1, 128;" ::: "memory");  // xch is reused by the next tile
       }
       break;
     }
@@ -439,6 +463,11 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 && !CS ? 2 : 1))
     const int r = threadIdx.x;
     const uint32_t lane_base = tmem_base + ((uint32_t)(warp * 32) << 16);
     const uint32_t k1024 = 0x64006400u;  // fp16x2 {1024, 1024}
+    // fused input RMSNorm: thread r normalises 16-byte chunk (r & 7) of activation rows
+    // (r >> 3) + 16k of both 64-wide boxes of every stage; rn[k] is that row's 1/rms
+    float rn[BN / 16];
+#pragma unroll
+    for (int kk = 0; kk < BN / 16; ++kk) rn[kk] = 0.0f;
     for (int i = 0; i < n_iter; ++i) {
       const int s = i % STAGES;
       const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
@@ -477,6 +506,55 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 && !CS ? 2 : 1))
           }
         }
         tmem_st32(lane_base + (uint32_t)a * 64u + (uint32_t)h * 32u, out);
+      }
+      if (p.norm_w) {
+        if (i == 0) {
+          pdl_wait();  // the row sums of squares come from the previous kernel
+#pragma unroll
+          for (int kk = 0; kk < BN / 16; ++kk) {
+            const int m = (r >> 3) + 16 * kk;
+            float sum = 0.0f;
+            if (m < p.M)
+              for (int t = 0; t < p.ss_tiles; ++t) sum += p.ss_in[(size_t)t * p.M + m];
+            rn[kk] = rsqrtf(sum / (float)p.K + p.norm_eps);
+          }
+        }
+        if (!mbar_wait(xfull(s), ph, abort_flag, p.status)) {
+          tc_wait_st();  // no TMEM store of this thread may be in flight at teardown
+          break;
+        }
+        const int kb = (int)((start + i) % KB);
+        const int c = r & 7;
+#pragma unroll
+        for (int bx = 0; bx < 2; ++bx) {
+          // the RMSNorm weights of these 8 columns (dspark_rmsnorm: bf16(x * r * w))
+          const uint4 wq8 = *reinterpret_cast<const uint4*>(p.norm_w + kb * BK + bx * 64 + c * 8);
+          const __nv_bfloat162* wv = reinterpret_cast<const __nv_bfloat162*>(&wq8);
+#pragma unroll
+          for (int kk = 0; kk < BN / 16; ++kk) {
+            const int m = (r >> 3) + 16 * kk;
+            if (m >= p.M) continue;
+            const uint32_t addr = x_s + s * L::kXBytes + bx * BN * 128 + m * 128 + ((c ^ (m & 7)) << 4);
+            uint32_t v[4];
+            asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
+                         : "r"(addr));
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const float2 hv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v[q]));
+              const float2 wf = __bfloat1622float2(wv[q]);
+              const __nv_bfloat162 xn = __floats2bfloat162_rn(hv.x * rn[kk] * wf.x, hv.y * rn[kk] * wf.y);
+              const float2 xf = __bfloat1622float2(xn);
+              const __half2 x16 = __floats2half2_rn(xf.x, xf.y);
+              v[q] = *reinterpret_cast<const uint32_t*>(&x16);
+            }
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v[0]), "r"(v[1]),
+                         "r"(v[2]), "r"(v[3])
+                         : "memory");
+          }
+        }
+        // the MMA reads the tile through the async proxy
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       }
       tc_wait_st();
       tc_fence_before();
@@ -1445,7 +1523,8 @@ static int launch_tc(const void* x, int ldx, const uint8_t* wq, const uint32_t* 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  p.csplit = ROPE ? 0 : plan_csplit<BN>(p.tiles, p.kb);  // the fused epilogue is stream-K only
+  // the fused epilogues (RoPE, row sums of squares) are stream-K only
+  p.csplit = (ROPE || p.ss_out) ? 0 : plan_csplit<BN>(p.tiles, p.kb);
   long long grid;
   if (p.csplit > 1) {
     grid = (long long)p.tiles * p.csplit;
@@ -1556,8 +1635,8 @@ static int gemm_common_checks(const void* x, int ldx, const uint8_t* wq, const u
 static int gemm_launch(const void* x, int ldx, const uint8_t* wq, const uint32_t* wsb, int M, int N,
                        int K, void* y, int ldy, const void* residual, int ldr, int epilogue,
                        void* workspace, size_t workspace_bytes, const void* pf0, size_t pf0_bytes,
-                       const void* pf1, size_t pf1_bytes, const w8::RopeEpi* rope, int* status,
-                       dspark_stream_t stream) {
+                       const void* pf1, size_t pf1_bytes, const w8::RopeEpi* rope,
+                       const dspark_gemm_opts* opts, int* status, dspark_stream_t stream) {
   const size_t need = w8::ws_bytes(M, N, K);
   if (!workspace || workspace_bytes < need)
     return set_error(DSPARK_ERR_WORKSPACE, "w8a16_gemm: workspace %zu < %zu bytes", workspace_bytes, need);
@@ -1575,6 +1654,23 @@ static int gemm_launch(const void* x, int ldx, const uint8_t* wq, const uint32_t
   p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + counters);
   p.status = status;
   if (rope) p.rope = *rope;
+  if (opts) {
+    if (opts->row_sumsq) {
+      if (epilogue != DSPARK_EPI_RESIDUAL_BF16)
+        return set_error(DSPARK_ERR_INVALID, "w8a16_gemm: row_sumsq needs the RESIDUAL_BF16 epilogue");
+      p.ss_out = opts->row_sumsq;
+    }
+    if (opts->norm_w) {
+      if (!opts->norm_sumsq || opts->norm_tiles <= 0)
+        return set_error(DSPARK_ERR_INVALID, "w8a16_gemm: norm_w without norm_sumsq / norm_tiles");
+      if (reinterpret_cast<uintptr_t>(opts->norm_w) & 15)
+        return set_error(DSPARK_ERR_ALIGN, "w8a16_gemm: norm_w not 16-byte aligned");
+      p.norm_w = static_cast<const __nv_bfloat16*>(opts->norm_w);
+      p.ss_in = opts->norm_sumsq;
+      p.ss_tiles = opts->norm_tiles;
+      p.norm_eps = opts->norm_eps;
+    }
+  }
   const void* pf[2] = {pf0, pf1};
   const size_t pfb[2] = {pf0_bytes, pf1_bytes};
   for (int r = 0; r < 2; ++r) {
@@ -1608,7 +1704,24 @@ extern "C" int dspark_w8a16_gemm_pf(const void* x, int ldx, const uint8_t* wq, c
   int rc = gemm_common_checks(x, ldx, wq, wsb, M, N, K, y, epilogue, residual);
   if (rc) return rc;
   return gemm_launch(x, ldx, wq, wsb, M, N, K, y, ldy, residual, ldr, epilogue, workspace,
-                     workspace_bytes, pf0, pf0_bytes, pf1, pf1_bytes, nullptr, status, stream);
+                     workspace_bytes, pf0, pf0_bytes, pf1, pf1_bytes, nullptr, nullptr, status,
+                     stream);
+}
+
+extern "C" size_t dspark_gemm_opts_size(void) { return sizeof(dspark_gemm_opts); }
+
+extern "C" int dspark_w8a16_gemm_ex(const void* x, int ldx, const uint8_t* wq, const uint32_t* wsb,
+                                    int M, int N, int K, void* y, int ldy, const void* residual,
+                                    int ldr, int epilogue, const dspark_gemm_opts* opts,
+                                    void* workspace, size_t workspace_bytes, int* status,
+                                    dspark_stream_t stream) {
+  int rc = gemm_common_checks(x, ldx, wq, wsb, M, N, K, y, epilogue, residual);
+  if (rc) return rc;
+  const dspark_gemm_opts z{};
+  const dspark_gemm_opts& o = opts ? *opts : z;
+  return gemm_launch(x, ldx, wq, wsb, M, N, K, y, ldy, residual, ldr, epilogue, workspace,
+                     workspace_bytes, o.prefetch[0], o.prefetch_bytes[0], o.prefetch[1],
+                     o.prefetch_bytes[1], nullptr, &o, status, stream);
 }
 
 extern "C" int dspark_w8a16_gemm_qkv_rope(const void* x, int ldx, const uint8_t* wq,
@@ -1616,10 +1729,10 @@ extern "C" int dspark_w8a16_gemm_qkv_rope(const void* x, int ldx, const uint8_t*
                                           int Hkv, int hd, const void* q_norm_w,
                                           const void* k_norm_w, float eps, const float* inv_freq,
                                           const int32_t* pos0, void* q_out,
-                                          const dspark_kv_layout* kv, void* workspace,
-                                          size_t workspace_bytes, const void* pf0,
-                                          size_t pf0_bytes, const void* pf1, size_t pf1_bytes,
-                                          int* status, dspark_stream_t stream) {
+                                          const dspark_kv_layout* kv,
+                                          const dspark_gemm_opts* opts, void* workspace,
+                                          size_t workspace_bytes, int* status,
+                                          dspark_stream_t stream) {
   if (hd != 64 && hd != 128)
     return set_error(DSPARK_ERR_UNSUPPORTED, "w8a16_gemm_qkv_rope: head_dim %d", hd);
   if (T <= 0 || M % T || Hkv <= 0 || Hq < 0 || !k_norm_w || !inv_freq || !pos0 || !kv ||
@@ -1642,8 +1755,13 @@ extern "C" int dspark_w8a16_gemm_qkv_rope(const void* x, int ldx, const uint8_t*
   r.kv = *kv;
   r.eps = eps;
   r.T = T; r.Hq = Hq; r.Hkv = Hkv; r.hd = hd;
+  const dspark_gemm_opts z{};
+  const dspark_gemm_opts& o = opts ? *opts : z;
+  if (o.row_sumsq)
+    return set_error(DSPARK_ERR_INVALID, "w8a16_gemm_qkv_rope: row_sumsq is not produced here");
   return gemm_launch(x, ldx, wq, wsb, M, N, K, nullptr, 0, nullptr, 0, -1, workspace,
-                     workspace_bytes, pf0, pf0_bytes, pf1, pf1_bytes, &r, status, stream);
+                     workspace_bytes, o.prefetch[0], o.prefetch_bytes[0], o.prefetch[1],
+                     o.prefetch_bytes[1], &r, &o, status, stream);
 }
 
 extern "C" int dspark_w8a16_gemm(const void* x, int ldx, const uint8_t* wq, const uint32_t* wsb,

@@ -7,6 +7,8 @@ status word that bounded device waits report into.
 """
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from . import _lib
@@ -89,29 +91,60 @@ def gemm_plan(M: int, N: int, K: int) -> dict:
     return {"grid": g.value, "cluster": c.value, "max_clusters": mc.value}
 
 
+class RowNorm:
+    """An RMSNorm fused into the GEMM that consumes it: the weights, eps, and the per-tile row
+    sums of squares [N/128, M] (fp32) written by the residual GEMM that produced the input."""
+
+    __slots__ = ("w", "eps", "sumsq")
+
+    def __init__(self, w: torch.Tensor, eps: float, sumsq: torch.Tensor):
+        self.w, self.eps, self.sumsq = w, float(eps), sumsq
+
+
+def _opts(prefetch: PackedLinear | None, norm: RowNorm | None,
+          sumsq_out: torch.Tensor | None) -> _lib.GemmOpts:
+    o = _lib.GemmOpts()
+    if prefetch is not None and PREFETCH_LIMIT > 0:
+        # q is row-major [N, K]: a prefix of it is whole 128-row tiles. sb is [K/64, N] (1/16 of
+        # q's bytes), so any prefix covers a few groups of every row: warm all of it, up to
+        # limit / 8.
+        o.prefetch[0] = prefetch.q.data_ptr()
+        o.prefetch_bytes[0] = min(prefetch.q.numel(), PREFETCH_LIMIT)
+        o.prefetch[1] = prefetch.sb.data_ptr()
+        o.prefetch_bytes[1] = min(prefetch.sb.numel() * 4, PREFETCH_LIMIT // 8)
+    if norm is not None:
+        o.norm_w = norm.w.data_ptr()
+        o.norm_sumsq = norm.sumsq.data_ptr()
+        o.norm_tiles = norm.sumsq.shape[0]
+        o.norm_eps = norm.eps
+    if sumsq_out is not None:
+        o.row_sumsq = sumsq_out.data_ptr()
+    return o
+
+
 def gemm(x16: torch.Tensor, w: PackedLinear, y: torch.Tensor, *, epilogue=_lib.EPI_STORE_BF16,
          residual: torch.Tensor | None = None, scratch: Scratch, M: int | None = None,
-         prefetch: PackedLinear | None = None) -> torch.Tensor:
+         prefetch: PackedLinear | None = None, norm: RowNorm | None = None,
+         sumsq_out: torch.Tensor | None = None) -> torch.Tensor:
     """y = x16 @ W^T with the chosen epilogue (see include/dspark_b200.h). `prefetch`: the next
-    projection's weights, warmed in L2 (up to PREFETCH_LIMIT bytes) during this GEMM's tail."""
+    projection's weights, warmed in L2 (up to PREFETCH_LIMIT bytes) during this GEMM's tail.
+    `norm`: x16 is the bf16 residual stream and the GEMM consumes its RMSNorm. `sumsq_out`
+    (RESIDUAL_BF16 only): per-tile row sums of squares of y for the next fused norm."""
     _require_cuda(x16, y)
     M = x16.shape[0] if M is None else M
     K = w.K
-    assert x16.dtype == torch.float16 and x16.shape[-1] >= K
+    want = torch.bfloat16 if norm is not None else torch.float16
+    assert x16.dtype == want and x16.shape[-1] >= K
     ws = scratch.get("gemm", gemm_workspace_bytes(M, w.N, K))
-    if prefetch is None or PREFETCH_LIMIT <= 0:
+    if norm is None and sumsq_out is None and (prefetch is None or PREFETCH_LIMIT <= 0):
         call("dspark_w8a16_gemm", _p(x16), x16.stride(0), _p(w.q), _p(w.sb), M, w.N, K, _p(y),
              y.stride(0), _p(residual), residual.stride(0) if residual is not None else 0,
              epilogue, _p(ws), ws.numel(), _p(scratch.status), _stream())
         return y
-    # q is row-major [N, K]: a prefix of it is whole 128-row tiles. sb is [K/64, N] (1/16 of q's
-    # bytes), so any prefix covers a few groups of every row: warm all of it, up to limit / 8.
-    qb = min(prefetch.q.numel(), PREFETCH_LIMIT)
-    sbb = min(prefetch.sb.numel() * 4, PREFETCH_LIMIT // 8)
-    call("dspark_w8a16_gemm_pf", _p(x16), x16.stride(0), _p(w.q), _p(w.sb), M, w.N, K, _p(y),
+    opts = _opts(prefetch, norm, sumsq_out)
+    call("dspark_w8a16_gemm_ex", _p(x16), x16.stride(0), _p(w.q), _p(w.sb), M, w.N, K, _p(y),
          y.stride(0), _p(residual), residual.stride(0) if residual is not None else 0, epilogue,
-         _p(ws), ws.numel(), _p(prefetch.q), qb, _p(prefetch.sb), sbb, _p(scratch.status),
-         _stream())
+         ctypes.byref(opts), _p(ws), ws.numel(), _p(scratch.status), _stream())
     return y
 
 
@@ -119,23 +152,19 @@ def gemm_qkv_rope(x16: torch.Tensor, w: PackedLinear, *, T: int, Hq: int, Hkv: i
                   q_norm: torch.Tensor | None, k_norm: torch.Tensor, eps: float,
                   inv_freq: torch.Tensor, pos0: torch.Tensor, q_out: torch.Tensor | None,
                   kv: KvLayout, scratch: Scratch, M: int | None = None,
-                  prefetch: PackedLinear | None = None) -> None:
+                  prefetch: PackedLinear | None = None, norm: RowNorm | None = None) -> None:
     """The q|k|v GEMM with the per-head norm + RoPE + q / paged K/V writes in its epilogue
-    (one launch; equals gemm(STORE_BF16) + qkv_rope_kv_write)."""
+    (one launch; equals gemm(STORE_BF16) + qkv_rope_kv_write). `norm` as in gemm()."""
     _require_cuda(x16)
     M = x16.shape[0] if M is None else M
     K = w.K
-    assert x16.dtype == torch.float16 and x16.shape[-1] >= K and w.N == (Hq + 2 * Hkv) * hd
+    want = torch.bfloat16 if norm is not None else torch.float16
+    assert x16.dtype == want and x16.shape[-1] >= K and w.N == (Hq + 2 * Hkv) * hd
     ws = scratch.get("gemm", gemm_workspace_bytes(M, w.N, K))
-    pq = psb = None
-    qb = sbb = 0
-    if prefetch is not None and PREFETCH_LIMIT > 0:
-        pq, psb = prefetch.q, prefetch.sb
-        qb = min(prefetch.q.numel(), PREFETCH_LIMIT)
-        sbb = min(prefetch.sb.numel() * 4, PREFETCH_LIMIT // 8)
+    opts = _opts(prefetch, norm, None)
     call("dspark_w8a16_gemm_qkv_rope", _p(x16), x16.stride(0), _p(w.q), _p(w.sb), M, K, T, Hq,
          Hkv, hd, _p(q_norm), _p(k_norm), float(eps), _p(inv_freq), _p(pos0), _p(q_out), kv,
-         _p(ws), ws.numel(), _p(pq), qb, _p(psb), sbb, _p(scratch.status), _stream())
+         ctypes.byref(opts), _p(ws), ws.numel(), _p(scratch.status), _stream())
 
 
 def gemm_simt(x16, w: PackedLinear, y, *, epilogue=_lib.EPI_STORE_BF16, residual=None, M=None):

@@ -64,6 +64,9 @@ class Buffers:
                         if n_tap else None)
         self.logits = (torch.zeros(M, cfg.vocab_size, dtype=torch.bfloat16, device=device)
                        if logits else None)
+        # per-128-column-tile row sums of squares of h, written by the residual GEMMs for the
+        # RMSNorm fused into the next GEMM
+        self.sumsq = torch.zeros(H // 128, M, dtype=torch.float32, device=device)
 
 
 class Target:
@@ -145,6 +148,10 @@ class Target:
     # the q|k|v GEMM runs the per-head norm + RoPE + KV write in its epilogue (one launch
     # instead of two; bit-identical outputs)
     fuse_qkv_rope = True
+    # every RMSNorm but the first layer's input norm runs inside the GEMM that consumes it (the
+    # residual GEMM before it writes per-tile sums of squares); the only difference from the
+    # separate norm kernel is the fp32 summation order of the squares
+    fuse_norm = True
 
     def forward(self, buf: Buffers, state: CacheState, tap=(), *, splits: int | None = None,
                 with_logits: bool = True) -> None:
@@ -159,40 +166,59 @@ class Target:
         H = c.hidden_size
         ops.embed(buf.ids, self.embed, buf.h, M)
         n_layers = len(self.layers)
+        eps = c.rms_norm_eps
+        fuse = self.fuse_norm
+        ss = buf.sumsq if fuse else None
         for l, L in enumerate(self.layers):
             kv = state.layout(l)
             # each GEMM warms L2 with the next GEMM's weights (the head after the last layer)
             nxt = self.layers[l + 1].qkv if l + 1 < n_layers else (self.head if with_logits else None)
-            ops.rmsnorm(buf.h, L.input_ln, c.rms_norm_eps, y16=buf.xn16, M=M)
-            self._qkv_rope(buf, L, kv, state, B, T, M)
+            if fuse and l > 0:
+                self._qkv_rope(buf, L, kv, state, B, T, M, x=buf.h,
+                               norm=ops.RowNorm(L.input_ln, eps, ss))
+            else:
+                ops.rmsnorm(buf.h, L.input_ln, eps, y16=buf.xn16, M=M)
+                self._qkv_rope(buf, L, kv, state, B, T, M)
             ops.attention(buf.q, B, T, c.num_attention_heads, kv, state.seq_len, True,
                           self.scale, buf.attn16, splits, sc)
             ops.gemm(buf.attn16, L.o, buf.h, epilogue=EPI_RESIDUAL_BF16, residual=buf.h,
-                     scratch=sc, M=M, prefetch=L.gu)
-            ops.rmsnorm(buf.h, L.post_ln, c.rms_norm_eps, y16=buf.xn16, M=M)
-            ops.gemm(buf.xn16, L.gu, buf.act16, epilogue=EPI_SILU_MUL_F16, scratch=sc, M=M,
-                     prefetch=L.down)
+                     scratch=sc, M=M, prefetch=L.gu, sumsq_out=ss)
+            if fuse:
+                ops.gemm(buf.h, L.gu, buf.act16, epilogue=EPI_SILU_MUL_F16, scratch=sc, M=M,
+                         prefetch=L.down, norm=ops.RowNorm(L.post_ln, eps, ss))
+            else:
+                ops.rmsnorm(buf.h, L.post_ln, eps, y16=buf.xn16, M=M)
+                ops.gemm(buf.xn16, L.gu, buf.act16, epilogue=EPI_SILU_MUL_F16, scratch=sc, M=M,
+                         prefetch=L.down)
             ops.gemm(buf.act16, L.down, buf.h, epilogue=EPI_RESIDUAL_BF16, residual=buf.h,
-                     scratch=sc, M=M, prefetch=nxt)
+                     scratch=sc, M=M, prefetch=nxt, sumsq_out=ss)
             if l in tap_idx:
                 j = tap_idx[l]
                 ops.bf16_to_f16(buf.h, buf.fused16[:, j * H:(j + 1) * H], M, H)
         if with_logits:
-            ops.rmsnorm(buf.h, self.norm, c.rms_norm_eps, y16=buf.xn16, M=M)
-            ops.gemm(buf.xn16, self.head, buf.logits, epilogue=EPI_STORE_BF16, scratch=sc, M=M)
+            if fuse:
+                ops.gemm(buf.h, self.head, buf.logits, epilogue=EPI_STORE_BF16, scratch=sc, M=M,
+                         norm=ops.RowNorm(self.norm, eps, ss))
+            else:
+                ops.rmsnorm(buf.h, self.norm, eps, y16=buf.xn16, M=M)
+                ops.gemm(buf.xn16, self.head, buf.logits, epilogue=EPI_STORE_BF16, scratch=sc, M=M)
 
-    def _qkv_rope(self, buf: Buffers, L, kv, state: CacheState, B: int, T: int, M: int) -> None:
-        """q|k|v projection of buf.xn16, per-head q/k norm + RoPE at state.seq_len, q into
-        buf.q and K/V into the layer's paged cache."""
+    def _qkv_rope(self, buf: Buffers, L, kv, state: CacheState, B: int, T: int, M: int,
+                  x: torch.Tensor | None = None, norm: "ops.RowNorm | None" = None) -> None:
+        """q|k|v projection of x (buf.xn16, or the bf16 residual stream with its fused input
+        norm), per-head q/k norm + RoPE at state.seq_len, q into buf.q and K/V into the layer's
+        paged cache."""
         c, sc = self.cfg, self.scratch
+        x = buf.xn16 if x is None else x
         if self.fuse_qkv_rope:
-            ops.gemm_qkv_rope(buf.xn16, L.qkv, T=T, Hq=c.num_attention_heads,
+            ops.gemm_qkv_rope(x, L.qkv, T=T, Hq=c.num_attention_heads,
                               Hkv=c.num_key_value_heads, hd=c.head_dim, q_norm=L.q_norm,
                               k_norm=L.k_norm, eps=c.rms_norm_eps, inv_freq=self.inv_freq,
                               pos0=state.seq_len, q_out=buf.q, kv=kv, scratch=sc, M=M,
-                              prefetch=L.o)
+                              prefetch=L.o, norm=norm)
             return
-        ops.gemm(buf.xn16, L.qkv, buf.qkv, epilogue=EPI_STORE_BF16, scratch=sc, M=M, prefetch=L.o)
+        ops.gemm(x, L.qkv, buf.qkv, epilogue=EPI_STORE_BF16, scratch=sc, M=M, prefetch=L.o,
+                 norm=norm)
         ops.qkv_rope_kv_write(buf.qkv, B, T, c.num_attention_heads, c.num_key_value_heads,
                               c.head_dim, L.q_norm, L.k_norm, c.rms_norm_eps, self.inv_freq,
                               state.seq_len, buf.q, kv)

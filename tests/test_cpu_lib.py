@@ -71,3 +71,9 @@ def test_chain_phase_struct_matches_the_c_layout():
     import ctypes
     from mlx_dspark_b200 import _lib
     assert ctypes.sizeof(_lib.ChainPhase) == _lib.lib().dspark_chain_phase_size()
+
+
+def test_gemm_opts_struct_matches_the_c_layout():
+    import ctypes
+    from mlx_dspark_b200 import _lib
+    assert ctypes.sizeof(_lib.GemmOpts) == _lib.lib().dspark_gemm_opts_size()

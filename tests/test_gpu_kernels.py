@@ -154,6 +154,50 @@ def test_gemm_residual_and_silu_epilogues(cuda, M, H, I):
     assert ((h.float().cpu() - ref_h).abs() <= bh).all(), ((h.float().cpu() - ref_h).abs() / bh).max()
 
 
+@pytest.mark.parametrize("M,H,N", [(9, 4096, 1024), (1, 1024, 512), (33, 2048, 256),
+                                   (64, 512, 384)])
+def test_gemm_fused_rmsnorm_and_row_sumsq(cuda, M, H, N):
+    """The residual epilogue's per-tile row sums of squares are the sums of the squares of the
+    bf16 rows it wrote, and a GEMM fed the raw residual stream with the fused RMSNorm matches
+    dspark_rmsnorm + GEMM to one bf16 rounding of its inputs (the squares are summed in another
+    fp32 order, so 1/rms may differ in its last bits)."""
+    sc = ops.Scratch(cuda)
+    Kd = 512
+    d = _qrand(H, Kd, 11)
+    x = _x16(M, Kd, 3).to(torch.float16).to(cuda)
+    r0 = torch.randn(M, H, generator=torch.Generator().manual_seed(5)).to(torch.bfloat16)
+    h = r0.clone().to(cuda)
+    ss = torch.zeros(H // 128, M, dtype=torch.float32, device=cuda)
+    ops.gemm(x, pack(d, device=cuda), h, epilogue=EPI_RESIDUAL_BF16, residual=h, scratch=sc,
+             sumsq_out=ss)
+    torch.cuda.synchronize()
+    sc.check_status()
+    hf = h.float().cpu().double()
+    ref_ss = (hf ** 2).reshape(M, H // 128, 128).sum(-1).t()
+    assert torch.allclose(ss.cpu().double(), ref_ss, rtol=1e-5, atol=1e-6)
+    eps = 1e-6
+    w = (1 + 0.1 * torch.randn(H, generator=torch.Generator().manual_seed(6))).to(torch.bfloat16).to(cuda)
+    qt = _qrand(N, H, 12)
+    wn = pack(qt, device=cuda)
+    xn16 = torch.zeros(M, H, dtype=torch.float16, device=cuda)
+    y1 = torch.zeros(M, N, dtype=torch.float32, device=cuda)
+    y2 = torch.zeros_like(y1)
+    ops.rmsnorm(h, w, eps, y16=xn16, M=M)
+    ops.gemm(xn16, wn, y1, epilogue=EPI_STORE_F32, scratch=sc, M=M)
+    ops.gemm(h, wn, y2, epilogue=EPI_STORE_F32, scratch=sc, M=M, norm=ops.RowNorm(w, eps, ss))
+    torch.cuda.synchronize()
+    sc.check_status()
+    xn = xn16.float().cpu()
+    bound = (xn.abs() @ qt.dequant().abs().t()) * (2.0 ** -8 + 2.0 ** -9) + 1e-5
+    diff = (y1.cpu() - y2.cpu()).abs()
+    assert (diff <= bound).all(), (diff / bound).max()
+    # the fused path is deterministic
+    y3 = torch.zeros_like(y1)
+    ops.gemm(h, wn, y3, epilogue=EPI_STORE_F32, scratch=sc, M=M, norm=ops.RowNorm(w, eps, ss))
+    torch.cuda.synchronize()
+    assert torch.equal(y2, y3)
+
+
 def test_rmsnorm_and_embed(cuda):
     M, H, V = 9, 1024, 4096
     x = torch.randn(M, H).to(torch.bfloat16)
