@@ -110,7 +110,8 @@ __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x));
 
 template <int BN>
 __device__ __forceinline__ void epilogue_store(const Params& p, int tile, int er, const float* acc,
-                                               float* xch) {
+                                               float* xch,
+                                               const __nv_bfloat162* rpre = nullptr) {
   const int n = tile * BM + er;
   switch (p.epilogue) {
     case DSPARK_EPI_STORE_BF16: {
@@ -137,8 +138,13 @@ __device__ __forceinline__ void epilogue_store(const Params& p, int tile, int er
       for (int c0 = 0; c0 < BN; c0 += 16) {  // 16 rows at a time bounds the registers held
         __nv_bfloat16 rv[16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j)
-          rv[j] = c0 + j < p.M ? r[(size_t)(c0 + j) * p.ldr + n] : __float2bfloat16_rn(0.0f);
+        for (int j = 0; j < 16; ++j) {
+          const int m = c0 + j;
+          if (rpre)  // read by the caller before it waited on the other contributors
+            rv[j] = (m & 1) ? rpre[m >> 1].y : rpre[m >> 1].x;
+          else
+            rv[j] = m < p.M ? r[(size_t)m * p.ldr + n] : __float2bfloat16_rn(0.0f);
+        }
 #pragma unroll
         for (int j = 0; j < 16; ++j)
           if (c0 + j < p.M) {
@@ -611,20 +617,37 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 && !CS ? 2 : 1))
         else
           epilogue_store<BN>(p, tile, er, acc, xch);
       } else {
-        // partial of this CTA, column-major [m][128] and only the M real activation rows: the
-        // stores are coalesced, and each contributor's partial is one contiguous M*512-byte block
+        // partial of this CTA, row-major [128][MP] with MP = M rounded up to 4: thread er's
+        // values are 16-byte vectors, and each contributor's partial is one contiguous
+        // 128*MP*4-byte block
         const int slot = (int)blockIdx.x * 2 + (seg == 0 ? 0 : 1);
-        float* part = p.partials + (size_t)slot * BN * BM + er;
+        const int MP = (p.M + 3) & ~3;
+        {
+          float4* part = reinterpret_cast<float4*>(p.partials + (size_t)slot * BN * BM + er * MP);
 #pragma unroll
-        for (int m = 0; m < BN; ++m)
-          if (m < p.M) part[m * BM] = acc[m];
-        if (p.epilogue == DSPARK_EPI_RESIDUAL_BF16) {
-          // the finishing CTA reads the residual rows of this tile last: warm L1 with them now,
-          // so that read overlaps the arrival round trip instead of following it
+          for (int j = 0; j < BN / 4; ++j)
+            if (4 * j < MP) part[j] = make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
+        }
+        // the residual rows of this tile, read now so that the read overlaps the arrival round
+        // trip (only the CTA that finishes the tile writes them): into registers at BN 16, into
+        // L1 at the wider shapes, whose registers are taken
+        constexpr bool kPre = BN <= 16;
+        __nv_bfloat162 rpre[kPre ? BN / 2 : 1];
+        const bool res = !ROPE && p.epilogue == DSPARK_EPI_RESIDUAL_BF16;
+        if (res) {
           const __nv_bfloat16* rp = static_cast<const __nv_bfloat16*>(p.residual) + tile * BM + er;
+          if constexpr (kPre) {
 #pragma unroll
-          for (int m = 0; m < BN; ++m)
-            if (m < p.M) asm volatile("prefetch.global.L1 [%0];" ::"l"(rp + (size_t)m * p.ldr));
+            for (int j = 0; j < BN / 2; ++j) {
+              const int m = 2 * j;
+              rpre[j].x = m < p.M ? rp[(size_t)m * p.ldr] : __float2bfloat16_rn(0.0f);
+              rpre[j].y = m + 1 < p.M ? rp[(size_t)(m + 1) * p.ldr] : __float2bfloat16_rn(0.0f);
+            }
+          } else {
+#pragma unroll
+            for (int m = 0; m < BN; ++m)
+              if (m < p.M) asm volatile("prefetch.global.L1 [%0];" ::"l"(rp + (size_t)m * p.ldr));
+          }
         }
         asm volatile("bar.sync 1, 128;" ::: "memory");
         const long long c_lo = range_owner(tile_lo, total, G);
@@ -633,7 +656,7 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 && !CS ? 2 : 1))
         // contributor c keeps this tile in its partial slot 2c + 1 only if the tile is its second
         // segment, which only the first contributor's range can make it (ranges are contiguous)
         const int cj_lo = range_start(c_lo, total, G) >= tile_lo ? 0 : 1;
-        const uint32_t blk = (uint32_t)p.M * BM * 4u;
+        const uint32_t blk = (uint32_t)MP * BM * 4u;
         // the stage ring is idle once this CTA's last segment is accumulated (every copy into
         // it has landed and been consumed), so the finishing CTA can stage the partials there
         const bool ring_free = seg_end == end && (uint32_t)nctr * blk <= (uint32_t)STAGES * L::kStageBytes;
@@ -674,41 +697,53 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 && !CS ? 2 : 1))
               mbar_wait(fix_bar, fix_phase, &never, p.status);
             }
             fix_phase ^= 1u;
-            // contributor order, as in the register path below; four contributors' values are
+            // contributor order, as in the register path below; two contributors' vectors are
             // loaded before they are added so the shared-memory loads overlap
-            const float* st = reinterpret_cast<const float*>(sbase) + er;
-            const int stride = (int)(blk / 4);
+            const float4* st = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(sbase) + er * MP);
+            const int stride = (int)(blk / 16);  // float4s per contributor block
             int ci = 0;
-            for (; ci + 4 <= nctr; ci += 4) {
+            for (; ci + 2 <= nctr; ci += 2) {
 #pragma unroll
-              for (int m = 0; m < BN; ++m)
-                if (m < p.M) {
-                  const float* q = st + ci * stride + m * BM;
-                  const float v0 = q[0], v1 = q[stride], v2 = q[2 * stride], v3 = q[3 * stride];
-                  sum[m] = (((sum[m] + v0) + v1) + v2) + v3;
+              for (int j = 0; j < BN / 4; ++j)
+                if (4 * j < MP) {
+                  const float4 v0 = st[ci * stride + j], v1 = st[(ci + 1) * stride + j];
+                  sum[4 * j] = (sum[4 * j] + v0.x) + v1.x;
+                  sum[4 * j + 1] = (sum[4 * j + 1] + v0.y) + v1.y;
+                  sum[4 * j + 2] = (sum[4 * j + 2] + v0.z) + v1.z;
+                  sum[4 * j + 3] = (sum[4 * j + 3] + v0.w) + v1.w;
                 }
             }
             for (; ci < nctr; ++ci) {
 #pragma unroll
-              for (int m = 0; m < BN; ++m)
-                if (m < p.M) sum[m] += st[ci * stride + m * BM];
+              for (int j = 0; j < BN / 4; ++j)
+                if (4 * j < MP) {
+                  const float4 v0 = st[ci * stride + j];
+                  sum[4 * j] += v0.x;
+                  sum[4 * j + 1] += v0.y;
+                  sum[4 * j + 2] += v0.z;
+                  sum[4 * j + 3] += v0.w;
+                }
             }
           } else {
             for (long long c = c_lo; c <= c_hi; ++c) {
               const int cj = c == c_lo ? cj_lo : 0;
-              const float* cp = p.partials + ((size_t)c * 2 + cj) * BN * BM + er;
-              float t[BN];
+              const float4* cp = reinterpret_cast<const float4*>(p.partials + ((size_t)c * 2 + cj) * BN * BM + er * MP);
 #pragma unroll
-              for (int m = 0; m < BN; ++m) t[m] = m < p.M ? __ldcg(cp + m * BM) : 0.0f;
-#pragma unroll
-              for (int m = 0; m < BN; ++m) sum[m] += t[m];
+              for (int j = 0; j < BN / 4; ++j)
+                if (4 * j < MP) {
+                  const float4 v0 = __ldcg(cp + j);
+                  sum[4 * j] += v0.x;
+                  sum[4 * j + 1] += v0.y;
+                  sum[4 * j + 2] += v0.z;
+                  sum[4 * j + 3] += v0.w;
+                }
             }
           }
           if (er == 0) p.counters[tile] = 0;
           if constexpr (ROPE)
             rope_epilogue<BN>(p, tile, er, sum, xch);
           else
-            epilogue_store<BN>(p, tile, er, sum, xch);
+            epilogue_store<BN>(p, tile, er, sum, xch, (kPre && res) ? rpre : nullptr);
         }
         asm volatile("bar.sync 1, 128;" ::: "memory");
       }
