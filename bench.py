@@ -194,7 +194,7 @@ def gemm_roofline(target, M, reps=5):
     H, I = c.hidden_size, c.intermediate_size
     # the residual stream the norm-fused GEMMs read, and its per-tile row sums of squares
     hin = torch.randn(M, H, device=dev).to(torch.bfloat16)
-    ss = torch.full((H // 128, M), 128.0, dtype=torch.float32, device=dev)
+    ss = torch.full((M, H // 128), 128.0, dtype=torch.float32, device=dev)
     eps = c.rms_norm_eps
 
     def one_pass():

@@ -97,15 +97,16 @@ int dspark_w8a16_gemm_pf(const void* x, int ldx, const uint8_t* wq, const uint32
                          dspark_stream_t stream);
 /* Options of dspark_w8a16_gemm_ex (zero-initialise; NULL pointers switch a feature off).
  *   prefetch[2], prefetch_bytes[2]: as dspark_w8a16_gemm_pf.
- *   row_sumsq (RESIDUAL_BF16 epilogue only): fp32 [N/128, M] output; entry (t, m) is the sum of
- *     the squares of the bf16 outputs y[m, 128t .. 128t+127] this call writes, summed in a fixed
- *     order — the pieces of the next RMSNorm of the residual stream.
+ *   row_sumsq (STORE_BF16 / RESIDUAL_BF16 epilogues): fp32 [M, N/128] output; entry (m, t) is
+ *     the sum of the squares of the bf16 outputs y[m, 128t .. 128t+127] this call writes, summed
+ *     in a fixed order — the pieces of the next RMSNorm of that row.
  *   norm_w, norm_sumsq, norm_tiles, norm_eps: fuse the RMSNorm of the GEMM input (mlx.fast.rms_norm,
  *     the input/post-attention/final norms of the Qwen3 layers). x is then the bf16 residual stream
  *     [M, K] itself; the GEMM consumes bf16(x[m,k] * r[m] * w[k]) (as dspark_rmsnorm's output)
- *     with r[m] = rsqrt(sum_t norm_sumsq[t, m] / K + eps) from the row_sumsq of the GEMM that
- *     wrote x (norm_tiles = its N/128). The only difference from dspark_rmsnorm + this GEMM is the
- *     fp32 summation order of the squares. */
+ *     with r[m] = rsqrt(sum_t norm_sumsq[m, t] / K + eps), t in order, from the row_sumsq of the
+ *     GEMM that wrote x (norm_tiles = its N/128; norm_ld = the row stride in floats, 0 meaning
+ *     norm_tiles; 16-byte aligned rows when norm_ld % 4 == 0). The only difference from
+ *     dspark_rmsnorm + this GEMM is the fp32 summation order of the squares. */
 typedef struct dspark_gemm_opts {
   const void* prefetch[2];
   size_t prefetch_bytes[2];
@@ -114,6 +115,8 @@ typedef struct dspark_gemm_opts {
   const void* norm_w;
   int norm_tiles;
   float norm_eps;
+  int norm_ld;
+  int reserved;
 } dspark_gemm_opts;
 int dspark_w8a16_gemm_ex(const void* x, int ldx, const uint8_t* wq, const uint32_t* wsb, int M,
                          int N, int K, void* y, int ldy, const void* residual, int ldr,

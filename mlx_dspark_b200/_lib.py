@@ -51,7 +51,8 @@ class GemmOpts(ctypes.Structure):
     """dspark_gemm_opts (include/dspark_b200.h)."""
     _fields_ = [("prefetch", c_void_p * 2), ("prefetch_bytes", c_size_t * 2),
                 ("row_sumsq", c_void_p), ("norm_sumsq", c_void_p), ("norm_w", c_void_p),
-                ("norm_tiles", c_int), ("norm_eps", c_float)]
+                ("norm_tiles", c_int), ("norm_eps", c_float), ("norm_ld", c_int),
+                ("reserved", c_int)]
 
 
 # name -> (restype, argtypes); mirrors include/dspark_b200.h

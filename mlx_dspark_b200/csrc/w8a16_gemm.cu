@@ -83,14 +83,15 @@ struct Params {
   // memory. 0: stream-K over the whole grid.
   int csplit;
   RopeEpi rope;
-  // RMSNorm plumbing between GEMMs (dspark_gemm_opts): the RESIDUAL_BF16 epilogue writes per-tile
-  // sums of squares of its bf16 outputs to ss_out [tiles][M]; a GEMM with norm_w set reads the raw
-  // bf16 residual stream as x and normalises each activation tile in shared memory before the MMA,
-  // with r[m] = rsqrt(sum_t ss_in[t][m] / K + eps)
+  // RMSNorm plumbing between GEMMs (dspark_gemm_opts): the STORE_BF16 / RESIDUAL_BF16 epilogues
+  // write per-tile sums of squares of their bf16 outputs to ss_out [M][tiles]; a GEMM with norm_w
+  // set reads the raw bf16 row as x and normalises each activation tile in shared memory before
+  // the MMA, with r[m] = rsqrt(sum_t ss_in[m][t] / K + eps)
   float* ss_out;
   const float* ss_in;
   const __nv_bfloat16* norm_w;
   int ss_tiles;
+  int ss_ld;  // row stride of ss_in in floats (>= ss_tiles)
   float norm_eps;
   // L2 prefetch of the next kernel's operands: CTA b warms bytes [b*chunk, (b+1)*chunk) of each
   // range after issuing its last load (16-byte aligned, sizes multiples of 16)
@@ -116,9 +117,25 @@ __device__ __forceinline__ void epilogue_store(const Params& p, int tile, int er
   switch (p.epilogue) {
     case DSPARK_EPI_STORE_BF16: {
       __nv_bfloat16* y = static_cast<__nv_bfloat16*>(p.y);
+      const int lane = er & 31, ew = er >> 5;
 #pragma unroll
       for (int m = 0; m < BN; ++m)
-        if (m < p.M) y[(size_t)m * p.ldy + n] = __float2bfloat16_rn(acc[m]);
+        if (m < p.M) {
+          const __nv_bfloat16 o = __float2bfloat16_rn(acc[m]);
+          y[(size_t)m * p.ldy + n] = o;
+          if (p.ss_out) {
+            const float v = __bfloat162float(o);
+            const float w = warp_sum(v * v);
+            if (lane == 0) xch[ew * BN + m] = w;
+          }
+        }
+      if (p.ss_out) {
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (er < p.M)
+          p.ss_out[(size_t)er * p.tiles + tile] =
+              ((xch[er] + xch[BN + er]) + xch[2 * BN + er]) + xch[3 * BN + er];
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+      }
       break;
     }
     case DSPARK_EPI_STORE_F32: {
@@ -161,7 +178,7 @@ __device__ __forceinline__ void epilogue_store(const Params& p, int tile, int er
       if (p.ss_out) {
         asm volatile("bar.sync 1, 128;" ::: "memory");
         if (er < p.M)
-          p.ss_out[(size_t)tile * p.M + er] =
+          p.ss_out[(size_t)er * p.tiles + tile] =
               ((xch[er] + xch[BN + er]) + xch[2 * BN + er]) + xch[3 * BN + er];
         asm volatile("bar.sync 1, 128;" ::: "memory");  // xch is reused by the next tile
       }
@@ -520,8 +537,17 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 && !CS ? 2 : 1))
           for (int kk = 0; kk < BN / 16; ++kk) {
             const int m = (r >> 3) + 16 * kk;
             float sum = 0.0f;
-            if (m < p.M)
-              for (int t = 0; t < p.ss_tiles; ++t) sum += p.ss_in[(size_t)t * p.M + m];
+            if (m < p.M) {
+              // the row's per-tile sums, contiguous: 16-byte loads, added in tile order
+              const float* row = p.ss_in + (size_t)m * p.ss_ld;
+              int t = 0;
+              if ((p.ss_ld & 3) == 0)
+                for (; t + 4 <= p.ss_tiles; t += 4) {
+                  const float4 q4 = *reinterpret_cast<const float4*>(row + t);
+                  sum = (((sum + q4.x) + q4.y) + q4.z) + q4.w;
+                }
+              for (; t < p.ss_tiles; ++t) sum += row[t];
+            }
             rn[kk] = rsqrtf(sum / (float)p.K + p.norm_eps);
           }
         }
@@ -1691,8 +1717,9 @@ static int gemm_launch(const void* x, int ldx, const uint8_t* wq, const uint32_t
   if (rope) p.rope = *rope;
   if (opts) {
     if (opts->row_sumsq) {
-      if (epilogue != DSPARK_EPI_RESIDUAL_BF16)
-        return set_error(DSPARK_ERR_INVALID, "w8a16_gemm: row_sumsq needs the RESIDUAL_BF16 epilogue");
+      if (epilogue != DSPARK_EPI_RESIDUAL_BF16 && epilogue != DSPARK_EPI_STORE_BF16)
+        return set_error(DSPARK_ERR_INVALID,
+                         "w8a16_gemm: row_sumsq needs the STORE_BF16 or RESIDUAL_BF16 epilogue");
       p.ss_out = opts->row_sumsq;
     }
     if (opts->norm_w) {
@@ -1703,6 +1730,12 @@ static int gemm_launch(const void* x, int ldx, const uint8_t* wq, const uint32_t
       p.norm_w = static_cast<const __nv_bfloat16*>(opts->norm_w);
       p.ss_in = opts->norm_sumsq;
       p.ss_tiles = opts->norm_tiles;
+      p.ss_ld = opts->norm_ld > 0 ? opts->norm_ld : opts->norm_tiles;
+      if (p.ss_ld < opts->norm_tiles)
+        return set_error(DSPARK_ERR_INVALID, "w8a16_gemm: norm_ld %d < norm_tiles %d", p.ss_ld,
+                         opts->norm_tiles);
+      if ((p.ss_ld & 3) == 0 && (reinterpret_cast<uintptr_t>(opts->norm_sumsq) & 15))
+        return set_error(DSPARK_ERR_ALIGN, "w8a16_gemm: norm_sumsq not 16-byte aligned");
       p.norm_eps = opts->norm_eps;
     }
   }

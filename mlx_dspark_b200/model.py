@@ -71,6 +71,9 @@ class DraftBuffers:
         self.ctx_h = torch.zeros(ctx_rows, H, dtype=torch.bfloat16, device=device)
         self.ctx_x16 = torch.zeros(ctx_rows, H, dtype=torch.float16, device=device)
         self.ctx_kv = torch.zeros(ctx_rows, 2 * kv_dim, dtype=torch.bfloat16, device=device)
+        # per-128-column-tile row sums of squares for the RMSNorms fused into the next GEMM
+        self.sumsq = torch.zeros(M, H // 128, dtype=torch.float32, device=device)
+        self.ctx_sumsq = torch.zeros(H // 128 * ctx_rows, dtype=torch.float32, device=device)
 
 
 class BlockDrafter:
@@ -130,38 +133,56 @@ class BlockDrafter:
         written at ctx positions seq_len[b] + t."""
         c, sc = self.config, self.scratch
         M = B * T
-        ops.gemm(fused16, self.fc, buf.ctx_h, epilogue=EPI_STORE_BF16, scratch=sc, M=M)
-        ops.rmsnorm(buf.ctx_h, self.hidden_norm, c.rms_norm_eps, y16=buf.ctx_x16, M=M)
+        eps = c.rms_norm_eps
+        # fc -> (hidden_norm fused into each layer's k|v GEMM, whose epilogue runs k_norm + RoPE
+        # and writes K/V into the context cache)
+        ss = buf.ctx_sumsq[:c.hidden_size // 128 * M].view(M, c.hidden_size // 128)
+        ops.gemm(fused16, self.fc, buf.ctx_h, epilogue=EPI_STORE_BF16, scratch=sc, M=M,
+                 sumsq_out=ss)
+        hn = ops.RowNorm(self.hidden_norm, eps, ss)
         for l, L in enumerate(self.layers):
-            ops.gemm(buf.ctx_x16, L.kv, buf.ctx_kv, epilogue=EPI_STORE_BF16, scratch=sc, M=M)
-            ops.qkv_rope_kv_write(buf.ctx_kv, B, T, 0, c.num_key_value_heads, c.head_dim, None,
-                                  L.k_norm, c.rms_norm_eps, self.inv_freq, ctx.seq_len, None,
-                                  ctx.layout(l))
+            ops.gemm_qkv_rope(buf.ctx_h, L.kv, T=T, Hq=0, Hkv=c.num_key_value_heads,
+                              hd=c.head_dim, q_norm=None, k_norm=L.k_norm, eps=eps,
+                              inv_freq=self.inv_freq, pos0=ctx.seq_len, q_out=None,
+                              kv=ctx.layout(l), scratch=sc, M=M, norm=hn)
 
     def backbone_dev(self, pending: torch.Tensor, B: int, ctx: CacheState, buf: DraftBuffers,
-                     splits: int) -> None:
+                     splits: int, final_norm: bool = True) -> None:
         """Block [pending, mask x (k-1)] of each row at positions seq_len[b] + i -> layers over
-        [ctx; block] -> final norm into buf.xn16 (fp16, the head GEMM input)."""
+        [ctx; block] -> final norm into buf.xn16 (fp16, the head GEMM input). With
+        final_norm=False the block's hidden states stay in buf.h with their row sums of squares
+        in buf.sumsq, for a head GEMM that fuses the final norm (final_head_norm())."""
         c, sc = self.config, self.scratch
         k = self.block_size
         M = B * k
+        eps = c.rms_norm_eps
+        ss = buf.sumsq
         ops.embed_block(pending, B, k, self.mask_token_id, self.embed_w, buf.h, buf.ids)
         for l, L in enumerate(self.layers):
             kv = ctx.layout(l)
-            ops.rmsnorm(buf.h, L.input_ln, c.rms_norm_eps, y16=buf.xn16, M=M)
-            ops.gemm(buf.xn16, L.qkv, buf.qkv, epilogue=EPI_STORE_BF16, scratch=sc, M=M)
-            ops.qkv_rope_kv_write(buf.qkv, B, k, c.num_attention_heads, c.num_key_value_heads,
-                                  c.head_dim, L.q_norm, L.k_norm, c.rms_norm_eps, self.inv_freq,
-                                  ctx.seq_len, buf.q, kv)
+            if l == 0:
+                ops.rmsnorm(buf.h, L.input_ln, eps, y16=buf.xn16, M=M)
+                x, nrm = buf.xn16, None
+            else:
+                x, nrm = buf.h, ops.RowNorm(L.input_ln, eps, ss)
+            ops.gemm_qkv_rope(x, L.qkv, T=k, Hq=c.num_attention_heads,
+                              Hkv=c.num_key_value_heads, hd=c.head_dim, q_norm=L.q_norm,
+                              k_norm=L.k_norm, eps=eps, inv_freq=self.inv_freq, pos0=ctx.seq_len,
+                              q_out=buf.q, kv=kv, scratch=sc, M=M, norm=nrm)
             ops.attention(buf.q, B, k, c.num_attention_heads, kv, ctx.seq_len, False, c.scaling,
                           buf.attn16, splits, sc)
             ops.gemm(buf.attn16, L.o, buf.h, epilogue=EPI_RESIDUAL_BF16, residual=buf.h,
-                     scratch=sc, M=M)
-            ops.rmsnorm(buf.h, L.post_ln, c.rms_norm_eps, y16=buf.xn16, M=M)
-            ops.gemm(buf.xn16, L.gu, buf.act16, epilogue=EPI_SILU_MUL_F16, scratch=sc, M=M)
+                     scratch=sc, M=M, sumsq_out=ss)
+            ops.gemm(buf.h, L.gu, buf.act16, epilogue=EPI_SILU_MUL_F16, scratch=sc, M=M,
+                     norm=ops.RowNorm(L.post_ln, eps, ss))
             ops.gemm(buf.act16, L.down, buf.h, epilogue=EPI_RESIDUAL_BF16, residual=buf.h,
-                     scratch=sc, M=M)
-        ops.rmsnorm(buf.h, self.norm, c.rms_norm_eps, y16=buf.xn16, M=M)
+                     scratch=sc, M=M, sumsq_out=ss)
+        if final_norm:
+            ops.rmsnorm(buf.h, self.norm, eps, y16=buf.xn16, M=M)
+
+    def final_head_norm(self, buf: DraftBuffers) -> "ops.RowNorm":
+        """The final norm of a backbone_dev(final_norm=False) block, for the head GEMM."""
+        return ops.RowNorm(self.norm, self.config.rms_norm_eps, buf.sumsq)
 
     # ------------------------------------------------------------------ reference API
     def update_context(self, target_hidden_cat, ctx_offset, ctx_caches) -> None:
@@ -218,10 +239,10 @@ class DSparkDrafter(BlockDrafter):
         (generate.py:846-852,910) or a temperature draft keeping q (model.py:283-309)."""
         sc = self.scratch
         k = self.block_size
-        self.backbone_dev(pending, B, ctx, buf, splits)
+        self.backbone_dev(pending, B, ctx, buf, splits, final_norm=False)
         head_rows = cap if B == 1 else B * k
-        ops.gemm(buf.xn16, self.head_w, buf.base, epilogue=EPI_STORE_BF16, scratch=sc,
-                 M=head_rows)
+        ops.gemm(buf.h, self.head_w, buf.base, epilogue=EPI_STORE_BF16, scratch=sc,
+                 M=head_rows, norm=self.final_head_norm(buf))
         rows_per_b = cap if B == 1 else k
         sampled = sampling is not None and sampling.active
         m = self.markov_head

@@ -93,12 +93,12 @@ def gemm_plan(M: int, N: int, K: int) -> dict:
 
 class RowNorm:
     """An RMSNorm fused into the GEMM that consumes it: the weights, eps, and the per-tile row
-    sums of squares [N/128, M] (fp32) written by the residual GEMM that produced the input."""
+    sums of squares [M, N/128] (fp32) written by the GEMM that produced the input."""
 
     __slots__ = ("w", "eps", "sumsq")
 
     def __init__(self, w: torch.Tensor, eps: float, sumsq: torch.Tensor):
-        self.w, self.eps, self.sumsq = w, float(eps), sumsq
+        self.w, self.eps, self.sumsq = w, float(eps), sumsq  # sumsq [rows, N/128 tiles]
 
 
 def _opts(prefetch: PackedLinear | None, norm: RowNorm | None,
@@ -115,8 +115,9 @@ def _opts(prefetch: PackedLinear | None, norm: RowNorm | None,
     if norm is not None:
         o.norm_w = norm.w.data_ptr()
         o.norm_sumsq = norm.sumsq.data_ptr()
-        o.norm_tiles = norm.sumsq.shape[0]
+        o.norm_tiles = norm.sumsq.shape[1]
         o.norm_eps = norm.eps
+        o.norm_ld = norm.sumsq.stride(0)
     if sumsq_out is not None:
         o.row_sumsq = sumsq_out.data_ptr()
     return o
@@ -129,12 +130,14 @@ def gemm(x16: torch.Tensor, w: PackedLinear, y: torch.Tensor, *, epilogue=_lib.E
     """y = x16 @ W^T with the chosen epilogue (see include/dspark_b200.h). `prefetch`: the next
     projection's weights, warmed in L2 (up to PREFETCH_LIMIT bytes) during this GEMM's tail.
     `norm`: x16 is the bf16 residual stream and the GEMM consumes its RMSNorm. `sumsq_out`
-    (RESIDUAL_BF16 only): per-tile row sums of squares of y for the next fused norm."""
+    (STORE_BF16 / RESIDUAL_BF16): per-tile row sums of squares of y for the next fused norm."""
     _require_cuda(x16, y)
     M = x16.shape[0] if M is None else M
     K = w.K
     want = torch.bfloat16 if norm is not None else torch.float16
     assert x16.dtype == want and x16.shape[-1] >= K
+    if sumsq_out is not None:  # written as a packed [M, N/128] block
+        assert sumsq_out.is_contiguous() and tuple(sumsq_out.shape) == (M, w.N // 128)
     ws = scratch.get("gemm", gemm_workspace_bytes(M, w.N, K))
     if norm is None and sumsq_out is None and (prefetch is None or PREFETCH_LIMIT <= 0):
         call("dspark_w8a16_gemm", _p(x16), x16.stride(0), _p(w.q), _p(w.sb), M, w.N, K, _p(y),

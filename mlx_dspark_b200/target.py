@@ -66,7 +66,7 @@ class Buffers:
                        if logits else None)
         # per-128-column-tile row sums of squares of h, written by the residual GEMMs for the
         # RMSNorm fused into the next GEMM
-        self.sumsq = torch.zeros(H // 128, M, dtype=torch.float32, device=device)
+        self.sumsq = torch.zeros(M, H // 128, dtype=torch.float32, device=device)
 
 
 class Target:

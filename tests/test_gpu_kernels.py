@@ -167,13 +167,13 @@ def test_gemm_fused_rmsnorm_and_row_sumsq(cuda, M, H, N):
     x = _x16(M, Kd, 3).to(torch.float16).to(cuda)
     r0 = torch.randn(M, H, generator=torch.Generator().manual_seed(5)).to(torch.bfloat16)
     h = r0.clone().to(cuda)
-    ss = torch.zeros(H // 128, M, dtype=torch.float32, device=cuda)
+    ss = torch.zeros(M, H // 128, dtype=torch.float32, device=cuda)
     ops.gemm(x, pack(d, device=cuda), h, epilogue=EPI_RESIDUAL_BF16, residual=h, scratch=sc,
              sumsq_out=ss)
     torch.cuda.synchronize()
     sc.check_status()
     hf = h.float().cpu().double()
-    ref_ss = (hf ** 2).reshape(M, H // 128, 128).sum(-1).t()
+    ref_ss = (hf ** 2).reshape(M, H // 128, 128).sum(-1)
     assert torch.allclose(ss.cpu().double(), ref_ss, rtol=1e-5, atol=1e-6)
     eps = 1e-6
     w = (1 + 0.1 * torch.randn(H, generator=torch.Generator().manual_seed(6))).to(torch.bfloat16).to(cuda)
