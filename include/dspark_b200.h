@@ -106,7 +106,9 @@ int dspark_w8a16_gemm_pf(const void* x, int ldx, const uint8_t* wq, const uint32
  *     with r[m] = rsqrt(sum_t norm_sumsq[m, t] / K + eps), t in order, from the row_sumsq of the
  *     GEMM that wrote x (norm_tiles = its N/128; norm_ld = the row stride in floats, 0 meaning
  *     norm_tiles; 16-byte aligned rows when norm_ld % 4 == 0). The only difference from
- *     dspark_rmsnorm + this GEMM is the fp32 summation order of the squares. */
+ *     dspark_rmsnorm + this GEMM is the fp32 summation order of the squares.
+ *   copy_f16, copy_f16_ld: RESIDUAL_BF16 only; the epilogue also stores each bf16 output as fp16
+ *     (exact) at copy_f16[m * copy_f16_ld + n] (the drafter's hidden-state tap). */
 typedef struct dspark_gemm_opts {
   const void* prefetch[2];
   size_t prefetch_bytes[2];
@@ -117,6 +119,9 @@ typedef struct dspark_gemm_opts {
   float norm_eps;
   int norm_ld;
   int reserved;
+  void* copy_f16;   /* RESIDUAL_BF16 only: also store fp16(y) here (the hidden-state tap) */
+  int copy_f16_ld;  /* its row stride in elements */
+  int reserved2;
 } dspark_gemm_opts;
 int dspark_w8a16_gemm_ex(const void* x, int ldx, const uint8_t* wq, const uint32_t* wsb, int M,
                          int N, int K, void* y, int ldy, const void* residual, int ldr,
@@ -148,6 +153,12 @@ int dspark_w8a16_gemm_plan(int M, int N, int K, int* grid, int* cluster, int* ma
  * ------------------------------------------------------------------------------------- */
 int dspark_embed_w8(const int32_t* ids, int M, const uint8_t* wq, const uint32_t* wsb, int V,
                     int H, void* out, int ldo, dspark_stream_t stream);
+/* The same gather that also writes the per-128-column-tile row sums of squares of its bf16
+ * outputs, sumsq [M, H/128] (the row_sumsq of dspark_gemm_opts), so the first layer's input
+ * RMSNorm can run inside the q|k|v GEMM. H % 128 == 0. */
+int dspark_embed_w8_sumsq(const int32_t* ids, int M, const uint8_t* wq, const uint32_t* wsb,
+                          int V, int H, void* out, int ldo, float* sumsq,
+                          dspark_stream_t stream);
 
 /* -------------------------------------------------------------------------------------
  * K6 — RMSNorm over rows, mlx.fast.rms_norm semantics (fp32 math, one bf16 rounding).

@@ -52,7 +52,8 @@ class GemmOpts(ctypes.Structure):
     _fields_ = [("prefetch", c_void_p * 2), ("prefetch_bytes", c_size_t * 2),
                 ("row_sumsq", c_void_p), ("norm_sumsq", c_void_p), ("norm_w", c_void_p),
                 ("norm_tiles", c_int), ("norm_eps", c_float), ("norm_ld", c_int),
-                ("reserved", c_int)]
+                ("reserved", c_int), ("copy_f16", c_void_p), ("copy_f16_ld", c_int),
+                ("reserved2", c_int)]
 
 
 # name -> (restype, argtypes); mirrors include/dspark_b200.h
@@ -68,6 +69,7 @@ SIGNATURES = {
     "dspark_w8a16_gemm_split_mode": (I, [I]),
     "dspark_w8a16_gemm_plan": (I, [I, I, I, P, P, P]),
     "dspark_embed_w8": (I, [P, I, P, P, I, I, P, I, P]),
+    "dspark_embed_w8_sumsq": (I, [P, I, P, P, I, I, P, I, P, P]),
     "dspark_embed_block_w8": (I, [P, I, I, I, P, P, I, I, P, I, P, P]),
     "dspark_rmsnorm": (I, [P, I, P, I, I, c_float, P, I, P, I, P]),
     "dspark_kv_page_bytes": (c_longlong, [I, I, I, I]),

@@ -31,6 +31,39 @@ __global__ void __launch_bounds__(256) embed_w8_kernel(const int32_t* __restrict
   }
 }
 
+// the same gather, plus the per-128-column-tile sums of squares of the bf16 outputs
+// (sumsq[m, t]): warp w covers columns [128(w + 8j), 128(w + 8j) + 128) in pass j
+__global__ void __launch_bounds__(256) embed_w8_sumsq_kernel(const int32_t* __restrict__ ids,
+                                                             const uint8_t* __restrict__ wq,
+                                                             const uint32_t* __restrict__ wsb, int V,
+                                                             int H, __nv_bfloat16* __restrict__ out,
+                                                             int ldo, float* __restrict__ sumsq) {
+  pdl_enter();
+  const int m = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int id = ids[m];
+  id = id < 0 ? 0 : (id >= V ? V - 1 : id);
+  const uint8_t* row = wq + (size_t)id * H;
+  for (int k = threadIdx.x * 4; k < H; k += blockDim.x * 4) {
+    const uint32_t q4 = *reinterpret_cast<const uint32_t*>(row + k);
+    const uint32_t sbv = wsb[(size_t)(k >> 6) * V + id];
+    const __half2 sb = *reinterpret_cast<const __half2*>(&sbv);
+    const float s = __low2float(sb), b = __high2float(sb);
+    __nv_bfloat16 o[4];
+    float sq = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      o[j] = __float2bfloat16_rn(fmaf(s, (float)((q4 >> (8 * j)) & 0xFF), b));
+      const float v = __bfloat162float(o[j]);
+      sq += v * v;
+    }
+    *reinterpret_cast<uint2*>(out + (size_t)m * ldo + k) = *reinterpret_cast<const uint2*>(o);
+    sq = warp_sum(sq);
+    if (lane == 0) sumsq[(size_t)m * (H / 128) + (k - lane * 4) / 128] = sq;
+  }
+  (void)warp;
+}
+
 // drafter block embedding: row (b, i) embeds pending[b] for i == 0, else mask_id
 // (the block [pending, mask x (k-1)] of src/mlx_dspark/generate.py:848-849)
 __global__ void __launch_bounds__(256) embed_block_w8_kernel(const int32_t* __restrict__ pending,
@@ -139,6 +172,18 @@ extern "C" int dspark_embed_w8(const int32_t* ids, int M, const uint8_t* wq, con
   return launch_pdl("embed_w8", embed_w8_kernel, dim3(M), dim3(256), 0,
                     static_cast<cudaStream_t>(stream), ids, wq, wsb, V, H,
                     static_cast<__nv_bfloat16*>(out), ldo);
+}
+
+extern "C" int dspark_embed_w8_sumsq(const int32_t* ids, int M, const uint8_t* wq,
+                                     const uint32_t* wsb, int V, int H, void* out, int ldo,
+                                     float* sumsq, dspark_stream_t stream) {
+  if (!ids || !wq || !wsb || !out || !sumsq || M <= 0 || V <= 0 || H <= 0 || H % 128 || ldo < H ||
+      ldo % 4)
+    return set_error(DSPARK_ERR_INVALID, "embed_w8_sumsq: bad arguments (M=%d V=%d H=%d ldo=%d)", M,
+                     V, H, ldo);
+  return launch_pdl("embed_w8_sumsq", embed_w8_sumsq_kernel, dim3(M), dim3(256), 0,
+                    static_cast<cudaStream_t>(stream), ids, wq, wsb, V, H,
+                    static_cast<__nv_bfloat16*>(out), ldo, sumsq);
 }
 
 extern "C" int dspark_rmsnorm(const void* x, int ldx, const void* w, int M, int H, float eps,

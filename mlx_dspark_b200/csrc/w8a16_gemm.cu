@@ -93,6 +93,8 @@ struct Params {
   int ss_tiles;
   int ss_ld;  // row stride of ss_in in floats (>= ss_tiles)
   float norm_eps;
+  __half* copy16;  // RESIDUAL_BF16: fp16 copy of the output rows (tap), or null
+  int copy16_ld;
   // L2 prefetch of the next kernel's operands: CTA b warms bytes [b*chunk, (b+1)*chunk) of each
   // range after issuing its last load (16-byte aligned, sizes multiples of 16)
   const char* pf_ptr[2];
@@ -167,6 +169,7 @@ __device__ __forceinline__ void epilogue_store(const Params& p, int tile, int er
           if (c0 + j < p.M) {
             const __nv_bfloat16 o = __float2bfloat16_rn(__bfloat162float(rv[j]) + bf16_round(acc[c0 + j]));
             y[(size_t)(c0 + j) * p.ldy + n] = o;
+            if (p.copy16) p.copy16[(size_t)(c0 + j) * p.copy16_ld + n] = __float2half_rn(__bfloat162float(o));
             if (p.ss_out) {
               // this row's share of the next RMSNorm: warp sum, then the 4 warps in order
               const float v = __bfloat162float(o);
@@ -1716,6 +1719,12 @@ static int gemm_launch(const void* x, int ldx, const uint8_t* wq, const uint32_t
   p.status = status;
   if (rope) p.rope = *rope;
   if (opts) {
+    if (opts->copy_f16) {
+      if (epilogue != DSPARK_EPI_RESIDUAL_BF16 || opts->copy_f16_ld < N)
+        return set_error(DSPARK_ERR_INVALID, "w8a16_gemm: copy_f16 needs RESIDUAL_BF16 and ld >= N");
+      p.copy16 = static_cast<__half*>(opts->copy_f16);
+      p.copy16_ld = opts->copy_f16_ld;
+    }
     if (opts->row_sumsq) {
       if (epilogue != DSPARK_EPI_RESIDUAL_BF16 && epilogue != DSPARK_EPI_STORE_BF16)
         return set_error(DSPARK_ERR_INVALID,

@@ -102,8 +102,12 @@ class RowNorm:
 
 
 def _opts(prefetch: PackedLinear | None, norm: RowNorm | None,
-          sumsq_out: torch.Tensor | None) -> _lib.GemmOpts:
+          sumsq_out: torch.Tensor | None, copy16: torch.Tensor | None = None) -> _lib.GemmOpts:
     o = _lib.GemmOpts()
+    if copy16 is not None:
+        assert copy16.dtype == torch.float16 and copy16.stride(1) == 1
+        o.copy_f16 = copy16.data_ptr()
+        o.copy_f16_ld = copy16.stride(0)
     if prefetch is not None and PREFETCH_LIMIT > 0:
         # q is row-major [N, K]: a prefix of it is whole 128-row tiles. sb is [K/64, N] (1/16 of
         # q's bytes), so any prefix covers a few groups of every row: warm all of it, up to
@@ -126,11 +130,12 @@ def _opts(prefetch: PackedLinear | None, norm: RowNorm | None,
 def gemm(x16: torch.Tensor, w: PackedLinear, y: torch.Tensor, *, epilogue=_lib.EPI_STORE_BF16,
          residual: torch.Tensor | None = None, scratch: Scratch, M: int | None = None,
          prefetch: PackedLinear | None = None, norm: RowNorm | None = None,
-         sumsq_out: torch.Tensor | None = None) -> torch.Tensor:
+         sumsq_out: torch.Tensor | None = None, copy16: torch.Tensor | None = None) -> torch.Tensor:
     """y = x16 @ W^T with the chosen epilogue (see include/dspark_b200.h). `prefetch`: the next
     projection's weights, warmed in L2 (up to PREFETCH_LIMIT bytes) during this GEMM's tail.
     `norm`: x16 is the bf16 residual stream and the GEMM consumes its RMSNorm. `sumsq_out`
-    (STORE_BF16 / RESIDUAL_BF16): per-tile row sums of squares of y for the next fused norm."""
+    (STORE_BF16 / RESIDUAL_BF16): per-tile row sums of squares of y for the next fused norm.
+    `copy16` (RESIDUAL_BF16): an fp16 view [M, N] that also receives y (the hidden-state tap)."""
     _require_cuda(x16, y)
     M = x16.shape[0] if M is None else M
     K = w.K
@@ -139,12 +144,12 @@ def gemm(x16: torch.Tensor, w: PackedLinear, y: torch.Tensor, *, epilogue=_lib.E
     if sumsq_out is not None:  # written as a packed [M, N/128] block
         assert sumsq_out.is_contiguous() and tuple(sumsq_out.shape) == (M, w.N // 128)
     ws = scratch.get("gemm", gemm_workspace_bytes(M, w.N, K))
-    if norm is None and sumsq_out is None and (prefetch is None or PREFETCH_LIMIT <= 0):
+    if norm is None and sumsq_out is None and copy16 is None and (prefetch is None or PREFETCH_LIMIT <= 0):
         call("dspark_w8a16_gemm", _p(x16), x16.stride(0), _p(w.q), _p(w.sb), M, w.N, K, _p(y),
              y.stride(0), _p(residual), residual.stride(0) if residual is not None else 0,
              epilogue, _p(ws), ws.numel(), _p(scratch.status), _stream())
         return y
-    opts = _opts(prefetch, norm, sumsq_out)
+    opts = _opts(prefetch, norm, sumsq_out, copy16)
     call("dspark_w8a16_gemm_ex", _p(x16), x16.stride(0), _p(w.q), _p(w.sb), M, w.N, K, _p(y),
          y.stride(0), _p(residual), residual.stride(0) if residual is not None else 0, epilogue,
          ctypes.byref(opts), _p(ws), ws.numel(), _p(scratch.status), _stream())
@@ -178,9 +183,17 @@ def gemm_simt(x16, w: PackedLinear, y, *, epilogue=_lib.EPI_STORE_BF16, residual
     return y
 
 
-def embed(ids: torch.Tensor, w: PackedLinear, out: torch.Tensor, M: int | None = None) -> torch.Tensor:
+def embed(ids: torch.Tensor, w: PackedLinear, out: torch.Tensor, M: int | None = None,
+          sumsq: torch.Tensor | None = None) -> torch.Tensor:
+    """`sumsq` [M, H/128] fp32: also write the per-tile row sums of squares of the output (for
+    the first layer's fused input norm)."""
     _require_cuda(ids, out)
     M = ids.numel() if M is None else M
+    if sumsq is not None:
+        assert sumsq.is_contiguous() and tuple(sumsq.shape) == (M, w.K // 128)
+        call("dspark_embed_w8_sumsq", _p(ids), M, _p(w.q), _p(w.sb), w.N, w.K, _p(out),
+             out.stride(0), _p(sumsq), _stream())
+        return out
     call("dspark_embed_w8", _p(ids), M, _p(w.q), _p(w.sb), w.N, w.K, _p(out), out.stride(0), _stream())
     return out
 

@@ -164,16 +164,16 @@ class Target:
         splits = splits or self.attn_splits(B, state.max_pages)
         tap_idx = {l: j for j, l in enumerate(tap)}
         H = c.hidden_size
-        ops.embed(buf.ids, self.embed, buf.h, M)
         n_layers = len(self.layers)
         eps = c.rms_norm_eps
         fuse = self.fuse_norm
         ss = buf.sumsq if fuse else None
+        ops.embed(buf.ids, self.embed, buf.h, M, sumsq=ss)
         for l, L in enumerate(self.layers):
             kv = state.layout(l)
             # each GEMM warms L2 with the next GEMM's weights (the head after the last layer)
             nxt = self.layers[l + 1].qkv if l + 1 < n_layers else (self.head if with_logits else None)
-            if fuse and l > 0:
+            if fuse:
                 self._qkv_rope(buf, L, kv, state, B, T, M, x=buf.h,
                                norm=ops.RowNorm(L.input_ln, eps, ss))
             else:
@@ -190,11 +190,10 @@ class Target:
                 ops.rmsnorm(buf.h, L.post_ln, eps, y16=buf.xn16, M=M)
                 ops.gemm(buf.xn16, L.gu, buf.act16, epilogue=EPI_SILU_MUL_F16, scratch=sc, M=M,
                          prefetch=L.down)
+            # the drafter's tap of this layer's output is written by the same epilogue
+            tap16 = buf.fused16[:M, tap_idx[l] * H:(tap_idx[l] + 1) * H] if l in tap_idx else None
             ops.gemm(buf.act16, L.down, buf.h, epilogue=EPI_RESIDUAL_BF16, residual=buf.h,
-                     scratch=sc, M=M, prefetch=nxt, sumsq_out=ss)
-            if l in tap_idx:
-                j = tap_idx[l]
-                ops.bf16_to_f16(buf.h, buf.fused16[:, j * H:(j + 1) * H], M, H)
+                     scratch=sc, M=M, prefetch=nxt, sumsq_out=ss, copy16=tap16)
         if with_logits:
             if fuse:
                 ops.gemm(buf.h, self.head, buf.logits, epilogue=EPI_STORE_BF16, scratch=sc, M=M,

@@ -168,13 +168,16 @@ def test_gemm_fused_rmsnorm_and_row_sumsq(cuda, M, H, N):
     r0 = torch.randn(M, H, generator=torch.Generator().manual_seed(5)).to(torch.bfloat16)
     h = r0.clone().to(cuda)
     ss = torch.zeros(M, H // 128, dtype=torch.float32, device=cuda)
+    tap = torch.zeros(M, 2 * H, dtype=torch.float16, device=cuda)  # the copy lands in a column slice
     ops.gemm(x, pack(d, device=cuda), h, epilogue=EPI_RESIDUAL_BF16, residual=h, scratch=sc,
-             sumsq_out=ss)
+             sumsq_out=ss, copy16=tap[:, H:])
     torch.cuda.synchronize()
     sc.check_status()
     hf = h.float().cpu().double()
     ref_ss = (hf ** 2).reshape(M, H // 128, 128).sum(-1)
     assert torch.allclose(ss.cpu().double(), ref_ss, rtol=1e-5, atol=1e-6)
+    assert torch.equal(tap[:, H:].cpu(), h.cpu().to(torch.float16))
+    assert not tap[:, :H].any()
     eps = 1e-6
     w = (1 + 0.1 * torch.randn(H, generator=torch.Generator().manual_seed(6))).to(torch.bfloat16).to(cuda)
     qt = _qrand(N, H, 12)
@@ -215,7 +218,15 @@ def test_rmsnorm_and_embed(cuda):
     emb = _qrand(V, H, 11)
     ids = torch.tensor([0, 5, V - 1, 17, 17, 4000, 3, 2, 1], dtype=torch.int32)
     out = torch.zeros(len(ids), H, dtype=torch.bfloat16, device=cuda)
+    # the gather with per-tile row sums of squares equals the plain gather
+    out_s = torch.zeros_like(out)
+    ss = torch.zeros(len(ids), H // 128, dtype=torch.float32, device=cuda)
+    ops.embed(ids.to(cuda), pack(emb, device=cuda), out_s, sumsq=ss)
     ops.embed(ids.to(cuda), pack(emb, device=cuda), out)
+    torch.cuda.synchronize()
+    assert torch.equal(out_s, out)
+    ref_ss = (out.float().cpu().double() ** 2).reshape(len(ids), H // 128, 128).sum(-1)
+    assert torch.allclose(ss.cpu().double(), ref_ss, rtol=1e-5, atol=1e-6)
     ref = oq.bf(emb.dequant()[ids.long()])
     torch.cuda.synchronize()
     assert torch.allclose(out.float().cpu(), ref, rtol=2 ** -8, atol=1e-7)
@@ -260,9 +271,10 @@ def test_qkv_rope_kv_write(cuda, hd, kv8):
     pool, st = _pool_and_state(cuda, Hkv, hd, kv8, B, 256)
     pos0 = torch.tensor([60, 3], dtype=torch.int32)  # row 0 straddles a page boundary
     st.seq_len.copy_(pos0.to(cuda))
-    qkv = torch.randn(B * T, (Hq + 2 * Hkv) * hd).to(torch.bfloat16)
-    qn = (1 + 0.1 * torch.randn(hd)).to(torch.bfloat16)
-    kn = (1 + 0.1 * torch.randn(hd)).to(torch.bfloat16)
+    g = torch.Generator().manual_seed(hd + 2 * int(kv8))
+    qkv = torch.randn(B * T, (Hq + 2 * Hkv) * hd, generator=g).to(torch.bfloat16)
+    qn = (1 + 0.1 * torch.randn(hd, generator=g)).to(torch.bfloat16)
+    kn = (1 + 0.1 * torch.randn(hd, generator=g)).to(torch.bfloat16)
     freqs = oq.inv_freq(hd, 1e6)
     q_out = torch.zeros(B * T, Hq * hd, dtype=torch.bfloat16, device=cuda)
     ops.qkv_rope_kv_write(qkv.to(cuda), B, T, Hq, Hkv, hd, qn.to(cuda), kn.to(cuda), eps,
@@ -277,7 +289,10 @@ def test_qkv_rope_kv_write(cuda, hd, kv8):
         q = oq.rope(oq.rms_norm(q, qn, eps), pos, freqs)
         k = oq.rope(oq.rms_norm(k, kn, eps), pos, freqs)
         gq = q_out[b * T:(b + 1) * T].float().cpu().reshape(T, Hq, hd).transpose(0, 1)
-        assert torch.allclose(gq, q, rtol=2 ** -6, atol=1e-5), (gq - q).abs().max()
+        # x*cos - y*sin can cancel: a small output carries the absolute rounding of its terms,
+        # so the absolute part of the tolerance follows the head's magnitude
+        tol = 2 ** -6 * q.abs() + 2 ** -8 * q.abs().amax(-1, keepdim=True) + 1e-5
+        assert ((gq - q).abs() <= tol).all(), (gq - q).abs().max()
         K, V = _read_kv(pool, st, b, int(pos0[b]) + T, Hkv, hd)
         Kn, Vn = K[:, int(pos0[b]):], V[:, int(pos0[b]):]
         if kv8:
@@ -287,7 +302,8 @@ def test_qkv_rope_kv_write(cuda, hd, kv8):
             assert ((Kn - k).abs() <= tol_k * 1.01).all()
             assert torch.equal(Vn, v), (Vn - v).abs().max()
         else:
-            assert torch.allclose(Kn, k, rtol=2 ** -6, atol=1e-5)
+            ktol = 2 ** -6 * k.abs() + 2 ** -8 * k.abs().amax(-1, keepdim=True) + 1e-5
+            assert ((Kn - k).abs() <= ktol).all(), (Kn - k).abs().max()
             assert torch.equal(Vn, v)
 
 
@@ -458,7 +474,7 @@ def test_markov_sample_block(cuda):
     from oracle.dspark import DSparkRef
     V, R, cap = 4096, 256, 6
     w1, w2 = _qrand(V, R, 21), _qrand(V, R, 22)
-    base = (torch.randn(cap, V) * 0.01).to(torch.bfloat16)
+    base = (torch.randn(cap, V, generator=torch.Generator().manual_seed(23)) * 0.01).to(torch.bfloat16)
 
     class W:  # the oracle only reads markov_w1/markov_w2 here
         markov_w1, markov_w2 = w1, w2
