@@ -283,18 +283,23 @@ int dspark_w8a16_gemm_qkv_rope(const void* x, int ldx, const uint8_t* wq, const 
  * q   : bf16 [B*T, Hq*hd]; out: fp16 [B*T, ldo] (bf16-rounded, the o_proj GEMM input)
  * workspace: dspark_attention_workspace_bytes(...) bytes for the split partials.
  * Splits (at most max_splits, at least one page each) are merged in split order in one of
- * two forms:
- *   - two launches (default): partials in the workspace, merged by a second kernel; with one
- *     split the first launch writes the output directly;
- *   - one launch, cluster form (merge mode 1): the S splits of a (row, kv head) run as one
- *     thread-block cluster (S a power of two <= 16) and merge through distributed shared
- *     memory; used when the block table has at most 4 pages per split and B*Hkv clusters are
- *     resident at once, else the two-launch form. Slower on B200 (clusters cannot start on SMs
- *     as the previous kernel drains).
+ * three forms (with one split the attention launch writes the output directly):
+ *   - two launches (merge mode 0, default): partials merged by a second kernel;
+ *   - one launch (mode 2, when status is non-NULL and max_splits*Hkv*B CTAs fit on the device
+ *     at once, else two launches): each split stores its partial, waits (bounded:
+ *     DSPARK_ERR_TIMEOUT in *status) until its siblings have, then finishes a slice of the
+ *     query rows with the same arithmetic as the second kernel; no faster on B200 (PDL hides
+ *     the second launch);
+ *   - one launch, cluster form (mode 1): the S splits of a (row, kv head) run as one thread
+ *     block cluster (S a power of two <= 16) and merge through distributed shared memory; used
+ *     when the block table has at most 4 pages per split and B*Hkv clusters are resident at
+ *     once, else two launches. Slower on B200 (clusters cannot start on SMs as the previous
+ *     kernel drains).
  * ------------------------------------------------------------------------------------- */
 size_t dspark_attention_workspace_bytes(int B, int T, int Hq, int Hkv, int hd, int max_splits);
 /* Process-wide choice of the merge form: 0 (default) two launches, 1 cluster form where it
- * applies (no reference counterpart; for A/B parity tests and measurements). */
+ * applies, 2 in-kernel where it applies (no reference counterpart; for A/B tests and
+ * measurements). */
 int dspark_attention_merge_mode(int mode);
 int dspark_attention(const void* q, int B, int T, int Hq, const dspark_kv_layout* kv,
                      const int32_t* kv_len, int causal, float scale, void* out, int ldo,

@@ -85,8 +85,58 @@ struct Args {
   int ldo;
   float* ws_o;   // [B*Hkv][nsplit][R][HD]
   float* ws_ml;  // [B*Hkv][nsplit][R][2]
-  int* counters; // [B*Hkv]
+  int* counters; // [B*Hkv] arrivals, then [B*Hkv] merges done (in-kernel merge form)
+  int* status;   // DSPARK_ERR_TIMEOUT if a bounded wait runs out
+  int merge_inline;
 };
+
+constexpr int kMaxBH = 4096;  // B*Hkv rows of counters
+
+// One query row of the merge: lanes over the head dimension, splits in order (max, then the
+// rescaled sums and O), bf16-rounded output written as fp16.
+template <int HD>
+__device__ __forceinline__ void merge_row(const Args& a, int b, int h, int r, int nsplit, int lane) {
+  constexpr int E = HD / 32;
+  const int bh = b * a.kv.num_kv_heads + h;
+  const size_t base0 = (size_t)bh * a.nsplit * a.R;
+  float M = -INFINITY;
+  for (int sp = lane; sp < nsplit; sp += 32)
+    M = fmaxf(M, __ldcg(a.ws_ml + (base0 + (size_t)sp * a.R + r) * 2));
+  M = warp_max(M);
+  float Ls = 0.0f;
+  for (int sp = lane; sp < nsplit; sp += 32) {
+    const float ms = __ldcg(a.ws_ml + (base0 + (size_t)sp * a.R + r) * 2);
+    if (ms != -INFINITY) Ls += __ldcg(a.ws_ml + (base0 + (size_t)sp * a.R + r) * 2 + 1) * exp2f(ms - M);
+  }
+  Ls = warp_sum(Ls);
+  float acc[E];
+#pragma unroll
+  for (int k = 0; k < E; ++k) acc[k] = 0.0f;
+#pragma unroll 4
+  for (int sp = 0; sp < nsplit; ++sp) {
+    const size_t row = base0 + (size_t)sp * a.R + r;
+    const float ms = __ldcg(a.ws_ml + row * 2);
+    const float e = ms == -INFINITY ? 0.0f : exp2f(ms - M);  // empty splits hold zeros
+    const float* src = a.ws_o + row * HD + lane * E;
+    float v[E];
+    if constexpr (E == 4) {
+      const float4 t = __ldcg(reinterpret_cast<const float4*>(src));
+      v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+    } else {
+      const float2 t = __ldcg(reinterpret_cast<const float2*>(src));
+      v[0] = t.x; v[1] = t.y;
+    }
+#pragma unroll
+    for (int k = 0; k < E; ++k) acc[k] = fmaf(e, v[k], acc[k]);
+  }
+  const float inv = Ls > 0.0f ? 1.0f / Ls : 0.0f;
+  const int t = r % a.T, g = r / a.T;
+  __half* dst = a.out + (size_t)(b * a.T + t) * a.ldo + (size_t)(h * a.G + g) * HD + lane * E;
+#pragma unroll
+  for (int k = 0; k < E; k += 2)
+    *reinterpret_cast<__half2*>(dst + k) =
+        __floats2half2_rn(bf16_round(acc[k] * inv), bf16_round(acc[k + 1] * inv));
+}
 
 template <int HD, bool KV8>
 __device__ __forceinline__ void issue_tile(const Args& a, uint8_t* buf, int b, int h, int page) {
@@ -370,6 +420,48 @@ __global__ void __launch_bounds__(256) attn_kernel(const Args a) {
     if (r0 < a.R) *reinterpret_cast<float2*>(a.ws_o + (sbase + r0) * HD + d) = make_float2(o[j][0], o[j][1]);
     if (r1 < a.R) *reinterpret_cast<float2*>(a.ws_o + (sbase + r1) * HD + d) = make_float2(o[j][2], o[j][3]);
   }
+  if (!a.merge_inline) return;  // attn_combine_kernel merges
+  // In-kernel merge: every active split of (row, kv head) announces its partial, waits until
+  // all have (they are resident together: the host launches this form only when the whole grid
+  // fits on the device at once, and no CTA of it waits on a later kernel), then finishes rows
+  // [split*R/nsplit, (split+1)*R/nsplit). The wait is bounded and reports DSPARK_ERR_TIMEOUT.
+  __shared__ int timed_out;
+  __syncthreads();  // every thread's partial stores precede the release below
+  if (threadIdx.x == 0) {
+    timed_out = 0;
+    int old;
+    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(a.counters + bh) : "memory");
+    if (old != nsplit - 1) {
+      const unsigned long long t0 = globaltimer_ns();
+      while (true) {
+        int v;
+        asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(a.counters + bh) : "memory");
+        if (v >= nsplit) break;
+        if (globaltimer_ns() - t0 > kSpinLimitNs) {
+          report_error(a.status, DSPARK_ERR_TIMEOUT);
+          timed_out = 1;
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+  }
+  __syncthreads();
+  if (!timed_out) {
+    const int rlo = split * a.R / nsplit, rhi = (split + 1) * a.R / nsplit;
+    const int nwarps = blockDim.x >> 5;
+    for (int r = rlo + warp; r < rhi; r += nwarps) merge_row<HD>(a, b, h, r, nsplit, lane);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    // the last split to finish its rows rearms both counters for the next launch (every
+    // sibling has left its wait by then)
+    const int done = atomicAdd(a.counters + kMaxBH + bh, 1);
+    if (done == nsplit - 1) {
+      a.counters[bh] = 0;
+      a.counters[kMaxBH + bh] = 0;
+    }
+  }
 }
 
 // Merge of the split partials: one warp per query row (8 rows per CTA), every (row, kv head,
@@ -378,7 +470,6 @@ __global__ void __launch_bounds__(256) attn_kernel(const Args a) {
 template <int HD>
 __global__ void __launch_bounds__(256) attn_combine_kernel(const Args a) {
   pdl_enter();
-  constexpr int E = HD / 32;  // output dims per lane
   const int h = blockIdx.y, b = blockIdx.z;
   const int kvlen = a.kv_len[b];
   const int npages = (kvlen + a.T + KT - 1) / KT;
@@ -387,55 +478,40 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const Args a) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = blockIdx.x * 8 + warp;
   if (r >= a.R) return;
-  const int bh = b * a.kv.num_kv_heads + h;
-  const size_t base0 = (size_t)bh * a.nsplit * a.R;
-  float M = -INFINITY;
-  for (int sp = lane; sp < nsplit; sp += 32)
-    M = fmaxf(M, __ldcg(a.ws_ml + (base0 + (size_t)sp * a.R + r) * 2));
-  M = warp_max(M);
-  float Ls = 0.0f;
-  for (int sp = lane; sp < nsplit; sp += 32) {
-    const float ms = __ldcg(a.ws_ml + (base0 + (size_t)sp * a.R + r) * 2);
-    if (ms != -INFINITY) Ls += __ldcg(a.ws_ml + (base0 + (size_t)sp * a.R + r) * 2 + 1) * exp2f(ms - M);
-  }
-  Ls = warp_sum(Ls);
-  float acc[E];
-#pragma unroll
-  for (int k = 0; k < E; ++k) acc[k] = 0.0f;
-#pragma unroll 4
-  for (int sp = 0; sp < nsplit; ++sp) {
-    const size_t row = base0 + (size_t)sp * a.R + r;
-    const float ms = __ldcg(a.ws_ml + row * 2);
-    const float e = ms == -INFINITY ? 0.0f : exp2f(ms - M);  // empty splits hold zeros
-    const float* src = a.ws_o + row * HD + lane * E;
-    float v[E];
-    if constexpr (E == 4) {
-      const float4 t = __ldcg(reinterpret_cast<const float4*>(src));
-      v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
-    } else {
-      const float2 t = __ldcg(reinterpret_cast<const float2*>(src));
-      v[0] = t.x; v[1] = t.y;
-    }
-#pragma unroll
-    for (int k = 0; k < E; ++k) acc[k] = fmaf(e, v[k], acc[k]);
-  }
-  const float inv = Ls > 0.0f ? 1.0f / Ls : 0.0f;
-  const int t = r % a.T, g = r / a.T;
-  __half* dst = a.out + (size_t)(b * a.T + t) * a.ldo + (size_t)(h * a.G + g) * HD + lane * E;
-#pragma unroll
-  for (int k = 0; k < E; k += 2)
-    *reinterpret_cast<__half2*>(dst + k) =
-        __floats2half2_rn(bf16_round(acc[k] * inv), bf16_round(acc[k + 1] * inv));
+  merge_row<HD>(a, b, h, r, nsplit, lane);
 }
 
 // Cluster form limits: at most this many block-table pages per split (longer contexts keep
 // more splits than one cluster holds), and one wave of clusters.
 constexpr int kClusterPagesPerSplit = 4;
-// 0 (default): two-kernel form; 1: cluster form where it fits. Measured on B200 at C2 (verify
-// attention, 18 pages, 8 kv heads, us per call in a chain of 36): cluster form (16-CTA clusters,
-// 2 pages per split) 16.9, two-kernel form (37 splits) 11.4. A cluster starts only when all of its
-// CTAs fit in one GPC at once, so it cannot fill SMs as the previous kernel drains.
+// 0 (default): two kernels; 1: cluster form where it fits; 2: in-kernel merge where the grid
+// fits the device at once, else two kernels. Measured on B200 at C2 (verify attention, 18 pages,
+// 8 kv heads, us per call in a chain of 36): two kernels (37 splits) 11.4-11.6, in-kernel merge
+// 11.4, cluster form (16-CTA clusters, 2 pages per split) 16.9. PDL already hides the second
+// launch; a cluster starts only when all of its CTAs fit in one GPC at once, so it cannot fill
+// SMs as the previous kernel drains.
 static int g_merge_mode = 0;
+
+// CTAs of kernel k resident on the whole device at once (cached per kernel, block, smem)
+template <typename K>
+static int resident_ctas(K k, int threads, int smem) {
+  struct Entry { const void* k; int threads, smem, n; };
+  static Entry cache[32];
+  static int used = 0;
+  for (int i = 0; i < used; ++i)
+    if (cache[i].k == (const void*)k && cache[i].threads == threads && cache[i].smem == smem)
+      return cache[i].n;
+  int per_sm = 0, dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, threads, (size_t)smem) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;  // not cached: asked again next time
+  }
+  const int n = per_sm * sms;
+  if (used < 32) cache[used++] = Entry{(const void*)k, threads, smem, n};
+  return n;
+}
 
 // Max resident clusters of `size` CTAs of kernel k (cached per kernel, size, block and shared
 // memory; 0 if the query fails or the size needs an attribute the device refuses).
@@ -498,8 +574,9 @@ static int launch_cluster(K k, dim3 grid, dim3 block, int smem, int size, cudaSt
 static size_t ws_layout(int B, int T, int Hq, int Hkv, int hd, int nsplit, size_t* off_ml,
                         size_t* off_o) {
   const int R = (Hq / Hkv) * T;
-  // fixed-size counter region first: calls of other (B, Hkv) never overlap it with data
-  const size_t counters = 4096 * sizeof(int);
+  // fixed-size counter region first (arrivals, merges done): calls of other (B, Hkv) never
+  // overlap it with data
+  const size_t counters = 2 * kMaxBH * sizeof(int);
   const size_t ml = (((size_t)B * Hkv * nsplit * R * 2 * sizeof(float)) + 255) & ~(size_t)255;
   const size_t o = (size_t)B * Hkv * nsplit * R * hd * sizeof(float);
   if (off_ml) *off_ml = counters;
@@ -513,7 +590,7 @@ static size_t ws_layout(int B, int T, int Hq, int Hkv, int hd, int nsplit, size_
 using namespace dspark;
 
 extern "C" int dspark_attention_merge_mode(int mode) {
-  if (mode < 0 || mode > 1) return set_error(DSPARK_ERR_INVALID, "attention_merge_mode: %d", mode);
+  if (mode < 0 || mode > 2) return set_error(DSPARK_ERR_INVALID, "attention_merge_mode: %d", mode);
   attn::g_merge_mode = mode;
   return DSPARK_OK;
 }
@@ -528,7 +605,6 @@ extern "C" int dspark_attention(const void* q, int B, int T, int Hq, const dspar
                                 const int32_t* kv_len, int causal, float scale, void* out, int ldo,
                                 int max_splits, void* workspace, size_t workspace_bytes,
                                 int* status, dspark_stream_t stream) {
-  (void)status;
   if (!q || !kv || !kv->pool || !kv->block_table || !kv_len || !out || B <= 0 || T <= 0 || Hq <= 0)
     return set_error(DSPARK_ERR_INVALID, "attention: bad arguments");
   const int Hkv = kv->num_kv_heads, hd = kv->head_dim;
@@ -542,7 +618,7 @@ extern "C" int dspark_attention(const void* q, int B, int T, int Hq, const dspar
   if (R > 128) return set_error(DSPARK_ERR_UNSUPPORTED, "attention: %d query rows per kv head > 128", R);
   if (ldo < Hq * hd || ldo % 4) return set_error(DSPARK_ERR_INVALID, "attention: ldo");
   if (max_splits < 1 || max_splits > 256) return set_error(DSPARK_ERR_INVALID, "attention: max_splits");
-  if (B * Hkv > 4096) return set_error(DSPARK_ERR_UNSUPPORTED, "attention: B*Hkv > 4096");
+  if (B * Hkv > attn::kMaxBH) return set_error(DSPARK_ERR_UNSUPPORTED, "attention: B*Hkv > %d", attn::kMaxBH);
   size_t off_ml, off_o;
   const size_t need = attn::ws_layout(B, T, Hq, Hkv, hd, max_splits, &off_ml, &off_o);
   if (!workspace || workspace_bytes < need)
@@ -556,6 +632,8 @@ extern "C" int dspark_attention(const void* q, int B, int T, int Hq, const dspar
   a.out = static_cast<__half*>(out);
   a.ldo = ldo;
   a.counters = static_cast<int*>(workspace);
+  a.status = status;
+  a.merge_inline = 0;
   a.ws_ml = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + off_ml);
   a.ws_o = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + off_o);
   const int warps = (R + 15) / 16;
@@ -574,8 +652,13 @@ extern "C" int dspark_attention(const void* q, int B, int T, int Hq, const dspar
     }
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
       return set_error(DSPARK_ERR_CUDA, "attention: cudaFuncSetAttribute failed");
+    // in-kernel merge: the splits wait for one another, so the whole grid must be resident at
+    // once, and a status word must take a timed-out wait
+    a.merge_inline = (attn::g_merge_mode == 2 && max_splits > 1 && status &&
+                      (long long)max_splits * Hkv * B <= attn::resident_ctas(kern, (int)block.x, smem))
+                         ? 1 : 0;
     int rc = launch_pdl("attention", kern, grid, block, (size_t)smem, st, a);
-    if (rc || max_splits == 1) return rc;
+    if (rc || max_splits == 1 || a.merge_inline) return rc;
     return launch_pdl("attention.combine", combine, dim3((R + 7) / 8, Hkv, B), dim3(256), 0, st, a);
   };
   using namespace attn;

@@ -76,8 +76,9 @@ def gemm_split_mode(mode: int) -> None:
 
 
 def attention_merge_mode(mode: int) -> None:
-    """0: split-KV partials merged by a second launch (default); 1: inside one cluster launch
-    where it applies. Process-wide; captured graphs keep their form."""
+    """0 (default): split-KV partials merged by a second launch; 1: inside one cluster launch
+    where it applies; 2: inside the attention launch where its grid fits the device at once.
+    Process-wide; captured graphs keep their form."""
     _lib.check(_lib.lib().dspark_attention_merge_mode(int(mode)), "attention_merge_mode")
 
 

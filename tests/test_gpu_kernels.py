@@ -386,17 +386,24 @@ def test_attention_paged(cuda, hd, kv8, causal, T, lens):
     ops.attention(q.to(cuda), B, T, Hq, st.layout(0), st.seq_len, causal, hd ** -0.5, out,
                   splits, sc)
     torch.cuda.synchronize()
-    # the cluster merge form on the same inputs (where it applies; the default is two launches):
-    # both must match the oracle; they split the pages differently, so P's bf16 rounding per
-    # split makes them differ by a few output ulps, not bitwise
+    # the other merge forms on the same inputs (the default merges in a second launch): the
+    # cluster form (mode 1, where it applies) splits the pages differently, so P's bf16 rounding
+    # per split makes it differ by a few output ulps; the in-kernel merge (mode 2) performs the
+    # same arithmetic as the default, bit for bit
     out3 = torch.zeros_like(out)
+    out4 = torch.zeros_like(out)
     try:
         ops.attention_merge_mode(1)
         ops.attention(q.to(cuda), B, T, Hq, st.layout(0), st.seq_len, causal, hd ** -0.5, out3,
                       splits, sc)
+        ops.attention_merge_mode(2)
+        ops.attention(q.to(cuda), B, T, Hq, st.layout(0), st.seq_len, causal, hd ** -0.5, out4,
+                      splits, sc)
         torch.cuda.synchronize()
+        sc.check_status()
     finally:
         ops.attention_merge_mode(0)
+    assert torch.equal(out4, out)
     for b, L in enumerate(lens):
         K, V = _read_kv(pool, st, b, L + T, Hkv, hd)
         qb = q[b * T:(b + 1) * T].float().reshape(T, Hq, hd).transpose(0, 1)
