@@ -64,68 +64,99 @@ __global__ void __launch_bounds__(kThreads) markov_step_kernel(
   }
   __syncthreads();
   // w2 . e = sum_g (s_g * sum_{r in g} q_r e_r + b_g * sum_{r in g} e_r)
-  if (threadIdx.x < NB * kG) {
-    const int b = threadIdx.x / kG, g = threadIdx.x % kG;
-    float s = 0.0f;
-    for (int r = 0; r < 64; ++r) s += e[b][g * 64 + r];
-    esum[b][g] = s;
+  // group sums of e: one warp per (b, g), a fixed tree
+  for (int bg = warp; bg < NB * kG; bg += kThreads / 32) {
+    const int b = bg / kG, g = bg % kG;
+    float s = warp_sum(e[b][g * 64 + lane] + e[b][g * 64 + 32 + lane]);
+    if (lane == 0) esum[b][g] = s;
   }
   __syncthreads();
   Best best[NB];
 #pragma unroll
   for (int b = 0; b < NB; ++b) best[b] = Best{-INFINITY, 0x7fffffff};
-  const int nthr = gridDim.x * kThreads;
-  for (int v = blockIdx.x * kThreads + threadIdx.x; v < V; v += nthr) {
-    const uint4* rowp = reinterpret_cast<const uint4*>(w2q + (size_t)v * kR);
-    uint4 q[kR / 16];
+  // w2 . e, one warp per 8 vocabulary rows at a time: lane l reads bytes [8l, 8l + 8) of each
+  // row (one coalesced 256-byte row per warp load, 8 rows in flight) and forms its 8-term
+  // partial; the 8 lanes of each 64-wide group combine by a reduce-scatter (lane k & 7 ends
+  // with row k's group sum), and lane k then adds the groups in order:
+  //   d = fma(s_g, qsum_g, fma(b_g, esum_g, d)), g = 0..3
+  const int lane8 = lane & 7, grp = lane >> 3;
+  const int gwarp = blockIdx.x * (kThreads / 32) + warp;
+  const int nwarp = gridDim.x * (kThreads / 32);
+  for (int v0 = gwarp * 8; v0 < V; v0 += nwarp * 8) {
+    uint2 q8[8];
+    uint32_t sbk = 0;
 #pragma unroll
-    for (int j = 0; j < kR / 16; ++j) q[j] = __ldg(rowp + j);
-    uint32_t sbv[kG];
-#pragma unroll
-    for (int g = 0; g < kG; ++g) sbv[g] = __ldg(w2sb + (size_t)g * V + v);
-    float d[NB];
-#pragma unroll
-    for (int b = 0; b < NB; ++b) d[b] = 0.0f;
-#pragma unroll
-    for (int g = 0; g < kG; ++g) {
-      float qd[NB];
-#pragma unroll
-      for (int b = 0; b < NB; ++b) qd[b] = 0.0f;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint32_t words[4] = {q[g * 4 + j].x, q[g * 4 + j].y, q[g * 4 + j].z, q[g * 4 + j].w};
-#pragma unroll
-        for (int wi = 0; wi < 4; ++wi) {
-          const int r0 = g * 64 + j * 16 + wi * 4;
-          float ev[NB][4];
-#pragma unroll
-          for (int b = 0; b < NB; ++b) {
-            const float4 t = *reinterpret_cast<const float4*>(&e[b][r0]);
-            ev[b][0] = t.x; ev[b][1] = t.y; ev[b][2] = t.z; ev[b][3] = t.w;
-          }
-#pragma unroll
-          for (int by = 0; by < 4; ++by) {
-            // exact byte -> float: the fp32 bit pattern of 2^23 + q, minus 2^23
-            const float qf =
-                __uint_as_float(__byte_perm(words[wi], 0x4B000000u, 0x7650 + by)) - 8388608.0f;
-#pragma unroll
-            for (int b = 0; b < NB; ++b) qd[b] = fmaf(qf, ev[b][by], qd[b]);
-          }
-        }
-      }
-      const __half2 sb = *reinterpret_cast<const __half2*>(&sbv[g]);
-      const float s = __low2float(sb), bb = __high2float(sb);
-#pragma unroll
-      for (int b = 0; b < NB; ++b) d[b] = fmaf(s, qd[b], fmaf(bb, esum[b][g], d[b]));
+    for (int k = 0; k < 8; ++k) {
+      const int v = min(v0 + k, V - 1);  // rows past V: any valid row, result discarded
+      q8[k] = __ldg(reinterpret_cast<const uint2*>(w2q + (size_t)v * kR) + lane);
+    }
+    {
+      const int v = min(v0 + lane8, V - 1);  // this lane's (row k = lane & 7, group) scale/bias
+      sbk = __ldg(w2sb + (size_t)grp * V + v);
     }
 #pragma unroll
     for (int b = 0; b < NB; ++b) {
-      const float logit =
-          bf16_round(__bfloat162float(base[(size_t)(b * rows_per_b + step) * ld + v]) + bf16_round(d[b]));
-      if (SAMPLE)
-        out[(size_t)b * ld_out + v] = __float2bfloat16_rn(logit);
-      else
-        best[b] = better(best[b], Best{logit, v});
+      float ev[8];  // this lane's 8 columns of e_b (shared memory; registers stay free at large B)
+      {
+        const float4 t0 = *reinterpret_cast<const float4*>(&e[b][lane * 8]);
+        const float4 t1 = *reinterpret_cast<const float4*>(&e[b][lane * 8 + 4]);
+        ev[0] = t0.x; ev[1] = t0.y; ev[2] = t0.z; ev[3] = t0.w;
+        ev[4] = t1.x; ev[5] = t1.y; ev[6] = t1.z; ev[7] = t1.w;
+      }
+      float x[8];  // this lane's partial of every row of the batch
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const uint32_t w0 = q8[k].x, w1 = q8[k].y;
+        float acc = 0.0f;
+#pragma unroll
+        for (int by = 0; by < 4; ++by) {
+          // exact byte -> float: the fp32 bit pattern of 2^23 + q, minus 2^23
+          acc = fmaf(__uint_as_float(__byte_perm(w0, 0x4B000000u, 0x7650 + by)) - 8388608.0f, ev[by], acc);
+        }
+#pragma unroll
+        for (int by = 0; by < 4; ++by)
+          acc = fmaf(__uint_as_float(__byte_perm(w1, 0x4B000000u, 0x7650 + by)) - 8388608.0f, ev[4 + by], acc);
+        x[k] = acc;
+      }
+      // reduce-scatter over the group's 8 lanes: keep the half of the rows matching each lane bit
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const bool hi = lane & 4;
+        const float send = hi ? x[i] : x[i + 4];
+        const float keep = hi ? x[i + 4] : x[i];
+        x[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+      }
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const bool hi = lane & 2;
+        const float send = hi ? x[i] : x[i + 2];
+        const float keep = hi ? x[i + 2] : x[i];
+        x[i] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+      }
+      {
+        const bool hi = lane & 1;
+        const float send = hi ? x[0] : x[1];
+        const float keep = hi ? x[1] : x[0];
+        x[0] = keep + __shfl_xor_sync(0xffffffffu, send, 1);
+      }
+      // x[0] = group grp's sum of row v0 + lane8; lane lane8 gathers the 4 groups in order
+      float d = 0.0f;
+#pragma unroll
+      for (int g = 0; g < kG; ++g) {
+        const float qs = __shfl_sync(0xffffffffu, x[0], g * 8 + lane8);
+        const uint32_t sbv = __shfl_sync(0xffffffffu, sbk, g * 8 + lane8);
+        const __half2 sb = *reinterpret_cast<const __half2*>(&sbv);
+        d = fmaf(__low2float(sb), qs, fmaf(__high2float(sb), esum[b][g], d));
+      }
+      const int v = v0 + lane8;
+      if (lane < 8 && v < V) {
+        const float logit =
+            bf16_round(__bfloat162float(base[(size_t)(b * rows_per_b + step) * ld + v]) + bf16_round(d));
+        if (SAMPLE)
+          out[(size_t)b * ld_out + v] = __float2bfloat16_rn(logit);
+        else
+          best[b] = better(best[b], Best{logit, v});
+      }
     }
   }
   if (SAMPLE) return;
