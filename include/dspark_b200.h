@@ -145,6 +145,24 @@ int dspark_w8a16_gemm_split_mode(int mode);
 int dspark_w8a16_gemm_plan(int M, int N, int K, int* grid, int* cluster, int* max_active);
 
 /* -------------------------------------------------------------------------------------
+ * K1w — the same W8A16 product for prefill chunks (large M). Replaces the QuantizedLinear
+ * calls of Target.run over one prefill chunk (src/mlx_dspark/generate.py:613-656 ->
+ * src/mlx_dspark/target.py:51-75) and of the drafter's update_context over the chunk's tapped
+ * hidden states (src/mlx_dspark/model.py:253-256).
+ *   x fp16 [M, K] (16-byte aligned rows), any M >= 1; N a multiple of 128, K of 64;
+ *   epilogue STORE_BF16, RESIDUAL_BF16 (y may alias residual; copy_f16 optional, as in
+ *   dspark_gemm_opts), SILU_MUL_F16 (interleaved gate/up pack, y [M, N/2]) or STORE_F32.
+ * Outputs are the verify GEMM's: the same fp16 weights, fp32 accumulation (in another order)
+ * and the same epilogue roundings. Persistent tcgen05 kernel, one CTA per SM, tiles of 128
+ * weight rows x 256 tokens (128 when M <= 128); no workspace. */
+int dspark_w8a16_gemm_wide(const void* x, int ldx, const uint8_t* wq, const uint32_t* wsb, int M,
+                           int N, int K, int epilogue, void* y, int ldy, const void* residual,
+                           int ldr, void* copy_f16, int copy_f16_ld, int* status,
+                           dspark_stream_t stream);
+/* The launch dspark_w8a16_gemm_wide makes for this shape: *bn tokens per tile, *grid CTAs. */
+int dspark_w8a16_gemm_wide_plan(int M, int N, int K, int* bn, int* grid);
+
+/* -------------------------------------------------------------------------------------
  * K13 — embedding dequant-gather. Replaces mlx QuantizedEmbedding (embed_tokens,
  * src/mlx_dspark/target.py:63; drafter embed src/mlx_dspark/model.py:372-373).
  *   out[m, :] = bf16(scale * q[ids[m], :] + bias) * embed_scale (embed_scale 1 for Qwen3)

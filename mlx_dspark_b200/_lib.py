@@ -68,6 +68,8 @@ SIGNATURES = {
     "dspark_w8a16_gemm_simt": (I, [P, I, P, P, I, I, I, P, I, P, I, I, P]),
     "dspark_w8a16_gemm_split_mode": (I, [I]),
     "dspark_w8a16_gemm_plan": (I, [I, I, I, P, P, P]),
+    "dspark_w8a16_gemm_wide": (I, [P, I, P, P, I, I, I, I, P, I, P, I, P, I, P, P]),
+    "dspark_w8a16_gemm_wide_plan": (I, [I, I, I, P, P]),
     "dspark_embed_w8": (I, [P, I, P, P, I, I, P, I, P]),
     "dspark_embed_w8_sumsq": (I, [P, I, P, P, I, I, P, I, P, P]),
     "dspark_embed_block_w8": (I, [P, I, I, I, P, P, I, I, P, I, P, P]),

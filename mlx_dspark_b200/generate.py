@@ -31,8 +31,8 @@ import torch
 from . import ops
 from .kvcache import CacheState, RowView
 from .model import Sampling
+from .target import PREFILL_CHUNK
 
-PREFILL_CHUNK = 2048  # reference knob (generate.py:613); the device chunk is min(this, chunk_len)
 
 
 @dataclass
@@ -109,13 +109,29 @@ def prefill_rows(target, ids: list[int], tstate, tap=(), drafter=None, cstate=No
                  dbuf_key=None):
     """Chunked prefill of one row with the tap feeding the drafter context per chunk
     (_prefill_tapped, generate.py:632-656). `tstate`/`cstate` are one-row views whose
-    lengths advance on the device. Returns the last chunk's logits row (bf16, device)."""
-    T = min(target.chunk_len(1), PREFILL_CHUNK)
+    lengths advance on the device. Returns the last chunk's logits row (bf16, device).
+    Chunks of more than target.wide_min_tokens tokens (up to PREFILL_CHUNK) run through the
+    large-M GEMM (Target.prefill_chunk, BlockDrafter.update_context_wide); the rest through
+    the verify forward."""
+    T = target.chunk_len(1)
     n = len(ids)
     ids_dev = torch.as_tensor(ids, dtype=torch.int32).to(target.device)
     last = None
     pos = 0
     while pos < n:
+        if n - pos > target.wide_min_tokens:
+            t = min(PREFILL_CHUNK, n - pos)
+            buf = target.prefill_buffers(t, len(tap))
+            buf.ids.copy_(ids_dev[pos:pos + t])
+            target.prefill_chunk(buf, tstate, tap, logits="last" if pos + t == n else None)
+            if drafter is not None:
+                drafter.update_context_wide(buf.fused16, t, cstate)
+                cstate.seq_len.add_(t)
+            tstate.seq_len.add_(t)
+            pos += t
+            if pos == n:
+                last = buf.logits[0].clone()
+            continue
         t = min(T, n - pos)
         buf = target.buffers(1, t, len(tap))
         buf.ids.copy_(ids_dev[pos:pos + t])

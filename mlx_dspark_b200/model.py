@@ -28,7 +28,7 @@ from . import ops
 from ._lib import EPI_RESIDUAL_BF16, EPI_SILU_MUL_F16, EPI_STORE_BF16
 from .config import DFlashConfig, DSparkConfig
 from .kvcache import PAGE, CacheState, CtxCaches, PagePool
-from .target import PackedLayer, Target, rope_inv_freq
+from .target import PREFILL_CHUNK, PackedLayer, Target, rope_inv_freq
 from .weights import DFlashWeights, DSparkWeights, pack
 
 
@@ -146,6 +146,37 @@ class BlockDrafter:
                               inv_freq=self.inv_freq, pos0=ctx.seq_len, q_out=None,
                               kv=ctx.layout(l), scratch=sc, M=M, norm=hn)
 
+    def update_context_wide(self, fused16: torch.Tensor, T: int, ctx) -> None:
+        """update_context_dev for a prefill chunk: T tapped rows of row 0 of ctx through the
+        large-M GEMM (model.py:253-256 over one 2048-row chunk, generate.py:646-647). The
+        hidden norm runs as its own kernel here; the only difference from the fused form is
+        the fp32 summation order of the squares."""
+        c, sc = self.config, self.scratch
+        eps = c.rms_norm_eps
+        pb = self._prefill_rows(T)
+        h, x16, kvo = pb["h"][:T], pb["x16"][:T], pb["kv"][:T]
+        ops.gemm_wide(fused16, self.fc, h, epilogue=EPI_STORE_BF16, scratch=sc, M=T)
+        ops.rmsnorm(h, self.hidden_norm, eps, y16=x16, M=T)
+        for l, L in enumerate(self.layers):
+            ops.gemm_wide(x16, L.kv, kvo, epilogue=EPI_STORE_BF16, scratch=sc, M=T)
+            ops.qkv_rope_kv_write(kvo, 1, T, 0, c.num_key_value_heads, c.head_dim, None,
+                                  L.k_norm, eps, self.inv_freq, ctx.seq_len[:1], None,
+                                  ctx.layout(l))
+
+    def _prefill_rows(self, T: int) -> dict:
+        """Context-update buffers for prefill chunks, kept at the largest T asked for."""
+        pb = self._bufs.get("prefill")
+        if pb is None or pb["cap"] < T:
+            c = self.config
+            H, kv_dim = c.hidden_size, c.num_key_value_heads * c.head_dim
+            self._bufs.pop("prefill", None)
+            pb = {"cap": T,
+                  "h": torch.zeros(T, H, dtype=torch.bfloat16, device=self.device),
+                  "x16": torch.zeros(T, H, dtype=torch.float16, device=self.device),
+                  "kv": torch.zeros(T, 2 * kv_dim, dtype=torch.bfloat16, device=self.device)}
+            self._bufs["prefill"] = pb
+        return pb
+
     def backbone_dev(self, pending: torch.Tensor, B: int, ctx: CacheState, buf: DraftBuffers,
                      splits: int, final_norm: bool = True) -> None:
         """Block [pending, mask x (k-1)] of each row at positions seq_len[b] + i -> layers over
@@ -195,11 +226,14 @@ class BlockDrafter:
         pos = 0
         T = self.target.chunk_len(1)
         while pos < n:
-            t = min(T, n - pos)
-            buf = self.buffers(1, self.block_size, t)
+            wide = n - pos > self.target.wide_min_tokens
+            t = min(PREFILL_CHUNK if wide else T, n - pos)
             f16 = fused[pos:pos + t].to(torch.float16).contiguous()
             ctx_caches.set_len(0, ctx_offset + pos)
-            self.update_context_dev(f16, 1, t, ctx_caches, buf)
+            if wide:
+                self.update_context_wide(f16, t, ctx_caches)
+            else:
+                self.update_context_dev(f16, 1, t, ctx_caches, self.buffers(1, self.block_size, t))
             pos += t
         ctx_caches.set_len(0, ctx_offset + n)
 

@@ -157,6 +157,30 @@ def gemm(x16: torch.Tensor, w: PackedLinear, y: torch.Tensor, *, epilogue=_lib.E
     return y
 
 
+def gemm_wide(x16: torch.Tensor, w: PackedLinear, y: torch.Tensor, *,
+              epilogue=_lib.EPI_STORE_BF16, residual: torch.Tensor | None = None,
+              scratch: Scratch, M: int | None = None,
+              copy16: torch.Tensor | None = None) -> torch.Tensor:
+    """y = x16 @ W^T for a prefill chunk (any M; the persistent large-M tcgen05 kernel), with
+    the epilogues of gemm(). `copy16` (RESIDUAL_BF16): an fp16 view [M, N] that also receives
+    y (the hidden-state tap)."""
+    _require_cuda(x16, y)
+    M = x16.shape[0] if M is None else M
+    K = w.K
+    assert x16.dtype == torch.float16 and x16.shape[-1] >= K
+    call("dspark_w8a16_gemm_wide", _p(x16), x16.stride(0), _p(w.q), _p(w.sb), M, w.N, K, epilogue,
+         _p(y), y.stride(0), _p(residual), residual.stride(0) if residual is not None else 0,
+         _p(copy16), copy16.stride(0) if copy16 is not None else 0, _p(scratch.status),
+         _stream())
+    return y
+
+
+def gemm_wide_plan(M: int, N: int, K: int) -> dict:
+    bn, grid = ctypes.c_int(), ctypes.c_int()
+    call("dspark_w8a16_gemm_wide_plan", M, N, K, ctypes.byref(bn), ctypes.byref(grid))
+    return {"bn": bn.value, "grid": grid.value}
+
+
 def gemm_qkv_rope(x16: torch.Tensor, w: PackedLinear, *, T: int, Hq: int, Hkv: int, hd: int,
                   q_norm: torch.Tensor | None, k_norm: torch.Tensor, eps: float,
                   inv_freq: torch.Tensor, pos0: torch.Tensor, q_out: torch.Tensor | None,

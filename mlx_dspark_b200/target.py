@@ -26,6 +26,7 @@ from .weights import PackedLinear, TargetWeights, pack
 
 MAX_M = 64          # rows per W8A16 GEMM launch
 MAX_ATTN_ROWS = 128  # query rows per kv head per attention CTA
+PREFILL_CHUNK = 2048  # tokens per prefill chunk (the reference's PREFILL_CHUNK, generate.py:613)
 
 
 def rope_inv_freq(head_dim: int, theta: float, device) -> torch.Tensor:
@@ -67,6 +68,41 @@ class Buffers:
         # per-128-column-tile row sums of squares of h, written by the residual GEMMs for the
         # RMSNorm fused into the next GEMM
         self.sumsq = torch.zeros(M, H // 128, dtype=torch.float32, device=device)
+
+
+class PrefillBuffers:
+    """Activations of a prefill chunk of up to `cap` tokens of one row (the large-M GEMM path);
+    rows(T) views the first T rows of each."""
+
+    def __init__(self, cfg: TargetConfig, T: int, n_tap: int, device, all_logits: bool = False):
+        H, I = cfg.hidden_size, cfg.intermediate_size
+        self.T = self.cap = T
+        self.all_logits = all_logits
+        self.ids = torch.zeros(T, dtype=torch.int32, device=device)
+        self.h = torch.zeros(T, H, dtype=torch.bfloat16, device=device)
+        self.xn16 = torch.zeros(T, H, dtype=torch.float16, device=device)
+        self.qkv = torch.zeros(T, cfg.qkv_dim, dtype=torch.bfloat16, device=device)
+        self.q = torch.zeros(T, cfg.q_dim, dtype=torch.bfloat16, device=device)
+        self.attn16 = torch.zeros(T, cfg.q_dim, dtype=torch.float16, device=device)
+        self.act16 = torch.zeros(T, I, dtype=torch.float16, device=device)
+        self.fused16 = (torch.zeros(T, n_tap * H, dtype=torch.float16, device=device)
+                        if n_tap else None)
+        # the last row's logits (prefill), or every row's (the run() API)
+        self.logits = torch.zeros(T if all_logits else 1, cfg.vocab_size, dtype=torch.bfloat16,
+                                  device=device)
+
+    def rows(self, T: int) -> "PrefillBuffers":
+        """The same buffers cut to the first T rows (shared storage)."""
+        assert 1 <= T <= self.cap
+        v = object.__new__(PrefillBuffers)
+        v.__dict__.update(self.__dict__)
+        v.T = T
+        for f in ("ids", "h", "xn16", "qkv", "q", "attn16", "act16", "fused16"):
+            t = getattr(self, f)
+            setattr(v, f, None if t is None else t[:T])
+        if self.all_logits:
+            v.logits = self.logits[:T]
+        return v
 
 
 class Target:
@@ -139,6 +175,81 @@ class Target:
     def chunk_len(self, B: int = 1) -> int:
         """Largest T with B*T <= 64 GEMM rows and G*T <= 128 attention rows."""
         return max(1, min(MAX_M // B, MAX_ATTN_ROWS // self.group))
+
+    # prefill chunks longer than this run through the large-M GEMM (prefill_chunk); shorter
+    # ones through the verify forward
+    wide_min_tokens = MAX_M
+
+    def prefill_buffers(self, T: int, n_tap: int, all_logits: bool = False) -> PrefillBuffers:
+        """Buffers for a T-token prefill chunk: one set per (n_tap, all_logits) kept at the
+        largest T asked for so far, viewed at T rows."""
+        key = ("prefill", n_tap, all_logits)
+        b = self._bufs.get(key)
+        if b is None or b.cap < T:
+            self._bufs.pop(key, None)
+            b = PrefillBuffers(self.cfg, T, n_tap, self.device, all_logits)
+            self._bufs[key] = b
+        return b.rows(T)
+
+    def prefill_chunk(self, buf: PrefillBuffers, state: CacheState, tap=(), *,
+                      logits: str | None = "last") -> None:
+        """One prefill chunk of row 0 of `state` (ids in buf.ids) at positions seq_len[0] + t,
+        through the large-M W8 GEMM (Target.run over one chunk, target.py:51-75, as
+        _prefill_tapped drives it, generate.py:632-656). Writes the chunk's KV and taps;
+        logits "last" (the last row, into buf.logits[0]), "all" or None. Does not advance
+        seq_len. Attention runs the chunk's queries as rows of 128 // G tokens each: row v sees
+        the keys before position seq_len + v * (128 // G) plus its own causal block, so the
+        verify attention kernel serves the whole chunk in one launch (two when T is not a
+        multiple of the row length)."""
+        c, sc = self.cfg, self.scratch
+        T = buf.T
+        H, eps = c.hidden_size, c.rms_norm_eps
+        Hq, Hkv, hd = c.num_attention_heads, c.num_key_value_heads, c.head_dim
+        tap_idx = {l: j for j, l in enumerate(tap)}
+        tq = MAX_ATTN_ROWS // self.group
+        V, rem = divmod(T, tq)
+        pos0 = state.seq_len[:1]
+        if V:
+            bt_v = state.block_table[:1].expand(V, -1).contiguous()
+            kvl_v = pos0 + torch.arange(V, dtype=torch.int32, device=self.device) * tq
+            splits_v = max(1, min(state.max_pages, (2 * 148) // (V * Hkv)))
+        if rem:
+            kvl_r = pos0 + V * tq
+            splits_r = self.attn_splits(1, state.max_pages)
+        ops.embed(buf.ids, self.embed, buf.h, T)
+        for l, L in enumerate(self.layers):
+            kv = state.layout(l)
+            ops.rmsnorm(buf.h, L.input_ln, eps, y16=buf.xn16, M=T)
+            ops.gemm_wide(buf.xn16, L.qkv, buf.qkv, epilogue=EPI_STORE_BF16, scratch=sc, M=T)
+            ops.qkv_rope_kv_write(buf.qkv, 1, T, Hq, Hkv, hd, L.q_norm, L.k_norm, eps,
+                                  self.inv_freq, pos0, buf.q, kv)
+            if V:
+                ops.attention(buf.q, V, tq, Hq, state.pool.layout(l, bt_v), kvl_v, True,
+                              self.scale, buf.attn16, splits_v, sc)
+            if rem:
+                ops.attention(buf.q[V * tq:], 1, rem, Hq, kv, kvl_r, True, self.scale,
+                              buf.attn16[V * tq:], splits_r, sc)
+            self._wide_residual(buf.attn16, L.o, buf.h, T)
+            ops.rmsnorm(buf.h, L.post_ln, eps, y16=buf.xn16, M=T)
+            ops.gemm_wide(buf.xn16, L.gu, buf.act16, epilogue=EPI_SILU_MUL_F16, scratch=sc, M=T)
+            tap16 = buf.fused16[:, tap_idx[l] * H:(tap_idx[l] + 1) * H] if l in tap_idx else None
+            self._wide_residual(buf.act16, L.down, buf.h, T, tap16)
+        if logits == "last":
+            ops.rmsnorm(buf.h[T - 1:], self.norm, eps, y16=buf.xn16[T - 1:], M=1)
+            ops.gemm(buf.xn16[T - 1:], self.head, buf.logits[:1], epilogue=EPI_STORE_BF16,
+                     scratch=sc, M=1)
+        elif logits == "all":
+            assert buf.logits.shape[0] == T
+            ops.rmsnorm(buf.h, self.norm, eps, y16=buf.xn16, M=T)
+            ops.gemm_wide(buf.xn16, self.head, buf.logits, epilogue=EPI_STORE_BF16, scratch=sc,
+                          M=T)
+
+    def _wide_residual(self, x16: torch.Tensor, w: PackedLinear, h: torch.Tensor, T: int,
+                       copy16: torch.Tensor | None = None) -> None:
+        """h += x16 @ W^T (bf16 residual add in the GEMM epilogue), optionally also into the
+        fp16 tap `copy16`."""
+        ops.gemm_wide(x16, w, h, epilogue=EPI_RESIDUAL_BF16, residual=h, scratch=self.scratch,
+                      M=T, copy16=copy16)
 
     # ------------------------------------------------------------------ the forward
     # Run each layer's GEMMs and small ops as one dspark_run_chain launch. Off by default: on
@@ -284,10 +395,16 @@ class Target:
                  if tap else None)
         pos = 0
         while pos < Ltot:
-            t = min(T, Ltot - pos)
-            buf = self.buffers(1, t, len(tap))
-            buf.ids.copy_(ids[pos:pos + t])
-            self.forward(buf, st, tap)
+            if Ltot - pos > self.wide_min_tokens:
+                t = min(PREFILL_CHUNK, Ltot - pos)
+                buf = self.prefill_buffers(t, len(tap), all_logits=True)
+                buf.ids.copy_(ids[pos:pos + t])
+                self.prefill_chunk(buf, st, tap, logits="all")
+            else:
+                t = min(T, Ltot - pos)
+                buf = self.buffers(1, t, len(tap))
+                buf.ids.copy_(ids[pos:pos + t])
+                self.forward(buf, st, tap)
             logits[pos:pos + t].copy_(buf.logits)
             if tap:
                 fused[pos:pos + t].copy_(buf.fused16)

@@ -161,6 +161,16 @@ class TPTarget(Target):
             ops.rmsnorm(buf.h, self.norm, c.rms_norm_eps, y16=buf.xn16, M=M)
             ops.gemm(buf.xn16, self.head, buf.logits, epilogue=EPI_STORE_BF16, scratch=sc, M=M)
 
+    def _wide_residual(self, x16, w, h, T, copy16=None) -> None:
+        """The row-parallel projection of a prefill chunk: fp32 partial, NCCL all-reduce, then
+        the bf16 residual add (as forward())."""
+        part = self._partial(T)
+        ops.gemm_wide(x16, w, part, epilogue=EPI_STORE_F32, scratch=self.scratch, M=T)
+        self._all_reduce(part)
+        ops.residual_add_f32(h, part, T)
+        if copy16 is not None:
+            ops.bf16_to_f16(h, copy16, T, h.shape[1])
+
     # ------------------------------------------------------------------ vocab-parallel argmax
     def _shard_bufs(self, rows: int):
         b = self._shard.get(rows)
