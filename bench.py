@@ -62,6 +62,9 @@ def parse():
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     ap.add_argument("--layers", type=int, default=None,
                     help="depth-reduced target (same widths) for profiling captures")
+    ap.add_argument("--profile-prefill", action="store_true",
+                    help="small run for ncu: two prefills of --prompt-len tokens (default 2048) "
+                         "through the large-M GEMM, nothing else")
     return ap.parse_args()
 
 
@@ -294,6 +297,92 @@ def cpu_baseline(tw, prompt_len, budget):
                       f"{dt:.1f} s"}
 
 
+def prefill_measure(target, drafter, prompt, reps=2):
+    """Prefill of the prompt (target chunks + the drafter's context update, as the decode loops
+    run it) timed with CUDA events, and the large-M GEMMs of one chunk timed alone: every
+    layer's q|k|v, o, gate|up and down at M = min(prompt, PREFILL_CHUNK) rows (tensor roofline:
+    2*M*N*K FLOPs per GEMM)."""
+    from mlx_dspark_b200 import ops
+    from mlx_dspark_b200._lib import EPI_RESIDUAL_BF16, EPI_SILU_MUL_F16, EPI_STORE_BF16
+    from mlx_dspark_b200.generate import SpecSession, prefill_rows
+    from mlx_dspark_b200.target import PREFILL_CHUNK
+
+    n = len(prompt)
+    times = []
+    for _ in range(reps):
+        sess = SpecSession(target, drafter, 1, drafter.block_size, n + 64)
+        torch.cuda.synchronize()
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record()
+        prefill_rows(target, prompt, sess.tstate, sess.tap, drafter, sess.cstate)
+        e.record()
+        torch.cuda.synchronize()
+        times.append(s.elapsed_time(e))
+        sess.release()
+    target.scratch.check_status()
+    c, dev, sc = target.cfg, target.device, target.scratch
+    M = min(n, PREFILL_CHUNK)
+    H, I = c.hidden_size, c.intermediate_size
+    x = torch.randn(M, max(H, I, c.q_dim), device=dev).to(torch.float16)
+    h = torch.zeros(M, H, dtype=torch.bfloat16, device=dev)
+    qkv = torch.zeros(M, c.qkv_dim, dtype=torch.bfloat16, device=dev)
+    act = torch.zeros(M, I, dtype=torch.float16, device=dev)
+
+    def one_pass():
+        for L in target.layers:
+            ops.gemm_wide(x[:, :H], L.qkv, qkv, epilogue=EPI_STORE_BF16, scratch=sc, M=M)
+            ops.gemm_wide(x[:, :c.q_dim], L.o, h, epilogue=EPI_RESIDUAL_BF16, residual=h,
+                          scratch=sc, M=M)
+            ops.gemm_wide(x[:, :H], L.gu, act, epilogue=EPI_SILU_MUL_F16, scratch=sc, M=M)
+            ops.gemm_wide(x[:, :I], L.down, h, epilogue=EPI_RESIDUAL_BF16, residual=h,
+                          scratch=sc, M=M)
+
+    flops = 2.0 * M * sum(L.qkv.N * L.qkv.K + L.o.N * L.o.K + L.gu.N * L.gu.K + L.down.N * L.down.K
+                          for L in target.layers)
+    one_pass()
+    torch.cuda.synchronize()
+    s = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    s.record()
+    one_pass()
+    e.record()
+    torch.cuda.synchronize()
+    target.scratch.check_status()
+    us = s.elapsed_time(e) * 1000.0
+    peaks = load_peaks()
+    tf = flops / (us * 1e-6) / 1e12
+    ms = min(times)
+    return {"tokens": n, "ms": round(ms, 2), "tok_s": round(n / (ms / 1000.0), 1),
+            "chunk": M, "gemm_us_per_pass": round(us, 1),
+            "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peaks["bf16_tflops"],
+                         "unit": "TFLOP/s", "frac": round(tf / peaks["bf16_tflops"], 4),
+                         "kernel": f"w8a16_wide_kernel (all layers' q|k|v, o, gate|up, down at M={M})",
+                         "peak_source": peaks["source"] + " (MEASURED_PEAKS.json bf16_tflops, burst: "
+                                        "the GEMMs are timed alone)"}}
+
+
+def run_profile_prefill(args):
+    """Two prefills of a random prompt (target chunks + drafter context) on one GPU: the
+    second one's w8a16_wide launches are the ones an ncu capture skips to."""
+    from mlx_dspark_b200.config import WORKLOADS
+    from mlx_dspark_b200.generate import SpecSession, prefill_rows
+
+    wl = WORKLOADS[args.workload]
+    _, target, drafter, _ = build_models(wl, wl.seed, args.layers, keep_cpu=False)
+    n = args.prompt_len or 2048
+    prompt = torch.randint(0, target.cfg.vocab_size, (n,),
+                           generator=torch.Generator().manual_seed(wl.seed)).tolist()
+    for _ in range(2):
+        sess = SpecSession(target, drafter, 1, drafter.block_size, n + 64)
+        prefill_rows(target, prompt, sess.tstate, sess.tap, drafter, sess.cstate)
+        torch.cuda.synchronize()
+        sess.release()
+    target.scratch.check_status()
+    print(json.dumps({"profile_prefill": n, "layers": len(target.layers)}), flush=True)
+    return 0
+
+
 # ----------------------------------------------------------------------------------------
 def run_ours(args, world, rank):
     from mlx_dspark_b200 import _lib
@@ -391,6 +480,8 @@ def run_ours(args, world, rank):
                       "api": "mlx_dspark_b200.speculative_generate (host loop, one sync per round)",
                       "rounds": res.num_rounds, "mean_accept_len": round(res.mean_accept_len, 3),
                       "prefill_s": round(res.seconds - res.decode_seconds, 3)}
+    if not args.profile:
+        out["prefill"] = prefill_measure(target, drafter, prompt)
     if want_cpu:
         out["cpu_baseline"] = cpu_baseline(tw, prompt_len, args.cpu_budget)
     return out
@@ -452,6 +543,8 @@ def main():
             print(json.dumps(out), flush=True)
         return 0
     world, rank, _ = dist_setup(args.gpus)
+    if args.profile_prefill:
+        return run_profile_prefill(args)
     try:
         out = run_ours(args, world, rank)
         if rank == 0:

@@ -167,6 +167,31 @@ __device__ __forceinline__ void bulk_load_g2s(uint32_t dst, const void* src, uin
       "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
       : "memory");
 }
+// Tiled TMA store shared -> global (no multicast; rows past the map's extent are not written),
+// tracked in this thread's bulk async-groups. x * element size is a multiple of 16 bytes and
+// both coordinates are non-negative at every call site.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(c0), "r"(c1)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// wait until at most N of this thread's bulk groups still read their shared-memory source
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// wait until every bulk group of this thread has completed (writes performed)
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+// orders this thread's generic-proxy shared-memory writes before later async-proxy reads
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
 // Orders this thread's earlier generic-proxy accesses (and what it acquired) before its later
 // async-proxy (bulk copy / TMA) accesses of global memory.
 __device__ __forceinline__ void fence_proxy_async_global() {

@@ -20,9 +20,13 @@
 //   - One thread issues tcgen05.mma (A from TMEM, B = activations from shared memory) into the
 //     TMEM accumulator: one of 256 columns at BN 256, two of 128 at BN 128.
 //   - Four epilogue warps read the accumulator, round it to bf16 pairs held in registers,
-//     release it to the MMA warp, and only then store: bf16, bf16 residual add (with an
-//     optional fp16 copy), or SiLU(gate) * up as fp16. The fp32 store (a diagnostic) reads the
-//     accumulator chunk by chunk before releasing it.
+//     release it to the MMA warp, and only then write the outputs: bf16, bf16 residual add
+//     (with an optional fp16 copy), or SiLU(gate) * up as fp16. They fill a ring of shared
+//     staging buffers 16 activation rows at a time, and one thread writes each chunk with a
+//     TMA tensor store; the residual add reads its chunks through TMA loads issued two chunks
+//     ahead. (Per-thread 2-byte global stores and loads measured 17-80 us per tile under the
+//     mainloop's L2 traffic, longer than the tile's MMAs.) The fp32 store (a diagnostic)
+//     writes from registers before releasing the accumulator.
 // Every wait is bounded (DSPARK_ERR_TIMEOUT in the caller's status word, then every role
 // unwinds); the roles that later meet at a named barrier first agree on a vote.
 #include <algorithm>
@@ -46,6 +50,8 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kWBytes = BM * BK;  // 8 KB
 constexpr uint32_t kSBBytes = BM * 4;  // 512 B
 constexpr int kXchStride = 12;         // u32 per exchanged row: 8 used, 48-byte rows
+constexpr int kNB = 4;                 // output staging ring: 16 activation rows per buffer
+constexpr uint32_t kStgBytes = 4096;   // 16 rows x 256 B (bf16 x 128 columns)
 
 struct Params {
   int M, N, K;
@@ -68,7 +74,8 @@ struct Cfg {
   static constexpr uint32_t kStageBytes = kWBytes + kXBytes + kSBBytes;
   static constexpr uint32_t kXchBytes = 64u * kXchStride * 4u;
   static constexpr uint32_t kBarBytes = 512;
-  static constexpr uint32_t kTotal = 1024 + kStages * kStageBytes + kXchBytes + kBarBytes;
+  static constexpr uint32_t kTotal =
+      1024 + kStages * kStageBytes + kNB * kStgBytes + kXchBytes + kBarBytes;
 };
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
@@ -90,101 +97,21 @@ __device__ __forceinline__ bool epi_all(bool ok) {
   return r != 0;
 }
 
-// Stores of one finished tile from the bf16-rounded accumulator pairs pk[j] = (row 2j, 2j + 1).
-// Thread er owns weight row er of the tile: output column n = nt * 128 + er (SiLU: nt * 64 + er
-// for the gate rows er < 64), activation rows m0 .. m0 + mc - 1.
-template <int BN>
-__device__ __forceinline__ void store_tile(const Params& p, int nt, int mt, int er,
-                                           const uint32_t (&pk)[BN / 2], uint32_t* xch) {
-  const int m0 = mt * BN;
-  const int mc = min(BN, p.M - m0);
-  switch (p.epilogue) {
-    case DSPARK_EPI_STORE_BF16: {
-      uint16_t* y = static_cast<uint16_t*>(p.y) + (size_t)m0 * p.ldy + nt * BM + er;
-#pragma unroll
-      for (int j = 0; j < BN / 2; ++j) {
-        if (2 * j < mc) y[(size_t)(2 * j) * p.ldy] = (uint16_t)(pk[j] & 0xFFFFu);
-        if (2 * j + 1 < mc) y[(size_t)(2 * j + 1) * p.ldy] = (uint16_t)(pk[j] >> 16);
-      }
-      break;
-    }
-    case DSPARK_EPI_RESIDUAL_BF16: {
-      // y may be the residual itself: each element is read, then written, by this thread only
-      const size_t n = (size_t)nt * BM + er;
-      __nv_bfloat16* y = static_cast<__nv_bfloat16*>(p.y) + (size_t)m0 * p.ldy + n;
-      const __nv_bfloat16* r = static_cast<const __nv_bfloat16*>(p.residual) + (size_t)m0 * p.ldr + n;
-      __half* c16 = p.copy16 ? p.copy16 + (size_t)m0 * p.copy16_ld + n : nullptr;
-#pragma unroll
-      for (int c0 = 0; c0 < BN; c0 += 8) {
-        float rv[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          rv[j] = c0 + j < mc ? __bfloat162float(r[(size_t)(c0 + j) * p.ldr]) : 0.0f;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int m = c0 + j;
-          if (m < mc) {
-            const float a = (m & 1) ? hi_f(pk[m >> 1]) : lo_f(pk[m >> 1]);
-            const __nv_bfloat16 o = __float2bfloat16_rn(rv[j] + a);
-            y[(size_t)m * p.ldy] = o;
-            if (c16) c16[(size_t)m * p.copy16_ld] = __float2half_rn(__bfloat162float(o));
-          }
-        }
-      }
-      break;
-    }
-    case DSPARK_EPI_SILU_MUL_F16: {
-      // rows [0,64) of the tile are gate rows, [64,128) the matching up rows: the up rows hand
-      // their bf16 values to the gate rows through shared memory, 16 activation rows a round
-      __half* y = static_cast<__half*>(p.y) + (size_t)m0 * p.ldy + nt * 64 + er;
-#pragma unroll
-      for (int c0 = 0; c0 < BN / 2; c0 += 8) {
-        if (er >= 64) {
-          uint4* dst = reinterpret_cast<uint4*>(xch + (er - 64) * kXchStride);
-#pragma unroll
-          for (int q = 0; q < 2; ++q)
-            dst[q] = make_uint4(pk[c0 + 4 * q], pk[c0 + 4 * q + 1], pk[c0 + 4 * q + 2], pk[c0 + 4 * q + 3]);
-        }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (er < 64) {
-          uint32_t up[8];
-          const uint4* src = reinterpret_cast<const uint4*>(xch + er * kXchStride);
-#pragma unroll
-          for (int q = 0; q < 2; ++q) {
-            const uint4 v = src[q];
-            up[4 * q] = v.x; up[4 * q + 1] = v.y; up[4 * q + 2] = v.z; up[4 * q + 3] = v.w;
-          }
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int m = 2 * c0 + j;
-            if (m < mc) {
-              const float g = (j & 1) ? hi_f(pk[c0 + (j >> 1)]) : lo_f(pk[c0 + (j >> 1)]);
-              const float u = (j & 1) ? hi_f(up[j >> 1]) : lo_f(up[j >> 1]);
-              const float s = bf16_round(silu_f(g));
-              y[(size_t)m * p.ldy] = __float2half_rn(bf16_round(s * u));
-            }
-          }
-        }
-        asm volatile("bar.sync 1, 128;" ::: "memory");  // xch is refilled next round
-      }
-      break;
-    }
-    default:
-      break;
-  }
-}
-
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     w8a16_wide_kernel(const __grid_constant__ CUtensorMap tm_w,
                       const __grid_constant__ CUtensorMap tm_sb,
-                      const __grid_constant__ CUtensorMap tm_x, const Params p) {
+                      const __grid_constant__ CUtensorMap tm_x,
+                      const __grid_constant__ CUtensorMap tm_y,   // output (store)
+                      const __grid_constant__ CUtensorMap tm_r,   // residual (load)
+                      const __grid_constant__ CUtensorMap tm_c,   // fp16 copy (store)
+                      const Params p) {
   using C = Cfg<BN>;
   constexpr int S = C::kStages;
   constexpr int NACC = C::kAccBufs;
   static_assert(NACC * BN <= (int)kARing0, "TMEM layout");
   static_assert(kARing0 + AB * 32 <= kTmemCols, "TMEM layout");
-  static_assert((2 * S + 2 * AB + 2 * NACC + 2) * 8 <= (int)C::kBarBytes, "barrier region");
+  static_assert((2 * S + 2 * AB + 2 * NACC + kNB + 2) * 8 <= (int)C::kBarBytes, "barrier region");
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -192,8 +119,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t w_s = base;                    // S x 8 KB, 1024-aligned
   const uint32_t x_s = w_s + S * kWBytes;       // S x BN*128 B, 1024-aligned
   const uint32_t sb_s = x_s + S * C::kXBytes;   // S x 512 B
-  uint32_t* xch = reinterpret_cast<uint32_t*>(sbase + S * C::kStageBytes);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sbase + S * C::kStageBytes + C::kXchBytes);
+  const uint32_t stg_s = sb_s + S * kSBBytes;   // kNB x 4 KB output staging, 512-aligned
+  uint8_t* stg = sbase + S * C::kStageBytes;
+  uint32_t* xch = reinterpret_cast<uint32_t*>(stg + kNB * kStgBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(stg + kNB * kStgBytes + C::kXchBytes);
   auto full = [&](int s) { return smem_u32(bars + s); };
   auto empty = [&](int s) { return smem_u32(bars + S + s); };
   auto afull = [&](int a) { return smem_u32(bars + 2 * S + a); };
@@ -201,7 +130,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto accfull = [&](int b) { return smem_u32(bars + 2 * S + 2 * AB + b); };
   auto accempty = [&](int b) { return smem_u32(bars + 2 * S + 2 * AB + NACC + b); };
   const uint32_t done_bar = smem_u32(bars + 2 * S + 2 * AB + 2 * NACC);
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * S + 2 * AB + 2 * NACC + 1);
+  auto rbar = [&](int b) { return smem_u32(bars + 2 * S + 2 * AB + 2 * NACC + 1 + b); };
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * S + 2 * AB + 2 * NACC + 1 + kNB);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -220,6 +150,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(accempty(b), kEpiWarps);
     }
     mbar_init(done_bar, 1);
+    for (int b = 0; b < kNB; ++b) mbar_init(rbar(b), 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -228,6 +159,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&tm_w);
       tma_prefetch_desc(&tm_sb);
       tma_prefetch_desc(&tm_x);
+      tma_prefetch_desc(&tm_y);
     }
     __syncwarp();
     tmem_alloc(smem_u32(tmem_holder), kTmemCols);
@@ -364,14 +296,34 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp < kConvWarps + kEpiWarps) {
-    // epilogue: thread er owns row er of the tile (TMEM lane er)
+    // epilogue: thread er owns row er of the tile (TMEM lane er) == column er of each staged
+    // chunk; thread 0 issues the chunk's TMA loads and stores. gc counts this CTA's chunks over
+    // its tiles (staging buffer gc % kNB, residual-load phase (gc / kNB) & 1); lr counts the
+    // residual loads issued (always chunks gc .. lr - 1 in flight).
     const int quad = warp & 3;
     const int er = quad * 32 + lane;
+    const bool issuer = er == 0;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const bool res = p.epilogue == DSPARK_EPI_RESIDUAL_BF16;
+    const bool silu = p.epilogue == DSPARK_EPI_SILU_MUL_F16;
+    const bool cp16 = p.copy16 != nullptr;
+    const uint64_t pol_r = policy_evict_normal();
     pdl_wait();  // the residual and the outputs belong to the kernels before this one
-    int tl = 0;
+    int tl = 0, gc = 0, lr = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++tl) {
       const int nt = t / p.m_tiles, mt = t - nt * p.m_tiles;
+      const int m0 = mt * BN;
+      const int nch = min(BN / 16, (p.M - m0 + 15) / 16);
+      if (res && issuer) {
+        // this tile's first two residual chunks, into buffers last stored from by chunks
+        // gc - 4 and gc - 3 (at most gc - 2 and gc - 1 may still be reading)
+        bulk_wait_read<2>();
+        for (int j = 0; j < 2 && j < nch; ++j, ++lr) {
+          const int b = lr % kNB;
+          mbar_arrive_expect_tx(rbar(b), kStgBytes);
+          tma_load_2d(stg_s + b * kStgBytes, &tm_r, rbar(b), nt * BM, m0 + 16 * j, pol_r);
+        }
+      }
       const int ab = tl % NACC;
       const uint32_t abph = (uint32_t)(tl / NACC) & 1u;
       const bool w_ok = mbar_wait(accfull(ab), abph, abort_flag, p.status);
@@ -379,7 +331,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint32_t acc_t = tmem_base + lane_off + (uint32_t)(ab * BN);
       if (p.epilogue == DSPARK_EPI_STORE_F32) {
-        const int m0 = mt * BN;
         const int mc = min(BN, p.M - m0);
         float* y = static_cast<float*>(p.y) + (size_t)m0 * p.ldy + nt * BM + er;
         for (int c = 0; c < BN / 16; ++c) {
@@ -413,7 +364,94 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(accempty(ab));  // the MMA warp may refill it meanwhile
-      store_tile<BN>(p, nt, mt, er, pk, xch);
+
+#pragma unroll
+      for (int c = 0; c < BN / 16; ++c) {
+        if (c < nch) {  // the same for every epilogue thread
+          const int b = gc % kNB;
+          uint8_t* bp = stg + b * kStgBytes;
+          if (res) {
+            if (issuer && c + 2 < nch) {
+              bulk_wait_read<1>();  // chunk gc - 2, the last user of that buffer, is done reading
+              const int b2 = lr % kNB;
+              mbar_arrive_expect_tx(rbar(b2), kStgBytes);
+              tma_load_2d(stg_s + b2 * kStgBytes, &tm_r, rbar(b2), nt * BM, m0 + 16 * (c + 2), pol_r);
+              ++lr;
+            }
+            // a timeout records the status and the chunk is still written, so that every
+            // thread takes the same barriers
+            mbar_wait(rbar(b), (uint32_t)(gc / kNB) & 1u, abort_flag, p.status);
+          }
+          if (silu) {
+            // rows [0,64) of the tile are gate rows, [64,128) the matching up rows. Gate row r
+            // and up row r finish output column r together: the gate thread takes activation
+            // rows 0-7 of the chunk, the up thread rows 8-15, each handing the other the bf16
+            // values it lacks (xch row r: gate words of rows 8-15, then up words of rows 0-7)
+            const bool gate = er < 64;
+            const int r = gate ? er : er - 64;
+            uint4* xr = reinterpret_cast<uint4*>(xch + r * kXchStride);
+            if (gate)
+              xr[0] = make_uint4(pk[8 * c + 4], pk[8 * c + 5], pk[8 * c + 6], pk[8 * c + 7]);
+            else
+              xr[1] = make_uint4(pk[8 * c], pk[8 * c + 1], pk[8 * c + 2], pk[8 * c + 3]);
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            const uint4 o4 = gate ? xr[1] : xr[0];
+            const uint32_t other[4] = {o4.x, o4.y, o4.z, o4.w};
+            const int row0 = gate ? 0 : 8;  // this thread's activation rows of the chunk
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              // compile-time indices on both sides keep pk in registers
+              const uint32_t own = gate ? pk[8 * c + (j >> 1)] : pk[8 * c + 4 + (j >> 1)];
+              const float a = (j & 1) ? hi_f(own) : lo_f(own);
+              const float b2 = (j & 1) ? hi_f(other[j >> 1]) : lo_f(other[j >> 1]);
+              const float g = gate ? a : b2, u = gate ? b2 : a;
+              const float sg = bf16_round(silu_f(g));
+              *reinterpret_cast<__half*>(bp + (row0 + j) * 128 + r * 2) =
+                  __float2half_rn(bf16_round(sg * u));
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const float a = (j & 1) ? hi_f(pk[8 * c + (j >> 1)]) : lo_f(pk[8 * c + (j >> 1)]);
+              __nv_bfloat16* sp = reinterpret_cast<__nv_bfloat16*>(bp + j * 256 + er * 2);
+              *sp = __float2bfloat16_rn(res ? __bfloat162float(*sp) + a : a);
+            }
+          }
+          fence_proxy_async_smem();
+          if (issuer) bulk_wait_read<kNB - 2>();  // frees the next chunk's buffer (chunk gc - 3)
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          if (issuer) {
+            tma_store_2d(&tm_y, stg_s + b * kStgBytes, silu ? nt * 64 : nt * BM, m0 + 16 * c);
+            bulk_commit();
+          }
+          if (cp16) {
+            // the fp16 copy of the same chunk, converted in place once the bf16 store has read it
+            if (issuer) bulk_wait_read<0>();
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              uint16_t* sp = reinterpret_cast<uint16_t*>(bp + j * 256 + er * 2);
+              const __half h = __float2half_rn(__uint_as_float((uint32_t)*sp << 16));
+              *sp = *reinterpret_cast<const uint16_t*>(&h);
+            }
+            fence_proxy_async_smem();
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            if (issuer) {
+              tma_store_2d(&tm_c, stg_s + b * kStgBytes, nt * BM, m0 + 16 * c);
+              bulk_commit();
+            }
+          }
+          ++gc;
+        }
+      }
+    }
+    if (issuer) {
+      // residual loads issued but not consumed (only after a timeout), then every store
+      for (int i = gc; i < lr; ++i) {
+        volatile int never = 0;
+        mbar_wait(rbar(i % kNB), (uint32_t)(i / kNB) & 1u, &never, p.status);
+      }
+      bulk_wait_all();
     }
   }
 
@@ -442,6 +480,25 @@ static int launch_wide(const void* x, int ldx, const uint8_t* wq, const uint32_t
   if ((rc = make_map_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x, (uint64_t)p.K, (uint64_t)p.M,
                         (uint64_t)ldx * 2, 64, BN, CU_TENSOR_MAP_SWIZZLE_128B)))
     return rc;
+  // output, residual and fp16-copy maps: rows of 16 activations, 128 (SiLU: 64) columns
+  CUtensorMap ty = tx, tr = tx, tc = tx;  // unused ones stay copies of tx
+  if (p.epilogue == DSPARK_EPI_SILU_MUL_F16) {
+    if ((rc = make_map_2d(&ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.y, (uint64_t)(p.N / 2),
+                          (uint64_t)p.M, (uint64_t)p.ldy * 2, 64, 16, CU_TENSOR_MAP_SWIZZLE_NONE)))
+      return rc;
+  } else if (p.epilogue != DSPARK_EPI_STORE_F32) {
+    if ((rc = make_map_2d(&ty, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.y, (uint64_t)p.N,
+                          (uint64_t)p.M, (uint64_t)p.ldy * 2, BM, 16, CU_TENSOR_MAP_SWIZZLE_NONE)))
+      return rc;
+  }
+  if (p.epilogue == DSPARK_EPI_RESIDUAL_BF16 &&
+      (rc = make_map_2d(&tr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.residual, (uint64_t)p.N,
+                        (uint64_t)p.M, (uint64_t)p.ldr * 2, BM, 16, CU_TENSOR_MAP_SWIZZLE_NONE)))
+    return rc;
+  if (p.copy16 &&
+      (rc = make_map_2d(&tc, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.copy16, (uint64_t)p.N,
+                        (uint64_t)p.M, (uint64_t)p.copy16_ld * 2, BM, 16, CU_TENSOR_MAP_SWIZZLE_NONE)))
+    return rc;
   auto kern = w8a16_wide_kernel<BN>;
   static bool configured = false;
   if (!configured) {
@@ -452,7 +509,7 @@ static int launch_wide(const void* x, int ldx, const uint8_t* wq, const uint32_t
   }
   const int grid = std::min(p.n_tiles * p.m_tiles, sm_count());
   return launch_pdl("w8a16_wide", kern, dim3(grid), dim3(kThreads), (size_t)C::kTotal, st, tw, tsb,
-                    tx, p);
+                    tx, ty, tr, tc, p);
 }
 
 }  // namespace w8w

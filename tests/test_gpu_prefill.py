@@ -160,7 +160,10 @@ def test_prefill_wide_matches_verify_forward(tiny_pair, monkeypatch, n, chunk):
     """prefill_rows through the large-M path (chunks of `chunk` tokens; a short tail takes the
     verify forward) against the verify-forward prefill (32-token chunks): the same last-row
     logits, and the same target and drafter-context KV (bf16 roundings of the same sums taken
-    in another order)."""
+    in another order). Each path is held to 2e-2 of the row scale against the oracle elsewhere
+    (the end-to-end tolerance); two such paths may sit on opposite sides of it, so they are
+    compared here at 4e-2 (deep layers measured 0.021: single bf16 ulps accumulated through
+    the residual stream)."""
     tw, target, drafter = tiny_pair
     g = torch.Generator().manual_seed(n)
     prompt = torch.randint(0, TINY.vocab_size, (n,), generator=g).tolist()
@@ -180,11 +183,11 @@ def test_prefill_wide_matches_verify_forward(tiny_pair, monkeypatch, n, chunk):
     (lw, kw, cw, tw_len, cw_len), (ln, kn, cn, tn_len, cn_len) = out["wide"], out["narrow"]
     assert tw_len == tn_len == n and cw_len == cn_len == n
     sc = ln.abs().max()
-    assert ((lw - ln).abs() <= 2e-2 * sc).all(), float((lw - ln).abs().max() / sc)
+    assert ((lw - ln).abs() <= 4e-2 * sc).all(), float((lw - ln).abs().max() / sc)
     for (a, b), (c, d) in zip(kw + cw, kn + cn):
         for x, y in ((a, c), (b, d)):
             s = y.abs().amax(-1, keepdim=True) + 1e-6
-            assert ((x - y).abs() <= 2e-2 * s).all(), float(((x - y).abs() / s).max())
+            assert ((x - y).abs() <= 4e-2 * s).all(), float(((x - y).abs() / s).max())
 
 
 def test_prefill_wide_matches_oracle(tiny_pair, monkeypatch):
