@@ -83,9 +83,11 @@ class SpecSlots:
         if not batched_drafter:
             raise NotImplementedError("the per-row drafter mode (Stage A) is not built; the "
                                       "batched drafter covers it")
-        if cap_controller is not None:
-            raise NotImplementedError("the per-width cap controller is not built")
         cfg = drafter.config
+        # optional CapController: the cap of a round at batch width B is cap_for(B) (the live
+        # cap at B = 1), and every row's outcome feeds its acceptance estimate
+        # (batch_engine.py:535-538,595-596); a cap change switches the session's round buffers
+        self.ctrl = cap_controller
         self.target, self.tokenizer, self.drafter = target, tokenizer, drafter
         self.tap = list(cfg.target_layer_ids)
         self.k = int(cfg.block_size)
@@ -122,7 +124,8 @@ class SpecSlots:
         s = self.sessions.get(B)
         if s is None:
             s = SpecSession(self.target, self.drafter, B, self.cap, self.max_tokens,
-                            states=(self.tstate, self.cstate))
+                            states=(self.tstate, self.cstate),
+                            max_cap=self.k if self.ctrl is not None else None)
             self.sessions[B] = s
         return s
 
@@ -189,6 +192,9 @@ class SpecSlots:
         if B == 0:
             return finished
         sess = self._session(B)
+        if self.ctrl is not None:
+            want = self.ctrl.cap_for(B) if B > 1 else self.ctrl.cap
+            sess.set_cap(max(1, min(int(want), self.k)))
         sess.pending_host[:B] = torch.tensor(self.pending[:B], dtype=torch.int32)
         plans = sess.step(self.use_graph, feed_pending=True)
         if self.use_graph and sess.graph is None:
@@ -198,6 +204,8 @@ class SpecSlots:
             committed = plans[b][2:3 + n]
             self.trk[b].commit(committed, accept_len=len(committed))
             self.pending[b] = self.trk[b].out_ids[-1]
+            if self.ctrl is not None:
+                self.ctrl.update(n, sess.cap)
         finished += self._sweep_finished()
         return finished
 

@@ -148,13 +148,22 @@ def prefill_rows(target, ids: list[int], tstate, tap=(), drafter=None, cstate=No
 
 
 class SpecSession:
-    """Static state and buffers of a B-row speculative decode with `cap` drafts per round."""
+    """Static state and buffers of a B-row speculative decode with `cap` drafts per round.
+
+    The verify width T = cap + 1 is baked into a round's buffers and captured graph. set_cap()
+    switches to another cap (up to max_cap) over the same KV state, keeping one set of round
+    buffers and one graph per cap used, so a cap controller can move the cap between rounds."""
+
+    _ROUND = ("T", "vbuf", "dbuf", "draft", "argmax", "plan", "plan_host", "q", "graph",
+              "_graph_versions")
 
     def __init__(self, target, drafter, B: int, cap: int, max_tokens: int, *,
                  override: dict | None = None, sampling: Sampling | None = None,
-                 seeds=None, penalties: tuple[float, float] = (0.0, 0.0), states=None):
+                 seeds=None, penalties: tuple[float, float] = (0.0, 0.0), states=None,
+                 max_cap: int | None = None):
         self.target, self.drafter = target, drafter
         self.B, self.cap = B, cap
+        self.max_cap = max(cap, int(max_cap or cap))
         self.sampling = sampling if (sampling is not None and sampling.active) else None
         if self.sampling is not None and not target.capturable:
             raise NotImplementedError("sampled decoding of a tensor-parallel target is not built")
@@ -166,11 +175,10 @@ class SpecSession:
             self.counts = torch.zeros(B, target.cfg.vocab_size, dtype=torch.int32,
                                       device=target.device)
         self.k = drafter.block_size
-        self.T = cap + 1
         self.tap = list(drafter.config.target_layer_ids)
         dev = target.device
         # pages for the whole request budget, plus one drafted block past the end
-        cap_tokens = max_tokens + self.k + self.T + 64
+        cap_tokens = max_tokens + self.k + self.max_cap + 1 + 64
         self._owns_states = states is None
         if states is None:
             self.tstate = CacheState(target.new_pool(cap_tokens, B), B, cap_tokens, dev)
@@ -181,20 +189,14 @@ class SpecSession:
         else:
             # caller-owned rows (prefix reuse, the batch engine): the caller provides pages
             self.tstate, self.cstate = states
-        self.vbuf = target.buffers(B, self.T, len(self.tap))
-        self.dbuf = drafter.buffers(B, self.k, B * self.T)
         self.pending = torch.zeros(B, dtype=torch.int32, device=dev)
-        self.draft = torch.zeros(B, cap, dtype=torch.int32, device=dev)
-        self.argmax = torch.zeros(B * self.T, dtype=torch.int32, device=dev)
-        self.plan = torch.zeros(B, self.T + 2, dtype=torch.int32, device=dev)
-        self.plan_host = torch.zeros(B, self.T + 2, dtype=torch.int32, pin_memory=True)
         self.pending_host = torch.zeros(B, dtype=torch.int32, pin_memory=True)
         self.splits_t = target.attn_splits(B, self.tstate.max_pages)
         self.splits_c = target.attn_splits(B, self.cstate.max_pages)
         self.rng = ops.rng_state(list(seeds) if seeds is not None else [0] * B, dev)
-        self.q = None
-        if self.sampling is not None:
-            self.q = torch.zeros(B * cap, target.cfg.vocab_size, dtype=torch.float32, device=dev)
+        self._rounds: dict[int, dict] = {}
+        for f, v in self._make_round(cap).items():
+            setattr(self, f, v)
         self.override = None
         if override is not None:
             if self.sampling is not None:
@@ -206,11 +208,39 @@ class SpecSession:
                 "round": torch.zeros(B, dtype=torch.int32, device=dev),
                 "prompt_len": torch.as_tensor(o["prompt_len"], dtype=torch.int32).to(dev),
             }
-        self.graph = None
         self.done = torch.cuda.Event()
+
+    def _make_round(self, cap: int) -> dict:
+        t, d, B, dev = self.target, self.drafter, self.B, self.target.device
+        T = cap + 1
+        return {"T": T, "vbuf": t.buffers(B, T, len(self.tap)),
+                "dbuf": d.buffers(B, self.k, B * T),
+                "draft": torch.zeros(B, cap, dtype=torch.int32, device=dev),
+                "argmax": torch.zeros(B * T, dtype=torch.int32, device=dev),
+                "plan": torch.zeros(B, T + 2, dtype=torch.int32, device=dev),
+                "plan_host": torch.zeros(B, T + 2, dtype=torch.int32, pin_memory=True),
+                "q": (torch.zeros(B * cap, t.cfg.vocab_size, dtype=torch.float32, device=dev)
+                      if self.sampling is not None else None),
+                "graph": None, "_graph_versions": None}
+
+    def set_cap(self, cap: int) -> None:
+        """Draft and verify `cap` tokens from the next round on (1 <= cap <= max_cap)."""
+        cap = int(cap)
+        if cap == self.cap:
+            return
+        if not 1 <= cap <= self.max_cap:
+            raise ValueError(f"cap {cap} outside [1, {self.max_cap}]")
+        if self.override is not None:
+            raise ValueError("the draft override fixes the cap")
+        self._rounds[self.cap] = {f: getattr(self, f) for f in self._ROUND}
+        r = self._rounds.pop(cap, None) or self._make_round(cap)
+        for f, v in r.items():
+            setattr(self, f, v)
+        self.cap = cap
 
     def release(self):
         self.graph = None
+        self._rounds.clear()
         if self._owns_states:
             self.tstate.release()
             self.cstate.release()
@@ -315,7 +345,10 @@ def _caller_states(drafter, cache, ctx_caches, reuse_len: int, tokens: int):
 
 def _spec_loop(target, tokenizer, drafter, ids, cap, max_new_tokens, sampling, seed, use_graph,
                draft_override, verbose, penalties=(0.0, 0.0), lookup_max_draft=0, cache=None,
-               ctx_caches=None, reuse_len: int = 0) -> GenResult:
+               ctx_caches=None, reuse_len: int = 0, cap_controller=None) -> GenResult:
+    """The decode loop of speculative_generate / dflash_generate. `cap` is the ceiling; with a
+    cap_controller each drafter round uses min(controller.cap, cap) and feeds the outcome back
+    (generate.py:846-847,924-925); lookup rounds neither use nor update it."""
     eos_ids = eos_token_ids(tokenizer)
     budget = len(ids) + max_new_tokens + cap + 1
     sampling = sampling if (sampling is not None and sampling.active) else None
@@ -327,9 +360,11 @@ def _spec_loop(target, tokenizer, drafter, ids, cap, max_new_tokens, sampling, s
         states = (tstate, cstate)
     else:
         reuse_len = 0
-    sess = SpecSession(target, drafter, 1, cap, budget, override=draft_override,
+    ctrl = cap_controller
+    first_cap = cap if ctrl is None else max(1, min(int(ctrl.cap), cap))
+    sess = SpecSession(target, drafter, 1, first_cap, budget, override=draft_override,
                        sampling=sampling, seeds=[0 if seed is None else int(seed)],
-                       penalties=penalties, states=states)
+                       penalties=penalties, states=states, max_cap=cap)
     try:
         t0 = time.time()
         # prefill only the part of the prompt past the reused prefix (generate.py:640-650)
@@ -355,10 +390,14 @@ def _spec_loop(target, tokenizer, drafter, ids, cap, max_new_tokens, sampling, s
                 lookup_rounds += 1
                 plan = sess.lookup_round(pending, lk)
             else:
+                if ctrl is not None:
+                    sess.set_cap(max(1, min(int(ctrl.cap), cap)))
                 sess.pending_host[0] = pending
                 plan = sess.step(use_graph, feed_pending=True)[0]
                 if use_graph and sess.graph is None:
                     sess.capture()
+                if ctrl is not None:
+                    ctrl.update(plan[0], sess.cap)
             n = plan[0]
             committed = plan[2:3 + n]
             accept.append(len(committed))
@@ -374,7 +413,7 @@ def _spec_loop(target, tokenizer, drafter, ids, cap, max_new_tokens, sampling, s
             rounds += 1
             if verbose:
                 src = "lookup" if lk else "drafter"
-                print(f"  round {rounds:3d}: {src} drafted {len(lk) if lk else cap}, accepted {n}, "
+                print(f"  round {rounds:3d}: {src} drafted {len(lk) if lk else sess.cap}, accepted {n}, "
                       f"committed {len(committed)}")
         t2 = time.time()
         text = _decode(tokenizer, [t for t in out if t not in eos_ids])
@@ -416,7 +455,7 @@ def speculative_generate(target, tokenizer, drafter, prompt: str = "", *,
                       Sampling(temperature, top_p, top_k), seed, use_graph, draft_override,
                       verbose, (presence_penalty, frequency_penalty),
                       max(1, int(lookup_max_draft)) if lookup_drafts else 0, cache, ctx_caches,
-                      reuse_len)
+                      reuse_len, cap_controller)
 
 
 def dflash_generate(target_model, tokenizer, drafter, prompt: str = "", *,
@@ -434,7 +473,8 @@ def dflash_generate(target_model, tokenizer, drafter, prompt: str = "", *,
     if prompt_ids is None:
         prompt_ids = list(tokenizer.encode(prompt))
     return _spec_loop(target_model, tokenizer, drafter, list(prompt_ids), cap, max_new_tokens,
-                      Sampling(temperature, top_p, top_k), seed, use_graph, None, verbose)
+                      Sampling(temperature, top_p, top_k), seed, use_graph, None, verbose,
+                      cap_controller=cap_controller)
 
 
 class GreedySession:
