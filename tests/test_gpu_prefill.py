@@ -211,3 +211,27 @@ def test_prefill_wide_matches_oracle(tiny_pair, monkeypatch):
     gf = fused[0].float().cpu()
     fs = rf.abs().amax(-1, keepdim=True)
     assert ((gf - rf).abs() <= 2e-2 * fs).all(), float(((gf - rf).abs() / fs).max())
+
+
+def test_prefill_wide_kv8_matches_verify_forward(cuda, monkeypatch):
+    """The same comparison with the 8-bit KV cache (C4's cache): chunks quantize K/V on write
+    through the same kernel, and the last-row logits of the two prefill paths agree."""
+    tw = generate_target(TINY, 4, "cpu")
+    target, _ = load_target(TINY, weights=tw, device=cuda, kv_bits=8)
+    dcfg = dspark_for(TINY)
+    drafter, _ = load_drafter(target, dcfg, weights=generate_dspark(dcfg, 4, "cpu"), device=cuda)
+    prompt = torch.randint(0, TINY.vocab_size, (400,),
+                           generator=torch.Generator().manual_seed(4)).tolist()
+    lasts = {}
+    for mode in ("wide", "narrow"):
+        monkeypatch.setattr(generate, "PREFILL_CHUNK", 192)
+        monkeypatch.setattr(target, "wide_min_tokens", 64 if mode == "wide" else 10 ** 9)
+        sess = SpecSession(target, drafter, 1, 8, 464)
+        assert sess.tstate.pool.kv8
+        lasts[mode] = prefill_rows(target, prompt, sess.tstate, sess.tap, drafter,
+                                   sess.cstate).float().cpu()
+        torch.cuda.synchronize()
+        target.scratch.check_status()
+        sess.release()
+    sc = lasts["narrow"].abs().max()
+    assert ((lasts["wide"] - lasts["narrow"]).abs() <= 4e-2 * sc).all()
