@@ -404,7 +404,11 @@ def run_ours(args, world, rank):
         ref = torch.randint(0, V, (ref_len,), generator=g).tolist()
     else:
         ref = greedy_generate(target, None, prompt_ids=prompt, max_new_tokens=ref_len).token_ids
-    agree = (torch.rand(1, rounds, cap, generator=torch.Generator().manual_seed(7)) < (wl.accept_p or 0.7)).to(torch.uint8)
+    # one Bernoulli row per round, for the timed rounds and for every round the e2e decode can
+    # take (at most one per token); past the last row the override repeats it, which would
+    # replace the Bernoulli draw by one fixed pattern. The leading rows do not depend on the count.
+    agree_rounds = max(rounds, 512 + cap + 2)
+    agree = (torch.rand(1, agree_rounds, cap, generator=torch.Generator().manual_seed(7)) < (wl.accept_p or 0.7)).to(torch.uint8)
     override = {"ref": torch.tensor([ref]), "agree": agree, "prompt_len": [prompt_len]}
     budget = prompt_len + ref_len + 64
     sess = SpecSession(target, drafter, 1, cap, budget, override=override)

@@ -17,6 +17,7 @@
 // SAMPLE form: it writes the biased logits row and the next launch (dspark_sample_rows) draws
 // token i from truncate(softmax(logits_i / T)), keeping q_i for the acceptance test.
 #include "common.cuh"
+#include "tensor_map.cuh"
 
 namespace dspark {
 namespace mk {
@@ -81,19 +82,25 @@ __global__ void __launch_bounds__(kThreads) markov_step_kernel(
   //   d = fma(s_g, qsum_g, fma(b_g, esum_g, d)), g = 0..3
   const int lane8 = lane & 7, grp = lane >> 3;
   const int gwarp = blockIdx.x * (kThreads / 32) + warp;
-  const int nwarp = gridDim.x * (kThreads / 32);
-  for (int v0 = gwarp * 8; v0 < V; v0 += nwarp * 8) {
-    uint2 q8[8];
-    uint32_t sbk = 0;
+  const int stride = gridDim.x * (kThreads / 32) * 8;
+  // the 8 rows' W8 bytes (lane: bytes [8l, 8l + 8) of each) and this lane's (row lane & 7,
+  // group lane >> 3) scale/bias; rows past V read any valid row, their result is discarded
+  auto load_rows = [&](int vb, uint2 (&q)[8], uint32_t& sb) {
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-      const int v = min(v0 + k, V - 1);  // rows past V: any valid row, result discarded
-      q8[k] = __ldg(reinterpret_cast<const uint2*>(w2q + (size_t)v * kR) + lane);
+      const int v = min(vb + k, V - 1);
+      q[k] = __ldg(reinterpret_cast<const uint2*>(w2q + (size_t)v * kR) + lane);
     }
-    {
-      const int v = min(v0 + lane8, V - 1);  // this lane's (row k = lane & 7, group) scale/bias
-      sbk = __ldg(w2sb + (size_t)grp * V + v);
-    }
+    sb = __ldg(w2sb + (size_t)grp * V + min(vb + lane8, V - 1));
+  };
+  uint2 q8[8];
+  uint32_t sbk = 0;
+  if (gwarp * 8 < V) load_rows(gwarp * 8, q8, sbk);
+  for (int v0 = gwarp * 8; v0 < V; v0 += stride) {
+    // the warp's next 8 rows are in flight while these are reduced
+    uint2 qn[8];
+    uint32_t sbn = 0;
+    if (v0 + stride < V) load_rows(v0 + stride, qn, sbn);
 #pragma unroll
     for (int b = 0; b < NB; ++b) {
       float ev[8];  // this lane's 8 columns of e_b (shared memory; registers stay free at large B)
@@ -158,6 +165,9 @@ __global__ void __launch_bounds__(kThreads) markov_step_kernel(
           best[b] = better(best[b], Best{logit, v});
       }
     }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) q8[k] = qn[k];
+    sbk = sbn;
   }
   if (SAMPLE) return;
 #pragma unroll
@@ -212,10 +222,41 @@ __global__ void __launch_bounds__(kThreads) markov_step_kernel(
   if (threadIdx.x == 0) *counter = 0;
 }
 
+// Greedy steps: as many CTAs as the device keeps resident at once (the occupancy of the
+// batch width's instance: 4 per SM at B = 1), so every warp walks its rows with the next 8 in
+// flight and no CTA waits for a second wave. Measured on B200 with V = 151936 before this
+// sizing: 297 CTAs (two per SM), 18.5 us per step.
+template <int NB>
+static int resident_ctas() {
+  static int cached = 0;  // a failed query (no device) is retried on the next call
+  if (cached) return cached;
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, markov_step_kernel<NB, false>, kThreads,
+                                                    0) != cudaSuccess || n < 1)
+    return 2;
+  cached = n;
+  return n;
+}
+static int ctas_per_sm(int B) {
+  switch (B) {
+    case 1: return resident_ctas<1>();
+    case 2: return resident_ctas<2>();
+    case 3: return resident_ctas<3>();
+    case 4: return resident_ctas<4>();
+    case 5: return resident_ctas<5>();
+    case 6: return resident_ctas<6>();
+    case 7: return resident_ctas<7>();
+    default: return resident_ctas<8>();
+  }
+}
+static int step_grid(int B, int V) {
+  const int by_rows = (V + 63) / 64;  // at least 8 rows per warp
+  const int g = std::min(by_rows, sm_count() * ctas_per_sm(B));
+  return g < 1 ? 1 : g;
+}
+
 static size_t ws(int B, int V, int* grid_out, size_t* off_i, size_t* off_c) {
-  // one thread per vocabulary row, two rows per thread
-  int grid = (V + 2 * kThreads - 1) / (2 * kThreads);
-  if (grid < 1) grid = 1;
+  const int grid = step_grid(B, V);
   if (grid_out) *grid_out = grid;
   // counter word first (fixed offset for every shape), then the two partial arrays
   const size_t pv = (((size_t)grid * B * 4) + 255) & ~(size_t)255;
