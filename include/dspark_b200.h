@@ -6,8 +6,10 @@
  * Conventions shared by every entry point:
  *   - Pointers are device pointers unless a parameter says "host". Shapes are explicit
  *     ints; leading dimensions are in elements. No torch types cross this boundary.
- *   - Calls are stream-ordered and asynchronous; nothing is allocated inside the library.
- *     Scratch memory is passed in by the caller (sizes from the *_workspace_bytes queries).
+ *   - Calls are stream-ordered and asynchronous; nothing is allocated inside the library
+ *     except by dspark_peer_alloc (the IPC-shareable buffers of the tensor-parallel fused
+ *     all-reduce). Scratch memory is passed in by the caller (sizes from the *_workspace_bytes
+ *     queries).
  *   - The return value is a status code (DSPARK_OK = 0). On failure the thread-local
  *     message from dspark_last_error() says what was wrong.
  *   - Kernels that wait on the device (pipeline barriers, grid barriers) give up after a
@@ -55,7 +57,9 @@ enum {
   DSPARK_EPI_RESIDUAL_BF16 = 1, /* y[m,n] = bf16(r[m,n] + bf16(acc)); y may alias r          */
   DSPARK_EPI_SILU_MUL_F16 = 2,  /* gate/up interleaved in 64-row halves of each 128-row tile;
                                    y[m,j] = fp16(bf16(bf16(silu(g)) * u)), y has N/2 columns */
-  DSPARK_EPI_STORE_F32 = 3      /* y[m,n] = acc (fp32)                                       */
+  DSPARK_EPI_STORE_F32 = 3,     /* y[m,n] = acc (fp32)                                       */
+  DSPARK_EPI_PEER_F32 = 4       /* dspark_w8a16_gemm_peer only: acc to every rank's receive
+                                   buffer, then the tile's epoch flag (fused all-reduce)      */
 };
 
 /* library identity */
@@ -143,6 +147,52 @@ int dspark_w8a16_gemm_split_mode(int mode);
  * the cluster size of the split-K form (0 = stream-K), *max_active (optional) = how many
  * clusters of the preferred size the device keeps resident (-1 if none or not queried). */
 int dspark_w8a16_gemm_plan(int M, int N, int K, int* grid, int* cluster, int* max_active);
+
+/* -------------------------------------------------------------------------------------
+ * K1p — tensor-parallel row-split projection with its all-reduce fused into the GEMM: the
+ * GEMM-epilogue one-shot all-reduce over NVLink peer memory. Replaces, for the tensor-parallel
+ * Qwen3-32B target, the NCCL all-reduce of [M, N] after o_proj and down_proj and the residual
+ * add after it (no reference counterpart: the reference runs on one device).
+ *
+ * Every rank holds a receive buffer recv [2][world][m_cap][N] fp32 and flags [2][world][N/128]
+ * int32, both from dspark_peer_alloc, and maps every peer's pair through CUDA IPC handles. For
+ * all-reduce number `epoch` (1, 2, ...; slot = epoch & 1):
+ *   - dspark_w8a16_gemm_peer: the CTA that finishes output tile t stores its fp32 tile (rows
+ *     < M, columns 128t..128t+127) into recv_r[slot][rank] of every rank r with plain
+ *     stores over NVLink, then, after a system-scope fence, writes epoch into
+ *     flags_r[slot][rank][t] with a system-scope release store. No TMA and no multicast.
+ *   - dspark_peer_reduce_residual: on each rank, CTA t waits (acquire loads, bounded by
+ *     timeout_ns, DSPARK_ERR_TIMEOUT in *status on expiry) until flags[slot][r][t] == epoch for
+ *     every r, then h[m, n] = bf16(h[m, n] + bf16(sum over r in rank order of recv[slot][r][m][n])).
+ * Two slots keep epoch e + 2's stores out of a slot a peer may still read for epoch e: a rank
+ * issues them only after its own reduce for e + 1 has seen every peer's flags for e + 1, which
+ * each peer raises after its reduce for e. Every rank calls both, in the same order, every epoch.
+ * ------------------------------------------------------------------------------------- */
+typedef struct dspark_peer_ar {
+  void* recv[8];   /* rank r's receive buffer as mapped in this process (own one at [rank]) */
+  void* flags[8];  /* rank r's flag array as mapped in this process */
+  int world;       /* ranks, 2..8 */
+  int rank;
+  int m_cap;       /* rows per rank slot in recv */
+  int n;           /* columns (the projection's N, a multiple of 128) */
+  int epoch;       /* this all-reduce's number, >= 1 */
+  int reserved;
+} dspark_peer_ar;
+/* cudaMalloc'd, zero-filled memory for recv / flags (IPC needs its own allocation), and its
+ * release. These two entry points allocate; nothing else in the library does. */
+int dspark_peer_alloc(size_t bytes, void** ptr);
+int dspark_peer_free(void* ptr);
+/* 64-byte CUDA IPC handle of a dspark_peer_alloc pointer; open a peer's handle in this process
+ * (peer access enabled) and close it again. */
+int dspark_ipc_handle(const void* ptr, void* handle64);
+int dspark_ipc_open(const void* handle64, void** ptr);
+int dspark_ipc_close(void* ptr);
+/* y = x . W^T of this rank's K-slice, all-reduced as described above (M <= min(64, m_cap)). */
+int dspark_w8a16_gemm_peer(const void* x, int ldx, const uint8_t* wq, const uint32_t* wsb, int M,
+                           int N, int K, const dspark_peer_ar* ar, void* workspace,
+                           size_t workspace_bytes, int* status, dspark_stream_t stream);
+int dspark_peer_reduce_residual(void* h, int ldh, int M, const dspark_peer_ar* ar,
+                                long long timeout_ns, int* status, dspark_stream_t stream);
 
 /* -------------------------------------------------------------------------------------
  * K1w — the same W8A16 product for prefill chunks (large M). Replaces the QuantizedLinear

@@ -12,10 +12,11 @@ from pathlib import Path
 LIB_PATH = Path(__file__).resolve().with_name("libdspark_b200.so")
 
 DSPARK_OK = 0
+DSPARK_ERR_TIMEOUT = 4
 ERR_NAMES = {1: "invalid argument", 2: "alignment", 3: "launch failed", 4: "device wait timed out",
              5: "unsupported", 6: "CUDA error", 7: "workspace"}
 
-EPI_STORE_BF16, EPI_RESIDUAL_BF16, EPI_SILU_MUL_F16, EPI_STORE_F32 = 0, 1, 2, 3
+EPI_STORE_BF16, EPI_RESIDUAL_BF16, EPI_SILU_MUL_F16, EPI_STORE_F32, EPI_PEER_F32 = 0, 1, 2, 3, 4
 
 
 class DsparkError(RuntimeError):
@@ -56,6 +57,14 @@ class GemmOpts(ctypes.Structure):
                 ("reserved2", c_int)]
 
 
+class PeerAR(ctypes.Structure):
+    """dspark_peer_ar (include/dspark_b200.h): the ranks' mapped buffers of one fused
+    all-reduce."""
+    _fields_ = [("recv", c_void_p * 8), ("flags", c_void_p * 8), ("world", c_int),
+                ("rank", c_int), ("m_cap", c_int), ("n", c_int), ("epoch", c_int),
+                ("reserved", c_int)]
+
+
 # name -> (restype, argtypes); mirrors include/dspark_b200.h
 SIGNATURES = {
     "dspark_version": (I, []),
@@ -68,6 +77,13 @@ SIGNATURES = {
     "dspark_w8a16_gemm_simt": (I, [P, I, P, P, I, I, I, P, I, P, I, I, P]),
     "dspark_w8a16_gemm_split_mode": (I, [I]),
     "dspark_w8a16_gemm_plan": (I, [I, I, I, P, P, P]),
+    "dspark_peer_alloc": (I, [c_size_t, POINTER(c_void_p)]),
+    "dspark_peer_free": (I, [P]),
+    "dspark_ipc_handle": (I, [P, P]),
+    "dspark_ipc_open": (I, [P, POINTER(c_void_p)]),
+    "dspark_ipc_close": (I, [P]),
+    "dspark_w8a16_gemm_peer": (I, [P, I, P, P, I, I, I, POINTER(PeerAR), P, c_size_t, P, P]),
+    "dspark_peer_reduce_residual": (I, [P, I, I, POINTER(PeerAR), c_longlong, P, P]),
     "dspark_w8a16_gemm_wide": (I, [P, I, P, P, I, I, I, I, P, I, P, I, P, I, P, P]),
     "dspark_w8a16_gemm_wide_plan": (I, [I, I, I, P, P]),
     "dspark_embed_w8": (I, [P, I, P, P, I, I, P, I, P]),

@@ -100,6 +100,10 @@ struct Params {
   // range after issuing its last load (16-byte aligned, sizes multiples of 16)
   const char* pf_ptr[2];
   unsigned long long pf_bytes[2];
+  // PEER_F32 (dspark_w8a16_gemm_peer): every rank's receive buffer and flags, as mapped here
+  float* peer_y[8];
+  int* peer_f[8];
+  int peer_world, peer_rank, peer_mcap, peer_epoch;
 };
 
 __device__ __forceinline__ long long range_start(long long b, long long total, long long G) {
@@ -112,7 +116,9 @@ __device__ __forceinline__ long long range_owner(long long g, long long total, l
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
 
-template <int BN>
+// PEER: the instance of the tensor-parallel fused all-reduce (dspark_w8a16_gemm_peer); the
+// other instances carry no code for it
+template <int BN, bool PEER = false>
 __device__ __forceinline__ void epilogue_store(const Params& p, int tile, int er, const float* acc,
                                                float* xch,
                                                const __nv_bfloat162* rpre = nullptr) {
@@ -138,6 +144,28 @@ __device__ __forceinline__ void epilogue_store(const Params& p, int tile, int er
           p.ss_out[(size_t)er * p.tiles + tile] =
               ((xch[er] + xch[BN + er]) + xch[2 * BN + er]) + xch[3 * BN + er];
         asm volatile("bar.sync 1, 128;" ::: "memory");
+      }
+      break;
+    }
+    case DSPARK_EPI_PEER_F32: {
+      if constexpr (PEER) {
+        // one-shot all-reduce, send half: this rank's fp32 tile into slot (epoch & 1), source row
+        // block `rank`, of every rank's receive buffer (plain stores over NVLink), then, once the
+        // tile's 128 threads have stored, the tile's epoch flag on every rank
+        const int slot = p.peer_epoch & 1;
+        const size_t off = ((size_t)(slot * p.peer_world + p.peer_rank) * p.peer_mcap) * p.N + n;
+        for (int r = 0; r < p.peer_world; ++r) {
+          float* y = p.peer_y[r] + off;
+#pragma unroll
+          for (int m = 0; m < BN; ++m)
+            if (m < p.M) y[(size_t)m * p.N] = acc[m];
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (er == 0) {
+          __threadfence_system();
+          const size_t fo = (size_t)(slot * p.peer_world + p.peer_rank) * p.tiles + tile;
+          for (int r = 0; r < p.peer_world; ++r) st_release_sys(p.peer_f[r] + fo, p.peer_epoch);
+        }
       }
       break;
     }
@@ -291,7 +319,7 @@ struct Smem {
   static constexpr uint32_t kTotal = 1024 + STAGES * kStageBytes + kXchBytes + kBarBytes;
 };
 
-template <int BN, int STAGES, bool CS, bool ROPE>
+template <int BN, int STAGES, bool CS, bool ROPE, bool PEER = false>
 __global__ void __launch_bounds__(kThreads, (BN <= 32 && !CS ? 2 : 1))
     w8a16_tc_kernel(const __grid_constant__ CUtensorMap tm_w,
                     const __grid_constant__ CUtensorMap tm_sb,
@@ -645,7 +673,7 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 && !CS ? 2 : 1))
         if constexpr (ROPE)
           rope_epilogue<BN>(p, tile, er, acc, xch);
         else
-          epilogue_store<BN>(p, tile, er, acc, xch);
+          epilogue_store<BN, PEER>(p, tile, er, acc, xch);
       } else {
         // partial of this CTA, row-major [128][MP] with MP = M rounded up to 4: thread er's
         // values are 16-byte vectors, and each contributor's partial is one contiguous
@@ -773,7 +801,7 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 && !CS ? 2 : 1))
           if constexpr (ROPE)
             rope_epilogue<BN>(p, tile, er, sum, xch);
           else
-            epilogue_store<BN>(p, tile, er, sum, xch, (kPre && res) ? rpre : nullptr);
+            epilogue_store<BN, PEER>(p, tile, er, sum, xch, (kPre && res) ? rpre : nullptr);
         }
         asm volatile("bar.sync 1, 128;" ::: "memory");
       }
@@ -1505,7 +1533,7 @@ static int plan_csplit(int tiles, int kb) {
   return 0;
 }
 
-template <int BN, bool ROPE = false>
+template <int BN, bool ROPE = false, bool PEER = false>
 static int launch_tc(const void* x, int ldx, const uint8_t* wq, const uint32_t* wsb, Params p,
                      cudaStream_t st) {
   constexpr int S = Cfg<BN>::kStages;
@@ -1524,7 +1552,7 @@ static int launch_tc(const void* x, int ldx, const uint8_t* wq, const uint32_t* 
     return rc;
   constexpr int SC = CfgCs<BN>::kStages;
   using LC = Smem<BN, SC>;
-  auto kern = w8a16_tc_kernel<BN, S, false, ROPE>;
+  auto kern = w8a16_tc_kernel<BN, S, false, ROPE, PEER>;
   auto kern_cs = w8a16_tc_kernel<BN, SC, true, false>;
   static bool configured = false;
   if (!configured) {
@@ -1545,7 +1573,7 @@ static int launch_tc(const void* x, int ldx, const uint8_t* wq, const uint32_t* 
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   // the fused epilogues (RoPE, row sums of squares) are stream-K only
-  p.csplit = (ROPE || p.ss_out) ? 0 : plan_csplit<BN>(p.tiles, p.kb);
+  p.csplit = (ROPE || p.ss_out || p.epilogue == DSPARK_EPI_PEER_F32) ? 0 : plan_csplit<BN>(p.tiles, p.kb);
   long long grid;
   if (p.csplit > 1) {
     grid = (long long)p.tiles * p.csplit;
@@ -1657,7 +1685,8 @@ static int gemm_launch(const void* x, int ldx, const uint8_t* wq, const uint32_t
                        int K, void* y, int ldy, const void* residual, int ldr, int epilogue,
                        void* workspace, size_t workspace_bytes, const void* pf0, size_t pf0_bytes,
                        const void* pf1, size_t pf1_bytes, const w8::RopeEpi* rope,
-                       const dspark_gemm_opts* opts, int* status, dspark_stream_t stream) {
+                       const dspark_gemm_opts* opts, int* status, dspark_stream_t stream,
+                       const dspark_peer_ar* peer = nullptr) {
   const size_t need = w8::ws_bytes(M, N, K);
   if (!workspace || workspace_bytes < need)
     return set_error(DSPARK_ERR_WORKSPACE, "w8a16_gemm: workspace %zu < %zu bytes", workspace_bytes, need);
@@ -1675,6 +1704,16 @@ static int gemm_launch(const void* x, int ldx, const uint8_t* wq, const uint32_t
   p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + counters);
   p.status = status;
   if (rope) p.rope = *rope;
+  if (peer) {
+    for (int r = 0; r < peer->world; ++r) {
+      p.peer_y[r] = static_cast<float*>(peer->recv[r]);
+      p.peer_f[r] = static_cast<int*>(peer->flags[r]);
+    }
+    p.peer_world = peer->world;
+    p.peer_rank = peer->rank;
+    p.peer_mcap = peer->m_cap;
+    p.peer_epoch = peer->epoch;
+  }
   if (opts) {
     if (opts->copy_f16) {
       if (epilogue != DSPARK_EPI_RESIDUAL_BF16 || opts->copy_f16_ld < N)
@@ -1714,6 +1753,14 @@ static int gemm_launch(const void* x, int ldx, const uint8_t* wq, const uint32_t
     p.pf_bytes[r] = pf[r] ? (unsigned long long)(pfb[r] & ~(size_t)15) : 0ull;
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (peer) {
+    switch (w8::pick_bn(M)) {
+      case 16: return w8::launch_tc<16, false, true>(x, ldx, wq, wsb, p, st);
+      case 32: return w8::launch_tc<32, false, true>(x, ldx, wq, wsb, p, st);
+      case 48: return w8::launch_tc<48, false, true>(x, ldx, wq, wsb, p, st);
+      default: return w8::launch_tc<64, false, true>(x, ldx, wq, wsb, p, st);
+    }
+  }
   if (rope) {
     switch (w8::pick_bn(M)) {
       case 16: return w8::launch_tc<16, true>(x, ldx, wq, wsb, p, st);
@@ -1804,6 +1851,27 @@ extern "C" int dspark_w8a16_gemm(const void* x, int ldx, const uint8_t* wq, cons
                                  int* status, dspark_stream_t stream) {
   return dspark_w8a16_gemm_pf(x, ldx, wq, wsb, M, N, K, y, ldy, residual, ldr, epilogue, workspace,
                               workspace_bytes, nullptr, 0, nullptr, 0, status, stream);
+}
+
+extern "C" int dspark_w8a16_gemm_peer(const void* x, int ldx, const uint8_t* wq,
+                                      const uint32_t* wsb, int M, int N, int K,
+                                      const dspark_peer_ar* ar, void* workspace,
+                                      size_t workspace_bytes, int* status, dspark_stream_t stream) {
+  if (!ar) return set_error(DSPARK_ERR_INVALID, "w8a16_gemm_peer: no peer descriptor");
+  if (ar->world < 2 || ar->world > 8 || ar->rank < 0 || ar->rank >= ar->world || ar->n != N ||
+      ar->epoch < 1 || M > ar->m_cap)
+    return set_error(DSPARK_ERR_INVALID,
+                     "w8a16_gemm_peer: world=%d rank=%d n=%d (N=%d) epoch=%d M=%d m_cap=%d",
+                     ar->world, ar->rank, ar->n, N, ar->epoch, M, ar->m_cap);
+  for (int r = 0; r < ar->world; ++r)
+    if (!ar->recv[r] || !ar->flags[r])
+      return set_error(DSPARK_ERR_INVALID, "w8a16_gemm_peer: rank %d's buffers missing", r);
+  int rc = gemm_common_checks(x, ldx, wq, wsb, M, N, K, ar->recv[ar->rank], DSPARK_EPI_STORE_F32,
+                              nullptr);
+  if (rc) return rc;
+  return gemm_launch(x, ldx, wq, wsb, M, N, K, ar->recv[ar->rank], N, nullptr, 0,
+                     DSPARK_EPI_PEER_F32, workspace, workspace_bytes, nullptr, 0, nullptr, 0,
+                     nullptr, nullptr, status, stream, ar);
 }
 
 extern "C" int dspark_w8a16_gemm_plan(int M, int N, int K, int* grid, int* cluster,

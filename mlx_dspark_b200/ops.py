@@ -157,6 +157,27 @@ def gemm(x16: torch.Tensor, w: PackedLinear, y: torch.Tensor, *, epilogue=_lib.E
     return y
 
 
+def gemm_peer(x16: torch.Tensor, w: PackedLinear, ar, *, scratch: Scratch,
+              M: int | None = None) -> None:
+    """This rank's row-split product x16 @ W^T sent to every rank's receive buffer, slot
+    (ar.epoch & 1), with the tiles' epoch flags (dspark_w8a16_gemm_peer)."""
+    _require_cuda(x16)
+    M = x16.shape[0] if M is None else M
+    assert x16.dtype == torch.float16 and x16.shape[-1] >= w.K
+    ws = scratch.get("gemm", gemm_workspace_bytes(M, w.N, w.K))
+    call("dspark_w8a16_gemm_peer", _p(x16), x16.stride(0), _p(w.q), _p(w.sb), M, w.N, w.K,
+         ctypes.byref(ar), _p(ws), ws.numel(), _p(scratch.status), _stream())
+
+
+def peer_reduce_residual(h: torch.Tensor, ar, M: int, scratch: Scratch,
+                         timeout_ns: int = 2_000_000_000) -> None:
+    """h[:M] = bf16(h + bf16(sum over ranks, in order, of this epoch's partials)), after a
+    bounded wait for every rank's flags (DSPARK_ERR_TIMEOUT in scratch.status on expiry)."""
+    _require_cuda(h)
+    call("dspark_peer_reduce_residual", _p(h), h.stride(0), M, ctypes.byref(ar), int(timeout_ns),
+         _p(scratch.status), _stream())
+
+
 def gemm_wide(x16: torch.Tensor, w: PackedLinear, y: torch.Tensor, *,
               epilogue=_lib.EPI_STORE_BF16, residual: torch.Tensor | None = None,
               scratch: Scratch, M: int | None = None,

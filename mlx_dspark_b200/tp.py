@@ -25,7 +25,9 @@ from dataclasses import replace
 import torch
 import torch.distributed as dist
 
-from . import ops
+import ctypes
+
+from . import _lib, ops
 from ._lib import EPI_SILU_MUL_F16, EPI_STORE_BF16, EPI_STORE_F32
 from .target import Target
 from .weights import GROUP, LayerWeights, QTensor, TargetWeights, pack
@@ -102,12 +104,67 @@ def shard_target(tw: TargetWeights, rank: int, world: int):
     return TargetWeights(rcfg, tw.embed, layers, tw.norm, head), v0, valid
 
 
+class PeerAllReduce:
+    """The buffers of the fused one-shot all-reduce (dspark_w8a16_gemm_peer +
+    dspark_peer_reduce_residual): this rank's receive buffer [2][world][m_cap][n] fp32 and flags
+    [2][world][n/128] int32, their CUDA IPC handles exchanged over the process group, and every
+    peer's pair mapped here. Every rank builds it at the same point (a collective) and takes
+    epochs in the same order."""
+
+    def __init__(self, rank: int, world: int, group, m_cap: int, n: int):
+        if not 2 <= world <= 8:
+            raise ValueError("the fused all-reduce takes 2..8 ranks")
+        L = _lib.lib()
+        self.world, self.rank, self.m_cap, self.n = world, rank, m_cap, n
+        self._own, self._mapped = [], []
+        mine = []
+        for nbytes in (2 * world * m_cap * n * 4, 2 * world * (n // 128) * 4):
+            p = ctypes.c_void_p()
+            _lib.check(L.dspark_peer_alloc(nbytes, ctypes.byref(p)), "dspark_peer_alloc")
+            self._own.append(p.value)
+            h = ctypes.create_string_buffer(64)
+            _lib.check(L.dspark_ipc_handle(p.value, h), "dspark_ipc_handle")
+            mine.append(h.raw)
+        handles = [None] * world
+        dist.all_gather_object(handles, mine, group=group)
+        self.ar = _lib.PeerAR()
+        for r in range(world):
+            for j, field in enumerate(("recv", "flags")):
+                if r == rank:
+                    ptr = self._own[j]
+                else:
+                    p = ctypes.c_void_p()
+                    _lib.check(L.dspark_ipc_open(handles[r][j], ctypes.byref(p)), "dspark_ipc_open")
+                    self._mapped.append(p.value)
+                    ptr = p.value
+                getattr(self.ar, field)[r] = ptr
+        self.ar.world, self.ar.rank, self.ar.m_cap, self.ar.n = world, rank, m_cap, n
+        self.epoch = 0
+
+    def next(self):
+        self.epoch += 1
+        self.ar.epoch = self.epoch
+        return self.ar
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's (after every rank is done with them)."""
+        L = _lib.lib()
+        for p in self._mapped:
+            L.dspark_ipc_close(p)
+        for p in self._own:
+            L.dspark_peer_free(p)
+        self._mapped, self._own = [], []
+
+
 class TPTarget(Target):
     """One rank's share of a tensor-parallel target. The process group must be NCCL (one
     process per GPU) for device tensors; every rank runs the same decode loop."""
 
     capturable = False  # rounds with collectives run eagerly
     use_chain = False   # the all-reduces sit between the projections
+    # o_proj / down_proj of verify-sized calls (M <= 64) all-reduce through the fused GEMM
+    # epilogue over NVLink peer memory; False, or larger calls (prefill chunks): NCCL
+    fused_allreduce = True
 
     def __init__(self, weights: TargetWeights, rank: int, world: int, group=None, tokenizer=None,
                  *, kv_bits: int | None = None, device="cuda"):
@@ -120,6 +177,7 @@ class TPTarget(Target):
                                                                           device=device)
         self._partials: dict[int, torch.Tensor] = {}
         self._shard: dict[int, tuple] = {}
+        self.peer: PeerAllReduce | None = None
 
     def _partial(self, M: int) -> torch.Tensor:
         p = self._partials.get(M)
@@ -131,6 +189,29 @@ class TPTarget(Target):
     def _all_reduce(self, t: torch.Tensor) -> None:
         dist.all_reduce(t, group=self.pg)
 
+    def _row_parallel(self, x16: torch.Tensor, w, h: torch.Tensor, M: int) -> None:
+        """h[:M] += all-reduce over ranks of x16 @ W^T (this rank's K-slice)."""
+        if self.fused_allreduce and M <= 64:
+            if self.peer is None:
+                self.peer = PeerAllReduce(self.rank, self.world, self.pg, 64, self.cfg.hidden_size)
+            ar = self.peer.next()
+            ops.gemm_peer(x16, w, ar, scratch=self.scratch, M=M)
+            ops.peer_reduce_residual(h, ar, M, self.scratch)
+            return
+        part = self._partial(M)
+        ops.gemm(x16, w, part, epilogue=EPI_STORE_F32, scratch=self.scratch, M=M)
+        self._all_reduce(part)
+        ops.residual_add_f32(h, part, M)
+
+    def release_peer(self) -> None:
+        """Free the fused all-reduce's buffers; every rank calls it together (a barrier first,
+        so no rank unmaps memory a peer may still write)."""
+        if self.peer is not None:
+            torch.cuda.synchronize()
+            dist.barrier(group=self.pg)
+            self.peer.close()
+            self.peer = None
+
     def forward(self, buf, state, tap=(), *, splits: int | None = None,
                 with_logits: bool = True) -> None:
         c, sc = self.cfg, self.scratch
@@ -138,7 +219,6 @@ class TPTarget(Target):
         splits = splits or self.attn_splits(B, state.max_pages)
         tap_idx = {l: j for j, l in enumerate(tap)}
         H = c.hidden_size
-        part = self._partial(M)
         ops.embed(buf.ids, self.embed, buf.h, M)
         for l, L in enumerate(self.layers):
             kv = state.layout(l)
@@ -146,14 +226,10 @@ class TPTarget(Target):
             self._qkv_rope(buf, L, kv, state, B, T, M)
             ops.attention(buf.q, B, T, c.num_attention_heads, kv, state.seq_len, True,
                           self.scale, buf.attn16, splits, sc)
-            ops.gemm(buf.attn16, L.o, part, epilogue=EPI_STORE_F32, scratch=sc, M=M)
-            self._all_reduce(part)
-            ops.residual_add_f32(buf.h, part, M)
+            self._row_parallel(buf.attn16, L.o, buf.h, M)
             ops.rmsnorm(buf.h, L.post_ln, c.rms_norm_eps, y16=buf.xn16, M=M)
             ops.gemm(buf.xn16, L.gu, buf.act16, epilogue=EPI_SILU_MUL_F16, scratch=sc, M=M)
-            ops.gemm(buf.act16, L.down, part, epilogue=EPI_STORE_F32, scratch=sc, M=M)
-            self._all_reduce(part)
-            ops.residual_add_f32(buf.h, part, M)
+            self._row_parallel(buf.act16, L.down, buf.h, M)
             if l in tap_idx:
                 j = tap_idx[l]
                 ops.bf16_to_f16(buf.h, buf.fused16[:, j * H:(j + 1) * H], M, H)

@@ -47,6 +47,7 @@ def _rank_body(rank, world, port, q, log):
     from mlx_dspark_b200.weights import generate_dspark, generate_target
     rank, world, dev = init_process_group("nccl", timeout_s=60)
     print("initialised", flush=True)
+    target = None
     try:
         tw = generate_target(TINY, 0, "cpu")
         target = TPTarget(tw, rank, world, device=dev)
@@ -57,6 +58,17 @@ def _rank_body(rank, world, port, q, log):
         print("loaded", flush=True)
         logits, _ = target.run([prompt], target.make_cache(256), ())
         print("forward done", flush=True)
+        # a 9-token verify forward with the fused all-reduce (default) and with NCCL: with two
+        # ranks the fp32 sum of the two partials is the same in either order, so bitwise
+        outs = []
+        for fused in (True, False):
+            target.fused_allreduce = fused
+            outs.append(target.run([prompt[:9]], target.make_cache(64), ())[0])
+        target.fused_allreduce = True
+        target.scratch.check_status()
+        fused_same = torch.equal(outs[0], outs[1])
+        assert target.peer is not None and target.peer.epoch == 2 * TINY.num_hidden_layers
+        print("fused all-reduce checked", flush=True)
         local = logits[0, :, :target.vocab_valid].contiguous()
         parts = [torch.zeros_like(local) for _ in range(world)]
         dist.all_gather(parts, local)
@@ -70,8 +82,11 @@ def _rank_body(rank, world, port, q, log):
         dist.all_gather(all_toks, toks)
         if rank == 0:
             q.put(("ok", torch.cat(parts, 1).float().cpu(), prompt, spec.token_ids[:48],
-                   plain.token_ids[:32], all(torch.equal(t, all_toks[0]) for t in all_toks)))
+                   plain.token_ids[:32], all(torch.equal(t, all_toks[0]) for t in all_toks),
+                   fused_same))
     finally:
+        if target is not None:
+            target.release_peer()
         dist.destroy_process_group()
 
 
@@ -109,9 +124,9 @@ def test_tp2_matches_oracle():
                 p.join(timeout=30)
     assert msg is not None, "no result from the ranks (see gpurun_out/tp_rank*.log)"
     assert msg[0] == "ok", msg
-    _, gl, prompt, spec, plain, same = msg
+    _, gl, prompt, spec, plain, same, fused_same = msg
     assert all(p.exitcode == 0 for p in procs)
-    assert same
+    assert same and fused_same
     ref = Qwen3Ref(generate_target(TINY, 0, "cpu"))
     rl, _ = ref.run(prompt, ref.make_cache())
     scale = rl.abs().amax(-1, keepdim=True)
