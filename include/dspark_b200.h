@@ -204,13 +204,17 @@ int dspark_peer_reduce_residual(void* h, int ldh, int M, const dspark_peer_ar* a
  *   dspark_gemm_opts), SILU_MUL_F16 (interleaved gate/up pack, y [M, N/2]) or STORE_F32.
  * Outputs are the verify GEMM's: the same fp16 weights, fp32 accumulation (in another order)
  * and the same epilogue roundings. Persistent tcgen05 kernel, one CTA per SM, tiles of 128
- * weight rows x 256 tokens (128 when M <= 128); no workspace. */
+ * weight rows x 256 tokens (128 tokens when M <= 256 or when 256-token tiles would number at
+ * most 64); no workspace. */
 int dspark_w8a16_gemm_wide(const void* x, int ldx, const uint8_t* wq, const uint32_t* wsb, int M,
                            int N, int K, int epilogue, void* y, int ldy, const void* residual,
                            int ldr, void* copy_f16, int copy_f16_ld, int* status,
                            dspark_stream_t stream);
 /* The launch dspark_w8a16_gemm_wide makes for this shape: *bn tokens per tile, *grid CTAs. */
 int dspark_w8a16_gemm_wide_plan(int M, int N, int K, int* bn, int* grid);
+/* Tokens per tile of dspark_w8a16_gemm_wide, process-wide: 0 (default) picks by M, 128 or 256
+ * forces that width (measurements; no reference counterpart). */
+int dspark_w8a16_gemm_wide_bn(int bn);
 
 /* -------------------------------------------------------------------------------------
  * K13 — embedding dequant-gather. Replaces mlx QuantizedEmbedding (embed_tokens,

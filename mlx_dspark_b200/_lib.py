@@ -86,6 +86,7 @@ SIGNATURES = {
     "dspark_peer_reduce_residual": (I, [P, I, I, POINTER(PeerAR), c_longlong, P, P]),
     "dspark_w8a16_gemm_wide": (I, [P, I, P, P, I, I, I, I, P, I, P, I, P, I, P, P]),
     "dspark_w8a16_gemm_wide_plan": (I, [I, I, I, P, P]),
+    "dspark_w8a16_gemm_wide_bn": (I, [I]),
     "dspark_embed_w8": (I, [P, I, P, P, I, I, P, I, P]),
     "dspark_embed_w8_sumsq": (I, [P, I, P, P, I, I, P, I, P, P]),
     "dspark_embed_block_w8": (I, [P, I, I, I, P, P, I, I, P, I, P, P]),

@@ -463,7 +463,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-static int pick_bn(int M) { return M > 128 ? 256 : 128; }
+// Tokens per tile. 256 halves the weight conversions and the shared-memory traffic per token,
+// 128 doubles the tiles of a short call. Measured on B200 (Qwen3-8B q|k|v, o, gate|up, down,
+// us for the four): M 256: 241 at 128 vs 288 at 256; M 512: o and down faster at 128 (64 tiles
+// of 256 for 148 SMs), q|k|v and gate|up at 256; M >= 768: 256 for every shape. Hence 128 when
+// M <= 256 or when 256-token tiles would number at most 64. g_force_bn (dspark_w8a16_gemm_wide_bn)
+// overrides the choice for measurements and tests.
+static int g_force_bn = 0;
+static int pick_bn(int M, int N) {
+  if (g_force_bn) return g_force_bn;
+  const long long tiles256 = (long long)(N / BM) * ((M + 255) / 256);
+  return (M <= 256 || tiles256 <= 64) ? 128 : 256;
+}
 
 template <int BN>
 static int launch_wide(const void* x, int ldx, const uint8_t* wq, const uint32_t* wsb,
@@ -517,10 +528,17 @@ static int launch_wide(const void* x, int ldx, const uint8_t* wq, const uint32_t
 
 using namespace dspark;
 
+extern "C" int dspark_w8a16_gemm_wide_bn(int bn) {
+  if (bn != 0 && bn != 128 && bn != 256)
+    return set_error(DSPARK_ERR_INVALID, "w8a16_gemm_wide_bn: %d (0, 128 or 256)", bn);
+  w8w::g_force_bn = bn;
+  return DSPARK_OK;
+}
+
 extern "C" int dspark_w8a16_gemm_wide_plan(int M, int N, int K, int* bn, int* grid) {
   if (M < 1 || N <= 0 || K <= 0 || N % w8w::BM || K % w8w::BK || !bn || !grid)
     return set_error(DSPARK_ERR_INVALID, "w8a16_gemm_wide_plan: M=%d N=%d K=%d", M, N, K);
-  const int b = w8w::pick_bn(M);
+  const int b = w8w::pick_bn(M, N);
   const long long tiles = (long long)(N / w8w::BM) * ((M + b - 1) / b);
   *bn = b;
   *grid = (int)std::min<long long>(tiles, sm_count());
@@ -558,7 +576,7 @@ extern "C" int dspark_w8a16_gemm_wide(const void* x, int ldx, const uint8_t* wq,
   p.copy16_ld = copy_f16_ld;
   p.status = status;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (w8w::pick_bn(M) == 256) {
+  if (w8w::pick_bn(M, N) == 256) {
     p.m_tiles = (M + 255) / 256;
     return w8w::launch_wide<256>(x, ldx, wq, wsb, p, st);
   }

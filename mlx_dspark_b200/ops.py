@@ -196,6 +196,11 @@ def gemm_wide(x16: torch.Tensor, w: PackedLinear, y: torch.Tensor, *,
     return y
 
 
+def gemm_wide_bn(bn: int) -> None:
+    """Force the prefill GEMM's tokens per tile (128 / 256), or 0 to pick by M."""
+    call("dspark_w8a16_gemm_wide_bn", int(bn))
+
+
 def gemm_wide_plan(M: int, N: int, K: int) -> dict:
     bn, grid = ctypes.c_int(), ctypes.c_int()
     call("dspark_w8a16_gemm_wide_plan", M, N, K, ctypes.byref(bn), ctypes.byref(grid))

@@ -33,10 +33,26 @@ WIDE_SHAPES = [
 ]
 
 
+@pytest.fixture()
+def force_bn():
+    """Force the prefill GEMM's tokens per tile for one test, then restore the automatic pick."""
+    yield ops.gemm_wide_bn
+    ops.gemm_wide_bn(0)
+
+
+def test_gemm_wide_tile_width_rule():
+    """128 tokens per tile for short calls or few tiles, 256 otherwise (measured on B200)."""
+    for M, N, want in [(1, 128, 128), (256, 24576, 128), (512, 4096, 128), (512, 6144, 256),
+                       (768, 4096, 256), (1024, 4096, 256), (2048, 512, 128), (257, 6144, 256)]:
+        assert ops.gemm_wide_plan(M, N, 4096)["bn"] == want, (M, N)
+
+
+@pytest.mark.parametrize("bn", [128, 256])
 @pytest.mark.parametrize("M,N,K", WIDE_SHAPES)
-def test_gemm_wide_matches_fp32_bound(cuda, M, N, K):
+def test_gemm_wide_matches_fp32_bound(cuda, force_bn, M, N, K, bn):
     """fp32 outputs inside the fp16-weight bound (as the verify GEMM's test), deterministic
-    across calls."""
+    across calls, at both tile widths."""
+    force_bn(bn)
     qt = _qrand(N, K, seed=M * 31 + N + K)
     w = pack(qt, device=cuda)
     x = _x16(M, K, seed=N + K)
@@ -59,13 +75,15 @@ def test_gemm_wide_matches_fp32_bound(cuda, M, N, K):
                     f"max err {err.max():.3e}, ref max {ref.abs().max():.3e}")
     assert torch.equal(ys[0], ys[1])
     plan = ops.gemm_wide_plan(M, N, K)
-    assert plan["bn"] == (256 if M > 128 else 128) and plan["grid"] >= 1
+    assert plan["bn"] == bn and plan["grid"] >= 1
 
 
-def test_gemm_wide_kmap_diagnostic(cuda):
+@pytest.mark.parametrize("bn", [128, 256])
+def test_gemm_wide_kmap_diagnostic(cuda, force_bn, bn):
     """One-hot activation rows read single weight columns, Y[m, n] = W[n, k_m], at rows in
-    several 256-row tiles: pins the k <-> TMEM column mapping of the converter, the 64-byte
+    several token tiles: pins the k <-> TMEM column mapping of the converter, the 64-byte
     swizzle of the weight tile and the activation-row addressing."""
+    force_bn(bn)
     N, K = 256, 256
     ks = [0, 1, 2, 7, 8, 15, 16, 31, 32, 47, 63, 64, 65, 100, 127, 128, 191, 200, 255]
     M = 600
