@@ -62,6 +62,9 @@ def parse():
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     ap.add_argument("--layers", type=int, default=None,
                     help="depth-reduced target (same widths) for profiling captures")
+    ap.add_argument("--tp-allreduce", action="store_true",
+                    help="under torchrun (2..8 ranks): one row-split projection of the Qwen3-32B "
+                         "shapes at M = 9, the fused peer all-reduce against NCCL, one JSON line")
     ap.add_argument("--serve", action="store_true",
                     help="the continuous-batching workload (C4 shapes: 32 requests over 4 slots, a "
                          "shared 2048-token prefix, 8-bit KV) through serve_requests, one JSON line")
@@ -365,6 +368,74 @@ def prefill_measure(target, drafter, prompt, reps=2):
                                         "the GEMMs are timed alone)"}}
 
 
+def run_tp_allreduce(world, rank):
+    """o_proj and down_proj of Qwen3-32B split over `world` ranks at M = 9: GEMM + all-reduce +
+    residual add, the fused peer form (dspark_w8a16_gemm_peer + dspark_peer_reduce_residual)
+    against GEMM + NCCL all-reduce + dspark_residual_add_f32. 50 calls back to back, twice per
+    form, CUDA events, max over ranks."""
+    import torch.distributed as dist
+    from mlx_dspark_b200 import ops
+    from mlx_dspark_b200._lib import EPI_STORE_F32
+    from mlx_dspark_b200.tp import PeerAllReduce
+    from mlx_dspark_b200.weights import pack, quantize_w8g64
+
+    if world < 2:
+        raise SystemExit("--tp-allreduce runs under torchrun with 2..8 ranks")
+    dev = torch.device("cuda", torch.cuda.current_device())
+    H, M = 5120, 9
+    shapes = {"o_proj": (H, 8192 // world), "down_proj": (H, 25600 // world)}
+    sc = ops.Scratch(dev)
+    peer = PeerAllReduce(rank, world, None, 64, H)
+    res = {}
+    try:
+        for name, (N, K) in shapes.items():
+            g = torch.Generator(device=dev).manual_seed(rank * 7 + K)
+            w = pack(quantize_w8g64(torch.randn(N, K, generator=g, device=dev) * 0.02), device=dev)
+            x = torch.randn(M, K, device=dev, generator=g).to(torch.float16)
+            h = torch.zeros(M, H, dtype=torch.bfloat16, device=dev)
+            part = torch.zeros(M, H, dtype=torch.float32, device=dev)
+
+            def fused():
+                ar = peer.next()
+                ops.gemm_peer(x, w, ar, scratch=sc, M=M)
+                ops.peer_reduce_residual(h, ar, M, sc)
+
+            def nccl():
+                ops.gemm(x, w, part, epilogue=EPI_STORE_F32, scratch=sc, M=M)
+                dist.all_reduce(part)
+                ops.residual_add_f32(h, part, M)
+
+            for label, fn in (("fused", fused), ("nccl", nccl)) * 2:
+                for _ in range(5):
+                    fn()
+                torch.cuda.synchronize()
+                dist.barrier()
+                torch.cuda.synchronize()
+                a = torch.cuda.Event(enable_timing=True)
+                b = torch.cuda.Event(enable_timing=True)
+                a.record()
+                for _ in range(50):
+                    fn()
+                b.record()
+                torch.cuda.synchronize()
+                us = torch.tensor([a.elapsed_time(b) * 1000 / 50], device=dev)
+                dist.all_reduce(us, op=dist.ReduceOp.MAX)
+                res[f"{name}/{label}"] = round(float(us), 2)   # the second pass is kept
+            sc.check_status()
+    finally:
+        torch.cuda.synchronize()
+        dist.barrier()
+        peer.close()
+    if rank == 0:
+        print(json.dumps({"metric": "us per row-split projection + all-reduce + residual (M=9)",
+                          "unit": "us", "higher_is_better": False, "n_gpus": world,
+                          "config": {"model": "Qwen3-32B shapes", "tp": world},
+                          "data": "synthetic: random W8 weights and activations", **res}), flush=True)
+    import torch.distributed as _d
+    _d.destroy_process_group()
+    return 0
+
+
 def run_serve(args):
     """C4 on one GPU: 32 requests (a shared random 2048-token prefix plus a random 64-2048-token
     suffix, 128-1024 output tokens) through serve_requests with 4 slots, the 8-bit KV cache and
@@ -598,6 +669,8 @@ def main():
         return run_profile_prefill(args)
     if args.serve:
         return run_serve(args)
+    if args.tp_allreduce:
+        return run_tp_allreduce(world, rank)
     try:
         out = run_ours(args, world, rank)
         if rank == 0:
