@@ -226,12 +226,12 @@ __global__ void __launch_bounds__(kThreads) markov_step_kernel(
 // batch width's instance: 4 per SM at B = 1), so every warp walks its rows with the next 8 in
 // flight and no CTA waits for a second wave. Measured on B200 with V = 151936 before this
 // sizing: 297 CTAs (two per SM), 18.5 us per step.
-template <int NB>
+template <int NB, bool SAMPLE = false>
 static int resident_ctas() {
   static int cached = 0;  // a failed query (no device) is retried on the next call
   if (cached) return cached;
   int n = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, markov_step_kernel<NB, false>, kThreads,
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, markov_step_kernel<NB, SAMPLE>, kThreads,
                                                     0) != cudaSuccess || n < 1)
     return 2;
   cached = n;
@@ -248,6 +248,23 @@ static int ctas_per_sm(int B) {
     case 7: return resident_ctas<7>();
     default: return resident_ctas<8>();
   }
+}
+// the SAMPLE form (temperature drafts) writes the biased logits and keeps no partials
+static int sample_ctas_per_sm(int B) {
+  switch (B) {
+    case 1: return resident_ctas<1, true>();
+    case 2: return resident_ctas<2, true>();
+    case 3: return resident_ctas<3, true>();
+    case 4: return resident_ctas<4, true>();
+    case 5: return resident_ctas<5, true>();
+    case 6: return resident_ctas<6, true>();
+    case 7: return resident_ctas<7, true>();
+    default: return resident_ctas<8, true>();
+  }
+}
+static int sample_grid(int B, int V) {
+  const int g = std::min((V + 63) / 64, sm_count() * sample_ctas_per_sm(B));
+  return g < 1 ? 1 : g;
 }
 static int step_grid(int B, int V) {
   const int by_rows = (V + 63) / 64;  // at least 8 rows per warp
@@ -347,7 +364,7 @@ extern "C" int dspark_markov_sample_block_probs(
                      workspace_bytes, need);
   const int ld_out = (V + 7) & ~7;
   __nv_bfloat16* out = static_cast<__nv_bfloat16*>(workspace);
-  const int grid = (V + 2 * mk::kThreads - 1) / (2 * mk::kThreads);
+  const int grid = mk::sample_grid(B, V);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   auto run = [&](auto kern) {
     for (int i = 0; i < cap; ++i) {
