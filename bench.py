@@ -155,6 +155,28 @@ def allreduce_max(x: float, world: int) -> float:
     return float(t.item())
 
 
+def gather_all(obj, world: int) -> list:
+    """Every rank's `obj` (a small JSON-able value), in rank order."""
+    if world == 1:
+        return [obj]
+    import torch.distributed as dist
+    out = [None] * world
+    dist.all_gather_object(out, obj)
+    return out
+
+
+def cpu_model() -> str:
+    """The host CPU's model name (lscpu / /proc/cpuinfo)."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 def allreduce_sum(x: float, world: int) -> float:
     if world == 1:
         return x
@@ -297,6 +319,7 @@ def cpu_baseline(tw, prompt_len, budget):
     cw = tw.to("cpu")
     tps, n, dt, threads = time_greedy_decode(cw, prompt_len, budget_s=budget)
     return {"value": round(tps, 4), "unit": "tok/s", "cores": threads, "kind": "port",
+            "cpu": cpu_model(), "os_cpu_count": os.cpu_count(),
             "sample": f"{n} plain greedy decode steps of the Qwen3-8B W8 target at a "
                       f"{prompt_len}-token context (oracle port, fp32 math, int8 weights "
                       f"dequantized per step; KV of the context filled synthetically), "
@@ -526,7 +549,9 @@ def run_ours(args, world, rank):
     # take (at most one per token); past the last row the override repeats it, which would
     # replace the Bernoulli draw by one fixed pattern. The leading rows do not depend on the count.
     agree_rounds = max(rounds, 512 + cap + 2)
-    agree = (torch.rand(1, agree_rounds, cap, generator=torch.Generator().manual_seed(7)) < (wl.accept_p or 0.7)).to(torch.uint8)
+    p_agree = wl.accept_p or 0.7
+    expect_len = 1.0 + sum(p_agree ** i for i in range(1, cap + 1))
+    agree = (torch.rand(1, agree_rounds, cap, generator=torch.Generator().manual_seed(7)) < p_agree).to(torch.uint8)
     override = {"ref": torch.tensor([ref]), "agree": agree, "prompt_len": [prompt_len]}
     budget = prompt_len + ref_len + 64
     sess = SpecSession(target, drafter, 1, cap, budget, override=override)
@@ -566,6 +591,9 @@ def run_ours(args, world, rank):
     max_ms = allreduce_max(ms, world)
     all_tokens = allreduce_sum(float(tokens), world)
     value = all_tokens / (max_ms / 1000.0)
+    per_rank = gather_all({"rank": rank, "round_us": round(ms * 1000.0 / K, 1),
+                           "accept": round(tokens / K, 3), "verify_us": round(vus, 1),
+                           "sm_mhz": clk.get("sm_mhz"), "reasons": clk.get("reasons")}, world)
     peaks = load_peaks()
     out = {
         "metric": "accepted tok/s Qwen3-8B W8 DSpark (1/N GPU); verify-step us; HBM GB/s",
@@ -581,6 +609,11 @@ def run_ours(args, world, rank):
         "mean_accept_len": round(tokens / K, 3),
         "verify_step_us": round(vus, 1),
         "round_us": round(max_ms * 1000.0 / K, 1),
+        # tok/s if every round committed the configured expectation, 1 + sum_i p^i over the
+        # cap (3.20 at p = 0.7, cap 8): removes the mask sample's noise from the comparison
+        "expected_accept_len": round(expect_len, 3),
+        "value_at_expected_accept": round(world * expect_len / (max_ms / 1000.0 / K), 2),
+        "per_rank": per_rank,
         "verify_hbm_gbs": round(target.weight_bytes() / (vus * 1e-6) / 1e9, 1),
         "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4),
@@ -592,7 +625,7 @@ def run_ours(args, world, rank):
         "clocks": clk,
     }
     if not args.no_e2e and not args.profile:
-        res = speculative_generate(target, None, drafter, prompt_ids=prompt,
+        res = speculative_generate(target, None, drafter, lookup_drafts=False, prompt_ids=prompt,
                                    max_new_tokens=min(512, ref_len - 16), max_draft_tokens=cap,
                                    draft_override=override)
         e2e_tps = (res.num_tokens - 1) / res.decode_seconds
@@ -648,6 +681,7 @@ def run_reference(args, world, rank):
         "config": {"workload": wl.name, "model": "Qwen3-8B-arch W8 g64 (plain greedy decode)",
                    "global_batch": 1, "prompt_len": wl.prompt_len, "parallelism": "host cores"},
         "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": dec.threads, "kind": "port",
+                         "cpu": cpu_model(), "os_cpu_count": os.cpu_count(),
                          "sample": f"{n} greedy decode steps at a {wl.prompt_len}-token context "
                                    f"(mlx absent: oracle port of greedy_generate), {dt:.1f} s"},
         "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0,

@@ -18,7 +18,7 @@
  *
  * Reference interfaces replaced (paths inside regeter/mlx-dspark):
  *   the mlx-lm Qwen3 forward called by src/mlx_dspark/target.py:58-75 and
- *   src/mlx_dspark/batch_engine.py:184-206; the DSpark drafter src/mlx_dspark/model.py:241-437;
+ *   src/mlx_dspark/batch_engine.py:184-206; the DSpark drafter src/mlx_dspark/model.py:220-320;
  *   the DFlash drafter src/mlx_dspark/dflash_model.py:100-208; greedy acceptance
  *   src/mlx_dspark/generate.py:905-921 and batch_engine.py:573-595; speculative-sampling
  *   acceptance src/mlx_dspark/generate.py:659-688 with src/mlx_dspark/sampling.py:18-49.
@@ -218,7 +218,7 @@ int dspark_w8a16_gemm_wide_bn(int bn);
 
 /* -------------------------------------------------------------------------------------
  * K13 — embedding dequant-gather. Replaces mlx QuantizedEmbedding (embed_tokens,
- * src/mlx_dspark/target.py:63; drafter embed src/mlx_dspark/model.py:372-373).
+ * src/mlx_dspark/target.py:63; drafter embed src/mlx_dspark/model.py:244-245).
  *   out[m, :] = bf16(scale * q[ids[m], :] + bias) * embed_scale (embed_scale 1 for Qwen3)
  * ids is a device array of M token ids (read on the device, so the call can sit in a
  * CUDA graph whose ids change between replays).
@@ -235,7 +235,7 @@ int dspark_embed_w8_sumsq(const int32_t* ids, int M, const uint8_t* wq, const ui
 /* -------------------------------------------------------------------------------------
  * K6 — RMSNorm over rows, mlx.fast.rms_norm semantics (fp32 math, one bf16 rounding).
  * Replaces the input/post-attention/final norms of the Qwen3 layers and the drafter's
- * hidden_norm / norm (src/mlx_dspark/model.py:375-376,386-390).
+ * hidden_norm / norm (src/mlx_dspark/model.py:247-248,258-262).
  *   y = bf16(x * rsqrt(mean(x^2) + eps) * w). y_bf16 and y_f16 (bf16 value stored as fp16,
  *   the GEMM input format) are both optional.
  * ------------------------------------------------------------------------------------- */
@@ -318,7 +318,7 @@ int dspark_run_chain(int M, const dspark_chain_phase* phases, int n_phases, void
  * Replaces: Qwen3 attention pre-SDPA (mlx-lm qwen3; q_norm/k_norm then rope at
  * cache.offset) with KVCache.update_and_fetch / QuantizedKVCache (target.py:44-46),
  * BatchCache.update_and_fetch (batch_engine.py:132-147), DSparkAttention._kv/update_ctx
- * (model.py:241-256).
+ * (model.py:113-128).
  *
  * qkv  : bf16 [B*T, ldqkv]; columns [0, Hq*hd) = q, then Hkv*hd of k, then Hkv*hd of v
  *        (Hq may be 0: then only k and v are present)
@@ -351,7 +351,7 @@ int dspark_w8a16_gemm_qkv_rope(const void* x, int ldx, const uint8_t* wq, const 
  *   causal = 1: query t sees keys j <= kv_len[b] + t   (target verify, mlx-lm mask /
  *               build_batch_mask batch_engine.py:170-178)
  *   causal = 0: every query sees every key              (drafter block attention,
- *               model.py:258-283, dflash_model.py:100-134)
+ *               model.py:130-156, dflash_model.py:100-134)
  * q   : bf16 [B*T, Hq*hd]; out: fp16 [B*T, ldo] (bf16-rounded, the o_proj GEMM input)
  * workspace: dspark_attention_workspace_bytes(...) bytes for the split partials.
  * Splits (at most max_splits, at least one page each) are merged in split order in one of
@@ -417,7 +417,7 @@ int dspark_accept_greedy_noalloc(const void* logits, int ld, int B, int T, int V
 /* -------------------------------------------------------------------------------------
  * K10 — DSpark Markov head + greedy block sampling: sequential over cap positions,
  *   logits_i = base_i + w2 . w1[prev];  prev = argmax(logits_i)   (first index on ties)
- * Replaces DSparkDrafter.sample_block (src/mlx_dspark/model.py:398-409) and the batched
+ * Replaces DSparkDrafter.sample_block (src/mlx_dspark/model.py:270-281) and the batched
  * _batched_sample_block (batch_engine.py:414-428).
  * base : bf16 base logits; position i of row b is row (b * rows_per_b + i), i < cap
  * first_prev: [B] (the pending token of each row)
@@ -438,7 +438,7 @@ int dspark_markov_sample_block(const void* base, int ld, int rows_per_b, int B, 
  *
  * Distribution of a row: p = truncate(softmax(x)), x = bf16(logits / bf16(T)) (temp_mode 0,
  * the `v_logits / temperature` of generate.py:673,543) or bf16(logits * bf16(1/T))
- * (temp_mode 1, the `logits * inv_t` of model.py:300). Top-k keeps values >= the k-th largest
+ * (temp_mode 1, the `logits * inv_t` of model.py:304). Top-k keeps values >= the k-th largest
  * (ties kept); the nucleus keeps values >= the smallest value whose strictly-larger mass is
  * below top_p (src/mlx_dspark/sampling.py:18-44). top_k = 0 and top_p = 1 disable the cuts.
  * Weights are 2^-40 fixed point of a documented exp2 polynomial; every draw is an inverse-CDF

@@ -83,6 +83,8 @@ class SpecSlots:
         if not batched_drafter:
             raise NotImplementedError("the per-row drafter mode (Stage A) is not built; the "
                                       "batched drafter covers it")
+        if getattr(drafter, "target", None) is not target:
+            drafter.bind(target)
         cfg = drafter.config
         # optional CapController: the cap of a round at batch width B is cap_for(B) (the live
         # cap at B = 1), and every row's outcome feeds its acceptance estimate

@@ -298,6 +298,8 @@ def calibrate(target, drafter, *, mode: str, target_repo: str = "", drafter_repo
     (calibrate.py:338-404). mode "dspark": caps 1..block_size, widths cap + 1; mode "dflash":
     caps up to block_size - 1, a sample of widths, and one drafter cost (the backbone always
     denoises the whole block)."""
+    if getattr(drafter, "target", None) is not target:
+        drafter.bind(target)
     k = int(drafter.config.block_size)
     if mode == "dspark":
         max_cap = k

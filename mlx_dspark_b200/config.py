@@ -3,7 +3,7 @@ the named workload presets of the benchmark (C1..C5).
 
 ``DSparkConfig`` keeps the field names of the reference (src/mlx_dspark/config.py:67-133)
 for the qwen3 family; ``DFlashConfig`` mirrors src/mlx_dspark/dflash_model.py:52-71.
-``from_json`` applies the same format refusals as the reference (config.py:135-206).
+``from_json`` applies the same format refusals as the reference (config.py:87-185).
 """
 from __future__ import annotations
 
@@ -102,7 +102,7 @@ class DSparkConfig:
     @classmethod
     def from_json(cls, path: str | Path) -> "DSparkConfig":
         """Parse a DeepSpec-format drafter config.json with the reference's refusals
-        (src/mlx_dspark/config.py:135-206). Only the qwen3 family is built here."""
+        (src/mlx_dspark/config.py:87-185). Only the qwen3 family is built here."""
         with open(path) as f:
             c = json.load(f)
         mt = c.get("model_type", "")

@@ -51,13 +51,16 @@ __global__ void __launch_bounds__(kThreads) accept_greedy_kernel(
   __shared__ int is_last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int kWarps = kThreads / 32;
+  // 16-byte loads only where every row start is 16-byte aligned (a row-major view of any
+  // offset or stride still takes the scalar path)
+  const bool vec = ((ld & 7) == 0) && ((reinterpret_cast<uintptr_t>(logits) & 15) == 0);
   // one warp per row (rows strided over the warps), no block barrier in the scan: every
   // lane's loads of a row are independent, so a row costs about one memory round trip
   for (int r = warp; r < rows; r += kWarps) {
     const __nv_bfloat16* row = logits + (size_t)r * ld;
     Best b{-INFINITY, 0x7fffffff};
     for (int v = v0 + lane * 8; v < v1; v += 32 * 8) {
-      if (v + 8 <= v1 && ((ld & 7) == 0)) {
+      if (v + 8 <= v1 && vec) {
         const uint4 u = __ldg(reinterpret_cast<const uint4*>(row + v));
         const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
 #pragma unroll

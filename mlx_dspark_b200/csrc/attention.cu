@@ -18,7 +18,7 @@
 // Semantics follow mx.fast.scaled_dot_product_attention as called from the reference:
 // fp32 scores q.k * scale, fp32 softmax, output rounded to bf16; masks as in
 // create_attention_mask / build_batch_mask (src/mlx_dspark/batch_engine.py:170-178) for the
-// causal verify, and no mask for the drafter block (src/mlx_dspark/model.py:258-283,
+// causal verify, and no mask for the drafter block (src/mlx_dspark/model.py:130-156,
 // src/mlx_dspark/dflash_model.py:127-133).
 #include <algorithm>
 

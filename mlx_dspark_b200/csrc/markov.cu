@@ -1,8 +1,8 @@
 // K10 — DSpark Markov head with greedy block sampling.
 //
-// Reference: DSparkDrafter.sample_block (src/mlx_dspark/model.py:398-409), batched form
+// Reference: DSparkDrafter.sample_block (src/mlx_dspark/model.py:270-281), batched form
 // _batched_sample_block (src/mlx_dspark/batch_engine.py:414-428), VanillaMarkov
-// (model.py:324-336):
+// (model.py:196-208):
 //   for i in range(cap): logits_i = base_i + w2(w1[prev]); prev = argmax(logits_i)
 // One launch per position i. Each thread owns vocabulary rows: it issues the row's 256 W8
 // bytes as 16 independent 16-byte loads before any arithmetic (memory-level parallelism; the

@@ -74,6 +74,55 @@ def eos_token_ids(tokenizer) -> set[int]:
     return ids
 
 
+class StopStreaming(Exception):
+    """The name the reference's streaming callbacks raise to end a generation early
+    (generate.py:231-235). Streaming callbacks (on_text) are refused here, so no loop raises
+    or catches it; it exists so reference callers that import it keep working."""
+
+
+def _flat_ids(r) -> list[int] | None:
+    """A flat id list out of what a chat template returns: ids, a batch of one, or an
+    encoding with input_ids / ids."""
+    if hasattr(r, "input_ids"):
+        r = r.input_ids
+    elif isinstance(r, dict) and "input_ids" in r:
+        r = r["input_ids"]
+    elif hasattr(r, "ids"):
+        r = r.ids
+    if hasattr(r, "tolist"):
+        r = r.tolist()
+    if isinstance(r, (list, tuple)):
+        if r and isinstance(r[0], (list, tuple)):
+            r = r[0]
+        return [int(x) for x in r]
+    return None
+
+
+def encode_messages(tokenizer, messages: list[dict], add_generation_prompt: bool = True,
+                    **template_kwargs) -> list[int]:
+    """Ids of a chat transcript through the tokenizer's chat template (generate.py:71-96);
+    template keyword arguments a tokenizer rejects are dropped and the call retried; without a
+    template, the message contents joined by newlines."""
+    if getattr(tokenizer, "chat_template", None):
+        try:
+            r = tokenizer.apply_chat_template(messages, add_generation_prompt=add_generation_prompt,
+                                              **template_kwargs)
+        except (TypeError, ValueError):
+            r = tokenizer.apply_chat_template(messages, add_generation_prompt=add_generation_prompt)
+        ids = _flat_ids(r)
+        if ids is not None:
+            return ids
+    return list(tokenizer.encode("\n".join(str(m.get("content", "")) for m in messages)))
+
+
+def encode_prompt(tokenizer, prompt: str, use_chat: bool = True) -> list[int]:
+    """Ids of one user prompt, through the chat template when the tokenizer has one and
+    use_chat is set (generate.py:99-108)."""
+    if use_chat and getattr(tokenizer, "chat_template", None):
+        return encode_messages(tokenizer, [{"role": "user", "content": prompt}])
+    return list(tokenizer.encode(prompt))
+
+
 def capture_graph(fn) -> torch.cuda.CUDAGraph:
     """Record fn()'s launches into a CUDA graph on a side stream. capture_begin/capture_end
     directly: the torch.cuda.graph context also empties the caching allocator on entry, which
@@ -161,6 +210,8 @@ class SpecSession:
                  override: dict | None = None, sampling: Sampling | None = None,
                  seeds=None, penalties: tuple[float, float] = (0.0, 0.0), states=None,
                  max_cap: int | None = None):
+        if getattr(drafter, "target", None) is not target:
+            drafter.bind(target)   # a drafter from load_drafter / load_dflash comes unbound
         self.target, self.drafter = target, drafter
         self.B, self.cap = B, cap
         self.max_cap = max(cap, int(max_cap or cap))
@@ -271,6 +322,7 @@ class SpecSession:
         d.update_context_dev(self.vbuf.fused16, B, T, self.cstate, self.dbuf)
         ops.commit_lengths(self.plan, B, self.tstate.seq_len, self.cstate.seq_len)
         self.plan_host.copy_(self.plan, non_blocking=True)
+        t.scratch.read_status_async()
 
     def _versions(self):
         return (self.tstate.pool.version, self.cstate.pool.version,
@@ -314,6 +366,7 @@ class SpecSession:
             self.launch_round()
         self.done.record()
         self.done.synchronize()
+        self.target.scratch.raise_on_status()
         return self.plan_host.tolist()
 
 
@@ -434,7 +487,7 @@ def speculative_generate(target, tokenizer, drafter, prompt: str = "", *,
                          prompt_ids: list[int] | None = None, cache=None, ctx_caches=None,
                          reuse_len: int = 0, max_new_tokens: int = 128,
                          confidence_threshold: float = 0.0, max_draft_tokens: int | None = 2,
-                         cap_controller=None, lookup_drafts: bool = False,
+                         cap_controller=None, lookup_drafts: bool = True,
                          lookup_max_draft: int = 6, temperature: float = 0.0, top_p: float = 1.0,
                          top_k: int = 0, presence_penalty: float = 0.0,
                          frequency_penalty: float = 0.0, logprobs: int | None = None,
@@ -450,7 +503,7 @@ def speculative_generate(target, tokenizer, drafter, prompt: str = "", *,
     k = drafter.config.block_size
     cap = k if max_draft_tokens is None else max(1, min(int(max_draft_tokens), k))
     if prompt_ids is None:
-        prompt_ids = list(tokenizer.encode(prompt))
+        prompt_ids = encode_prompt(tokenizer, prompt, apply_chat_template)
     return _spec_loop(target, tokenizer, drafter, list(prompt_ids), cap, max_new_tokens,
                       Sampling(temperature, top_p, top_k), seed, use_graph, draft_override,
                       verbose, (presence_penalty, frequency_penalty),
@@ -471,7 +524,7 @@ def dflash_generate(target_model, tokenizer, drafter, prompt: str = "", *,
     kdraft = drafter.config.block_size - 1
     cap = kdraft if max_draft_tokens is None else max(1, min(int(max_draft_tokens), kdraft))
     if prompt_ids is None:
-        prompt_ids = list(tokenizer.encode(prompt))
+        prompt_ids = encode_prompt(tokenizer, prompt, apply_chat_template)
     return _spec_loop(target_model, tokenizer, drafter, list(prompt_ids), cap, max_new_tokens,
                       Sampling(temperature, top_p, top_k), seed, use_graph, None, verbose,
                       cap_controller=cap_controller)
@@ -526,6 +579,7 @@ class GreedySession:
         if self.counts is not None:
             ops.penalty_counts_add(self.counts, self.plan, self.B)
         self.plan_host.copy_(self.plan, non_blocking=True)
+        t.scratch.read_status_async()
 
     def capture(self):
         if not self.target.capturable:
@@ -539,6 +593,7 @@ class GreedySession:
             self.launch_step()
         self.done.record()
         self.done.synchronize()
+        self.target.scratch.raise_on_status()
         return self.plan_host.tolist()
 
 
@@ -555,7 +610,7 @@ def greedy_generate(target, tokenizer, prompt: str = "", *, prompt_ids: list[int
         raise NotImplementedError("logprobs are not built")
     eos_ids = eos_token_ids(tokenizer)
     if prompt_ids is None:
-        prompt_ids = list(tokenizer.encode(prompt))
+        prompt_ids = encode_prompt(tokenizer, prompt, apply_chat_template)
     ids = list(prompt_ids)
     sampling = Sampling(temperature, top_p, top_k)
     sess = GreedySession(target, 1, len(ids) + max_new_tokens + 1, sampling,
@@ -588,4 +643,5 @@ def greedy_generate(target, tokenizer, prompt: str = "", *, prompt_ids: list[int
 
 
 __all__ = ["GenResult", "SpecSession", "GreedySession", "speculative_generate",
-           "dflash_generate", "greedy_generate", "prefill_rows", "eos_token_ids", "RowView"]
+           "dflash_generate", "greedy_generate", "prefill_rows", "eos_token_ids", "RowView",
+           "StopStreaming", "encode_messages", "encode_prompt"]

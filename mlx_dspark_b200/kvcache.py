@@ -264,7 +264,7 @@ class TargetCache(list):
 
 class _CtxLayer:
     """One layer's view of a drafter context cache (reference CtxCache duck type,
-    src/mlx_dspark/model.py:176-208): every layer shares the cache's single length."""
+    src/mlx_dspark/model.py:48-80): every layer shares the cache's single length."""
 
     def __init__(self, parent: "CtxCaches"):
         self._parent = parent

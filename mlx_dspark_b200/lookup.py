@@ -7,7 +7,7 @@ lookup draft runs on the device like a drafter round: exact argmax match when gr
 temperature > 0 the one-hot proposal of the rejection sampler (dspark_accept_sample with
 q_onehot), so the output stays an exact sample of the target.
 
-lookup_generate is the pure prompt-lookup loop (lookup.py:92-205): a plain 1-token step when
+lookup_generate is the pure prompt-lookup loop (lookup.py:92-202): a plain 1-token step when
 nothing matches, a wider verify of [pending] + draft when something does.
 """
 from __future__ import annotations
@@ -114,8 +114,10 @@ class BlockVerifier:
 
     def finish(self, plan, plan_host) -> list[int]:
         plan_host.copy_(plan, non_blocking=True)
+        self.target.scratch.read_status_async()
         self.done.record()
         self.done.synchronize()
+        self.target.scratch.raise_on_status()
         return plan_host[0].tolist()
 
     def run(self, pending: int, draft: list[int]) -> list[int]:
@@ -129,7 +131,7 @@ def lookup_generate(target_model, tokenizer, prompt: str = "", *,
                     ngram_max: int = 4, temperature: float = 0.0, top_p: float = 1.0,
                     top_k: int = 0, seed: int | None = None, apply_chat_template: bool = True,
                     stop: list[str] | None = None, on_text=None) -> GenResult:
-    """Prompt-lookup speculative decoding, batch 1, no drafter model (lookup.py:92-205)."""
+    """Prompt-lookup speculative decoding, batch 1, no drafter model (lookup.py:92-202)."""
     eos_ids = eos_token_ids(tokenizer)
     if prompt_ids is None:
         prompt_ids = list(tokenizer.encode(prompt))

@@ -4,14 +4,14 @@ DFlash (block diffusion), both conditioned on target hidden states.
 Both follow the same device path (BlockDrafter):
   context : fused target hidden [rows, n_tap*H] -> fc -> hidden_norm -> per layer
             k_norm/RoPE K and V written into the drafter's paged context cache
-            (DSpark update_context, src/mlx_dspark/model.py:381-384 and :254-256;
+            (DSpark update_context, src/mlx_dspark/model.py:253-256 and :126-128;
             DFlash KV injection, src/mlx_dspark/dflash_model.py:100-124)
   block   : [pending, mask x (k-1)] -> embed -> layers (q from the block, K/V = [ctx; block],
-            no mask) -> final norm (model.py:258-283,386-390; dflash_model.py:125-134,197-205)
+            no mask) -> final norm (model.py:130-156,258-262; dflash_model.py:125-134,197-205)
 The block K/V are written after the committed context for the duration of one draft; the
 context update of the accepted rows overwrites them.
 
-DSparkDrafter — drop-in for DSparkDrafter (model.py:348-437): own or shared embedding / head,
+DSparkDrafter — drop-in for DSparkDrafter (model.py:220-320): own or shared embedding / head,
 head over the first cap rows, then the sequential Markov head (greedy, or temperature drafts
 with the q distributions kept for the acceptance test).
 DFlashDrafter — drop-in for DFlashDraftModel (dflash_model.py:167-208) bound to a target: the
@@ -81,14 +81,18 @@ class BlockDrafter:
 
     logits_start = 0
 
-    def __init__(self, cfg, fc, hidden_norm, norm, layer_weights, target: Target, embed_w, head_w,
-                 device):
+    def __init__(self, cfg, fc, hidden_norm, norm, layer_weights, device, own_embed=None,
+                 own_head=None):
         self.config = cfg
         self.block_size = cfg.block_size
         self.mask_token_id = cfg.mask_token_id
         self.device = torch.device(device)
-        self.target = target
-        self.embed_w, self.head_w = embed_w, head_w
+        # the drafter's own embedding / head when its checkpoint carries them; otherwise it
+        # shares the target's, which bind() attaches
+        self._own_embed, self._own_head = own_embed, own_head
+        self.target = None
+        self.scratch = None
+        self.embed_w, self.head_w = own_embed, own_head
         self.fc = pack(fc, device=device)
         self.hidden_norm = hidden_norm.to(device)
         self.norm = norm.to(device)
@@ -98,9 +102,31 @@ class BlockDrafter:
             pl.kv = pack(lw.wk, lw.wv, device=device)
             self.layers.append(pl)
         self.inv_freq = rope_inv_freq(cfg.head_dim, cfg.rope_theta, device)
-        self.scratch = target.scratch
         self._bufs = {}
         self.rng = ops.rng_state(0, self.device)
+
+    def bind(self, target: Target):
+        """Attach the drafter to the target whose hidden states condition its drafts: the
+        target's workspaces, and its embedding and head where the drafter has none of its own
+        (DFlashDraftModel.bind, dflash_model.py:168-184; a DSpark drafter with shared
+        embeddings the same way). Returns self; binding again to another target re-attaches."""
+        if self.target is target:
+            return self
+        if getattr(target, "cfg", None) is not None and \
+                target.cfg.hidden_size != self.config.hidden_size:
+            raise ValueError(f"drafter hidden_size {self.config.hidden_size} does not match the "
+                             f"target's {target.cfg.hidden_size}")
+        self.target = target
+        self.scratch = target.scratch
+        self.embed_w = target.embed if self._own_embed is None else self._own_embed
+        self.head_w = target.draft_head if self._own_head is None else self._own_head
+        self._bufs = {}
+        return self
+
+    def _need_target(self) -> None:
+        if self.target is None:
+            raise RuntimeError("the drafter is not bound to a target: call drafter.bind(target) "
+                               "(the generate loops do this)")
 
     def seed(self, seed: int) -> None:
         """Seed the device Philox stream used by host-API draws (mx.random.seed)."""
@@ -119,6 +145,7 @@ class BlockDrafter:
                          len(self.layers))
 
     def buffers(self, B: int, k: int, ctx_rows: int) -> DraftBuffers:
+        self._need_target()
         key = (B, k, ctx_rows)
         b = self._bufs.get(key)
         if b is None:
@@ -217,7 +244,8 @@ class BlockDrafter:
 
     # ------------------------------------------------------------------ reference API
     def update_context(self, target_hidden_cat, ctx_offset, ctx_caches) -> None:
-        """fused [1, n, n_tap*H] at context positions ctx_offset.. (model.py:381-384)."""
+        """fused [1, n, n_tap*H] at context positions ctx_offset.. (model.py:253-256)."""
+        self._need_target()
         ctx_caches = getattr(ctx_caches, "state", ctx_caches)
         fused = target_hidden_cat.reshape(-1, target_hidden_cat.shape[-1])
         n = fused.shape[0]
@@ -238,7 +266,8 @@ class BlockDrafter:
         ctx_caches.set_len(0, ctx_offset + n)
 
     def embed(self, ids):
-        """ids [1, L] -> [1, L, H] bf16 (model.py:372-373)."""
+        """ids [1, L] -> [1, L, H] bf16 (model.py:244-245)."""
+        self._need_target()
         ids = torch.as_tensor(ids, dtype=torch.int32).reshape(-1).to(self.device)
         out = torch.empty(ids.numel(), self.config.hidden_size, dtype=torch.bfloat16,
                           device=self.device)
@@ -247,23 +276,24 @@ class BlockDrafter:
 
 
 class DSparkDrafter(BlockDrafter):
-    def __init__(self, weights: DSparkWeights, target: Target, device="cuda"):
+    def __init__(self, weights: DSparkWeights, target: Target | None = None, device="cuda"):
         cfg = weights.cfg
         self.softcap = cfg.final_logit_softcapping
         if self.softcap is not None:
             raise NotImplementedError("logit softcapping (gemma4 drafters) is not built")
         if cfg.norm_style != "qwen":
             raise NotImplementedError("only the qwen3 drafter family is built")
-        embed_w = target.embed if weights.embed is None else pack(weights.embed, device=device)
-        head_w = target.draft_head if weights.lm_head is None else pack(weights.lm_head,
-                                                                         device=device)
+        own_embed = None if weights.embed is None else pack(weights.embed, device=device)
+        own_head = None if weights.lm_head is None else pack(weights.lm_head, device=device)
         super().__init__(cfg, weights.fc, weights.hidden_norm, weights.norm, weights.layers,
-                         target, embed_w, head_w, device)
+                         device, own_embed, own_head)
         self.markov_head = None
         if weights.markov_w1 is not None:
             self.markov_head = _Markov(pack(weights.markov_w1, device=device),
                                        pack(weights.markov_w2, device=device), cfg.markov_rank)
         self.confidence_head = None
+        if target is not None:
+            self.bind(target)
 
     def draft_dev(self, pending: torch.Tensor, B: int, cap: int, ctx: CacheState,
                   buf: DraftBuffers, draft: torch.Tensor, verify_ids: torch.Tensor | None,
@@ -306,6 +336,7 @@ class DSparkDrafter(BlockDrafter):
     # ------------------------------------------------------------------ reference API
     def sample_block(self, base_logits, first_prev_token: int):
         """base [cap, V] -> [cap] greedy tokens with the Markov head (model.py:270-281)."""
+        self._need_target()
         base = base_logits.reshape(-1, base_logits.shape[-1]).to(torch.bfloat16).contiguous()
         cap = base.shape[0]
         if self.markov_head is None:
@@ -321,6 +352,7 @@ class DSparkDrafter(BlockDrafter):
         """Temperature draft (model.py:283-309): (tokens [cap], probs [cap, V]). Draws come from
         this drafter's Philox stream (seed()); the stream does not advance (the acceptance
         step advances it in a decode loop)."""
+        self._need_target()
         base = base_logits.reshape(-1, base_logits.shape[-1]).to(torch.bfloat16).contiguous()
         cap, V = base.shape
         draft = torch.empty(cap, dtype=torch.int32, device=self.device)
@@ -351,20 +383,18 @@ class DFlashDrafter(BlockDrafter):
 
     logits_start = 1
 
-    def __init__(self, weights: DFlashWeights, target: Target, device="cuda"):
+    def __init__(self, weights: DFlashWeights, target: Target | None = None, device="cuda"):
         cfg: DFlashConfig = weights.cfg
         if any(t != "full_attention" for t in cfg.layer_types):
             raise NotImplementedError("sliding-window DFlash layers are not built")
         if cfg.final_logit_softcapping is not None:
             raise NotImplementedError("logit softcapping is not built")
         super().__init__(cfg, weights.fc, weights.hidden_norm, weights.norm, weights.layers,
-                         target, target.embed, target.draft_head, device)
+                         device)
         self.markov_head = None
         self.confidence_head = None
-
-    def bind(self, target_model=None):
-        """The embedding and head are the target's from construction (dflash_model.py:171-186)."""
-        return self
+        if target is not None:
+            self.bind(target)
 
     def make_cache(self, max_tokens: int = 4096) -> CtxCaches:
         return self.make_ctx_cache(max_tokens)

@@ -40,6 +40,7 @@ class Scratch:
         self.bufs: dict[str, torch.Tensor] = {}
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.version = 0  # bumped when a buffer moves (captured graphs hold the addresses)
+        self._status_host = None
 
     def get(self, family: str, nbytes: int) -> torch.Tensor:
         b = self.bufs.get(family)
@@ -51,6 +52,23 @@ class Scratch:
 
     def reserve(self, family: str, nbytes: int) -> None:
         self.get(family, nbytes)
+
+    def read_status_async(self) -> None:
+        """Enqueue a copy of the status word into pinned host memory on the current stream
+        (inside a captured round it becomes part of the graph). The decode loops call it
+        next to their per-round plan read and raise_on_status() after that round's sync, so a
+        bounded device wait that ran out fails the round instead of letting it commit tokens
+        computed from stale data."""
+        if self._status_host is None:
+            self._status_host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+        self._status_host.copy_(self.status, non_blocking=True)
+
+    def raise_on_status(self) -> None:
+        """After the stream synchronised past read_status_async(): raise DsparkError (and
+        reset the workspaces, as check_status does) if a kernel reported an error."""
+        if self._status_host is not None and int(self._status_host[0]) != 0:
+            self._status_host.zero_()
+            self.check_status()
 
     def check_status(self) -> None:
         s = int(self.status.item())

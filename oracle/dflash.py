@@ -7,7 +7,7 @@ cache offset and v_proj(.) are appended to the layer's cache (update_and_fetch);
 queries and keys are roped at offset + S; SDPA with no mask over [ctx; block]; final norm; the
 target's head on rows logits_start.. . The decoder layer (input norm, attention, residual,
 post norm, SwiGLU MLP, residual) is the qwen 2-norm layer DSparkRef already restates, so the
-same code serves (dflash_model.py:137-147 vs model.py:313-321).
+same code serves (dflash_model.py:137-147 vs model.py:185-194).
 
 dflash_generate_ref follows src/mlx_dspark/generate.py:468-601: greedy (argmax drafts, exact
 argmax-match verify) or sampled (q = truncate(softmax(head / T)), drafts drawn from q,

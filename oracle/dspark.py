@@ -1,6 +1,6 @@
 """Oracle DSpark drafter, greedy acceptance and decode loops (CPU). TEST INFRASTRUCTURE ONLY.
 
-Drafter: src/mlx_dspark/model.py:176-437 (CtxCache append, DSparkAttention._kv /
+Drafter: src/mlx_dspark/model.py:48-320 (CtxCache append, DSparkAttention._kv /
 update_ctx / attend, qwen 2-norm layer, VanillaMarkov, sample_block).
 Greedy loops: speculative_generate's fused greedy path src/mlx_dspark/generate.py:806-961
 (with lookup drafts off and no confidence head) and greedy_generate :373-465.
@@ -13,7 +13,7 @@ from .qwen3 import F32, Qwen3Ref, bf, inv_freq, prefill, rms_norm, rope, sdpa, s
 
 
 class CtxCacheRef:
-    """model.py:176-208 — per-layer context K/V, append-only (trim_to for prefix reuse)."""
+    """model.py:48-80 — per-layer context K/V, append-only (trim_to for prefix reuse)."""
 
     def __init__(self):
         self.k = None
@@ -61,7 +61,7 @@ class DSparkRef:
                   + e.biases.to(F32).repeat_interleave(64, 1)[ids], self.rnd)
 
     def _kv(self, L, x):
-        """DSparkAttention._kv (model.py:241-252): K = k_norm(k_proj(x)), V = v_proj(x)."""
+        """DSparkAttention._kv (model.py:113-124): K = k_norm(k_proj(x)), V = v_proj(x)."""
         c = self.cfg
         T = x.shape[0]
         k = self._lin(x, L.wk).reshape(T, c.num_key_value_heads, c.head_dim).transpose(0, 1)
@@ -70,7 +70,7 @@ class DSparkRef:
         return k, v
 
     def update_context(self, fused, ctx_offset, ctx_caches):
-        """model.py:381-384 + update_ctx :254-256 (V is not roped)."""
+        """model.py:253-256 + update_ctx :126-128 (V is not roped)."""
         f = rms_norm(self._lin(fused, self.w.fc), self.w.hidden_norm, self.cfg.rms_norm_eps, self.rnd)
         pos = torch.arange(ctx_offset, ctx_offset + f.shape[0])
         for L, cache in zip(self.w.layers, ctx_caches):
@@ -78,7 +78,7 @@ class DSparkRef:
             cache.append(rope(k, pos, self.freqs, self.rnd), v)
 
     def attend(self, L, h, block_offset, cache):
-        """model.py:258-283: Q from the block, K/V = [ctx; block], no mask."""
+        """model.py:130-156: Q from the block, K/V = [ctx; block], no mask."""
         c = self.cfg
         T = h.shape[0]
         q = self._lin(h, L.wq).reshape(T, c.num_attention_heads, c.head_dim).transpose(0, 1)
@@ -92,7 +92,7 @@ class DSparkRef:
         return self._lin(a.transpose(0, 1).reshape(T, -1), L.wo)
 
     def backbone(self, noise, block_offset, ctx_caches):
-        """model.py:386-390 with the qwen 2-norm layer :313-321."""
+        """model.py:258-262 with the qwen 2-norm layer :185-194."""
         c = self.cfg
         h = noise
         for L, cache in zip(self.w.layers, ctx_caches):
@@ -107,14 +107,14 @@ class DSparkRef:
         return self._lin(hidden, self.head_t)
 
     def step_bias(self, prev: int):
-        """VanillaMarkov.step_bias (model.py:335-336): w2(w1[prev])."""
+        """VanillaMarkov.step_bias (model.py:207-208): w2(w1[prev])."""
         w1, w2 = self.w.markov_w1, self.w.markov_w2
         e = bf(w1.scales[prev].to(F32).repeat_interleave(64) * w1.q[prev].to(F32)
                + w1.biases[prev].to(F32).repeat_interleave(64), self.rnd)
         return self._lin(e[None], w2)[0]
 
     def sample_block(self, base_logits, first_prev_token: int):
-        """model.py:398-409 (argmax = first index of the maximum)."""
+        """model.py:270-281 (argmax = first index of the maximum)."""
         if self.w.markov_w1 is None:
             return [int(i) for i in base_logits.argmax(-1)]
         toks, prev = [], int(first_prev_token)

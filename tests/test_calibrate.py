@@ -3,7 +3,9 @@ knee detection, interpolation, the acceptance EWMA, the rate-maximising cap with
 the per-batch-width cap and the disk cache."""
 import pytest
 
-from mlx_dspark_b200 import calibrate as cal
+import importlib
+
+cal = importlib.import_module("mlx_dspark_b200.calibrate")
 
 
 def test_knee_width():

@@ -77,3 +77,58 @@ def test_gemm_opts_struct_matches_the_c_layout():
     import ctypes
     from mlx_dspark_b200 import _lib
     assert ctypes.sizeof(_lib.GemmOpts) == _lib.lib().dspark_gemm_opts_size()
+
+
+# The public names of the reference package (src/mlx_dspark/__init__.py:89-116): each one is
+# exported here or listed, with the reason, in mlx_dspark_b200.NOT_PROVIDED.
+REFERENCE_ALL = [
+    "DSparkConfig", "DFlashConfig", "DFlashDraftModel", "Target", "load_drafter", "load_dflash",
+    "load_target", "load_pair", "load_dflash_pair", "speculative_generate", "dflash_generate",
+    "lookup_generate", "greedy_generate", "calibrate", "CapController", "NGramIndex",
+    "StopStreaming", "encode_messages", "encode_prompt", "GenResult", "Engine", "run_server",
+    "PRESETS", "DFLASH_PRESETS", "REGISTRY", "resolve", "resolve_mode", "apply_wired_limit",
+    "DEFAULT_TARGET", "DEFAULT_DRAFTER",
+]
+
+
+def test_reference_public_names_exported_or_excused():
+    import mlx_dspark_b200 as pkg
+    missing = [n for n in REFERENCE_ALL
+               if n not in pkg.NOT_PROVIDED and not (n in pkg.__all__ and hasattr(pkg, n))]
+    assert not missing, missing
+    for n, why in pkg.NOT_PROVIDED.items():
+        assert n in REFERENCE_ALL and why
+
+
+def test_loader_signatures_follow_the_reference():
+    import inspect
+
+    from mlx_dspark_b200 import load
+    sig = inspect.signature(load.load_drafter)
+    first = list(sig.parameters)[0]
+    assert first == "repo_or_path"
+    for kw, default in (("quantize", True), ("bits", 4), ("group_size", 64), ("strict", True)):
+        p = sig.parameters[kw]
+        assert p.kind is p.KEYWORD_ONLY and p.default == default, kw
+    assert list(inspect.signature(load.load_dflash).parameters)[0] == "repo_or_path"
+    for fn in (load.load_pair, load.load_dflash_pair):
+        assert "drafter" in inspect.signature(fn).parameters
+    from mlx_dspark_b200.generate import speculative_generate
+    assert inspect.signature(speculative_generate).parameters["lookup_drafts"].default is True
+    with pytest.raises(ValueError):
+        load.load_drafter("tiny", group_size=32, device="cpu")
+
+
+def test_resolve_rules():
+    from mlx_dspark_b200 import load
+    assert load.resolve("mlx-community/Qwen3-8B-4bit") == (
+        "mlx-community/Qwen3-8B-4bit", "deepseek-ai/dspark_qwen3_8b_block7")
+    assert load.resolve("some/unknown-model", mode="lookup") == ("some/unknown-model", None)
+    assert load.resolve("qwen3", mode="dflash")[1] == "z-lab/Qwen3-4B-DFlash-b16"
+    assert load.resolve("x/y", drafter="my/drafter") == ("x/y", "my/drafter")
+    with pytest.raises(ValueError):
+        load.resolve("some/unknown-model")
+    assert load.resolve_mode("mlx-community/Qwen3-4B-8bit")[0] == "dspark"
+    assert load.resolve_mode("some/unknown-model") == ("lookup", "some/unknown-model", None)
+    with pytest.raises(ValueError):
+        load.load_target("not/a-cached-repo", device="cpu")

@@ -10,7 +10,7 @@ import torch
 from mlx_dspark_b200.batch_engine import (SpecSlots, batch_generate_baseline, batch_spec_generate,
                                           serve_requests)
 from mlx_dspark_b200.config import TINY, dspark_for
-from mlx_dspark_b200.load import load_drafter, load_target
+from mlx_dspark_b200.load import drafter_for, load_target
 from mlx_dspark_b200.weights import generate_dspark, generate_target
 from oracle.qwen3 import Qwen3Ref
 
@@ -46,7 +46,7 @@ def tiny(cuda):
     out = {"tw": tw, "ref": Qwen3Ref(tw)}
     for kv in (None, 8):
         t, _ = load_target(TINY, weights=tw, kv_bits=kv, device=cuda)
-        d, _ = load_drafter(t, dcfg, weights=dw, device=cuda)
+        d, _ = drafter_for(t, dcfg, weights=dw, device=cuda)
         out[kv] = (t, d)
     g = torch.Generator().manual_seed(5)
     shared = torch.randint(0, TINY.vocab_size, (130,), generator=g).tolist()

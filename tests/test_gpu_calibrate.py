@@ -6,11 +6,13 @@ import json
 import pytest
 import torch
 
-from mlx_dspark_b200 import calibrate as cal
+import importlib
+
+cal = importlib.import_module("mlx_dspark_b200.calibrate")
 from mlx_dspark_b200.batch_engine import SpecSlots
 from mlx_dspark_b200.config import TINY, dspark_for
 from mlx_dspark_b200.generate import speculative_generate
-from mlx_dspark_b200.load import load_drafter, load_target
+from mlx_dspark_b200.load import drafter_for, load_target
 from mlx_dspark_b200.weights import generate_dspark, generate_target
 from oracle.qwen3 import Qwen3Ref
 
@@ -22,7 +24,7 @@ def pair(cuda):
     tw = generate_target(TINY, 5, "cpu")
     dcfg = dspark_for(TINY)
     target, _ = load_target(TINY, weights=tw, device=cuda)
-    drafter, _ = load_drafter(target, dcfg, weights=generate_dspark(dcfg, 5, "cpu"), device=cuda)
+    drafter, _ = drafter_for(target, dcfg, weights=generate_dspark(dcfg, 5, "cpu"), device=cuda)
     g = torch.Generator().manual_seed(5)
     prompt = torch.randint(0, TINY.vocab_size, (90,), generator=g).tolist()
     return target, drafter, prompt, Qwen3Ref(tw)
@@ -92,7 +94,7 @@ def test_spec_decode_lossless_under_changing_caps(pair):
     for use_graph in (True, False):
         ctl.used.clear()
         ctl.cap = 1
-        res = speculative_generate(target, None, drafter, prompt_ids=prompt, max_new_tokens=64,
+        res = speculative_generate(target, None, drafter, lookup_drafts=False, prompt_ids=prompt, max_new_tokens=64,
                                    max_draft_tokens=None, cap_controller=ctl, use_graph=use_graph)
         assert res.num_tokens >= 64 and _greedy_ok(ref_t, prompt, res.token_ids[:64]) <= 3
         assert len(set(ctl.used)) == min(drafter.block_size, len(ctl.used)) > 1
@@ -102,7 +104,7 @@ def test_spec_decode_lossless_under_changing_caps(pair):
     # the real controller drives the same loop
     live = cal.CapController({w: 1.0 for w in range(2, 10)}, 0.1, drafter.block_size,
                              init_cap=2, repick_every=2)
-    res = speculative_generate(target, None, drafter, prompt_ids=prompt, max_new_tokens=64,
+    res = speculative_generate(target, None, drafter, lookup_drafts=False, prompt_ids=prompt, max_new_tokens=64,
                                max_draft_tokens=None, cap_controller=live)
     assert _greedy_ok(ref_t, prompt, res.token_ids[:64]) <= 3
     assert live.rounds == res.num_rounds

@@ -1,6 +1,6 @@
 """End-to-end GPU parity on the tiny config (BASELINE C1 shapes) against the CPU oracle.
 
-Tolerances (written here, explained in DESIGN.md):
+Tolerances:
   * logits: |gpu - oracle| <= 2e-2 * max|oracle row| (bf16 rtol 2e-2 of the row scale);
   * greedy tokens, teacher-forced: every emitted token is the oracle's argmax at its
     position, unless the oracle's margin top1 - logit[token] is within GAP_TOL. The logits
@@ -12,7 +12,7 @@ import torch
 
 from mlx_dspark_b200.config import TINY, dspark_for
 from mlx_dspark_b200.generate import greedy_generate, speculative_generate
-from mlx_dspark_b200.load import load_drafter, load_target
+from mlx_dspark_b200.load import drafter_for, load_target
 from mlx_dspark_b200.weights import generate_dspark, generate_target
 from oracle.dspark import DSparkRef
 from oracle.qwen3 import Qwen3Ref, prefill
@@ -28,7 +28,7 @@ def tiny(cuda):
     dcfg = dspark_for(TINY)
     dw = generate_dspark(dcfg, SEED, "cpu")
     target, tok = load_target(TINY, weights=tw, device=cuda)
-    drafter, _ = load_drafter(target, dcfg, weights=dw, device=cuda)
+    drafter, _ = drafter_for(target, dcfg, weights=dw, device=cuda)
     ref_t = Qwen3Ref(tw)
     ref_d = DSparkRef(dw, tw)
     g = torch.Generator().manual_seed(SEED)
@@ -100,7 +100,7 @@ def test_greedy_decode_teacher_forced(tiny):
 
 
 def test_speculative_decode_is_target_greedy(tiny):
-    res = speculative_generate(tiny["target"], None, tiny["drafter"], prompt_ids=tiny["prompt"],
+    res = speculative_generate(tiny["target"], None, tiny["drafter"], lookup_drafts=False, prompt_ids=tiny["prompt"],
                                max_new_tokens=96, max_draft_tokens=None)
     assert res.num_tokens >= 96
     assert sum(res.accept_lengths) + 1 == res.num_tokens
@@ -108,7 +108,7 @@ def test_speculative_decode_is_target_greedy(tiny):
     excused, worst = teacher_forced_check(tiny["ref_t"], tiny["prompt"], res.token_ids)
     assert excused <= 3, (excused, worst)
     # the graph-replayed rounds and eager rounds agree exactly
-    res2 = speculative_generate(tiny["target"], None, tiny["drafter"], prompt_ids=tiny["prompt"],
+    res2 = speculative_generate(tiny["target"], None, tiny["drafter"], lookup_drafts=False, prompt_ids=tiny["prompt"],
                                 max_new_tokens=96, max_draft_tokens=None, use_graph=False)
     assert res2.token_ids == res.token_ids and res2.accept_lengths == res.accept_lengths
 
@@ -150,7 +150,7 @@ def test_override_accept_lengths_exact(tiny):
     rounds = N
     agree = (torch.rand(1, rounds, cap, generator=g) < 0.7).to(torch.uint8)
     ov = {"ref": torch.tensor([ref]), "agree": agree, "prompt_len": [len(prompt)]}
-    res = speculative_generate(target, None, drafter, prompt_ids=prompt, max_new_tokens=N,
+    res = speculative_generate(target, None, drafter, lookup_drafts=False, prompt_ids=prompt, max_new_tokens=N,
                                max_draft_tokens=cap, draft_override=ov)
     assert res.token_ids[:N] == ref[:N]
     for r, a in enumerate(res.accept_lengths):

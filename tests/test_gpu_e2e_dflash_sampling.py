@@ -17,7 +17,7 @@ import torch
 from mlx_dspark_b200.config import TINY, dflash_for, dspark_for
 from mlx_dspark_b200.generate import (GreedySession, SpecSession, dflash_generate,
                                       greedy_generate, prefill_rows, speculative_generate)
-from mlx_dspark_b200.load import load_dflash_drafter, load_drafter, load_target
+from mlx_dspark_b200.load import dflash_drafter_for, drafter_for, load_target
 from mlx_dspark_b200.model import Sampling
 from mlx_dspark_b200.weights import generate_dflash, generate_dspark, generate_target
 from oracle import sampling as S
@@ -37,10 +37,10 @@ def pair(cuda):
     target, _ = load_target(TINY, weights=tw, device=cuda)
     fcfg = dflash_for(TINY)
     fw = generate_dflash(fcfg, SEED, "cpu")
-    dflash, _ = load_dflash_drafter(target, fcfg, weights=fw, device=cuda)
+    dflash, _ = dflash_drafter_for(target, fcfg, weights=fw, device=cuda)
     dcfg = dspark_for(TINY)
     dw = generate_dspark(dcfg, SEED, "cpu")
-    dspark, _ = load_drafter(target, dcfg, weights=dw, device=cuda)
+    dspark, _ = drafter_for(target, dcfg, weights=dw, device=cuda)
     g = torch.Generator().manual_seed(SEED)
     prompt = torch.randint(0, TINY.vocab_size, (128,), generator=g).tolist()
     return dict(tw=tw, target=target, dflash=dflash, dspark=dspark, ref_t=Qwen3Ref(tw),
@@ -144,14 +144,14 @@ def test_sampled_rounds_replay_exactly(pair, kind):
 def test_sampled_generate_is_deterministic_and_graph_equal(pair):
     kw = dict(prompt_ids=pair["prompt"], max_new_tokens=48, temperature=0.8, top_p=0.9, top_k=40,
               seed=11)
-    a = speculative_generate(pair["target"], None, pair["dspark"], max_draft_tokens=None, **kw)
-    b = speculative_generate(pair["target"], None, pair["dspark"], max_draft_tokens=None,
+    a = speculative_generate(pair["target"], None, pair["dspark"], lookup_drafts=False, max_draft_tokens=None, **kw)
+    b = speculative_generate(pair["target"], None, pair["dspark"], lookup_drafts=False, max_draft_tokens=None,
                              use_graph=False, **kw)
     assert a.token_ids == b.token_ids and a.accept_lengths == b.accept_lengths
     c = dflash_generate(pair["target"], None, pair["dflash"], **kw)
     d = dflash_generate(pair["target"], None, pair["dflash"], use_graph=False, **kw)
     assert c.token_ids == d.token_ids
-    e = speculative_generate(pair["target"], None, pair["dspark"], max_draft_tokens=None,
+    e = speculative_generate(pair["target"], None, pair["dspark"], lookup_drafts=False, max_draft_tokens=None,
                              **{**kw, "seed": 12})
     assert e.token_ids != a.token_ids  # another seed, another sample
 
@@ -201,7 +201,7 @@ def _penalized_teacher_forced(ref_t, prompt, tokens, P, F):
 
 def test_penalized_greedy_decoding_matches_oracle(pair):
     P, F = 0.6, 0.4
-    spec = speculative_generate(pair["target"], None, pair["dspark"], prompt_ids=pair["prompt"],
+    spec = speculative_generate(pair["target"], None, pair["dspark"], lookup_drafts=False, prompt_ids=pair["prompt"],
                                 max_new_tokens=48, max_draft_tokens=None, presence_penalty=P,
                                 frequency_penalty=F)
     plain = greedy_generate(pair["target"], None, prompt_ids=pair["prompt"], max_new_tokens=48,

@@ -9,7 +9,7 @@ import torch
 
 from mlx_dspark_b200.config import TINY, dspark_for
 from mlx_dspark_b200.engine import BatchEngine, Engine, maybe_batch_engine
-from mlx_dspark_b200.load import load_drafter, load_target
+from mlx_dspark_b200.load import drafter_for, load_target
 from mlx_dspark_b200.weights import generate_dspark, generate_target
 from oracle.qwen3 import Qwen3Ref
 
@@ -21,7 +21,7 @@ def pair(cuda):
     tw = generate_target(TINY, 6, "cpu")
     dcfg = dspark_for(TINY)
     target, _ = load_target(TINY, weights=tw, device=cuda)
-    drafter, _ = load_drafter(target, dcfg, weights=generate_dspark(dcfg, 6, "cpu"), device=cuda)
+    drafter, _ = drafter_for(target, dcfg, weights=generate_dspark(dcfg, 6, "cpu"), device=cuda)
     return target, drafter, Qwen3Ref(tw)
 
 

@@ -9,7 +9,7 @@ import torch
 from mlx_dspark_b200.config import TINY, dspark_for
 from mlx_dspark_b200.generate import speculative_generate
 from mlx_dspark_b200.kvcache import CacheState
-from mlx_dspark_b200.load import load_drafter, load_target
+from mlx_dspark_b200.load import drafter_for, load_target
 from mlx_dspark_b200.lookup import BlockVerifier, lookup_generate
 from mlx_dspark_b200.model import Sampling
 from mlx_dspark_b200 import ops
@@ -28,7 +28,7 @@ def tiny(cuda):
     tw = generate_target(TINY, 0, "cpu")
     target, _ = load_target(TINY, weights=tw, device=cuda)
     dcfg = dspark_for(TINY)
-    drafter, _ = load_drafter(target, dcfg, weights=generate_dspark(dcfg, 0, "cpu"), device=cuda)
+    drafter, _ = drafter_for(target, dcfg, weights=generate_dspark(dcfg, 0, "cpu"), device=cuda)
     g = torch.Generator().manual_seed(0)
     prompt = torch.randint(0, TINY.vocab_size, (128,), generator=g).tolist()
     return dict(target=target, drafter=drafter, ref_t=Qwen3Ref(tw), prompt=prompt)
@@ -50,7 +50,7 @@ def test_hybrid_lookup_rounds_are_target_greedy(tiny):
     assert sum(res.accept_lengths) + 1 == res.num_tokens
     excused, worst = teacher_forced_check(tiny["ref_t"], tiny["prompt"], res.token_ids[:96])
     assert excused <= 3, (excused, worst)
-    plain = speculative_generate(tiny["target"], None, tiny["drafter"], prompt_ids=tiny["prompt"],
+    plain = speculative_generate(tiny["target"], None, tiny["drafter"], lookup_drafts=False, prompt_ids=tiny["prompt"],
                                  max_new_tokens=96, max_draft_tokens=None)
     n = min(len(res.token_ids), len(plain.token_ids), 96)
     assert res.token_ids[:n] == plain.token_ids[:n]

@@ -9,7 +9,7 @@ from mlx_dspark_b200._lib import (EPI_RESIDUAL_BF16, EPI_SILU_MUL_F16, EPI_STORE
                                   EPI_STORE_F32)
 from mlx_dspark_b200.config import TINY, dspark_for
 from mlx_dspark_b200.generate import SpecSession, prefill_rows
-from mlx_dspark_b200.load import load_drafter, load_target
+from mlx_dspark_b200.load import drafter_for, load_target
 from mlx_dspark_b200.weights import generate_dspark, generate_target, pack, quantize_w8g64
 from oracle import qwen3 as oq
 from oracle.qwen3 import Qwen3Ref
@@ -157,7 +157,7 @@ def tiny_pair(cuda):
     dcfg = dspark_for(TINY)
     dw = generate_dspark(dcfg, 3, "cpu")
     target, _ = load_target(TINY, weights=tw, device=cuda)
-    drafter, _ = load_drafter(target, dcfg, weights=dw, device=cuda)
+    drafter, _ = drafter_for(target, dcfg, weights=dw, device=cuda)
     return tw, target, drafter
 
 
@@ -237,7 +237,7 @@ def test_prefill_wide_kv8_matches_verify_forward(cuda, monkeypatch):
     tw = generate_target(TINY, 4, "cpu")
     target, _ = load_target(TINY, weights=tw, device=cuda, kv_bits=8)
     dcfg = dspark_for(TINY)
-    drafter, _ = load_drafter(target, dcfg, weights=generate_dspark(dcfg, 4, "cpu"), device=cuda)
+    drafter, _ = drafter_for(target, dcfg, weights=generate_dspark(dcfg, 4, "cpu"), device=cuda)
     prompt = torch.randint(0, TINY.vocab_size, (400,),
                            generator=torch.Generator().manual_seed(4)).tolist()
     lasts = {}

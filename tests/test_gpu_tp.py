@@ -42,7 +42,7 @@ def _rank_body(rank, world, port, q, log):
     import torch.distributed as dist
     from mlx_dspark_b200.config import TINY, dspark_for
     from mlx_dspark_b200.generate import greedy_generate, speculative_generate
-    from mlx_dspark_b200.load import load_drafter
+    from mlx_dspark_b200.load import drafter_for
     from mlx_dspark_b200.tp import TPTarget, init_process_group
     from mlx_dspark_b200.weights import generate_dspark, generate_target
     rank, world, dev = init_process_group("nccl", timeout_s=60)
@@ -52,7 +52,7 @@ def _rank_body(rank, world, port, q, log):
         tw = generate_target(TINY, 0, "cpu")
         target = TPTarget(tw, rank, world, device=dev)
         dcfg = dspark_for(TINY)
-        drafter, _ = load_drafter(target, dcfg, weights=generate_dspark(dcfg, 0, "cpu"), device=dev)
+        drafter, _ = drafter_for(target, dcfg, weights=generate_dspark(dcfg, 0, "cpu"), device=dev)
         g = torch.Generator().manual_seed(0)
         prompt = torch.randint(0, TINY.vocab_size, (96,), generator=g).tolist()
         print("loaded", flush=True)
@@ -72,7 +72,7 @@ def _rank_body(rank, world, port, q, log):
         local = logits[0, :, :target.vocab_valid].contiguous()
         parts = [torch.zeros_like(local) for _ in range(world)]
         dist.all_gather(parts, local)
-        spec = speculative_generate(target, None, drafter, prompt_ids=prompt, max_new_tokens=48,
+        spec = speculative_generate(target, None, drafter, lookup_drafts=False, prompt_ids=prompt, max_new_tokens=48,
                                     max_draft_tokens=None)
         print("spec done", flush=True)
         plain = greedy_generate(target, None, prompt_ids=prompt, max_new_tokens=32)
@@ -103,7 +103,8 @@ def test_tp2_matches_oracle():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    logdir = os.environ.get("DSPARK_TEST_LOGDIR", "gpurun_out")
+    import tempfile
+    logdir = os.environ.get("DSPARK_TEST_LOGDIR") or tempfile.mkdtemp(prefix="dspark_tp_")
     os.makedirs(logdir, exist_ok=True)
     procs = [ctx.Process(target=_rank_main, args=(r, 2, port, q, logdir)) for r in range(2)]
     for p in procs:
@@ -122,7 +123,7 @@ def test_tp2_matches_oracle():
             if p.is_alive():
                 p.terminate()
                 p.join(timeout=30)
-    assert msg is not None, "no result from the ranks (see gpurun_out/tp_rank*.log)"
+    assert msg is not None, f"no result from the ranks (see {logdir}/tp_rank*.log)"
     assert msg[0] == "ok", msg
     _, gl, prompt, spec, plain, same, fused_same = msg
     assert all(p.exitcode == 0 for p in procs)

@@ -95,7 +95,7 @@ def test_gqa_broadcast_equals_explicit_tiling():
 
 
 def test_topp_speculative_sampling_is_lossless():
-    """tests/test_generate_helpers.py:205-230 of the reference: the committed token is an
+    """tests/test_generate_helpers.py:145-170 of the reference: the committed token is an
     exact sample from top-p/top-k(softmax(target/T)) whatever the draft q (0.02 max-abs,
     20000 draws)."""
     import numpy as np
