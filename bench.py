@@ -66,8 +66,9 @@ def parse():
                     help="under torchrun (2..8 ranks): one row-split projection of the Qwen3-32B "
                          "shapes at M = 9, the fused peer all-reduce against NCCL, one JSON line")
     ap.add_argument("--serve", action="store_true",
-                    help="the continuous-batching workload (C4 shapes: 32 requests over 4 slots, a "
-                         "shared 2048-token prefix, 8-bit KV) through serve_requests, one JSON line")
+                    help="the continuous-batching workload (C4 shapes: 32 requests, 4 slots per GPU, "
+                         "a shared 2048-token prefix, 8-bit KV) over --gpus replicas, one JSON line "
+                         "(run as one process; it starts a worker process per GPU)")
     ap.add_argument("--profile-prefill", action="store_true",
                     help="small run for ncu: two prefills of --prompt-len tokens (default 2048) "
                          "through the large-M GEMM, nothing else")
@@ -460,16 +461,21 @@ def run_tp_allreduce(world, rank):
 
 
 def run_serve(args):
-    """C4 on one GPU: 32 requests (a shared random 2048-token prefix plus a random 64-2048-token
-    suffix, 128-1024 output tokens) through serve_requests with 4 slots, the 8-bit KV cache and
-    DSpark cap 8. With random weights the drafts are rejected, so the figure measures the
-    batched verify, admission and prefill machinery, not speculation."""
-    from mlx_dspark_b200.batch_engine import serve_requests
-    from mlx_dspark_b200.config import WORKLOADS
+    """C4 continuous batching: 32 requests (a shared random 2048-token prefix plus a random
+    64-2048-token suffix, 128-1024 output tokens) over N GPUs, one ReplicaPool worker process
+    per GPU (its own Qwen3-8B W8 replica with the 8-bit KV cache, a 4-slot BatchEngine, DSpark
+    cap 8, no collective), each request sent to the least-loaded replica. Value = generated
+    tokens / wall time from the first submit to the last result, after one warm-up request per
+    replica. With random weights the drafts are rejected, so the figure measures the batched
+    verify, admission and prefill machinery, not speculation."""
+    import functools
+
+    from mlx_dspark_b200.config import TARGETS, WORKLOADS
+    from mlx_dspark_b200.engine import ReplicaPool, serving_replica
 
     wl = WORKLOADS["C4"]
-    _, target, drafter, _ = build_models(wl, wl.seed, args.layers, keep_cpu=False)
-    V = target.cfg.vocab_size
+    n = max(1, args.gpus)
+    V = TARGETS[wl.target].vocab_size
     g = torch.Generator().manual_seed(4)
     prefix = torch.randint(0, V, (wl.prompt_len,), generator=g).tolist()
     reqs = []
@@ -477,28 +483,39 @@ def run_serve(args):
         sfx = int(torch.randint(64, 2049, (1,), generator=g))
         out = int(torch.randint(128, 1025, (1,), generator=g))
         reqs.append((prefix + torch.randint(0, V, (sfx,), generator=g).tolist(), out))
-    cap = wl.block_size
-    serve_requests(target, None, drafter, [(prefix[:300], 16), (prefix[:200], 16)],
-                   capacity=wl.batch, max_draft_tokens=cap)   # warm-up: graphs, workspaces
-    torch.cuda.synchronize()
-    t0 = time.time()
-    res, st = serve_requests(target, None, drafter, reqs, capacity=wl.batch, max_draft_tokens=cap)
-    torch.cuda.synchronize()
-    dt = time.time() - t0
-    target.scratch.check_status()
+    slot_tokens = max(len(p) + m for p, m in reqs) + 2 * wl.block_size + 64
+    factory = functools.partial(serving_replica, target=wl.target, seed=wl.seed,
+                                kv_bits=wl.kv_bits, block_size=wl.block_size,
+                                max_batch=wl.batch, slot_tokens=slot_tokens,
+                                max_draft_tokens=wl.block_size)
+    pool = ReplicaPool(factory, list(range(n)))
+    try:
+        warm = [pool.submit(prefix[:300], max_tokens=16, temperature=0.0) for _ in range(n)]
+        for f in warm:
+            f.result()
+        pool.assigned = [0] * n
+        t0 = time.time()
+        futs = [pool.submit(p, max_tokens=m, temperature=0.0) for p, m in reqs]
+        res = [f.result() for f in futs]
+        dt = time.time() - t0
+        assigned = list(pool.assigned)
+    finally:
+        pool.close()
     toks = sum(r.num_tokens for r in res)
-    rounds_with_drafts = sum(len(r.accept_lengths) for r in res)
+    rounds = sum(r.num_rounds for r in res)
     print(json.dumps({
-        "metric": "served tok/s, continuous batching (C4 shapes, 1 GPU)", "value": round(toks / dt, 1),
-        "unit": "tok/s", "higher_is_better": True, "n_gpus": 1,
-        "config": {"workload": wl.name, "requests": len(reqs), "slots": wl.batch,
-                   "kv_bits": wl.kv_bits, "draft_cap": cap, "shared_prefix": wl.prompt_len},
+        "metric": "served tok/s, continuous batching (C4 shapes)", "value": round(toks / dt, 1),
+        "unit": "tok/s", "higher_is_better": True, "n_gpus": n, "scaling": "strong",
+        "config": {"workload": wl.name, "requests": len(reqs), "slots_per_gpu": wl.batch,
+                   "kv_bits": wl.kv_bits, "draft_cap": wl.block_size,
+                   "shared_prefix": wl.prompt_len, "dispatch": "least outstanding tokens",
+                   "parallelism": f"request-parallel x{n} (one process per GPU)"},
         "data": "synthetic: random-init W8 weights (seed 1), random prompt ids; drafts rejected",
-        "tokens": toks, "seconds": round(dt, 2), "rounds": st["rounds"],
-        "ms_per_round": round(1000 * dt / max(1, st["rounds"]), 2),
-        "mean_accept_len": round(sum(sum(r.accept_lengths) for r in res) / max(1, rounds_with_drafts), 3),
-        "prompt_tokens": sum(len(p) for p, _ in reqs), "prefill_tokens": st["prefill_tokens"],
-        "prefix_hits": st["prefix_hits"], "prefix_reused_tokens": st["prefix_reused_tokens"]}),
+        "tokens": toks, "seconds": round(dt, 2), "requests_per_gpu": assigned,
+        "mean_accept_len": round(toks / max(1, rounds), 3),
+        "prompt_tokens": sum(len(p) for p, _ in reqs),
+        "replicas": {str(k): v.get("batching") for k, v in sorted(pool.replica_metrics.items())},
+        "prefix_cache": {str(k): v.get("prefix_cache") for k, v in sorted(pool.replica_metrics.items())}}),
         flush=True)
     return 0
 
@@ -698,11 +715,11 @@ def main():
         if out is not None:
             print(json.dumps(out), flush=True)
         return 0
+    if args.serve:
+        return run_serve(args)       # one process per GPU of its own (ReplicaPool)
     world, rank, _ = dist_setup(args.gpus)
     if args.profile_prefill:
         return run_profile_prefill(args)
-    if args.serve:
-        return run_serve(args)
     if args.tp_allreduce:
         return run_tp_allreduce(world, rank)
     try:

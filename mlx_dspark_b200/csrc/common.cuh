@@ -46,6 +46,12 @@ __device__ __forceinline__ float bf16_round(float x) {
   return __bfloat162float(__float2bfloat16_rn(x));
 }
 
+// x * sigmoid(x) with every rounding explicit: the compiler may not contract it differently
+// in different kernels, so every GEMM epilogue that applies it gives the same bits
+__device__ __forceinline__ float silu_rn(float x) {
+  return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x)));
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -44,11 +44,11 @@ __device__ __forceinline__ void rope_kv_head(const __nv_bfloat16* head, int Hq, 
     const __nv_bfloat16* nw = h < Hq ? qnw : knw;
     float ss = 0.0f;
 #pragma unroll
-    for (int e = 0; e < E; ++e) ss += x[e] * x[e];
+    for (int e = 0; e < E; ++e) ss = __fmaf_rn(x[e], x[e], ss);
     ss = warp_sum(ss);
-    const float r = rsqrtf(ss / (float)HD + eps);
+    const float r = rsqrtf(__fadd_rn(__fdiv_rn(ss, (float)HD), eps));
 #pragma unroll
-    for (int e = 0; e < E; ++e) x[e] = bf16_round(x[e] * r * __bfloat162float(nw[lane * E + e]));
+    for (int e = 0; e < E; ++e) x[e] = bf16_round(__fmul_rn(__fmul_rn(x[e], r), __bfloat162float(nw[lane * E + e])));
     // RoPE (rotate-half): pair element i with i + HD/2
     float other[E];
 #pragma unroll
@@ -59,7 +59,9 @@ __device__ __forceinline__ void rope_kv_head(const __nv_bfloat16* head, int Hq, 
       const int fi = (lane & 15) * E + e;
       float sn, cs;
       sincosf((float)pos * inv_freq[fi], &sn, &cs);
-      x[e] = upper ? bf16_round(x[e] * cs + other[e] * sn) : bf16_round(x[e] * cs - other[e] * sn);
+      // explicit roundings: the same bits in every kernel that inlines this
+      x[e] = upper ? bf16_round(__fadd_rn(__fmul_rn(x[e], cs), __fmul_rn(other[e], sn)))
+                   : bf16_round(__fsub_rn(__fmul_rn(x[e], cs), __fmul_rn(other[e], sn)));
     }
   }
   if (h < Hq) {
@@ -77,8 +79,13 @@ __device__ __forceinline__ void rope_kv_head(const __nv_bfloat16* head, int Hq, 
 #pragma unroll
     for (int e = 0; e < E; ++e) dst[e] = __float2bfloat16_rn(x[e]);
   } else {
-    // affine 8-bit, group 64 along head_dim: scale = (max-min)/255, bias = min (bf16),
-    // q = clamp(rint((x - bias) / scale), 0, 255)
+    // affine 8-bit, group 64 along head_dim, by the rule of MLX's affine quantizer (what
+    // QuantizedKVCache(64, 8) applies through mx.quantize): in fp32,
+    //   scale = max((max - min) / 255, 1e-7), negated unless |min| > |max|;
+    //   edge  = the value of larger magnitude (min or max), made exactly representable:
+    //   q0 = round(edge / scale); scale = edge / q0 and bias = edge, or bias = 0 if q0 == 0;
+    //   q = min(round((x - bias) / scale), 255)   (round: halves away from zero)
+    // with the fp32 scale and bias; both are stored as bf16 (the dequantization operands).
     constexpr int LPG = 64 / E;  // lanes per group
     float mn = x[0], mx = x[0];
 #pragma unroll
@@ -88,13 +95,19 @@ __device__ __forceinline__ void rope_kv_head(const __nv_bfloat16* head, int Hq, 
       mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     }
-    const float sc = bf16_round((mx - mn) / 255.0f);
-    const float bi = bf16_round(mn);
+    float sc = fmaxf((mx - mn) / 255.0f, 1e-7f);
+    const bool neg_edge = fabsf(mn) > fabsf(mx);
+    sc = neg_edge ? sc : -sc;
+    const float edge = neg_edge ? mn : mx;
+    const float q0 = roundf(edge / sc);
+    const bool at_zero = q0 == 0.0f;
+    sc = at_zero ? sc : edge / q0;
+    const float bi = at_zero ? 0.0f : edge;
     uint8_t* qdst = a.page + row * HD + lane * E;
 #pragma unroll
     for (int e = 0; e < E; ++e) {
-      float qv = sc > 0.0f ? rintf((x[e] - bi) / sc) : 0.0f;
-      qv = fminf(fmaxf(qv, 0.0f), 255.0f);
+      // (x - bias) / scale >= 0 by construction; the lower clamp only guards the cast
+      const float qv = fminf(fmaxf(roundf((x[e] - bi) / sc), 0.0f), 255.0f);
       qdst[e] = (uint8_t)qv;
     }
     if ((lane % LPG) == 0) {

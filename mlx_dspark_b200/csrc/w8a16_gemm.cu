@@ -44,8 +44,6 @@ constexpr int kEpiWarps = 4;    // warps 4..7
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr int kThreads = 320;
-constexpr int kABufs = 2;       // TMEM A ring (64 columns each: 128 fp16 per lane)
-constexpr int kTmemCols = 256;  // [0,128) A ring, [128,256) two accumulators of <= 64 columns
 constexpr uint32_t kWBytes = BM * BK;   // 16 KB
 constexpr uint32_t kSBBytes = 2 * BM * 4;  // 1 KB
 // Workspace: a fixed counter region first (one int per N-tile, at most kMaxTiles), then the
@@ -79,10 +77,6 @@ struct Params {
   float* partials;  // [grid][2][BN][128]
   int* counters;    // [tiles]
   int* status;
-  // > 1: cluster split-K. CTA b works on tile b / csplit, k-slice b % csplit; the csplit CTAs
-  // of a tile form one thread-block cluster and sum their partials through distributed shared
-  // memory. 0: stream-K over the whole grid.
-  int csplit;
   RopeEpi rope;
   // RMSNorm plumbing between GEMMs (dspark_gemm_opts): the STORE_BF16 / RESIDUAL_BF16 epilogues
   // write per-tile sums of squares of their bf16 outputs to ss_out [M][tiles]; a GEMM with norm_w
@@ -100,6 +94,11 @@ struct Params {
   // range after issuing its last load (16-byte aligned, sizes multiples of 16)
   const char* pf_ptr[2];
   unsigned long long pf_bytes[2];
+  // tile-ready chaining (dspark_gemm_opts.chain_*): finished tiles counted in this launch's
+  // slot; activations (and norm sums) read once the previous GEMM's slot is full, instead of
+  // after that grid has completed (griddepcontrol.wait)
+  int* chain_sync;
+  int chain_slot, chain_wait, chain_wait_tiles;
   // PEER_F32 (dspark_w8a16_gemm_peer): every rank's receive buffer and flags, as mapped here
   float* peer_y[8];
   int* peer_f[8];
@@ -114,12 +113,70 @@ __device__ __forceinline__ long long range_owner(long long g, long long total, l
   return ((g + 1) * G + total - 1) / total - 1;
 }
 
-__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
+constexpr int kChainStride = 32;  // ints per chain slot (128 bytes): [0] finished tiles of the
+                                  // slot's GEMM, [1] CTAs of the GEMM waiting on it that have
+                                  // seen [0] full
+__device__ __forceinline__ int ld_acquire_gpu_i(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// A finished tile of a GEMM that owns a chain slot: once the 128 epilogue threads have
+// stored it, one release increment of the slot (cumulative through the barrier).
+template <typename PT>
+__device__ __forceinline__ void chain_tile_done(const PT& p, int er) {
+  if (p.chain_slot < 0) return;
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+  if (er == 0)
+    asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(p.chain_sync + p.chain_slot * kChainStride)
+                 : "memory");
+}
+
+// The inputs of this GEMM are ready: the previous kernel has completed (griddepcontrol.wait),
+// or, chained, every tile of the previous GEMM is finished (a bounded acquire poll of its
+// slot). False if the wait gave up (DSPARK_ERR_TIMEOUT in *status, abort flag set).
+template <typename PT>
+__device__ __forceinline__ bool inputs_ready(const PT& p, volatile int* abort_flag) {
+  if (p.chain_wait < 0) {
+    pdl_wait();
+    return true;
+  }
+  const int* cnt = p.chain_sync + p.chain_wait * kChainStride;
+  if (ld_acquire_gpu_i(cnt) >= p.chain_wait_tiles) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  while (ld_acquire_gpu_i(cnt) < p.chain_wait_tiles) {
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > kSpinLimitNs) {
+      *abort_flag = 1;
+      report_error(p.status, DSPARK_ERR_TIMEOUT);
+      return false;
+    }
+    __nanosleep(32);
+  }
+  return true;
+}
+
+// Chained: this CTA has seen the slot it waited on full. The last of the `workers` CTAs that
+// wait on it (those with work) resets the slot for its next use. That happens before this
+// GEMM finishes any tile, so before anything that follows it in the chain can run, and so
+// before the slot's owner runs again.
+template <typename PT>
+__device__ __forceinline__ void chain_passed(const PT& p, int workers) {
+  int* slot = p.chain_sync + p.chain_wait * kChainStride;
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(slot + 1) : "memory");
+  if (old == workers - 1) {
+    asm volatile("st.relaxed.gpu.global.s32 [%0], 0;" ::"l"(slot) : "memory");
+    asm volatile("st.relaxed.gpu.global.s32 [%0], 0;" ::"l"(slot + 1) : "memory");
+    __threadfence();
+  }
+}
+
 
 // PEER: the instance of the tensor-parallel fused all-reduce (dspark_w8a16_gemm_peer); the
 // other instances carry no code for it
-template <int BN, bool PEER = false>
-__device__ __forceinline__ void epilogue_store(const Params& p, int tile, int er, const float* acc,
+template <int BN, bool PEER = false, typename PT>
+__device__ __forceinline__ void epilogue_store(const PT& p, int tile, int er, const float* acc,
                                                float* xch,
                                                const __nv_bfloat162* rpre = nullptr) {
   const int n = tile * BM + er;
@@ -134,7 +191,7 @@ __device__ __forceinline__ void epilogue_store(const Params& p, int tile, int er
           y[(size_t)m * p.ldy + n] = o;
           if (p.ss_out) {
             const float v = __bfloat162float(o);
-            const float w = warp_sum(v * v);
+            const float w = warp_sum(__fmul_rn(v, v));
             if (lane == 0) xch[ew * BN + m] = w;
           }
         }
@@ -191,7 +248,7 @@ __device__ __forceinline__ void epilogue_store(const Params& p, int tile, int er
           if (rpre)  // read by the caller before it waited on the other contributors
             rv[j] = (m & 1) ? rpre[m >> 1].y : rpre[m >> 1].x;
           else
-            rv[j] = m < p.M ? r[(size_t)m * p.ldr + n] : __float2bfloat16_rn(0.0f);
+            rv[j] = m < p.M ? __ldcg(r + (size_t)m * p.ldr + n) : __float2bfloat16_rn(0.0f);
         }
 #pragma unroll
         for (int j = 0; j < 16; ++j)
@@ -202,7 +259,7 @@ __device__ __forceinline__ void epilogue_store(const Params& p, int tile, int er
             if (p.ss_out) {
               // this row's share of the next RMSNorm: warp sum, then the 4 warps in order
               const float v = __bfloat162float(o);
-              const float w = warp_sum(v * v);
+              const float w = warp_sum(__fmul_rn(v, v));
               if (lane == 0) xch[ew * BN + c0 + j] = w;
             }
           }
@@ -237,7 +294,7 @@ __device__ __forceinline__ void epilogue_store(const Params& p, int tile, int er
             if (c0 + j < p.M) {
               const float g = bf16_round(acc[c0 + j]);
               const float u = bf16_round(up[j]);
-              const float s = bf16_round(silu_f(g));
+              const float s = bf16_round(silu_rn(g));
               y[(size_t)(c0 + j) * p.ldy + col] = __float2half_rn(bf16_round(s * u));
             }
         }
@@ -250,42 +307,12 @@ __device__ __forceinline__ void epilogue_store(const Params& p, int tile, int er
   }
 }
 
-// One output of the tile from its accumulated value v (and, for SILU_MUL, the matching up-row
-// value vu): the same arithmetic as epilogue_store, element by element. `row` is the tile row
-// (for SILU_MUL a gate row < 64), m the activation row.
-__device__ __forceinline__ void epilogue_one(const Params& p, int tile, int row, int m, float v,
-                                             float vu) {
-  switch (p.epilogue) {
-    case DSPARK_EPI_STORE_BF16:
-      static_cast<__nv_bfloat16*>(p.y)[(size_t)m * p.ldy + tile * BM + row] = __float2bfloat16_rn(v);
-      break;
-    case DSPARK_EPI_STORE_F32:
-      static_cast<float*>(p.y)[(size_t)m * p.ldy + tile * BM + row] = v;
-      break;
-    case DSPARK_EPI_RESIDUAL_BF16: {
-      const size_t n = (size_t)tile * BM + row;
-      const float rv = __bfloat162float(static_cast<const __nv_bfloat16*>(p.residual)[(size_t)m * p.ldr + n]);
-      static_cast<__nv_bfloat16*>(p.y)[(size_t)m * p.ldy + n] = __float2bfloat16_rn(rv + bf16_round(v));
-      break;
-    }
-    case DSPARK_EPI_SILU_MUL_F16: {
-      const float g = bf16_round(v);
-      const float u = bf16_round(vu);
-      const float sg = bf16_round(silu_f(g));
-      static_cast<__half*>(p.y)[(size_t)m * p.ldy + tile * 64 + row] = __float2half_rn(bf16_round(sg * u));
-      break;
-    }
-    default:
-      break;
-  }
-}
-
 // The fused q|k|v epilogue of a finished tile: stage the tile's bf16 outputs (the values the
 // separate q|k|v GEMM would store) in shared memory as [m][128], then one warp per (token, head
 // in the tile) runs the same norm + RoPE + KV write as the standalone kernel. The staging fits
 // the exchange buffer: BN x 128 bf16 = 64 x BN fp32.
-template <int BN>
-__device__ __forceinline__ void rope_epilogue(const Params& p, int tile, int er, const float* acc,
+template <int BN, typename PT>
+__device__ __forceinline__ void rope_epilogue(const PT& p, int tile, int er, const float* acc,
                                               float* xch) {
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(xch);
 #pragma unroll
@@ -319,8 +346,8 @@ struct Smem {
   static constexpr uint32_t kTotal = 1024 + STAGES * kStageBytes + kXchBytes + kBarBytes;
 };
 
-template <int BN, int STAGES, bool CS, bool ROPE, bool PEER = false>
-__global__ void __launch_bounds__(kThreads, (BN <= 32 && !CS ? 2 : 1))
+template <int BN, int STAGES, bool ROPE, bool PEER = false>
+__global__ void __launch_bounds__(kThreads, (BN <= 32 ? 2 : 1))
     w8a16_tc_kernel(const __grid_constant__ CUtensorMap tm_w,
                     const __grid_constant__ CUtensorMap tm_sb,
                     const __grid_constant__ CUtensorMap tm_x, const Params p) {
@@ -329,13 +356,13 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 && !CS ? 2 : 1))
   // fp32 accumulators of ACCS columns. Two CTAs per SM share the 512 columns; one CTA per SM
   // takes all of them for a deeper ring (the ring depth bounds how far conversion runs ahead
   // of MMA completion).
-  constexpr bool kTwoPerSm = BN <= 32 && !CS;
+  constexpr bool kTwoPerSm = BN <= 32;
   constexpr int AB = kTwoPerSm ? 3 : 6;
   constexpr uint32_t ACCS = BN <= 32 ? 32u : 64u;
   constexpr uint32_t ACC0 = (uint32_t)AB * 64u;
   constexpr uint32_t TC = kTwoPerSm ? 256u : 512u;
   static_assert(ACC0 + 2 * ACCS <= TC, "TMEM layout");
-  static_assert(3 * STAGES + 2 * AB + 8 <= (int)(L::kBarBytes / 8), "barrier region");
+  static_assert(3 * STAGES + 2 * AB + 9 <= (int)(L::kBarBytes / 8), "barrier region");
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -359,6 +386,8 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 && !CS ? 2 : 1))
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_holder + 2);
   const uint32_t fix_bar = smem_u32(bars + 3 * STAGES + 2 * AB + 7);  // stream-K fixup copies
+  // the producer's wait for this GEMM's inputs, passed on to the converters (one poller per CTA)
+  const uint32_t ready_bar = smem_u32(bars + 3 * STAGES + 2 * AB + 8);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -379,6 +408,7 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 && !CS ? 2 : 1))
     }
     mbar_init(done_bar, 1);
     mbar_init(fix_bar, 1);
+    mbar_init(ready_bar, 1);
     *abort_flag = 0;
     *last_flag = 0;
     fence_mbar_init();
@@ -402,15 +432,8 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 && !CS ? 2 : 1))
   const long long G = gridDim.x;
   const long long total = p.total;
   const int KB = p.kb;
-  long long start, end;
-  if constexpr (CS) {
-    const int tile = (int)(blockIdx.x / p.csplit), r = (int)(blockIdx.x % p.csplit);
-    start = (long long)tile * KB + (long long)r * KB / p.csplit;
-    end = (long long)tile * KB + (long long)(r + 1) * KB / p.csplit;
-  } else {
-    start = range_start(blockIdx.x, total, G);
-    end = range_start(blockIdx.x + 1, total, G);
-  }
+  const long long start = range_start(blockIdx.x, total, G);
+  const long long end = range_start(blockIdx.x + 1, total, G);
   const int n_iter = (int)(end - start);
 
   if (warp == kProducerWarp) {
@@ -426,8 +449,17 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 && !CS ? 2 : 1))
         tma_load_2d(w_s + i * kWBytes, &tm_w, full(i), kb * BK, tile * BM, pol_w);
         tma_load_2d(sb_s + i * kSBBytes, &tm_sb, full(i), tile * BM, kb * 2, pol_w);
       }
-      pdl_wait();  // activations are written by the previous kernel
-      for (int i = 0; i < pre; ++i) {
+      // activations are written by the previous kernel (or the previous chained GEMM, whose
+      // generic stores this TMA reads through the async proxy); a chained CTA without work
+      // reads nothing and does not wait
+      const bool chained = p.chain_wait >= 0;
+      const bool in_ok = (chained && n_iter == 0) ? true : inputs_ready(p, abort_flag);
+      if (in_ok) mbar_arrive(ready_bar);
+      if (chained && n_iter > 0 && in_ok) {
+        fence_proxy_async_global();
+        chain_passed(p, (int)(total < G ? total : G));
+      }
+      for (int i = 0; i < (in_ok ? pre : 0); ++i) {
         const long long g = start + i;
         const int kb = (int)(g % KB);
         mbar_arrive_expect_tx(xfull(i), L::kXBytes);
@@ -435,7 +467,7 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 && !CS ? 2 : 1))
         tma_load_2d(x_s + i * L::kXBytes + BN * 128, &tm_x, xfull(i), kb * BK + 64, 0, pol_x);
       }
       int issued = pre;
-      for (int i = pre; i < n_iter; ++i) {
+      for (int i = pre; i < (in_ok ? n_iter : 0); ++i) {
         const int s = i % STAGES;
         const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
         if (!mbar_wait(empty(s), ph ^ 1u, abort_flag, p.status)) break;
@@ -564,7 +596,12 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 && !CS ? 2 : 1))
       }
       if (p.norm_w) {
         if (i == 0) {
-          pdl_wait();  // the row sums of squares come from the previous kernel
+          // the row sums of squares come from the previous kernel / chained GEMM: ready once
+          // the producer's wait has passed
+          if (!mbar_wait(ready_bar, 0, abort_flag, p.status)) {
+            tc_wait_st();
+            break;
+          }
 #pragma unroll
           for (int kk = 0; kk < BN / 16; ++kk) {
             const int m = (r >> 3) + 16 * kk;
@@ -573,14 +610,15 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 && !CS ? 2 : 1))
               // the row's per-tile sums, contiguous: 16-byte loads, added in tile order
               const float* row = p.ss_in + (size_t)m * p.ss_ld;
               int t = 0;
+              // (read from L2: written by another grid that may still be running)
               if ((p.ss_ld & 3) == 0)
                 for (; t + 4 <= p.ss_tiles; t += 4) {
-                  const float4 q4 = *reinterpret_cast<const float4*>(row + t);
+                  const float4 q4 = __ldcg(reinterpret_cast<const float4*>(row + t));
                   sum = (((sum + q4.x) + q4.y) + q4.z) + q4.w;
                 }
-              for (; t < p.ss_tiles; ++t) sum += row[t];
+              for (; t < p.ss_tiles; ++t) sum += __ldcg(row + t);
             }
-            rn[kk] = rsqrtf(sum / (float)p.K + p.norm_eps);
+            rn[kk] = rsqrtf(__fadd_rn(__fdiv_rn(sum, (float)p.K), p.norm_eps));
           }
         }
         if (!mbar_wait(xfull(s), ph, abort_flag, p.status)) {
@@ -607,7 +645,7 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 && !CS ? 2 : 1))
             for (int q = 0; q < 4; ++q) {
               const float2 hv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v[q]));
               const float2 wf = __bfloat1622float2(wv[q]);
-              const __nv_bfloat162 xn = __floats2bfloat162_rn(hv.x * rn[kk] * wf.x, hv.y * rn[kk] * wf.y);
+              const __nv_bfloat162 xn = __floats2bfloat162_rn(__fmul_rn(__fmul_rn(hv.x, rn[kk]), wf.x), __fmul_rn(__fmul_rn(hv.y, rn[kk]), wf.y));
               const float2 xf = __bfloat1622float2(xn);
               const __half2 x16 = __floats2half2_rn(xf.x, xf.y);
               v[q] = *reinterpret_cast<const uint32_t*>(&x16);
@@ -632,7 +670,9 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 && !CS ? 2 : 1))
     // epilogue: thread er owns row er of the tile (TMEM lane er)
     const int er = threadIdx.x - kConvWarps * 32;
     const int quad = warp & 3;
-    pdl_wait();
+    // outputs may still be read by the previous kernel; a chained GEMM's inputs come from the
+    // GEMM before it, whose reads of this GEMM's outputs ended before its tiles were finished
+    if (p.chain_wait < 0) pdl_wait();
     int seg = 0;
     uint32_t fix_phase = 0;
     long long g = start;
@@ -660,20 +700,12 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 && !CS ? 2 : 1))
       __syncwarp();
       if (lane == 0) mbar_arrive(accempty(ab));
 
-      if constexpr (CS) {
-        // cluster split-K: this CTA's only segment. Every MMA of the CTA has completed, so no
-        // copy or MMA touches the stage ring any more: the partial goes to its start, row er's
-        // BN values contiguous, and the cluster sums them after the role loops.
-        float4* part = reinterpret_cast<float4*>(reinterpret_cast<float*>(sbase) + er * BN);
-#pragma unroll
-        for (int j = 0; j < BN / 4; ++j)
-          part[j] = make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
-        (void)whole;
-      } else if (whole) {
+      if (whole) {
         if constexpr (ROPE)
           rope_epilogue<BN>(p, tile, er, acc, xch);
         else
           epilogue_store<BN, PEER>(p, tile, er, acc, xch);
+        chain_tile_done(p, er);
       } else {
         // partial of this CTA, row-major [128][MP] with MP = M rounded up to 4: thread er's
         // values are 16-byte vectors, and each contributor's partial is one contiguous
@@ -698,8 +730,8 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 && !CS ? 2 : 1))
 #pragma unroll
             for (int j = 0; j < BN / 2; ++j) {
               const int m = 2 * j;
-              rpre[j].x = m < p.M ? rp[(size_t)m * p.ldr] : __float2bfloat16_rn(0.0f);
-              rpre[j].y = m + 1 < p.M ? rp[(size_t)(m + 1) * p.ldr] : __float2bfloat16_rn(0.0f);
+              rpre[j].x = m < p.M ? __ldcg(rp + (size_t)m * p.ldr) : __float2bfloat16_rn(0.0f);
+              rpre[j].y = m + 1 < p.M ? __ldcg(rp + (size_t)(m + 1) * p.ldr) : __float2bfloat16_rn(0.0f);
             }
           } else {
 #pragma unroll
@@ -802,6 +834,7 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 && !CS ? 2 : 1))
             rope_epilogue<BN>(p, tile, er, sum, xch);
           else
             epilogue_store<BN, PEER>(p, tile, er, sum, xch, (kPre && res) ? rpre : nullptr);
+          chain_tile_done(p, er);
         }
         asm volatile("bar.sync 1, 128;" ::: "memory");
       }
@@ -810,45 +843,10 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 && !CS ? 2 : 1))
     }
   }
 
-  if constexpr (CS) {
-    // Every thread of every CTA of the cluster takes both cluster barriers (no early exits
-    // above, and each role loop ends after its bounded waits), so both barriers complete.
-    cluster_sync_all();  // release/acquire: every CTA's partial is visible cluster-wide
-    if (warp >= kConvWarps && warp < kConvWarps + kEpiWarps && !*abort_flag) {
-      // CTA rank r finishes tile rows [r0, r1) for every activation row, summing the csplit
-      // partials in rank order (the same order whichever CTA finishes first)
-      const int t = threadIdx.x - kConvWarps * 32;
-      const int c = p.csplit;
-      const int rank = (int)(blockIdx.x % c);  // == %cluster_ctarank: clusters are (c, 1, 1)
-      const int tile = (int)(blockIdx.x / c);
-      const bool silu = p.epilogue == DSPARK_EPI_SILU_MUL_F16;
-      const int rows = silu ? BM / 2 : BM;
-      const int r0 = rank * rows / c, r1 = (rank + 1) * rows / c;
-      const int nr = r1 - r0;
-      uint32_t peer[8];  // shared::cluster address of each slice's partial
-#pragma unroll
-      for (int q = 0; q < 8; ++q) peer[q] = q < c ? mapa_shared(base, (uint32_t)q) : 0u;
-      auto slice_sum = [&](uint32_t off) {
-        float v[8];
-#pragma unroll
-        for (int q = 0; q < 8; ++q)
-          if (q < c) v[q] = ld_shared_cluster_f32(peer[q] + off);
-        float sum = 0.0f;
-#pragma unroll
-        for (int q = 0; q < 8; ++q)
-          if (q < c) sum += v[q];
-        return sum;
-      };
-      for (int o = t; o < nr * p.M; o += kEpiWarps * 32) {
-        const int m = o / nr, row = r0 + (o - m * nr);
-        const float sv = slice_sum((uint32_t)(row * BN + m) * 4u);
-        const float su = silu ? slice_sum((uint32_t)((row + BM / 2) * BN + m) * 4u) : 0.0f;
-        epilogue_one(p, tile, row, m, sv, su);
-      }
-    }
-    cluster_sync_all();  // no CTA leaves while a peer still reads its shared memory
-  }
 
+  // a role that ran on one lane (producer, MMA issuer) rejoins its warp before the
+  // CTA barrier: the barrier counts whole warps, and TMEM is freed after it
+  __syncwarp();
   tc_fence_before();
   __syncthreads();
   if (warp == kProducerWarp) {
@@ -858,158 +856,102 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 && !CS ? 2 : 1))
 }
 
 // ------------------------------------------------------------------------------------------
-// SIMT cross-check kernel: one warp per output column n, fp32 dequant and accumulation.
-// Used by the GPU tests to check the tensor-core path on the device and as a diagnostic.
-template <int MT>
-__global__ void __launch_bounds__(256) w8a16_simt_kernel(const __half* __restrict__ x, int ldx,
-                                                         const uint8_t* __restrict__ wq,
-                                                         const uint32_t* __restrict__ wsb,
-                                                         Params p) {
-  pdl_wait();
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (warp >= p.N) return;
-  const int n = warp;
-  float acc[MT];
-#pragma unroll
-  for (int m = 0; m < MT; ++m) acc[m] = 0.0f;
-  for (int k = lane; k < p.K; k += 32) {
-    const uint32_t sbv = wsb[(size_t)(k >> 6) * p.N + n];
-    const __half2 sb2 = *reinterpret_cast<const __half2*>(&sbv);
-    const float w = __low2float(sb2) * (float)wq[(size_t)n * p.K + k] + __high2float(sb2);
-#pragma unroll
-    for (int m = 0; m < MT; ++m)
-      if (m < p.M) acc[m] += __half2float(x[(size_t)m * ldx + k]) * w;
-  }
-#pragma unroll
-  for (int m = 0; m < MT; ++m) acc[m] = warp_sum(acc[m]);
-  if (lane != 0) return;
-  // scalar epilogue (one thread per column)
-  for (int m = 0; m < p.M; ++m) {
-    const float a = acc[m];
-    switch (p.epilogue) {
-      case DSPARK_EPI_STORE_BF16:
-        static_cast<__nv_bfloat16*>(p.y)[(size_t)m * p.ldy + n] = __float2bfloat16_rn(a);
-        break;
-      case DSPARK_EPI_STORE_F32:
-        static_cast<float*>(p.y)[(size_t)m * p.ldy + n] = a;
-        break;
-      case DSPARK_EPI_RESIDUAL_BF16: {
-        const float rv =
-            __bfloat162float(static_cast<const __nv_bfloat16*>(p.residual)[(size_t)m * p.ldr + n]);
-        static_cast<__nv_bfloat16*>(p.y)[(size_t)m * p.ldy + n] =
-            __float2bfloat16_rn(rv + bf16_round(a));
-        break;
-      }
-      default:
-        break;  // the gate/up pairing needs the tiled kernel
-    }
-  }
-}
+// K1s — the W8 GEMMs between two attention kernels as ONE persistent launch ("stream").
+//
+// A verify layer runs o (+residual) -> gate|up (input norm, SiLU*up) -> down (+residual, tap)
+// -> the next layer's q|k|v (input norm, RoPE + KV write). At M <= 64 rows each is a few
+// microseconds of weight streaming, and as separate launches each also paid a ramp (its CTAs
+// start as the previous kernel's CTAs leave) and a tail (the stream-K fixups of the last
+// tiles). Here one resident grid walks the jobs in order, each CTA taking its stream-K range of
+// every job:
+//   - the producer thread streams the weight tiles of every job back to back, waiting only for
+//     free ring slots, so the next job's weights are already in shared memory while the
+//     previous job finishes;
+//   - the same thread issues a job's activation loads once every tile of the job before it is
+//     finished: the CTA that finishes a tile raises the job's counter with release semantics,
+//     and the producer polls it with acquire loads (the first job's activations come from the
+//     previous kernel, behind griddepcontrol.wait);
+//   - converter, MMA and epilogue warps are those of w8a16_tc_kernel; a tile split across CTAs
+//     is summed in a fixed-point accumulator (each contributor adds its fp32 partial as a 64-bit
+//     integer of 2^-32 units with an atomic add, so the sum does not depend on arrival order)
+//     and finished by its last contributor, which reads that one block: the end of a job costs
+//     one L2 round trip instead of one per contributor. One accumulator region per job, since
+//     CTAs work on different jobs at the same time.
+// L1 is not coherent inside a kernel, so data written by other CTAs of this launch (residual
+// rows, row sums of squares, partials) is read through L2 (ld.global.cg). Every CTA must be
+// resident together (a CTA can wait for another's tiles): the host sizes the grid to the
+// device's resident CTAs for this instance, and every wait is bounded.
+constexpr int kStreamMaxJobs = 5;
+constexpr int kStreamMaxTiles = 2048;       // 128-row tiles per job (N <= 262144)
+constexpr int kSyncStride = 32;             // ints between the sync counters (128 bytes)
+constexpr size_t kStreamSyncBytes = 1024;   // kStreamMaxJobs + 1 counters
+constexpr int kEpiRope = 100;               // a job's epilogue: the fused q|k|v RoPE + KV write
+static_assert((kStreamMaxJobs + 2) * kSyncStride * sizeof(int) <= kStreamSyncBytes, "sync region");
+constexpr unsigned long long kResidentLimitNs = 100000000ull;  // 100 ms for every CTA to start
 
-// ------------------------------------------------------------------------------------------
-// Layer chain: the GEMMs and small ops between two attention kernels as phases of ONE
-// persistent launch (cooperative: every CTA resident, so grid-wide waits are safe):
-//   o_proj (+residual) -> RMSNorm -> gate|up (SiLU*up) -> down (+residual) [-> tap copy]
-//   -> next layer's RMSNorm -> next q|k|v -> q/k norm + RoPE + paged KV write
-// The per-launch ramp and tail (~6-9 us a GEMM) are paid once per layer. Warp roles are the
-// GEMM's; the producer warp splits in two lanes: lane 0 streams every phase's weight tiles
-// without waiting for anything but free ring slots (so the next projection's weights are in
-// flight while the previous phase finishes), lane 1 issues a GEMM phase's activation loads
-// only once the grid-wide counter of the phase before it is full. The epilogue warps finish
-// the GEMM tiles, run the elementwise phases, and arrive on each phase's counter.
-constexpr int kChainMaxPhases = 10;
-constexpr int kChainMaxGemm = 4;
-enum { kPhGemm = 0, kPhNorm = 1, kPhRope = 2, kPhCopy = 3 };
-// Grid barriers follow GEMM and NORM phases. A barrier may spread its arrivals over kBarSlots
-// counters on separate 128-byte lines (CTA c adds to slot c % kBarSlots; a waiter sums them);
-// one slot measured fastest on B200 (16 slots: polling 16 lines costs more than the contention
-// it removes).
-constexpr int kBarSlots = 1;
-constexpr int kBarStride = 32;  // ints between slots (128 bytes)
-constexpr int kChainMaxBars = kChainMaxPhases;
-constexpr size_t kBarRegion = (((size_t)(kChainMaxBars * kBarSlots + 1) * kBarStride * 4) + 255) & ~(size_t)255;
-
-struct ChainGemm {
-  int N, K, tiles, kb;
+struct SJob {
+  int M, N, K, tiles, kb;
   long long total;
   int epilogue;
+  int wait_prev;  // 1: x (and residual / norm sums) come from the previous job of the launch
+  int ldy, ldr;
   void* y;
-  int ldy;
   const void* residual;
-  int ldr;
-  int* counters;
-  float* partials;
+  unsigned long long* acc64;  // [tiles][M][128] fixed-point accumulators, this job's region
+  int* counters;               // [tiles], this job's region
+  float* ss_out;
+  const float* ss_in;
+  const __nv_bfloat16* norm_w;
+  int ss_tiles, ss_ld;
+  float norm_eps;
+  __half* copy16;
+  int copy16_ld;
+  int* chain_sync;  // (dspark_gemm_opts fields the stream launch does not use)
+  int chain_slot, chain_wait, chain_wait_tiles;
+  RopeEpi rope;
 };
-struct ChainPhase {
-  int kind;
-  int gemm;        // GEMM phases: index into ChainParams::g and ChainMaps
-  int wait_bar;    // grid barrier to acquire before reading inputs (-1: the previous kernel)
-  int arrive_bar;  // grid barrier to arrive on afterwards (-1: none)
-  int local_norm;  // GEMM: NORM phase (run by this CTA) whose output is X (-1: none)
-  // NORM: x (bf16) -> y16 (fp16) ; COPY: x (bf16) -> y16 (fp16), cols = H
-  const __nv_bfloat16* x;
-  int ldx;
-  const __nv_bfloat16* w;
-  int H;
-  float eps;
-  __half* y16;
-  int ldy16;
-  // ROPE
-  const __nv_bfloat16* qkv;
-  int ldqkv, T, Hq, Hkv, hd;
-  const __nv_bfloat16* qnw;
-  const __nv_bfloat16* knw;
-  const float* inv_freq;
-  const int32_t* pos0;
-  __nv_bfloat16* q_out;
-  dspark_kv_layout kv;
-};
-struct ChainParams {
-  int M, nphases, ngemm;
-  ChainPhase ph[kChainMaxPhases];
-  ChainGemm g[kChainMaxGemm];
-  int* bars;  // one arrival counter per phase, then a done counter
+struct StreamParams {
+  int njobs;
+  SJob job[kStreamMaxJobs];
+  int* sync;    // job j's finished tiles at sync[j * kSyncStride]; exited CTAs at
+                // sync[kStreamMaxJobs * kSyncStride]; started CTAs one stride further
   int* status;
 };
-struct ChainMaps {
-  CUtensorMap w[kChainMaxGemm], sb[kChainMaxGemm], x[kChainMaxGemm];
+struct StreamMaps {
+  CUtensorMap w[kStreamMaxJobs], sb[kStreamMaxJobs], x[kStreamMaxJobs];
 };
 
-__device__ __forceinline__ int bar_count(const int* bar) {
-  int sum = 0;
-#pragma unroll
-  for (int k = 0; k < kBarSlots; ++k) {
-    int v;
-    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(bar + k * kBarStride) : "memory");
-    sum += v;
-  }
-  return sum;
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
 }
-__device__ __forceinline__ bool grid_wait(const int* bar, int target, volatile int* abort_flag,
-                                          int* status) {
-  if (bar_count(bar) >= target) return true;
-  const unsigned long long t0 = globaltimer_ns();
-  while (true) {
-    __nanosleep(32);
-    if (bar_count(bar) >= target) return true;
-    if (*abort_flag) return false;
-    if (globaltimer_ns() - t0 > kSpinLimitNs) {
-      *abort_flag = 1;
-      report_error(status, DSPARK_ERR_TIMEOUT);
-      return false;
-    }
-  }
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
-__device__ __forceinline__ void grid_arrive(int* bar) {
-  int* slot = bar + (int)(blockIdx.x % kBarSlots) * kBarStride;
-  asm volatile("fence.acq_rel.gpu;\n\tred.release.gpu.global.add.s32 [%0], 1;" ::"l"(slot) : "memory");
+__device__ __forceinline__ void red_release_gpu_add(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(kThreads, (BN <= 32 ? 2 : 1))
-    chain_kernel(const __grid_constant__ ChainMaps maps, const __grid_constant__ ChainParams p) {
+    w8_stream_kernel(const __grid_constant__ StreamMaps maps, const __grid_constant__ StreamParams sp) {
   using L = Smem<BN, STAGES>;
+  constexpr bool kTwoPerSm = BN <= 32;
+  constexpr int AB = kTwoPerSm ? 3 : 6;
+  constexpr uint32_t ACCS = BN <= 32 ? 32u : 64u;
+  constexpr uint32_t ACC0 = (uint32_t)AB * 64u;
+  constexpr uint32_t TC = kTwoPerSm ? 256u : 512u;
+  static_assert(ACC0 + 2 * ACCS <= TC, "TMEM layout");
+  static_assert(3 * STAGES + 2 * AB + 8 <= (int)(L::kBarBytes / 8), "barrier region");
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -1024,22 +966,22 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 ? 2 : 1))
   auto xfull = [&](int s) { return smem_u32(bars + STAGES + s); };
   auto empty = [&](int s) { return smem_u32(bars + 2 * STAGES + s); };
   auto afull = [&](int a) { return smem_u32(bars + 3 * STAGES + a); };
-  auto aempty = [&](int a) { return smem_u32(bars + 3 * STAGES + kABufs + a); };
-  auto accfull = [&](int b) { return smem_u32(bars + 3 * STAGES + 2 * kABufs + b); };
-  auto accempty = [&](int b) { return smem_u32(bars + 3 * STAGES + 2 * kABufs + 2 + b); };
-  const uint32_t done_bar = smem_u32(bars + 3 * STAGES + 2 * kABufs + 4);
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 3 * STAGES + 2 * kABufs + 5);
+  auto aempty = [&](int a) { return smem_u32(bars + 3 * STAGES + AB + a); };
+  auto accfull = [&](int b) { return smem_u32(bars + 3 * STAGES + 2 * AB + b); };
+  auto accempty = [&](int b) { return smem_u32(bars + 3 * STAGES + 2 * AB + 2 + b); };
+  const uint32_t done_bar = smem_u32(bars + 3 * STAGES + 2 * AB + 4);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 3 * STAGES + 2 * AB + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_holder + 2);
+  volatile int* epi_flag = reinterpret_cast<volatile int*>(tmem_holder + 3);
+  // this CTA's stream-K range of every job, and the running unit index where each job starts
+  __shared__ long long s_st[kStreamMaxJobs], s_en[kStreamMaxJobs];
+  __shared__ int s_u0[kStreamMaxJobs + 1];
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const int nj = sp.njobs;
   const long long G = gridDim.x;
-  const int Gi = (int)gridDim.x;
-  // NORM phases run redundantly in every CTA; this CTA's activation producer waits for its
-  // own epilogue warps to finish the rows (one use per launch: parity 0)
-  __shared__ uint64_t local_done[kChainMaxPhases];
-  auto bar_at = [&](int b) { return p.bars + b * kBarSlots * kBarStride; };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -1047,7 +989,7 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 ? 2 : 1))
       mbar_init(xfull(s), 1);
       mbar_init(empty(s), kConvWarps + 1);
     }
-    for (int a = 0; a < kABufs; ++a) {
+    for (int a = 0; a < AB; ++a) {
       mbar_init(afull(a), kConvWarps);
       mbar_init(aempty(a), 1);
     }
@@ -1056,21 +998,37 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 ? 2 : 1))
       mbar_init(accempty(b), kEpiWarps);
     }
     mbar_init(done_bar, 1);
-    for (int q = 0; q < kChainMaxPhases; ++q) mbar_init(smem_u32(&local_done[q]), 1);
     *abort_flag = 0;
     *last_flag = 0;
+    // a job of fewer units than CTAs spreads over its first `total` CTAs only, so that every
+    // CTA in a tile's contributor range owns at least one of its units
+    int u = 0;
+    for (int j = 0; j < nj; ++j) {
+      const long long tot = sp.job[j].total;
+      const long long Gj = tot < G ? tot : G;
+      long long st = 0, en = 0;
+      if ((long long)blockIdx.x < Gj) {
+        st = range_start(blockIdx.x, tot, Gj);
+        en = range_start(blockIdx.x + 1, tot, Gj);
+      }
+      s_st[j] = st;
+      s_en[j] = en;
+      s_u0[j] = u;
+      u += (int)(en - st);
+    }
+    s_u0[nj] = u;
     fence_mbar_init();
   }
   if (warp == kProducerWarp) {
     if (lane == 0) {
-      for (int j = 0; j < p.ngemm; ++j) {
+      for (int j = 0; j < nj; ++j) {
         tma_prefetch_desc(&maps.w[j]);
         tma_prefetch_desc(&maps.sb[j]);
         tma_prefetch_desc(&maps.x[j]);
       }
     }
     __syncwarp();
-    tmem_alloc(smem_u32(tmem_holder), kTmemCols);
+    tmem_alloc(smem_u32(tmem_holder), TC);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -1078,153 +1036,193 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 ? 2 : 1))
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
   pdl_launch_dependents();
-
-  // A GEMM phase spreads over Gj = min(G, units) CTAs, so every CTA that owns a range owns at
-  // least one unit (the stream-K fixup counts contributors by range); the rest sit it out.
-  auto phase_range = [&](const ChainGemm& gj, long long& st, long long& en) {
-    const long long Gj = gj.total < G ? gj.total : G;
-    if ((long long)blockIdx.x < Gj) {
-      st = range_start(blockIdx.x, gj.total, Gj);
-      en = range_start(blockIdx.x + 1, gj.total, Gj);
-    } else {
-      st = en = 0;
-    }
-  };
-  // total units of this CTA over all GEMM phases (phase order)
-  int n_units = 0;
-  for (int j = 0; j < p.ngemm; ++j) {
-    long long st, en;
-    phase_range(p.g[j], st, en);
-    n_units += (int)(en - st);
-  }
+  const int n_units = s_u0[nj];
+  // CTAs that have started, counted once the previous kernel is complete (the previous stream
+  // launch on this workspace resets the counter as its last CTA leaves, which may be after
+  // this launch's CTAs begin)
+  int* started = sp.sync + (kStreamMaxJobs + 1) * kSyncStride;
 
   if (warp == kProducerWarp) {
-    if (lane == 0) {
-      // weights and (scale, bias): depend on nothing, streamed through every phase
+    if (lane == 0 && n_units > 0) {
       const uint64_t pol_w = policy_evict_first();
-      int u = 0;
-      bool ok = true;
-      for (int j = 0; j < p.ngemm && ok; ++j) {
-        const ChainGemm& gj = p.g[j];
-        long long st, en;
-        phase_range(gj, st, en);
-        for (long long g = st; g < en; ++g, ++u) {
-          const int s = u % STAGES;
-          const uint32_t ph = (uint32_t)(u / STAGES) & 1u;
-          if (u >= STAGES && !mbar_wait(empty(s), ph ^ 1u, abort_flag, p.status)) { ok = false; break; }
-          const int tile = (int)(g / gj.kb), kb = (int)(g % gj.kb);
-          mbar_arrive_expect_tx(full(s), kWBytes + kSBBytes);
-          tma_load_2d(w_s + s * kWBytes, &maps.w[j], full(s), kb * BK, tile * BM, pol_w);
-          tma_load_2d(sb_s + s * kSBBytes, &maps.sb[j], full(s), tile * BM, kb * 2, pol_w);
-        }
-      }
-      const int issued = u;
-      const int first = issued > STAGES ? issued - STAGES : 0;
-      for (int i = first; i < issued; ++i) {
-        volatile int never = 0;
-        mbar_wait(full(i % STAGES), (uint32_t)(i / STAGES) & 1u, &never, p.status);
-      }
-    } else if (lane == 1) {
-      // activations: a GEMM phase's X is complete once the counter of the phase before it is
-      // full (the first phase's X comes from the previous kernel)
       const uint64_t pol_x = policy_evict_last();
-      int u = 0;
-      bool ok = true;
-      for (int q = 0; q < p.nphases && ok; ++q) {
-        if (p.ph[q].kind != kPhGemm) continue;
-        const int j = p.ph[q].gemm;
-        const ChainGemm& gj = p.g[j];
-        long long st, en;
-        phase_range(gj, st, en);
-        if (st == en) continue;
-        if (p.ph[q].wait_bar < 0) pdl_wait();
-        else if (!grid_wait(bar_at(p.ph[q].wait_bar), Gi, abort_flag, p.status)) { ok = false; break; }
-        if (p.ph[q].local_norm >= 0 &&
-            !mbar_wait(smem_u32(&local_done[p.ph[q].local_norm]), 0, abort_flag, p.status)) { ok = false; break; }
-        // the phase before wrote X with generic stores; these loads go through the async proxy
-        asm volatile("fence.proxy.async.global;" ::: "memory");
-        for (long long g = st; g < en; ++g, ++u) {
-          const int s = u % STAGES;
-          const uint32_t ph = (uint32_t)(u / STAGES) & 1u;
-          if (u >= STAGES && !mbar_wait(empty(s), ph ^ 1u, abort_flag, p.status)) { ok = false; break; }
-          const int kb = (int)(g % gj.kb);
-          mbar_arrive_expect_tx(xfull(s), L::kXBytes);
-          tma_load_2d(x_s + s * L::kXBytes, &maps.x[j], xfull(s), kb * BK, 0, pol_x);
-          tma_load_2d(x_s + s * L::kXBytes + BN * 128, &maps.x[j], xfull(s), kb * BK + 64, 0, pol_x);
+      int wi = 0, xi = 0, wj = 0, xj = 0;
+      bool xready = false, ok = true, resident = false;
+      unsigned long long idle_since = 0;
+      while (ok && xi < n_units) {
+        // weights: depend on nothing, so they run ahead across job boundaries, up to the ring
+        // (a slot frees only once the activations of its previous unit were consumed). With no
+        // activation load left to issue, wait for the slot on the barrier itself (the thread
+        // resumes as soon as it completes); otherwise only test it.
+        while (wi < n_units && wi < xi + STAGES) {
+          const int s = wi % STAGES;
+          if (wi >= STAGES) {
+            const uint32_t par = ((uint32_t)(wi / STAGES) & 1u) ^ 1u;
+            if (xi == wi) {
+              if (!mbar_wait(empty(s), par, abort_flag, sp.status)) {
+                ok = false;
+                break;
+              }
+            } else if (!mbar_test(empty(s), par)) {
+              break;
+            }
+          }
+          while (wi >= s_u0[wj + 1]) ++wj;
+          const SJob& J = sp.job[wj];
+          const long long g = s_st[wj] + (wi - s_u0[wj]);
+          const int tile = (int)(g / J.kb), kb = (int)(g % J.kb);
+          mbar_arrive_expect_tx(full(s), kWBytes + kSBBytes);
+          tma_load_2d(w_s + s * kWBytes, &maps.w[wj], full(s), kb * BK, tile * BM, pol_w);
+          tma_load_2d(sb_s + s * kSBBytes, &maps.sb[wj], full(s), tile * BM, kb * 2, pol_w);
+          ++wi;
         }
+        if (!ok) break;
+        // activations of the units whose weights are issued (their slots are free), once the
+        // job's input is complete
+        bool blocked = false;
+        while (xi < wi) {
+          while (xi >= s_u0[xj + 1]) {
+            ++xj;
+            xready = false;
+          }
+          const SJob& J = sp.job[xj];
+          if (!xready) {
+            if (!J.wait_prev) {
+              pdl_wait();
+              xready = true;
+            } else {
+              // a CTA that waits for other CTAs' tiles needs every CTA resident; if some never
+              // start, say so rather than wait on work nobody runs
+              if (!resident) {
+                const unsigned long long t0 = globaltimer_ns();
+                while (ld_acquire_gpu(started) < (int)gridDim.x) {
+                  if (*abort_flag || globaltimer_ns() - t0 > kResidentLimitNs) {
+                    *abort_flag = 1;
+                    report_error(sp.status, DSPARK_ERR_UNSUPPORTED);
+                    break;
+                  }
+                  __nanosleep(64);
+                }
+                if (*abort_flag) {
+                  ok = false;
+                  break;
+                }
+                resident = true;
+              }
+              xready = ld_acquire_gpu(sp.sync + (xj - 1) * kSyncStride) >= sp.job[xj - 1].tiles;
+            }
+            // written with generic stores by other CTAs; read here through the async proxy
+            if (xready) fence_proxy_async_global();
+          }
+          if (!xready) {
+            blocked = true;
+            break;
+          }
+          const int s = xi % STAGES;
+          const long long g = s_st[xj] + (xi - s_u0[xj]);
+          const int kb = (int)(g % J.kb);
+          mbar_arrive_expect_tx(xfull(s), L::kXBytes);
+          tma_load_2d(x_s + s * L::kXBytes, &maps.x[xj], xfull(s), kb * BK, 0, pol_x);
+          tma_load_2d(x_s + s * L::kXBytes + BN * 128, &maps.x[xj], xfull(s), kb * BK + 64, 0,
+                      pol_x);
+          ++xi;
+        }
+        if (!ok) break;
+        if (!blocked) {
+          idle_since = 0;
+          continue;
+        }
+        // waiting for the previous job to finish: poll its counter, bounded
+        if (*abort_flag) break;
+        const unsigned long long now = globaltimer_ns();
+        if (idle_since == 0) {
+          idle_since = now;
+        } else if (now - idle_since > kSpinLimitNs) {
+          *abort_flag = 1;
+          report_error(sp.status, DSPARK_ERR_TIMEOUT);
+          break;
+        }
+        __nanosleep(32);
       }
-      const int issued = u;
-      const int first = issued > STAGES ? issued - STAGES : 0;
-      for (int i = first; i < issued; ++i) {
-        volatile int never = 0;
-        mbar_wait(xfull(i % STAGES), (uint32_t)(i / STAGES) & 1u, &never, p.status);
-      }
+      // drain: no bulk copy may still be writing into this CTA's shared memory at exit
+      volatile int never = 0;
+      for (int i = (wi > STAGES ? wi - STAGES : 0); i < wi; ++i)
+        mbar_wait(full(i % STAGES), (uint32_t)(i / STAGES) & 1u, &never, sp.status);
+      for (int i = (xi > STAGES ? xi - STAGES : 0); i < xi; ++i)
+        mbar_wait(xfull(i % STAGES), (uint32_t)(i / STAGES) & 1u, &never, sp.status);
     }
   } else if (warp == kMmaWarp) {
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_f16(BM, BN);
-      int seg = 0, u = 0;
-      bool ok = true;
-      for (int j = 0; j < p.ngemm && ok; ++j) {
-        const ChainGemm& gj = p.g[j];
-        long long st, en;
-        phase_range(gj, st, en);
-        for (long long g = st; g < en; ++g, ++u) {
-          const int kb = (int)(g % gj.kb);
-          const bool seg_first = (g == st) || (kb == 0);
-          const bool seg_last = (g == en - 1) || (kb == gj.kb - 1);
-          const int s = u % STAGES;
-          const uint32_t ph = (uint32_t)(u / STAGES) & 1u;
-          const int a = u % kABufs;
-          const uint32_t aph = (uint32_t)(u / kABufs) & 1u;
-          const int ab = seg & 1;
-          const uint32_t abph = (uint32_t)(seg >> 1) & 1u;
-          if (seg_first && !mbar_wait(accempty(ab), abph ^ 1u, abort_flag, p.status)) { ok = false; break; }
-          if (!mbar_wait(afull(a), aph, abort_flag, p.status)) { ok = false; break; }
-          if (!mbar_wait(xfull(s), ph, abort_flag, p.status)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t d_tmem = tmem_base + 128u + (uint32_t)ab * 64u;
+      int seg = 0, j = 0;
+      for (int u = 0; u < n_units; ++u) {
+        while (u >= s_u0[j + 1]) ++j;
+        const SJob& J = sp.job[j];
+        const long long g = s_st[j] + (u - s_u0[j]);
+        const int kb = (int)(g % J.kb);
+        const bool seg_first = (u == s_u0[j]) || (kb == 0);
+        const bool seg_last = (u == s_u0[j + 1] - 1) || (kb == J.kb - 1);
+        const int s = u % STAGES;
+        const uint32_t ph = (uint32_t)(u / STAGES) & 1u;
+        const int a = u % AB;
+        const uint32_t aph = (uint32_t)(u / AB) & 1u;
+        const int ab = seg & 1;
+        const uint32_t abph = (uint32_t)(seg >> 1) & 1u;
+        if (seg_first && !mbar_wait(accempty(ab), abph ^ 1u, abort_flag, sp.status)) break;
+        if (!mbar_wait(afull(a), aph, abort_flag, sp.status)) break;
+        if (!mbar_wait(xfull(s), ph, abort_flag, sp.status)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + ACC0 + (uint32_t)ab * ACCS;
 #pragma unroll
-          for (int jj = 0; jj < BK / 16; ++jj) {
-            const uint32_t a_tmem = tmem_base + (uint32_t)a * 64u + (uint32_t)jj * 8u;
-            const uint32_t b_addr = x_s + s * L::kXBytes + (jj >> 2) * (BN * 128) + (jj & 3) * 32;
-            tc_mma_ts(d_tmem, a_tmem, umma_desc_sw128_kmajor(b_addr), idesc,
-                      (seg_first && jj == 0) ? 0u : 1u);
-          }
-          tc_commit(empty(s));
-          tc_commit(aempty(a));
-          if (seg_last) {
-            tc_commit(accfull(ab));
-            ++seg;
-          }
+        for (int jj = 0; jj < BK / 16; ++jj) {
+          const uint32_t a_tmem = tmem_base + (uint32_t)a * 64u + (uint32_t)jj * 8u;
+          const uint32_t b_addr = x_s + s * L::kXBytes + (jj >> 2) * (BN * 128) + (jj & 3) * 32;
+          tc_mma_ts(d_tmem, a_tmem, umma_desc_sw128_kmajor(b_addr), idesc,
+                    (seg_first && jj == 0) ? 0u : 1u);
+        }
+        tc_commit(empty(s));
+        tc_commit(aempty(a));
+        if (seg_last) {
+          tc_commit(accfull(ab));
+          ++seg;
         }
       }
+      // every MMA issued above has finished before TMEM is released
       tc_commit(done_bar);
       volatile int never = 0;
-      mbar_wait(done_bar, 0, &never, p.status);
+      mbar_wait(done_bar, 0, &never, sp.status);
     }
   } else if (warp < kConvWarps) {
+    // converters: thread r owns weight row r of the tile == TMEM lane r
     const int r = threadIdx.x;
     const uint32_t lane_base = tmem_base + ((uint32_t)(warp * 32) << 16);
-    const uint32_t k1024 = 0x64006400u;
-    for (int i = 0; i < n_units; ++i) {
-      const int s = i % STAGES;
-      const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
-      const int a = i % kABufs;
-      const uint32_t aph = (uint32_t)(i / kABufs) & 1u;
-      if (!mbar_wait(full(s), ph, abort_flag, p.status)) break;
-      if (!mbar_wait(aempty(a), aph ^ 1u, abort_flag, p.status)) break;
+    const uint32_t k1024 = 0x64006400u;  // fp16x2 {1024, 1024}
+    float rn[BN / 16];
+#pragma unroll
+    for (int kk = 0; kk < BN / 16; ++kk) rn[kk] = 0.0f;
+    int j = 0;
+    for (int u = 0; u < n_units; ++u) {
+      while (u >= s_u0[j + 1]) ++j;
+      const SJob& J = sp.job[j];
+      const int s = u % STAGES;
+      const uint32_t ph = (uint32_t)(u / STAGES) & 1u;
+      const int a = u % AB;
+      const uint32_t aph = (uint32_t)(u / AB) & 1u;
+      // the lanes of a warp leave together if a wait gives up (the warp syncs below)
+      bool wok = mbar_wait(full(s), ph, abort_flag, sp.status);
+      wok = wok && mbar_wait(aempty(a), aph ^ 1u, abort_flag, sp.status);
+      if (!__all_sync(0xffffffffu, wok)) break;
       tc_fence_after();
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         uint32_t sbv;
         asm volatile("ld.shared.b32 %0, [%1];" : "=r"(sbv) : "r"(sb_s + s * kSBBytes + (h * BM + r) * 4));
-        const uint32_t sc2 = __byte_perm(sbv, 0, 0x1010);
-        const uint32_t bi2 = __byte_perm(sbv, 0, 0x3232);
+        const uint32_t sc2 = __byte_perm(sbv, 0, 0x1010);  // {scale, scale}
+        const uint32_t bi2 = __byte_perm(sbv, 0, 0x3232);  // {bias, bias}
         uint32_t out[32];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int chunk = h * 4 + j;
+        for (int c4 = 0; c4 < 4; ++c4) {
+          const int chunk = h * 4 + c4;
           const uint32_t addr = w_s + s * kWBytes + r * 128 + ((chunk ^ (r & 7)) << 4);
           uint32_t v0, v1, v2, v3;
           asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
@@ -1240,11 +1238,69 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 ? 2 : 1))
               qh = __hsub2(qh, *reinterpret_cast<const __half2*>(&k1024));
               const __half2 wv = __hfma2(qh, *reinterpret_cast<const __half2*>(&sc2),
                                          *reinterpret_cast<const __half2*>(&bi2));
-              out[j * 8 + w * 2 + hh] = *reinterpret_cast<const uint32_t*>(&wv);
+              out[c4 * 8 + w * 2 + hh] = *reinterpret_cast<const uint32_t*>(&wv);
             }
           }
         }
         tmem_st32(lane_base + (uint32_t)a * 64u + (uint32_t)h * 32u, out);
+      }
+      if (J.norm_w) {
+        // the activations landing means the job's input (and its row sums) is complete
+        if (!__all_sync(0xffffffffu, mbar_wait(xfull(s), ph, abort_flag, sp.status))) {
+          tc_wait_st();  // no TMEM store of this thread may be in flight at teardown
+          break;
+        }
+        if (u == s_u0[j]) {
+          if (!J.wait_prev) pdl_wait();
+#pragma unroll
+          for (int kk = 0; kk < BN / 16; ++kk) {
+            const int m = (r >> 3) + 16 * kk;
+            float sum = 0.0f;
+            if (m < J.M) {
+              const float* row = J.ss_in + (size_t)m * J.ss_ld;
+              int t = 0;
+              if ((J.ss_ld & 3) == 0)
+                for (; t + 4 <= J.ss_tiles; t += 4) {
+                  const float4 q4 = __ldcg(reinterpret_cast<const float4*>(row + t));
+                  sum = (((sum + q4.x) + q4.y) + q4.z) + q4.w;
+                }
+              for (; t < J.ss_tiles; ++t) sum += __ldcg(row + t);
+            }
+            rn[kk] = rsqrtf(__fadd_rn(__fdiv_rn(sum, (float)J.K), J.norm_eps));
+          }
+        }
+        const long long g = s_st[j] + (u - s_u0[j]);
+        const int kb = (int)(g % J.kb);
+        const int c = r & 7;
+#pragma unroll
+        for (int bx = 0; bx < 2; ++bx) {
+          const uint4 wq8 = *reinterpret_cast<const uint4*>(J.norm_w + kb * BK + bx * 64 + c * 8);
+          const __nv_bfloat162* wv = reinterpret_cast<const __nv_bfloat162*>(&wq8);
+#pragma unroll
+          for (int kk = 0; kk < BN / 16; ++kk) {
+            const int m = (r >> 3) + 16 * kk;
+            if (m >= J.M) continue;
+            const uint32_t addr = x_s + s * L::kXBytes + bx * BN * 128 + m * 128 + ((c ^ (m & 7)) << 4);
+            uint32_t v[4];
+            asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
+                         : "r"(addr));
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const float2 hv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v[q]));
+              const float2 wf = __bfloat1622float2(wv[q]);
+              const __nv_bfloat162 xn = __floats2bfloat162_rn(__fmul_rn(__fmul_rn(hv.x, rn[kk]), wf.x), __fmul_rn(__fmul_rn(hv.y, rn[kk]), wf.y));
+              const float2 xf = __bfloat1622float2(xn);
+              const __half2 x16 = __floats2half2_rn(xf.x, xf.y);
+              v[q] = *reinterpret_cast<const uint32_t*>(&x16);
+            }
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v[0]), "r"(v[1]),
+                         "r"(v[2]), "r"(v[3])
+                         : "memory");
+          }
+        }
+        // the MMA reads the tile through the async proxy
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       }
       tc_wait_st();
       tc_fence_before();
@@ -1255,190 +1311,154 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 ? 2 : 1))
       }
     }
   } else if (warp < kConvWarps + kEpiWarps) {
+    // epilogue: thread er owns row er of the tile (TMEM lane er)
     const int er = threadIdx.x - kConvWarps * 32;
     const int quad = warp & 3;
-    const int ew = warp - kConvWarps;  // 0..3
-    pdl_wait();
+    pdl_wait();  // outputs may still be read by the previous kernel
+    if (er == 0) red_release_gpu_add(started, 1);
     int seg = 0;
     bool ok = true;
-    for (int q = 0; q < p.nphases && ok; ++q) {
-      const ChainPhase& P = p.ph[q];
-      if (P.kind == kPhGemm) {
-        if (P.wait_bar >= 0) {
-          // acquire what earlier phases wrote (the residual of down is written by o's epilogue)
-          if (er == 0) *last_flag = grid_wait(bar_at(P.wait_bar), Gi, abort_flag, p.status) ? 1 : 0;
-          asm volatile("bar.sync 1, 128;" ::: "memory");
-          if (!*last_flag) { ok = false; break; }
-          asm volatile("bar.sync 1, 128;" ::: "memory");
-        }
-        const int j = P.gemm;
-        const ChainGemm& gj = p.g[j];
-        Params pp{};
-        pp.M = p.M;
-        pp.epilogue = gj.epilogue;
-        pp.y = gj.y;
-        pp.ldy = gj.ldy;
-        pp.residual = gj.residual;
-        pp.ldr = gj.ldr;
-        const int KB = gj.kb;
-        const long long total = gj.total;
-        const long long Gj = total < G ? total : G;
-        long long start, end;
-        phase_range(gj, start, end);
-        int lseg = 0;
-        long long g = start;
-        while (g < end) {
-          const int tile = (int)(g / KB);
-          const long long tile_lo = (long long)tile * KB;
-          const long long seg_end = (end < tile_lo + KB) ? end : tile_lo + KB;
-          const bool whole = (g == tile_lo) && (seg_end == tile_lo + KB);
-          const int ab = seg & 1;
-          const uint32_t abph = (uint32_t)(seg >> 1) & 1u;
-          if (!mbar_wait(accfull(ab), abph, abort_flag, p.status)) { ok = false; break; }
-          tc_fence_after();
-          float acc[BN];
-#pragma unroll
-          for (int c = 0; c < BN / 16; ++c) {
-            uint32_t rr[16];
-            tmem_ld16(tmem_base + ((uint32_t)(quad * 32) << 16) + 128u + (uint32_t)ab * 64u + (uint32_t)c * 16u, rr);
-            tc_wait_ld();
-#pragma unroll
-            for (int t = 0; t < 16; ++t) acc[c * 16 + t] = __uint_as_float(rr[t]);
-          }
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(accempty(ab));
-          if (whole) {
-            epilogue_store<BN>(pp, tile, er, acc, xch);
-          } else {
-            const int slot = (int)blockIdx.x * 2 + (lseg == 0 ? 0 : 1);
-            float4* part = reinterpret_cast<float4*>(gj.partials + (size_t)slot * BN * BM + er * BN);
-#pragma unroll
-            for (int jj = 0; jj < BN / 4; ++jj)
-              part[jj] = make_float4(acc[4 * jj], acc[4 * jj + 1], acc[4 * jj + 2], acc[4 * jj + 3]);
-            asm volatile("bar.sync 1, 128;" ::: "memory");
-            const long long c_lo = range_owner(tile_lo, total, Gj);
-            const long long c_hi = range_owner(tile_lo + KB - 1, total, Gj);
-            if (er == 0) {
-              const int contributors = (int)(c_hi - c_lo + 1);
-              int old;
-              asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;"
-                           : "=r"(old)
-                           : "l"(gj.counters + tile)
-                           : "memory");
-              *last_flag = (old == contributors - 1) ? 1 : 0;
-            }
-            asm volatile("bar.sync 1, 128;" ::: "memory");
-            if (*last_flag) {
-              float sum[BN];
-#pragma unroll
-              for (int m = 0; m < BN; ++m) sum[m] = 0.0f;
-              for (long long c = c_lo; c <= c_hi; ++c) {
-                const int cj = (range_start(c, total, Gj) >= tile_lo) ? 0 : 1;
-                const float4* cp = reinterpret_cast<const float4*>(
-                    gj.partials + ((size_t)c * 2 + cj) * BN * BM + er * BN);
-#pragma unroll
-                for (int jj = 0; jj < BN / 4; ++jj) {
-                  const float4 t = __ldcg(cp + jj);
-                  sum[4 * jj] += t.x;
-                  sum[4 * jj + 1] += t.y;
-                  sum[4 * jj + 2] += t.z;
-                  sum[4 * jj + 3] += t.w;
-                }
-              }
-              if (er == 0) gj.counters[tile] = 0;
-              epilogue_store<BN>(pp, tile, er, sum, xch);
-            }
-            asm volatile("bar.sync 1, 128;" ::: "memory");
-          }
-          ++seg;
-          ++lseg;
-          g = seg_end;
-        }
-      } else {
-        if (P.wait_bar >= 0) {
-          if (er == 0) *last_flag = grid_wait(bar_at(P.wait_bar), Gi, abort_flag, p.status) ? 1 : 0;
-          asm volatile("bar.sync 1, 128;" ::: "memory");
-          if (!*last_flag) { ok = false; break; }
-        }
-        if (P.kind == kPhNorm) {
-          // rows m = blockIdx.x, blockIdx.x + G, ...: y16 = fp16(bf16(x * rsqrt(mean x^2 + eps) * w))
-          for (int m = blockIdx.x; m < p.M; m += Gi) {
-            const __nv_bfloat16* xr = P.x + (size_t)m * P.ldx;
-            float ss = 0.0f;
-            for (int k = er * 2; k < P.H; k += 256) {
-              const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(xr + k));
-              ss += v.x * v.x + v.y * v.y;
-            }
-            ss = warp_sum(ss);
-            if (lane == 0) xch[ew] = ss;
-            asm volatile("bar.sync 1, 128;" ::: "memory");
-            const float tot = (xch[0] + xch[1]) + (xch[2] + xch[3]);
-            const float rr = rsqrtf(tot / (float)P.H + P.eps);
-            for (int k = er * 2; k < P.H; k += 256) {
-              const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(xr + k));
-              const float2 wv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(P.w + k));
-              const __nv_bfloat162 o = __floats2bfloat162_rn(v.x * rr * wv.x, v.y * rr * wv.y);
-              const float2 of = __bfloat1622float2(o);
-              *reinterpret_cast<__half2*>(P.y16 + (size_t)m * P.ldy16 + k) = __floats2half2_rn(of.x, of.y);
-            }
-            asm volatile("bar.sync 1, 128;" ::: "memory");
-          }
-        } else if (P.kind == kPhCopy) {
-          const long long n2 = (long long)p.M * (P.H / 2);
-          for (long long i = (long long)blockIdx.x * 128 + er; i < n2; i += (long long)Gi * 128) {
-            const int m = (int)(i / (P.H / 2)), k = (int)(i % (P.H / 2)) * 2;
-            const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(P.x + (size_t)m * P.ldx + k));
-            *reinterpret_cast<__half2*>(P.y16 + (size_t)m * P.ldy16 + k) = __floats2half2_rn(v.x, v.y);
-          }
-        } else if (P.kind == kPhRope) {
-          const int nheads = P.Hq + 2 * P.Hkv;
-          const int items = p.M * nheads;
-          for (int it = blockIdx.x * kEpiWarps + ew; it < items; it += Gi * kEpiWarps) {
-            const int m = it / nheads, h = it - m * nheads;
-            const int b = m / P.T, t = m - b * P.T;
-            const int pos = P.pos0[b] + t;
-            if (P.hd == 128)
-              rope_kv_item<4>(P.qkv + (size_t)m * P.ldqkv, P.Hq, P.Hkv, h, P.qnw, P.knw, P.eps,
-                              P.inv_freq, b, pos, P.q_out + (size_t)m * P.Hq * 128, P.kv, lane);
-            else
-              rope_kv_item<2>(P.qkv + (size_t)m * P.ldqkv, P.Hq, P.Hkv, h, P.qnw, P.knw, P.eps,
-                              P.inv_freq, b, pos, P.q_out + (size_t)m * P.Hq * 64, P.kv, lane);
-          }
-        }
-      }
-      // this CTA's share of phase q is written: make it visible to later TMA (async proxy)
-      // reads, then one release arrival per CTA
-      if (P.arrive_bar >= 0) {
-        asm volatile("fence.proxy.async.global;" ::: "memory");
+    for (int j = 0; j < nj && ok; ++j) {
+      const SJob& J = sp.job[j];
+      const long long total = J.total;
+      const long long Gj = total < G ? total : G;
+      const int KB = J.kb;
+      const long long end = s_en[j];
+      int lseg = 0;
+      long long g = s_st[j];
+      while (g < end) {
+        const int tile = (int)(g / KB);
+        const long long tile_lo = (long long)tile * KB;
+        const long long seg_end = (end < tile_lo + KB) ? end : tile_lo + KB;
+        const bool whole = (g == tile_lo) && (seg_end == tile_lo + KB);
+        const int ab = seg & 1;
+        const uint32_t abph = (uint32_t)(seg >> 1) & 1u;
+        // one thread waits and the barrier hands its verdict to all 128, so that every thread
+        // of the epilogue leaves together if the wait gives up
+        if (er == 0) *epi_flag = mbar_wait(accfull(ab), abph, abort_flag, sp.status) ? 1 : 0;
         asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (er == 0) grid_arrive(bar_at(P.arrive_bar));
+        if (!*epi_flag) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        float acc[BN];
+#pragma unroll
+        for (int c = 0; c < BN / 16; ++c) {
+          uint32_t rr[16];
+          tmem_ld16(tmem_base + ((uint32_t)(quad * 32) << 16) + ACC0 + (uint32_t)ab * ACCS +
+                        (uint32_t)c * 16u,
+                    rr);
+          tc_wait_ld();
+#pragma unroll
+          for (int t = 0; t < 16; ++t) acc[c * 16 + t] = __uint_as_float(rr[t]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(accempty(ab));
+
+        bool finished = false;
+        if (whole) {
+          if (J.epilogue == kEpiRope)
+            rope_epilogue<BN>(J, tile, er, acc, xch);
+          else
+            epilogue_store<BN>(J, tile, er, acc, xch);
+          finished = true;
+        } else {
+          // Split tile: each contributor adds its partial into the tile's accumulator as 64-bit
+          // fixed point (2^-32 units) with integer atomics; integer sums do not depend on the
+          // order of arrival, so the result is deterministic, and the last contributor reads
+          // one accumulator block instead of every contributor's partial (one L2 round trip).
+          // Row er, activation row m lives at acc64[(tile * M + m) * 128 + er].
+          unsigned long long* a64 = J.acc64 + (size_t)tile * J.M * BM + er;
+          const bool res_pre = J.epilogue == DSPARK_EPI_RESIDUAL_BF16 && BN <= 16;
+          __nv_bfloat162 rpre[BN <= 16 ? BN / 2 : 1];
+          if constexpr (BN <= 16) {
+            // the residual rows, read before the arrival round trip (only the finisher uses them)
+            if (res_pre) {
+              const __nv_bfloat16* rp = static_cast<const __nv_bfloat16*>(J.residual) + tile * BM + er;
+#pragma unroll
+              for (int q = 0; q < BN / 2; ++q) {
+                const int m = 2 * q;
+                rpre[q].x = m < J.M ? __ldcg(rp + (size_t)m * J.ldr) : __float2bfloat16_rn(0.0f);
+                rpre[q].y = m + 1 < J.M ? __ldcg(rp + (size_t)(m + 1) * J.ldr) : __float2bfloat16_rn(0.0f);
+              }
+            }
+          }
+#pragma unroll
+          for (int m = 0; m < BN; ++m)
+            if (m < J.M)
+              asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(a64 + (size_t)m * BM),
+                           "l"((unsigned long long)__float2ll_rn(acc[m] * 4294967296.0f))
+                           : "memory");
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          const long long c_lo = range_owner(tile_lo, total, Gj);
+          const long long c_hi = range_owner(tile_lo + KB - 1, total, Gj);
+          const int nctr = (int)(c_hi - c_lo + 1);
+          if (er == 0) {
+            // release: the block's atomics (ordered before it by the barrier) are visible to
+            // whoever reads the final count; acquire: the last arriver sees every contribution
+            int old;
+            asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;"
+                         : "=r"(old)
+                         : "l"(J.counters + tile)
+                         : "memory");
+            *last_flag = old == nctr - 1 ? 1 : 0;
+          }
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          if (*last_flag) {
+            float sum[BN];
+            long long v[BN];
+#pragma unroll
+            for (int m = 0; m < BN; ++m)
+              v[m] = m < J.M ? (long long)__ldcg(a64 + (size_t)m * BM) : 0ll;
+#pragma unroll
+            for (int m = 0; m < BN; ++m) {
+              sum[m] = (float)((double)v[m] * 2.3283064365386963e-10);  // 2^-32
+              if (m < J.M) __stcg(a64 + (size_t)m * BM, 0ull);           // ready for the next call
+            }
+            if (er == 0) J.counters[tile] = 0;
+            if (J.epilogue == kEpiRope)
+              rope_epilogue<BN>(J, tile, er, sum, xch);
+            else
+              epilogue_store<BN>(J, tile, er, sum, xch, res_pre ? rpre : nullptr);
+            finished = true;
+          }
+        }
+        // every epilogue thread's stores of the tile precede the job counter's release
+        // (cumulative through the barrier); the reader fences the async proxy before its TMA
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (finished && er == 0) red_release_gpu_add(sp.sync + j * kSyncStride, 1);
+        ++seg;
+        ++lseg;
+        g = seg_end;
       }
     }
   }
 
+  // a role that ran on one lane (producer, MMA issuer) rejoins its warp before the
+  // CTA barrier: the barrier counts whole warps, and TMEM is freed after it
+  __syncwarp();
   tc_fence_before();
   __syncthreads();
   if (warp == kProducerWarp) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, kTmemCols);
+    tmem_dealloc(tmem_base, TC);
   }
-  // every thread of every CTA is past its last grid wait once `done` reaches G: the last CTA
-  // resets the phase counters for the next launch
+  // once every CTA has passed its last wait, the last one to leave resets the job counters
+  // for the next launch on this workspace
   if (threadIdx.x == 0) {
+    int* exited = sp.sync + kStreamMaxJobs * kSyncStride;
     int old;
-    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;"
-                 : "=r"(old)
-                 : "l"(p.bars + kChainMaxBars * kBarSlots * kBarStride)
-                 : "memory");
-    if (old == Gi - 1) {
-      for (int k = 0; k < kChainMaxBars * kBarSlots; ++k) p.bars[k * kBarStride] = 0;
-      p.bars[kChainMaxBars * kBarSlots * kBarStride] = 0;
+    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(exited) : "memory");
+    if (old == (int)gridDim.x - 1) {
+      for (int q = 0; q < kStreamMaxJobs; ++q) sp.sync[q * kSyncStride] = 0;
+      *exited = 0;
+      *started = 0;
       __threadfence();
     }
   }
 }
-
 // ------------------------------------------------------------------------------------------
 // host side
 static int pick_bn(int M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 48 ? 48 : 64; }
@@ -1453,84 +1473,9 @@ template <>
 struct Cfg<48> { static constexpr int kStages = 5; static constexpr int kCtasPerSm = 1; };
 template <>
 struct Cfg<64> { static constexpr int kStages = 5; static constexpr int kCtasPerSm = 1; };
-// stage ring of the cluster split-K form (one CTA per SM)
-template <int BN>
-struct CfgCs { static constexpr int kStages = BN <= 32 ? 8 : 6; };
-
-// Split mode of the small-M GEMM: 0 stream-K for every shape (default), 1 cluster split-K for
-// shapes with few tiles where one wave of clusters fits. Measured on B200 in a chain of C2 verify
-// GEMMs (us per launch, stream-K vs cluster): q|k|v 12.2 vs 17.6, o 12.3 vs 13.1, down 19.0 vs
-// 25.1. The cluster form runs one CTA per SM, and its CTAs cannot start until the previous
-// kernel's CTAs have left their SM, so it loses more at the launch boundary than it saves in the
-// reduction.
-static int g_split_mode = 0;
-
-// Cluster split-K for GEMMs with few 128-row tiles (q|k|v, o, down at Qwen3 widths): every
-// tile's K is cut into c slices of one cluster, so no single CTA sums ~10 partials at the end.
-// The device keeps about one CTA of a cluster kernel per SM resident, so the cluster form runs
-// one CTA per SM with a deeper stage ring (the same bytes in flight per SM as two CTAs of the
-// stream-K form). Candidates: tiles <= SMs / 2, the largest c <= 8 with tiles * c <= SMs, at
-// least 3/5 of the SMs busy; otherwise stream-K.
-static int pick_csplit(int tiles, int kb, int c_max) {
-  if (g_split_mode != 1) return 0;
-  const int sms = sm_count();
-  if (tiles <= 0 || tiles * 2 > sms) return 0;
-  int c = std::min(std::min(c_max, kb), sms / tiles);
-  if (c < 2 || tiles * c * 5 < sms * 3) return 0;
-  return c;
-}
-
 static long long grid_for(long long total, int ctas_per_sm) {
   const long long g = (long long)sm_count() * ctas_per_sm;
   return std::min<long long>(g, total);
-}
-
-// Max active clusters of c CTAs of the cluster-split kernel (cached per c; a failed query is
-// retried on the next call and meanwhile reads as "does not fit"). -1: query failed.
-template <int BN>
-static int max_clusters(int c) {
-  constexpr int S = CfgCs<BN>::kStages;
-  using L = Smem<BN, S>;
-  static int cache[9] = {0};  // max active clusters + 1
-  if (c < 2 || c > 8) return -1;
-  if (cache[c]) return cache[c] - 1;
-  auto kern_cs = w8a16_tc_kernel<BN, S, true, false>;
-  if (cudaFuncSetAttribute(kern_cs, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kTotal) !=
-      cudaSuccess) {
-    cudaGetLastError();
-    return -1;
-  }
-  cudaLaunchConfig_t q = {};
-  q.blockDim = dim3(kThreads);
-  q.dynamicSmemBytes = L::kTotal;
-  q.gridDim = dim3((unsigned)(c * 64));
-  cudaLaunchAttribute qa[1];
-  qa[0].id = cudaLaunchAttributeClusterDimension;
-  qa[0].val.clusterDim.x = (unsigned)c;
-  qa[0].val.clusterDim.y = 1;
-  qa[0].val.clusterDim.z = 1;
-  q.attrs = qa;
-  q.numAttrs = 1;
-  int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, kern_cs, &q) != cudaSuccess) {
-    cudaGetLastError();
-    return -1;
-  }
-  cache[c] = n + 1;
-  return n;
-}
-
-// cluster size for this GEMM: pick_csplit's choice if one wave of its clusters is resident
-// at once, else 0 (stream-K)
-template <int BN>
-static int plan_csplit(int tiles, int kb) {
-  for (int c_max = 8; c_max >= 2;) {
-    const int c = pick_csplit(tiles, kb, c_max);
-    if (c < 2) return 0;
-    if (max_clusters<BN>(c) >= tiles) return c;
-    c_max = c - 1;  // fewer, wider slices
-  }
-  return 0;
 }
 
 template <int BN, bool ROPE = false, bool PEER = false>
@@ -1550,100 +1495,103 @@ static int launch_tc(const void* x, int ldx, const uint8_t* wq, const uint32_t* 
   if ((rc = make_map_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x, (uint64_t)p.K, (uint64_t)p.M,
                         (uint64_t)ldx * 2, 64, BN, CU_TENSOR_MAP_SWIZZLE_128B)))
     return rc;
-  constexpr int SC = CfgCs<BN>::kStages;
-  using LC = Smem<BN, SC>;
-  auto kern = w8a16_tc_kernel<BN, S, false, ROPE, PEER>;
-  auto kern_cs = w8a16_tc_kernel<BN, SC, true, false>;
+  auto kern = w8a16_tc_kernel<BN, S, ROPE, PEER>;
   static bool configured = false;
   if (!configured) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kTotal) !=
             cudaSuccess ||
-        cudaFuncSetAttribute(kern_cs, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)LC::kTotal) !=
-            cudaSuccess)
-      return set_error(DSPARK_ERR_CUDA, "cudaFuncSetAttribute(smem=%u/%u) failed", L::kTotal, LC::kTotal);
+        cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
+      return set_error(DSPARK_ERR_CUDA, "cudaFuncSetAttribute(smem=%u) failed", L::kTotal);
     configured = true;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = L::kTotal;
   cfg.stream = st;
-  cudaLaunchAttribute attr[2];
+  cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  // the fused epilogues (RoPE, row sums of squares) are stream-K only
-  p.csplit = (ROPE || p.ss_out || p.epilogue == DSPARK_EPI_PEER_F32) ? 0 : plan_csplit<BN>(p.tiles, p.kb);
-  long long grid;
-  if (p.csplit > 1) {
-    grid = (long long)p.tiles * p.csplit;
-    cfg.dynamicSmemBytes = LC::kTotal;
-    attr[1].id = cudaLaunchAttributeClusterDimension;
-    attr[1].val.clusterDim.x = (unsigned)p.csplit;
-    attr[1].val.clusterDim.y = 1;
-    attr[1].val.clusterDim.z = 1;
-    cfg.numAttrs = 2;
-  } else {
-    grid = grid_for(p.total, Cfg<BN>::kCtasPerSm);
-  }
-  cfg.gridDim = dim3((unsigned)grid);
-  cudaError_t e = p.csplit > 1 ? cudaLaunchKernelEx(&cfg, kern_cs, tw, tsb, tx, p)
-                               : cudaLaunchKernelEx(&cfg, kern, tw, tsb, tx, p);
+  cfg.gridDim = dim3((unsigned)grid_for(p.total, Cfg<BN>::kCtasPerSm));
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tw, tsb, tx, p);
   if (e != cudaSuccess)
     return set_error(DSPARK_ERR_LAUNCH, "w8a16 tc launch failed: %s", cudaGetErrorString(e));
   note_launch();
   return DSPARK_OK;
 }
 
-// ---- layer chain host side
+// ---- stream (K1s) host side
+// workspace: [sync counters, kStreamSyncBytes] [kStreamMaxJobs x kStreamMaxTiles tile
+// counters] [per job: the fixed-point accumulators of its tiles, tiles x M x 128 x 8 bytes].
+// The counter region has a fixed size, so launches of different job lists sharing a workspace
+// never place one launch's accumulators over another's counters; every completed launch leaves
+// the counters and the accumulators it touched at zero.
+static size_t stream_acc_bytes(int M, int tiles) {
+  return ((size_t)tiles * M * BM * sizeof(unsigned long long) + 255) & ~(size_t)255;
+}
+static size_t stream_ws(int M, const int* tiles, int n) {
+  size_t b = kStreamSyncBytes + (size_t)kStreamMaxJobs * kStreamMaxTiles * sizeof(int);
+  for (int j = 0; j < n; ++j) b += stream_acc_bytes(M, tiles[j]);
+  return b;
+}
+
+// Stage ring of the stream kernel: one deeper than the single GEMM's at BN 16 (two CTAs of
+// ~113 KB still fit an SM), since the ring is what keeps the next job's weights streaming
+// while the previous job's last tiles finish.
 template <int BN>
-static int launch_chain(const ChainMaps& maps, const ChainParams& p, cudaStream_t st) {
-  constexpr int S = Cfg<BN>::kStages;
+struct SCfg { static constexpr int kStages = BN == 16 ? 5 : Cfg<BN>::kStages; };
+
+// Every CTA of a stream launch must be resident at once (CTAs wait for each other's tiles).
+// The grid is the single-GEMM kernel's resident grid: two CTAs per SM for BN <= 32 (ten warps
+// and ~92 KB of shared memory each; measured on B200 with per-CTA %smid stamps: all 296 CTAs
+// start within a microsecond, two on every SM; the occupancy query reports one for this
+// shape, so it is not used), one for the wider instances. The kernel checks residency itself:
+// before any wait on another CTA, every CTA must have started (a bounded wait that reports
+// DSPARK_ERR_UNSUPPORTED instead of deadlocking).
+template <int BN>
+static int stream_grid(int* grid) {
+  constexpr int S = SCfg<BN>::kStages;
   using L = Smem<BN, S>;
-  auto kern = chain_kernel<BN, S>;
-  static bool configured = false;
-  if (!configured) {
+  auto kern = w8_stream_kernel<BN, S>;
+  static bool configured[16] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 16) return set_error(DSPARK_ERR_UNSUPPORTED, "w8a16_stream: device %d", dev);
+  if (!configured[dev]) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kTotal) !=
-        cudaSuccess)
-      return set_error(DSPARK_ERR_CUDA, "chain: cudaFuncSetAttribute(smem=%u) failed", L::kTotal);
-    configured = true;
+            cudaSuccess ||
+        cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
+      return set_error(DSPARK_ERR_CUDA, "w8a16_stream: cudaFuncSetAttribute(smem=%u) failed", L::kTotal);
+    configured[dev] = true;
   }
-  int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, L::kTotal) != cudaSuccess ||
-      per_sm < 1)
-    return set_error(DSPARK_ERR_LAUNCH, "chain: no resident CTA fits");
-  const int grid = sm_count() * std::min(per_sm, Cfg<BN>::kCtasPerSm);
+  *grid = sm_count() * Cfg<BN>::kCtasPerSm;
+  return DSPARK_OK;
+}
+
+template <int BN>
+static int launch_stream(const StreamMaps& maps, const StreamParams& p, cudaStream_t st) {
+  constexpr int S = SCfg<BN>::kStages;
+  using L = Smem<BN, S>;
+  auto kern = w8_stream_kernel<BN, S>;
+  int grid = 0;
+  const int rc = stream_grid<BN>(&grid);
+  if (rc) return rc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = L::kTotal;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, maps, p);
-  if (e != cudaSuccess) return set_error(DSPARK_ERR_LAUNCH, "chain launch failed: %s", cudaGetErrorString(e));
+  if (e != cudaSuccess)
+    return set_error(DSPARK_ERR_LAUNCH, "w8a16_stream launch failed: %s", cudaGetErrorString(e));
   note_launch();
   return DSPARK_OK;
-}
-
-static int chain_grid(int M) {
-  const int bn = pick_bn(M);
-  return sm_count() * (bn <= 32 ? 2 : 1);
-}
-
-// workspace: [phase counters + done (256 B)] [stream-K tile counters, a FIXED region of
-// kMaxTiles ints for every phase list] [2 partial regions]. The fixed region keeps one chain's
-// partials from landing where another chain (a different phase list sharing the workspace)
-// keeps its counters.
-static size_t chain_ws(int M, const dspark_chain_phase* ph, int n, size_t* off_part) {
-  (void)ph;
-  (void)n;
-  const size_t part = (size_t)chain_grid(M) * 2 * pick_bn(M) * BM * sizeof(float);
-  if (off_part) *off_part = kBarRegion + kCounterBytes;
-  return kBarRegion + kCounterBytes + 2 * part;
 }
 
 static size_t ws_bytes(int M, int N, int K) {
@@ -1679,6 +1627,56 @@ static int gemm_common_checks(const void* x, int ldx, const uint8_t* wq, const u
   return DSPARK_OK;
 }
 
+// The dspark_gemm_opts fields shared by the single GEMM and the stream jobs: the fp16 tap
+// copy, the row sums of squares out of the epilogue, and the input RMSNorm fused into the
+// converters. T is w8::Params or w8::SJob.
+template <typename T>
+static int apply_opts(T& p, const dspark_gemm_opts& o, int epilogue, int N) {
+  if (o.copy_f16) {
+    if (epilogue != DSPARK_EPI_RESIDUAL_BF16 || o.copy_f16_ld < N)
+      return set_error(DSPARK_ERR_INVALID, "w8a16_gemm: copy_f16 needs RESIDUAL_BF16 and ld >= N");
+    p.copy16 = static_cast<__half*>(o.copy_f16);
+    p.copy16_ld = o.copy_f16_ld;
+  }
+  if (o.row_sumsq) {
+    if (epilogue != DSPARK_EPI_RESIDUAL_BF16 && epilogue != DSPARK_EPI_STORE_BF16)
+      return set_error(DSPARK_ERR_INVALID,
+                       "w8a16_gemm: row_sumsq needs the STORE_BF16 or RESIDUAL_BF16 epilogue");
+    p.ss_out = o.row_sumsq;
+  }
+  if (o.norm_w) {
+    if (!o.norm_sumsq || o.norm_tiles <= 0)
+      return set_error(DSPARK_ERR_INVALID, "w8a16_gemm: norm_w without norm_sumsq / norm_tiles");
+    if (reinterpret_cast<uintptr_t>(o.norm_w) & 15)
+      return set_error(DSPARK_ERR_ALIGN, "w8a16_gemm: norm_w not 16-byte aligned");
+    p.norm_w = static_cast<const __nv_bfloat16*>(o.norm_w);
+    p.ss_in = o.norm_sumsq;
+    p.ss_tiles = o.norm_tiles;
+    p.ss_ld = o.norm_ld > 0 ? o.norm_ld : o.norm_tiles;
+    if (p.ss_ld < o.norm_tiles)
+      return set_error(DSPARK_ERR_INVALID, "w8a16_gemm: norm_ld %d < norm_tiles %d", p.ss_ld,
+                       o.norm_tiles);
+    if ((p.ss_ld & 3) == 0 && (reinterpret_cast<uintptr_t>(o.norm_sumsq) & 15))
+      return set_error(DSPARK_ERR_ALIGN, "w8a16_gemm: norm_sumsq not 16-byte aligned");
+    p.norm_eps = o.norm_eps;
+  }
+  // the struct holds slot + 1 (0: none), so a zero-initialised opts chains nothing
+  const int slot = o.chain_slot - 1, wait = o.chain_wait - 1;
+  p.chain_slot = -1;
+  p.chain_wait = -1;
+  if (slot >= 0 || wait >= 0) {
+    if (!o.chain_sync || slot >= DSPARK_CHAIN_SLOTS || wait >= DSPARK_CHAIN_SLOTS || slot < -1 ||
+        wait < -1 || (wait >= 0 && (o.chain_wait_tiles <= 0 || wait == slot)))
+      return set_error(DSPARK_ERR_INVALID, "w8a16_gemm: bad chain (sync=%p slot=%d wait=%d tiles=%d)",
+                       (void*)o.chain_sync, slot, wait, o.chain_wait_tiles);
+    p.chain_sync = o.chain_sync;
+    p.chain_slot = slot;
+    p.chain_wait = wait;
+    p.chain_wait_tiles = o.chain_wait_tiles;
+  }
+  return DSPARK_OK;
+}
+
 // Shared launch path of the W8 GEMM entry points: rope != nullptr selects the fused q|k|v
 // epilogue (y unused).
 static int gemm_launch(const void* x, int ldx, const uint8_t* wq, const uint32_t* wsb, int M, int N,
@@ -1691,6 +1689,7 @@ static int gemm_launch(const void* x, int ldx, const uint8_t* wq, const uint32_t
   if (!workspace || workspace_bytes < need)
     return set_error(DSPARK_ERR_WORKSPACE, "w8a16_gemm: workspace %zu < %zu bytes", workspace_bytes, need);
   w8::Params p{};
+  p.chain_slot = p.chain_wait = -1;
   p.M = M; p.N = N; p.K = K;
   p.tiles = N / w8::BM;
   p.kb = K / w8::BK;
@@ -1715,34 +1714,8 @@ static int gemm_launch(const void* x, int ldx, const uint8_t* wq, const uint32_t
     p.peer_epoch = peer->epoch;
   }
   if (opts) {
-    if (opts->copy_f16) {
-      if (epilogue != DSPARK_EPI_RESIDUAL_BF16 || opts->copy_f16_ld < N)
-        return set_error(DSPARK_ERR_INVALID, "w8a16_gemm: copy_f16 needs RESIDUAL_BF16 and ld >= N");
-      p.copy16 = static_cast<__half*>(opts->copy_f16);
-      p.copy16_ld = opts->copy_f16_ld;
-    }
-    if (opts->row_sumsq) {
-      if (epilogue != DSPARK_EPI_RESIDUAL_BF16 && epilogue != DSPARK_EPI_STORE_BF16)
-        return set_error(DSPARK_ERR_INVALID,
-                         "w8a16_gemm: row_sumsq needs the STORE_BF16 or RESIDUAL_BF16 epilogue");
-      p.ss_out = opts->row_sumsq;
-    }
-    if (opts->norm_w) {
-      if (!opts->norm_sumsq || opts->norm_tiles <= 0)
-        return set_error(DSPARK_ERR_INVALID, "w8a16_gemm: norm_w without norm_sumsq / norm_tiles");
-      if (reinterpret_cast<uintptr_t>(opts->norm_w) & 15)
-        return set_error(DSPARK_ERR_ALIGN, "w8a16_gemm: norm_w not 16-byte aligned");
-      p.norm_w = static_cast<const __nv_bfloat16*>(opts->norm_w);
-      p.ss_in = opts->norm_sumsq;
-      p.ss_tiles = opts->norm_tiles;
-      p.ss_ld = opts->norm_ld > 0 ? opts->norm_ld : opts->norm_tiles;
-      if (p.ss_ld < opts->norm_tiles)
-        return set_error(DSPARK_ERR_INVALID, "w8a16_gemm: norm_ld %d < norm_tiles %d", p.ss_ld,
-                         opts->norm_tiles);
-      if ((p.ss_ld & 3) == 0 && (reinterpret_cast<uintptr_t>(opts->norm_sumsq) & 15))
-        return set_error(DSPARK_ERR_ALIGN, "w8a16_gemm: norm_sumsq not 16-byte aligned");
-      p.norm_eps = opts->norm_eps;
-    }
+    const int rc = apply_opts(p, *opts, epilogue, N);
+    if (rc) return rc;
   }
   const void* pf[2] = {pf0, pf1};
   const size_t pfb[2] = {pf0_bytes, pf1_bytes};
@@ -1874,162 +1847,161 @@ extern "C" int dspark_w8a16_gemm_peer(const void* x, int ldx, const uint8_t* wq,
                      nullptr, nullptr, status, stream, ar);
 }
 
-extern "C" int dspark_w8a16_gemm_plan(int M, int N, int K, int* grid, int* cluster,
-                                      int* max_active) {
-  using namespace w8;
-  if (M < 1 || M > 64 || N <= 0 || K <= 0 || N % BM || K % BK || !grid || !cluster)
-    return set_error(DSPARK_ERR_INVALID, "w8a16_gemm_plan: bad arguments");
-  const int tiles = N / BM, kb = K / BK;
-  const int bn = pick_bn(M);
-  const int cps = bn <= 32 ? 2 : 1;
-  int c = 0, mc = 0;
-  const int saved = g_split_mode;
-  g_split_mode = 1;
-  const int c0 = pick_csplit(tiles, kb, 8);  // the cluster size mode 1 would try first
-  g_split_mode = saved;
-  switch (bn) {
-    case 16: c = plan_csplit<16>(tiles, kb); mc = max_clusters<16>(c0); break;
-    case 32: c = plan_csplit<32>(tiles, kb); mc = max_clusters<32>(c0); break;
-    case 48: c = plan_csplit<48>(tiles, kb); mc = max_clusters<48>(c0); break;
-    default: c = plan_csplit<64>(tiles, kb); mc = max_clusters<64>(c0); break;
-  }
-  *cluster = c;
-  *grid = c > 1 ? tiles * c : (int)grid_for((long long)tiles * kb, cps);
-  if (max_active) *max_active = mc;
+// The q|k|v RoPE epilogue's arguments, checked as dspark_w8a16_gemm_qkv_rope checks them.
+static int make_rope(w8::RopeEpi* r, int M, int T, int Hq, int Hkv, int hd, const void* q_norm_w,
+                     const void* k_norm_w, float eps, const float* inv_freq, const int32_t* pos0,
+                     void* q_out, const dspark_kv_layout* kv, const char* what) {
+  if (hd != 64 && hd != 128) return set_error(DSPARK_ERR_UNSUPPORTED, "%s: head_dim %d", what, hd);
+  if (T <= 0 || M % T || Hkv <= 0 || Hq < 0 || !k_norm_w || !inv_freq || !pos0 || !kv ||
+      !kv->pool || !kv->block_table || (Hq > 0 && (!q_out || !q_norm_w)))
+    return set_error(DSPARK_ERR_INVALID, "%s: bad RoPE arguments", what);
+  if (kv->head_dim != hd || kv->num_kv_heads != Hkv || kv->page_size <= 0 ||
+      kv->page_bytes != dspark_kv_page_bytes(kv->page_size, Hkv, hd, kv->kv8))
+    return set_error(DSPARK_ERR_INVALID, "%s: kv layout does not match", what);
+  r->qnw = static_cast<const __nv_bfloat16*>(q_norm_w);
+  r->knw = static_cast<const __nv_bfloat16*>(k_norm_w);
+  r->inv_freq = inv_freq;
+  r->pos0 = pos0;
+  r->q_out = static_cast<__nv_bfloat16*>(q_out);
+  r->kv = *kv;
+  r->eps = eps;
+  r->T = T; r->Hq = Hq; r->Hkv = Hkv; r->hd = hd;
   return DSPARK_OK;
 }
 
-extern "C" int dspark_w8a16_gemm_split_mode(int mode) {
-  if (mode < 0 || mode > 1) return set_error(DSPARK_ERR_INVALID, "w8a16_gemm_split_mode: %d", mode);
-  w8::g_split_mode = mode;
-  return DSPARK_OK;
+extern "C" size_t dspark_stream_job_size(void) { return sizeof(dspark_stream_job); }
+
+// tiles of a job as the launch sees it (0 for a malformed job: the launch rejects it)
+static int stream_job_tiles(const dspark_stream_job& q) {
+  const int N = q.epilogue == DSPARK_EPI_QKV_ROPE ? (q.Hq + 2 * q.Hkv) * q.hd : q.N;
+  return N > 0 && N % 128 == 0 ? N / 128 : 0;
 }
 
-extern "C" size_t dspark_chain_phase_size(void) { return sizeof(dspark_chain_phase); }
-
-extern "C" size_t dspark_chain_workspace_bytes(int M, const dspark_chain_phase* phases, int n) {
-  if (M <= 0 || M > 64 || !phases || n <= 0) return 0;
-  return w8::chain_ws(M, phases, n, nullptr);
+extern "C" size_t dspark_w8a16_stream_workspace_bytes(int M, const dspark_stream_job* jobs,
+                                                      int n_jobs) {
+  if (M < 1 || M > 64 || !jobs || n_jobs < 1 || n_jobs > w8::kStreamMaxJobs) return 0;
+  int tiles[w8::kStreamMaxJobs];
+  for (int j = 0; j < n_jobs; ++j) tiles[j] = stream_job_tiles(jobs[j]);
+  return w8::stream_ws(M, tiles, n_jobs);
 }
 
-extern "C" int dspark_run_chain(int M, const dspark_chain_phase* ph, int n, void* workspace,
-                                size_t workspace_bytes, int* status, dspark_stream_t stream) {
+extern "C" int dspark_w8a16_stream(int M, const dspark_stream_job* jobs, int n_jobs,
+                                   void* workspace, size_t workspace_bytes, int* status,
+                                   dspark_stream_t stream) {
   using namespace w8;
-  if (!ph || n <= 0 || n > kChainMaxPhases) return set_error(DSPARK_ERR_INVALID, "chain: %d phases", n);
-  if (M < 1 || M > 64) return set_error(DSPARK_ERR_INVALID, "chain: M=%d not in [1,64]", M);
-  size_t off_part = 0;
-  const size_t need = chain_ws(M, ph, n, &off_part);
+  if (!jobs || n_jobs < 1 || n_jobs > kStreamMaxJobs)
+    return set_error(DSPARK_ERR_INVALID, "w8a16_stream: %d jobs (1..%d)", n_jobs, kStreamMaxJobs);
+  if (M < 1 || M > 64) return set_error(DSPARK_ERR_INVALID, "w8a16_stream: M=%d not in [1,64]", M);
+  int tiles[kStreamMaxJobs];
+  for (int j = 0; j < n_jobs; ++j) tiles[j] = stream_job_tiles(jobs[j]);
+  const size_t need = stream_ws(M, tiles, n_jobs);
   if (!workspace || workspace_bytes < need)
-    return set_error(DSPARK_ERR_WORKSPACE, "chain: workspace %zu < %zu bytes", workspace_bytes, need);
-  const int BNv = pick_bn(M);
-  {
-    long long tiles = 0;
-    for (int i = 0; i < n; ++i)
-      if (ph[i].kind == DSPARK_PHASE_GEMM) tiles += ph[i].N / BM;
-    if (tiles > kMaxTiles) return set_error(DSPARK_ERR_UNSUPPORTED, "chain: %lld tiles > %d", tiles, kMaxTiles);
-  }
-  ChainMaps maps;
+    return set_error(DSPARK_ERR_WORKSPACE, "w8a16_stream: workspace %zu < %zu bytes", workspace_bytes, need);
+  if (reinterpret_cast<uintptr_t>(workspace) & 255)
+    return set_error(DSPARK_ERR_ALIGN, "w8a16_stream: workspace not 256-byte aligned");
+  StreamMaps maps;
   memset(&maps, 0, sizeof(maps));
-  ChainParams p;
+  StreamParams p;
   memset(&p, 0, sizeof(p));
-  p.M = M;
-  p.nphases = n;
+  p.njobs = n_jobs;
   p.status = status;
   uint8_t* w = static_cast<uint8_t*>(workspace);
-  p.bars = reinterpret_cast<int*>(w);
-  int* counters = reinterpret_cast<int*>(w + kBarRegion);
-  const size_t part_bytes = (size_t)chain_grid(M) * 2 * BNv * BM * sizeof(float);
-  int ng = 0;
-  // dependencies: a grid barrier after every GEMM and NORM phase but the last phase; every
-  // phase reads what was written before the latest barrier
-  int nbar = 0, last_bar = -1;
-  for (int i = 0; i < n; ++i) {
-    const dspark_chain_phase& q = ph[i];
-    ChainPhase& P = p.ph[i];
-    P.kind = q.kind;
-    P.wait_bar = last_bar;
-    P.arrive_bar = -1;
-    P.local_norm = -1;
-    if ((q.kind == DSPARK_PHASE_GEMM || q.kind == DSPARK_PHASE_NORM) && i < n - 1) {
-      P.arrive_bar = nbar++;
-      last_bar = P.arrive_bar;
+  p.sync = reinterpret_cast<int*>(w);
+  int* ctr = reinterpret_cast<int*>(w + kStreamSyncBytes);
+  uint8_t* acc = w + kStreamSyncBytes + (size_t)kStreamMaxJobs * kStreamMaxTiles * sizeof(int);
+  const int BNv = pick_bn(M);
+  for (int j = 0; j < n_jobs; ++j) {
+    const dspark_stream_job& q = jobs[j];
+    const bool rope = q.epilogue == DSPARK_EPI_QKV_ROPE;
+    const int N = rope ? (q.Hq + 2 * q.Hkv) * q.hd : q.N;
+    if (!rope && (q.epilogue < 0 || q.epilogue > 3))
+      return set_error(DSPARK_ERR_INVALID, "w8a16_stream: job %d epilogue %d", j, q.epilogue);
+    int rc = gemm_common_checks(q.x, q.ldx, q.wq, q.wsb, M, N, q.K,
+                                rope ? (q.q_out ? q.q_out : q.kv.pool) : q.y,
+                                rope ? DSPARK_EPI_STORE_BF16 : q.epilogue, q.residual);
+    if (rc) return rc;
+    if (N / BM > kStreamMaxTiles)
+      return set_error(DSPARK_ERR_UNSUPPORTED, "w8a16_stream: job %d has %d tiles (max %d)", j,
+                       N / BM, kStreamMaxTiles);
+    if (j == 0 && q.wait_prev)
+      return set_error(DSPARK_ERR_INVALID, "w8a16_stream: the first job has no previous job");
+    SJob& J = p.job[j];
+    J.M = M; J.N = N; J.K = q.K;
+    J.tiles = N / BM;
+    J.kb = q.K / BK;
+    J.total = (long long)J.tiles * J.kb;
+    J.epilogue = rope ? kEpiRope : q.epilogue;
+    J.wait_prev = q.wait_prev ? 1 : 0;
+    J.y = q.y; J.ldy = q.ldy;
+    J.residual = q.residual; J.ldr = q.ldr;
+    J.counters = ctr + (size_t)j * kStreamMaxTiles;
+    J.acc64 = reinterpret_cast<unsigned long long*>(acc);
+    acc += stream_acc_bytes(M, J.tiles);
+    if ((rc = apply_opts(J, q.opts, rope ? DSPARK_EPI_STORE_BF16 : q.epilogue, N))) return rc;
+    if (rope) {
+      if (q.opts.row_sumsq || q.opts.copy_f16)
+        return set_error(DSPARK_ERR_INVALID, "w8a16_stream: job %d: the RoPE epilogue writes no rows", j);
+      if ((rc = make_rope(&J.rope, M, q.T, q.Hq, q.Hkv, q.hd, q.q_norm_w, q.k_norm_w, q.eps,
+                          q.inv_freq, q.pos0, q.q_out, &q.kv, "w8a16_stream")))
+        return rc;
     }
-    switch (q.kind) {
-      case DSPARK_PHASE_GEMM: {
-        if (ng >= kChainMaxGemm) return set_error(DSPARK_ERR_UNSUPPORTED, "chain: more than %d GEMMs", kChainMaxGemm);
-        int rc = gemm_common_checks(q.x, q.ldx, q.wq, q.wsb, M, q.N, q.K, q.y, q.epilogue, q.residual);
-        if (rc) return rc;
-        ChainGemm& g = p.g[ng];
-        g.N = q.N; g.K = q.K; g.tiles = q.N / BM; g.kb = q.K / BK;
-        g.total = (long long)g.tiles * g.kb;
-        g.epilogue = q.epilogue; g.y = q.y; g.ldy = q.ldy; g.residual = q.residual; g.ldr = q.ldr;
-        g.counters = counters;
-        counters += g.tiles;
-        g.partials = reinterpret_cast<float*>(w + off_part + (size_t)(ng & 1) * part_bytes);
-        if ((rc = make_map_2d(&maps.w[ng], CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, q.wq, (uint64_t)q.K,
-                              (uint64_t)q.N, (uint64_t)q.K, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B)))
-          return rc;
-        if ((rc = make_map_2d(&maps.sb[ng], CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, q.wsb, (uint64_t)q.N,
-                              (uint64_t)(q.K / 64), (uint64_t)q.N * 4, BM, 2, CU_TENSOR_MAP_SWIZZLE_NONE)))
-          return rc;
-        if ((rc = make_map_2d(&maps.x[ng], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, q.x, (uint64_t)q.K,
-                              (uint64_t)M, (uint64_t)q.ldx * 2, 64, BNv, CU_TENSOR_MAP_SWIZZLE_128B)))
-          return rc;
-        P.gemm = ng++;
-        break;
-      }
-      case DSPARK_PHASE_NORM:
-      case DSPARK_PHASE_COPY_F16:
-        if (!q.x || !q.y || q.H <= 0 || q.H % 2 || q.ldx < q.H || q.ldy < q.H || q.ldx % 2 || q.ldy % 2 ||
-            (q.kind == DSPARK_PHASE_NORM && !q.w))
-          return set_error(DSPARK_ERR_INVALID, "chain: bad norm/copy phase %d", i);
-        P.x = static_cast<const __nv_bfloat16*>(q.x); P.ldx = q.ldx;
-        P.w = static_cast<const __nv_bfloat16*>(q.w); P.H = q.H; P.eps = q.eps;
-        P.y16 = static_cast<__half*>(q.y); P.ldy16 = q.ldy;
-        break;
-      case DSPARK_PHASE_ROPE_KV:
-        if (!q.qkv || !q.k_norm || !q.inv_freq || !q.pos0 || (q.Hq > 0 && (!q.q_out || !q.q_norm)) ||
-            (q.hd != 64 && q.hd != 128) || q.T <= 0 || M % q.T || q.kv.head_dim != q.hd ||
-            q.kv.num_kv_heads != q.Hkv || !q.kv.pool || !q.kv.block_table)
-          return set_error(DSPARK_ERR_INVALID, "chain: bad rope phase %d", i);
-        P.qkv = static_cast<const __nv_bfloat16*>(q.qkv); P.ldqkv = q.ldqkv; P.T = q.T;
-        P.Hq = q.Hq; P.Hkv = q.Hkv; P.hd = q.hd;
-        P.qnw = static_cast<const __nv_bfloat16*>(q.q_norm);
-        P.knw = static_cast<const __nv_bfloat16*>(q.k_norm);
-        P.eps = q.eps; P.inv_freq = q.inv_freq; P.pos0 = q.pos0;
-        P.q_out = static_cast<__nv_bfloat16*>(q.q_out); P.kv = q.kv;
-        break;
-      default:
-        return set_error(DSPARK_ERR_INVALID, "chain: phase %d kind %d", i, q.kind);
-    }
+    if ((rc = make_map_2d(&maps.w[j], CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, q.wq, (uint64_t)q.K,
+                          (uint64_t)N, (uint64_t)q.K, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B)))
+      return rc;
+    if ((rc = make_map_2d(&maps.sb[j], CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, q.wsb, (uint64_t)N,
+                          (uint64_t)(q.K / 64), (uint64_t)N * 4, BM, 2, CU_TENSOR_MAP_SWIZZLE_NONE)))
+      return rc;
+    if ((rc = make_map_2d(&maps.x[j], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, q.x, (uint64_t)q.K,
+                          (uint64_t)M, (uint64_t)q.ldx * 2, 64, BNv, CU_TENSOR_MAP_SWIZZLE_128B)))
+      return rc;
   }
-  p.ngemm = ng;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   switch (BNv) {
-    case 16: return launch_chain<16>(maps, p, st);
-    case 32: return launch_chain<32>(maps, p, st);
-    case 48: return launch_chain<48>(maps, p, st);
-    default: return launch_chain<64>(maps, p, st);
+    case 16: return launch_stream<16>(maps, p, st);
+    case 32: return launch_stream<32>(maps, p, st);
+    case 48: return launch_stream<48>(maps, p, st);
+    default: return launch_stream<64>(maps, p, st);
   }
 }
 
-// Diagnostic entry point: the same product on CUDA cores (fp32 dequant, one warp per
-// column). Not used on the serving path.
-extern "C" int dspark_w8a16_gemm_simt(const void* x, int ldx, const uint8_t* wq,
-                                      const uint32_t* wsb, int M, int N, int K, void* y, int ldy,
-                                      const void* residual, int ldr, int epilogue,
-                                      dspark_stream_t stream) {
-  int rc = gemm_common_checks(x, ldx, wq, wsb, M, N, K, y, epilogue, residual);
-  if (rc) return rc;
-  if (epilogue == DSPARK_EPI_SILU_MUL_F16)
-    return set_error(DSPARK_ERR_UNSUPPORTED, "w8a16_gemm_simt: silu-mul epilogue not supported");
-  w8::Params p{};
-  p.M = M; p.N = N; p.K = K;
-  p.ldy = ldy; p.ldr = ldr; p.epilogue = epilogue; p.y = y; p.residual = residual;
-  const int blocks = (N * 32 + 255) / 256;
-  w8::w8a16_simt_kernel<64><<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __half*>(x), ldx, wq, wsb, p);
-  const int lrc = check_launch("w8a16_gemm_simt");
-  if (lrc == DSPARK_OK) note_launch();
-  return lrc;
+extern "C" int dspark_w8a16_stream_grid(int M, int* grid) {
+  using namespace w8;
+  if (M < 1 || M > 64 || !grid) return set_error(DSPARK_ERR_INVALID, "w8a16_stream_grid: bad arguments");
+  switch (pick_bn(M)) {
+    case 16: return stream_grid<16>(grid);
+    case 32: return stream_grid<32>(grid);
+    case 48: return stream_grid<48>(grid);
+    default: return stream_grid<64>(grid);
+  }
+}
+
+// Diagnostic: why a stream instance gets the grid it gets. info[0..7] = grid, resident CTAs per
+// SM by the occupancy query, registers per thread, static shared bytes, dynamic shared bytes
+// requested, dynamic shared bytes available per CTA at two CTAs per SM, max dynamic shared
+// bytes per CTA (attribute), the function's max threads per block.
+extern "C" int dspark_w8a16_stream_info(int M, int* info) {
+  using namespace w8;
+  if (M < 1 || M > 64 || !info) return set_error(DSPARK_ERR_INVALID, "w8a16_stream_info: bad arguments");
+  int grid = 0;
+  int rc;
+  cudaFuncAttributes fa{};
+  size_t avail = 0;
+  int occ = 0;
+  unsigned kt = 0;
+  auto fill = [&](auto kern, unsigned total) {
+    cudaFuncGetAttributes(&fa, kern);
+    cudaOccupancyAvailableDynamicSMemPerBlock(&avail, kern, 2, kThreads);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, total);
+    kt = total;
+  };
+  switch (pick_bn(M)) {
+    case 16: rc = stream_grid<16>(&grid); fill(w8_stream_kernel<16, 5>, Smem<16, 5>::kTotal); break;
+    case 32: rc = stream_grid<32>(&grid); fill(w8_stream_kernel<32, 4>, Smem<32, 4>::kTotal); break;
+    case 48: rc = stream_grid<48>(&grid); fill(w8_stream_kernel<48, 5>, Smem<48, 5>::kTotal); break;
+    default: rc = stream_grid<64>(&grid); fill(w8_stream_kernel<64, 5>, Smem<64, 5>::kTotal); break;
+  }
+  info[0] = grid; info[1] = occ; info[2] = fa.numRegs; info[3] = (int)fa.sharedSizeBytes;
+  info[4] = (int)kt; info[5] = (int)avail; info[6] = fa.maxDynamicSharedSizeBytes;
+  info[7] = fa.maxThreadsPerBlock;
+  return rc;
 }

@@ -78,7 +78,6 @@ struct Cfg {
       1024 + kStages * kStageBytes + kNB * kStgBytes + kXchBytes + kBarBytes;
 };
 
-__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
 __device__ __forceinline__ float lo_f(uint32_t v) { return __uint_as_float(v << 16); }
 __device__ __forceinline__ float hi_f(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
 
@@ -405,7 +404,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               const float a = (j & 1) ? hi_f(own) : lo_f(own);
               const float b2 = (j & 1) ? hi_f(other[j >> 1]) : lo_f(other[j >> 1]);
               const float g = gate ? a : b2, u = gate ? b2 : a;
-              const float sg = bf16_round(silu_f(g));
+              const float sg = bf16_round(silu_rn(g));
               *reinterpret_cast<__half*>(bp + (row0 + j) * 128 + r * 2) =
                   __float2half_rn(bf16_round(sg * u));
             }
@@ -455,6 +454,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
+  // a role that ran on one lane (producer, MMA issuer) rejoins its warp before the CTA
+  // barrier: the barrier counts whole warps, and TMEM is freed after it
+  __syncwarp();
   tc_fence_before();
   __syncthreads();
   if (warp == kProducerWarp) {

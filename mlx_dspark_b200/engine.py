@@ -1,31 +1,38 @@
-"""The serving layer between requests and the decode loops: Engine and BatchEngine.
+"""Serving on the device: Engine (one request at a time), BatchEngine (continuous batching on
+one GPU) and ReplicaPool (request-parallel serving over several GPUs).
 
-Drop-in for the scheduling half of src/mlx_dspark/server.py (Engine 75-365, BatchEngine
-381-608, maybe_batch_engine 611-622); the HTTP handler, CLI and request parsing are out of scope.
+The reference's serving layer (src/mlx_dspark/server.py:75-622) schedules one MLX device from
+an HTTP server; the HTTP handler, CLI and request parsing stay out of scope here. What is kept
+is the interface: Engine(target, tokenizer, drafter, mode=...).generate(...) -> GenResult with
+the same prefix-reuse rules (acquire before, store after, reset on any error), the same
+per-mode decode loops, the cumulative stats behind /metrics, and the `x_mlx_dspark` block;
+BatchEngine and maybe_batch_engine wrap an Engine the same way.
 
-Engine runs every request on one worker thread (one CUDA stream, one set of captured graphs),
-reuses a stored conversation prefix through PrefixCache (acquire before, store after; reset on
-any error), dispatches by mode (dspark / dflash / lookup / baseline) and keeps the cumulative
-stats that /metrics and the `x_mlx_dspark` block report.
-
-BatchEngine puts a scheduler loop on that same thread. Requests queue up, the loop gathers
-them for a short window (20 ms), groups them by sampling parameters, and:
-  - penalties or logprobs: serial (the batched round applies neither);
-  - a lone request, or a dspark group with temperature > 0: serial;
-  - a greedy dspark group: one continuous SpecSlots session - a finished row is delivered at
-    once and its slot admits the next queued or newly arriving greedy request; an arrival that
-    cannot join (sampled, penalised, too long) stops admissions and runs after the session;
-  - a greedy baseline group: the static batched baseline.
+How work reaches the GPU is this build's own:
+  * Engine owns one device thread (a single-worker executor): every launch, captured graph and
+    cache of a GPU is touched from that thread only.
+  * BatchEngine turns that thread into a loop over a slot table that lives as long as the
+    engine (its page pools and captured round graphs are made once). A request is classified
+    once, when submitted: a greedy request that fits a slot joins the admission queue, any
+    other request (sampled, penalised, logprobs, too long) the solo queue. Each pass of the
+    loop admits queued requests into free slots (a prefill that maps stored prefix pages),
+    runs one speculative round over the active rows and hands finished rows back at once; solo
+    requests run alone when the table is empty. A solo request that has waited longer than
+    solo_wait_s pauses admissions so the table drains and it gets the GPU.
+  * ReplicaPool runs one worker process per GPU, each with its own model replica and
+    BatchEngine, and no collective between them. The host sends each request to the replica
+    with the least outstanding work (prompt plus max new tokens of its unfinished requests).
 Stop strings and streaming callbacks are not built: requests that use them are refused with
-NotImplementedError instead of being run without them.
+NotImplementedError rather than run without them.
 """
 from __future__ import annotations
 
 import atexit
-import queue as _queue
+import itertools
 import threading
 import time
-from concurrent.futures import ThreadPoolExecutor
+from collections import deque
+from concurrent.futures import Future, ThreadPoolExecutor
 
 from .batch_engine import SpecSlots, batch_generate_baseline, batchable
 from .generate import GenResult, dflash_generate, greedy_generate, speculative_generate
@@ -40,8 +47,17 @@ def _refuse_unbuilt(stop, on_text) -> None:
         raise NotImplementedError("stop strings and streaming callbacks are not built")
 
 
+def _params(max_tokens, temperature, top_p=1.0, top_k=0, presence_penalty=0.0,
+            frequency_penalty=0.0, logprobs=None, stop=None, seed=None) -> dict:
+    return dict(max_tokens=int(max_tokens), temperature=float(temperature), top_p=float(top_p),
+                top_k=int(top_k or 0), presence_penalty=float(presence_penalty or 0.0),
+                frequency_penalty=float(frequency_penalty or 0.0), logprobs=logprobs,
+                stop=list(stop or []), seed=seed)
+
+
 class Engine:
-    """Loaded target/drafter -> GenResult, one request at a time (server.py:75-365)."""
+    """Loaded target/drafter -> GenResult, one request at a time on the engine's device thread
+    (the reference's Engine, server.py:75-365)."""
 
     def __init__(self, target, tokenizer, drafter, *, mode: str, model_id: str = "",
                  target_repo: str = "", drafter_repo: str | None = None,
@@ -58,22 +74,24 @@ class Engine:
         self.model_id = model_id or str(target_repo).rstrip("/").split("/")[-1]
         self.target_repo, self.drafter_repo = target_repo, drafter_repo
         self.max_draft_tokens = max_draft_tokens
-        self.cap_controller = cap_controller      # persists across requests (--max-draft auto)
+        self.cap_controller = cap_controller      # kept across requests (auto cap)
         self.lookup_drafts = lookup_drafts
-        self.cache_tokens = int(cache_tokens)     # initial size of a cache (they grow on demand)
+        self.cache_tokens = int(cache_tokens)     # first size of a cache; caches grow on demand
         self.prefix_cache_slots = max(1, int(prefix_cache_slots))
         self.default_max_tokens = default_max_tokens
         self.max_tokens_cap = max_tokens_cap
         self._executor = executor or ThreadPoolExecutor(max_workers=1,
-                                                        thread_name_prefix="dspark-gen")
-        self.prefix = self._build_prefix_cache(prefix_cache)
+                                                        thread_name_prefix="dspark-device")
+        self.prefix = self._make_prefix_cache(prefix_cache)
         self.created = int(time.time())
         self.stats = {"requests": 0, "prompt_tokens": 0, "completion_tokens": 0,
                       "generation_seconds": 0.0, "sum_accept_len": 0.0}
+        self._decode = {"dspark": self._run_dspark, "dflash": self._run_dflash,
+                        "lookup": self._run_lookup, "baseline": self._run_baseline}[mode]
 
-    def _build_prefix_cache(self, enabled: bool):
-        """Prefix reuse where a cache can roll back exactly: dspark, lookup and baseline
-        (server.py:143-160); DFlash's drafter cache cannot, so it runs without."""
+    def _make_prefix_cache(self, enabled: bool):
+        """Conversation prefix reuse for the modes whose caches roll back exactly (dspark,
+        lookup, baseline); the DFlash drafter's context cache cannot (server.py:143-160)."""
         if not enabled or self.mode == "dflash":
             return None
         probe = self.target.make_cache(64)
@@ -92,47 +110,21 @@ class Engine:
                  top_k: int = 0, presence_penalty: float = 0.0, frequency_penalty: float = 0.0,
                  logprobs: int | None = None, stop=None, seed: int | None = None,
                  on_text=None) -> GenResult:
-        return self._executor.submit(
-            self._generate_impl, list(prompt_ids), max_tokens, temperature, top_p, top_k, stop,
-            seed, on_text, presence_penalty, frequency_penalty, logprobs).result()
+        p = _params(max_tokens, temperature, top_p, top_k, presence_penalty, frequency_penalty,
+                    logprobs, stop, seed)
+        return self._executor.submit(self.run_request, list(prompt_ids), p, on_text).result()
 
-    def _generate_impl(self, prompt_ids, max_tokens, temperature, top_p, top_k, stop, seed,
-                       on_text, presence_penalty=0.0, frequency_penalty=0.0,
-                       logprobs=None) -> GenResult:
-        _refuse_unbuilt(stop, on_text)
+    def run_request(self, prompt_ids: list[int], p: dict, on_text=None) -> GenResult:
+        """One request on the calling thread (the engine's device thread)."""
+        _refuse_unbuilt(p["stop"], on_text)
         cache = ctx = None
         reuse = 0
         if self.prefix is not None:
             cache, ctx, reuse = self.prefix.acquire(prompt_ids)
         try:
-            if self.mode == "dspark":
-                res = speculative_generate(
-                    self.target, self.tokenizer, self.drafter, prompt_ids=prompt_ids,
-                    cache=cache, ctx_caches=ctx, reuse_len=reuse, max_new_tokens=max_tokens,
-                    max_draft_tokens=self.max_draft_tokens, cap_controller=self.cap_controller,
-                    lookup_drafts=self.lookup_drafts, temperature=temperature, top_p=top_p,
-                    top_k=top_k, presence_penalty=presence_penalty,
-                    frequency_penalty=frequency_penalty, logprobs=logprobs, seed=seed)
-            elif self.mode == "dflash":
-                res = dflash_generate(
-                    self.target, self.tokenizer, self.drafter, prompt_ids=prompt_ids,
-                    max_new_tokens=max_tokens, max_draft_tokens=self.max_draft_tokens,
-                    cap_controller=self.cap_controller, temperature=temperature, top_p=top_p,
-                    top_k=top_k, seed=seed)
-            elif self.mode == "lookup":
-                res = lookup_generate(
-                    self.target, self.tokenizer, prompt_ids=prompt_ids, cache=cache,
-                    reuse_len=reuse, max_new_tokens=max_tokens,
-                    max_draft_tokens=self.max_draft_tokens or 6, temperature=temperature,
-                    top_p=top_p, top_k=top_k, seed=seed)
-            else:
-                res = greedy_generate(
-                    self.target, self.tokenizer, prompt_ids=prompt_ids, cache=cache,
-                    reuse_len=reuse, max_new_tokens=max_tokens, temperature=temperature,
-                    top_p=top_p, top_k=top_k, presence_penalty=presence_penalty,
-                    frequency_penalty=frequency_penalty, logprobs=logprobs, seed=seed)
+            res = self._decode(prompt_ids, p, cache, ctx, reuse)
         except BaseException:
-            # never keep a cache whose contents no longer match its recorded tokens
+            # a cache whose contents no longer match its token record is never kept
             if self.prefix is not None:
                 self.prefix.reset()
                 for c in (cache, ctx):
@@ -143,6 +135,35 @@ class Engine:
             self.prefix.store(cache, ctx, prompt_ids, res.token_ids)
         self._count(len(prompt_ids), res, res.seconds)
         return res
+
+    def _run_dspark(self, ids, p, cache, ctx, reuse) -> GenResult:
+        return speculative_generate(
+            self.target, self.tokenizer, self.drafter, prompt_ids=ids, cache=cache,
+            ctx_caches=ctx, reuse_len=reuse, max_new_tokens=p["max_tokens"],
+            max_draft_tokens=self.max_draft_tokens, cap_controller=self.cap_controller,
+            lookup_drafts=self.lookup_drafts, temperature=p["temperature"], top_p=p["top_p"],
+            top_k=p["top_k"], presence_penalty=p["presence_penalty"],
+            frequency_penalty=p["frequency_penalty"], logprobs=p["logprobs"], seed=p["seed"])
+
+    def _run_dflash(self, ids, p, cache, ctx, reuse) -> GenResult:
+        return dflash_generate(
+            self.target, self.tokenizer, self.drafter, prompt_ids=ids,
+            max_new_tokens=p["max_tokens"], max_draft_tokens=self.max_draft_tokens,
+            cap_controller=self.cap_controller, temperature=p["temperature"], top_p=p["top_p"],
+            top_k=p["top_k"], seed=p["seed"])
+
+    def _run_lookup(self, ids, p, cache, ctx, reuse) -> GenResult:
+        return lookup_generate(
+            self.target, self.tokenizer, prompt_ids=ids, cache=cache, reuse_len=reuse,
+            max_new_tokens=p["max_tokens"], max_draft_tokens=self.max_draft_tokens or 6,
+            temperature=p["temperature"], top_p=p["top_p"], top_k=p["top_k"], seed=p["seed"])
+
+    def _run_baseline(self, ids, p, cache, ctx, reuse) -> GenResult:
+        return greedy_generate(
+            self.target, self.tokenizer, prompt_ids=ids, cache=cache, reuse_len=reuse,
+            max_new_tokens=p["max_tokens"], temperature=p["temperature"], top_p=p["top_p"],
+            top_k=p["top_k"], presence_penalty=p["presence_penalty"],
+            frequency_penalty=p["frequency_penalty"], logprobs=p["logprobs"], seed=p["seed"])
 
     def _count(self, prompt_tokens: int, res: GenResult, seconds: float | None) -> None:
         s = self.stats
@@ -155,7 +176,7 @@ class Engine:
 
     # ---------------------------------------------------------------- reporting
     def spec_info(self, res: GenResult) -> dict:
-        """The non-standard `x_mlx_dspark` block of a response (server.py:331-343)."""
+        """The `x_mlx_dspark` block of a response (server.py:331-343)."""
         info = {"mode": self.mode, "accept_len": round(res.mean_accept_len, 3),
                 "tokens_per_sec": round(res.tokens_per_sec, 1),
                 "target_forwards": res.target_forwards}
@@ -182,223 +203,335 @@ class Engine:
 
 
 # -------------------------------------------------------------------------------------------
-_STOP = object()   # wakes the scheduler so it can return
+class _Request:
+    __slots__ = ("prompt_ids", "params", "on_text", "future", "t_submit")
 
-
-class _Job:
-    __slots__ = ("prompt_ids", "params", "on_text", "result", "error", "done")
-
-    def __init__(self, prompt_ids, params, on_text):
+    def __init__(self, prompt_ids, params: dict, on_text=None):
         self.prompt_ids = list(prompt_ids)
         self.params = params
         self.on_text = on_text
-        self.result = None
-        self.error = None
-        self.done = threading.Event()
+        self.future: Future = Future()
+        self.t_submit = time.time()
 
 
 class BatchEngine:
-    """Continuous batching in front of an Engine (server.py:381-608); see the module docstring
-    for the routing. Callers block in generate() while the scheduler runs their job."""
+    """Continuous batching in front of an Engine on its device thread (see the module
+    docstring). generate() blocks its caller until the request's result is ready."""
 
-    def __init__(self, engine: Engine, *, max_batch: int = 4, window_s: float = 0.02,
-                 slot_tokens: int | None = None):
+    def __init__(self, engine: Engine, *, max_batch: int = 4, slot_tokens: int | None = None,
+                 solo_wait_s: float = 0.25):
         self.engine = engine
         self.max_batch = max(2, int(max_batch))
-        self.window_s = float(window_s)
-        # positions per slot of a session (its page pools are sized up front)
+        # positions per slot (the slot table's page pools are sized up front)
         self.slot_tokens = int(slot_tokens or engine.cache_tokens)
-        self._q: _queue.Queue = _queue.Queue()
-        self.batch_stats = {"batched_requests": 0, "batches": 0, "max_batch_seen": 0,
-                            "serial_requests": 0}
+        self.solo_wait_s = float(solo_wait_s)
+        self._cv = threading.Condition()
+        self._slot_q: deque[_Request] = deque()
+        self._solo_q: deque[_Request] = deque()
         self._closed = False
-        engine._executor.submit(self._scheduler)
+        self._slots: SpecSlots | None = None
+        self.batch_stats = {"slot_requests": 0, "solo_requests": 0, "rounds": 0,
+                            "max_active": 0, "static_batches": 0}
+        self._loop = engine._executor.submit(self._device_loop)
         atexit.register(self.close)
 
-    def close(self) -> None:
-        if not self._closed:
-            self._closed = True
-            self._q.put(_STOP)
-
     def __getattr__(self, name):   # model_id, mode, spec_info, created, ... of the engine
+        if name == "engine":
+            raise AttributeError(name)
         return getattr(self.engine, name)
 
-    def generate(self, prompt_ids, *, max_tokens: int, temperature: float, top_p: float = 1.0,
-                 top_k: int = 0, presence_penalty: float = 0.0, frequency_penalty: float = 0.0,
-                 logprobs: int | None = None, stop=None, seed: int | None = None,
-                 on_text=None) -> GenResult:
-        job = _Job(prompt_ids, dict(max_tokens=max_tokens, temperature=temperature, top_p=top_p,
-                                    top_k=top_k, presence_penalty=presence_penalty,
-                                    frequency_penalty=frequency_penalty, logprobs=logprobs,
-                                    stop=list(stop or []), seed=seed), on_text)
-        self._q.put(job)
-        job.done.wait()
-        if job.error is not None:
-            raise job.error
-        return job.result
+    # ---------------------------------------------------------------- submission
+    def fits_slot(self, prompt_ids, p: dict, on_text=None) -> bool:
+        """A request runs in the slot table when it decodes greedily with no per-request
+        state the batched round lacks (penalties, logprobs, stop strings, callbacks) and its
+        prompt plus output fits one slot."""
+        if self.engine.mode not in ("dspark", "baseline"):
+            return False
+        block = self.engine.drafter.block_size if self.engine.drafter is not None else 0
+        need = len(prompt_ids) + p["max_tokens"] + 2 * block + 2
+        return (p["temperature"] == 0.0 and not p["presence_penalty"]
+                and not p["frequency_penalty"] and p["logprobs"] is None and not p["stop"]
+                and on_text is None and need <= self.slot_tokens)
+
+    def submit(self, prompt_ids, *, max_tokens: int, temperature: float, top_p: float = 1.0,
+               top_k: int = 0, presence_penalty: float = 0.0, frequency_penalty: float = 0.0,
+               logprobs: int | None = None, stop=None, seed: int | None = None,
+               on_text=None) -> Future:
+        p = _params(max_tokens, temperature, top_p, top_k, presence_penalty, frequency_penalty,
+                    logprobs, stop, seed)
+        req = _Request(prompt_ids, p, on_text)
+        if stop or on_text is not None:
+            req.future.set_exception(NotImplementedError(
+                "stop strings and streaming callbacks are not built"))
+            return req.future
+        with self._cv:
+            if self._closed:
+                raise RuntimeError("BatchEngine is closed")
+            (self._slot_q if self.fits_slot(req.prompt_ids, p, on_text) else self._solo_q).append(req)
+            self._cv.notify()
+        return req.future
+
+    def generate(self, prompt_ids, **kw) -> GenResult:
+        return self.submit(prompt_ids, **kw).result()
+
+    def close(self) -> None:
+        with self._cv:
+            if self._closed:
+                return
+            self._closed = True
+            self._cv.notify()
+        try:
+            self._loop.result(timeout=600)
+        except Exception:  # noqa: BLE001 - closing must not raise from a failed loop
+            pass
 
     def metrics(self) -> dict:
         m = self.engine.metrics()
         m["batching"] = {"max_batch": self.max_batch, **self.batch_stats}
         return m
 
-    # ---------------------------------------------------------------- scheduler
-    def _scheduler(self) -> None:
+    # ---------------------------------------------------------------- device thread
+    def _active(self) -> int:
+        return self._slots.n_active if self._slots is not None else 0
+
+    def _device_loop(self) -> None:
         while True:
-            batch = []
+            admit: list[_Request] = []
+            solo = None
+            with self._cv:
+                while not (self._slot_q or self._solo_q or self._active() or self._closed):
+                    self._cv.wait()
+                if self._closed and not (self._slot_q or self._solo_q or self._active()):
+                    break
+                active = self._active()
+                solo_due = bool(self._solo_q) and (
+                    not active or time.time() - self._solo_q[0].t_submit > self.solo_wait_s)
+                if not solo_due:
+                    free = self.max_batch - active
+                    while self._slot_q and len(admit) < free:
+                        admit.append(self._slot_q.popleft())
+                if self._solo_q and not active and not admit:
+                    solo = self._solo_q.popleft()
             try:
-                job = self._q.get()
-                if job is _STOP:
-                    return
-                batch = [job]
-                end = time.time() + self.window_s
-                while len(batch) < self.max_batch:
-                    left = end - time.time()
-                    if left <= 0:
-                        break
-                    try:
-                        nxt = self._q.get(timeout=left)
-                    except _queue.Empty:
-                        break
-                    if nxt is _STOP:
-                        self._q.put(nxt)          # finish this batch, return on the next get
-                        break
-                    batch.append(nxt)
-                self._run(batch)
-            except Exception as e:  # noqa: BLE001 - a dead scheduler would strand every caller
-                for j in batch:
-                    if not j.done.is_set():
-                        j.error = RuntimeError(f"batch scheduler error: {e}")
-                        j.done.set()
+                if self.engine.mode == "baseline" and admit:
+                    self._static_batch(admit)
+                    continue
+                for r in admit:
+                    self._admit(r)
+                if self._active():
+                    self._round()
+                elif solo is not None:
+                    self._solo(solo)
+            except BaseException as e:  # noqa: BLE001 - the loop must keep serving
+                self._fail_active(e)
+        if self._slots is not None:
+            self._slots.release()
+            self._slots = None
 
-    def _run(self, batch: list[_Job]) -> None:
-        groups: dict = {}
-        for j in batch:
-            p = j.params
-            if p["presence_penalty"] or p["frequency_penalty"] or p["logprobs"] is not None:
-                self._run_serial(j)
-                continue
-            groups.setdefault((p["temperature"], p["top_p"], p["top_k"]), []).append(j)
-        mode = self.engine.mode
-        for key, jobs in groups.items():
-            sampled = key[0] > 0
-            if len(jobs) == 1 or sampled or mode not in ("dspark", "baseline"):
-                # lone requests and sampled groups (no batched sampling round here) run serially
-                for j in jobs:
-                    self._run_serial(j)
-            elif mode == "dspark":
-                self._run_session(jobs)
-            else:
-                self._run_batched(jobs)
+    def _table(self) -> SpecSlots:
+        if self._slots is None:
+            eng = self.engine
+            self._slots = SpecSlots(eng.target, eng.tokenizer, eng.drafter,
+                                    capacity=self.max_batch,
+                                    max_draft_tokens=eng.max_draft_tokens or 2,
+                                    cap_controller=eng.cap_controller,
+                                    max_tokens=self.slot_tokens)
+        return self._slots
 
-    def _batchable_greedy(self, job: _Job) -> bool:
-        p = job.params
-        need = len(job.prompt_ids) + int(p["max_tokens"]) + 2 * self.engine.drafter.block_size + 2
-        return (not p["presence_penalty"] and not p["frequency_penalty"]
-                and p["logprobs"] is None and not p["temperature"] and not p["stop"]
-                and job.on_text is None and need <= self.slot_tokens)
-
-    def _admit(self, slots: SpecSlots, job: _Job) -> bool:
+    def _admit(self, r: _Request) -> None:
         try:
-            slots.admit(job.prompt_ids, max_new_tokens=job.params["max_tokens"], meta=job)
-            return True
-        except BaseException as e:  # noqa: BLE001 - one bad request must not end the session
-            job.error = e
-            job.done.set()
-            return False
+            self._table().admit(r.prompt_ids, max_new_tokens=r.params["max_tokens"], meta=r)
+            self.batch_stats["slot_requests"] += 1
+        except BaseException as e:  # noqa: BLE001 - one bad request must not stop the table
+            r.future.set_exception(e)
 
-    def _run_session(self, jobs: list[_Job]) -> None:
-        eng = self.engine
-        waiting, deferred = [], []
-        for j in jobs:
-            (waiting if self._batchable_greedy(j) else deferred).append(j)
-        admitted = peak = 0
+    def _round(self) -> None:
         t0 = time.time()
-        slots = SpecSlots(eng.target, eng.tokenizer, eng.drafter, capacity=self.max_batch,
-                          max_draft_tokens=eng.max_draft_tokens or 2,
-                          cap_controller=eng.cap_controller, max_tokens=self.slot_tokens)
-        try:
-            while slots.n_active or waiting:
-                while waiting and slots.has_free_slot:
-                    admitted += self._admit(slots, waiting.pop(0))
-                if not deferred:
-                    # pull requests that arrived meanwhile into the free capacity
-                    while len(waiting) < self.max_batch:
-                        try:
-                            nj = self._q.get_nowait()
-                        except _queue.Empty:
-                            break
-                        if nj is _STOP:
-                            self._q.put(nj)
-                            break
-                        if self._batchable_greedy(nj):
-                            waiting.append(nj)
-                        else:
-                            deferred.append(nj)   # stop admitting; it runs after the session
-                            break
-                    while waiting and slots.has_free_slot:
-                        admitted += self._admit(slots, waiting.pop(0))
-                peak = max(peak, slots.n_active)
-                for job, res in slots.step():
-                    job.result = res
-                    job.done.set()
-                    eng._count(len(job.prompt_ids), res, None)
-        except BaseException as e:  # noqa: BLE001
-            for j in waiting + [slots.meta[b] for b in range(slots.n_active)]:
-                if j is not None and not j.done.is_set():
-                    j.error = e
-                    j.done.set()
-        finally:
-            slots.release()
-        eng.stats["generation_seconds"] += time.time() - t0
-        self.batch_stats["batched_requests"] += admitted
-        self.batch_stats["batches"] += 1
-        self.batch_stats["max_batch_seen"] = max(self.batch_stats["max_batch_seen"], peak)
-        for j in deferred:
-            self._run_serial(j)
+        table = self._table()
+        self.batch_stats["max_active"] = max(self.batch_stats["max_active"], table.n_active)
+        for r, res in table.step():
+            self.engine._count(len(r.prompt_ids), res, None)
+            r.future.set_result(res)
+        self.batch_stats["rounds"] += 1
+        self.engine.stats["generation_seconds"] += time.time() - t0
 
-    def _run_serial(self, job: _Job) -> None:
-        try:
-            p = job.params
-            job.result = self.engine._generate_impl(
-                job.prompt_ids, p["max_tokens"], p["temperature"], p["top_p"], p["top_k"],
-                p["stop"], p["seed"], job.on_text, p["presence_penalty"],
-                p["frequency_penalty"], p["logprobs"])
-            self.batch_stats["serial_requests"] += 1
-        except BaseException as e:  # noqa: BLE001
-            job.error = e
-        finally:
-            job.done.set()
+    def _fail_active(self, e: BaseException) -> None:
+        """A failed round ends every row of the table; the table is rebuilt on next use."""
+        if self._slots is not None:
+            for b in range(self._slots.n_active):
+                r = self._slots.meta[b]
+                if r is not None and not r.future.done():
+                    r.future.set_exception(e)
+            try:
+                self._slots.release()
+            finally:
+                self._slots = None
 
-    def _run_batched(self, jobs: list[_Job]) -> None:
-        """Greedy baseline rows through the static batched kernel; one wall time per batch."""
+    def _solo(self, r: _Request) -> None:
         try:
-            for j in jobs:
-                _refuse_unbuilt(j.params["stop"], j.on_text)
+            r.future.set_result(self.engine.run_request(r.prompt_ids, r.params, r.on_text))
+            self.batch_stats["solo_requests"] += 1
+        except BaseException as e:  # noqa: BLE001
+            r.future.set_exception(e)
+
+    def _static_batch(self, reqs: list[_Request]) -> None:
+        """Baseline mode: greedy rows decoded together by the batched plain-decode graph."""
+        try:
             res = batch_generate_baseline(self.engine.target, self.engine.tokenizer,
-                                          [j.prompt_ids for j in jobs],
-                                          max_new_tokens=[j.params["max_tokens"] for j in jobs])
+                                          [r.prompt_ids for r in reqs],
+                                          max_new_tokens=[r.params["max_tokens"] for r in reqs])
         except BaseException as e:  # noqa: BLE001
-            for j in jobs:
-                j.error = e
-                j.done.set()
+            for r in reqs:
+                r.future.set_exception(e)
             return
-        for j, r in zip(jobs, res):
-            j.result = r
-            j.done.set()
-            self.engine._count(len(j.prompt_ids), r, None)
+        for r, x in zip(reqs, res):
+            self.engine._count(len(r.prompt_ids), x, None)
+            r.future.set_result(x)
         self.engine.stats["generation_seconds"] += res[0].seconds
-        self.batch_stats["batched_requests"] += len(jobs)
-        self.batch_stats["batches"] += 1
-        self.batch_stats["max_batch_seen"] = max(self.batch_stats["max_batch_seen"], len(jobs))
+        self.batch_stats["slot_requests"] += len(reqs)
+        self.batch_stats["static_batches"] += 1
+        self.batch_stats["max_active"] = max(self.batch_stats["max_active"], len(reqs))
 
 
 def maybe_batch_engine(engine: Engine, max_batch: int):
-    """A BatchEngine around `engine` when batching applies (max_batch > 1, a batchable target,
-    mode dspark or baseline); otherwise the engine itself (server.py:611-622)."""
+    """A BatchEngine around `engine` when batching applies (max_batch > 1, mode dspark or
+    baseline, a target that batches), else the engine itself (server.py:611-622)."""
     if max_batch <= 1 or engine.mode not in ("dspark", "baseline") or not batchable(engine.target):
         return engine
     return BatchEngine(engine, max_batch=max_batch)
 
 
-__all__ = ["Engine", "BatchEngine", "maybe_batch_engine", "MODES"]
+# -------------------------------------------------------------------------------------------
+def _replica_main(index: int, device, factory, inbox, outbox) -> None:
+    """Worker process of a ReplicaPool: build the serving object on `device`, then answer
+    (id, prompt_ids, params) messages from `inbox` on `outbox` until it receives None."""
+    try:
+        if device is not None:
+            import torch
+            torch.cuda.set_device(device)
+        server = factory(device)
+    except BaseException as e:  # noqa: BLE001 - report and exit
+        outbox.put(("failed", index, f"{type(e).__name__}: {e}"))
+        return
+    outbox.put(("ready", index, None))
+    lock = threading.Lock()
+
+    def reply(rid, fut):
+        try:
+            msg = ("done", rid, fut.result())
+        except BaseException as e:  # noqa: BLE001
+            msg = ("error", rid, f"{type(e).__name__}: {e}")
+        with lock:
+            outbox.put(msg)
+
+    while True:
+        msg = inbox.get()
+        if msg is None:
+            break
+        rid, prompt_ids, params = msg
+        fut = server.submit(prompt_ids, **params)
+        fut.add_done_callback(lambda f, rid=rid: reply(rid, f))
+    try:
+        server.close()
+    finally:
+        outbox.put(("closed", index, getattr(server, "metrics", lambda: {})()))
+
+
+class ReplicaPool:
+    """Request-parallel serving over several GPUs (no collective): one worker process per
+    device, each running factory(device) -> an object with submit(prompt_ids, **params) ->
+    Future and close() (a BatchEngine, as serving_replica builds). submit() sends a request to
+    the replica whose unfinished requests hold the fewest prompt + max-new tokens, ties to the
+    lowest index, and returns a Future of its GenResult."""
+
+    def __init__(self, factory, devices, *, start_timeout_s: float = 1800.0):
+        import torch.multiprocessing as mp
+        ctx = mp.get_context("spawn")
+        self.devices = list(devices)
+        self._inbox = [ctx.Queue() for _ in self.devices]
+        self._outbox = ctx.Queue()
+        self._procs = [ctx.Process(target=_replica_main, args=(i, d, factory, self._inbox[i],
+                                                               self._outbox), daemon=True)
+                       for i, d in enumerate(self.devices)]
+        for p in self._procs:
+            p.start()
+        self.load = [0] * len(self.devices)        # outstanding tokens per replica
+        self.assigned = [0] * len(self.devices)    # requests sent to each replica
+        self.replica_metrics: dict[int, dict] = {}
+        self._pending: dict[int, tuple[Future, int, int]] = {}
+        self._ids = itertools.count()
+        self._lock = threading.Lock()
+        ready = 0
+        deadline = time.time() + start_timeout_s
+        while ready < len(self.devices):
+            left = deadline - time.time()
+            kind, idx, info = self._outbox.get(timeout=max(1.0, left))
+            if kind == "failed":
+                self._stop_all()
+                raise RuntimeError(f"replica {idx} failed to start: {info}")
+            ready += kind == "ready"
+        self._collector = threading.Thread(target=self._collect, daemon=True)
+        self._collector.start()
+
+    def submit(self, prompt_ids, **params) -> Future:
+        cost = len(prompt_ids) + int(params.get("max_tokens", 0))
+        fut: Future = Future()
+        with self._lock:
+            i = min(range(len(self.devices)), key=lambda k: (self.load[k], k))
+            rid = next(self._ids)
+            self.load[i] += cost
+            self.assigned[i] += 1
+            self._pending[rid] = (fut, i, cost)
+        self._inbox[i].put((rid, list(prompt_ids), dict(params)))
+        return fut
+
+    def generate(self, prompt_ids, **params) -> GenResult:
+        return self.submit(prompt_ids, **params).result()
+
+    def _collect(self) -> None:
+        closed = 0
+        while closed < len(self.devices):
+            kind, key, payload = self._outbox.get()
+            if kind == "closed":
+                self.replica_metrics[key] = payload
+                closed += 1
+                continue
+            with self._lock:
+                fut, i, cost = self._pending.pop(key)
+                self.load[i] -= cost
+            if kind == "done":
+                fut.set_result(payload)
+            else:
+                fut.set_exception(RuntimeError(payload))
+
+    def _stop_all(self) -> None:
+        for q in self._inbox:
+            q.put(None)
+        for p in self._procs:
+            p.join(timeout=120)
+            if p.is_alive():
+                p.terminate()
+
+    def close(self) -> None:
+        self._stop_all()
+        self._collector.join(timeout=60)
+
+
+def serving_replica(device, *, target: str = "qwen3-8b", seed: int = 1, kv_bits: int | None = 8,
+                    block_size: int = 8, max_batch: int = 4, slot_tokens: int = 4608,
+                    max_draft_tokens: int = 8):
+    """A ReplicaPool factory: a synthetic target of a preset architecture (seeded weights, the
+    same on every replica) with a DSpark drafter, served by a BatchEngine on `device`."""
+    import functools  # noqa: F401 - the factory is usually passed as functools.partial
+    from .config import TARGETS, dspark_for
+    from .load import drafter_for, load_target
+    tgt, tok = load_target(target, kv_bits=kv_bits, seed=seed, device=device)
+    drafter, _ = drafter_for(tgt, dspark_for(TARGETS[target], block_size=block_size), seed=seed,
+                             device=device)
+    eng = Engine(tgt, tok, drafter, mode="dspark", max_draft_tokens=max_draft_tokens,
+                 lookup_drafts=False, cache_tokens=slot_tokens)
+    return BatchEngine(eng, max_batch=max_batch, slot_tokens=slot_tokens)
+
+
+__all__ = ["Engine", "BatchEngine", "ReplicaPool", "maybe_batch_engine", "serving_replica",
+           "MODES"]

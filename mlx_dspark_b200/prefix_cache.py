@@ -39,22 +39,24 @@ def _trim_target(cache, to_len: int) -> None:
 
 
 def target_cache_reusable(cache) -> bool:
-    """Every layer can roll back to any earlier position: KVCache and QuantizedKVCache (the
-    paged caches here, whose trim is pure offset arithmetic); a RotatingKVCache only with the
-    rotation machinery (max_size / is_trimmable), its wrap checked per entry at store time
-    (prefix_cache.py:62-79)."""
-    def ok(c) -> bool:
-        name = type(c).__name__
-        if not (hasattr(c, "trim") and hasattr(c, "offset")):
-            return False
-        kind = getattr(cache, "kind", name)
-        if kind in ("KVCache", "QuantizedKVCache") or name in ("KVCache", "QuantizedKVCache"):
-            return True
-        if name == "RotatingKVCache":
-            return hasattr(c, "max_size") and hasattr(c, "is_trimmable")
-        return False
+    """Whether a target cache can be cut back to any earlier length exactly, which reuse of a
+    stored conversation needs (the reference's rule, prefix_cache.py:62-79, restated for the
+    caches here). The caches this build makes are paged (kvcache.TargetCache over a
+    CacheState), where a trim is a length update, so they always can. A cache object handed in
+    by a caller qualifies when every layer view offers offset and trim; a sliding-window view
+    (mlx-lm's RotatingKVCache) also has to report its window (max_size) and whether it has
+    wrapped (is_trimmable), which store() checks before keeping it."""
+    if isinstance(getattr(cache, "state", None), CacheState):
+        return True
 
-    return all(ok(c) for c in cache)
+    def view_ok(c) -> bool:
+        if not (hasattr(c, "offset") and callable(getattr(c, "trim", None))):
+            return False
+        if type(c).__name__ == "RotatingKVCache" or getattr(c, "max_size", None) is not None:
+            return hasattr(c, "max_size") and callable(getattr(c, "is_trimmable", None))
+        return True
+
+    return all(view_ok(c) for c in cache)
 
 
 def _storable(cache) -> bool:

@@ -4,8 +4,10 @@ TEST / BENCHMARK INFRASTRUCTURE ONLY (bench.py's cpu_baseline leg and --impl ref
 The reference's MLX CPU backend cannot run here (mlx is not installed), so this is the
 oracle port of greedy_generate's per-token work (src/mlx_dspark/generate.py:433-450: one
 target forward of one token over the KV cache, then argmax), written for speed on CPU:
-weights stay int8 + bf16 scale/bias and are dequantized on the fly per linear, in row
-chunks that stay in cache; math is fp32 with the oracle's bf16 rounding points.
+weights stay int8 + bf16 scale/bias and every linear is one pass over them in C
+(oracle/cpu_gemv.c: the group's scale and bias applied to its partial dot product, as MLX's
+CPU qmv does, threads over rows); the rest is fp32 torch with the oracle's bf16 rounding
+points. Without the built C library the linears fall back to torch, dequantizing row chunks.
 """
 from __future__ import annotations
 
@@ -15,6 +17,31 @@ import time
 import torch
 
 from .qwen3 import F32, bf, inv_freq, rms_norm, rope, silu
+
+_GEMV = None
+
+
+def _gemv_lib():
+    """oracle/_build/libcpu_gemv.so (oracle/build_cpu.py), or None when it is not built."""
+    global _GEMV
+    if _GEMV is None:
+        import ctypes
+        from pathlib import Path
+        path = Path(__file__).resolve().parent / "_build" / "libcpu_gemv.so"
+        if not path.exists():
+            try:
+                from .build_cpu import build
+                build()
+            except Exception:  # noqa: BLE001 - the torch path still works
+                _GEMV = False
+                return None
+        lib = ctypes.CDLL(str(path))
+        P = ctypes.c_void_p
+        lib.dspark_cpu_w8_gemv.argtypes = [P, P, P, P, P, ctypes.c_int, ctypes.c_int, P,
+                                           ctypes.c_int]
+        lib.dspark_cpu_w8_gemv.restype = None
+        _GEMV = lib
+    return _GEMV or None
 
 
 class StreamingDecoder:
@@ -42,6 +69,18 @@ class StreamingDecoder:
 
     def _lin(self, x, qt):
         N, K = qt.q.shape
+        lib = _gemv_lib()
+        if lib is not None:
+            import ctypes
+            xc = x.to(F32).contiguous()
+            out = torch.empty(N, dtype=F32)
+            xs = torch.empty(K // 64, dtype=F32)
+            q, sc, bi = qt.q.contiguous(), qt.scales.contiguous(), qt.biases.contiguous()
+            P = ctypes.c_void_p
+            lib.dspark_cpu_w8_gemv(P(q.data_ptr()), P(sc.data_ptr()), P(bi.data_ptr()),
+                                   P(xc.data_ptr()), P(out.data_ptr()), N, K, P(xs.data_ptr()),
+                                   self.threads)
+            return bf(out)
         out = torch.empty(N, dtype=F32)
         for r0 in range(0, N, self.chunk):
             r1 = min(N, r0 + self.chunk)

@@ -67,17 +67,33 @@ def silu(x):
     return x / (1.0 + torch.exp(-x))
 
 
+def _round_half_away(v: torch.Tensor) -> torch.Tensor:
+    """Round to nearest with halves away from zero (C roundf / Metal round), exactly."""
+    t = torch.trunc(v)
+    return t + torch.where((v - t).abs() >= 0.5, torch.sign(v), torch.zeros_like(v))
+
+
 def quantize_kv(x: torch.Tensor):
-    """Affine 8-bit group-64 along head_dim (the build's quantize-on-write rule):
-    scale = bf16((max-min)/255), bias = bf16(min), q = clamp(rint((x-bias)/scale), 0, 255).
-    Returns the dequantized bf16 values dequant = bf16(scale*q + bias)."""
+    """Affine 8-bit group-64 along head_dim with the rule of MLX's affine quantizer, which
+    QuantizedKVCache(64, 8) applies (src/mlx_dspark/target.py:44-46 -> mx.quantize), in fp32:
+    scale = max((max-min)/255, 1e-7), negated unless |min| > |max|; the larger-magnitude edge
+    is made exact: q0 = round(edge/scale), scale = edge/q0, bias = edge (bias 0, scale kept,
+    when q0 == 0); q = min(round((x-bias)/scale), 255), rounding halves away from zero; scale
+    and bias stored as bf16. Returns the dequantized values bf16(scale_bf16 * q + bias_bf16)."""
     *lead, d = x.shape
     g = x.to(F32).reshape(*lead, d // 64, 64)
     mn, mx = g.amin(-1, keepdim=True), g.amax(-1, keepdim=True)
-    s = ((mx - mn) / 255.0).to(torch.bfloat16).to(F32)
-    b = mn.to(torch.bfloat16).to(F32)
-    q = torch.where(s > 0, torch.round((g - b) / torch.where(s > 0, s, torch.ones_like(s))),
-                    torch.zeros_like(g)).clamp(0, 255)
+    sc = torch.clamp((mx - mn) / 255.0, min=1e-7)
+    neg_edge = mn.abs() > mx.abs()
+    sc = torch.where(neg_edge, sc, -sc)
+    edge = torch.where(neg_edge, mn, mx)
+    q0 = _round_half_away(edge / sc)
+    at_zero = q0 == 0
+    sc = torch.where(at_zero, sc, edge / torch.where(at_zero, torch.ones_like(q0), q0))
+    bi = torch.where(at_zero, torch.zeros_like(edge), edge)
+    q = _round_half_away((g - bi) / sc).clamp(0, 255)
+    s = sc.to(torch.bfloat16).to(F32)
+    b = bi.to(torch.bfloat16).to(F32)
     return bf(s * q + b).reshape(*lead, d)
 
 

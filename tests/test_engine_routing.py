@@ -1,7 +1,11 @@
-"""BatchEngine routing on the CPU with a stub engine (src/mlx_dspark/server.py:438-487): which
-requests share a continuous session, which go serial, and that every caller gets its result."""
+"""The serving layer's host logic on the CPU: how BatchEngine classifies requests (slot table or
+solo), that its device loop admits into free slots, steps the table, runs solo requests when the
+table is empty and pauses admissions for a solo request that waited too long, that a failed round
+fails only the table's rows, and that ReplicaPool sends each request to the least-loaded replica
+(worker processes started with spawn, stub servers, no GPU)."""
 import threading
-from concurrent.futures import ThreadPoolExecutor
+import time
+from concurrent.futures import Future
 from types import SimpleNamespace
 
 import pytest
@@ -10,8 +14,16 @@ from mlx_dspark_b200 import engine as eng_mod
 from mlx_dspark_b200.generate import GenResult
 
 
+def _res(ids, n=1):
+    return GenResult(text="", token_ids=list(ids), num_tokens=len(ids), num_rounds=n,
+                     accept_lengths=[1] * n, target_forwards=n, seconds=0.0)
+
+
 class _StubEngine:
+    """Stands in for Engine: runs solo requests instantly and records them."""
+
     def __init__(self, mode="dspark"):
+        from concurrent.futures import ThreadPoolExecutor
         self.mode = mode
         self._executor = ThreadPoolExecutor(max_workers=1)
         self.cache_tokens = 4096
@@ -20,83 +32,146 @@ class _StubEngine:
         self.cap_controller = None
         self.stats = {"requests": 0, "prompt_tokens": 0, "completion_tokens": 0,
                       "generation_seconds": 0.0, "sum_accept_len": 0.0}
-        self.serial = []
+        self.solo = []
 
-    def _generate_impl(self, prompt_ids, max_tokens, temperature, *rest):
-        stop, on_text = rest[2], rest[4]
-        eng_mod._refuse_unbuilt(stop, on_text)
-        self.serial.append(tuple(prompt_ids))
-        return GenResult(text="", token_ids=list(prompt_ids), num_tokens=len(prompt_ids),
-                         num_rounds=1, accept_lengths=[1], target_forwards=1, seconds=0.0)
+    def run_request(self, prompt_ids, p, on_text=None):
+        self.solo.append(prompt_ids[0])
+        return _res(prompt_ids)
+
+    def _count(self, *a):
+        self.stats["requests"] += 1
 
     def metrics(self):
-        return {}
+        return dict(self.stats)
 
 
-def _job(ids, **kw):
-    p = dict(max_tokens=8, temperature=0.0, top_p=1.0, top_k=0, presence_penalty=0.0,
-             frequency_penalty=0.0, logprobs=None, stop=[], seed=None)
-    p.update(kw)
-    return eng_mod._Job(ids, p, None)
+class _FakeTable:
+    """A slot table whose rows finish after `rounds` steps each."""
+
+    def __init__(self, capacity, rounds=2, fail_on=None):
+        self.capacity, self.rounds, self.fail_on = capacity, rounds, fail_on
+        self.rows = []            # [request, steps left]
+        self.admitted = []
+        self.steps = 0
+        self.released = False
+
+    @property
+    def n_active(self):
+        return len(self.rows)
+
+    @property
+    def meta(self):
+        return [r for r, _ in self.rows]
+
+    def admit(self, ids, *, max_new_tokens, meta):
+        assert len(self.rows) < self.capacity
+        self.admitted.append(ids[0])
+        self.rows.append([meta, self.rounds])
+
+    def step(self):
+        self.steps += 1
+        if self.fail_on is not None and self.steps == self.fail_on:
+            raise RuntimeError("device error")
+        done, keep = [], []
+        for r in self.rows:
+            r[1] -= 1
+            (done if r[1] == 0 else keep).append(r)
+        self.rows = keep
+        return [(r, _res(r.prompt_ids)) for r, _ in done]
+
+    def release(self):
+        self.released = True
 
 
 @pytest.fixture()
 def batch_engine(monkeypatch):
+    tables = []
+
+    def fake_table(self):
+        if self._slots is None:
+            self._slots = _FakeTable(self.max_batch, fail_on=getattr(self, "_fail_on", None))
+            tables.append(self._slots)
+        return self._slots
+
+    monkeypatch.setattr(eng_mod.BatchEngine, "_table", fake_table)
     e = _StubEngine()
-    be = eng_mod.BatchEngine(e, max_batch=4, window_s=0.2)
-    sessions, batched = [], []
-
-    def fake_session(self, jobs):
-        sessions.append([j.prompt_ids[0] for j in jobs])
-        for j in jobs:
-            j.result = "batched"
-            j.done.set()
-
-    def fake_batched(self, jobs):
-        batched.append([j.prompt_ids[0] for j in jobs])
-        for j in jobs:
-            j.result = "static"
-            j.done.set()
-
-    monkeypatch.setattr(eng_mod.BatchEngine, "_run_session", fake_session)
-    monkeypatch.setattr(eng_mod.BatchEngine, "_run_batched", fake_batched)
-    yield e, be, sessions, batched
+    be = eng_mod.BatchEngine(e, max_batch=2, solo_wait_s=0.05)
+    yield e, be, tables
     be.close()
     e._executor.shutdown(wait=True)
 
 
-def test_routing_by_sampling_and_penalties(batch_engine):
-    e, be, sessions, batched = batch_engine
-    jobs = [_job([1]), _job([2]), _job([3], temperature=0.7), _job([4], temperature=0.7),
-            _job([5], presence_penalty=0.5), _job([6], logprobs=2), _job([7], top_k=5)]
-    be._run(jobs)
-    assert sessions == [[1, 2]]                        # the greedy group shares a session
-    assert sorted(s[0] for s in e.serial) == [3, 4, 5, 6, 7]   # sampled, penalised, logprobs, alone
-    assert all(j.done.is_set() for j in jobs) and be.batch_stats["serial_requests"] == 5
-    e.mode = "baseline"
-    sessions.clear()
-    be._run([_job([8]), _job([9])])
-    assert batched == [[8, 9]] and not sessions
+def test_classification():
+    e = _StubEngine()
+    be = eng_mod.BatchEngine.__new__(eng_mod.BatchEngine)
+    be.engine, be.slot_tokens = e, 4096
+    ok = eng_mod._params(16, 0.0)
+    assert be.fits_slot([1] * 10, ok)
+    assert not be.fits_slot([1] * 10, eng_mod._params(16, 0.7))                  # sampled
+    assert not be.fits_slot([1] * 10, eng_mod._params(16, 0.0, presence_penalty=0.5))
+    assert not be.fits_slot([1] * 10, eng_mod._params(16, 0.0, logprobs=2))
+    assert not be.fits_slot([1] * 5000, ok)                                       # too long
+    e.mode = "lookup"
+    assert not be.fits_slot([1] * 10, ok)
 
 
-def test_queue_delivers_every_caller_and_refusals(batch_engine):
-    e, be, sessions, _ = batch_engine
-    out = {}
+def test_loop_batches_greedy_and_runs_solo_requests(batch_engine):
+    e, be, tables = batch_engine
+    futs = [be.submit([i], max_tokens=4, temperature=0.0) for i in range(5)]
+    futs.append(be.submit([9], max_tokens=4, temperature=0.8))
+    futs.append(be.submit([10], max_tokens=4, temperature=0.0, presence_penalty=0.3))
+    res = [f.result(timeout=10) for f in futs]
+    assert [r.token_ids[0] for r in res] == [0, 1, 2, 3, 4, 9, 10]
+    assert sorted(tables[0].admitted) == [0, 1, 2, 3, 4] and sorted(e.solo) == [9, 10]
+    st = be.metrics()["batching"]
+    assert st["slot_requests"] == 5 and st["solo_requests"] == 2 and st["max_active"] == 2
+    with pytest.raises(NotImplementedError):
+        be.generate([1], max_tokens=4, temperature=0.0, stop=["x"])
 
-    def call(i, **kw):
-        try:
-            out[i] = be.generate([i], max_tokens=4, temperature=kw.get("t", 0.0),
-                                 stop=kw.get("stop"))
-        except NotImplementedError as err:
-            out[i] = err
 
-    ts = [threading.Thread(target=call, args=(i,)) for i in range(3)]
-    ts.append(threading.Thread(target=call, args=(9,), kwargs={"t": 0.5, "stop": ["x"]}))
-    for t in ts:
-        t.start()
-    for t in ts:
-        t.join(10)
-    assert out[0] == out[1] == out[2] == "batched" and sessions and sum(map(len, sessions)) == 3
-    assert isinstance(out[9], NotImplementedError)
-    assert be._batchable_greedy(_job([1] * 5000)) is False      # longer than a slot
-    assert be._batchable_greedy(_job([1], stop=["\n"])) is False
+def test_failed_round_fails_only_its_rows(batch_engine):
+    e, be, tables = batch_engine
+    be._fail_on = 1
+    a = be.submit([1], max_tokens=4, temperature=0.0)
+    with pytest.raises(RuntimeError):
+        a.result(timeout=10)
+    assert tables[0].released
+    be._fail_on = None
+    b = be.submit([2], max_tokens=4, temperature=0.0)
+    assert b.result(timeout=10).token_ids == [2]      # a fresh table serves the next request
+
+
+def _stub_server(device, delay=0.0):
+    class S:
+        def submit(self, prompt_ids, **params):
+            f = Future()
+
+            def done():
+                time.sleep(delay * len(prompt_ids))
+                f.set_result(_res(prompt_ids + [params["max_tokens"]]))
+            threading.Thread(target=done).start()
+            return f
+
+        def close(self):
+            pass
+
+        def metrics(self):
+            return {"device": device}
+    return S()
+
+
+def test_replica_pool_least_loaded_dispatch():
+    import functools
+    pool = eng_mod.ReplicaPool(functools.partial(_stub_server, delay=0.002), [None, None],
+                               start_timeout_s=120)
+    try:
+        # one long request, then short ones: the short ones go to the other replica first
+        fl = pool.submit([1] * 200, max_tokens=100)
+        fs = [pool.submit([2] * 10, max_tokens=10) for _ in range(4)]
+        assert pool.assigned == [1, 4]
+        out = [f.result(timeout=60) for f in [fl] + fs]
+        assert out[0].token_ids[-1] == 100 and all(o.token_ids[-1] == 10 for o in out[1:])
+        assert pool.load == [0, 0]
+    finally:
+        pool.close()
+    assert set(pool.replica_metrics) == {0, 1}

@@ -1,7 +1,7 @@
-"""Engine and BatchEngine on the GPU (src/mlx_dspark/server.py:75-608): prefix reuse across
-requests, a concurrent mix (greedy rows batched in one continuous session, sampled and
-penalised requests serial) whose greedy outputs are the target's greedy decoding, stats, and
-the refusal of stop strings."""
+"""Engine and BatchEngine on the GPU (the reference's serving layer, src/mlx_dspark/server.py:
+75-622): prefix reuse across requests, a concurrent mix (greedy rows in the persistent slot
+table, sampled and penalised requests solo) whose greedy outputs are the target's greedy
+decoding, stats, and the refusal of stop strings."""
 import threading
 
 import pytest
@@ -77,7 +77,6 @@ def test_batch_engine_concurrent_mix(pair):
                     lookup_drafts=False, cache_tokens=512)
     be = maybe_batch_engine(engine, 4)
     assert isinstance(be, BatchEngine)
-    be.window_s = 0.5   # every request below arrives inside one gather window
     prompts = [_prompt(60 + 5 * i, 10 + i) for i in range(4)]
     out, errs = {}, {}
 
@@ -104,8 +103,15 @@ def test_batch_engine_concurrent_mix(pair):
             assert _greedy_ok(ref, prompts[i], out[i].token_ids[:20]) <= 2
         assert out[4].num_tokens >= 20 and out[5].num_tokens >= 20
         st = be.metrics()["batching"]
-        assert st["batched_requests"] == 4 and st["serial_requests"] == 2
-        assert st["max_batch_seen"] >= 2 and be.metrics()["requests"] == 6
+        assert st["slot_requests"] == 4 and st["solo_requests"] == 2
+        assert st["max_active"] >= 1 and be.metrics()["requests"] == 6
+        # a second wave reuses the same slot table (no new pools or graphs)
+        table = be._slots
+        more = [be.submit(prompts[i], max_tokens=12, temperature=0.0) for i in range(4)]
+        for i, f in enumerate(more):
+            r = f.result(timeout=300)
+            assert _greedy_ok(ref, prompts[i], r.token_ids[:12]) <= 2
+        assert be._slots is table
     finally:
         be.close()
         engine.close()

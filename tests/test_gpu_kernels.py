@@ -52,11 +52,6 @@ def test_w8a16_gemm_tc_matches_fp32_bound(cuda, M, N, K):
         idx = bad.nonzero()[:8].tolist()
         pytest.fail(f"{int(bad.sum())} of {M*N} outside bound; first {idx}; "
                     f"max err {err.max():.3e}, ref max {ref.abs().max():.3e}")
-    # the CUDA-core kernel computes the same product in fp32 dequant
-    y2 = torch.zeros_like(y)
-    ops.gemm_simt(x.to(torch.float16).to(cuda), w, y2, epilogue=EPI_STORE_F32)
-    torch.cuda.synchronize()
-    assert ((y2.cpu() - ref).abs() <= bound).all()
     # second call reuses the workspace counters (left at zero by the first)
     y3 = torch.zeros_like(y)
     ops.gemm(x.to(torch.float16).to(cuda), w, y3, epilogue=EPI_STORE_F32, scratch=sc)
@@ -83,42 +78,61 @@ def test_w8a16_gemm_kmap_diagnostic(cuda):
     assert (err <= exp.abs().max() * 2 ** -10 + 1e-6).all(), f"per-k max err {err.tolist()}"
 
 
-@pytest.mark.parametrize("M,N,K", [(9, 4096, 4096), (9, 6144, 4096), (9, 4096, 12288),
-                                   (16, 2048, 2048), (32, 4096, 1024), (1, 4096, 4096)])
-def test_gemm_cluster_split_matches_stream_k(cuda, M, N, K):
-    """Stream-K (default) and cluster split-K (split mode 1, for GEMMs with few tiles: q|k|v,
-    o, down) both stay inside the fp16-weight bound, each is deterministic, and they differ only
-    by the fp32 summation order of the split tiles."""
-    qt = _qrand(N, K, seed=M + N + 3 * K)
-    w = pack(qt, device=cuda)
-    x = _x16(M, K, seed=K)
-    ref = x @ qt.dequant().t()
-    bound = (x.abs() @ qt.dequant().abs().t()) * 2.0 ** -10 + 1e-5
+@pytest.mark.parametrize("M,H,I,V", [(1, 1024, 2048, 4096), (9, 1024, 2048, 4096),
+                                     (9, 4096, 12288, 2048), (36, 1024, 3072, 1024),
+                                     (64, 512, 1024, 8192)])
+def test_gemm_stream_matches_separate_launches(cuda, M, H, I, V):
+    """A layer's GEMM chain as one dspark_w8a16_stream launch (o +residual and row sums ->
+    gate|up with the fused input norm and SiLU*up -> down +residual, row sums and the fp16 tap
+    -> head with the fused final norm) against the four separate launches: split tiles are
+    summed in fixed point there and in ordered fp32 here, so outputs agree to a bf16 ulp of
+    the row scale (2^-6 allowed as the errors pass through four GEMMs), and the stream launch
+    repeats exactly (its counters and accumulators are left at zero)."""
+    from mlx_dspark_b200._lib import EPI_RESIDUAL_BF16, EPI_SILU_MUL_F16, EPI_STORE_BF16
+    wo = pack(_qrand(H, H, 1), device=cuda)
+    wgu = pack(_qrand(2 * I, H, 2), device=cuda)
+    wd = pack(_qrand(H, I, 3), device=cuda)
+    wh = pack(_qrand(V, H, 4), device=cuda)
+    ln1 = (1 + 0.1 * torch.randn(H, generator=torch.Generator().manual_seed(5))).to(torch.bfloat16).to(cuda)
+    ln2 = (1 + 0.1 * torch.randn(H, generator=torch.Generator().manual_seed(6))).to(torch.bfloat16).to(cuda)
+    x = _x16(M, H, seed=7).to(torch.float16).to(cuda)
+    h0 = _x16(M, H, seed=8).to(torch.bfloat16).to(cuda)
     sc = ops.Scratch(cuda)
-    out = {}
-    assert ops.gemm_plan(M, N, K)["cluster"] == 0  # stream-K by default
-    try:
-        for mode in (0, 1):
-            ops.gemm_split_mode(mode)
-            if mode == 1 and (N, K) in ((4096, 4096), (4096, 12288)) and M <= 32:
-                # the Qwen3-8B o / down shapes take the cluster form on a B200 (148 SMs)
-                assert ops.gemm_plan(M, N, K)["cluster"] > 1, ops.gemm_plan(M, N, K)
-            ys = []
-            for _ in range(2):
-                y = torch.zeros(M, N, dtype=torch.float32, device=cuda)
-                ops.gemm(x.to(torch.float16).to(cuda), w, y, epilogue=EPI_STORE_F32, scratch=sc)
-                ys.append(y)
-            torch.cuda.synchronize()
-            sc.check_status()
-            assert torch.equal(ys[0], ys[1]), f"split mode {mode} not deterministic"
-            err = (ys[0].cpu() - ref).abs()
-            assert (err <= bound).all(), f"mode {mode}: {int((err > bound).sum())} outside bound"
-            out[mode] = ys[0].cpu()
-    finally:
-        ops.gemm_split_mode(0)
-    # the two orders agree to fp32 summation error
-    tol = (x.abs() @ qt.dequant().abs().t()) * 2.0 ** -18 + 1e-7
-    assert ((out[0] - out[1]).abs() <= tol).all()
+
+    def run(stream: bool):
+        h = h0.clone()
+        ss = torch.zeros(M, H // 128, dtype=torch.float32, device=cuda)
+        act = torch.zeros(M, I, dtype=torch.float16, device=cuda)
+        tap = torch.zeros(M, 2 * H, dtype=torch.float16, device=cuda)
+        logits = torch.zeros(M, V, dtype=torch.bfloat16, device=cuda)
+        n1, n2 = ops.RowNorm(ln1, 1e-6, ss), ops.RowNorm(ln2, 1e-6, ss)
+        if stream:
+            ops.gemm_stream(M, [
+                ops.gemm_job(x, wo, h, epilogue=EPI_RESIDUAL_BF16, residual=h, sumsq_out=ss,
+                             wait_prev=False),
+                ops.gemm_job(h, wgu, act, epilogue=EPI_SILU_MUL_F16, norm=n1),
+                ops.gemm_job(act, wd, h, epilogue=EPI_RESIDUAL_BF16, residual=h, sumsq_out=ss,
+                             copy16=tap[:, H:]),
+                ops.gemm_job(h, wh, logits, epilogue=EPI_STORE_BF16, norm=n2)], sc)
+        else:
+            ops.gemm(x, wo, h, epilogue=EPI_RESIDUAL_BF16, residual=h, scratch=sc, sumsq_out=ss)
+            ops.gemm(h, wgu, act, epilogue=EPI_SILU_MUL_F16, scratch=sc, norm=n1)
+            ops.gemm(act, wd, h, epilogue=EPI_RESIDUAL_BF16, residual=h, scratch=sc,
+                     sumsq_out=ss, copy16=tap[:, H:])
+            ops.gemm(h, wh, logits, epilogue=EPI_STORE_BF16, scratch=sc, norm=n2)
+        torch.cuda.synchronize()
+        sc.check_status()
+        return [t.cpu() for t in (h, ss, act, tap, logits)]
+
+    sep = run(False)
+    first = run(True)
+    assert all(torch.equal(a, b) for a, b in zip(run(True), first)), "stream not deterministic"
+    for name, a, b in zip(("h", "sumsq", "act", "tap", "logits"), first, sep):
+        a, b = a.float(), b.float()
+        scale = b.abs().amax(-1, keepdim=True) + 1e-6
+        err = float(((a - b).abs() / scale).max())
+        assert err <= 2.0 ** -6, (name, err)
+    assert sep[4].float().abs().max() > 0
 
 
 @pytest.mark.parametrize("M,H,I", [(9, 512, 1536), (36, 1024, 2048), (1, 256, 384),
@@ -518,3 +532,33 @@ def test_shared_workspace_across_shapes(cuda):
         bound = (x.abs() @ qt.dequant().abs().t()) * 2.0 ** -10 + 1e-5
         assert ((y.cpu() - ref).abs() <= bound).all(), (i, M, N, K)
     assert int(sc.bufs["gemm"][:65536].view(torch.int32).abs().sum()) == 0
+
+
+def test_kv8_quantizer_follows_mlx_rule_exactly(cuda):
+    """The quantize-on-write of 8-bit pages against the oracle's restatement of MLX's affine
+    quantizer, bit for bit on the V rows (written without norm or RoPE): groups whose larger-
+    magnitude edge is the minimum or the maximum, an all-zero group, constant groups of either
+    sign, and random groups."""
+    B, T, Hq, Hkv, hd, eps = 1, 8, 0, 1, 128, 1e-6
+    pool, st = _pool_and_state(cuda, Hkv, hd, True, B, 256)
+    st.seq_len.fill_(0)
+    g = torch.Generator().manual_seed(17)
+    v = torch.randn(T, hd, generator=g)
+    v[0, :64] = 0.0                                  # all zero: bias 0, q 0
+    v[1, :64] = -0.75                                # constant negative
+    v[1, 64:] = 0.5                                  # constant positive
+    v[2, :64] = torch.linspace(-3.0, 1.0, 64)        # |min| > |max|
+    v[2, 64:] = torch.linspace(-1.0, 3.0, 64)        # |max| >= |min|
+    v[3] *= 1e-4                                     # tiny range
+    v[4, :64] = torch.linspace(-1.0, 1.0, 64)        # symmetric edges
+    v = v.to(torch.bfloat16)
+    qkv = torch.cat([torch.randn(T, hd, generator=g).to(torch.bfloat16), v], dim=1)  # k | v
+    kn = torch.ones(hd, dtype=torch.bfloat16)
+    freqs = oq.inv_freq(hd, 1e6)
+    ops.qkv_rope_kv_write(qkv.to(cuda), B, T, Hq, Hkv, hd, None, kn.to(cuda), eps,
+                          freqs.to(cuda), st.seq_len, None, st.layout(0))
+    torch.cuda.synchronize()
+    _, V = _read_kv(pool, st, 0, T, Hkv, hd)
+    ref = oq.quantize_kv(v.float()[None])
+    assert torch.equal(V, ref), (V - ref).abs().max()
+    assert torch.equal(V[0, 0, :64], torch.zeros(64))
