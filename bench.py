@@ -315,16 +315,15 @@ def read_traffic():
 
 
 def cpu_baseline(tw, prompt_len, budget):
-    from oracle.cpu_baseline import time_greedy_decode
+    from oracle.cpu_baseline import linear_kind, time_greedy_decode
 
     cw = tw.to("cpu")
     tps, n, dt, threads = time_greedy_decode(cw, prompt_len, budget_s=budget)
     return {"value": round(tps, 4), "unit": "tok/s", "cores": threads, "kind": "port",
             "cpu": cpu_model(), "os_cpu_count": os.cpu_count(),
             "sample": f"{n} plain greedy decode steps of the Qwen3-8B W8 target at a "
-                      f"{prompt_len}-token context (oracle port, fp32 math, int8 weights "
-                      f"dequantized per step; KV of the context filled synthetically), "
-                      f"{dt:.1f} s"}
+                      f"{prompt_len}-token context (oracle port, fp32 math, {linear_kind()}; "
+                      f"KV of the context filled synthetically), {dt:.1f} s"}
 
 
 def prefill_measure(target, drafter, prompt, reps=2):
@@ -667,7 +666,7 @@ def run_reference(args, world, rank):
         return None
     from mlx_dspark_b200.config import TARGETS, WORKLOADS
     from mlx_dspark_b200.weights import generate_target
-    from oracle.cpu_baseline import StreamingDecoder
+    from oracle.cpu_baseline import StreamingDecoder, linear_kind
 
     wl = WORKLOADS[args.workload]
     dev = "cuda" if torch.cuda.is_available() else "cpu"
@@ -700,7 +699,8 @@ def run_reference(args, world, rank):
         "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": dec.threads, "kind": "port",
                          "cpu": cpu_model(), "os_cpu_count": os.cpu_count(),
                          "sample": f"{n} greedy decode steps at a {wl.prompt_len}-token context "
-                                   f"(mlx absent: oracle port of greedy_generate), {dt:.1f} s"},
+                                   f"(mlx absent: oracle port of greedy_generate, "
+                                   f"{linear_kind()}), {dt:.1f} s"},
         "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }

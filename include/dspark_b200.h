@@ -58,10 +58,8 @@ enum {
   DSPARK_EPI_SILU_MUL_F16 = 2,  /* gate/up interleaved in 64-row halves of each 128-row tile;
                                    y[m,j] = fp16(bf16(bf16(silu(g)) * u)), y has N/2 columns */
   DSPARK_EPI_STORE_F32 = 3,     /* y[m,n] = acc (fp32)                                       */
-  DSPARK_EPI_PEER_F32 = 4,      /* dspark_w8a16_gemm_peer only: acc to every rank's receive
+  DSPARK_EPI_PEER_F32 = 4       /* dspark_w8a16_gemm_peer only: acc to every rank's receive
                                    buffer, then the tile's epoch flag (fused all-reduce)      */
-  DSPARK_EPI_QKV_ROPE = 16      /* dspark_w8a16_stream jobs only: the fused q|k|v epilogue of
-                                   dspark_w8a16_gemm_qkv_rope (per-head norm + RoPE + KV write) */
 };
 
 /* library identity */
@@ -128,22 +126,7 @@ typedef struct dspark_gemm_opts {
   void* copy_f16;   /* RESIDUAL_BF16 only: also store fp16(y) here (the hidden-state tap) */
   int copy_f16_ld;  /* its row stride in elements */
   int reserved2;
-  /* Tile-ready chaining of consecutive GEMMs on one stream; the two slot fields hold a slot
-   * index + 1, so a zero-initialised struct chains nothing.
-   * chain_sync: DSPARK_CHAIN_SLOTS slots of 128 bytes, zero-filled once, caller-owned.
-   * chain_slot = s + 1: this GEMM counts its finished tiles in slot s; the GEMM launched right
-   *   after it must then chain-wait on s (which resets the slot for its next use).
-   * chain_wait = s + 1: this GEMM's inputs (x, the norm sums, the residual) were written by the
-   *   GEMM counting into slot s, chain_wait_tiles (that GEMM's N/128) tiles, launched right
-   *   before this one: it reads them once that count is full instead of after that grid has
-   *   completed. (No reference counterpart: launch scheduling.) */
-  int* chain_sync;
-  int chain_slot;
-  int chain_wait;
-  int chain_wait_tiles;
-  int reserved3;
 } dspark_gemm_opts;
-enum { DSPARK_CHAIN_SLOTS = 1024 };
 int dspark_w8a16_gemm_ex(const void* x, int ldx, const uint8_t* wq, const uint32_t* wsb, int M,
                          int N, int K, void* y, int ldy, const void* residual, int ldr,
                          int epilogue, const dspark_gemm_opts* opts, void* workspace,
@@ -264,61 +247,6 @@ typedef struct dspark_kv_layout {
 } dspark_kv_layout;
 
 long long dspark_kv_page_bytes(int page_size, int num_kv_heads, int head_dim, int kv8);
-
-/* -------------------------------------------------------------------------------------
- * K1s — a list of small-M W8 GEMMs ("jobs") as ONE persistent launch, each job's input
- * produced by the job before it: between two attention kernels of the verify forward that is
- * o (+residual) -> gate|up (input norm, SiLU*up) -> down (+residual, tap) -> the next layer's
- * q|k|v (input norm, RoPE + KV write), or the final norm and the LM head after the last down
- * (the QuantizedLinear calls of mlx-lm's Qwen3 decoder layer under src/mlx_dspark/target.py:
- * 58-75 and src/mlx_dspark/batch_engine.py:184-206, one launch instead of one per linear).
- * Each job computes what the dspark_w8a16_gemm_ex (or, with DSPARK_EPI_QKV_ROPE,
- * dspark_w8a16_gemm_qkv_rope) call with the same fields computes. Tiles split across CTAs are
- * summed as 64-bit fixed point (2^-32 units, integer atomics): deterministic, and within fp32
- * rounding of the single GEMM's ordered fp32 sum (the outputs agree to a bf16 ulp).
- * Weights of every job stream without waiting; a job's activations are read only once every
- * tile of the job before it is finished (wait_prev = 1), or once the previous kernel has
- * completed (wait_prev = 0, required of job 0). Every CTA of the launch is resident at once
- * and every device wait is bounded (DSPARK_ERR_TIMEOUT in *status).
- * M <= 64 rows (shared by all jobs); at most 5 jobs; N/128 <= 2048 per job.
- * workspace: dspark_w8a16_stream_workspace_bytes(M, jobs, n_jobs) bytes, 256-byte aligned,
- * zero-filled once; every completed call leaves its counters and accumulators at zero. Calls
- * sharing a workspace must run in stream order.
- * (No reference counterpart as a unit: MLX dispatches each linear as its own kernel.) */
-typedef struct dspark_stream_job {
-  const void* x;               /* fp16 [M, K]; bf16 residual rows when opts.norm_w is set */
-  int ldx;
-  const uint8_t* wq;           /* dspark_w8a16_gemm weight layout */
-  const uint32_t* wsb;
-  int N, K;                    /* N ignored with DSPARK_EPI_QKV_ROPE: (Hq + 2*Hkv) * hd */
-  int epilogue;                /* DSPARK_EPI_STORE_BF16 / RESIDUAL_BF16 / SILU_MUL_F16 /
-                                  STORE_F32, or DSPARK_EPI_QKV_ROPE */
-  void* y;
-  int ldy;
-  const void* residual;
-  int ldr;
-  dspark_gemm_opts opts;       /* as dspark_w8a16_gemm_ex; prefetch is ignored */
-  int wait_prev;               /* 1: x (and residual / norm sums) come from the previous job */
-  /* DSPARK_EPI_QKV_ROPE only: as dspark_w8a16_gemm_qkv_rope */
-  int T, Hq, Hkv, hd;
-  const void* q_norm_w;
-  const void* k_norm_w;
-  float eps;
-  const float* inv_freq;
-  const int32_t* pos0;
-  void* q_out;
-  dspark_kv_layout kv;
-} dspark_stream_job;
-size_t dspark_stream_job_size(void); /* sizeof(dspark_stream_job), for bindings to check */
-size_t dspark_w8a16_stream_workspace_bytes(int M, const dspark_stream_job* jobs, int n_jobs);
-int dspark_w8a16_stream(int M, const dspark_stream_job* jobs, int n_jobs, void* workspace,
-                        size_t workspace_bytes, int* status, dspark_stream_t stream);
-/* CTAs of a stream launch of M rows on the current device (every one resident at once). */
-int dspark_w8a16_stream_grid(int M, int* grid);
-/* Diagnostic: info[8] = grid, resident CTAs per SM (occupancy query), registers per thread,
- * static shared bytes, dynamic shared bytes requested, dynamic shared bytes available per CTA
- * at two CTAs per SM, the max dynamic shared bytes attribute, max threads per block. */
-int dspark_w8a16_stream_info(int M, int* info);
 
 
 /* -------------------------------------------------------------------------------------

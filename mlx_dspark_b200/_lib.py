@@ -17,8 +17,6 @@ ERR_NAMES = {1: "invalid argument", 2: "alignment", 3: "launch failed", 4: "devi
              5: "unsupported", 6: "CUDA error", 7: "workspace"}
 
 EPI_STORE_BF16, EPI_RESIDUAL_BF16, EPI_SILU_MUL_F16, EPI_STORE_F32, EPI_PEER_F32 = 0, 1, 2, 3, 4
-EPI_QKV_ROPE = 16  # dspark_w8a16_stream jobs: the fused q|k|v RoPE + KV write epilogue
-CHAIN_SLOTS = 1024  # DSPARK_CHAIN_SLOTS
 
 
 class DsparkError(RuntimeError):
@@ -42,19 +40,7 @@ class GemmOpts(ctypes.Structure):
                 ("row_sumsq", c_void_p), ("norm_sumsq", c_void_p), ("norm_w", c_void_p),
                 ("norm_tiles", c_int), ("norm_eps", c_float), ("norm_ld", c_int),
                 ("reserved", c_int), ("copy_f16", c_void_p), ("copy_f16_ld", c_int),
-                ("reserved2", c_int), ("chain_sync", c_void_p), ("chain_slot", c_int),
-                ("chain_wait", c_int), ("chain_wait_tiles", c_int), ("reserved3", c_int)]
-
-
-class StreamJob(ctypes.Structure):
-    """dspark_stream_job (include/dspark_b200.h): one GEMM of a dspark_w8a16_stream launch."""
-    _fields_ = [("x", c_void_p), ("ldx", c_int), ("wq", c_void_p), ("wsb", c_void_p),
-                ("N", c_int), ("K", c_int), ("epilogue", c_int), ("y", c_void_p), ("ldy", c_int),
-                ("residual", c_void_p), ("ldr", c_int), ("opts", GemmOpts), ("wait_prev", c_int),
-                ("T", c_int), ("Hq", c_int), ("Hkv", c_int), ("hd", c_int),
-                ("q_norm_w", c_void_p), ("k_norm_w", c_void_p), ("eps", c_float),
-                ("inv_freq", c_void_p), ("pos0", c_void_p), ("q_out", c_void_p),
-                ("kv", KvLayout)]
+                ("reserved2", c_int)]
 
 
 class PeerAR(ctypes.Structure):
@@ -96,11 +82,6 @@ SIGNATURES = {
     "dspark_w8a16_gemm_ex": (I, [P, I, P, P, I, I, I, P, I, P, I, I, POINTER(GemmOpts), P,
                                  c_size_t, P, P]),
     "dspark_gemm_opts_size": (c_size_t, []),
-    "dspark_stream_job_size": (c_size_t, []),
-    "dspark_w8a16_stream_workspace_bytes": (c_size_t, [I, P, I]),
-    "dspark_w8a16_stream": (I, [I, P, I, P, c_size_t, P, P]),
-    "dspark_w8a16_stream_grid": (I, [I, P]),
-    "dspark_w8a16_stream_info": (I, [I, P]),
     "dspark_attention_workspace_bytes": (c_size_t, [I, I, I, I, I, I]),
     "dspark_attention_merge_mode": (I, [I]),
     "dspark_attention": (I, [P, I, I, I, POINTER(KvLayout), P, I, c_float, P, I, I, P,

@@ -46,10 +46,14 @@ __device__ __forceinline__ float bf16_round(float x) {
   return __bfloat162float(__float2bfloat16_rn(x));
 }
 
-// x * sigmoid(x) with every rounding explicit: the compiler may not contract it differently
-// in different kernels, so every GEMM epilogue that applies it gives the same bits
-__device__ __forceinline__ float silu_rn(float x) {
-  return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x)));
+// x * sigmoid(x) = x / (1 + e^-x) as a fixed instruction sequence (hardware exponential, the
+// approximate divide, an explicitly rounded add): nothing the compiler may contract
+// differently, so every GEMM epilogue that applies it gives the same bits. The result is
+// rounded to bf16 by every caller, far coarser than the few-ulp fp32 error of the fast
+// forms; the IEEE divide it replaces is a long dependent sequence per row that kept the
+// epilogue's rows from overlapping.
+__device__ __forceinline__ float silu_f(float x) {
+  return __fdividef(x, __fadd_rn(1.0f, __expf(-x)));
 }
 
 __device__ __forceinline__ float warp_sum(float v) {

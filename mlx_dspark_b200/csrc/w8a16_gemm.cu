@@ -94,11 +94,6 @@ struct Params {
   // range after issuing its last load (16-byte aligned, sizes multiples of 16)
   const char* pf_ptr[2];
   unsigned long long pf_bytes[2];
-  // tile-ready chaining (dspark_gemm_opts.chain_*): finished tiles counted in this launch's
-  // slot; activations (and norm sums) read once the previous GEMM's slot is full, instead of
-  // after that grid has completed (griddepcontrol.wait)
-  int* chain_sync;
-  int chain_slot, chain_wait, chain_wait_tiles;
   // PEER_F32 (dspark_w8a16_gemm_peer): every rank's receive buffer and flags, as mapped here
   float* peer_y[8];
   int* peer_f[8];
@@ -113,66 +108,27 @@ __device__ __forceinline__ long long range_owner(long long g, long long total, l
   return ((g + 1) * G + total - 1) / total - 1;
 }
 
-constexpr int kChainStride = 32;  // ints per chain slot (128 bytes): [0] finished tiles of the
-                                  // slot's GEMM, [1] CTAs of the GEMM waiting on it that have
-                                  // seen [0] full
-__device__ __forceinline__ int ld_acquire_gpu_i(const int* p) {
-  int v;
-  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-// A finished tile of a GEMM that owns a chain slot: once the 128 epilogue threads have
-// stored it, one release increment of the slot (cumulative through the barrier).
-template <typename PT>
-__device__ __forceinline__ void chain_tile_done(const PT& p, int er) {
-  if (p.chain_slot < 0) return;
-  asm volatile("bar.sync 1, 128;" ::: "memory");
-  if (er == 0)
-    asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(p.chain_sync + p.chain_slot * kChainStride)
-                 : "memory");
-}
-
-// The inputs of this GEMM are ready: the previous kernel has completed (griddepcontrol.wait),
-// or, chained, every tile of the previous GEMM is finished (a bounded acquire poll of its
-// slot). False if the wait gave up (DSPARK_ERR_TIMEOUT in *status, abort flag set).
-template <typename PT>
-__device__ __forceinline__ bool inputs_ready(const PT& p, volatile int* abort_flag) {
-  if (p.chain_wait < 0) {
-    pdl_wait();
-    return true;
-  }
-  const int* cnt = p.chain_sync + p.chain_wait * kChainStride;
-  if (ld_acquire_gpu_i(cnt) >= p.chain_wait_tiles) return true;
-  const unsigned long long t0 = globaltimer_ns();
-  while (ld_acquire_gpu_i(cnt) < p.chain_wait_tiles) {
-    if (*abort_flag) return false;
-    if (globaltimer_ns() - t0 > kSpinLimitNs) {
-      *abort_flag = 1;
-      report_error(p.status, DSPARK_ERR_TIMEOUT);
-      return false;
-    }
-    __nanosleep(32);
-  }
-  return true;
+// Sums of squares of 16 rows' outputs across the warp, into xch[ew * BN + c0 + j] (lane 0,
+// rows below M): the 16 butterfly reductions run interleaved rather than one row after another.
+template <int BN>
+__device__ __forceinline__ void row_sumsq16(const float* o, float* xch, int ew, int lane, int c0,
+                                            int M) {
+  float w[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) w[j] = __fmul_rn(o[j], o[j]);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+    for (int j = 0; j < 16; ++j) w[j] += __shfl_xor_sync(0xffffffffu, w[j], off);
+  if (lane == 0)
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (c0 + j < M) xch[ew * BN + c0 + j] = w[j];
 }
 
-// Chained: this CTA has seen the slot it waited on full. The last of the `workers` CTAs that
-// wait on it (those with work) resets the slot for its next use. That happens before this
-// GEMM finishes any tile, so before anything that follows it in the chain can run, and so
-// before the slot's owner runs again.
-template <typename PT>
-__device__ __forceinline__ void chain_passed(const PT& p, int workers) {
-  int* slot = p.chain_sync + p.chain_wait * kChainStride;
-  int old;
-  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(slot + 1) : "memory");
-  if (old == workers - 1) {
-    asm volatile("st.relaxed.gpu.global.s32 [%0], 0;" ::"l"(slot) : "memory");
-    asm volatile("st.relaxed.gpu.global.s32 [%0], 0;" ::"l"(slot + 1) : "memory");
-    __threadfence();
-  }
-}
-
-
+// The epilogues compute all rows of a 16-row chunk that holds any of the M rows without a branch
+// per row (rows past M hold zeros: their activations are the tensor map's zero fill), so the
+// rows' arithmetic and reductions overlap; only the stores are predicated on m < M.
 // PEER: the instance of the tensor-parallel fused all-reduce (dspark_w8a16_gemm_peer); the
 // other instances carry no code for it
 template <int BN, bool PEER = false, typename PT>
@@ -185,16 +141,16 @@ __device__ __forceinline__ void epilogue_store(const PT& p, int tile, int er, co
       __nv_bfloat16* y = static_cast<__nv_bfloat16*>(p.y);
       const int lane = er & 31, ew = er >> 5;
 #pragma unroll
-      for (int m = 0; m < BN; ++m)
-        if (m < p.M) {
-          const __nv_bfloat16 o = __float2bfloat16_rn(acc[m]);
-          y[(size_t)m * p.ldy + n] = o;
-          if (p.ss_out) {
-            const float v = __bfloat162float(o);
-            const float w = warp_sum(__fmul_rn(v, v));
-            if (lane == 0) xch[ew * BN + m] = w;
-          }
-        }
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        if (c0 >= p.M) break;
+        float o[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) o[j] = bf16_round(acc[c0 + j]);
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          if (c0 + j < p.M) y[(size_t)(c0 + j) * p.ldy + n] = __float2bfloat16_rn(o[j]);
+        if (p.ss_out) row_sumsq16<BN>(o, xch, ew, lane, c0, p.M);
+      }
       if (p.ss_out) {
         asm volatile("bar.sync 1, 128;" ::: "memory");
         if (er < p.M)
@@ -241,6 +197,7 @@ __device__ __forceinline__ void epilogue_store(const PT& p, int tile, int er, co
       const int lane = er & 31, ew = er >> 5;
 #pragma unroll
       for (int c0 = 0; c0 < BN; c0 += 16) {  // 16 rows at a time bounds the registers held
+        if (c0 >= p.M) break;
         __nv_bfloat16 rv[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
@@ -250,19 +207,18 @@ __device__ __forceinline__ void epilogue_store(const PT& p, int tile, int er, co
           else
             rv[j] = m < p.M ? __ldcg(r + (size_t)m * p.ldr + n) : __float2bfloat16_rn(0.0f);
         }
+        float o[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          o[j] = bf16_round(__bfloat162float(rv[j]) + bf16_round(acc[c0 + j]));
 #pragma unroll
         for (int j = 0; j < 16; ++j)
           if (c0 + j < p.M) {
-            const __nv_bfloat16 o = __float2bfloat16_rn(__bfloat162float(rv[j]) + bf16_round(acc[c0 + j]));
-            y[(size_t)(c0 + j) * p.ldy + n] = o;
-            if (p.copy16) p.copy16[(size_t)(c0 + j) * p.copy16_ld + n] = __float2half_rn(__bfloat162float(o));
-            if (p.ss_out) {
-              // this row's share of the next RMSNorm: warp sum, then the 4 warps in order
-              const float v = __bfloat162float(o);
-              const float w = warp_sum(__fmul_rn(v, v));
-              if (lane == 0) xch[ew * BN + c0 + j] = w;
-            }
+            y[(size_t)(c0 + j) * p.ldy + n] = __float2bfloat16_rn(o[j]);
+            if (p.copy16) p.copy16[(size_t)(c0 + j) * p.copy16_ld + n] = __float2half_rn(o[j]);
           }
+        // the rows' shares of the next RMSNorm: warp sums here, then the 4 warps in order
+        if (p.ss_out) row_sumsq16<BN>(o, xch, ew, lane, c0, p.M);
       }
       if (p.ss_out) {
         asm volatile("bar.sync 1, 128;" ::: "memory");
@@ -285,18 +241,20 @@ __device__ __forceinline__ void epilogue_store(const PT& p, int tile, int er, co
         const int col = tile * 64 + er;
 #pragma unroll
         for (int c0 = 0; c0 < BN; c0 += 16) {
+          if (c0 >= p.M) break;
           // the exchanged values first (xch is a generic pointer the stores may alias)
-          float up[16];
+          float a[16];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) up[j] = xch[er * BN + c0 + j];
+          for (int j = 0; j < 16; ++j) a[j] = xch[er * BN + c0 + j];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float g = bf16_round(acc[c0 + j]);
+            const float s = bf16_round(silu_f(g));
+            a[j] = bf16_round(__fmul_rn(s, bf16_round(a[j])));
+          }
 #pragma unroll
           for (int j = 0; j < 16; ++j)
-            if (c0 + j < p.M) {
-              const float g = bf16_round(acc[c0 + j]);
-              const float u = bf16_round(up[j]);
-              const float s = bf16_round(silu_rn(g));
-              y[(size_t)(c0 + j) * p.ldy + col] = __float2half_rn(bf16_round(s * u));
-            }
+            if (c0 + j < p.M) y[(size_t)(c0 + j) * p.ldy + col] = __float2half_rn(a[j]);
         }
       }
       asm volatile("bar.sync 1, 128;" ::: "memory");
@@ -362,7 +320,7 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 ? 2 : 1))
   constexpr uint32_t ACC0 = (uint32_t)AB * 64u;
   constexpr uint32_t TC = kTwoPerSm ? 256u : 512u;
   static_assert(ACC0 + 2 * ACCS <= TC, "TMEM layout");
-  static_assert(3 * STAGES + 2 * AB + 9 <= (int)(L::kBarBytes / 8), "barrier region");
+  static_assert(3 * STAGES + 2 * AB + 8 <= (int)(L::kBarBytes / 8), "barrier region");
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -386,8 +344,6 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 ? 2 : 1))
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_holder + 2);
   const uint32_t fix_bar = smem_u32(bars + 3 * STAGES + 2 * AB + 7);  // stream-K fixup copies
-  // the producer's wait for this GEMM's inputs, passed on to the converters (one poller per CTA)
-  const uint32_t ready_bar = smem_u32(bars + 3 * STAGES + 2 * AB + 8);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -408,7 +364,6 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 ? 2 : 1))
     }
     mbar_init(done_bar, 1);
     mbar_init(fix_bar, 1);
-    mbar_init(ready_bar, 1);
     *abort_flag = 0;
     *last_flag = 0;
     fence_mbar_init();
@@ -449,17 +404,8 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 ? 2 : 1))
         tma_load_2d(w_s + i * kWBytes, &tm_w, full(i), kb * BK, tile * BM, pol_w);
         tma_load_2d(sb_s + i * kSBBytes, &tm_sb, full(i), tile * BM, kb * 2, pol_w);
       }
-      // activations are written by the previous kernel (or the previous chained GEMM, whose
-      // generic stores this TMA reads through the async proxy); a chained CTA without work
-      // reads nothing and does not wait
-      const bool chained = p.chain_wait >= 0;
-      const bool in_ok = (chained && n_iter == 0) ? true : inputs_ready(p, abort_flag);
-      if (in_ok) mbar_arrive(ready_bar);
-      if (chained && n_iter > 0 && in_ok) {
-        fence_proxy_async_global();
-        chain_passed(p, (int)(total < G ? total : G));
-      }
-      for (int i = 0; i < (in_ok ? pre : 0); ++i) {
+      pdl_wait();  // activations are written by the previous kernel
+      for (int i = 0; i < pre; ++i) {
         const long long g = start + i;
         const int kb = (int)(g % KB);
         mbar_arrive_expect_tx(xfull(i), L::kXBytes);
@@ -467,7 +413,7 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 ? 2 : 1))
         tma_load_2d(x_s + i * L::kXBytes + BN * 128, &tm_x, xfull(i), kb * BK + 64, 0, pol_x);
       }
       int issued = pre;
-      for (int i = pre; i < (in_ok ? n_iter : 0); ++i) {
+      for (int i = pre; i < n_iter; ++i) {
         const int s = i % STAGES;
         const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
         if (!mbar_wait(empty(s), ph ^ 1u, abort_flag, p.status)) break;
@@ -596,12 +542,7 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 ? 2 : 1))
       }
       if (p.norm_w) {
         if (i == 0) {
-          // the row sums of squares come from the previous kernel / chained GEMM: ready once
-          // the producer's wait has passed
-          if (!mbar_wait(ready_bar, 0, abort_flag, p.status)) {
-            tc_wait_st();
-            break;
-          }
+          pdl_wait();  // the row sums of squares come from the previous kernel
 #pragma unroll
           for (int kk = 0; kk < BN / 16; ++kk) {
             const int m = (r >> 3) + 16 * kk;
@@ -670,9 +611,7 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 ? 2 : 1))
     // epilogue: thread er owns row er of the tile (TMEM lane er)
     const int er = threadIdx.x - kConvWarps * 32;
     const int quad = warp & 3;
-    // outputs may still be read by the previous kernel; a chained GEMM's inputs come from the
-    // GEMM before it, whose reads of this GEMM's outputs ended before its tiles were finished
-    if (p.chain_wait < 0) pdl_wait();
+    pdl_wait();  // outputs may still be read by the previous kernel
     int seg = 0;
     uint32_t fix_phase = 0;
     long long g = start;
@@ -705,7 +644,6 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 ? 2 : 1))
           rope_epilogue<BN>(p, tile, er, acc, xch);
         else
           epilogue_store<BN, PEER>(p, tile, er, acc, xch);
-        chain_tile_done(p, er);
       } else {
         // partial of this CTA, row-major [128][MP] with MP = M rounded up to 4: thread er's
         // values are 16-byte vectors, and each contributor's partial is one contiguous
@@ -834,7 +772,6 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 ? 2 : 1))
             rope_epilogue<BN>(p, tile, er, sum, xch);
           else
             epilogue_store<BN, PEER>(p, tile, er, sum, xch, (kPre && res) ? rpre : nullptr);
-          chain_tile_done(p, er);
         }
         asm volatile("bar.sync 1, 128;" ::: "memory");
       }
@@ -855,610 +792,6 @@ __global__ void __launch_bounds__(kThreads, (BN <= 32 ? 2 : 1))
   }
 }
 
-// ------------------------------------------------------------------------------------------
-// K1s — the W8 GEMMs between two attention kernels as ONE persistent launch ("stream").
-//
-// A verify layer runs o (+residual) -> gate|up (input norm, SiLU*up) -> down (+residual, tap)
-// -> the next layer's q|k|v (input norm, RoPE + KV write). At M <= 64 rows each is a few
-// microseconds of weight streaming, and as separate launches each also paid a ramp (its CTAs
-// start as the previous kernel's CTAs leave) and a tail (the stream-K fixups of the last
-// tiles). Here one resident grid walks the jobs in order, each CTA taking its stream-K range of
-// every job:
-//   - the producer thread streams the weight tiles of every job back to back, waiting only for
-//     free ring slots, so the next job's weights are already in shared memory while the
-//     previous job finishes;
-//   - the same thread issues a job's activation loads once every tile of the job before it is
-//     finished: the CTA that finishes a tile raises the job's counter with release semantics,
-//     and the producer polls it with acquire loads (the first job's activations come from the
-//     previous kernel, behind griddepcontrol.wait);
-//   - converter, MMA and epilogue warps are those of w8a16_tc_kernel; a tile split across CTAs
-//     is summed in a fixed-point accumulator (each contributor adds its fp32 partial as a 64-bit
-//     integer of 2^-32 units with an atomic add, so the sum does not depend on arrival order)
-//     and finished by its last contributor, which reads that one block: the end of a job costs
-//     one L2 round trip instead of one per contributor. One accumulator region per job, since
-//     CTAs work on different jobs at the same time.
-// L1 is not coherent inside a kernel, so data written by other CTAs of this launch (residual
-// rows, row sums of squares, partials) is read through L2 (ld.global.cg). Every CTA must be
-// resident together (a CTA can wait for another's tiles): the host sizes the grid to the
-// device's resident CTAs for this instance, and every wait is bounded.
-constexpr int kStreamMaxJobs = 5;
-constexpr int kStreamMaxTiles = 2048;       // 128-row tiles per job (N <= 262144)
-constexpr int kSyncStride = 32;             // ints between the sync counters (128 bytes)
-constexpr size_t kStreamSyncBytes = 1024;   // kStreamMaxJobs + 1 counters
-constexpr int kEpiRope = 100;               // a job's epilogue: the fused q|k|v RoPE + KV write
-static_assert((kStreamMaxJobs + 2) * kSyncStride * sizeof(int) <= kStreamSyncBytes, "sync region");
-constexpr unsigned long long kResidentLimitNs = 100000000ull;  // 100 ms for every CTA to start
-
-struct SJob {
-  int M, N, K, tiles, kb;
-  long long total;
-  int epilogue;
-  int wait_prev;  // 1: x (and residual / norm sums) come from the previous job of the launch
-  int ldy, ldr;
-  void* y;
-  const void* residual;
-  unsigned long long* acc64;  // [tiles][M][128] fixed-point accumulators, this job's region
-  int* counters;               // [tiles], this job's region
-  float* ss_out;
-  const float* ss_in;
-  const __nv_bfloat16* norm_w;
-  int ss_tiles, ss_ld;
-  float norm_eps;
-  __half* copy16;
-  int copy16_ld;
-  int* chain_sync;  // (dspark_gemm_opts fields the stream launch does not use)
-  int chain_slot, chain_wait, chain_wait_tiles;
-  RopeEpi rope;
-};
-struct StreamParams {
-  int njobs;
-  SJob job[kStreamMaxJobs];
-  int* sync;    // job j's finished tiles at sync[j * kSyncStride]; exited CTAs at
-                // sync[kStreamMaxJobs * kSyncStride]; started CTAs one stride further
-  int* status;
-};
-struct StreamMaps {
-  CUtensorMap w[kStreamMaxJobs], sb[kStreamMaxJobs], x[kStreamMaxJobs];
-};
-
-__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}\n"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
-  int v;
-  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void red_release_gpu_add(int* p, int v) {
-  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-template <int BN, int STAGES>
-__global__ void __launch_bounds__(kThreads, (BN <= 32 ? 2 : 1))
-    w8_stream_kernel(const __grid_constant__ StreamMaps maps, const __grid_constant__ StreamParams sp) {
-  using L = Smem<BN, STAGES>;
-  constexpr bool kTwoPerSm = BN <= 32;
-  constexpr int AB = kTwoPerSm ? 3 : 6;
-  constexpr uint32_t ACCS = BN <= 32 ? 32u : 64u;
-  constexpr uint32_t ACC0 = (uint32_t)AB * 64u;
-  constexpr uint32_t TC = kTwoPerSm ? 256u : 512u;
-  static_assert(ACC0 + 2 * ACCS <= TC, "TMEM layout");
-  static_assert(3 * STAGES + 2 * AB + 8 <= (int)(L::kBarBytes / 8), "barrier region");
-  extern __shared__ uint8_t smem_raw[];
-  const uint32_t raw = smem_u32(smem_raw);
-  const uint32_t base = (raw + 1023u) & ~1023u;
-  uint8_t* sbase = smem_raw + (base - raw);
-
-  const uint32_t w_s = base;
-  const uint32_t x_s = base + STAGES * kWBytes;
-  const uint32_t sb_s = x_s + STAGES * L::kXBytes;
-  float* xch = reinterpret_cast<float*>(sbase + STAGES * L::kStageBytes);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sbase + STAGES * L::kStageBytes + L::kXchBytes);
-  auto full = [&](int s) { return smem_u32(bars + s); };
-  auto xfull = [&](int s) { return smem_u32(bars + STAGES + s); };
-  auto empty = [&](int s) { return smem_u32(bars + 2 * STAGES + s); };
-  auto afull = [&](int a) { return smem_u32(bars + 3 * STAGES + a); };
-  auto aempty = [&](int a) { return smem_u32(bars + 3 * STAGES + AB + a); };
-  auto accfull = [&](int b) { return smem_u32(bars + 3 * STAGES + 2 * AB + b); };
-  auto accempty = [&](int b) { return smem_u32(bars + 3 * STAGES + 2 * AB + 2 + b); };
-  const uint32_t done_bar = smem_u32(bars + 3 * STAGES + 2 * AB + 4);
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 3 * STAGES + 2 * AB + 5);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
-  volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_holder + 2);
-  volatile int* epi_flag = reinterpret_cast<volatile int*>(tmem_holder + 3);
-  // this CTA's stream-K range of every job, and the running unit index where each job starts
-  __shared__ long long s_st[kStreamMaxJobs], s_en[kStreamMaxJobs];
-  __shared__ int s_u0[kStreamMaxJobs + 1];
-
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int nj = sp.njobs;
-  const long long G = gridDim.x;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(full(s), 1);
-      mbar_init(xfull(s), 1);
-      mbar_init(empty(s), kConvWarps + 1);
-    }
-    for (int a = 0; a < AB; ++a) {
-      mbar_init(afull(a), kConvWarps);
-      mbar_init(aempty(a), 1);
-    }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(accfull(b), 1);
-      mbar_init(accempty(b), kEpiWarps);
-    }
-    mbar_init(done_bar, 1);
-    *abort_flag = 0;
-    *last_flag = 0;
-    // a job of fewer units than CTAs spreads over its first `total` CTAs only, so that every
-    // CTA in a tile's contributor range owns at least one of its units
-    int u = 0;
-    for (int j = 0; j < nj; ++j) {
-      const long long tot = sp.job[j].total;
-      const long long Gj = tot < G ? tot : G;
-      long long st = 0, en = 0;
-      if ((long long)blockIdx.x < Gj) {
-        st = range_start(blockIdx.x, tot, Gj);
-        en = range_start(blockIdx.x + 1, tot, Gj);
-      }
-      s_st[j] = st;
-      s_en[j] = en;
-      s_u0[j] = u;
-      u += (int)(en - st);
-    }
-    s_u0[nj] = u;
-    fence_mbar_init();
-  }
-  if (warp == kProducerWarp) {
-    if (lane == 0) {
-      for (int j = 0; j < nj; ++j) {
-        tma_prefetch_desc(&maps.w[j]);
-        tma_prefetch_desc(&maps.sb[j]);
-        tma_prefetch_desc(&maps.x[j]);
-      }
-    }
-    __syncwarp();
-    tmem_alloc(smem_u32(tmem_holder), TC);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem_base = *tmem_holder;
-  pdl_launch_dependents();
-  const int n_units = s_u0[nj];
-  // CTAs that have started, counted once the previous kernel is complete (the previous stream
-  // launch on this workspace resets the counter as its last CTA leaves, which may be after
-  // this launch's CTAs begin)
-  int* started = sp.sync + (kStreamMaxJobs + 1) * kSyncStride;
-
-  if (warp == kProducerWarp) {
-    if (lane == 0 && n_units > 0) {
-      const uint64_t pol_w = policy_evict_first();
-      const uint64_t pol_x = policy_evict_last();
-      int wi = 0, xi = 0, wj = 0, xj = 0;
-      bool xready = false, ok = true, resident = false;
-      unsigned long long idle_since = 0;
-      while (ok && xi < n_units) {
-        // weights: depend on nothing, so they run ahead across job boundaries, up to the ring
-        // (a slot frees only once the activations of its previous unit were consumed). With no
-        // activation load left to issue, wait for the slot on the barrier itself (the thread
-        // resumes as soon as it completes); otherwise only test it.
-        while (wi < n_units && wi < xi + STAGES) {
-          const int s = wi % STAGES;
-          if (wi >= STAGES) {
-            const uint32_t par = ((uint32_t)(wi / STAGES) & 1u) ^ 1u;
-            if (xi == wi) {
-              if (!mbar_wait(empty(s), par, abort_flag, sp.status)) {
-                ok = false;
-                break;
-              }
-            } else if (!mbar_test(empty(s), par)) {
-              break;
-            }
-          }
-          while (wi >= s_u0[wj + 1]) ++wj;
-          const SJob& J = sp.job[wj];
-          const long long g = s_st[wj] + (wi - s_u0[wj]);
-          const int tile = (int)(g / J.kb), kb = (int)(g % J.kb);
-          mbar_arrive_expect_tx(full(s), kWBytes + kSBBytes);
-          tma_load_2d(w_s + s * kWBytes, &maps.w[wj], full(s), kb * BK, tile * BM, pol_w);
-          tma_load_2d(sb_s + s * kSBBytes, &maps.sb[wj], full(s), tile * BM, kb * 2, pol_w);
-          ++wi;
-        }
-        if (!ok) break;
-        // activations of the units whose weights are issued (their slots are free), once the
-        // job's input is complete
-        bool blocked = false;
-        while (xi < wi) {
-          while (xi >= s_u0[xj + 1]) {
-            ++xj;
-            xready = false;
-          }
-          const SJob& J = sp.job[xj];
-          if (!xready) {
-            if (!J.wait_prev) {
-              pdl_wait();
-              xready = true;
-            } else {
-              // a CTA that waits for other CTAs' tiles needs every CTA resident; if some never
-              // start, say so rather than wait on work nobody runs
-              if (!resident) {
-                const unsigned long long t0 = globaltimer_ns();
-                while (ld_acquire_gpu(started) < (int)gridDim.x) {
-                  if (*abort_flag || globaltimer_ns() - t0 > kResidentLimitNs) {
-                    *abort_flag = 1;
-                    report_error(sp.status, DSPARK_ERR_UNSUPPORTED);
-                    break;
-                  }
-                  __nanosleep(64);
-                }
-                if (*abort_flag) {
-                  ok = false;
-                  break;
-                }
-                resident = true;
-              }
-              xready = ld_acquire_gpu(sp.sync + (xj - 1) * kSyncStride) >= sp.job[xj - 1].tiles;
-            }
-            // written with generic stores by other CTAs; read here through the async proxy
-            if (xready) fence_proxy_async_global();
-          }
-          if (!xready) {
-            blocked = true;
-            break;
-          }
-          const int s = xi % STAGES;
-          const long long g = s_st[xj] + (xi - s_u0[xj]);
-          const int kb = (int)(g % J.kb);
-          mbar_arrive_expect_tx(xfull(s), L::kXBytes);
-          tma_load_2d(x_s + s * L::kXBytes, &maps.x[xj], xfull(s), kb * BK, 0, pol_x);
-          tma_load_2d(x_s + s * L::kXBytes + BN * 128, &maps.x[xj], xfull(s), kb * BK + 64, 0,
-                      pol_x);
-          ++xi;
-        }
-        if (!ok) break;
-        if (!blocked) {
-          idle_since = 0;
-          continue;
-        }
-        // waiting for the previous job to finish: poll its counter, bounded
-        if (*abort_flag) break;
-        const unsigned long long now = globaltimer_ns();
-        if (idle_since == 0) {
-          idle_since = now;
-        } else if (now - idle_since > kSpinLimitNs) {
-          *abort_flag = 1;
-          report_error(sp.status, DSPARK_ERR_TIMEOUT);
-          break;
-        }
-        __nanosleep(32);
-      }
-      // drain: no bulk copy may still be writing into this CTA's shared memory at exit
-      volatile int never = 0;
-      for (int i = (wi > STAGES ? wi - STAGES : 0); i < wi; ++i)
-        mbar_wait(full(i % STAGES), (uint32_t)(i / STAGES) & 1u, &never, sp.status);
-      for (int i = (xi > STAGES ? xi - STAGES : 0); i < xi; ++i)
-        mbar_wait(xfull(i % STAGES), (uint32_t)(i / STAGES) & 1u, &never, sp.status);
-    }
-  } else if (warp == kMmaWarp) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_f16(BM, BN);
-      int seg = 0, j = 0;
-      for (int u = 0; u < n_units; ++u) {
-        while (u >= s_u0[j + 1]) ++j;
-        const SJob& J = sp.job[j];
-        const long long g = s_st[j] + (u - s_u0[j]);
-        const int kb = (int)(g % J.kb);
-        const bool seg_first = (u == s_u0[j]) || (kb == 0);
-        const bool seg_last = (u == s_u0[j + 1] - 1) || (kb == J.kb - 1);
-        const int s = u % STAGES;
-        const uint32_t ph = (uint32_t)(u / STAGES) & 1u;
-        const int a = u % AB;
-        const uint32_t aph = (uint32_t)(u / AB) & 1u;
-        const int ab = seg & 1;
-        const uint32_t abph = (uint32_t)(seg >> 1) & 1u;
-        if (seg_first && !mbar_wait(accempty(ab), abph ^ 1u, abort_flag, sp.status)) break;
-        if (!mbar_wait(afull(a), aph, abort_flag, sp.status)) break;
-        if (!mbar_wait(xfull(s), ph, abort_flag, sp.status)) break;
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + ACC0 + (uint32_t)ab * ACCS;
-#pragma unroll
-        for (int jj = 0; jj < BK / 16; ++jj) {
-          const uint32_t a_tmem = tmem_base + (uint32_t)a * 64u + (uint32_t)jj * 8u;
-          const uint32_t b_addr = x_s + s * L::kXBytes + (jj >> 2) * (BN * 128) + (jj & 3) * 32;
-          tc_mma_ts(d_tmem, a_tmem, umma_desc_sw128_kmajor(b_addr), idesc,
-                    (seg_first && jj == 0) ? 0u : 1u);
-        }
-        tc_commit(empty(s));
-        tc_commit(aempty(a));
-        if (seg_last) {
-          tc_commit(accfull(ab));
-          ++seg;
-        }
-      }
-      // every MMA issued above has finished before TMEM is released
-      tc_commit(done_bar);
-      volatile int never = 0;
-      mbar_wait(done_bar, 0, &never, sp.status);
-    }
-  } else if (warp < kConvWarps) {
-    // converters: thread r owns weight row r of the tile == TMEM lane r
-    const int r = threadIdx.x;
-    const uint32_t lane_base = tmem_base + ((uint32_t)(warp * 32) << 16);
-    const uint32_t k1024 = 0x64006400u;  // fp16x2 {1024, 1024}
-    float rn[BN / 16];
-#pragma unroll
-    for (int kk = 0; kk < BN / 16; ++kk) rn[kk] = 0.0f;
-    int j = 0;
-    for (int u = 0; u < n_units; ++u) {
-      while (u >= s_u0[j + 1]) ++j;
-      const SJob& J = sp.job[j];
-      const int s = u % STAGES;
-      const uint32_t ph = (uint32_t)(u / STAGES) & 1u;
-      const int a = u % AB;
-      const uint32_t aph = (uint32_t)(u / AB) & 1u;
-      // the lanes of a warp leave together if a wait gives up (the warp syncs below)
-      bool wok = mbar_wait(full(s), ph, abort_flag, sp.status);
-      wok = wok && mbar_wait(aempty(a), aph ^ 1u, abort_flag, sp.status);
-      if (!__all_sync(0xffffffffu, wok)) break;
-      tc_fence_after();
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        uint32_t sbv;
-        asm volatile("ld.shared.b32 %0, [%1];" : "=r"(sbv) : "r"(sb_s + s * kSBBytes + (h * BM + r) * 4));
-        const uint32_t sc2 = __byte_perm(sbv, 0, 0x1010);  // {scale, scale}
-        const uint32_t bi2 = __byte_perm(sbv, 0, 0x3232);  // {bias, bias}
-        uint32_t out[32];
-#pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {
-          const int chunk = h * 4 + c4;
-          const uint32_t addr = w_s + s * kWBytes + r * 128 + ((chunk ^ (r & 7)) << 4);
-          uint32_t v0, v1, v2, v3;
-          asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
-                       : "=r"(v0), "=r"(v1), "=r"(v2), "=r"(v3)
-                       : "r"(addr));
-          const uint32_t vv[4] = {v0, v1, v2, v3};
-#pragma unroll
-          for (int w = 0; w < 4; ++w) {
-#pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-              const uint32_t q2 = __byte_perm(vv[w], 0x64646464u, hh ? 0x4342u : 0x4140u);
-              __half2 qh = *reinterpret_cast<const __half2*>(&q2);
-              qh = __hsub2(qh, *reinterpret_cast<const __half2*>(&k1024));
-              const __half2 wv = __hfma2(qh, *reinterpret_cast<const __half2*>(&sc2),
-                                         *reinterpret_cast<const __half2*>(&bi2));
-              out[c4 * 8 + w * 2 + hh] = *reinterpret_cast<const uint32_t*>(&wv);
-            }
-          }
-        }
-        tmem_st32(lane_base + (uint32_t)a * 64u + (uint32_t)h * 32u, out);
-      }
-      if (J.norm_w) {
-        // the activations landing means the job's input (and its row sums) is complete
-        if (!__all_sync(0xffffffffu, mbar_wait(xfull(s), ph, abort_flag, sp.status))) {
-          tc_wait_st();  // no TMEM store of this thread may be in flight at teardown
-          break;
-        }
-        if (u == s_u0[j]) {
-          if (!J.wait_prev) pdl_wait();
-#pragma unroll
-          for (int kk = 0; kk < BN / 16; ++kk) {
-            const int m = (r >> 3) + 16 * kk;
-            float sum = 0.0f;
-            if (m < J.M) {
-              const float* row = J.ss_in + (size_t)m * J.ss_ld;
-              int t = 0;
-              if ((J.ss_ld & 3) == 0)
-                for (; t + 4 <= J.ss_tiles; t += 4) {
-                  const float4 q4 = __ldcg(reinterpret_cast<const float4*>(row + t));
-                  sum = (((sum + q4.x) + q4.y) + q4.z) + q4.w;
-                }
-              for (; t < J.ss_tiles; ++t) sum += __ldcg(row + t);
-            }
-            rn[kk] = rsqrtf(__fadd_rn(__fdiv_rn(sum, (float)J.K), J.norm_eps));
-          }
-        }
-        const long long g = s_st[j] + (u - s_u0[j]);
-        const int kb = (int)(g % J.kb);
-        const int c = r & 7;
-#pragma unroll
-        for (int bx = 0; bx < 2; ++bx) {
-          const uint4 wq8 = *reinterpret_cast<const uint4*>(J.norm_w + kb * BK + bx * 64 + c * 8);
-          const __nv_bfloat162* wv = reinterpret_cast<const __nv_bfloat162*>(&wq8);
-#pragma unroll
-          for (int kk = 0; kk < BN / 16; ++kk) {
-            const int m = (r >> 3) + 16 * kk;
-            if (m >= J.M) continue;
-            const uint32_t addr = x_s + s * L::kXBytes + bx * BN * 128 + m * 128 + ((c ^ (m & 7)) << 4);
-            uint32_t v[4];
-            asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
-                         : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
-                         : "r"(addr));
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const float2 hv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v[q]));
-              const float2 wf = __bfloat1622float2(wv[q]);
-              const __nv_bfloat162 xn = __floats2bfloat162_rn(__fmul_rn(__fmul_rn(hv.x, rn[kk]), wf.x), __fmul_rn(__fmul_rn(hv.y, rn[kk]), wf.y));
-              const float2 xf = __bfloat1622float2(xn);
-              const __half2 x16 = __floats2half2_rn(xf.x, xf.y);
-              v[q] = *reinterpret_cast<const uint32_t*>(&x16);
-            }
-            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v[0]), "r"(v[1]),
-                         "r"(v[2]), "r"(v[3])
-                         : "memory");
-          }
-        }
-        // the MMA reads the tile through the async proxy
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      }
-      tc_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(empty(s));
-        mbar_arrive(afull(a));
-      }
-    }
-  } else if (warp < kConvWarps + kEpiWarps) {
-    // epilogue: thread er owns row er of the tile (TMEM lane er)
-    const int er = threadIdx.x - kConvWarps * 32;
-    const int quad = warp & 3;
-    pdl_wait();  // outputs may still be read by the previous kernel
-    if (er == 0) red_release_gpu_add(started, 1);
-    int seg = 0;
-    bool ok = true;
-    for (int j = 0; j < nj && ok; ++j) {
-      const SJob& J = sp.job[j];
-      const long long total = J.total;
-      const long long Gj = total < G ? total : G;
-      const int KB = J.kb;
-      const long long end = s_en[j];
-      int lseg = 0;
-      long long g = s_st[j];
-      while (g < end) {
-        const int tile = (int)(g / KB);
-        const long long tile_lo = (long long)tile * KB;
-        const long long seg_end = (end < tile_lo + KB) ? end : tile_lo + KB;
-        const bool whole = (g == tile_lo) && (seg_end == tile_lo + KB);
-        const int ab = seg & 1;
-        const uint32_t abph = (uint32_t)(seg >> 1) & 1u;
-        // one thread waits and the barrier hands its verdict to all 128, so that every thread
-        // of the epilogue leaves together if the wait gives up
-        if (er == 0) *epi_flag = mbar_wait(accfull(ab), abph, abort_flag, sp.status) ? 1 : 0;
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (!*epi_flag) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        float acc[BN];
-#pragma unroll
-        for (int c = 0; c < BN / 16; ++c) {
-          uint32_t rr[16];
-          tmem_ld16(tmem_base + ((uint32_t)(quad * 32) << 16) + ACC0 + (uint32_t)ab * ACCS +
-                        (uint32_t)c * 16u,
-                    rr);
-          tc_wait_ld();
-#pragma unroll
-          for (int t = 0; t < 16; ++t) acc[c * 16 + t] = __uint_as_float(rr[t]);
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(accempty(ab));
-
-        bool finished = false;
-        if (whole) {
-          if (J.epilogue == kEpiRope)
-            rope_epilogue<BN>(J, tile, er, acc, xch);
-          else
-            epilogue_store<BN>(J, tile, er, acc, xch);
-          finished = true;
-        } else {
-          // Split tile: each contributor adds its partial into the tile's accumulator as 64-bit
-          // fixed point (2^-32 units) with integer atomics; integer sums do not depend on the
-          // order of arrival, so the result is deterministic, and the last contributor reads
-          // one accumulator block instead of every contributor's partial (one L2 round trip).
-          // Row er, activation row m lives at acc64[(tile * M + m) * 128 + er].
-          unsigned long long* a64 = J.acc64 + (size_t)tile * J.M * BM + er;
-          const bool res_pre = J.epilogue == DSPARK_EPI_RESIDUAL_BF16 && BN <= 16;
-          __nv_bfloat162 rpre[BN <= 16 ? BN / 2 : 1];
-          if constexpr (BN <= 16) {
-            // the residual rows, read before the arrival round trip (only the finisher uses them)
-            if (res_pre) {
-              const __nv_bfloat16* rp = static_cast<const __nv_bfloat16*>(J.residual) + tile * BM + er;
-#pragma unroll
-              for (int q = 0; q < BN / 2; ++q) {
-                const int m = 2 * q;
-                rpre[q].x = m < J.M ? __ldcg(rp + (size_t)m * J.ldr) : __float2bfloat16_rn(0.0f);
-                rpre[q].y = m + 1 < J.M ? __ldcg(rp + (size_t)(m + 1) * J.ldr) : __float2bfloat16_rn(0.0f);
-              }
-            }
-          }
-#pragma unroll
-          for (int m = 0; m < BN; ++m)
-            if (m < J.M)
-              asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(a64 + (size_t)m * BM),
-                           "l"((unsigned long long)__float2ll_rn(acc[m] * 4294967296.0f))
-                           : "memory");
-          asm volatile("bar.sync 1, 128;" ::: "memory");
-          const long long c_lo = range_owner(tile_lo, total, Gj);
-          const long long c_hi = range_owner(tile_lo + KB - 1, total, Gj);
-          const int nctr = (int)(c_hi - c_lo + 1);
-          if (er == 0) {
-            // release: the block's atomics (ordered before it by the barrier) are visible to
-            // whoever reads the final count; acquire: the last arriver sees every contribution
-            int old;
-            asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;"
-                         : "=r"(old)
-                         : "l"(J.counters + tile)
-                         : "memory");
-            *last_flag = old == nctr - 1 ? 1 : 0;
-          }
-          asm volatile("bar.sync 1, 128;" ::: "memory");
-          if (*last_flag) {
-            float sum[BN];
-            long long v[BN];
-#pragma unroll
-            for (int m = 0; m < BN; ++m)
-              v[m] = m < J.M ? (long long)__ldcg(a64 + (size_t)m * BM) : 0ll;
-#pragma unroll
-            for (int m = 0; m < BN; ++m) {
-              sum[m] = (float)((double)v[m] * 2.3283064365386963e-10);  // 2^-32
-              if (m < J.M) __stcg(a64 + (size_t)m * BM, 0ull);           // ready for the next call
-            }
-            if (er == 0) J.counters[tile] = 0;
-            if (J.epilogue == kEpiRope)
-              rope_epilogue<BN>(J, tile, er, sum, xch);
-            else
-              epilogue_store<BN>(J, tile, er, sum, xch, res_pre ? rpre : nullptr);
-            finished = true;
-          }
-        }
-        // every epilogue thread's stores of the tile precede the job counter's release
-        // (cumulative through the barrier); the reader fences the async proxy before its TMA
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (finished && er == 0) red_release_gpu_add(sp.sync + j * kSyncStride, 1);
-        ++seg;
-        ++lseg;
-        g = seg_end;
-      }
-    }
-  }
-
-  // a role that ran on one lane (producer, MMA issuer) rejoins its warp before the
-  // CTA barrier: the barrier counts whole warps, and TMEM is freed after it
-  __syncwarp();
-  tc_fence_before();
-  __syncthreads();
-  if (warp == kProducerWarp) {
-    tc_fence_after();
-    tmem_dealloc(tmem_base, TC);
-  }
-  // once every CTA has passed its last wait, the last one to leave resets the job counters
-  // for the next launch on this workspace
-  if (threadIdx.x == 0) {
-    int* exited = sp.sync + kStreamMaxJobs * kSyncStride;
-    int old;
-    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(exited) : "memory");
-    if (old == (int)gridDim.x - 1) {
-      for (int q = 0; q < kStreamMaxJobs; ++q) sp.sync[q * kSyncStride] = 0;
-      *exited = 0;
-      *started = 0;
-      __threadfence();
-    }
-  }
-}
 // ------------------------------------------------------------------------------------------
 // host side
 static int pick_bn(int M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 48 ? 48 : 64; }
@@ -1521,79 +854,6 @@ static int launch_tc(const void* x, int ldx, const uint8_t* wq, const uint32_t* 
   return DSPARK_OK;
 }
 
-// ---- stream (K1s) host side
-// workspace: [sync counters, kStreamSyncBytes] [kStreamMaxJobs x kStreamMaxTiles tile
-// counters] [per job: the fixed-point accumulators of its tiles, tiles x M x 128 x 8 bytes].
-// The counter region has a fixed size, so launches of different job lists sharing a workspace
-// never place one launch's accumulators over another's counters; every completed launch leaves
-// the counters and the accumulators it touched at zero.
-static size_t stream_acc_bytes(int M, int tiles) {
-  return ((size_t)tiles * M * BM * sizeof(unsigned long long) + 255) & ~(size_t)255;
-}
-static size_t stream_ws(int M, const int* tiles, int n) {
-  size_t b = kStreamSyncBytes + (size_t)kStreamMaxJobs * kStreamMaxTiles * sizeof(int);
-  for (int j = 0; j < n; ++j) b += stream_acc_bytes(M, tiles[j]);
-  return b;
-}
-
-// Stage ring of the stream kernel: one deeper than the single GEMM's at BN 16 (two CTAs of
-// ~113 KB still fit an SM), since the ring is what keeps the next job's weights streaming
-// while the previous job's last tiles finish.
-template <int BN>
-struct SCfg { static constexpr int kStages = BN == 16 ? 5 : Cfg<BN>::kStages; };
-
-// Every CTA of a stream launch must be resident at once (CTAs wait for each other's tiles).
-// The grid is the single-GEMM kernel's resident grid: two CTAs per SM for BN <= 32 (ten warps
-// and ~92 KB of shared memory each; measured on B200 with per-CTA %smid stamps: all 296 CTAs
-// start within a microsecond, two on every SM; the occupancy query reports one for this
-// shape, so it is not used), one for the wider instances. The kernel checks residency itself:
-// before any wait on another CTA, every CTA must have started (a bounded wait that reports
-// DSPARK_ERR_UNSUPPORTED instead of deadlocking).
-template <int BN>
-static int stream_grid(int* grid) {
-  constexpr int S = SCfg<BN>::kStages;
-  using L = Smem<BN, S>;
-  auto kern = w8_stream_kernel<BN, S>;
-  static bool configured[16] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 16) return set_error(DSPARK_ERR_UNSUPPORTED, "w8a16_stream: device %d", dev);
-  if (!configured[dev]) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kTotal) !=
-            cudaSuccess ||
-        cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
-      return set_error(DSPARK_ERR_CUDA, "w8a16_stream: cudaFuncSetAttribute(smem=%u) failed", L::kTotal);
-    configured[dev] = true;
-  }
-  *grid = sm_count() * Cfg<BN>::kCtasPerSm;
-  return DSPARK_OK;
-}
-
-template <int BN>
-static int launch_stream(const StreamMaps& maps, const StreamParams& p, cudaStream_t st) {
-  constexpr int S = SCfg<BN>::kStages;
-  using L = Smem<BN, S>;
-  auto kern = w8_stream_kernel<BN, S>;
-  int grid = 0;
-  const int rc = stream_grid<BN>(&grid);
-  if (rc) return rc;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)grid);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = L::kTotal;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, maps, p);
-  if (e != cudaSuccess)
-    return set_error(DSPARK_ERR_LAUNCH, "w8a16_stream launch failed: %s", cudaGetErrorString(e));
-  note_launch();
-  return DSPARK_OK;
-}
-
 static size_t ws_bytes(int M, int N, int K) {
   const int bn = pick_bn(M);
   const int cps = bn <= 32 ? 2 : 1;
@@ -1627,11 +887,9 @@ static int gemm_common_checks(const void* x, int ldx, const uint8_t* wq, const u
   return DSPARK_OK;
 }
 
-// The dspark_gemm_opts fields shared by the single GEMM and the stream jobs: the fp16 tap
-// copy, the row sums of squares out of the epilogue, and the input RMSNorm fused into the
-// converters. T is w8::Params or w8::SJob.
-template <typename T>
-static int apply_opts(T& p, const dspark_gemm_opts& o, int epilogue, int N) {
+// The dspark_gemm_opts fields: the fp16 tap copy, the row sums of squares out of the epilogue,
+// and the input RMSNorm fused into the converters.
+static int apply_opts(w8::Params& p, const dspark_gemm_opts& o, int epilogue, int N) {
   if (o.copy_f16) {
     if (epilogue != DSPARK_EPI_RESIDUAL_BF16 || o.copy_f16_ld < N)
       return set_error(DSPARK_ERR_INVALID, "w8a16_gemm: copy_f16 needs RESIDUAL_BF16 and ld >= N");
@@ -1660,20 +918,6 @@ static int apply_opts(T& p, const dspark_gemm_opts& o, int epilogue, int N) {
       return set_error(DSPARK_ERR_ALIGN, "w8a16_gemm: norm_sumsq not 16-byte aligned");
     p.norm_eps = o.norm_eps;
   }
-  // the struct holds slot + 1 (0: none), so a zero-initialised opts chains nothing
-  const int slot = o.chain_slot - 1, wait = o.chain_wait - 1;
-  p.chain_slot = -1;
-  p.chain_wait = -1;
-  if (slot >= 0 || wait >= 0) {
-    if (!o.chain_sync || slot >= DSPARK_CHAIN_SLOTS || wait >= DSPARK_CHAIN_SLOTS || slot < -1 ||
-        wait < -1 || (wait >= 0 && (o.chain_wait_tiles <= 0 || wait == slot)))
-      return set_error(DSPARK_ERR_INVALID, "w8a16_gemm: bad chain (sync=%p slot=%d wait=%d tiles=%d)",
-                       (void*)o.chain_sync, slot, wait, o.chain_wait_tiles);
-    p.chain_sync = o.chain_sync;
-    p.chain_slot = slot;
-    p.chain_wait = wait;
-    p.chain_wait_tiles = o.chain_wait_tiles;
-  }
   return DSPARK_OK;
 }
 
@@ -1689,7 +933,6 @@ static int gemm_launch(const void* x, int ldx, const uint8_t* wq, const uint32_t
   if (!workspace || workspace_bytes < need)
     return set_error(DSPARK_ERR_WORKSPACE, "w8a16_gemm: workspace %zu < %zu bytes", workspace_bytes, need);
   w8::Params p{};
-  p.chain_slot = p.chain_wait = -1;
   p.M = M; p.N = N; p.K = K;
   p.tiles = N / w8::BM;
   p.kb = K / w8::BK;
@@ -1867,141 +1110,4 @@ static int make_rope(w8::RopeEpi* r, int M, int T, int Hq, int Hkv, int hd, cons
   r->eps = eps;
   r->T = T; r->Hq = Hq; r->Hkv = Hkv; r->hd = hd;
   return DSPARK_OK;
-}
-
-extern "C" size_t dspark_stream_job_size(void) { return sizeof(dspark_stream_job); }
-
-// tiles of a job as the launch sees it (0 for a malformed job: the launch rejects it)
-static int stream_job_tiles(const dspark_stream_job& q) {
-  const int N = q.epilogue == DSPARK_EPI_QKV_ROPE ? (q.Hq + 2 * q.Hkv) * q.hd : q.N;
-  return N > 0 && N % 128 == 0 ? N / 128 : 0;
-}
-
-extern "C" size_t dspark_w8a16_stream_workspace_bytes(int M, const dspark_stream_job* jobs,
-                                                      int n_jobs) {
-  if (M < 1 || M > 64 || !jobs || n_jobs < 1 || n_jobs > w8::kStreamMaxJobs) return 0;
-  int tiles[w8::kStreamMaxJobs];
-  for (int j = 0; j < n_jobs; ++j) tiles[j] = stream_job_tiles(jobs[j]);
-  return w8::stream_ws(M, tiles, n_jobs);
-}
-
-extern "C" int dspark_w8a16_stream(int M, const dspark_stream_job* jobs, int n_jobs,
-                                   void* workspace, size_t workspace_bytes, int* status,
-                                   dspark_stream_t stream) {
-  using namespace w8;
-  if (!jobs || n_jobs < 1 || n_jobs > kStreamMaxJobs)
-    return set_error(DSPARK_ERR_INVALID, "w8a16_stream: %d jobs (1..%d)", n_jobs, kStreamMaxJobs);
-  if (M < 1 || M > 64) return set_error(DSPARK_ERR_INVALID, "w8a16_stream: M=%d not in [1,64]", M);
-  int tiles[kStreamMaxJobs];
-  for (int j = 0; j < n_jobs; ++j) tiles[j] = stream_job_tiles(jobs[j]);
-  const size_t need = stream_ws(M, tiles, n_jobs);
-  if (!workspace || workspace_bytes < need)
-    return set_error(DSPARK_ERR_WORKSPACE, "w8a16_stream: workspace %zu < %zu bytes", workspace_bytes, need);
-  if (reinterpret_cast<uintptr_t>(workspace) & 255)
-    return set_error(DSPARK_ERR_ALIGN, "w8a16_stream: workspace not 256-byte aligned");
-  StreamMaps maps;
-  memset(&maps, 0, sizeof(maps));
-  StreamParams p;
-  memset(&p, 0, sizeof(p));
-  p.njobs = n_jobs;
-  p.status = status;
-  uint8_t* w = static_cast<uint8_t*>(workspace);
-  p.sync = reinterpret_cast<int*>(w);
-  int* ctr = reinterpret_cast<int*>(w + kStreamSyncBytes);
-  uint8_t* acc = w + kStreamSyncBytes + (size_t)kStreamMaxJobs * kStreamMaxTiles * sizeof(int);
-  const int BNv = pick_bn(M);
-  for (int j = 0; j < n_jobs; ++j) {
-    const dspark_stream_job& q = jobs[j];
-    const bool rope = q.epilogue == DSPARK_EPI_QKV_ROPE;
-    const int N = rope ? (q.Hq + 2 * q.Hkv) * q.hd : q.N;
-    if (!rope && (q.epilogue < 0 || q.epilogue > 3))
-      return set_error(DSPARK_ERR_INVALID, "w8a16_stream: job %d epilogue %d", j, q.epilogue);
-    int rc = gemm_common_checks(q.x, q.ldx, q.wq, q.wsb, M, N, q.K,
-                                rope ? (q.q_out ? q.q_out : q.kv.pool) : q.y,
-                                rope ? DSPARK_EPI_STORE_BF16 : q.epilogue, q.residual);
-    if (rc) return rc;
-    if (N / BM > kStreamMaxTiles)
-      return set_error(DSPARK_ERR_UNSUPPORTED, "w8a16_stream: job %d has %d tiles (max %d)", j,
-                       N / BM, kStreamMaxTiles);
-    if (j == 0 && q.wait_prev)
-      return set_error(DSPARK_ERR_INVALID, "w8a16_stream: the first job has no previous job");
-    SJob& J = p.job[j];
-    J.M = M; J.N = N; J.K = q.K;
-    J.tiles = N / BM;
-    J.kb = q.K / BK;
-    J.total = (long long)J.tiles * J.kb;
-    J.epilogue = rope ? kEpiRope : q.epilogue;
-    J.wait_prev = q.wait_prev ? 1 : 0;
-    J.y = q.y; J.ldy = q.ldy;
-    J.residual = q.residual; J.ldr = q.ldr;
-    J.counters = ctr + (size_t)j * kStreamMaxTiles;
-    J.acc64 = reinterpret_cast<unsigned long long*>(acc);
-    acc += stream_acc_bytes(M, J.tiles);
-    if ((rc = apply_opts(J, q.opts, rope ? DSPARK_EPI_STORE_BF16 : q.epilogue, N))) return rc;
-    if (rope) {
-      if (q.opts.row_sumsq || q.opts.copy_f16)
-        return set_error(DSPARK_ERR_INVALID, "w8a16_stream: job %d: the RoPE epilogue writes no rows", j);
-      if ((rc = make_rope(&J.rope, M, q.T, q.Hq, q.Hkv, q.hd, q.q_norm_w, q.k_norm_w, q.eps,
-                          q.inv_freq, q.pos0, q.q_out, &q.kv, "w8a16_stream")))
-        return rc;
-    }
-    if ((rc = make_map_2d(&maps.w[j], CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, q.wq, (uint64_t)q.K,
-                          (uint64_t)N, (uint64_t)q.K, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B)))
-      return rc;
-    if ((rc = make_map_2d(&maps.sb[j], CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, q.wsb, (uint64_t)N,
-                          (uint64_t)(q.K / 64), (uint64_t)N * 4, BM, 2, CU_TENSOR_MAP_SWIZZLE_NONE)))
-      return rc;
-    if ((rc = make_map_2d(&maps.x[j], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, q.x, (uint64_t)q.K,
-                          (uint64_t)M, (uint64_t)q.ldx * 2, 64, BNv, CU_TENSOR_MAP_SWIZZLE_128B)))
-      return rc;
-  }
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  switch (BNv) {
-    case 16: return launch_stream<16>(maps, p, st);
-    case 32: return launch_stream<32>(maps, p, st);
-    case 48: return launch_stream<48>(maps, p, st);
-    default: return launch_stream<64>(maps, p, st);
-  }
-}
-
-extern "C" int dspark_w8a16_stream_grid(int M, int* grid) {
-  using namespace w8;
-  if (M < 1 || M > 64 || !grid) return set_error(DSPARK_ERR_INVALID, "w8a16_stream_grid: bad arguments");
-  switch (pick_bn(M)) {
-    case 16: return stream_grid<16>(grid);
-    case 32: return stream_grid<32>(grid);
-    case 48: return stream_grid<48>(grid);
-    default: return stream_grid<64>(grid);
-  }
-}
-
-// Diagnostic: why a stream instance gets the grid it gets. info[0..7] = grid, resident CTAs per
-// SM by the occupancy query, registers per thread, static shared bytes, dynamic shared bytes
-// requested, dynamic shared bytes available per CTA at two CTAs per SM, max dynamic shared
-// bytes per CTA (attribute), the function's max threads per block.
-extern "C" int dspark_w8a16_stream_info(int M, int* info) {
-  using namespace w8;
-  if (M < 1 || M > 64 || !info) return set_error(DSPARK_ERR_INVALID, "w8a16_stream_info: bad arguments");
-  int grid = 0;
-  int rc;
-  cudaFuncAttributes fa{};
-  size_t avail = 0;
-  int occ = 0;
-  unsigned kt = 0;
-  auto fill = [&](auto kern, unsigned total) {
-    cudaFuncGetAttributes(&fa, kern);
-    cudaOccupancyAvailableDynamicSMemPerBlock(&avail, kern, 2, kThreads);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, total);
-    kt = total;
-  };
-  switch (pick_bn(M)) {
-    case 16: rc = stream_grid<16>(&grid); fill(w8_stream_kernel<16, 5>, Smem<16, 5>::kTotal); break;
-    case 32: rc = stream_grid<32>(&grid); fill(w8_stream_kernel<32, 4>, Smem<32, 4>::kTotal); break;
-    case 48: rc = stream_grid<48>(&grid); fill(w8_stream_kernel<48, 5>, Smem<48, 5>::kTotal); break;
-    default: rc = stream_grid<64>(&grid); fill(w8_stream_kernel<64, 5>, Smem<64, 5>::kTotal); break;
-  }
-  info[0] = grid; info[1] = occ; info[2] = fa.numRegs; info[3] = (int)fa.sharedSizeBytes;
-  info[4] = (int)kt; info[5] = (int)avail; info[6] = fa.maxDynamicSharedSizeBytes;
-  info[7] = fa.maxThreadsPerBlock;
-  return rc;
 }

@@ -404,7 +404,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               const float a = (j & 1) ? hi_f(own) : lo_f(own);
               const float b2 = (j & 1) ? hi_f(other[j >> 1]) : lo_f(other[j >> 1]);
               const float g = gate ? a : b2, u = gate ? b2 : a;
-              const float sg = bf16_round(silu_rn(g));
+              const float sg = bf16_round(silu_f(g));
               *reinterpret_cast<__half*>(bp + (row0 + j) * 128 + r * 2) =
                   __float2half_rn(bf16_round(sg * u));
             }

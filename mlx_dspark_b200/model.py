@@ -164,20 +164,9 @@ class BlockDrafter:
         # fc -> (hidden_norm fused into each layer's k|v GEMM, whose epilogue runs k_norm + RoPE
         # and writes K/V into the context cache)
         ss = buf.ctx_sumsq[:c.hidden_size // 128 * M].view(M, c.hidden_size // 128)
-        hn = ops.RowNorm(self.hidden_norm, eps, ss)
-        if self._stream() and len(self.layers) < ops.STREAM_MAX_JOBS:
-            jobs = [ops.gemm_job(fused16, self.fc, buf.ctx_h, epilogue=EPI_STORE_BF16,
-                                 sumsq_out=ss, wait_prev=False)]
-            for l, L in enumerate(self.layers):
-                jobs.append(ops.qkv_rope_job(buf.ctx_h, L.kv, T=T, Hq=0,
-                                             Hkv=c.num_key_value_heads, hd=c.head_dim,
-                                             q_norm=None, k_norm=L.k_norm, eps=eps,
-                                             inv_freq=self.inv_freq, pos0=ctx.seq_len,
-                                             q_out=None, kv=ctx.layout(l), norm=hn))
-            ops.gemm_stream(M, jobs, sc)
-            return
         ops.gemm(fused16, self.fc, buf.ctx_h, epilogue=EPI_STORE_BF16, scratch=sc, M=M,
                  sumsq_out=ss)
+        hn = ops.RowNorm(self.hidden_norm, eps, ss)
         for l, L in enumerate(self.layers):
             ops.gemm_qkv_rope(buf.ctx_h, L.kv, T=T, Hq=0, Hkv=c.num_key_value_heads,
                               hd=c.head_dim, q_norm=None, k_norm=L.k_norm, eps=eps,
@@ -215,77 +204,39 @@ class BlockDrafter:
             self._bufs["prefill"] = pb
         return pb
 
-    def _stream(self) -> bool:
-        """Run the GEMMs between attention kernels as one dspark_w8a16_stream launch (the
-        target's setting)."""
-        return bool(getattr(self.target, "use_stream", False))
-
-    def _qkv_job(self, x, L, l: int, B: int, ctx: CacheState, buf: DraftBuffers, norm, wait_prev):
-        c = self.config
-        return ops.qkv_rope_job(x, L.qkv, T=self.block_size, Hq=c.num_attention_heads,
-                                Hkv=c.num_key_value_heads, hd=c.head_dim, q_norm=L.q_norm,
-                                k_norm=L.k_norm, eps=c.rms_norm_eps, inv_freq=self.inv_freq,
-                                pos0=ctx.seq_len, q_out=buf.q, kv=ctx.layout(l), norm=norm,
-                                wait_prev=wait_prev)
-
     def backbone_dev(self, pending: torch.Tensor, B: int, ctx: CacheState, buf: DraftBuffers,
-                     splits: int, final_norm: bool = True, head=None) -> bool:
+                     splits: int, final_norm: bool = True) -> None:
         """Block [pending, mask x (k-1)] of each row at positions seq_len[b] + i -> layers over
         [ctx; block] -> final norm into buf.xn16 (fp16, the head GEMM input). With
         final_norm=False the block's hidden states stay in buf.h with their row sums of squares
-        in buf.sumsq, for a head GEMM that fuses the final norm (final_head_norm()). `head`
-        (weights, output): with final_norm=False and the stream form, that head GEMM over all
-        B*k rows joins the last layer's launch; returns whether it ran."""
+        in buf.sumsq, for a head GEMM that fuses the final norm (final_head_norm())."""
         c, sc = self.config, self.scratch
         k = self.block_size
         M = B * k
         eps = c.rms_norm_eps
         ss = buf.sumsq
-        n = len(self.layers)
-        stream = self._stream()
-        head_done = False
         ops.embed_block(pending, B, k, self.mask_token_id, self.embed_w, buf.h, buf.ids)
         for l, L in enumerate(self.layers):
             kv = ctx.layout(l)
-            if l == 0 or not stream:
-                if l == 0:
-                    ops.rmsnorm(buf.h, L.input_ln, eps, y16=buf.xn16, M=M)
-                    x, nrm = buf.xn16, None
-                else:
-                    x, nrm = buf.h, ops.RowNorm(L.input_ln, eps, ss)
-                ops.gemm_qkv_rope(x, L.qkv, T=k, Hq=c.num_attention_heads,
-                                  Hkv=c.num_key_value_heads, hd=c.head_dim, q_norm=L.q_norm,
-                                  k_norm=L.k_norm, eps=eps, inv_freq=self.inv_freq,
-                                  pos0=ctx.seq_len, q_out=buf.q, kv=kv, scratch=sc, M=M,
-                                  norm=nrm)
+            if l == 0:
+                ops.rmsnorm(buf.h, L.input_ln, eps, y16=buf.xn16, M=M)
+                x, nrm = buf.xn16, None
+            else:
+                x, nrm = buf.h, ops.RowNorm(L.input_ln, eps, ss)
+            ops.gemm_qkv_rope(x, L.qkv, T=k, Hq=c.num_attention_heads,
+                              Hkv=c.num_key_value_heads, hd=c.head_dim, q_norm=L.q_norm,
+                              k_norm=L.k_norm, eps=eps, inv_freq=self.inv_freq, pos0=ctx.seq_len,
+                              q_out=buf.q, kv=kv, scratch=sc, M=M, norm=nrm)
             ops.attention(buf.q, B, k, c.num_attention_heads, kv, ctx.seq_len, False, c.scaling,
                           buf.attn16, splits, sc)
-            if not stream:
-                ops.gemm(buf.attn16, L.o, buf.h, epilogue=EPI_RESIDUAL_BF16, residual=buf.h,
-                         scratch=sc, M=M, sumsq_out=ss)
-                ops.gemm(buf.h, L.gu, buf.act16, epilogue=EPI_SILU_MUL_F16, scratch=sc, M=M,
-                         norm=ops.RowNorm(L.post_ln, eps, ss))
-                ops.gemm(buf.act16, L.down, buf.h, epilogue=EPI_RESIDUAL_BF16, residual=buf.h,
-                         scratch=sc, M=M, sumsq_out=ss)
-                continue
-            jobs = [ops.gemm_job(buf.attn16, L.o, buf.h, epilogue=EPI_RESIDUAL_BF16,
-                                 residual=buf.h, sumsq_out=ss, wait_prev=False),
-                    ops.gemm_job(buf.h, L.gu, buf.act16, epilogue=EPI_SILU_MUL_F16,
-                                 norm=ops.RowNorm(L.post_ln, eps, ss)),
-                    ops.gemm_job(buf.act16, L.down, buf.h, epilogue=EPI_RESIDUAL_BF16,
-                                 residual=buf.h, sumsq_out=ss)]
-            if l + 1 < n:
-                jobs.append(self._qkv_job(buf.h, self.layers[l + 1], l + 1, B, ctx, buf,
-                                          ops.RowNorm(self.layers[l + 1].input_ln, eps, ss), True))
-            elif head is not None and not final_norm:
-                w, out = head
-                jobs.append(ops.gemm_job(buf.h, w, out, epilogue=EPI_STORE_BF16,
-                                         norm=self.final_head_norm(buf)))
-                head_done = True
-            ops.gemm_stream(M, jobs, sc)
+            ops.gemm(buf.attn16, L.o, buf.h, epilogue=EPI_RESIDUAL_BF16, residual=buf.h,
+                     scratch=sc, M=M, sumsq_out=ss)
+            ops.gemm(buf.h, L.gu, buf.act16, epilogue=EPI_SILU_MUL_F16, scratch=sc, M=M,
+                     norm=ops.RowNorm(L.post_ln, eps, ss))
+            ops.gemm(buf.act16, L.down, buf.h, epilogue=EPI_RESIDUAL_BF16, residual=buf.h,
+                     scratch=sc, M=M, sumsq_out=ss)
         if final_norm:
             ops.rmsnorm(buf.h, self.norm, eps, y16=buf.xn16, M=M)
-        return head_done
 
     def final_head_norm(self, buf: DraftBuffers) -> "ops.RowNorm":
         """The final norm of a backbone_dev(final_norm=False) block, for the head GEMM."""
@@ -352,12 +303,10 @@ class DSparkDrafter(BlockDrafter):
         (generate.py:846-852,910) or a temperature draft keeping q (model.py:283-309)."""
         sc = self.scratch
         k = self.block_size
+        self.backbone_dev(pending, B, ctx, buf, splits, final_norm=False)
         head_rows = cap if B == 1 else B * k
-        fused = self.backbone_dev(pending, B, ctx, buf, splits, final_norm=False,
-                                  head=(self.head_w, buf.base) if head_rows == B * k else None)
-        if not fused:
-            ops.gemm(buf.h, self.head_w, buf.base, epilogue=EPI_STORE_BF16, scratch=sc,
-                     M=head_rows, norm=self.final_head_norm(buf))
+        ops.gemm(buf.h, self.head_w, buf.base, epilogue=EPI_STORE_BF16, scratch=sc,
+                 M=head_rows, norm=self.final_head_norm(buf))
         rows_per_b = cap if B == 1 else k
         sampled = sampling is not None and sampling.active
         m = self.markov_head

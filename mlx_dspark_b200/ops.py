@@ -12,7 +12,7 @@ import ctypes
 import torch
 
 from . import _lib
-from ._lib import KvLayout, StreamJob, call, lib
+from ._lib import KvLayout, call, lib
 from .weights import PackedLinear
 
 
@@ -33,8 +33,7 @@ def _require_cuda(*ts):
 class Scratch:
     """Zero-filled, grow-only workspaces per kernel family plus a device status word."""
 
-    FAMILIES = ("gemm", "attention", "accept", "markov", "accept_sample", "markov_probs", "stream",
-                "chain")
+    FAMILIES = ("gemm", "attention", "accept", "markov", "accept_sample", "markov_probs")
 
     def __init__(self, device="cuda"):
         self.device = torch.device(device)
@@ -42,7 +41,6 @@ class Scratch:
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.version = 0  # bumped when a buffer moves (captured graphs hold the addresses)
         self._status_host = None
-        self._chain_slots: dict = {}
 
     def get(self, family: str, nbytes: int) -> torch.Tensor:
         b = self.bufs.get(family)
@@ -54,20 +52,6 @@ class Scratch:
 
     def reserve(self, family: str, nbytes: int) -> None:
         self.get(family, nbytes)
-
-    def chain_sync(self) -> torch.Tensor:
-        """The tile-ready chaining slots (dspark_gemm_opts.chain_*), zero-filled."""
-        return self.get("chain", _lib.CHAIN_SLOTS * 128)
-
-    def chain_slot(self, key) -> int:
-        """A chaining slot reserved for one GEMM call site (stable per key)."""
-        s = self._chain_slots.get(key)
-        if s is None:
-            s = len(self._chain_slots)
-            if s >= _lib.CHAIN_SLOTS:
-                raise RuntimeError("out of GEMM chaining slots")
-            self._chain_slots[key] = s
-        return s
 
     def read_status_async(self) -> None:
         """Enqueue a copy of the status word into pinned host memory on the current stream
@@ -120,29 +104,9 @@ class RowNorm:
         self.w, self.eps, self.sumsq = w, float(eps), sumsq  # sumsq [rows, N/128 tiles]
 
 
-class Chain:
-    """Tile-ready chaining of a GEMM with the GEMMs launched right before / after it on the
-    same stream (dspark_gemm_opts.chain_*): `slot` counts this GEMM's finished tiles for the
-    next GEMM; `wait` (with `wait_tiles`, that GEMM's N/128) is the slot of the GEMM right
-    before, whose outputs this GEMM reads once all its tiles are finished."""
-
-    __slots__ = ("sync", "slot", "wait", "wait_tiles")
-
-    def __init__(self, scratch: "Scratch", slot: int | None = None, wait: int | None = None,
-                 wait_tiles: int = 0):
-        self.sync = scratch.chain_sync()
-        self.slot, self.wait, self.wait_tiles = slot, wait, int(wait_tiles)
-
-
 def _opts(prefetch: PackedLinear | None, norm: RowNorm | None,
-          sumsq_out: torch.Tensor | None, copy16: torch.Tensor | None = None,
-          chain: Chain | None = None) -> _lib.GemmOpts:
+          sumsq_out: torch.Tensor | None, copy16: torch.Tensor | None = None) -> _lib.GemmOpts:
     o = _lib.GemmOpts()
-    if chain is not None:
-        o.chain_sync = chain.sync.data_ptr()
-        o.chain_slot = 0 if chain.slot is None else chain.slot + 1
-        o.chain_wait = 0 if chain.wait is None else chain.wait + 1
-        o.chain_wait_tiles = chain.wait_tiles
     if copy16 is not None:
         assert copy16.dtype == torch.float16 and copy16.stride(1) == 1
         o.copy_f16 = copy16.data_ptr()
@@ -169,8 +133,7 @@ def _opts(prefetch: PackedLinear | None, norm: RowNorm | None,
 def gemm(x16: torch.Tensor, w: PackedLinear, y: torch.Tensor, *, epilogue=_lib.EPI_STORE_BF16,
          residual: torch.Tensor | None = None, scratch: Scratch, M: int | None = None,
          prefetch: PackedLinear | None = None, norm: RowNorm | None = None,
-         sumsq_out: torch.Tensor | None = None, copy16: torch.Tensor | None = None,
-         chain: Chain | None = None) -> torch.Tensor:
+         sumsq_out: torch.Tensor | None = None, copy16: torch.Tensor | None = None) -> torch.Tensor:
     """y = x16 @ W^T with the chosen epilogue (see include/dspark_b200.h). `prefetch`: the next
     projection's weights, warmed in L2 (up to PREFETCH_LIMIT bytes) during this GEMM's tail.
     `norm`: x16 is the bf16 residual stream and the GEMM consumes its RMSNorm. `sumsq_out`
@@ -184,13 +147,13 @@ def gemm(x16: torch.Tensor, w: PackedLinear, y: torch.Tensor, *, epilogue=_lib.E
     if sumsq_out is not None:  # written as a packed [M, N/128] block
         assert sumsq_out.is_contiguous() and tuple(sumsq_out.shape) == (M, w.N // 128)
     ws = scratch.get("gemm", gemm_workspace_bytes(M, w.N, K))
-    if norm is None and sumsq_out is None and copy16 is None and chain is None and \
+    if norm is None and sumsq_out is None and copy16 is None and \
             (prefetch is None or PREFETCH_LIMIT <= 0):
         call("dspark_w8a16_gemm", _p(x16), x16.stride(0), _p(w.q), _p(w.sb), M, w.N, K, _p(y),
              y.stride(0), _p(residual), residual.stride(0) if residual is not None else 0,
              epilogue, _p(ws), ws.numel(), _p(scratch.status), _stream())
         return y
-    opts = _opts(prefetch, norm, sumsq_out, copy16, chain)
+    opts = _opts(prefetch, norm, sumsq_out, copy16)
     call("dspark_w8a16_gemm_ex", _p(x16), x16.stride(0), _p(w.q), _p(w.sb), M, w.N, K, _p(y),
          y.stride(0), _p(residual), residual.stride(0) if residual is not None else 0, epilogue,
          ctypes.byref(opts), _p(ws), ws.numel(), _p(scratch.status), _stream())
@@ -251,8 +214,7 @@ def gemm_qkv_rope(x16: torch.Tensor, w: PackedLinear, *, T: int, Hq: int, Hkv: i
                   q_norm: torch.Tensor | None, k_norm: torch.Tensor, eps: float,
                   inv_freq: torch.Tensor, pos0: torch.Tensor, q_out: torch.Tensor | None,
                   kv: KvLayout, scratch: Scratch, M: int | None = None,
-                  prefetch: PackedLinear | None = None, norm: RowNorm | None = None,
-                  chain: Chain | None = None) -> None:
+                  prefetch: PackedLinear | None = None, norm: RowNorm | None = None) -> None:
     """The q|k|v GEMM with the per-head norm + RoPE + q / paged K/V writes in its epilogue
     (one launch; equals gemm(STORE_BF16) + qkv_rope_kv_write). `norm` as in gemm()."""
     _require_cuda(x16)
@@ -261,7 +223,7 @@ def gemm_qkv_rope(x16: torch.Tensor, w: PackedLinear, *, T: int, Hq: int, Hkv: i
     want = torch.bfloat16 if norm is not None else torch.float16
     assert x16.dtype == want and x16.shape[-1] >= K and w.N == (Hq + 2 * Hkv) * hd
     ws = scratch.get("gemm", gemm_workspace_bytes(M, w.N, K))
-    opts = _opts(prefetch, norm, None, chain=chain)
+    opts = _opts(prefetch, norm, None)
     call("dspark_w8a16_gemm_qkv_rope", _p(x16), x16.stride(0), _p(w.q), _p(w.sb), M, K, T, Hq,
          Hkv, hd, _p(q_norm), _p(k_norm), float(eps), _p(inv_freq), _p(pos0), _p(q_out), kv,
          ctypes.byref(opts), _p(ws), ws.numel(), _p(scratch.status), _stream())
@@ -459,69 +421,3 @@ def markov_sample_block_probs(base: torch.Tensor, rows_per_b: int, B: int, cap: 
          w2.K, _p(w1.q), _p(w1.sb), _p(w2.q), _p(w2.sb), _p(first_prev), _p(draft),
          _p(verify_ids), float(temperature), float(top_p), int(top_k or 0), _p(rng), _p(q_probs),
          q_probs.shape[-1], _p(ws), ws.numel(), _stream())
-
-
-# ----------------------------------------------------------------------------------------
-# K1s: a list of small-M W8 GEMMs, each fed by the one before it, as one persistent launch
-def gemm_job(x16: torch.Tensor, w: PackedLinear, y: torch.Tensor, *,
-             epilogue=_lib.EPI_STORE_BF16, residual: torch.Tensor | None = None,
-             norm: RowNorm | None = None, sumsq_out: torch.Tensor | None = None,
-             copy16: torch.Tensor | None = None, wait_prev: bool = True) -> StreamJob:
-    """One job of gemm_stream(): the gemm() call with the same arguments. `wait_prev`: the
-    inputs come from the previous job of the launch (False: from the kernel before it)."""
-    _require_cuda(x16, y)
-    want = torch.bfloat16 if norm is not None else torch.float16
-    assert x16.dtype == want and x16.shape[-1] >= w.K
-    j = StreamJob()
-    j.x, j.ldx, j.wq, j.wsb, j.N, j.K = x16.data_ptr(), x16.stride(0), _p(w.q), _p(w.sb), w.N, w.K
-    j.epilogue = int(epilogue)
-    j.y, j.ldy = y.data_ptr(), y.stride(0)
-    j.residual = _p(residual)
-    j.ldr = residual.stride(0) if residual is not None else 0
-    j.opts = _opts(None, norm, sumsq_out, copy16)
-    j.wait_prev = int(wait_prev)
-    return j
-
-
-def qkv_rope_job(x16: torch.Tensor, w: PackedLinear, *, T: int, Hq: int, Hkv: int, hd: int,
-                 q_norm: torch.Tensor | None, k_norm: torch.Tensor, eps: float,
-                 inv_freq: torch.Tensor, pos0: torch.Tensor, q_out: torch.Tensor | None,
-                 kv: KvLayout, norm: RowNorm | None = None, wait_prev: bool = True) -> StreamJob:
-    """One job of gemm_stream(): the gemm_qkv_rope() call with the same arguments."""
-    _require_cuda(x16)
-    want = torch.bfloat16 if norm is not None else torch.float16
-    assert x16.dtype == want and x16.shape[-1] >= w.K and w.N == (Hq + 2 * Hkv) * hd
-    j = StreamJob()
-    j.x, j.ldx, j.wq, j.wsb, j.N, j.K = x16.data_ptr(), x16.stride(0), _p(w.q), _p(w.sb), w.N, w.K
-    j.epilogue = _lib.EPI_QKV_ROPE
-    j.opts = _opts(None, norm, None)
-    j.wait_prev = int(wait_prev)
-    j.T, j.Hq, j.Hkv, j.hd = int(T), int(Hq), int(Hkv), int(hd)
-    j.q_norm_w, j.k_norm_w, j.eps = _p(q_norm), _p(k_norm), float(eps)
-    j.inv_freq, j.pos0, j.q_out, j.kv = _p(inv_freq), _p(pos0), _p(q_out), kv
-    return j
-
-
-def stream_workspace_bytes(M: int, jobs) -> int:
-    arr = (StreamJob * len(jobs))(*jobs)
-    return int(lib().dspark_w8a16_stream_workspace_bytes(M, arr, len(jobs)))
-
-
-STREAM_MAX_JOBS = 5
-
-
-def gemm_stream(M: int, jobs: list, scratch: Scratch) -> None:
-    """Run `jobs` (gemm_job / qkv_rope_job) in order as one launch of the persistent W8 kernel
-    (dspark_w8a16_stream): each job's weights stream while the job before it finishes, and its
-    activations are read once that job is complete. Outputs equal the separate calls'."""
-    arr = (StreamJob * len(jobs))(*jobs)
-    ws = scratch.get("stream", int(lib().dspark_w8a16_stream_workspace_bytes(M, arr, len(jobs))))
-    call("dspark_w8a16_stream", M, arr, len(jobs), _p(ws), ws.numel(), _p(scratch.status),
-         _stream())
-
-
-def stream_grid(M: int) -> int:
-    """CTAs of a dspark_w8a16_stream launch of M rows on the current device."""
-    g = ctypes.c_int()
-    call("dspark_w8a16_stream_grid", int(M), ctypes.byref(g))
-    return g.value

@@ -255,14 +255,6 @@ class Target:
                       M=T, copy16=copy16)
 
     # ------------------------------------------------------------------ the forward
-    # Run the GEMMs between two attention kernels (o, gate|up, down and the next layer's q|k|v,
-    # or the head after the last layer) as one dspark_w8a16_stream launch: each projection's
-    # weights stream while the one before it finishes. Outputs are bit-identical to the
-    # separate launches (same work split, same summation order).
-    use_stream = False
-    # consecutive GEMMs of a layer (o -> gate|up -> down -> next q|k|v or head) wait on the
-    # previous GEMM's finished-tile count instead of its grid's completion
-    chain_gemms = True
     # the q|k|v GEMM runs the per-head norm + RoPE + KV write in its epilogue (one launch
     # instead of two; bit-identical outputs)
     fuse_qkv_rope = True
@@ -275,8 +267,6 @@ class Target:
                 with_logits: bool = True) -> None:
         """Run B x T tokens (ids already in buf.ids) at positions state.seq_len[b] + t.
         Writes KV for all T positions; does not advance seq_len."""
-        if self.use_stream and self.fuse_norm and self.fuse_qkv_rope:
-            return self._forward_stream(buf, state, tap, splits=splits, with_logits=with_logits)
         c, sc = self.cfg, self.scratch
         B, T, M = buf.B, buf.T, buf.M
         splits = splits or self.attn_splits(B, state.max_pages)
@@ -287,63 +277,41 @@ class Target:
         fuse = self.fuse_norm
         ss = buf.sumsq if fuse else None
         ops.embed(buf.ids, self.embed, buf.h, M, sumsq=ss)
-        chain = self.chain_gemms and fuse and self.fuse_qkv_rope
-
-        def link(l, name, prev=None, tiles=0, own=True):
-            """The Chain of GEMM `name` of layer l: its own counting slot, and the slot of the
-            GEMM right before it (`prev`, `tiles` of them) whose outputs it reads."""
-            if not chain:
-                return None
-            return ops.Chain(sc, sc.chain_slot(("target", l, name)) if own else None,
-                             None if prev is None else sc.chain_slot(("target",) + prev), tiles)
-
-        prev_down = None
         for l, L in enumerate(self.layers):
             kv = state.layout(l)
             # each GEMM warms L2 with the next GEMM's weights (the head after the last layer)
             nxt = self.layers[l + 1].qkv if l + 1 < n_layers else (self.head if with_logits else None)
             if fuse:
                 self._qkv_rope(buf, L, kv, state, B, T, M, x=buf.h,
-                               norm=ops.RowNorm(L.input_ln, eps, ss),
-                               chain=link(l, "qkv", prev_down, self.layers[l - 1].down.N // 128
-                                          if l else 0, own=False) if prev_down else None)
+                               norm=ops.RowNorm(L.input_ln, eps, ss))
             else:
                 ops.rmsnorm(buf.h, L.input_ln, eps, y16=buf.xn16, M=M)
                 self._qkv_rope(buf, L, kv, state, B, T, M)
             ops.attention(buf.q, B, T, c.num_attention_heads, kv, state.seq_len, True,
                           self.scale, buf.attn16, splits, sc)
             ops.gemm(buf.attn16, L.o, buf.h, epilogue=EPI_RESIDUAL_BF16, residual=buf.h,
-                     scratch=sc, M=M, prefetch=L.gu, sumsq_out=ss, chain=link(l, "o"))
+                     scratch=sc, M=M, prefetch=L.gu, sumsq_out=ss)
             if fuse:
                 ops.gemm(buf.h, L.gu, buf.act16, epilogue=EPI_SILU_MUL_F16, scratch=sc, M=M,
-                         prefetch=L.down, norm=ops.RowNorm(L.post_ln, eps, ss),
-                         chain=link(l, "gu", (l, "o"), L.o.N // 128))
+                         prefetch=L.down, norm=ops.RowNorm(L.post_ln, eps, ss))
             else:
                 ops.rmsnorm(buf.h, L.post_ln, eps, y16=buf.xn16, M=M)
                 ops.gemm(buf.xn16, L.gu, buf.act16, epilogue=EPI_SILU_MUL_F16, scratch=sc, M=M,
                          prefetch=L.down)
             # the drafter's tap of this layer's output is written by the same epilogue
             tap16 = buf.fused16[:M, tap_idx[l] * H:(tap_idx[l] + 1) * H] if l in tap_idx else None
-            last = l + 1 == n_layers
             ops.gemm(buf.act16, L.down, buf.h, epilogue=EPI_RESIDUAL_BF16, residual=buf.h,
-                     scratch=sc, M=M, prefetch=nxt, sumsq_out=ss, copy16=tap16,
-                     chain=link(l, "down", (l, "gu"), L.gu.N // 128,
-                                own=not last or with_logits))
-            prev_down = (l, "down") if chain else None
+                     scratch=sc, M=M, prefetch=nxt, sumsq_out=ss, copy16=tap16)
         if with_logits:
             if fuse:
                 ops.gemm(buf.h, self.head, buf.logits, epilogue=EPI_STORE_BF16, scratch=sc, M=M,
-                         norm=ops.RowNorm(self.norm, eps, ss),
-                         chain=link(n_layers, "head", prev_down,
-                                    self.layers[-1].down.N // 128, own=False)
-                         if prev_down else None)
+                         norm=ops.RowNorm(self.norm, eps, ss))
             else:
                 ops.rmsnorm(buf.h, self.norm, eps, y16=buf.xn16, M=M)
                 ops.gemm(buf.xn16, self.head, buf.logits, epilogue=EPI_STORE_BF16, scratch=sc, M=M)
 
     def _qkv_rope(self, buf: Buffers, L, kv, state: CacheState, B: int, T: int, M: int,
-                  x: torch.Tensor | None = None, norm: "ops.RowNorm | None" = None,
-                  chain: "ops.Chain | None" = None) -> None:
+                  x: torch.Tensor | None = None, norm: "ops.RowNorm | None" = None) -> None:
         """q|k|v projection of x (buf.xn16, or the bf16 residual stream with its fused input
         norm), per-head q/k norm + RoPE at state.seq_len, q into buf.q and K/V into the layer's
         paged cache."""
@@ -354,54 +322,13 @@ class Target:
                               Hkv=c.num_key_value_heads, hd=c.head_dim, q_norm=L.q_norm,
                               k_norm=L.k_norm, eps=c.rms_norm_eps, inv_freq=self.inv_freq,
                               pos0=state.seq_len, q_out=buf.q, kv=kv, scratch=sc, M=M,
-                              prefetch=L.o, norm=norm, chain=chain)
+                              prefetch=L.o, norm=norm)
             return
         ops.gemm(x, L.qkv, buf.qkv, epilogue=EPI_STORE_BF16, scratch=sc, M=M, prefetch=L.o,
                  norm=norm)
         ops.qkv_rope_kv_write(buf.qkv, B, T, c.num_attention_heads, c.num_key_value_heads,
                               c.head_dim, L.q_norm, L.k_norm, c.rms_norm_eps, self.inv_freq,
                               state.seq_len, buf.q, kv)
-
-    def _qkv_job(self, buf: Buffers, L, state: CacheState, l: int, wait_prev: bool):
-        """The q|k|v + RoPE + KV write of layer l as a stream job: input norm fused, from the
-        residual stream and its row sums of squares."""
-        c = self.cfg
-        return ops.qkv_rope_job(buf.h, L.qkv, T=buf.T, Hq=c.num_attention_heads,
-                                Hkv=c.num_key_value_heads, hd=c.head_dim, q_norm=L.q_norm,
-                                k_norm=L.k_norm, eps=c.rms_norm_eps, inv_freq=self.inv_freq,
-                                pos0=state.seq_len, q_out=buf.q, kv=state.layout(l),
-                                norm=ops.RowNorm(L.input_ln, c.rms_norm_eps, buf.sumsq),
-                                wait_prev=wait_prev)
-
-    def _forward_stream(self, buf: Buffers, state: CacheState, tap=(), *,
-                        splits: int | None = None, with_logits: bool = True) -> None:
-        """forward() with the GEMMs between attention kernels as dspark_w8a16_stream launches:
-        embed -> [q|k|v 0] -> per layer: attention, then [o, gate|up, down (+tap), next q|k|v
-        or the head]. Three launches per layer (attention is two)."""
-        c, sc = self.cfg, self.scratch
-        B, T, M = buf.B, buf.T, buf.M
-        splits = splits or self.attn_splits(B, state.max_pages)
-        tap_idx = {l: j for j, l in enumerate(tap)}
-        H, eps, n = c.hidden_size, c.rms_norm_eps, len(self.layers)
-        ss = buf.sumsq
-        ops.embed(buf.ids, self.embed, buf.h, M, sumsq=ss)
-        ops.gemm_stream(M, [self._qkv_job(buf, self.layers[0], state, 0, False)], sc)
-        for l, L in enumerate(self.layers):
-            ops.attention(buf.q, B, T, c.num_attention_heads, state.layout(l), state.seq_len, True,
-                          self.scale, buf.attn16, splits, sc)
-            tap16 = buf.fused16[:M, tap_idx[l] * H:(tap_idx[l] + 1) * H] if l in tap_idx else None
-            jobs = [ops.gemm_job(buf.attn16, L.o, buf.h, epilogue=EPI_RESIDUAL_BF16, residual=buf.h,
-                                 sumsq_out=ss, wait_prev=False),
-                    ops.gemm_job(buf.h, L.gu, buf.act16, epilogue=EPI_SILU_MUL_F16,
-                                 norm=ops.RowNorm(L.post_ln, eps, ss)),
-                    ops.gemm_job(buf.act16, L.down, buf.h, epilogue=EPI_RESIDUAL_BF16,
-                                 residual=buf.h, sumsq_out=ss, copy16=tap16)]
-            if l + 1 < n:
-                jobs.append(self._qkv_job(buf, self.layers[l + 1], state, l + 1, True))
-            elif with_logits:
-                jobs.append(ops.gemm_job(buf.h, self.head, buf.logits, epilogue=EPI_STORE_BF16,
-                                         norm=ops.RowNorm(self.norm, eps, ss)))
-            ops.gemm_stream(M, jobs, sc)
 
     # ------------------------------------------------------------------ reference API
     def run(self, ids, cache: TargetCache, tap):

@@ -161,7 +161,6 @@ class TPTarget(Target):
     process per GPU) for device tensors; every rank runs the same decode loop."""
 
     capturable = False  # rounds with collectives run eagerly
-    use_stream = False  # the all-reduces sit between the projections (own forward)
     # o_proj / down_proj of verify-sized calls (M <= 64) all-reduce through the fused GEMM
     # epilogue over NVLink peer memory; False, or larger calls (prefill chunks): NCCL
     fused_allreduce = True

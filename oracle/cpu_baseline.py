@@ -44,6 +44,13 @@ def _gemv_lib():
     return _GEMV or None
 
 
+def linear_kind() -> str:
+    """How the timed decode computes its W8 linears (for the baseline's sample description)."""
+    if _gemv_lib() is not None:
+        return "int8 weights read once per step by the threaded C group-64 GEMV of oracle/cpu_gemv.c"
+    return "int8 weights dequantized per step in torch (oracle/cpu_gemv.c not built)"
+
+
 class StreamingDecoder:
     """One-token decode of a TargetWeights on the CPU with a dense per-layer KV cache."""
 

@@ -67,21 +67,6 @@ def test_pack_rejects_values_fp16_cannot_hold():
         pack(qt, device="cpu")
 
 
-def test_stream_job_struct_matches_the_c_layout():
-    import ctypes
-    from mlx_dspark_b200 import _lib
-    assert ctypes.sizeof(_lib.StreamJob) == _lib.lib().dspark_stream_job_size()
-    L = _lib.lib()
-    jobs = (_lib.StreamJob * 6)()
-    for j in jobs:
-        j.N, j.epilogue = 4096, 0
-    one = L.dspark_w8a16_stream_workspace_bytes(9, jobs, 1)
-    assert L.dspark_w8a16_stream_workspace_bytes(9, jobs, 5) - one == 4 * 32 * 9 * 128 * 8
-    assert L.dspark_w8a16_stream_workspace_bytes(9, jobs, 6) == 0
-    rc = L.dspark_w8a16_stream(9, None, 0, None, 0, None, None)
-    assert rc == 1 and b"jobs" in L.dspark_last_error()
-
-
 def test_gemm_opts_struct_matches_the_c_layout():
     import ctypes
     from mlx_dspark_b200 import _lib
