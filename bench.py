@@ -459,6 +459,118 @@ def run_tp_allreduce(world, rank):
     return 0
 
 
+def run_tp(args, world, rank):
+    """C5: one Qwen3-32B W8 request tensor-parallel over the `world` ranks (one process per
+    GPU; o_proj / down_proj row-split with an all-reduce after each), DSpark drafting
+    replicated on every rank. The same session is timed with the fused peer all-reduce (the
+    default) and with NCCL, eager rounds (rounds with collectives are not captured), CUDA
+    events, max over ranks."""
+    from mlx_dspark_b200 import _lib
+    from mlx_dspark_b200.config import TARGETS, WORKLOADS, dspark_for, with_layers
+    from mlx_dspark_b200.generate import SpecSession, greedy_generate, prefill_rows, speculative_generate
+    from mlx_dspark_b200.model import DSparkDrafter
+    from mlx_dspark_b200.tp import TPTarget
+    from mlx_dspark_b200.weights import generate_dspark, generate_target
+
+    wl = WORKLOADS[args.workload]
+    K, W = args.steps, args.warmup
+    dev = torch.device("cuda", torch.cuda.current_device())
+    tcfg = TARGETS[wl.target]
+    if args.layers:
+        tcfg = with_layers(tcfg, args.layers)
+    dcfg = dspark_for(tcfg, block_size=wl.block_size)
+    tw = generate_target(tcfg, wl.seed, "cuda")
+    target = TPTarget(tw, rank, world, kv_bits=wl.kv_bits, device=dev)
+    del tw
+    drafter = DSparkDrafter(generate_dspark(dcfg, wl.seed, "cuda"), target)
+    torch.cuda.empty_cache()
+    cap = wl.block_size
+    prompt_len = args.prompt_len or wl.prompt_len
+    V = tcfg.vocab_size
+    prompt = torch.randint(0, V, (prompt_len,), generator=torch.Generator().manual_seed(wl.seed)).tolist()
+    rounds = 3 * (K + W) + 4
+    ref_len = rounds * (cap + 1) + 16
+    ref = greedy_generate(target, None, prompt_ids=prompt, max_new_tokens=ref_len).token_ids
+    p_agree = wl.accept_p or 0.7
+    agree = (torch.rand(1, max(rounds, 256), cap, generator=torch.Generator().manual_seed(7))
+             < p_agree).to(torch.uint8)
+    override = {"ref": torch.tensor([ref]), "agree": agree, "prompt_len": [prompt_len]}
+    sess = SpecSession(target, drafter, 1, cap, prompt_len + ref_len + 64, override=override)
+    last = prefill_rows(target, prompt, sess.tstate, sess.tap, drafter, sess.cstate)
+    sess.pending.fill_(target.argmax_row(last))   # (the whole vocabulary's argmax under TP)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(torch.cuda.current_device())
+    clocks.start()
+    modes, launches = {}, 0
+    try:
+        for mode in ("nccl_graph", "nccl", "fused"):
+            # nccl_graph (the default): the whole round as one CUDA graph, the NCCL collectives
+            # captured with it; nccl: the same launches eagerly; fused: the peer all-reduce
+            # (host-side epochs: eager)
+            target.fused_allreduce = mode == "fused"
+            graph = mode == "nccl_graph"
+            if graph:
+                sess.step(use_graph=False)
+                torch.cuda.synchronize()
+                barrier(world)
+                sess.capture()
+            for _ in range(W):
+                sess.step(use_graph=graph)
+            torch.cuda.synchronize()
+            barrier(world)
+            len0 = int(sess.tstate.seq_len[0])
+            n0 = _lib.LAUNCHES["n"]
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(K):
+                sess.step(use_graph=graph)
+            b.record()
+            torch.cuda.synchronize()
+            ms = allreduce_max(a.elapsed_time(b), world)
+            tokens = int(sess.tstate.seq_len[0]) - len0
+            launches = _lib.LAUNCHES["n"] - n0 if mode == "nccl" else launches
+            modes[mode] = {"tok_s": round(tokens / (ms / 1000.0), 2),
+                           "round_us": round(ms * 1000.0 / K, 1),
+                           "mean_accept_len": round(tokens / K, 3)}
+        target.scratch.check_status()
+        target.fused_allreduce = False
+        sess.graph = None
+        res = speculative_generate(target, None, drafter, lookup_drafts=False, prompt_ids=prompt,
+                                   max_new_tokens=min(128, ref_len - 16), max_draft_tokens=cap,
+                                   draft_override=override)
+    finally:
+        clk = clocks.stop()
+        sess.graph = None        # a graph holding NCCL calls goes before the process group
+        torch.cuda.synchronize()
+        sess.release()
+        target.release_peer()
+    e2e_tps = allreduce_max((res.num_tokens - 1) / res.decode_seconds, world)
+    per_rank = gather_all({"rank": rank, "sm_mhz": clk.get("sm_mhz"), "reasons": clk.get("reasons")},
+                          world)
+    f = modes["nccl_graph"]
+    return {
+        "metric": "accepted tok/s Qwen3-32B W8 DSpark, one request tensor-parallel over N GPUs",
+        "value": f["tok_s"], "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": round(f["round_us"] / 1000.0, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None,
+        "dtype": "w8a16 (int8 weights, fp16 MMA, fp32 accumulate, bf16 activations)",
+        "data": "synthetic: random-init W8 g64 weights (seed 1), random prompt ids, "
+                "Bernoulli(0.7) draft-agree mask over the target's own greedy continuation",
+        "config": {"workload": wl.name, "model": f"Qwen3-32B-arch W8 g64 ({tcfg.num_hidden_layers} "
+                   f"layers) + DSpark 1-layer block 8", "global_batch": 1, "prompt_len": prompt_len,
+                   "draft_cap": cap, "parallelism": f"tp{world}",
+                   "l2": "inputs larger than L2 (32 GB of weights / N per GPU per round)"},
+        "round_us": f["round_us"], "mean_accept_len": f["mean_accept_len"],
+        "allreduce": {"nccl_graph": f, "nccl_eager": modes["nccl"], "fused_peer_eager": modes["fused"]},
+        "gpu_launches": launches, "clocks": clk, "per_rank": per_rank,
+        "e2e": {"value": round(e2e_tps, 2), "unit": "tok/s", "h2d_bytes_per_step": 4,
+                "d2h_bytes_per_step": 4 * (cap + 3),
+                "api": "mlx_dspark_b200.speculative_generate (host loop, captured rounds, NCCL)",
+                "rounds": res.num_rounds, "mean_accept_len": round(res.mean_accept_len, 3)},
+    }
+
+
 def run_serve(args):
     """C4 continuous batching: 32 requests (a shared random 2048-token prefix plus a random
     64-2048-token suffix, 128-1024 output tokens) over N GPUs, one ReplicaPool worker process
@@ -572,7 +684,7 @@ def run_ours(args, world, rank):
     budget = prompt_len + ref_len + 64
     sess = SpecSession(target, drafter, 1, cap, budget, override=override)
     last = prefill_rows(target, prompt, sess.tstate, sess.tap, drafter, sess.cstate)
-    sess.pending.fill_(int(last.float().argmax()))
+    sess.pending.fill_(target.argmax_row(last))   # (the whole vocabulary's argmax under TP)
     torch.cuda.synchronize()
     # one eager round (counts launches, sizes every workspace), then capture
     n0 = _lib.LAUNCHES["n"]
@@ -723,7 +835,10 @@ def main():
     if args.tp_allreduce:
         return run_tp_allreduce(world, rank)
     try:
-        out = run_ours(args, world, rank)
+        if args.workload == "C5" and world > 1:
+            out = run_tp(args, world, rank)
+        else:
+            out = run_ours(args, world, rank)
         if rank == 0:
             print(json.dumps(out), flush=True)
     finally:

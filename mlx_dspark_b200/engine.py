@@ -80,8 +80,10 @@ class Engine:
         self.prefix_cache_slots = max(1, int(prefix_cache_slots))
         self.default_max_tokens = default_max_tokens
         self.max_tokens_cap = max_tokens_cap
-        self._executor = executor or ThreadPoolExecutor(max_workers=1,
-                                                        thread_name_prefix="dspark-device")
+        # the CUDA current device is per thread: the device thread runs on the target's
+        self._executor = executor or ThreadPoolExecutor(
+            max_workers=1, thread_name_prefix="dspark-device",
+            initializer=_bind_device, initargs=(getattr(target, "device", None),))
         self.prefix = self._make_prefix_cache(prefix_cache)
         self.created = int(time.time())
         self.stats = {"requests": 0, "prompt_tokens": 0, "completion_tokens": 0,
@@ -402,6 +404,14 @@ def maybe_batch_engine(engine: Engine, max_batch: int):
 
 
 # -------------------------------------------------------------------------------------------
+def _bind_device(device) -> None:
+    """Make `device` (a CUDA device) the calling thread's current device."""
+    import torch
+    dev = torch.device(device) if device is not None else None
+    if dev is not None and dev.type == "cuda":
+        torch.cuda.set_device(dev)
+
+
 def _replica_main(index: int, device, factory, inbox, outbox) -> None:
     """Worker process of a ReplicaPool: build the serving object on `device`, then answer
     (id, prompt_ids, params) messages from `inbox` on `outbox` until it receives None."""

@@ -127,12 +127,14 @@ def capture_graph(fn) -> torch.cuda.CUDAGraph:
     """Record fn()'s launches into a CUDA graph on a side stream. capture_begin/capture_end
     directly: the torch.cuda.graph context also empties the caching allocator on entry, which
     frees every cached block (seconds after a large session is released) and would land inside
-    the first decode round."""
+    the first decode round. Thread-local capture mode: a serving process captures on its device
+    thread while other threads (request intake, the NCCL watchdog) keep making CUDA calls of
+    their own, which the global mode would count against the capture."""
     g = torch.cuda.CUDAGraph()
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(s):
-        g.capture_begin()
+        g.capture_begin(capture_error_mode="thread_local")
         try:
             fn()
         finally:
@@ -216,7 +218,7 @@ class SpecSession:
         self.B, self.cap = B, cap
         self.max_cap = max(cap, int(max_cap or cap))
         self.sampling = sampling if (sampling is not None and sampling.active) else None
-        if self.sampling is not None and not target.capturable:
+        if self.sampling is not None and getattr(target, "world", 1) > 1:
             raise NotImplementedError("sampled decoding of a tensor-parallel target is not built")
         # OpenAI presence / frequency penalties on the target rows (_Penalizer,
         # generate.py:179-228): completion-token counts per row live on the device
@@ -544,6 +546,8 @@ class GreedySession:
             self.counts = torch.zeros(B, target.cfg.vocab_size, dtype=torch.int32,
                                       device=target.device)
         self.sampling = sampling if (sampling is not None and sampling.active) else None
+        if self.sampling is not None and getattr(target, "world", 1) > 1:
+            raise NotImplementedError("sampled decoding of a tensor-parallel target is not built")
         self.rng = ops.rng_state(list(seeds) if seeds is not None else [0] * B, target.device)
         dev = target.device
         cap_tokens = max_tokens + 64

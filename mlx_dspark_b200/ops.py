@@ -40,7 +40,10 @@ class Scratch:
         self.bufs: dict[str, torch.Tensor] = {}
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.version = 0  # bumped when a buffer moves (captured graphs hold the addresses)
-        self._status_host = None
+        # pinned copy of the status word, allocated here: a pinned allocation inside a CUDA
+        # graph capture (the first read_status_async of a captured round) invalidates it
+        self._status_host = (torch.zeros(1, dtype=torch.int32, pin_memory=True)
+                             if self.device.type == "cuda" else None)
 
     def get(self, family: str, nbytes: int) -> torch.Tensor:
         b = self.bufs.get(family)
@@ -59,8 +62,6 @@ class Scratch:
         next to their per-round plan read and raise_on_status() after that round's sync, so a
         bounded device wait that ran out fails the round instead of letting it commit tokens
         computed from stale data."""
-        if self._status_host is None:
-            self._status_host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
         self._status_host.copy_(self.status, non_blocking=True)
 
     def raise_on_status(self) -> None:

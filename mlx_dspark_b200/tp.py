@@ -160,10 +160,17 @@ class TPTarget(Target):
     """One rank's share of a tensor-parallel target. The process group must be NCCL (one
     process per GPU) for device tensors; every rank runs the same decode loop."""
 
-    capturable = False  # rounds with collectives run eagerly
-    # o_proj / down_proj of verify-sized calls (M <= 64) all-reduce through the fused GEMM
-    # epilogue over NVLink peer memory; False, or larger calls (prefill chunks): NCCL
-    fused_allreduce = True
+    # o_proj / down_proj all-reduce. False (default): NCCL, captured with the rest of the round
+    # into one CUDA graph. True: verify-sized calls (M <= 64) through the fused GEMM epilogue
+    # over NVLink peer memory (dspark_w8a16_gemm_peer), whose host-side epochs keep those rounds
+    # eager; measured on Qwen3-32B at TP2 (16k context) it is the slower form: 13.5 ms per
+    # round against 12.6 ms for eager NCCL and 11.7 ms for captured NCCL. Prefill chunks
+    # (M > 64) always use NCCL.
+    fused_allreduce = False
+
+    @property
+    def capturable(self) -> bool:
+        return not self.fused_allreduce
 
     def __init__(self, weights: TargetWeights, rank: int, world: int, group=None, tokenizer=None,
                  *, kv_bits: int | None = None, device="cuda"):
