@@ -503,12 +503,12 @@ def run_tp(args, world, rank):
     clocks.start()
     modes, launches = {}, 0
     try:
-        for mode in ("nccl_graph", "nccl", "fused"):
-            # nccl_graph (the default): the whole round as one CUDA graph, the NCCL collectives
-            # captured with it; nccl: the same launches eagerly; fused: the peer all-reduce
-            # (host-side epochs: eager)
-            target.fused_allreduce = mode == "fused"
-            graph = mode == "nccl_graph"
+        for mode in ("fused_graph", "nccl_graph", "fused_eager"):
+            # fused_graph (the default): the whole round as one CUDA graph with the fused peer
+            # all-reduce; nccl_graph: the same with NCCL all-reduces captured in it;
+            # fused_eager: the default's launches without the graph
+            target.fused_allreduce = mode.startswith("fused")
+            graph = mode.endswith("_graph")
             if graph:
                 sess.step(use_graph=False)
                 torch.cuda.synchronize()
@@ -529,12 +529,12 @@ def run_tp(args, world, rank):
             torch.cuda.synchronize()
             ms = allreduce_max(a.elapsed_time(b), world)
             tokens = int(sess.tstate.seq_len[0]) - len0
-            launches = _lib.LAUNCHES["n"] - n0 if mode == "nccl" else launches
+            launches = _lib.LAUNCHES["n"] - n0 if mode == "fused_eager" else launches
             modes[mode] = {"tok_s": round(tokens / (ms / 1000.0), 2),
                            "round_us": round(ms * 1000.0 / K, 1),
                            "mean_accept_len": round(tokens / K, 3)}
         target.scratch.check_status()
-        target.fused_allreduce = False
+        target.fused_allreduce = True
         sess.graph = None
         res = speculative_generate(target, None, drafter, lookup_drafts=False, prompt_ids=prompt,
                                    max_new_tokens=min(128, ref_len - 16), max_draft_tokens=cap,
@@ -548,7 +548,7 @@ def run_tp(args, world, rank):
     e2e_tps = allreduce_max((res.num_tokens - 1) / res.decode_seconds, world)
     per_rank = gather_all({"rank": rank, "sm_mhz": clk.get("sm_mhz"), "reasons": clk.get("reasons")},
                           world)
-    f = modes["nccl_graph"]
+    f = modes["fused_graph"]
     return {
         "metric": "accepted tok/s Qwen3-32B W8 DSpark, one request tensor-parallel over N GPUs",
         "value": f["tok_s"], "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
@@ -562,11 +562,12 @@ def run_tp(args, world, rank):
                    "draft_cap": cap, "parallelism": f"tp{world}",
                    "l2": "inputs larger than L2 (32 GB of weights / N per GPU per round)"},
         "round_us": f["round_us"], "mean_accept_len": f["mean_accept_len"],
-        "allreduce": {"nccl_graph": f, "nccl_eager": modes["nccl"], "fused_peer_eager": modes["fused"]},
+        "allreduce": {"fused_peer_graph": f, "nccl_graph": modes["nccl_graph"],
+                      "fused_peer_eager": modes["fused_eager"]},
         "gpu_launches": launches, "clocks": clk, "per_rank": per_rank,
         "e2e": {"value": round(e2e_tps, 2), "unit": "tok/s", "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": 4 * (cap + 3),
-                "api": "mlx_dspark_b200.speculative_generate (host loop, captured rounds, NCCL)",
+                "api": "mlx_dspark_b200.speculative_generate (host loop, captured rounds)",
                 "rounds": res.num_rounds, "mean_accept_len": round(res.mean_accept_len, 3)},
     }
 

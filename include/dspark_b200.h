@@ -145,11 +145,14 @@ size_t dspark_gemm_opts_size(void); /* sizeof(dspark_gemm_opts), for bindings to
  * all-reduce number `epoch` (1, 2, ...; slot = epoch & 1):
  *   - dspark_w8a16_gemm_peer: the CTA that finishes output tile t stores its fp32 tile (rows
  *     < M, columns 128t..128t+127) into recv_r[slot][rank] of every rank r with plain
- *     stores over NVLink, then, after a system-scope fence, writes epoch into
- *     flags_r[slot][rank][t] with a system-scope release store. No TMA and no multicast.
+ *     stores over NVLink, then, after a system-scope acq_rel fence, writes epoch into
+ *     flags_r[slot][rank][t] with relaxed system-scope stores. No TMA and no multicast.
  *   - dspark_peer_reduce_residual: on each rank, CTA t waits (acquire loads, bounded by
  *     timeout_ns, DSPARK_ERR_TIMEOUT in *status on expiry) until flags[slot][r][t] == epoch for
  *     every r, then h[m, n] = bf16(h[m, n] + bf16(sum over r in rank order of recv[slot][r][m][n])).
+ *     It does not wait for the GEMM's grid to complete (the flags carry its inputs), so a tile
+ *     is summed as soon as every rank has finished it; it must follow the GEMM on the stream,
+ *     with h last written by a kernel that completed before the GEMM started.
  * Two slots keep epoch e + 2's stores out of a slot a peer may still read for epoch e: a rank
  * issues them only after its own reduce for e + 1 has seen every peer's flags for e + 1, which
  * each peer raises after its reduce for e. Every rank calls both, in the same order, every epoch.
@@ -161,8 +164,13 @@ typedef struct dspark_peer_ar {
   int rank;
   int m_cap;       /* rows per rank slot in recv */
   int n;           /* columns (the projection's N, a multiple of 128) */
-  int epoch;       /* this all-reduce's number, >= 1 */
+  int epoch;       /* this all-reduce's number, >= 1 (ignored when epoch_dev is set) */
   int reserved;
+  int* epoch_dev;  /* NULL, or 2 zero-initialised ints on this rank's device: [0] the number
+                    * of the last finished all-reduce, [1] scratch. The call's epoch is then
+                    * epoch_dev[0] + 1, read on the device, and the reduce stores it back when
+                    * every CTA is past its waits, so a CUDA graph of the calls replays with
+                    * fresh epochs. */
 } dspark_peer_ar;
 /* cudaMalloc'd, zero-filled memory for recv / flags (IPC needs its own allocation), and its
  * release. These two entry points allocate; nothing else in the library does. */
@@ -291,25 +299,11 @@ int dspark_w8a16_gemm_qkv_rope(const void* x, int ldx, const uint8_t* wq, const 
  *               model.py:130-156, dflash_model.py:100-134)
  * q   : bf16 [B*T, Hq*hd]; out: fp16 [B*T, ldo] (bf16-rounded, the o_proj GEMM input)
  * workspace: dspark_attention_workspace_bytes(...) bytes for the split partials.
- * Splits (at most max_splits, at least one page each) are merged in split order in one of
- * three forms (with one split the attention launch writes the output directly):
- *   - two launches (merge mode 0, default): partials merged by a second kernel;
- *   - one launch (mode 2, when status is non-NULL and max_splits*Hkv*B CTAs fit on the device
- *     at once, else two launches): each split stores its partial, waits (bounded:
- *     DSPARK_ERR_TIMEOUT in *status) until its siblings have, then finishes a slice of the
- *     query rows with the same arithmetic as the second kernel; no faster on B200 (PDL hides
- *     the second launch);
- *   - one launch, cluster form (mode 1): the S splits of a (row, kv head) run as one thread
- *     block cluster (S a power of two <= 16) and merge through distributed shared memory; used
- *     when the block table has at most 4 pages per split and B*Hkv clusters are resident at
- *     once, else two launches. Slower on B200 (clusters cannot start on SMs as the previous
- *     kernel drains).
+ * Splits (at most max_splits, at least one page each) are merged in split order by a second
+ * launch; with one split the attention launch writes the output directly. `status` is
+ * accepted for symmetry with the other entry points (nothing in attention waits).
  * ------------------------------------------------------------------------------------- */
 size_t dspark_attention_workspace_bytes(int B, int T, int Hq, int Hkv, int hd, int max_splits);
-/* Process-wide choice of the merge form: 0 (default) two launches, 1 cluster form where it
- * applies, 2 in-kernel where it applies (no reference counterpart; for A/B tests and
- * measurements). */
-int dspark_attention_merge_mode(int mode);
 int dspark_attention(const void* q, int B, int T, int Hq, const dspark_kv_layout* kv,
                      const int32_t* kv_len, int causal, float scale, void* out, int ldo,
                      int max_splits, void* workspace, size_t workspace_bytes, int* status,

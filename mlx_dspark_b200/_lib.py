@@ -48,7 +48,7 @@ class PeerAR(ctypes.Structure):
     all-reduce."""
     _fields_ = [("recv", c_void_p * 8), ("flags", c_void_p * 8), ("world", c_int),
                 ("rank", c_int), ("m_cap", c_int), ("n", c_int), ("epoch", c_int),
-                ("reserved", c_int)]
+                ("reserved", c_int), ("epoch_dev", c_void_p)]
 
 
 # name -> (restype, argtypes); mirrors include/dspark_b200.h
@@ -83,7 +83,6 @@ SIGNATURES = {
                                  c_size_t, P, P]),
     "dspark_gemm_opts_size": (c_size_t, []),
     "dspark_attention_workspace_bytes": (c_size_t, [I, I, I, I, I, I]),
-    "dspark_attention_merge_mode": (I, [I]),
     "dspark_attention": (I, [P, I, I, I, POINTER(KvLayout), P, I, c_float, P, I, I, P,
                              c_size_t, P, P]),
     "dspark_accept_workspace_bytes": (c_size_t, [I, I]),

@@ -6,14 +6,11 @@
 // to bf16 in shared memory). Scores and P.V run on bf16 m16n8k16 tensor-core MMAs with an
 // fp32 online softmax. Splits cover disjoint page ranges whose length is computed on the
 // device from kv_len, so the same launch serves every context length inside a CUDA graph.
-// Merging the per-split (max, sum, O) partials, in split order, into the bf16-rounded output
-// (written as fp16, the o_proj input) takes one of two forms:
-//   - two-kernel form (default): partials in the workspace, merged by attn_combine_kernel;
-//   - cluster form (opt-in, dspark_attention_merge_mode(1)): the splits of one (row, kv head)
-//     are one thread-block cluster; each CTA keeps its partial in shared memory and, after a
-//     cluster barrier, finishes a slice of the query rows by reading every split's partial
-//     through distributed shared memory (used where the block table holds at most 4 pages per
-//     split and one wave of clusters fits; otherwise the two-kernel form).
+// The per-split (max, sum, O) partials go to the workspace and attn_combine_kernel merges them,
+// in split order, into the bf16-rounded output (written as fp16, the o_proj input); a context
+// that fits one split is written directly. (Merging inside the attention kernel, through a
+// thread-block cluster or through a bounded wait on sibling splits, measured no faster: the
+// second launch hides under programmatic dependent launch.)
 //
 // Semantics follow mx.fast.scaled_dot_product_attention as called from the reference:
 // fp32 scores q.k * scale, fp32 softmax, output rounded to bf16; masks as in
@@ -85,12 +82,7 @@ struct Args {
   int ldo;
   float* ws_o;   // [B*Hkv][nsplit][R][HD]
   float* ws_ml;  // [B*Hkv][nsplit][R][2]
-  int* counters; // [B*Hkv] arrivals, then [B*Hkv] merges done (in-kernel merge form)
-  int* status;   // DSPARK_ERR_TIMEOUT if a bounded wait runs out
-  int merge_inline;
 };
-
-constexpr int kMaxBH = 4096;  // B*Hkv rows of counters
 
 // One query row of the merge: lanes over the head dimension, splits in order (max, then the
 // rescaled sums and O), bf16-rounded output written as fp16.
@@ -195,7 +187,7 @@ __device__ __forceinline__ void dequant_tile(uint8_t* buf) {
   }
 }
 
-template <int HD, bool KV8, bool CLUSTER>
+template <int HD, bool KV8>
 __global__ void __launch_bounds__(256) attn_kernel(const Args a) {
   using L = Layout<HD, KV8>;
   extern __shared__ __align__(16) uint8_t smem[];
@@ -208,10 +200,9 @@ __global__ void __launch_bounds__(256) attn_kernel(const Args a) {
   const int Ltot = kvlen + a.T;
   const int npages = (Ltot + KT - 1) / KT;
   // Splits actually used for this context: at least kMinPagesPerSplit pages each, so the
-  // merge stays cheap at short contexts; CTAs past them leave before touching the counter.
+  // merge stays cheap at short contexts; CTAs past them leave at once.
   const int nsplit = min(a.nsplit, (npages + kMinPagesPerSplit - 1) / kMinPagesPerSplit);
-  // (in the cluster form every CTA stays for the cluster barriers: unused splits are empty)
-  if (!CLUSTER && split >= nsplit) return;
+  if (split >= nsplit) return;
   const int pps = (npages + nsplit - 1) / nsplit;
   const int p_lo = split < nsplit ? split * pps : npages;
   const int p_hi = min(p_lo + pps, npages);
@@ -343,57 +334,6 @@ __global__ void __launch_bounds__(256) attn_kernel(const Args a) {
   l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
   l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
   l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-  if constexpr (CLUSTER) {
-    // this split's partial into this CTA's shared memory (the K/V tiles are no longer read):
-    // [R][2] (max, sum) then [R][HD] unnormalised O
-    float* pml = reinterpret_cast<float*>(smem);
-    float* po = pml + 2 * a.R;
-    if ((lane & 3) == 0) {
-      if (r0 < a.R) { pml[r0 * 2] = m0; pml[r0 * 2 + 1] = l0; }
-      if (r1 < a.R) { pml[r1 * 2] = m1; pml[r1 * 2 + 1] = l1; }
-    }
-#pragma unroll
-    for (int j = 0; j < HD / 8; ++j) {
-      const int d = j * 8 + (lane & 3) * 2;
-      if (r0 < a.R) *reinterpret_cast<float2*>(po + r0 * HD + d) = make_float2(o[j][0], o[j][1]);
-      if (r1 < a.R) *reinterpret_cast<float2*>(po + r1 * HD + d) = make_float2(o[j][2], o[j][3]);
-    }
-    cluster_sync_all();  // every split's partial is visible cluster-wide
-    // CTA `split` (its cluster rank) finishes rows [split*R/S, (split+1)*R/S), one warp per row,
-    // lanes over the head dimension; the same arithmetic as attn_combine_kernel
-    constexpr int E = HD / 32;
-    const int S = gridDim.x;
-    const int rlo = split * a.R / S, rhi = (split + 1) * a.R / S;
-    const uint32_t own = smem_u32(smem);
-    const int nwarps = blockDim.x >> 5;
-    for (int r = rlo + warp; r < rhi; r += nwarps) {
-      float M = -INFINITY;
-      for (int sp = 0; sp < S; ++sp)
-        M = fmaxf(M, ld_shared_cluster_f32(mapa_shared(own, (uint32_t)sp) + (uint32_t)(r * 2) * 4u));
-      float Ls = 0.0f, acc[E];
-#pragma unroll
-      for (int k = 0; k < E; ++k) acc[k] = 0.0f;
-      for (int sp = 0; sp < S; ++sp) {
-        const uint32_t pb = mapa_shared(own, (uint32_t)sp);
-        const float ms = ld_shared_cluster_f32(pb + (uint32_t)(r * 2) * 4u);
-        const float ls = ld_shared_cluster_f32(pb + (uint32_t)(r * 2 + 1) * 4u);
-        const float e = ms == -INFINITY ? 0.0f : exp2f(ms - M);  // empty splits hold zeros
-        if (ms != -INFINITY) Ls += ls * e;
-        const uint32_t ob = pb + (uint32_t)(2 * a.R + r * HD + lane * E) * 4u;
-#pragma unroll
-        for (int k = 0; k < E; ++k) acc[k] = fmaf(e, ld_shared_cluster_f32(ob + (uint32_t)k * 4u), acc[k]);
-      }
-      const float inv = Ls > 0.0f ? 1.0f / Ls : 0.0f;
-      const int t = r % a.T, g = r / a.T;
-      __half* dst = a.out + (size_t)(b * a.T + t) * a.ldo + (size_t)(h * a.G + g) * HD + lane * E;
-#pragma unroll
-      for (int k = 0; k < E; k += 2)
-        *reinterpret_cast<__half2*>(dst + k) =
-            __floats2half2_rn(bf16_round(acc[k] * inv), bf16_round(acc[k + 1] * inv));
-    }
-    cluster_sync_all();  // no CTA leaves while a peer still reads its shared memory
-    return;
-  }
   if (nsplit == 1) {
     // the whole context in one CTA: normalise and write the output directly
     const float inv0 = l0 > 0.0f ? 1.0f / l0 : 0.0f, inv1 = l1 > 0.0f ? 1.0f / l1 : 0.0f;
@@ -420,48 +360,6 @@ __global__ void __launch_bounds__(256) attn_kernel(const Args a) {
     if (r0 < a.R) *reinterpret_cast<float2*>(a.ws_o + (sbase + r0) * HD + d) = make_float2(o[j][0], o[j][1]);
     if (r1 < a.R) *reinterpret_cast<float2*>(a.ws_o + (sbase + r1) * HD + d) = make_float2(o[j][2], o[j][3]);
   }
-  if (!a.merge_inline) return;  // attn_combine_kernel merges
-  // In-kernel merge: every active split of (row, kv head) announces its partial, waits until
-  // all have (they are resident together: the host launches this form only when the whole grid
-  // fits on the device at once, and no CTA of it waits on a later kernel), then finishes rows
-  // [split*R/nsplit, (split+1)*R/nsplit). The wait is bounded and reports DSPARK_ERR_TIMEOUT.
-  __shared__ int timed_out;
-  __syncthreads();  // every thread's partial stores precede the release below
-  if (threadIdx.x == 0) {
-    timed_out = 0;
-    int old;
-    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(a.counters + bh) : "memory");
-    if (old != nsplit - 1) {
-      const unsigned long long t0 = globaltimer_ns();
-      while (true) {
-        int v;
-        asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(a.counters + bh) : "memory");
-        if (v >= nsplit) break;
-        if (globaltimer_ns() - t0 > kSpinLimitNs) {
-          report_error(a.status, DSPARK_ERR_TIMEOUT);
-          timed_out = 1;
-          break;
-        }
-        __nanosleep(64);
-      }
-    }
-  }
-  __syncthreads();
-  if (!timed_out) {
-    const int rlo = split * a.R / nsplit, rhi = (split + 1) * a.R / nsplit;
-    const int nwarps = blockDim.x >> 5;
-    for (int r = rlo + warp; r < rhi; r += nwarps) merge_row<HD>(a, b, h, r, nsplit, lane);
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    // the last split to finish its rows rearms both counters for the next launch (every
-    // sibling has left its wait by then)
-    const int done = atomicAdd(a.counters + kMaxBH + bh, 1);
-    if (done == nsplit - 1) {
-      a.counters[bh] = 0;
-      a.counters[kMaxBH + bh] = 0;
-    }
-  }
 }
 
 // Merge of the split partials: one warp per query row (8 rows per CTA), every (row, kv head,
@@ -481,119 +379,22 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const Args a) {
   merge_row<HD>(a, b, h, r, nsplit, lane);
 }
 
-// Cluster form limits: at most this many block-table pages per split (longer contexts keep
-// more splits than one cluster holds), and one wave of clusters.
-constexpr int kClusterPagesPerSplit = 4;
-// 0 (default): two kernels; 1: cluster form where it fits; 2: in-kernel merge where the grid
-// fits the device at once, else two kernels. Measured on B200 at C2 (verify attention, 18 pages,
-// 8 kv heads, us per call in a chain of 36): two kernels (37 splits) 11.4-11.6, in-kernel merge
-// 11.4, cluster form (16-CTA clusters, 2 pages per split) 16.9. PDL already hides the second
-// launch; a cluster starts only when all of its CTAs fit in one GPC at once, so it cannot fill
-// SMs as the previous kernel drains.
-static int g_merge_mode = 0;
 
-// CTAs of kernel k resident on the whole device at once (cached per kernel, block, smem)
-template <typename K>
-static int resident_ctas(K k, int threads, int smem) {
-  struct Entry { const void* k; int threads, smem, n; };
-  static Entry cache[32];
-  static int used = 0;
-  for (int i = 0; i < used; ++i)
-    if (cache[i].k == (const void*)k && cache[i].threads == threads && cache[i].smem == smem)
-      return cache[i].n;
-  int per_sm = 0, dev = 0, sms = 0;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, threads, (size_t)smem) != cudaSuccess) {
-    cudaGetLastError();
-    return 0;  // not cached: asked again next time
-  }
-  const int n = per_sm * sms;
-  if (used < 32) cache[used++] = Entry{(const void*)k, threads, smem, n};
-  return n;
-}
-
-// Max resident clusters of `size` CTAs of kernel k (cached per kernel, size, block and shared
-// memory; 0 if the query fails or the size needs an attribute the device refuses).
-template <typename K>
-static int max_clusters(K k, int size, int threads, int smem) {
-  struct Entry { const void* k; int size, threads, smem, n; };
-  static Entry cache[64];
-  static int used = 0;
-  for (int i = 0; i < used; ++i)
-    if (cache[i].k == (const void*)k && cache[i].size == size && cache[i].threads == threads &&
-        cache[i].smem == smem)
-      return cache[i].n;
-  int n = 0;
-  bool ok = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) == cudaSuccess;
-  if (ok && size > 8)
-    ok = cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess;
-  if (ok) {
-    cudaLaunchConfig_t q = {};
-    q.gridDim = dim3((unsigned)size, 1, 1);
-    q.blockDim = dim3((unsigned)threads);
-    q.dynamicSmemBytes = (size_t)smem;
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeClusterDimension;
-    at[0].val.clusterDim.x = (unsigned)size;
-    at[0].val.clusterDim.y = 1;
-    at[0].val.clusterDim.z = 1;
-    q.attrs = at;
-    q.numAttrs = 1;
-    if (cudaOccupancyMaxActiveClusters(&n, k, &q) != cudaSuccess) n = 0;
-  }
-  cudaGetLastError();
-  if (!ok) n = 0;
-  if (used < 64) cache[used++] = Entry{(const void*)k, size, threads, smem, n};
-  return n;
-}
-
-template <typename K>
-static int launch_cluster(K k, dim3 grid, dim3 block, int smem, int size, cudaStream_t st,
-                          const Args& a) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = (size_t)smem;
-  cfg.stream = st;
-  cudaLaunchAttribute at[2];
-  at[0].id = cudaLaunchAttributeClusterDimension;
-  at[0].val.clusterDim.x = (unsigned)size;
-  at[0].val.clusterDim.y = 1;
-  at[0].val.clusterDim.z = 1;
-  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  at[1].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = at;
-  cfg.numAttrs = 2;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, k, a);
-  if (e != cudaSuccess) return set_error(DSPARK_ERR_LAUNCH, "attention (cluster %d): %s", size, cudaGetErrorString(e));
-  note_launch();
-  return DSPARK_OK;
-}
 
 static size_t ws_layout(int B, int T, int Hq, int Hkv, int hd, int nsplit, size_t* off_ml,
                         size_t* off_o) {
   const int R = (Hq / Hkv) * T;
-  // fixed-size counter region first (arrivals, merges done): calls of other (B, Hkv) never
-  // overlap it with data
-  const size_t counters = 2 * kMaxBH * sizeof(int);
   const size_t ml = (((size_t)B * Hkv * nsplit * R * 2 * sizeof(float)) + 255) & ~(size_t)255;
   const size_t o = (size_t)B * Hkv * nsplit * R * hd * sizeof(float);
-  if (off_ml) *off_ml = counters;
-  if (off_o) *off_o = counters + ml;
-  return counters + ml + o;
+  if (off_ml) *off_ml = 0;
+  if (off_o) *off_o = ml;
+  return ml + o;
 }
 
 }  // namespace attn
 }  // namespace dspark
 
 using namespace dspark;
-
-extern "C" int dspark_attention_merge_mode(int mode) {
-  if (mode < 0 || mode > 2) return set_error(DSPARK_ERR_INVALID, "attention_merge_mode: %d", mode);
-  attn::g_merge_mode = mode;
-  return DSPARK_OK;
-}
 
 extern "C" size_t dspark_attention_workspace_bytes(int B, int T, int Hq, int Hkv, int hd,
                                                    int max_splits) {
@@ -618,7 +419,6 @@ extern "C" int dspark_attention(const void* q, int B, int T, int Hq, const dspar
   if (R > 128) return set_error(DSPARK_ERR_UNSUPPORTED, "attention: %d query rows per kv head > 128", R);
   if (ldo < Hq * hd || ldo % 4) return set_error(DSPARK_ERR_INVALID, "attention: ldo");
   if (max_splits < 1 || max_splits > 256) return set_error(DSPARK_ERR_INVALID, "attention: max_splits");
-  if (B * Hkv > attn::kMaxBH) return set_error(DSPARK_ERR_UNSUPPORTED, "attention: B*Hkv > %d", attn::kMaxBH);
   size_t off_ml, off_o;
   const size_t need = attn::ws_layout(B, T, Hq, Hkv, hd, max_splits, &off_ml, &off_o);
   if (!workspace || workspace_bytes < need)
@@ -631,47 +431,24 @@ extern "C" int dspark_attention(const void* q, int B, int T, int Hq, const dspar
   a.kv_len = kv_len;
   a.out = static_cast<__half*>(out);
   a.ldo = ldo;
-  a.counters = static_cast<int*>(workspace);
-  a.status = status;
-  a.merge_inline = 0;
   a.ws_ml = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + off_ml);
   a.ws_o = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + off_o);
   const int warps = (R + 15) / 16;
   const dim3 grid(max_splits, Hkv, B), block(warps * 32);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  auto go = [&](auto kern, auto kern_cl, auto combine, int smem) {
-    // cluster form: S splits per (row, kv head), S a power of two <= 16 and <= max_splits,
-    // when the block table holds at most kClusterPagesPerSplit pages per split and B*Hkv
-    // clusters are resident at once
-    const int smem_cl = std::max(smem, R * (hd + 2) * 4);
-    for (int S = 16; S >= 2 && attn::g_merge_mode == 1; S >>= 1) {
-      if (S > max_splits || (kv->max_pages + S - 1) / S > attn::kClusterPagesPerSplit) continue;
-      if (attn::max_clusters(kern_cl, S, (int)block.x, smem_cl) < B * Hkv) continue;
-      a.nsplit = S;
-      return launch_cluster(kern_cl, dim3(S, Hkv, B), block, smem_cl, S, st, a);
-    }
+  auto go = [&](auto kern, auto combine, int smem) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
       return set_error(DSPARK_ERR_CUDA, "attention: cudaFuncSetAttribute failed");
-    // in-kernel merge: the splits wait for one another, so the whole grid must be resident at
-    // once, and a status word must take a timed-out wait
-    a.merge_inline = (attn::g_merge_mode == 2 && max_splits > 1 && status &&
-                      (long long)max_splits * Hkv * B <= attn::resident_ctas(kern, (int)block.x, smem))
-                         ? 1 : 0;
     int rc = launch_pdl("attention", kern, grid, block, (size_t)smem, st, a);
-    if (rc || max_splits == 1 || a.merge_inline) return rc;
+    if (rc || max_splits == 1) return rc;
     return launch_pdl("attention.combine", combine, dim3((R + 7) / 8, Hkv, B), dim3(256), 0, st, a);
   };
   using namespace attn;
   if (hd == 128) {
     if (kv->kv8)
-      return go(attn_kernel<128, true, false>, attn_kernel<128, true, true>, attn_combine_kernel<128>,
-                Layout<128, true>::kBytes);
-    return go(attn_kernel<128, false, false>, attn_kernel<128, false, true>, attn_combine_kernel<128>,
-              Layout<128, false>::kBytes);
+      return go(attn_kernel<128, true>, attn_combine_kernel<128>, Layout<128, true>::kBytes);
+    return go(attn_kernel<128, false>, attn_combine_kernel<128>, Layout<128, false>::kBytes);
   }
-  if (kv->kv8)
-    return go(attn_kernel<64, true, false>, attn_kernel<64, true, true>, attn_combine_kernel<64>,
-              Layout<64, true>::kBytes);
-  return go(attn_kernel<64, false, false>, attn_kernel<64, false, true>, attn_combine_kernel<64>,
-            Layout<64, false>::kBytes);
+  if (kv->kv8) return go(attn_kernel<64, true>, attn_combine_kernel<64>, Layout<64, true>::kBytes);
+  return go(attn_kernel<64, false>, attn_combine_kernel<64>, Layout<64, false>::kBytes);
 }

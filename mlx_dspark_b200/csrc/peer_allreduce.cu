@@ -16,11 +16,19 @@ __device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__floa
 
 // CTA t: wait (bounded) for every rank's flag of tile t at this epoch, then
 // h[m, n] = bf16(h + bf16(sum_r recv[slot][r][m][n])), r = 0 .. world-1 in order.
+// The kernel does not wait for the GEMM before it to complete: the flags carry every input
+// (each tile's partials, this rank's included, behind a system-scope release), and the
+// residual rows were last written by a kernel that completed before that GEMM's CTAs started.
+// So a tile is summed as soon as every rank has finished it, while the GEMM's last tiles are
+// still running. With epoch_dev the epoch is epoch_dev[0] + 1; every CTA counts itself in
+// epoch_dev[1] when it is done, and the last one stores the epoch back (and clears the count):
+// by then every tile of this rank's GEMM, the only other reader, is finished.
 __global__ void __launch_bounds__(kCols) peer_reduce_residual_kernel(
     __nv_bfloat16* __restrict__ h, int ldh, int M, int N, const float* __restrict__ recv,
-    const int* __restrict__ flags, int world, int mcap, int epoch, long long timeout_ns,
-    int* status) {
-  pdl_enter();
+    const int* __restrict__ flags, int world, int mcap, int epoch_arg, int* epoch_dev,
+    long long timeout_ns, int* status) {
+  pdl_launch_dependents();
+  const int epoch = epoch_dev ? __ldcg(epoch_dev) + 1 : epoch_arg;
   const int tile = blockIdx.x, tiles = N / kCols;
   const int slot = epoch & 1;
   if (threadIdx.x < world) {
@@ -32,6 +40,7 @@ __global__ void __launch_bounds__(kCols) peer_reduce_residual_kernel(
           report_error(status, DSPARK_ERR_TIMEOUT);  // the sums below are then not meaningful
           break;
         }
+        __nanosleep(64);
       }
     }
   }
@@ -43,6 +52,19 @@ __global__ void __launch_bounds__(kCols) peer_reduce_residual_kernel(
       s += __ldcg(recv + (((size_t)slot * world + r) * mcap + m) * N + n);
     __nv_bfloat16* p = h + (size_t)m * ldh + n;
     *p = __float2bfloat16_rn(__bfloat162float(*p) + bf16r(s));
+  }
+  if (epoch_dev) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int old;
+      asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(epoch_dev + 1)
+                   : "memory");
+      if (old == (int)gridDim.x - 1) {
+        epoch_dev[1] = 0;
+        epoch_dev[0] = epoch;
+        __threadfence();
+      }
+    }
   }
 }
 
@@ -96,8 +118,8 @@ extern "C" int dspark_peer_reduce_residual(void* h, int ldh, int M, const dspark
                                            long long timeout_ns, int* status,
                                            dspark_stream_t stream) {
   if (!h || !ar || M <= 0 || M > ar->m_cap || ar->world < 2 || ar->world > 8 || ar->rank < 0 ||
-      ar->rank >= ar->world || ar->n <= 0 || ar->n % par::kCols || ldh < ar->n || ar->epoch < 1 ||
-      timeout_ns <= 0)
+      ar->rank >= ar->world || ar->n <= 0 || ar->n % par::kCols || ldh < ar->n ||
+      (ar->epoch < 1 && !ar->epoch_dev) || timeout_ns <= 0)
     return set_error(DSPARK_ERR_INVALID, "peer_reduce_residual: bad arguments");
   if (!ar->recv[ar->rank] || !ar->flags[ar->rank])
     return set_error(DSPARK_ERR_INVALID, "peer_reduce_residual: own buffers missing");
@@ -106,5 +128,5 @@ extern "C" int dspark_peer_reduce_residual(void* h, int ldh, int M, const dspark
                     static_cast<cudaStream_t>(stream), static_cast<__nv_bfloat16*>(h), ldh, M,
                     ar->n, static_cast<const float*>(ar->recv[ar->rank]),
                     static_cast<const int*>(ar->flags[ar->rank]), ar->world, ar->m_cap, ar->epoch,
-                    timeout_ns, status);
+                    ar->epoch_dev, timeout_ns, status);
 }

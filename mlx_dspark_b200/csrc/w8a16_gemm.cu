@@ -98,6 +98,7 @@ struct Params {
   float* peer_y[8];
   int* peer_f[8];
   int peer_world, peer_rank, peer_mcap, peer_epoch;
+  const int* peer_epoch_dev;  // set: the epoch is peer_epoch_dev[0] + 1 (device-resident)
 };
 
 __device__ __forceinline__ long long range_start(long long b, long long total, long long G) {
@@ -165,7 +166,10 @@ __device__ __forceinline__ void epilogue_store(const PT& p, int tile, int er, co
         // one-shot all-reduce, send half: this rank's fp32 tile into slot (epoch & 1), source row
         // block `rank`, of every rank's receive buffer (plain stores over NVLink), then, once the
         // tile's 128 threads have stored, the tile's epoch flag on every rank
-        const int slot = p.peer_epoch & 1;
+        // (a device-resident epoch was stored by the previous call's reduce, which completed
+        // before this epilogue's griddepcontrol.wait returned)
+        const int epoch = p.peer_epoch_dev ? __ldcg(p.peer_epoch_dev) + 1 : p.peer_epoch;
+        const int slot = epoch & 1;
         const size_t off = ((size_t)(slot * p.peer_world + p.peer_rank) * p.peer_mcap) * p.N + n;
         for (int r = 0; r < p.peer_world; ++r) {
           float* y = p.peer_y[r] + off;
@@ -175,9 +179,9 @@ __device__ __forceinline__ void epilogue_store(const PT& p, int tile, int er, co
         }
         asm volatile("bar.sync 1, 128;" ::: "memory");
         if (er == 0) {
-          __threadfence_system();
+          fence_acq_rel_sys();
           const size_t fo = (size_t)(slot * p.peer_world + p.peer_rank) * p.tiles + tile;
-          for (int r = 0; r < p.peer_world; ++r) st_release_sys(p.peer_f[r] + fo, p.peer_epoch);
+          for (int r = 0; r < p.peer_world; ++r) st_relaxed_sys(p.peer_f[r] + fo, epoch);
         }
       }
       break;
@@ -955,6 +959,7 @@ static int gemm_launch(const void* x, int ldx, const uint8_t* wq, const uint32_t
     p.peer_rank = peer->rank;
     p.peer_mcap = peer->m_cap;
     p.peer_epoch = peer->epoch;
+    p.peer_epoch_dev = peer->epoch_dev;
   }
   if (opts) {
     const int rc = apply_opts(p, *opts, epilogue, N);
@@ -1075,7 +1080,7 @@ extern "C" int dspark_w8a16_gemm_peer(const void* x, int ldx, const uint8_t* wq,
                                       size_t workspace_bytes, int* status, dspark_stream_t stream) {
   if (!ar) return set_error(DSPARK_ERR_INVALID, "w8a16_gemm_peer: no peer descriptor");
   if (ar->world < 2 || ar->world > 8 || ar->rank < 0 || ar->rank >= ar->world || ar->n != N ||
-      ar->epoch < 1 || M > ar->m_cap)
+      (ar->epoch < 1 && !ar->epoch_dev) || M > ar->m_cap)
     return set_error(DSPARK_ERR_INVALID,
                      "w8a16_gemm_peer: world=%d rank=%d n=%d (N=%d) epoch=%d M=%d m_cap=%d",
                      ar->world, ar->rank, ar->n, N, ar->epoch, M, ar->m_cap);

@@ -88,13 +88,6 @@ def gemm_workspace_bytes(M: int, N: int, K: int) -> int:
 PREFETCH_LIMIT = 16 << 20  # bytes of the next weights warmed in L2 (16 MB measured best on C2)
 
 
-def attention_merge_mode(mode: int) -> None:
-    """0 (default): split-KV partials merged by a second launch; 1: inside one cluster launch
-    where it applies; 2: inside the attention launch where its grid fits the device at once.
-    Process-wide; captured graphs keep their form."""
-    _lib.check(_lib.lib().dspark_attention_merge_mode(int(mode)), "attention_merge_mode")
-
-
 class RowNorm:
     """An RMSNorm fused into the GEMM that consumes it: the weights, eps, and the per-tile row
     sums of squares [M, N/128] (fp32) written by the GEMM that produced the input."""

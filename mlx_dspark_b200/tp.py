@@ -139,7 +139,12 @@ class PeerAllReduce:
                     ptr = p.value
                 getattr(self.ar, field)[r] = ptr
         self.ar.world, self.ar.rank, self.ar.m_cap, self.ar.n = world, rank, m_cap, n
-        self.epoch = 0
+        # device-resident epoch (dspark_peer_ar.epoch_dev): the calls take their numbers on the
+        # device, so a CUDA graph of a round replays with fresh epochs on every rank
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.epoch_dev = torch.zeros(2, dtype=torch.int32, device=dev)
+        self.ar.epoch_dev = self.epoch_dev.data_ptr()
+        self.epoch = 0  # calls issued from the host (eager or captured)
 
     def next(self):
         self.epoch += 1
@@ -160,17 +165,12 @@ class TPTarget(Target):
     """One rank's share of a tensor-parallel target. The process group must be NCCL (one
     process per GPU) for device tensors; every rank runs the same decode loop."""
 
-    # o_proj / down_proj all-reduce. False (default): NCCL, captured with the rest of the round
-    # into one CUDA graph. True: verify-sized calls (M <= 64) through the fused GEMM epilogue
-    # over NVLink peer memory (dspark_w8a16_gemm_peer), whose host-side epochs keep those rounds
-    # eager; measured on Qwen3-32B at TP2 (16k context) it is the slower form: 13.5 ms per
-    # round against 12.6 ms for eager NCCL and 11.7 ms for captured NCCL. Prefill chunks
-    # (M > 64) always use NCCL.
-    fused_allreduce = False
-
-    @property
-    def capturable(self) -> bool:
-        return not self.fused_allreduce
+    capturable = True  # a round, collectives included, is captured into one CUDA graph
+    # o_proj / down_proj all-reduce of verify-sized calls (M <= 64): True, the fused GEMM
+    # epilogue over NVLink peer memory (dspark_w8a16_gemm_peer + dspark_peer_reduce_residual,
+    # partials summed in rank order: the same bits whatever the call's M); False, NCCL. Prefill
+    # chunks (M > 64) always use NCCL.
+    fused_allreduce = True
 
     def __init__(self, weights: TargetWeights, rank: int, world: int, group=None, tokenizer=None,
                  *, kv_bits: int | None = None, device="cuda"):

@@ -58,17 +58,19 @@ def _rank_body(rank, world, port, q, log):
         print("loaded", flush=True)
         logits, _ = target.run([prompt], target.make_cache(256), ())
         print("forward done", flush=True)
-        # a 9-token verify forward with the fused peer all-reduce and with NCCL (the default):
+        # a 9-token verify forward with the fused peer all-reduce (the default) and with NCCL:
         # with two ranks the fp32 sum of the two partials is the same in either order, so
         # bitwise
         outs = []
         for fused in (True, False):
             target.fused_allreduce = fused
             outs.append(target.run([prompt[:9]], target.make_cache(64), ())[0])
-        target.fused_allreduce = False
+        target.fused_allreduce = True
         target.scratch.check_status()
         fused_same = torch.equal(outs[0], outs[1])
         assert target.peer is not None and target.peer.epoch == 2 * TINY.num_hidden_layers
+        # the calls took their epochs on the device, one per call
+        assert int(target.peer.epoch_dev[0]) == target.peer.epoch
         print("fused all-reduce checked", flush=True)
         local = logits[0, :, :target.vocab_valid].contiguous()
         parts = [torch.zeros_like(local) for _ in range(world)]
