@@ -166,11 +166,11 @@ typedef struct dspark_peer_ar {
   int n;           /* columns (the projection's N, a multiple of 128) */
   int epoch;       /* this all-reduce's number, >= 1 (ignored when epoch_dev is set) */
   int reserved;
-  int* epoch_dev;  /* NULL, or 2 zero-initialised ints on this rank's device: [0] the number
-                    * of the last finished all-reduce, [1] scratch. The call's epoch is then
-                    * epoch_dev[0] + 1, read on the device, and the reduce stores it back when
-                    * every CTA is past its waits, so a CUDA graph of the calls replays with
-                    * fresh epochs. */
+  int* epoch_dev;  /* NULL, or 4 zero-initialised ints on this rank's device: the calls then
+                    * number themselves on the device ([0] the last all-reduce whose reduce has
+                    * finished, read by the GEMM; [2] the last whose reduce has started, read
+                    * by the reduce; [1], [3] scratch), so a CUDA graph of the calls replays
+                    * with fresh epochs. */
 } dspark_peer_ar;
 /* cudaMalloc'd, zero-filled memory for recv / flags (IPC needs its own allocation), and its
  * release. These two entry points allocate; nothing else in the library does. */

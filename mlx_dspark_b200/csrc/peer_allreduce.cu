@@ -20,15 +20,38 @@ __device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__floa
 // (each tile's partials, this rank's included, behind a system-scope release), and the
 // residual rows were last written by a kernel that completed before that GEMM's CTAs started.
 // So a tile is summed as soon as every rank has finished it, while the GEMM's last tiles are
-// still running. With epoch_dev the epoch is epoch_dev[0] + 1; every CTA counts itself in
-// epoch_dev[1] when it is done, and the last one stores the epoch back (and clears the count):
-// by then every tile of this rank's GEMM, the only other reader, is finished.
+// still running.
+// With epoch_dev, the GEMMs and the reduces keep separate counts, because the reduce of call
+// e runs next to the GEMM of call e and may start before the reduce of call e - 1 is done:
+//   [2], [3]: the reduces' count. Every CTA reads [2] + 1 and counts itself in [3]; the last
+//     stores the epoch into [2] before triggering the next launch, and a later reduce starts
+//     only after that trigger (it follows a GEMM whose CTAs start after it).
+//   [0], [1]: the GEMMs' count, which a GEMM reads in its epilogue after the kernel before it
+//     completed. Every CTA counts itself in [1] when it is done, and the last stores the
+//     epoch into [0]: by then every tile of this rank's GEMM of this call is finished.
 __global__ void __launch_bounds__(kCols) peer_reduce_residual_kernel(
     __nv_bfloat16* __restrict__ h, int ldh, int M, int N, const float* __restrict__ recv,
     const int* __restrict__ flags, int world, int mcap, int epoch_arg, int* epoch_dev,
     long long timeout_ns, int* status) {
+  __shared__ int s_epoch;
+  if (threadIdx.x == 0) {
+    int e = epoch_arg;
+    if (epoch_dev) {
+      e = __ldcg(epoch_dev + 2) + 1;
+      int old;
+      asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(epoch_dev + 3)
+                   : "memory");
+      if (old == (int)gridDim.x - 1) {
+        epoch_dev[3] = 0;
+        epoch_dev[2] = e;
+        __threadfence();
+      }
+    }
+    s_epoch = e;
+  }
+  __syncthreads();
   pdl_launch_dependents();
-  const int epoch = epoch_dev ? __ldcg(epoch_dev) + 1 : epoch_arg;
+  const int epoch = s_epoch;
   const int tile = blockIdx.x, tiles = N / kCols;
   const int slot = epoch & 1;
   if (threadIdx.x < world) {

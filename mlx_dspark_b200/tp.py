@@ -142,7 +142,7 @@ class PeerAllReduce:
         # device-resident epoch (dspark_peer_ar.epoch_dev): the calls take their numbers on the
         # device, so a CUDA graph of a round replays with fresh epochs on every rank
         dev = torch.device("cuda", torch.cuda.current_device())
-        self.epoch_dev = torch.zeros(2, dtype=torch.int32, device=dev)
+        self.epoch_dev = torch.zeros(4, dtype=torch.int32, device=dev)
         self.ar.epoch_dev = self.epoch_dev.data_ptr()
         self.epoch = 0  # calls issued from the host (eager or captured)
 

@@ -71,6 +71,31 @@ def _rank_body(rank, world, port, q, log):
         assert target.peer is not None and target.peer.epoch == 2 * TINY.num_hidden_layers
         # the calls took their epochs on the device, one per call
         assert int(target.peer.epoch_dev[0]) == target.peer.epoch
+        # back-to-back calls, each reduce followed directly by the next GEMM (the reduce starts
+        # before its GEMM completes, so consecutive calls overlap): 16 accumulations of this
+        # rank's o_proj partials against NCCL's sum of the same partials (two ranks: the same
+        # fp32 sum in either order)
+        from mlx_dspark_b200 import ops
+        from mlx_dspark_b200._lib import EPI_STORE_F32
+        M, w = 9, target.layers[0].o
+        H = w.N
+        gx = torch.Generator(device=dev).manual_seed(100 + rank)
+        x = (torch.randn(M, w.K, generator=gx, device=dev) * 0.5).to(torch.float16)
+        part = torch.zeros(M, H, dtype=torch.float32, device=dev)
+        ops.gemm(x, w, part, epilogue=EPI_STORE_F32, scratch=target.scratch, M=M)
+        dist.all_reduce(part)
+        step = part.to(torch.bfloat16).float()
+        h = torch.zeros(M, H, dtype=torch.bfloat16, device=dev)
+        want = torch.zeros(M, H, dtype=torch.bfloat16, device=dev)
+        for _ in range(16):
+            ar = target.peer.next()
+            ops.gemm_peer(x, w, ar, scratch=target.scratch, M=M)
+            ops.peer_reduce_residual(h, ar, M, target.scratch)
+            want = (want.float() + step).to(torch.bfloat16)
+        torch.cuda.synchronize()
+        target.scratch.check_status()
+        assert torch.equal(h, want), float((h.float() - want.float()).abs().max())
+        assert int(target.peer.epoch_dev[0]) == target.peer.epoch
         print("fused all-reduce checked", flush=True)
         local = logits[0, :, :target.vocab_valid].contiguous()
         parts = [torch.zeros_like(local) for _ in range(world)]
