@@ -109,27 +109,48 @@ __device__ __forceinline__ long long range_owner(long long g, long long total, l
   return ((g + 1) * G + total - 1) / total - 1;
 }
 
-// Sums of squares of 16 rows' outputs across the warp, into xch[ew * BN + c0 + j] (lane 0,
-// rows below M): the 16 butterfly reductions run interleaved rather than one row after another.
-template <int BN>
-__device__ __forceinline__ void row_sumsq16(const float* o, float* xch, int ew, int lane, int c0,
-                                            int M) {
-  float w[16];
+// The bf16 tile staged in shared memory as [BN][BM] (the exchange buffer) goes out as 16-byte
+// vectors: rows < M of y (and their fp16 copy), one vector of 8 columns per thread per step.
+// With ss_out, thread m < M then sums the squares of row m's 128 staged values, in column
+// order with one rounding per step: the same order for a row whatever its place in the block.
+// y, ldy (and the copy) are 16-byte aligned / multiples of 8 (checked on the host).
+template <typename PT>
+__device__ __forceinline__ void store_staged_rows(const PT& p, int tile, int er,
+                                                  const __nv_bfloat16* xs) {
+  __nv_bfloat16* y = static_cast<__nv_bfloat16*>(p.y);
+  constexpr int kVec = BM / 8;  // 16-byte vectors per row
+  for (int i = er; i < p.M * kVec; i += kEpiWarps * 32) {
+    const int m = i / kVec, c = i - m * kVec;
+    const uint4 v = *reinterpret_cast<const uint4*>(xs + m * BM + c * 8);
+    *reinterpret_cast<uint4*>(y + (size_t)m * p.ldy + tile * BM + c * 8) = v;
+    if (p.copy16) {
+      const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&v);
+      uint4 h;
+      __half2* h2 = reinterpret_cast<__half2*>(&h);
 #pragma unroll
-  for (int j = 0; j < 16; ++j) w[j] = __fmul_rn(o[j], o[j]);
+      for (int k = 0; k < 4; ++k) h2[k] = __float22half2_rn(__bfloat1622float2(b2[k]));
+      *reinterpret_cast<uint4*>(p.copy16 + (size_t)m * p.copy16_ld + tile * BM + c * 8) = h;
+    }
+  }
+  if (p.ss_out && er < p.M) {
+    float acc = 0.0f;
+    for (int c = 0; c < kVec; ++c) {
+      const uint4 v = *reinterpret_cast<const uint4*>(xs + er * BM + c * 8);
+      const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&v);
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1)
-#pragma unroll
-    for (int j = 0; j < 16; ++j) w[j] += __shfl_xor_sync(0xffffffffu, w[j], off);
-  if (lane == 0)
-#pragma unroll
-    for (int j = 0; j < 16; ++j)
-      if (c0 + j < M) xch[ew * BN + c0 + j] = w[j];
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __bfloat1622float2(b2[k]);
+        acc = __fmaf_rn(f.x, f.x, acc);
+        acc = __fmaf_rn(f.y, f.y, acc);
+      }
+    }
+    p.ss_out[(size_t)er * p.tiles + tile] = acc;
+  }
 }
 
-// The epilogues compute all rows of a 16-row chunk that holds any of the M rows without a branch
-// per row (rows past M hold zeros: their activations are the tensor map's zero fill), so the
-// rows' arithmetic and reductions overlap; only the stores are predicated on m < M.
+// The SiLU epilogue computes all rows of a 16-row chunk that holds any of the M rows without a
+// branch per row (rows past M hold zeros: their activations are the tensor map's zero fill), so
+// the rows' arithmetic overlaps; only the stores are predicated on m < M.
 // PEER: the instance of the tensor-parallel fused all-reduce (dspark_w8a16_gemm_peer); the
 // other instances carry no code for it
 template <int BN, bool PEER = false, typename PT>
@@ -139,26 +160,14 @@ __device__ __forceinline__ void epilogue_store(const PT& p, int tile, int er, co
   const int n = tile * BM + er;
   switch (p.epilogue) {
     case DSPARK_EPI_STORE_BF16: {
-      __nv_bfloat16* y = static_cast<__nv_bfloat16*>(p.y);
-      const int lane = er & 31, ew = er >> 5;
+      // stage the tile's bf16 rows, then store them as vectors
+      __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(xch);
 #pragma unroll
-      for (int c0 = 0; c0 < BN; c0 += 16) {
-        if (c0 >= p.M) break;
-        float o[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) o[j] = bf16_round(acc[c0 + j]);
-#pragma unroll
-        for (int j = 0; j < 16; ++j)
-          if (c0 + j < p.M) y[(size_t)(c0 + j) * p.ldy + n] = __float2bfloat16_rn(o[j]);
-        if (p.ss_out) row_sumsq16<BN>(o, xch, ew, lane, c0, p.M);
-      }
-      if (p.ss_out) {
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (er < p.M)
-          p.ss_out[(size_t)er * p.tiles + tile] =
-              ((xch[er] + xch[BN + er]) + xch[2 * BN + er]) + xch[3 * BN + er];
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-      }
+      for (int m = 0; m < BN; ++m)
+        if (m < p.M) xs[m * BM + er] = __float2bfloat16_rn(acc[m]);
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      store_staged_rows(p, tile, er, xs);
+      asm volatile("bar.sync 1, 128;" ::: "memory");  // xch is reused by the next tile
       break;
     }
     case DSPARK_EPI_PEER_F32: {
@@ -194,11 +203,10 @@ __device__ __forceinline__ void epilogue_store(const PT& p, int tile, int er, co
       break;
     }
     case DSPARK_EPI_RESIDUAL_BF16: {
-      // y may be the residual itself (in place): read every row first, then store, so the
-      // loads are not ordered one by one behind the stores they might alias
-      __nv_bfloat16* y = static_cast<__nv_bfloat16*>(p.y);
+      // y may be the residual itself (in place): every residual value is read (below, or by
+      // the caller into rpre) before the barrier that precedes the first store
       const __nv_bfloat16* r = static_cast<const __nv_bfloat16*>(p.residual);
-      const int lane = er & 31, ew = er >> 5;
+      __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(xch);
 #pragma unroll
       for (int c0 = 0; c0 < BN; c0 += 16) {  // 16 rows at a time bounds the registers held
         if (c0 >= p.M) break;
@@ -211,26 +219,16 @@ __device__ __forceinline__ void epilogue_store(const PT& p, int tile, int er, co
           else
             rv[j] = m < p.M ? __ldcg(r + (size_t)m * p.ldr + n) : __float2bfloat16_rn(0.0f);
         }
-        float o[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j)
-          o[j] = bf16_round(__bfloat162float(rv[j]) + bf16_round(acc[c0 + j]));
-#pragma unroll
-        for (int j = 0; j < 16; ++j)
-          if (c0 + j < p.M) {
-            y[(size_t)(c0 + j) * p.ldy + n] = __float2bfloat16_rn(o[j]);
-            if (p.copy16) p.copy16[(size_t)(c0 + j) * p.copy16_ld + n] = __float2half_rn(o[j]);
-          }
-        // the rows' shares of the next RMSNorm: warp sums here, then the 4 warps in order
-        if (p.ss_out) row_sumsq16<BN>(o, xch, ew, lane, c0, p.M);
+          if (c0 + j < p.M)
+            xs[(c0 + j) * BM + er] =
+                __float2bfloat16_rn(__bfloat162float(rv[j]) + bf16_round(acc[c0 + j]));
       }
-      if (p.ss_out) {
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (er < p.M)
-          p.ss_out[(size_t)er * p.tiles + tile] =
-              ((xch[er] + xch[BN + er]) + xch[2 * BN + er]) + xch[3 * BN + er];
-        asm volatile("bar.sync 1, 128;" ::: "memory");  // xch is reused by the next tile
-      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      // the rows (and their fp16 copy) as vectors; the rows' shares of the next RMSNorm
+      store_staged_rows(p, tile, er, xs);
+      asm volatile("bar.sync 1, 128;" ::: "memory");  // xch is reused by the next tile
       break;
     }
     case DSPARK_EPI_SILU_MUL_F16: {
@@ -897,6 +895,8 @@ static int apply_opts(w8::Params& p, const dspark_gemm_opts& o, int epilogue, in
   if (o.copy_f16) {
     if (epilogue != DSPARK_EPI_RESIDUAL_BF16 || o.copy_f16_ld < N)
       return set_error(DSPARK_ERR_INVALID, "w8a16_gemm: copy_f16 needs RESIDUAL_BF16 and ld >= N");
+    if ((reinterpret_cast<uintptr_t>(o.copy_f16) & 15) || (o.copy_f16_ld & 7))
+      return set_error(DSPARK_ERR_ALIGN, "w8a16_gemm: copy_f16 must be 16-byte aligned, ld %% 8 == 0");
     p.copy16 = static_cast<__half*>(o.copy_f16);
     p.copy16_ld = o.copy_f16_ld;
   }
@@ -965,6 +965,10 @@ static int gemm_launch(const void* x, int ldx, const uint8_t* wq, const uint32_t
     const int rc = apply_opts(p, *opts, epilogue, N);
     if (rc) return rc;
   }
+  // the bf16 epilogues store their staged rows as 16-byte vectors
+  if (!rope && !peer && (epilogue == DSPARK_EPI_STORE_BF16 || epilogue == DSPARK_EPI_RESIDUAL_BF16) &&
+      ((reinterpret_cast<uintptr_t>(y) & 15) || (ldy & 7)))
+    return set_error(DSPARK_ERR_ALIGN, "w8a16_gemm: y must be 16-byte aligned with ldy %% 8 == 0 (ldy=%d)", ldy);
   const void* pf[2] = {pf0, pf1};
   const size_t pfb[2] = {pf0_bytes, pf1_bytes};
   for (int r = 0; r < 2; ++r) {

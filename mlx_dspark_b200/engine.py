@@ -83,7 +83,7 @@ class Engine:
         # the CUDA current device is per thread: the device thread runs on the target's
         self._executor = executor or ThreadPoolExecutor(
             max_workers=1, thread_name_prefix="dspark-device",
-            initializer=_bind_device, initargs=(getattr(target, "device", None),))
+            initializer=_bind_device, initargs=(_cuda_index(getattr(target, "device", None)),))
         self.prefix = self._make_prefix_cache(prefix_cache)
         self.created = int(time.time())
         self.stats = {"requests": 0, "prompt_tokens": 0, "completion_tokens": 0,
@@ -404,12 +404,23 @@ def maybe_batch_engine(engine: Engine, max_batch: int):
 
 
 # -------------------------------------------------------------------------------------------
-def _bind_device(device) -> None:
-    """Make `device` (a CUDA device) the calling thread's current device."""
+def _cuda_index(device) -> int | None:
+    """The CUDA device index of `device` (the constructing thread's current device for a bare
+    "cuda"), or None for a host device."""
     import torch
-    dev = torch.device(device) if device is not None else None
-    if dev is not None and dev.type == "cuda":
-        torch.cuda.set_device(dev)
+    if device is None:
+        return None
+    dev = torch.device(device)
+    if dev.type != "cuda":
+        return None
+    return dev.index if dev.index is not None else torch.cuda.current_device()
+
+
+def _bind_device(index: int | None) -> None:
+    """Make CUDA device `index` the calling thread's current device."""
+    if index is not None:
+        import torch
+        torch.cuda.set_device(index)
 
 
 def _replica_main(index: int, device, factory, inbox, outbox) -> None:
