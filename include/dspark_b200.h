@@ -48,7 +48,12 @@ enum {
   DSPARK_ERR_TIMEOUT = 4,     /* a bounded device-side wait gave up */
   DSPARK_ERR_UNSUPPORTED = 5, /* configuration not compiled in */
   DSPARK_ERR_CUDA = 6,        /* CUDA runtime / driver call failed */
-  DSPARK_ERR_WORKSPACE = 7    /* workspace missing or too small */
+  DSPARK_ERR_WORKSPACE = 7,   /* workspace missing or too small */
+  DSPARK_ERR_RANGE = 8        /* a value written as an fp16 GEMM operand (the SiLU*up
+                                 activations, the attention output, the fp16 hidden-state
+                                 taps) was outside the fp16 range (|x| > 65504) or NaN: the
+                                 kernel stores it as fp16 (an infinity) and records this code in
+                                 the caller's status word */
 };
 
 /* W8A16 GEMM epilogues */
@@ -300,8 +305,8 @@ int dspark_w8a16_gemm_qkv_rope(const void* x, int ldx, const uint8_t* wq, const 
  * q   : bf16 [B*T, Hq*hd]; out: fp16 [B*T, ldo] (bf16-rounded, the o_proj GEMM input)
  * workspace: dspark_attention_workspace_bytes(...) bytes for the split partials.
  * Splits (at most max_splits, at least one page each) are merged in split order by a second
- * launch; with one split the attention launch writes the output directly. `status` is
- * accepted for symmetry with the other entry points (nothing in attention waits).
+ * launch; with one split the attention launch writes the output directly. `status` (may be
+ * NULL) receives DSPARK_ERR_RANGE if an output is past the fp16 range.
  * ------------------------------------------------------------------------------------- */
 size_t dspark_attention_workspace_bytes(int B, int T, int Hq, int Hkv, int hd, int max_splits);
 int dspark_attention(const void* q, int B, int T, int Hq, const dspark_kv_layout* kv,
@@ -491,7 +496,7 @@ int dspark_embed_block_w8(const int32_t* pending, int B, int k, int mask_id, con
 /* bf16 -> fp16 copy of a [rows, cols] block: the target hidden-state tap written into the
  * fp16 fused-context GEMM input (src/mlx_dspark/target.py:66-69,75) */
 int dspark_bf16_to_f16(const void* src, int lds, void* dst, int ldd, int rows, int cols,
-                       dspark_stream_t stream);
+                       int* status, dspark_stream_t stream);  /* DSPARK_ERR_RANGE past fp16 */
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

@@ -14,7 +14,8 @@ LIB_PATH = Path(__file__).resolve().with_name("libdspark_b200.so")
 DSPARK_OK = 0
 DSPARK_ERR_TIMEOUT = 4
 ERR_NAMES = {1: "invalid argument", 2: "alignment", 3: "launch failed", 4: "device wait timed out",
-             5: "unsupported", 6: "CUDA error", 7: "workspace"}
+             5: "unsupported", 6: "CUDA error", 7: "workspace",
+             8: "fp16 operand out of range"}
 
 EPI_STORE_BF16, EPI_RESIDUAL_BF16, EPI_SILU_MUL_F16, EPI_STORE_F32, EPI_PEER_F32 = 0, 1, 2, 3, 4
 
@@ -92,7 +93,7 @@ SIGNATURES = {
     "dspark_draft_override": (I, [I, I, I, P, I, P, I, P, P, P, P, P]),
     "dspark_markov_workspace_bytes": (c_size_t, [I, I]),
     "dspark_markov_sample_block": (I, [P, I, I, I, I, I, I, P, P, P, P, P, P, P, P, c_size_t, P, P]),
-    "dspark_bf16_to_f16": (I, [P, I, P, I, I, I, P]),
+    "dspark_bf16_to_f16": (I, [P, I, P, I, I, I, P, P]),
     "dspark_apply_penalties": (I, [P, c_longlong, I, I, I, P, P, c_double, c_double, P]),
     "dspark_penalty_counts_add": (I, [P, I, I, P, I, P]),
     "dspark_argmax_rows": (I, [P, c_longlong, I, I, P, I, P, I, P, I, P]),

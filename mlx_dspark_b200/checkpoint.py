@@ -139,12 +139,27 @@ def pack_u8x4(q: torch.Tensor) -> torch.Tensor:
 
 
 def _as_bf16(t: torch.Tensor, name: str) -> torch.Tensor:
+    """Norm weights as the kernels read them, bf16. An fp16 checkpoint's values are rounded to
+    bf16 (a relative change of at most 2^-9 on a norm weight); fp32 values must be exact in
+    bf16."""
     if t.dtype == torch.bfloat16:
         return t
     b = t.to(torch.bfloat16)
-    if not torch.equal(b.to(t.dtype), t):
+    if t.dtype != torch.float16 and not torch.equal(b.to(t.dtype), t):
         raise ValueError(f"{name}: {t.dtype} values are not exactly representable in bf16")
     return b
+
+
+def _scale_dtype(t: torch.Tensor, name: str) -> torch.Tensor:
+    """Quantization scales / biases as stored: bf16 or fp16 (an fp16 source model's 8-bit
+    checkpoint) kept as they are; fp32 narrowed to bf16 or fp16 when one holds it exactly."""
+    if t.dtype in (torch.bfloat16, torch.float16):
+        return t
+    for dt in (torch.bfloat16, torch.float16):
+        n = t.to(dt)
+        if torch.equal(n.to(t.dtype), t):
+            return n
+    raise ValueError(f"{name}: {t.dtype} values are exact in neither bf16 nor fp16")
 
 
 def _qtensor(ts: dict, prefix: str, N: int, K: int) -> QTensor:
@@ -152,7 +167,8 @@ def _qtensor(ts: dict, prefix: str, N: int, K: int) -> QTensor:
     if tuple(w.shape) != (N, K // 4) or tuple(s.shape) != (N, K // GROUP) or tuple(b.shape) != (N, K // GROUP):
         raise ValueError(f"{prefix}: shapes {tuple(w.shape)}, {tuple(s.shape)}, {tuple(b.shape)} do "
                          f"not fit an 8-bit group-64 [{N}, {K}] linear")
-    return QTensor(unpack_u8x4(w), _as_bf16(s, prefix + ".scales"), _as_bf16(b, prefix + ".biases"))
+    return QTensor(unpack_u8x4(w), _scale_dtype(s, prefix + ".scales"),
+                   _scale_dtype(b, prefix + ".biases"))
 
 
 # ------------------------------------------------------------------------------------------

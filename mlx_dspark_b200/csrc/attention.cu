@@ -82,6 +82,7 @@ struct Args {
   int ldo;
   float* ws_o;   // [B*Hkv][nsplit][R][HD]
   float* ws_ml;  // [B*Hkv][nsplit][R][2]
+  int* status;   // DSPARK_ERR_RANGE if an output is past the fp16 range (NULL: unchecked)
 };
 
 // One query row of the merge: lanes over the head dimension, splits in order (max, then the
@@ -125,9 +126,12 @@ __device__ __forceinline__ void merge_row(const Args& a, int b, int h, int r, in
   const int t = r % a.T, g = r / a.T;
   __half* dst = a.out + (size_t)(b * a.T + t) * a.ldo + (size_t)(h * a.G + g) * HD + lane * E;
 #pragma unroll
-  for (int k = 0; k < E; k += 2)
-    *reinterpret_cast<__half2*>(dst + k) =
-        __floats2half2_rn(bf16_round(acc[k] * inv), bf16_round(acc[k + 1] * inv));
+  for (int k = 0; k < E; k += 2) {
+    const float o0 = bf16_round(acc[k] * inv), o1 = bf16_round(acc[k + 1] * inv);
+    check_f16(o0, a.status);
+    check_f16(o1, a.status);
+    *reinterpret_cast<__half2*>(dst + k) = __floats2half2_rn(o0, o1);
+  }
 }
 
 template <int HD, bool KV8>
@@ -342,8 +346,18 @@ __global__ void __launch_bounds__(256) attn_kernel(const Args a) {
 #pragma unroll
     for (int j = 0; j < HD / 8; ++j) {
       const int d = j * 8 + (lane & 3) * 2;
-      if (d0) *reinterpret_cast<__half2*>(d0 + d) = __floats2half2_rn(bf16_round(o[j][0] * inv0), bf16_round(o[j][1] * inv0));
-      if (d1) *reinterpret_cast<__half2*>(d1 + d) = __floats2half2_rn(bf16_round(o[j][2] * inv1), bf16_round(o[j][3] * inv1));
+      const float v0 = bf16_round(o[j][0] * inv0), v1 = bf16_round(o[j][1] * inv0);
+      const float v2 = bf16_round(o[j][2] * inv1), v3 = bf16_round(o[j][3] * inv1);
+      if (d0) {
+        check_f16(v0, a.status);
+        check_f16(v1, a.status);
+        *reinterpret_cast<__half2*>(d0 + d) = __floats2half2_rn(v0, v1);
+      }
+      if (d1) {
+        check_f16(v2, a.status);
+        check_f16(v3, a.status);
+        *reinterpret_cast<__half2*>(d1 + d) = __floats2half2_rn(v2, v3);
+      }
     }
     return;
   }
@@ -431,6 +445,7 @@ extern "C" int dspark_attention(const void* q, int B, int T, int Hq, const dspar
   a.kv_len = kv_len;
   a.out = static_cast<__half*>(out);
   a.ldo = ldo;
+  a.status = status;
   a.ws_ml = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + off_ml);
   a.ws_o = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + off_o);
   const int warps = (R + 15) / 16;

@@ -42,6 +42,13 @@ __device__ __forceinline__ void report_error(int* status, int code) {
   if (status != nullptr) atomicCAS(status, 0, code);
 }
 
+// A value about to be stored as an fp16 GEMM operand: bf16 values are exact in fp16 only
+// inside its range, so one past it (or a NaN) is reported as DSPARK_ERR_RANGE rather than
+// passed on silently as an infinity.
+__device__ __forceinline__ void check_f16(float v, int* status) {
+  if (!(fabsf(v) <= 65504.0f)) report_error(status, DSPARK_ERR_RANGE);
+}
+
 __device__ __forceinline__ float bf16_round(float x) {
   return __bfloat162float(__float2bfloat16_rn(x));
 }

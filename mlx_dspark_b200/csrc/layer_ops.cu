@@ -95,11 +95,13 @@ __global__ void __launch_bounds__(256) embed_block_w8_kernel(const int32_t* __re
 // bf16 -> fp16 copy of a [rows, cols] block (hidden-state taps into the fused GEMM input)
 __global__ void __launch_bounds__(256) bf16_to_f16_kernel(const __nv_bfloat16* __restrict__ src,
                                                           int lds, __half* __restrict__ dst,
-                                                          int ldd, int cols) {
+                                                          int ldd, int cols, int* status) {
   pdl_enter();
   const int r = blockIdx.x;
   for (int c = threadIdx.x * 2; c < cols; c += blockDim.x * 2) {
     const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + (size_t)r * lds + c));
+    check_f16(v.x, status);
+    check_f16(v.y, status);
     *reinterpret_cast<__half2*>(dst + (size_t)r * ldd + c) = __floats2half2_rn(v.x, v.y);
   }
 }
@@ -245,12 +247,12 @@ extern "C" int dspark_embed_block_w8(const int32_t* pending, int B, int k, int m
 }
 
 extern "C" int dspark_bf16_to_f16(const void* src, int lds, void* dst, int ldd, int rows, int cols,
-                                  dspark_stream_t stream) {
+                                  int* status, dspark_stream_t stream) {
   if (!src || !dst || rows <= 0 || cols <= 0 || cols % 2 || lds % 2 || ldd % 2)
     return set_error(DSPARK_ERR_INVALID, "bf16_to_f16: bad arguments");
   return launch_pdl("bf16_to_f16", bf16_to_f16_kernel, dim3(rows), dim3(256), 0,
                     static_cast<cudaStream_t>(stream), static_cast<const __nv_bfloat16*>(src), lds,
-                    static_cast<__half*>(dst), ldd, cols);
+                    static_cast<__half*>(dst), ldd, cols, status);
 }
 
 // h = bf16(h + bf16(sum)): the residual epilogue of a row-split projection whose fp32

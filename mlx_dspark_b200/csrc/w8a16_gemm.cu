@@ -128,7 +128,12 @@ __device__ __forceinline__ void store_staged_rows(const PT& p, int tile, int er,
       uint4 h;
       __half2* h2 = reinterpret_cast<__half2*>(&h);
 #pragma unroll
-      for (int k = 0; k < 4; ++k) h2[k] = __float22half2_rn(__bfloat1622float2(b2[k]));
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __bfloat1622float2(b2[k]);
+        check_f16(f.x, p.status);
+        check_f16(f.y, p.status);
+        h2[k] = __float22half2_rn(f);
+      }
       *reinterpret_cast<uint4*>(p.copy16 + (size_t)m * p.copy16_ld + tile * BM + c * 8) = h;
     }
   }
@@ -256,7 +261,10 @@ __device__ __forceinline__ void epilogue_store(const PT& p, int tile, int er, co
           }
 #pragma unroll
           for (int j = 0; j < 16; ++j)
-            if (c0 + j < p.M) y[(size_t)(c0 + j) * p.ldy + col] = __float2half_rn(a[j]);
+            if (c0 + j < p.M) {
+              check_f16(a[j], p.status);
+              y[(size_t)(c0 + j) * p.ldy + col] = __float2half_rn(a[j]);
+            }
         }
       }
       asm volatile("bar.sync 1, 128;" ::: "memory");

@@ -405,8 +405,9 @@ __global__ void __launch_bounds__(kThreads, 1)
               const float b2 = (j & 1) ? hi_f(other[j >> 1]) : lo_f(other[j >> 1]);
               const float g = gate ? a : b2, u = gate ? b2 : a;
               const float sg = bf16_round(silu_f(g));
-              *reinterpret_cast<__half*>(bp + (row0 + j) * 128 + r * 2) =
-                  __float2half_rn(bf16_round(sg * u));
+              const float act = bf16_round(sg * u);
+              check_f16(act, p.status);
+              *reinterpret_cast<__half*>(bp + (row0 + j) * 128 + r * 2) = __float2half_rn(act);
             }
           } else {
 #pragma unroll
@@ -430,7 +431,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
               uint16_t* sp = reinterpret_cast<uint16_t*>(bp + j * 256 + er * 2);
-              const __half h = __float2half_rn(__uint_as_float((uint32_t)*sp << 16));
+              const float tv = __uint_as_float((uint32_t)*sp << 16);
+              check_f16(tv, p.status);
+              const __half h = __float2half_rn(tv);
               *sp = *reinterpret_cast<const uint16_t*>(&h);
             }
             fence_proxy_async_smem();

@@ -315,8 +315,12 @@ def markov_sample_block(base: torch.Tensor, rows_per_b: int, B: int, cap: int, w
          ws.numel(), _p(scratch.status), _stream())
 
 
-def bf16_to_f16(src: torch.Tensor, dst: torch.Tensor, rows: int, cols: int) -> None:
-    call("dspark_bf16_to_f16", _p(src), src.stride(0), _p(dst), dst.stride(0), rows, cols, _stream())
+def bf16_to_f16(src: torch.Tensor, dst: torch.Tensor, rows: int, cols: int,
+                status: torch.Tensor | None = None) -> None:
+    """dst[:rows, :cols] = fp16(src); a value past the fp16 range sets DSPARK_ERR_RANGE in
+    `status` (a Scratch.status word)."""
+    call("dspark_bf16_to_f16", _p(src), src.stride(0), _p(dst), dst.stride(0), rows, cols,
+         _p(status), _stream())
 
 
 def apply_penalties(logits: torch.Tensor, B: int, T: int, counts: torch.Tensor,

@@ -238,7 +238,7 @@ class TPTarget(Target):
             self._row_parallel(buf.act16, L.down, buf.h, M)
             if l in tap_idx:
                 j = tap_idx[l]
-                ops.bf16_to_f16(buf.h, buf.fused16[:, j * H:(j + 1) * H], M, H)
+                ops.bf16_to_f16(buf.h, buf.fused16[:, j * H:(j + 1) * H], M, H, sc.status)
         if with_logits:
             ops.rmsnorm(buf.h, self.norm, c.rms_norm_eps, y16=buf.xn16, M=M)
             ops.gemm(buf.xn16, self.head, buf.logits, epilogue=EPI_STORE_BF16, scratch=sc, M=M)
@@ -251,7 +251,7 @@ class TPTarget(Target):
         self._all_reduce(part)
         ops.residual_add_f32(h, part, T)
         if copy16 is not None:
-            ops.bf16_to_f16(h, copy16, T, h.shape[1])
+            ops.bf16_to_f16(h, copy16, T, h.shape[1], self.scratch.status)
 
     # ------------------------------------------------------------------ vocab-parallel argmax
     def _shard_bufs(self, rows: int):

@@ -34,7 +34,7 @@ class QTensor:
     """Canonical W8 affine group-64 tensor."""
 
     q: torch.Tensor       # uint8 [N, K]
-    scales: torch.Tensor  # bf16 [N, K/64]
+    scales: torch.Tensor  # bf16 (or an fp16 checkpoint's fp16) [N, K/64]
     biases: torch.Tensor  # bf16 [N, K/64]
 
     @property
@@ -242,14 +242,18 @@ class PackedLinear:
 
 
 def _sb(scales: torch.Tensor, biases: torch.Tensor) -> torch.Tensor:
-    """bf16 (scale, bias) [N, G] -> int32 [G, N] of fp16 pairs (exactness checked)."""
+    """(scale, bias) [N, G] -> int32 [G, N] of fp16 pairs, the GEMM's dequantization operands.
+    fp16 holds every bf16 value of magnitude 2^-17 .. 65504 exactly (11 significand bits
+    against 8) and every fp16 checkpoint value. Smaller magnitudes (the groups of a nearly
+    constant weight row; MLX's quantizer floors a scale at 1e-7) round to fp16 subnormals, an
+    absolute error of at most 2^-25 per scale or bias, so at most 255 * 2^-25 ~ 7.6e-6 on a
+    weight of such a group. Values past the fp16 range are refused."""
     s16 = scales.to(torch.float16)
     b16 = biases.to(torch.float16)
-    for a, b, name in ((s16, scales, "scale"), (b16, biases, "bias")):
-        back = a.to(torch.float32)
-        if not torch.equal(back, b.to(torch.float32)):
-            bad = (back != b.to(torch.float32)).sum().item()
-            raise ValueError(f"{bad} W8 {name} values are not exactly representable in fp16")
+    for a, name in ((s16, "scale"), (b16, "bias")):
+        if not torch.isfinite(a).all():
+            bad = (~torch.isfinite(a)).sum().item()
+            raise ValueError(f"{bad} W8 {name} values are outside the fp16 range")
     lo = s16.view(torch.int16).to(torch.int32) & 0xFFFF
     hi = b16.view(torch.int16).to(torch.int32) << 16
     return (lo | hi).t().contiguous()

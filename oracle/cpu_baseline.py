@@ -77,7 +77,7 @@ class StreamingDecoder:
     def _lin(self, x, qt):
         N, K = qt.q.shape
         lib = _gemv_lib()
-        if lib is not None:
+        if lib is not None and qt.scales.dtype == torch.bfloat16 and qt.biases.dtype == torch.bfloat16:
             import ctypes
             xc = x.to(F32).contiguous()
             out = torch.empty(N, dtype=F32)

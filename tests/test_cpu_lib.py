@@ -60,11 +60,42 @@ def test_pack_layout_and_interleave():
     assert s == u.scales[1, 1].float() and b == u.biases[1, 1].float()
 
 
-def test_pack_rejects_values_fp16_cannot_hold():
-    qt = quantize_w8g64(torch.randn(128, 128) * 0.02)
-    qt.scales[0, 0] = torch.tensor(1e-7).to(torch.bfloat16)
+def test_pack_rounds_tiny_scales_and_refuses_fp16_overflow():
+    """Scales and biases below fp16's normal range (groups of nearly constant weights; MLX floors
+    a scale at 1e-7) pack as fp16 subnormals within 2^-25; values past 65504 are refused."""
+    g = torch.Generator().manual_seed(5)
+    w = torch.randn(256, 256, generator=g) * 0.02
+    w[0, :64] = 0.0                                      # constant group: scale floor 1e-7
+    w[1, :64] = 0.01 + torch.arange(64) * 1e-7           # range 6.3e-6: scale ~2.5e-8
+    qt = quantize_w8g64(w)
+    # a synthetic scale distribution down to 2^-30, and biases of either sign below 2^-17
+    qt.scales[2:, 0] = (2.0 ** -torch.linspace(4, 30, 254)).to(torch.bfloat16)
+    qt.biases[2:, 1] = (-(2.0 ** -torch.linspace(17, 28, 254))).to(torch.bfloat16)
+    assert float(qt.scales.float().abs().min()) < 2.0 ** -17
+    pl = pack(qt, device="cpu")
+    sb = pl.sb.t().contiguous()                          # [N, G] int32 of fp16 pairs
+    s16 = (sb & 0xFFFF).to(torch.int16).view(torch.float16).float()
+    b16 = (sb >> 16).to(torch.int16).view(torch.float16).float()
+    assert (s16 - qt.scales.float()).abs().max() <= 2.0 ** -25
+    assert (b16 - qt.biases.float()).abs().max() <= 2.0 ** -25
+    # and exactly where fp16 holds the value
+    big = qt.scales.float().abs() >= 2.0 ** -17
+    assert torch.equal(s16[big], qt.scales.float()[big])
+    qt.scales[0, 0] = torch.tensor(1e5).to(torch.bfloat16)
     with pytest.raises(ValueError):
         pack(qt, device="cpu")
+
+
+def test_checkpoint_keeps_fp16_scales():
+    """An fp16 source model's 8-bit checkpoint: scales and biases stay fp16 (packed exactly),
+    norm weights are rounded to bf16."""
+    from mlx_dspark_b200.checkpoint import _as_bf16, _scale_dtype
+    s = (torch.rand(4, 4) * 1e-3).to(torch.float16)
+    assert _scale_dtype(s, "s").dtype == torch.float16
+    assert _scale_dtype(s.float(), "s").dtype in (torch.bfloat16, torch.float16)
+    with pytest.raises(ValueError):
+        _scale_dtype(torch.tensor([1.0 + 2.0 ** -20]), "s")
+    assert _as_bf16(torch.ones(4, dtype=torch.float16) * 1.001, "n").dtype == torch.bfloat16
 
 
 def test_gemm_opts_struct_matches_the_c_layout():
