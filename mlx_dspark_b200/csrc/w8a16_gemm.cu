@@ -1107,24 +1107,3 @@ extern "C" int dspark_w8a16_gemm_peer(const void* x, int ldx, const uint8_t* wq,
                      nullptr, nullptr, status, stream, ar);
 }
 
-// The q|k|v RoPE epilogue's arguments, checked as dspark_w8a16_gemm_qkv_rope checks them.
-static int make_rope(w8::RopeEpi* r, int M, int T, int Hq, int Hkv, int hd, const void* q_norm_w,
-                     const void* k_norm_w, float eps, const float* inv_freq, const int32_t* pos0,
-                     void* q_out, const dspark_kv_layout* kv, const char* what) {
-  if (hd != 64 && hd != 128) return set_error(DSPARK_ERR_UNSUPPORTED, "%s: head_dim %d", what, hd);
-  if (T <= 0 || M % T || Hkv <= 0 || Hq < 0 || !k_norm_w || !inv_freq || !pos0 || !kv ||
-      !kv->pool || !kv->block_table || (Hq > 0 && (!q_out || !q_norm_w)))
-    return set_error(DSPARK_ERR_INVALID, "%s: bad RoPE arguments", what);
-  if (kv->head_dim != hd || kv->num_kv_heads != Hkv || kv->page_size <= 0 ||
-      kv->page_bytes != dspark_kv_page_bytes(kv->page_size, Hkv, hd, kv->kv8))
-    return set_error(DSPARK_ERR_INVALID, "%s: kv layout does not match", what);
-  r->qnw = static_cast<const __nv_bfloat16*>(q_norm_w);
-  r->knw = static_cast<const __nv_bfloat16*>(k_norm_w);
-  r->inv_freq = inv_freq;
-  r->pos0 = pos0;
-  r->q_out = static_cast<__nv_bfloat16*>(q_out);
-  r->kv = *kv;
-  r->eps = eps;
-  r->T = T; r->Hq = Hq; r->Hkv = Hkv; r->hd = hd;
-  return DSPARK_OK;
-}
