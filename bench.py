@@ -572,6 +572,88 @@ def run_tp(args, world, rank):
     }
 
 
+def run_c3(args, world, rank):
+    """C3: Qwen3-4B W8 with the DFlash drafter (2 layers, block 16), sampled at T 1.0,
+    top-p 0.95, top-k 50, one request per GPU (replicas under torchrun). Device time of K
+    captured rounds (the rejection-sampling acceptance and every draw on the device), then
+    the public dflash_generate loop end to end. With random weights the drafter's q and the
+    target's p are unrelated, so few drafts are accepted: the line measures the sampled
+    round's machinery (draft, verify, accept, residual draws), not speculation."""
+    from mlx_dspark_b200 import _lib
+    from mlx_dspark_b200.config import TARGETS, WORKLOADS, dflash_for, with_layers
+    from mlx_dspark_b200.generate import SpecSession, _pick_first, dflash_generate, prefill_rows
+    from mlx_dspark_b200.model import DFlashDrafter, Sampling
+    from mlx_dspark_b200.target import Target
+    from mlx_dspark_b200.weights import generate_dflash, generate_target
+
+    wl = WORKLOADS["C3"]
+    K, W = args.steps, args.warmup
+    tcfg = TARGETS[wl.target]
+    if args.layers:
+        tcfg = with_layers(tcfg, args.layers)
+    fcfg = dflash_for(tcfg, block_size=wl.block_size)
+    tw = generate_target(tcfg, wl.seed, "cuda")
+    target = Target(tw, kv_bits=wl.kv_bits)
+    del tw
+    drafter = DFlashDrafter(generate_dflash(fcfg, wl.seed, "cuda"), target)
+    torch.cuda.empty_cache()
+    cap = wl.block_size - 1
+    prompt_len = args.prompt_len or wl.prompt_len
+    prompt = torch.randint(0, tcfg.vocab_size, (prompt_len,),
+                           generator=torch.Generator().manual_seed(wl.seed + rank)).tolist()
+    sm = Sampling(wl.temperature, wl.top_p, wl.top_k)
+    sess = SpecSession(target, drafter, 1, cap, prompt_len + (K + W + 2) * (cap + 1) + 64,
+                       sampling=sm, seeds=[wl.seed + rank])
+    last = prefill_rows(target, prompt, sess.tstate, sess.tap, drafter, sess.cstate)
+    sess.pending.fill_(_pick_first(target, last, sm, sess.rng))
+    n0 = _lib.LAUNCHES["n"]
+    sess.step(use_graph=False)
+    launches = _lib.LAUNCHES["n"] - n0
+    sess.capture()
+    clocks = ClockSampler(torch.cuda.current_device())
+    clocks.start()
+    for _ in range(max(0, W - 1)):
+        sess.graph.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    len0 = int(sess.tstate.seq_len[0])
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(K):
+        sess.graph.replay()
+    b.record()
+    torch.cuda.synchronize()
+    tokens = int(sess.tstate.seq_len[0]) - len0
+    clk = clocks.stop()
+    target.scratch.check_status()
+    sess.release()
+    ms = allreduce_max(a.elapsed_time(b), world)
+    value = allreduce_sum(float(tokens), world) / (ms / 1000.0)
+    res = dflash_generate(target, None, drafter, prompt_ids=prompt, max_new_tokens=wl.new_tokens,
+                          temperature=wl.temperature, top_p=wl.top_p, top_k=wl.top_k,
+                          seed=wl.seed + rank)
+    e2e = allreduce_sum((res.num_tokens - 1) / res.decode_seconds, world)
+    return {
+        "metric": "accepted tok/s Qwen3-4B W8 DFlash block 16, sampled (T 1.0, top-p 0.95, top-k 50)",
+        "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": round(ms / K, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "w8a16 (int8 weights, fp16 MMA, fp32 accumulate, bf16 activations)",
+        "data": "synthetic: random-init W8 g64 weights (seed 0), random prompt ids; drafts and "
+                "acceptance sampled on the device (Philox)",
+        "config": {"workload": wl.name, "model": f"Qwen3-4B-arch W8 g64 ({tcfg.num_hidden_layers} "
+                   "layers) + DFlash 2-layer block 16", "global_batch": world, "prompt_len": prompt_len,
+                   "draft_cap": cap, "parallelism": f"request-parallel x{world} (replicas)",
+                   "l2": "inputs larger than L2 (4.4 GB of weights streamed per round)"},
+        "round_us": round(ms * 1000.0 / K, 1), "mean_accept_len": round(tokens / K, 3),
+        "gpu_launches": launches * K, "clocks": clk,
+        "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 4 * (cap + 3),
+                "api": "mlx_dspark_b200.dflash_generate (host loop, one sync per round)",
+                "rounds": res.num_rounds, "mean_accept_len": round(res.mean_accept_len, 3)},
+    }
+
+
 def run_serve(args):
     """C4 continuous batching: 32 requests (a shared random 2048-token prefix plus a random
     64-2048-token suffix, 128-1024 output tokens) over N GPUs, one ReplicaPool worker process
@@ -838,6 +920,8 @@ def main():
     try:
         if args.workload == "C5" and world > 1:
             out = run_tp(args, world, rank)
+        elif args.workload == "C3":
+            out = run_c3(args, world, rank)
         else:
             out = run_ours(args, world, rank)
         if rank == 0:
