@@ -65,6 +65,8 @@ def parse():
     ap.add_argument("--tp-allreduce", action="store_true",
                     help="under torchrun (2..8 ranks): one row-split projection of the Qwen3-32B "
                          "shapes at M = 9, the fused peer all-reduce against NCCL, one JSON line")
+    ap.add_argument("--attention-sweep", action="store_true",
+                    help="verify attention alone at 1k/5k/16.9k context (bf16 and KV8), one JSON line")
     ap.add_argument("--serve", action="store_true",
                     help="the continuous-batching workload (C4 shapes: 32 requests, 4 slots per GPU, "
                          "a shared 2048-token prefix, 8-bit KV) over --gpus replicas, one JSON line "
@@ -654,6 +656,61 @@ def run_c3(args, world, rank):
     }
 
 
+def run_attention_sweep(args):
+    """Verify attention alone (C2 shape: 1 row, 9 block tokens, 32 q / 8 kv heads, hd 128),
+    causal, at 1k, 5k and 16.9k tokens of context, bf16 and 8-bit pages: CUDA events over 200
+    back-to-back calls (after 20), µs per call and the KV bytes read per call over that time
+    against the measured HBM copy peak."""
+    from mlx_dspark_b200 import ops
+    from mlx_dspark_b200.kvcache import CacheState, PagePool
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    B, T, Hq, Hkv, hd = 1, 9, 32, 8, 128
+    peaks = load_peaks()
+    out = {"metric": "verify attention us per call (B 1, T 9, 32q/8kv, hd 128)", "unit": "us",
+           "higher_is_better": False, "n_gpus": 1, "data": "synthetic: random q and KV pages",
+           "peak_gbs": peaks["hbm_gbs"], "rows": []}
+    g = torch.Generator(device=dev).manual_seed(3)
+    for kv8 in (False, True):
+        for ctx in (1024, 5120, 16896):
+            tokens = ctx + T
+            pool = PagePool(1, (tokens + 63) // 64 + 1, Hkv, hd, kv8, dev)
+            st = CacheState(pool, B, tokens, dev)
+            st.ensure(0, tokens)
+            if not kv8:  # (8-bit pages stay zero-filled: codes and scales of a valid cache)
+                d = pool.data.view(torch.bfloat16)
+                d.copy_(torch.randn(d.shape, generator=g, device=dev).to(torch.bfloat16))
+            st.seq_len.fill_(ctx)
+            q = torch.randn(B * T, Hq * hd, generator=g, device=dev).to(torch.bfloat16)
+            o = torch.zeros(B * T, Hq * hd, dtype=torch.float16, device=dev)
+            sc = ops.Scratch(dev)
+            splits = max(1, min(256, 296 // (B * Hkv)))
+
+            def call():
+                ops.attention(q, B, T, Hq, st.layout(0), st.seq_len, True, hd ** -0.5, o, splits, sc)
+
+            for _ in range(20):
+                call()
+            torch.cuda.synchronize()
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(200):
+                call()
+            b.record()
+            torch.cuda.synchronize()
+            sc.check_status()
+            us = a.elapsed_time(b) * 1000.0 / 200
+            per_tok = 2 * Hkv * (hd + (hd // 64) * 4 if kv8 else hd * 2)
+            byts = tokens * per_tok
+            out["rows"].append({"context": ctx, "kv8": kv8, "us": round(us, 2),
+                                "kv_bytes": byts, "gbs": round(byts / us / 1e3, 1),
+                                "frac": round(byts / us / 1e3 / peaks["hbm_gbs"], 4)})
+            st.release()
+    print(json.dumps(out), flush=True)
+    return 0
+
+
 def run_serve(args):
     """C4 continuous batching: 32 requests (a shared random 2048-token prefix plus a random
     64-2048-token suffix, 128-1024 output tokens) over N GPUs, one ReplicaPool worker process
@@ -824,6 +881,9 @@ def run_ours(args, world, rank):
         # cap (3.20 at p = 0.7, cap 8): removes the mask sample's noise from the comparison
         "expected_accept_len": round(expect_len, 3),
         "value_at_expected_accept": round(world * expect_len / (max_ms / 1000.0 / K), 2),
+        # the north star quotes its targets at a mean accept length of 3.5 (the config's
+        # Bernoulli(0.7) mask over cap 8 expects 3.20): tok/s at this round time and 3.5 tokens
+        "value_at_accept_3_5": round(world * 3.5 / (max_ms / 1000.0 / K), 2),
         "per_rank": per_rank,
         "verify_hbm_gbs": round(target.weight_bytes() / (vus * 1e-6) / 1e9, 1),
         "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
@@ -841,10 +901,14 @@ def run_ours(args, world, rank):
                                    draft_override=override)
         e2e_tps = (res.num_tokens - 1) / res.decode_seconds
         e2e_all = allreduce_sum(e2e_tps, world)
+        hist = {}
+        for n in res.accept_lengths:
+            hist[str(n)] = hist.get(str(n), 0) + 1
         out["e2e"] = {"value": round(e2e_all, 2), "unit": "tok/s",
                       "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4 * (cap + 3),
                       "api": "mlx_dspark_b200.speculative_generate (host loop, one sync per round)",
                       "rounds": res.num_rounds, "mean_accept_len": round(res.mean_accept_len, 3),
+                      "committed_per_round": dict(sorted(hist.items(), key=lambda kv: int(kv[0]))),
                       "prefill_s": round(res.seconds - res.decode_seconds, 3)}
     if not args.profile:
         out["prefill"] = prefill_measure(target, drafter, prompt)
@@ -912,6 +976,9 @@ def main():
         return 0
     if args.serve:
         return run_serve(args)       # one process per GPU of its own (ReplicaPool)
+    if args.attention_sweep:
+        torch.cuda.set_device(0)
+        return run_attention_sweep(args)
     world, rank, _ = dist_setup(args.gpus)
     if args.profile_prefill:
         return run_profile_prefill(args)
