@@ -882,7 +882,8 @@ def run_ours(args, world, rank):
         "expected_accept_len": round(expect_len, 3),
         "value_at_expected_accept": round(world * expect_len / (max_ms / 1000.0 / K), 2),
         # the north star quotes its targets at a mean accept length of 3.5 (the config's
-        # Bernoulli(0.7) mask over cap 8 expects 3.20): tok/s at this round time and 3.5 tokens
+        # Bernoulli(0.7) mask over cap 8 expects 3.20): tok/s at the measured time per decode
+        # round with 3.5 tokens committed per round
         "value_at_accept_3_5": round(world * 3.5 / (max_ms / 1000.0 / K), 2),
         "per_rank": per_rank,
         "verify_hbm_gbs": round(target.weight_bytes() / (vus * 1e-6) / 1e9, 1),
