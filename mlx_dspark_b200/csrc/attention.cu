@@ -180,11 +180,14 @@ __device__ __forceinline__ void dequant_tile(uint8_t* buf) {
       const uint32_t sbv = sb[key * (HD / 64) + d0 / 64];
       const float s = __uint_as_float(sbv << 16), bb = __uint_as_float(sbv & 0xFFFF0000u);
       const uint2 q8 = *reinterpret_cast<const uint2*>(qs + key * HD + d0);
-      __nv_bfloat16 o[8];
+      __nv_bfloat162 o[4];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < 8; j += 2) {
         const uint32_t w = j < 4 ? q8.x : q8.y;
-        o[j] = __float2bfloat16_rn(fmaf(s, (float)((w >> (8 * (j & 3))) & 0xFF), bb));
+        // a code byte under the exponent of 2^23 reads as 2^23 + code (exact)
+        const float c0 = __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440 | (j & 3))) - 8388608.0f;
+        const float c1 = __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7441 | (j & 3))) - 8388608.0f;
+        o[j / 2] = __floats2bfloat162_rn(fmaf(s, c0, bb), fmaf(s, c1, bb));
       }
       *reinterpret_cast<uint4*>(dst + key * L::kRow + d0) = *reinterpret_cast<const uint4*>(o);
     }
@@ -251,83 +254,86 @@ __global__ void __launch_bounds__(256) attn_kernel(const Args a) {
       dequant_tile<HD>(cur);
       __syncthreads();
     }
-    const uint32_t ks = smem_u32(cur), vs = smem_u32(cur + L::kTile);
-    // S = Q K^T over 64 keys (8 n-tiles of 8 keys)
-    float s[8][4];
+    // warps past the last query row only help stage and dequantise the pages
+    if (warp * 16 < a.R) {
+      const uint32_t ks = smem_u32(cur), vs = smem_u32(cur + L::kTile);
+      // S = Q K^T over 64 keys (8 n-tiles of 8 keys)
+      float s[8][4];
 #pragma unroll
-    for (int jn = 0; jn < 8; ++jn) s[jn][0] = s[jn][1] = s[jn][2] = s[jn][3] = 0.0f;
+      for (int jn = 0; jn < 8; ++jn) s[jn][0] = s[jn][1] = s[jn][2] = s[jn][3] = 0.0f;
 #pragma unroll
-    for (int jn = 0; jn < 8; ++jn) {
+      for (int jn = 0; jn < 8; ++jn) {
 #pragma unroll
-      for (int kk = 0; kk < HD / 16; kk += 2) {
-        uint32_t b0, b1, b2, b3;
-        const int row = jn * 8 + (lane & 7);
-        const int col = kk * 16 + (lane >> 3) * 8;
-        ldsm_x4(ks + (row * L::kRow + col) * 2, b0, b1, b2, b3);
-        mma_bf16(s[jn], qf[kk], b0, b1);
-        mma_bf16(s[jn], qf[kk + 1], b2, b3);
+        for (int kk = 0; kk < HD / 16; kk += 2) {
+          uint32_t b0, b1, b2, b3;
+          const int row = jn * 8 + (lane & 7);
+          const int col = kk * 16 + (lane >> 3) * 8;
+          ldsm_x4(ks + (row * L::kRow + col) * 2, b0, b1, b2, b3);
+          mma_bf16(s[jn], qf[kk], b0, b1);
+          mma_bf16(s[jn], qf[kk + 1], b2, b3);
+        }
       }
-    }
-    // mask + online softmax (rows r0 and r1 of this thread)
-    const int kbase = p * KT + (lane & 3) * 2;
-    float mx0 = -INFINITY, mx1 = -INFINITY;
+      // mask + online softmax (rows r0 and r1 of this thread)
+      const int kbase = p * KT + (lane & 3) * 2;
+      float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
-    for (int jn = 0; jn < 8; ++jn) {
+      for (int jn = 0; jn < 8; ++jn) {
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        const int key = kbase + jn * 8 + c;
-        s[jn][c] = (key <= lim0) ? s[jn][c] * a.scale_log2 : -INFINITY;
-        s[jn][2 + c] = (key <= lim1) ? s[jn][2 + c] * a.scale_log2 : -INFINITY;
-        mx0 = fmaxf(mx0, s[jn][c]);
-        mx1 = fmaxf(mx1, s[jn][2 + c]);
+        for (int c = 0; c < 2; ++c) {
+          const int key = kbase + jn * 8 + c;
+          s[jn][c] = (key <= lim0) ? s[jn][c] * a.scale_log2 : -INFINITY;
+          s[jn][2 + c] = (key <= lim1) ? s[jn][2 + c] * a.scale_log2 : -INFINITY;
+          mx0 = fmaxf(mx0, s[jn][c]);
+          mx1 = fmaxf(mx1, s[jn][2 + c]);
+        }
       }
-    }
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-    const float mu0 = mn0 == -INFINITY ? 0.0f : mn0;
-    const float mu1 = mn1 == -INFINITY ? 0.0f : mn1;
-    const float al0 = exp2f(m0 - mu0), al1 = exp2f(m1 - mu1);
-    m0 = mn0;
-    m1 = mn1;
-    float sum0 = 0.0f, sum1 = 0.0f;
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+      const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+      const float mu0 = mn0 == -INFINITY ? 0.0f : mn0;
+      const float mu1 = mn1 == -INFINITY ? 0.0f : mn1;
+      const float al0 = exp2f(m0 - mu0), al1 = exp2f(m1 - mu1);
+      m0 = mn0;
+      m1 = mn1;
+      float sum0 = 0.0f, sum1 = 0.0f;
 #pragma unroll
-    for (int jn = 0; jn < 8; ++jn) {
-      s[jn][0] = exp2f(s[jn][0] - mu0);
-      s[jn][1] = exp2f(s[jn][1] - mu0);
-      s[jn][2] = exp2f(s[jn][2] - mu1);
-      s[jn][3] = exp2f(s[jn][3] - mu1);
-      sum0 += s[jn][0] + s[jn][1];
-      sum1 += s[jn][2] + s[jn][3];
-    }
-    l0 = l0 * al0 + sum0;
-    l1 = l1 * al1 + sum1;
+      for (int jn = 0; jn < 8; ++jn) {
+        s[jn][0] = exp2f(s[jn][0] - mu0);
+        s[jn][1] = exp2f(s[jn][1] - mu0);
+        s[jn][2] = exp2f(s[jn][2] - mu1);
+        s[jn][3] = exp2f(s[jn][3] - mu1);
+        sum0 += s[jn][0] + s[jn][1];
+        sum1 += s[jn][2] + s[jn][3];
+      }
+      l0 = l0 * al0 + sum0;
+      l1 = l1 * al1 + sum1;
 #pragma unroll
-    for (int j = 0; j < HD / 8; ++j) {
-      o[j][0] *= al0;
-      o[j][1] *= al0;
-      o[j][2] *= al1;
-      o[j][3] *= al1;
-    }
-    // O += P V (P as bf16 A fragments, 4 k-steps of 16 keys)
+      for (int j = 0; j < HD / 8; ++j) {
+        o[j][0] *= al0;
+        o[j][1] *= al0;
+        o[j][2] *= al1;
+        o[j][3] *= al1;
+      }
+      // O += P V (P as bf16 A fragments, 4 k-steps of 16 keys)
 #pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-      uint32_t pa[4];
-      pa[0] = pack_bf16(s[2 * kk][0], s[2 * kk][1]);
-      pa[1] = pack_bf16(s[2 * kk][2], s[2 * kk][3]);
-      pa[2] = pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-      pa[3] = pack_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+      for (int kk = 0; kk < 4; ++kk) {
+        uint32_t pa[4];
+        pa[0] = pack_bf16(s[2 * kk][0], s[2 * kk][1]);
+        pa[1] = pack_bf16(s[2 * kk][2], s[2 * kk][3]);
+        pa[2] = pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+        pa[3] = pack_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3]);
 #pragma unroll
-      for (int jd = 0; jd < HD / 8; jd += 2) {
-        uint32_t b0, b1, b2, b3;
-        const int mi = lane >> 3;
-        const int row = kk * 16 + (mi & 1) * 8 + (lane & 7);
-        const int col = (jd + (mi >> 1)) * 8;
-        ldsm_x4_t(vs + (row * L::kRow + col) * 2, b0, b1, b2, b3);
-        mma_bf16(o[jd], pa, b0, b1);
-        mma_bf16(o[jd + 1], pa, b2, b3);
+        for (int jd = 0; jd < HD / 8; jd += 2) {
+          uint32_t b0, b1, b2, b3;
+          const int mi = lane >> 3;
+          const int row = kk * 16 + (mi & 1) * 8 + (lane & 7);
+          const int col = (jd + (mi >> 1)) * 8;
+          ldsm_x4_t(vs + (row * L::kRow + col) * 2, b0, b1, b2, b3);
+          mma_bf16(o[jd], pa, b0, b1);
+          mma_bf16(o[jd + 1], pa, b2, b3);
+        }
       }
     }
     __syncthreads();
@@ -448,7 +454,8 @@ extern "C" int dspark_attention(const void* q, int B, int T, int Hq, const dspar
   a.status = status;
   a.ws_ml = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + off_ml);
   a.ws_o = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + off_o);
-  const int warps = (R + 15) / 16;
+  // (R + 15) / 16 warps hold query rows; 8-bit pages get at least 4 warps to dequantise them
+  const int warps = kv->kv8 ? max((R + 15) / 16, 4) : (R + 15) / 16;
   const dim3 grid(max_splits, Hkv, B), block(warps * 32);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   auto go = [&](auto kern, auto combine, int smem) {
