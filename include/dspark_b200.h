@@ -472,6 +472,16 @@ int dspark_argmax_rows(const void* logits, long long ld, int rows, int V, int32_
                        int tok_stride, int32_t* tokens2, int tok2_stride, float* values,
                        int index_offset, dspark_stream_t stream);
 
+/* Per-token logprobs of committed tokens (_logprobs_for_block, src/mlx_dspark/generate.py:149-176):
+ * the raw log-softmax of each row, logp = x - max(x) - log(sum(exp(x - max(x)))) in fp32.
+ * Row r's token is ids[(r / T) * ids_ld + r % T] (a plan row's committed tokens: ids = plan + 2,
+ * ids_ld = T + 2); logp[r] = its entry, NaN for a token outside [0, V). With top_k > 0 the
+ * min(top_k, V) largest entries go to top_ids / top_logp [rows, top_k] in descending order,
+ * equal values by smaller index. top_k <= 1024. One CTA per row. */
+int dspark_logprobs(const void* logits, long long ld, int rows, int V, const int32_t* ids,
+                    int ids_ld, int T, int top_k, float* logp, int32_t* top_ids, float* top_logp,
+                    dspark_stream_t stream);
+
 /* Tensor-parallel pieces (BASELINE C5: Qwen3-32B at TP 2/4/8; NCCL all-reduce after o_proj
  * and down_proj). The reference runs on one device and has no counterpart; they stand in for
  * its single-device o_proj / down_proj residual adds and the lm_head argmax.

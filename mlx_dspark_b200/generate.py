@@ -30,6 +30,7 @@ import torch
 
 from . import ops
 from .kvcache import CacheState, RowView
+from .logprobs import LogprobRows
 from .model import Sampling
 from .target import PREFILL_CHUNK
 
@@ -211,7 +212,7 @@ class SpecSession:
     def __init__(self, target, drafter, B: int, cap: int, max_tokens: int, *,
                  override: dict | None = None, sampling: Sampling | None = None,
                  seeds=None, penalties: tuple[float, float] = (0.0, 0.0), states=None,
-                 max_cap: int | None = None):
+                 max_cap: int | None = None, logprobs: int | None = None):
         if getattr(drafter, "target", None) is not target:
             drafter.bind(target)   # a drafter from load_drafter / load_dflash comes unbound
         self.target, self.drafter = target, drafter
@@ -227,6 +228,14 @@ class SpecSession:
         if any(self.penalties):
             self.counts = torch.zeros(B, target.cfg.vocab_size, dtype=torch.int32,
                                       device=target.device)
+        # per-token logprobs of the committed tokens (rows of a drafter round or of a lookup
+        # round, up to 64 wide), read from a raw copy of the logits when penalties are on
+        self.lp = None
+        if logprobs is not None:
+            if getattr(target, "world", 1) > 1:
+                raise NotImplementedError("logprobs of a tensor-parallel target are not built")
+            self.lp = LogprobRows(target.device, max(B * (self.max_cap + 1), 64), logprobs,
+                                  target.cfg.vocab_size, raw=self.counts is not None)
         self.k = drafter.block_size
         self.tap = list(drafter.config.target_layer_ids)
         dev = target.device
@@ -309,6 +318,8 @@ class SpecSession:
             ops.draft_override(B, cap, t.cfg.vocab_size, o["ref"], o["agree"], o["round"],
                                self.tstate.seq_len, o["prompt_len"], self.vbuf.ids)
         t.forward(self.vbuf, self.tstate, self.tap, splits=self.splits_t)
+        if self.lp is not None and self.counts is not None:
+            self.lp.snapshot(self.vbuf.logits, B * T)
         if self.counts is not None:
             ops.apply_penalties(self.vbuf.logits, B, T, self.counts, self.vbuf.ids,
                                 *self.penalties)
@@ -321,6 +332,8 @@ class SpecSession:
                               sc)
         if self.counts is not None:
             ops.penalty_counts_add(self.counts, self.plan, B)
+        if self.lp is not None:
+            self.lp.launch(self.vbuf.logits, B * T, self.plan[:, 2:], T + 2, T)
         d.update_context_dev(self.vbuf.fused16, B, T, self.cstate, self.dbuf)
         ops.commit_lengths(self.plan, B, self.tstate.seq_len, self.cstate.seq_len)
         self.plan_host.copy_(self.plan, non_blocking=True)
@@ -347,6 +360,7 @@ class SpecSession:
         if getattr(self, "_verifier", None) is None:
             self._verifier = BlockVerifier(self.target, self.tstate, self.tap, self.sampling,
                                            self.rng, self.counts, self.penalties, self.pending)
+            self._verifier.lp = self.lp
         T = len(draft) + 1
         buf, plan, plan_host = self._verifier.launch(pending, draft, commit=False)
         self.drafter.update_context_dev(buf.fused16, 1, T, self.cstate,
@@ -400,7 +414,8 @@ def _caller_states(drafter, cache, ctx_caches, reuse_len: int, tokens: int):
 
 def _spec_loop(target, tokenizer, drafter, ids, cap, max_new_tokens, sampling, seed, use_graph,
                draft_override, verbose, penalties=(0.0, 0.0), lookup_max_draft=0, cache=None,
-               ctx_caches=None, reuse_len: int = 0, cap_controller=None) -> GenResult:
+               ctx_caches=None, reuse_len: int = 0, cap_controller=None,
+               logprobs: int | None = None) -> GenResult:
     """The decode loop of speculative_generate / dflash_generate. `cap` is the ceiling; with a
     cap_controller each drafter round uses min(controller.cap, cap) and feeds the outcome back
     (generate.py:846-847,924-925); lookup rounds neither use nor update it."""
@@ -419,7 +434,7 @@ def _spec_loop(target, tokenizer, drafter, ids, cap, max_new_tokens, sampling, s
     first_cap = cap if ctrl is None else max(1, min(int(ctrl.cap), cap))
     sess = SpecSession(target, drafter, 1, first_cap, budget, override=draft_override,
                        sampling=sampling, seeds=[0 if seed is None else int(seed)],
-                       penalties=penalties, states=states, max_cap=cap)
+                       penalties=penalties, states=states, max_cap=cap, logprobs=logprobs)
     try:
         t0 = time.time()
         # prefill only the part of the prompt past the reused prefix (generate.py:640-650)
@@ -428,6 +443,12 @@ def _spec_loop(target, tokenizer, drafter, ids, cap, max_new_tokens, sampling, s
         sess.pending.fill_(pending)
         if sess.counts is not None:
             sess.counts[0, pending] += 1          # pen.add([pending]) (generate.py:784)
+        lp_list = None
+        if sess.lp is not None:
+            # the first token's entry comes from the prefill's last row (generate.py:786-787)
+            sess.lp.launch(last.view(1, -1), 1, sess.pending, 1, 1, use_snapshot=False)
+            torch.cuda.current_stream().synchronize()
+            lp_list = sess.lp.entries([pending])
         index = None
         if lookup_max_draft:
             from .lookup import NGramIndex  # lookup imports this module
@@ -462,6 +483,8 @@ def _spec_loop(target, tokenizer, drafter, ids, cap, max_new_tokens, sampling, s
                 appended.append(tok)
                 if tok in eos_ids:
                     break
+            if lp_list is not None:
+                lp_list.extend(sess.lp.entries(appended))
             if index is not None:
                 index.extend(appended)
             pending = out[-1]
@@ -475,7 +498,8 @@ def _spec_loop(target, tokenizer, drafter, ids, cap, max_new_tokens, sampling, s
         return GenResult(text=text, token_ids=out, num_tokens=len(out), num_rounds=len(accept),
                          accept_lengths=accept, target_forwards=len(accept) + 1,
                          seconds=t2 - t0, decode_seconds=t2 - t1, lookup_rounds=lookup_rounds,
-                         finish_reason=_finish_reason(out, max_new_tokens, pending, eos_ids))
+                         finish_reason=_finish_reason(out, max_new_tokens, pending, eos_ids),
+                         logprobs=lp_list)
     finally:
         sess.release()
         if cache is not None:
@@ -500,8 +524,8 @@ def speculative_generate(target, tokenizer, drafter, prompt: str = "", *,
     temperature 0: the output is the target's greedy decoding. temperature > 0: drafts are drawn
     from the drafter's truncated distributions and accepted by rejection sampling, so the output
     is a sample of top-p/top-k(softmax(target / T)) (lossless); `seed` seeds the Philox stream."""
-    if logprobs is not None or confidence_threshold > 0:
-        raise NotImplementedError("logprobs / confidence truncation are not built")
+    if confidence_threshold > 0:
+        raise NotImplementedError("confidence truncation is not built")
     k = drafter.config.block_size
     cap = k if max_draft_tokens is None else max(1, min(int(max_draft_tokens), k))
     if prompt_ids is None:
@@ -510,7 +534,7 @@ def speculative_generate(target, tokenizer, drafter, prompt: str = "", *,
                       Sampling(temperature, top_p, top_k), seed, use_graph, draft_override,
                       verbose, (presence_penalty, frequency_penalty),
                       max(1, int(lookup_max_draft)) if lookup_drafts else 0, cache, ctx_caches,
-                      reuse_len, cap_controller)
+                      reuse_len, cap_controller, logprobs)
 
 
 def dflash_generate(target_model, tokenizer, drafter, prompt: str = "", *,
@@ -538,7 +562,8 @@ class GreedySession:
     draw kernel advances on the device (so the step stays one CUDA graph)."""
 
     def __init__(self, target, B: int, max_tokens: int, sampling: Sampling | None = None,
-                 seeds=None, penalties: tuple[float, float] = (0.0, 0.0)):
+                 seeds=None, penalties: tuple[float, float] = (0.0, 0.0),
+                 logprobs: int | None = None):
         self.target, self.B = target, B
         self.penalties = (float(penalties[0] or 0.0), float(penalties[1] or 0.0))
         self.counts = None
@@ -548,6 +573,12 @@ class GreedySession:
         self.sampling = sampling if (sampling is not None and sampling.active) else None
         if self.sampling is not None and getattr(target, "world", 1) > 1:
             raise NotImplementedError("sampled decoding of a tensor-parallel target is not built")
+        self.lp = None
+        if logprobs is not None:
+            if getattr(target, "world", 1) > 1:
+                raise NotImplementedError("logprobs of a tensor-parallel target are not built")
+            self.lp = LogprobRows(target.device, B, logprobs, target.cfg.vocab_size,
+                                  raw=self.counts is not None)
         self.rng = ops.rng_state(list(seeds) if seeds is not None else [0] * B, target.device)
         dev = target.device
         cap_tokens = max_tokens + 64
@@ -571,6 +602,8 @@ class GreedySession:
         t.forward(self.buf, self.tstate, (), splits=self.splits)
         # T = 1: n = 0, bonus = argmax (or a draw); the next input id is written in place
         sm = self.sampling
+        if self.lp is not None and self.counts is not None:
+            self.lp.snapshot(self.buf.logits, self.B)
         if self.counts is not None:
             ops.apply_penalties(self.buf.logits, self.B, 1, self.counts, None, *self.penalties)
         if sm is None:
@@ -582,6 +615,8 @@ class GreedySession:
                               self.buf.ids, self.plan, t.scratch)
         if self.counts is not None:
             ops.penalty_counts_add(self.counts, self.plan, self.B)
+        if self.lp is not None:
+            self.lp.launch(self.buf.logits, self.B, self.plan[:, 2:], 3, 1)
         self.plan_host.copy_(self.plan, non_blocking=True)
         t.scratch.read_status_async()
 
@@ -610,8 +645,6 @@ def greedy_generate(target, tokenizer, prompt: str = "", *, prompt_ids: list[int
                     use_graph: bool = True) -> GenResult:
     """Plain decoding of the target (the baseline the speedup is measured against): greedy, or
     sampled with temperature / top-p / top-k from a Philox stream seeded by `seed`."""
-    if logprobs is not None:
-        raise NotImplementedError("logprobs are not built")
     eos_ids = eos_token_ids(tokenizer)
     if prompt_ids is None:
         prompt_ids = encode_prompt(tokenizer, prompt, apply_chat_template)
@@ -619,7 +652,7 @@ def greedy_generate(target, tokenizer, prompt: str = "", *, prompt_ids: list[int
     sampling = Sampling(temperature, top_p, top_k)
     sess = GreedySession(target, 1, len(ids) + max_new_tokens + 1, sampling,
                          [0 if seed is None else int(seed)],
-                         (presence_penalty, frequency_penalty))
+                         (presence_penalty, frequency_penalty), logprobs)
     try:
         t0 = time.time()
         last = prefill_rows(target, ids, sess.tstate, ())
@@ -627,7 +660,14 @@ def greedy_generate(target, tokenizer, prompt: str = "", *, prompt_ids: list[int
         if sess.counts is not None:
             sess.counts[0, nxt] += 1             # pen.add([nxt]) (generate.py:427)
         sess.buf.ids.fill_(nxt)
+        lp_list = None
+        if sess.lp is not None:
+            # every entry, the first included, is the raw row the token was picked from
+            # (generate.py:417-429)
+            sess.lp.launch(last.view(1, -1), 1, sess.buf.ids, 1, 1, use_snapshot=False)
         torch.cuda.synchronize()
+        if sess.lp is not None:
+            lp_list = sess.lp.entries([nxt])
         t1 = time.time()
         out = [nxt]
         while len(out) < max_new_tokens and nxt not in eos_ids:
@@ -636,12 +676,15 @@ def greedy_generate(target, tokenizer, prompt: str = "", *, prompt_ids: list[int
                 sess.capture()
             nxt = plan[2]
             out.append(nxt)
+            if lp_list is not None:
+                lp_list.extend(sess.lp.entries([nxt]))
         t2 = time.time()
         text = _decode(tokenizer, [t for t in out if t not in eos_ids])
         return GenResult(text=text, token_ids=out, num_tokens=len(out), num_rounds=len(out),
                          accept_lengths=[1] * len(out), target_forwards=len(out),
                          seconds=t2 - t0, decode_seconds=t2 - t1,
-                         finish_reason=_finish_reason(out, max_new_tokens, nxt, eos_ids))
+                         finish_reason=_finish_reason(out, max_new_tokens, nxt, eos_ids),
+                         logprobs=lp_list)
     finally:
         sess.release()
 

@@ -77,6 +77,7 @@ class BlockVerifier:
         dev = target.device
         self.pending = pending if pending is not None else torch.zeros(1, dtype=torch.int32, device=dev)
         self.ids_host = torch.zeros(64, dtype=torch.int32, pin_memory=True)
+        self.lp = None  # a LogprobRows of the decode, when per-token logprobs are requested
         self._plans: dict[int, tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = {}
         self.done = torch.cuda.Event()
 
@@ -97,6 +98,8 @@ class BlockVerifier:
         self.ids_host[:T] = torch.tensor([pending] + list(draft), dtype=torch.int32)
         buf.ids.copy_(self.ids_host[:T], non_blocking=True)
         t.forward(buf, self.tstate, self.tap)
+        if self.lp is not None and self.counts is not None:
+            self.lp.snapshot(buf.logits, T)
         if self.counts is not None:
             ops.apply_penalties(buf.logits, 1, T, self.counts, buf.ids, *self.penalties)
         plan, plan_host, argmax = self._plan(T)
@@ -110,6 +113,8 @@ class BlockVerifier:
                               self.rng, kv, commit, self.pending, plan, t.scratch, q_onehot=True)
         if self.counts is not None:
             ops.penalty_counts_add(self.counts, plan, 1)
+        if self.lp is not None:
+            self.lp.launch(buf.logits, T, plan[:, 2:], T + 2, T)
         return buf, plan, plan_host
 
     def finish(self, plan, plan_host) -> list[int]:

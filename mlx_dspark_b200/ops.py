@@ -350,6 +350,18 @@ def argmax_rows(logits: torch.Tensor, rows: int, tokens: torch.Tensor, tok_strid
     return tokens
 
 
+def logprobs(logits: torch.Tensor, rows: int, ids: torch.Tensor, ids_ld: int, T: int, top_k: int,
+             logp: torch.Tensor, top_ids: torch.Tensor | None = None,
+             top_logp: torch.Tensor | None = None, V: int | None = None) -> None:
+    """Raw log-softmax entry of each row's token (row r's token is ids[(r // T) * ids_ld + r % T])
+    into logp[r], and with top_k > 0 the row's top_k entries, descending, into top_ids /
+    top_logp [rows, top_k] (_logprobs_for_block, generate.py:149-176)."""
+    _require_cuda(logits, ids, logp, top_ids, top_logp)
+    call("dspark_logprobs", _p(logits), logits.stride(0), rows,
+         logits.shape[-1] if V is None else int(V), _p(ids), int(ids_ld), int(T), int(top_k),
+         _p(logp), _p(top_ids), _p(top_logp), _stream())
+
+
 def residual_add_f32(h: torch.Tensor, summed: torch.Tensor, M: int) -> None:
     """h[:M] = bf16(h + bf16(summed)) (row-split projection after its all-reduce)."""
     call("dspark_residual_add_f32", _p(h), h.stride(0), _p(summed), summed.stride(0), M,
