@@ -482,6 +482,21 @@ int dspark_logprobs(const void* logits, long long ld, int rows, int V, const int
                     int ids_ld, int T, int top_k, float* logp, int32_t* top_ids, float* top_logp,
                     dspark_stream_t stream);
 
+/* DSpark confidence head (ConfidenceHead, src/mlx_dspark/model.py:211-217; confidence_logits
+ * :311-320): per row i of hidden [rows, H] (bf16, row pitch ld), logit[i] = bf16(proj_w .
+ * [norm(h_i), w1[prev_i]] + proj_b) and conf[i] = bf16(sigmoid(logit[i])), the survival
+ * probabilities speculative_generate truncates a draft with (generate.py:875-885).
+ * norm_w non-null: the rows are the backbone's pre-norm hidden states and norm(h) =
+ * bf16(h * rsqrt(mean(h^2) + eps) * norm_w); null: the rows are already normalised.
+ * w1q / w1sb (the packed Markov w1, [V, R] codes and [R/64, V] fp16 scale|bias words) non-null:
+ * the features also hold bf16(dequant w1[prev_i]), prev_0 = first_prev[0] and prev_i =
+ * prev_rest[i - 1]; proj_w is bf16 [H + R] (R a multiple of 64), else bf16 [H]. proj_b is
+ * bf16 [1]. logit may be null. One CTA per row. */
+int dspark_confidence(const void* hidden, long long ld, int rows, int H, const void* norm_w,
+                      float eps, const uint8_t* w1q, const uint32_t* w1sb, int V, int R,
+                      const int32_t* first_prev, const int32_t* prev_rest, const void* proj_w,
+                      const void* proj_b, float* logit, float* conf, dspark_stream_t stream);
+
 /* Tensor-parallel pieces (BASELINE C5: Qwen3-32B at TP 2/4/8; NCCL all-reduce after o_proj
  * and down_proj). The reference runs on one device and has no counterpart; they stand in for
  * its single-device o_proj / down_proj residual adds and the lm_head argmax.

@@ -98,6 +98,7 @@ SIGNATURES = {
     "dspark_penalty_counts_add": (I, [P, I, I, P, I, P]),
     "dspark_argmax_rows": (I, [P, c_longlong, I, I, P, I, P, I, P, I, P]),
     "dspark_logprobs": (I, [P, c_longlong, I, I, P, I, I, I, P, P, P, P]),
+    "dspark_confidence": (I, [P, c_longlong, I, I, P, c_float, P, P, I, I, P, P, P, P, P, P, P]),
     "dspark_residual_add_f32": (I, [P, I, P, I, I, I, P]),
     "dspark_accept_greedy_sharded": (I, [P, P, I, I, I, P, P, I, P, P, P]),
     "dspark_sample_rows": (I, [P, c_longlong, I, I, I, c_float, I, c_double, I, P, I, I, P,

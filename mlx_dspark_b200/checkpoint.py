@@ -31,7 +31,7 @@ import torch
 
 from .config import DFlashConfig, DSparkConfig, TargetConfig
 from .weights import (GROUP, DFlashWeights, DSparkWeights, LayerWeights, QTensor,
-                      TargetWeights, quantize_w8g64)
+                      TargetWeights, confidence_in_dim, quantize_w8g64)
 
 # ------------------------------------------------------------------------------------------
 # safetensors
@@ -343,7 +343,7 @@ def load_dspark_checkpoint(path: str, *, strict: bool = True) -> DSparkWeights:
     """W8 weights of a DeepSpec-format DSpark drafter directory (bf16 safetensors). A name
     mismatch raises (strict=True, the reference's default: a partly loaded drafter drafts
     near-zero acceptance); strict=False tolerates extra tensors with a warning. The confidence
-    head is read by name but not used (no consumer on this path)."""
+    head's proj weight and bias are kept in bf16 (speculative_generate's confidence_threshold)."""
     cfg = DSparkConfig.from_json(os.path.join(path, "config.json"))
     if cfg.attention_bias:
         raise ValueError(f"{path}: attention biases are not supported by this build's drafter")
@@ -355,11 +355,18 @@ def load_dspark_checkpoint(path: str, *, strict: bool = True) -> DSparkWeights:
     if cfg.markov_rank > 0:
         w1 = quantize_w8g64(ts["markov_head.markov_w1.weight"].float())
         w2 = quantize_w8g64(ts["markov_head.markov_w2.weight"].float())
+    conf_w = conf_b = None
+    if cfg.enable_confidence_head:
+        conf_w = _as_bf16(ts["confidence_head.proj.weight"], "confidence_head.proj").reshape(-1)
+        conf_b = _as_bf16(ts["confidence_head.proj.bias"], "confidence_head.proj.bias").reshape(-1)
+        if conf_w.numel() != confidence_in_dim(cfg) or conf_b.numel() != 1:
+            raise ValueError(f"{path}: confidence_head.proj has {conf_w.numel()} inputs and "
+                             f"{conf_b.numel()} biases, expected {confidence_in_dim(cfg)} and 1")
     return DSparkWeights(cfg, quantize_w8g64(ts["fc.weight"].float()),
                          _as_bf16(ts["hidden_norm.weight"], "hidden_norm"), layers,
                          _as_bf16(ts["norm.weight"], "norm"), w1, w2,
                          quantize_w8g64(ts["embed_tokens.weight"].float()),
-                         quantize_w8g64(ts["lm_head.weight"].float()))
+                         quantize_w8g64(ts["lm_head.weight"].float()), conf_w, conf_b)
 
 
 def _layer_bf16(L: LayerWeights) -> dict:
@@ -391,9 +398,11 @@ def export_dspark_checkpoint(dw: DSparkWeights, path: str, config: dict) -> None
     if dw.lm_head is not None:
         items["lm_head.weight"] = dw.lm_head.dequant().to(torch.bfloat16)
     if dw.cfg.enable_confidence_head:
-        din = dw.cfg.hidden_size + (dw.cfg.markov_rank if dw.cfg.confidence_head_with_markov else 0)
-        items["confidence_head.proj.weight"] = torch.zeros(1, din, dtype=torch.bfloat16)
-        items["confidence_head.proj.bias"] = torch.zeros(1, dtype=torch.bfloat16)
+        din = confidence_in_dim(dw.cfg)
+        w = dw.conf_w if dw.conf_w is not None else torch.zeros(din, dtype=torch.bfloat16)
+        b = dw.conf_b if dw.conf_b is not None else torch.zeros(1, dtype=torch.bfloat16)
+        items["confidence_head.proj.weight"] = w.cpu().reshape(1, din)
+        items["confidence_head.proj.bias"] = b.cpu().reshape(1)
     write_safetensors(os.path.join(path, "model.safetensors"), items)
 
 

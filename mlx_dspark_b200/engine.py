@@ -61,7 +61,8 @@ class Engine:
 
     def __init__(self, target, tokenizer, drafter, *, mode: str, model_id: str = "",
                  target_repo: str = "", drafter_repo: str | None = None,
-                 max_draft_tokens: int | None = None, prefix_cache: bool = True,
+                 max_draft_tokens: int | None = None, confidence_threshold: float = 0.0,
+                 prefix_cache: bool = True,
                  prefix_cache_slots: int = 2, cache_tokens: int = 4096, cap_controller=None,
                  lookup_drafts: bool = True, default_max_tokens: int = 2048,
                  max_tokens_cap: int = 32768, executor: ThreadPoolExecutor | None = None):
@@ -74,6 +75,7 @@ class Engine:
         self.model_id = model_id or str(target_repo).rstrip("/").split("/")[-1]
         self.target_repo, self.drafter_repo = target_repo, drafter_repo
         self.max_draft_tokens = max_draft_tokens
+        self.confidence_threshold = float(confidence_threshold or 0.0)
         self.cap_controller = cap_controller      # kept across requests (auto cap)
         self.lookup_drafts = lookup_drafts
         self.cache_tokens = int(cache_tokens)     # first size of a cache; caches grow on demand
@@ -143,6 +145,7 @@ class Engine:
             self.target, self.tokenizer, self.drafter, prompt_ids=ids, cache=cache,
             ctx_caches=ctx, reuse_len=reuse, max_new_tokens=p["max_tokens"],
             max_draft_tokens=self.max_draft_tokens, cap_controller=self.cap_controller,
+            confidence_threshold=self.confidence_threshold,
             lookup_drafts=self.lookup_drafts, temperature=p["temperature"], top_p=p["top_p"],
             top_k=p["top_k"], presence_penalty=p["presence_penalty"],
             frequency_penalty=p["frequency_penalty"], logprobs=p["logprobs"], seed=p["seed"])

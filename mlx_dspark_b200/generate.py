@@ -271,6 +271,7 @@ class SpecSession:
                 "prompt_len": torch.as_tensor(o["prompt_len"], dtype=torch.int32).to(dev),
             }
         self.done = torch.cuda.Event()
+        self._conf = None  # confidence buffers (device, pinned host), made by conf_step
 
     def _make_round(self, cap: int) -> dict:
         t, d, B, dev = self.target, self.drafter, self.B, self.target.device
@@ -307,37 +308,100 @@ class SpecSession:
             self.tstate.release()
             self.cstate.release()
 
-    def launch_round(self) -> None:
-        d, t, sc = self.drafter, self.target, self.target.scratch
-        B, T, cap = self.B, self.T, self.cap
-        sm = self.sampling
+    def launch_draft(self) -> None:
+        """Draft cap tokens per row into self.draft and the verify ids of this cap's round."""
+        d, t = self.drafter, self.target
+        B, cap = self.B, self.cap
         d.draft_dev(self.pending, B, cap, self.cstate, self.dbuf, self.draft, self.vbuf.ids,
-                    self.splits_c, sampling=sm, rng=self.rng, q_probs=self.q)
+                    self.splits_c, sampling=self.sampling, rng=self.rng, q_probs=self.q)
         if self.override is not None:
             o = self.override
             ops.draft_override(B, cap, t.cfg.vocab_size, o["ref"], o["agree"], o["round"],
                                self.tstate.seq_len, o["prompt_len"], self.vbuf.ids)
-        t.forward(self.vbuf, self.tstate, self.tap, splits=self.splits_t)
+
+    def launch_verify(self, r: dict | None = None) -> None:
+        """Verify, accept and commit the block held in round r's verify ids (default: this
+        cap's round); the draft distributions and context buffers are this cap's."""
+        r = self._current() if r is None else r
+        d, t, sc = self.drafter, self.target, self.target.scratch
+        B, T = self.B, r["T"]
+        vbuf, plan, sm = r["vbuf"], r["plan"], self.sampling
+        t.forward(vbuf, self.tstate, self.tap, splits=self.splits_t)
         if self.lp is not None and self.counts is not None:
-            self.lp.snapshot(self.vbuf.logits, B * T)
+            self.lp.snapshot(vbuf.logits, B * T)
         if self.counts is not None:
-            ops.apply_penalties(self.vbuf.logits, B, T, self.counts, self.vbuf.ids,
-                                *self.penalties)
+            ops.apply_penalties(vbuf.logits, B, T, self.counts, vbuf.ids, *self.penalties)
         if sm is None:
-            t.greedy_accept(self.vbuf.logits, B, T, self.vbuf.ids, self.argmax, None, False,
-                            self.pending, self.plan)
+            t.greedy_accept(vbuf.logits, B, T, vbuf.ids, r["argmax"], None, False, self.pending,
+                            plan)
         else:
-            ops.accept_sample(self.vbuf.logits, B, T, self.vbuf.ids, self.q, sm.temperature,
-                              sm.top_p, sm.top_k, self.rng, None, False, self.pending, self.plan,
-                              sc)
+            ops.accept_sample(vbuf.logits, B, T, vbuf.ids, self.q, sm.temperature, sm.top_p,
+                              sm.top_k, self.rng, None, False, self.pending, plan, sc)
         if self.counts is not None:
-            ops.penalty_counts_add(self.counts, self.plan, B)
+            ops.penalty_counts_add(self.counts, plan, B)
         if self.lp is not None:
-            self.lp.launch(self.vbuf.logits, B * T, self.plan[:, 2:], T + 2, T)
-        d.update_context_dev(self.vbuf.fused16, B, T, self.cstate, self.dbuf)
-        ops.commit_lengths(self.plan, B, self.tstate.seq_len, self.cstate.seq_len)
-        self.plan_host.copy_(self.plan, non_blocking=True)
+            self.lp.launch(vbuf.logits, B * T, plan[:, 2:], T + 2, T)
+        d.update_context_dev(vbuf.fused16, B, T, self.cstate, self.dbuf)
+        ops.commit_lengths(plan, B, self.tstate.seq_len, self.cstate.seq_len)
+        r["plan_host"].copy_(plan, non_blocking=True)
         t.scratch.read_status_async()
+
+    def launch_round(self) -> None:
+        self.launch_draft()
+        self.launch_verify()
+
+    def _current(self) -> dict:
+        return {f: getattr(self, f) for f in self._ROUND}
+
+    def _round(self, cap: int) -> dict:
+        """Round buffers for `cap` drafts without switching to them (conf_step's shorter
+        verify); made on first use and kept with the other caps' rounds."""
+        if cap == self.cap:
+            return self._current()
+        r = self._rounds.get(cap)
+        if r is None:
+            r = self._rounds[cap] = self._make_round(cap)
+        return r
+
+    def conf_step(self, threshold: float) -> tuple[list[int], int]:
+        """A drafter round with confidence truncation (generate.py:855-887): draft cap tokens
+        and their survival probabilities, keep the longest prefix whose running product stays
+        >= threshold (at least one token), then verify, accept and commit that block. Runs
+        eagerly with one host sync between the phases, like the reference's two-phase path.
+        The round's input token comes from pending_host. Returns (plan row, drafted count)."""
+        if self.B != 1:
+            raise NotImplementedError("confidence truncation is batch 1 (as the reference)")
+        if self.drafter.confidence_head is None:
+            raise ValueError("the drafter has no confidence head")
+        if self._conf is None:
+            dev = self.target.device
+            self._conf = (torch.zeros(self.max_cap, dtype=torch.float32, device=dev),
+                          torch.zeros(self.max_cap, dtype=torch.float32, pin_memory=True))
+        conf_dev, conf_host = self._conf
+        cap = self.cap
+        self.pending.copy_(self.pending_host, non_blocking=True)
+        self.launch_draft()
+        self.drafter.confidence_dev(self.dbuf, self.pending, self.draft, cap, conf_dev)
+        conf_host[:cap].copy_(conf_dev[:cap], non_blocking=True)
+        self.target.scratch.read_status_async()
+        self.done.record()
+        self.done.synchronize()
+        self.target.scratch.raise_on_status()
+        surv, keep = 1.0, 0
+        for i, c in enumerate(conf_host[:cap].tolist()):
+            surv *= c
+            if surv < threshold:
+                break
+            keep = i + 1
+        keep = max(keep, 1)   # always propose at least one token
+        r = self._round(keep)
+        if keep != cap:
+            r["vbuf"].ids[:keep + 1].copy_(self.vbuf.ids[:keep + 1])
+        self.launch_verify(r)
+        self.done.record()
+        self.done.synchronize()
+        self.target.scratch.raise_on_status()
+        return r["plan_host"][0].tolist(), keep
 
     def _versions(self):
         return (self.tstate.pool.version, self.cstate.pool.version,
@@ -415,7 +479,7 @@ def _caller_states(drafter, cache, ctx_caches, reuse_len: int, tokens: int):
 def _spec_loop(target, tokenizer, drafter, ids, cap, max_new_tokens, sampling, seed, use_graph,
                draft_override, verbose, penalties=(0.0, 0.0), lookup_max_draft=0, cache=None,
                ctx_caches=None, reuse_len: int = 0, cap_controller=None,
-               logprobs: int | None = None) -> GenResult:
+               logprobs: int | None = None, confidence_threshold: float = 0.0) -> GenResult:
     """The decode loop of speculative_generate / dflash_generate. `cap` is the ceiling; with a
     cap_controller each drafter round uses min(controller.cap, cap) and feeds the outcome back
     (generate.py:846-847,924-925); lookup rounds neither use nor update it."""
@@ -431,6 +495,9 @@ def _spec_loop(target, tokenizer, drafter, ids, cap, max_new_tokens, sampling, s
     else:
         reuse_len = 0
     ctrl = cap_controller
+    # confidence truncation needs the drafter's confidence head; without one the threshold is
+    # ignored, as in the reference (generate.py:808)
+    use_conf = confidence_threshold > 0.0 and getattr(drafter, "confidence_head", None) is not None
     first_cap = cap if ctrl is None else max(1, min(int(ctrl.cap), cap))
     sess = SpecSession(target, drafter, 1, first_cap, budget, override=draft_override,
                        sampling=sampling, seeds=[0 if seed is None else int(seed)],
@@ -469,11 +536,15 @@ def _spec_loop(target, tokenizer, drafter, ids, cap, max_new_tokens, sampling, s
                 if ctrl is not None:
                     sess.set_cap(max(1, min(int(ctrl.cap), cap)))
                 sess.pending_host[0] = pending
-                plan = sess.step(use_graph, feed_pending=True)[0]
-                if use_graph and sess.graph is None:
-                    sess.capture()
+                if use_conf:
+                    plan, drafted = sess.conf_step(confidence_threshold)
+                else:
+                    plan = sess.step(use_graph, feed_pending=True)[0]
+                    drafted = sess.cap
+                    if use_graph and sess.graph is None:
+                        sess.capture()
                 if ctrl is not None:
-                    ctrl.update(plan[0], sess.cap)
+                    ctrl.update(plan[0], drafted)
             n = plan[0]
             committed = plan[2:3 + n]
             accept.append(len(committed))
@@ -491,7 +562,7 @@ def _spec_loop(target, tokenizer, drafter, ids, cap, max_new_tokens, sampling, s
             rounds += 1
             if verbose:
                 src = "lookup" if lk else "drafter"
-                print(f"  round {rounds:3d}: {src} drafted {len(lk) if lk else sess.cap}, accepted {n}, "
+                print(f"  round {rounds:3d}: {src} drafted {len(lk) if lk else drafted}, accepted {n}, "
                       f"committed {len(committed)}")
         t2 = time.time()
         text = _decode(tokenizer, [t for t in out if t not in eos_ids])
@@ -523,9 +594,11 @@ def speculative_generate(target, tokenizer, drafter, prompt: str = "", *,
     """Speculative decoding with the DSpark drafter, batch 1 (generate.py:691-978).
     temperature 0: the output is the target's greedy decoding. temperature > 0: drafts are drawn
     from the drafter's truncated distributions and accepted by rejection sampling, so the output
-    is a sample of top-p/top-k(softmax(target / T)) (lossless); `seed` seeds the Philox stream."""
-    if confidence_threshold > 0:
-        raise NotImplementedError("confidence truncation is not built")
+    is a sample of top-p/top-k(softmax(target / T)) (lossless); `seed` seeds the Philox stream.
+    confidence_threshold > 0 with a drafter that has a confidence head truncates each drafted
+    block where the running product of its survival probabilities falls below the threshold
+    (the output is unchanged; rounds get shorter). logprobs (an int, 0 = the committed token
+    only) returns per-token entries of the raw target distribution in GenResult.logprobs."""
     k = drafter.config.block_size
     cap = k if max_draft_tokens is None else max(1, min(int(max_draft_tokens), k))
     if prompt_ids is None:
@@ -534,7 +607,7 @@ def speculative_generate(target, tokenizer, drafter, prompt: str = "", *,
                       Sampling(temperature, top_p, top_k), seed, use_graph, draft_override,
                       verbose, (presence_penalty, frequency_penalty),
                       max(1, int(lookup_max_draft)) if lookup_drafts else 0, cache, ctx_caches,
-                      reuse_len, cap_controller, logprobs)
+                      reuse_len, cap_controller, logprobs, float(confidence_threshold))
 
 
 def dflash_generate(target_model, tokenizer, drafter, prompt: str = "", *,

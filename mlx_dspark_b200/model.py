@@ -52,6 +52,14 @@ class _Markov:
         self.w1, self.w2, self.rank = w1, w2, rank
 
 
+class _ConfidenceHead:
+    """The confidence head's projection (model.py:211-217): bf16 weight row [H (+ R)] and bf16
+    bias [1]; with_markov: its input also holds the previous token's Markov embedding."""
+
+    def __init__(self, w, b, with_markov: bool):
+        self.w, self.b, self.with_markov = w, b, with_markov
+
+
 class DraftBuffers:
     def __init__(self, cfg, B: int, k: int, ctx_rows: int, device):
         H, I = cfg.hidden_size, cfg.intermediate_size
@@ -292,8 +300,41 @@ class DSparkDrafter(BlockDrafter):
             self.markov_head = _Markov(pack(weights.markov_w1, device=device),
                                        pack(weights.markov_w2, device=device), cfg.markov_rank)
         self.confidence_head = None
+        if weights.conf_w is not None:
+            with_markov = cfg.confidence_head_with_markov and self.markov_head is not None
+            self.confidence_head = _ConfidenceHead(
+                weights.conf_w.to(device, torch.bfloat16).reshape(-1).contiguous(),
+                weights.conf_b.to(device, torch.bfloat16).reshape(-1).contiguous(), with_markov)
         if target is not None:
             self.bind(target)
+
+    def confidence_dev(self, buf: DraftBuffers, pending: torch.Tensor, draft: torch.Tensor,
+                       cap: int, conf: torch.Tensor) -> None:
+        """Survival probabilities of batch row 0's cap drafted positions into conf[:cap]
+        (generate.py:875-880): from the backbone's pre-norm block rows left in buf.h by
+        draft_dev, the pending token and the draft (prev_0 = pending, prev_i = draft[i-1])."""
+        ch = self.confidence_head
+        ops.confidence(buf.h, cap, ch.w, ch.b, conf, norm_w=self.norm,
+                       eps=self.config.rms_norm_eps,
+                       w1=self.markov_head.w1 if ch.with_markov else None,
+                       first_prev=pending, prev_rest=draft.view(-1) if cap > 1 else None)
+
+    def confidence_logits(self, block_hidden, prev_token_ids):
+        """Confidence-head logits of normalised block hidden states [cap, H] (or [1, cap, H])
+        and their previous tokens [cap] (model.py:311-320); None without a confidence head."""
+        ch = self.confidence_head
+        if ch is None:
+            return None
+        H = self.config.hidden_size
+        h = block_hidden.reshape(-1, H).to(self.device, torch.bfloat16).contiguous()
+        prev = torch.as_tensor(prev_token_ids, dtype=torch.int32).reshape(-1).to(self.device)
+        n = h.shape[0]
+        conf = torch.empty(n, dtype=torch.float32, device=self.device)
+        logit = torch.empty(n, dtype=torch.float32, device=self.device)
+        ops.confidence(h, n, ch.w, ch.b, conf,
+                       w1=self.markov_head.w1 if ch.with_markov else None,
+                       first_prev=prev[:1], prev_rest=prev[1:] if n > 1 else None, logit=logit)
+        return logit
 
     def draft_dev(self, pending: torch.Tensor, B: int, cap: int, ctx: CacheState,
                   buf: DraftBuffers, draft: torch.Tensor, verify_ids: torch.Tensor | None,

@@ -362,6 +362,21 @@ def logprobs(logits: torch.Tensor, rows: int, ids: torch.Tensor, ids_ld: int, T:
          _p(logp), _p(top_ids), _p(top_logp), _stream())
 
 
+def confidence(hidden: torch.Tensor, rows: int, proj_w: torch.Tensor, proj_b: torch.Tensor,
+               conf: torch.Tensor, *, norm_w: torch.Tensor | None = None, eps: float = 1e-6,
+               w1: PackedLinear | None = None, first_prev: torch.Tensor | None = None,
+               prev_rest: torch.Tensor | None = None, logit: torch.Tensor | None = None) -> None:
+    """Confidence-head survival probabilities of `rows` drafted positions (dspark_confidence):
+    conf[i] = bf16(sigmoid(proj([norm(hidden_i), w1[prev_i]]))), prev_0 = first_prev[0],
+    prev_i = prev_rest[i - 1]; without norm_w the rows are taken as already normalised."""
+    _require_cuda(hidden, proj_w, proj_b, conf, norm_w, first_prev, prev_rest, logit)
+    H = hidden.shape[-1]
+    call("dspark_confidence", _p(hidden), hidden.stride(0), rows, H, _p(norm_w), float(eps),
+         None if w1 is None else _p(w1.q), None if w1 is None else _p(w1.sb),
+         0 if w1 is None else w1.N, 0 if w1 is None else w1.K, _p(first_prev), _p(prev_rest),
+         _p(proj_w), _p(proj_b), _p(logit), _p(conf), _stream())
+
+
 def residual_add_f32(h: torch.Tensor, summed: torch.Tensor, M: int) -> None:
     """h[:M] = bf16(h + bf16(summed)) (row-split projection after its all-reduce)."""
     call("dspark_residual_add_f32", _p(h), h.stride(0), _p(summed), summed.stride(0), M,

@@ -161,6 +161,9 @@ class DSparkWeights:
     markov_w2: QTensor | None   # [V, R] linear R -> V
     embed: QTensor | None = None    # None: the target's embedding is shared
     lm_head: QTensor | None = None  # None: the target's head is shared
+    # confidence head proj (model.py:211-217): bf16 [H (+ R)] weight row and bf16 [1] bias
+    conf_w: torch.Tensor | None = None
+    conf_b: torch.Tensor | None = None
 
     def to(self, device) -> "DSparkWeights":
         f = lambda t: None if t is None else t.to(device)  # noqa: E731
@@ -169,7 +172,7 @@ class DSparkWeights:
             [LayerWeights(*(getattr(l, k).to(device) for k in LayerWeights.__dataclass_fields__))
              for l in self.layers],
             self.norm.to(device), f(self.markov_w1), f(self.markov_w2), f(self.embed),
-            f(self.lm_head))
+            f(self.lm_head), f(self.conf_w), f(self.conf_b))
 
 
 def generate_dspark(cfg: DSparkConfig, seed: int, device="cpu") -> DSparkWeights:
@@ -192,7 +195,22 @@ def generate_dspark(cfg: DSparkConfig, seed: int, device="cpu") -> DSparkWeights
     if not cfg.shared_embeddings:
         embed = _qlinear(gen, cfg.vocab_size, H, device)
         lm_head = _qlinear(gen, cfg.vocab_size, H, device)
-    return DSparkWeights(cfg, fc, hidden_norm, layers, norm, w1, w2, embed, lm_head)
+    conf_w = conf_b = None
+    if cfg.enable_confidence_head:
+        # drawn last so the other tensors do not depend on the flag; a logit ~ N(2, 1) keeps
+        # the per-position survival probabilities in the range where truncation varies
+        din = confidence_in_dim(cfg)
+        conf_w = (_randn(gen, (din,), device) * din ** -0.5).to(torch.bfloat16)
+        conf_b = torch.full((1,), 2.0, dtype=torch.bfloat16, device=device)
+    return DSparkWeights(cfg, fc, hidden_norm, layers, norm, w1, w2, embed, lm_head, conf_w,
+                         conf_b)
+
+
+def confidence_in_dim(cfg: DSparkConfig) -> int:
+    """Input width of the confidence head: H, plus the Markov rank when the head also reads the
+    previous token's Markov embedding (model.py:240-242)."""
+    with_markov = cfg.confidence_head_with_markov and cfg.markov_rank > 0
+    return cfg.hidden_size + (cfg.markov_rank if with_markov else 0)
 
 
 @dataclass

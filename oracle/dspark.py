@@ -113,6 +113,25 @@ class DSparkRef:
                + w1.biases[prev].to(F32).repeat_interleave(64), self.rnd)
         return self._lin(e[None], w2)[0]
 
+    def prev_embedding(self, prev: int):
+        """VanillaMarkov.prev_embeddings (model.py:204-205): bf16(dequant w1[prev])."""
+        w1 = self.w.markov_w1
+        return bf(w1.scales[prev].to(F32).repeat_interleave(64) * w1.q[prev].to(F32)
+                  + w1.biases[prev].to(F32).repeat_interleave(64), self.rnd)
+
+    def confidence_logits(self, hidden, prev_tokens):
+        """confidence_logits + ConfidenceHead (model.py:311-320, :211-217) over normalised block
+        rows [cap, H]: bf16(w . [hidden_i, w1[prev_i]] + b), fp32 accumulation."""
+        feats = hidden.to(F32)
+        if self.cfg.confidence_head_with_markov and self.w.markov_w1 is not None:
+            e = torch.stack([self.prev_embedding(int(p)) for p in prev_tokens])
+            feats = torch.cat([feats, e.to(F32)], dim=-1)
+        return bf(feats @ self.w.conf_w.to(F32) + self.w.conf_b.to(F32), self.rnd)
+
+    def confidence(self, hidden, prev_tokens):
+        """mx.sigmoid of the logits, rounded to bf16 (generate.py:878)."""
+        return bf(torch.sigmoid(self.confidence_logits(hidden, prev_tokens)), self.rnd)
+
     def sample_block(self, base_logits, first_prev_token: int):
         """model.py:270-281 (argmax = first index of the maximum)."""
         if self.w.markov_w1 is None:
@@ -149,11 +168,25 @@ def greedy_generate_ref(target: Qwen3Ref, prompt_ids, max_new_tokens, kv8=False)
     return out, rows
 
 
+def truncate_by_confidence(draft, conf, threshold):
+    """generate.py:875-887: keep drafted positions while the running product of survival
+    probabilities stays >= threshold; always propose at least one token."""
+    surv, keep = 1.0, 0
+    for i, c in enumerate(conf):
+        surv *= float(c)
+        if surv < threshold:
+            break
+        keep = i + 1
+    return list(draft[:keep]) or [draft[0]]
+
+
 def speculative_generate_ref(target: Qwen3Ref, drafter: DSparkRef, prompt_ids, max_new_tokens,
-                             max_draft_tokens=None, kv8=False, draft_override=None):
-    """speculative_generate fused greedy path (generate.py:806-961), lookup drafts off.
-    draft_override(round, draft, n_out) may replace the drafted tokens (benchmark configs).
-    Returns (out_ids, accept_lengths)."""
+                             max_draft_tokens=None, kv8=False, draft_override=None,
+                             confidence_threshold=0.0):
+    """speculative_generate greedy path (generate.py:806-961), lookup drafts off, with the
+    confidence truncation of the two-phase path when confidence_threshold > 0 and the drafter
+    has a confidence head. draft_override(round, draft, n_out) may replace the drafted tokens
+    (benchmark configs). Returns (out_ids, accept_lengths)."""
     cfg = drafter.cfg
     tap = list(cfg.target_layer_ids)
     k = cfg.block_size
@@ -178,6 +211,9 @@ def speculative_generate_ref(target: Qwen3Ref, drafter: DSparkRef, prompt_ids, m
         hidden = drafter.backbone(noise, n_cached, ctx)
         base = drafter.compute_logits(hidden[:cap])
         draft = drafter.sample_block(base, pending)
+        if confidence_threshold > 0 and drafter.w.conf_w is not None:
+            conf = drafter.confidence(hidden[:cap], [pending] + draft[:-1])
+            draft = truncate_by_confidence(draft, conf.tolist(), confidence_threshold)
         if draft_override is not None:
             draft = draft_override(rnd, draft, len(out))
         v_logits, v_fused = target.run([pending] + draft, cache, tap)
@@ -196,4 +232,4 @@ def speculative_generate_ref(target: Qwen3Ref, drafter: DSparkRef, prompt_ids, m
 
 
 __all__ = ["DSparkRef", "CtxCacheRef", "accept_greedy", "greedy_generate_ref",
-           "speculative_generate_ref", "Qwen3Ref"]
+           "speculative_generate_ref", "truncate_by_confidence", "Qwen3Ref"]

@@ -151,6 +151,25 @@ def test_dspark_checkpoint_round_trip(tmp_path, tiny_dspark):
     assert torch.equal(back.norm, dw.norm) and torch.equal(back.hidden_norm, dw.hidden_norm)
 
 
+def test_dspark_confidence_head_round_trip_and_size_check(tmp_path):
+    base = dataclasses.replace(dspark_for(TARGETS["tiny"]), shared_embeddings=False)
+    cfg = dataclasses.replace(base, enable_confidence_head=True)
+    dw = generate_dspark(cfg, 0, "cpu")
+    assert dw.conf_w.shape == (cfg.hidden_size + cfg.markov_rank,) and dw.conf_b.shape == (1,)
+    ck.export_dspark_checkpoint(dw, str(tmp_path), _dspark_config_json(cfg))
+    back = ck.load_dspark_checkpoint(str(tmp_path))
+    assert torch.equal(back.conf_w, dw.conf_w) and torch.equal(back.conf_b, dw.conf_b)
+    # the other tensors do not depend on the head being there
+    plain = generate_dspark(base, 0, "cpu")
+    assert plain.conf_w is None and torch.equal(plain.fc.q, dw.fc.q)
+    p = str(tmp_path / "model.safetensors")
+    ts = ck.read_safetensors(p)
+    ts["confidence_head.proj.weight"] = ts["confidence_head.proj.weight"][:, :-1].contiguous()
+    ck.write_safetensors(p, ts)
+    with pytest.raises(ValueError, match="confidence_head.proj"):
+        ck.load_dspark_checkpoint(str(tmp_path))
+
+
 def test_dspark_name_mismatch_strict_and_relaxed(tmp_path, tiny_dspark):
     ck.export_dspark_checkpoint(tiny_dspark, str(tmp_path), _dspark_config_json(tiny_dspark.cfg))
     p = str(tmp_path / "model.safetensors")

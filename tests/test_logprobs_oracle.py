@@ -38,3 +38,14 @@ def test_matches_float64_log_softmax():
     got = log_softmax_f32(x.numpy())
     want = torch.log_softmax(x.double(), -1).numpy()
     assert np.abs(got - want).max() < 2e-5
+
+
+def test_confidence_truncation_rule():
+    """generate.py:875-887: keep while the running survival product stays >= threshold,
+    always at least one drafted token."""
+    from oracle.dspark import truncate_by_confidence
+    d = [11, 12, 13, 14]
+    assert truncate_by_confidence(d, [0.9, 0.8, 0.5, 0.9], 0.5) == [11, 12]   # 0.9, 0.72, 0.36
+    assert truncate_by_confidence(d, [0.9, 0.8, 0.5, 0.9], 0.3) == [11, 12, 13, 14]
+    assert truncate_by_confidence(d, [0.4, 1.0, 1.0, 1.0], 0.5) == [11]       # none kept -> one
+    assert truncate_by_confidence(d, [1.0, 1.0, 1.0, 1.0], 1.0) == d
