@@ -104,7 +104,8 @@ def test_truncation_keeps_greedy_output(conf):
     mid = speculative_generate(t, None, d, confidence_threshold=0.5, **kw)
     assert mid.token_ids[:N] == ref[:N]
     assert all(2 <= a <= cap + 1 for a in mid.accept_lengths)
-    assert len(set(mid.accept_lengths)) > 1           # the threshold bites at varying depths
+    # survival products of ~0.7-0.9 per position fall below 0.5 before the eighth draft
+    assert max(mid.accept_lengths) < cap + 1
     # a drafter without the head ignores the threshold (generate.py:808)
     p = conf["plain"]
     assert (speculative_generate(t, None, p, confidence_threshold=0.5, **kw).accept_lengths
