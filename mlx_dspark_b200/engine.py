@@ -22,8 +22,9 @@ How work reaches the GPU is this build's own:
   * ReplicaPool runs one worker process per GPU, each with its own model replica and
     BatchEngine, and no collective between them. The host sends each request to the replica
     with the least outstanding work (prompt plus max new tokens of its unfinished requests).
-Stop strings and streaming callbacks are not built: requests that use them are refused with
-NotImplementedError rather than run without them.
+Requests with stop strings or an on_text streaming callback take the solo path (the slot
+table keeps no per-row text state). A ReplicaPool takes stop strings but not callbacks, which
+cannot be sent to its worker processes.
 """
 from __future__ import annotations
 
@@ -40,11 +41,6 @@ from .lookup import lookup_generate
 from .prefix_cache import PrefixCache, target_cache_reusable
 
 MODES = ("dspark", "dflash", "lookup", "baseline")
-
-
-def _refuse_unbuilt(stop, on_text) -> None:
-    if stop or on_text is not None:
-        raise NotImplementedError("stop strings and streaming callbacks are not built")
 
 
 def _params(max_tokens, temperature, top_p=1.0, top_k=0, presence_penalty=0.0,
@@ -120,13 +116,12 @@ class Engine:
 
     def run_request(self, prompt_ids: list[int], p: dict, on_text=None) -> GenResult:
         """One request on the calling thread (the engine's device thread)."""
-        _refuse_unbuilt(p["stop"], on_text)
         cache = ctx = None
         reuse = 0
         if self.prefix is not None:
             cache, ctx, reuse = self.prefix.acquire(prompt_ids)
         try:
-            res = self._decode(prompt_ids, p, cache, ctx, reuse)
+            res = self._decode(prompt_ids, p, cache, ctx, reuse, on_text)
         except BaseException:
             # a cache whose contents no longer match its token record is never kept
             if self.prefix is not None:
@@ -140,7 +135,7 @@ class Engine:
         self._count(len(prompt_ids), res, res.seconds)
         return res
 
-    def _run_dspark(self, ids, p, cache, ctx, reuse) -> GenResult:
+    def _run_dspark(self, ids, p, cache, ctx, reuse, on_text=None) -> GenResult:
         return speculative_generate(
             self.target, self.tokenizer, self.drafter, prompt_ids=ids, cache=cache,
             ctx_caches=ctx, reuse_len=reuse, max_new_tokens=p["max_tokens"],
@@ -148,27 +143,30 @@ class Engine:
             confidence_threshold=self.confidence_threshold,
             lookup_drafts=self.lookup_drafts, temperature=p["temperature"], top_p=p["top_p"],
             top_k=p["top_k"], presence_penalty=p["presence_penalty"],
-            frequency_penalty=p["frequency_penalty"], logprobs=p["logprobs"], seed=p["seed"])
+            frequency_penalty=p["frequency_penalty"], logprobs=p["logprobs"], seed=p["seed"],
+            stop=p["stop"], on_text=on_text)
 
-    def _run_dflash(self, ids, p, cache, ctx, reuse) -> GenResult:
+    def _run_dflash(self, ids, p, cache, ctx, reuse, on_text=None) -> GenResult:
         return dflash_generate(
             self.target, self.tokenizer, self.drafter, prompt_ids=ids,
             max_new_tokens=p["max_tokens"], max_draft_tokens=self.max_draft_tokens,
             cap_controller=self.cap_controller, temperature=p["temperature"], top_p=p["top_p"],
-            top_k=p["top_k"], seed=p["seed"])
+            top_k=p["top_k"], seed=p["seed"], stop=p["stop"], on_text=on_text)
 
-    def _run_lookup(self, ids, p, cache, ctx, reuse) -> GenResult:
+    def _run_lookup(self, ids, p, cache, ctx, reuse, on_text=None) -> GenResult:
         return lookup_generate(
             self.target, self.tokenizer, prompt_ids=ids, cache=cache, reuse_len=reuse,
             max_new_tokens=p["max_tokens"], max_draft_tokens=self.max_draft_tokens or 6,
-            temperature=p["temperature"], top_p=p["top_p"], top_k=p["top_k"], seed=p["seed"])
+            temperature=p["temperature"], top_p=p["top_p"], top_k=p["top_k"], seed=p["seed"],
+            stop=p["stop"], on_text=on_text)
 
-    def _run_baseline(self, ids, p, cache, ctx, reuse) -> GenResult:
+    def _run_baseline(self, ids, p, cache, ctx, reuse, on_text=None) -> GenResult:
         return greedy_generate(
             self.target, self.tokenizer, prompt_ids=ids, cache=cache, reuse_len=reuse,
             max_new_tokens=p["max_tokens"], temperature=p["temperature"], top_p=p["top_p"],
             top_k=p["top_k"], presence_penalty=p["presence_penalty"],
-            frequency_penalty=p["frequency_penalty"], logprobs=p["logprobs"], seed=p["seed"])
+            frequency_penalty=p["frequency_penalty"], logprobs=p["logprobs"], seed=p["seed"],
+            stop=p["stop"], on_text=on_text)
 
     def _count(self, prompt_tokens: int, res: GenResult, seconds: float | None) -> None:
         s = self.stats
@@ -248,8 +246,8 @@ class BatchEngine:
     # ---------------------------------------------------------------- submission
     def fits_slot(self, prompt_ids, p: dict, on_text=None) -> bool:
         """A request runs in the slot table when it decodes greedily with no per-request
-        state the batched round lacks (penalties, logprobs, stop strings, callbacks) and its
-        prompt plus output fits one slot."""
+        state the batched round lacks (penalties, logprobs, stop strings, callbacks; those run
+        alone) and its prompt plus output fits one slot."""
         if self.engine.mode not in ("dspark", "baseline"):
             return False
         block = self.engine.drafter.block_size if self.engine.drafter is not None else 0
@@ -265,10 +263,6 @@ class BatchEngine:
         p = _params(max_tokens, temperature, top_p, top_k, presence_penalty, frequency_penalty,
                     logprobs, stop, seed)
         req = _Request(prompt_ids, p, on_text)
-        if stop or on_text is not None:
-            req.future.set_exception(NotImplementedError(
-                "stop strings and streaming callbacks are not built"))
-            return req.future
         with self._cv:
             if self._closed:
                 raise RuntimeError("BatchEngine is closed")
@@ -498,6 +492,9 @@ class ReplicaPool:
         self._collector.start()
 
     def submit(self, prompt_ids, **params) -> Future:
+        if params.get("on_text") is not None:
+            raise ValueError("on_text callbacks cannot be sent to replica processes; stream "
+                             "from an in-process Engine or BatchEngine")
         cost = len(prompt_ids) + int(params.get("max_tokens", 0))
         fut: Future = Future()
         with self._lock:

@@ -32,6 +32,7 @@ from . import ops
 from .kvcache import CacheState, RowView
 from .logprobs import LogprobRows
 from .model import Sampling
+from .streaming import StopStreaming, TextStream
 from .target import PREFILL_CHUNK
 
 
@@ -73,12 +74,6 @@ def eos_token_ids(tokenizer) -> set[int]:
     if isinstance(e1, int):
         ids.add(e1)
     return ids
-
-
-class StopStreaming(Exception):
-    """The name the reference's streaming callbacks raise to end a generation early
-    (generate.py:231-235). Streaming callbacks (on_text) are refused here, so no loop raises
-    or catches it; it exists so reference callers that import it keep working."""
 
 
 def _flat_ids(r) -> list[int] | None:
@@ -150,8 +145,10 @@ def _decode(tokenizer, ids):
     return tokenizer.decode(ids)
 
 
-def _finish_reason(out_ids, max_new_tokens, last_tok, eos_ids) -> str:
-    if last_tok in eos_ids:
+def _finish_reason(out_ids, max_new_tokens, last_tok, eos_ids, stopped: bool = False) -> str:
+    """'stop' when eos or a stop string (or the streaming callback) ended the decode, else
+    'length' at the token cap (generate.py:365-370)."""
+    if stopped or last_tok in eos_ids:
         return "stop"
     return "length" if len(out_ids) >= max_new_tokens else "stop"
 
@@ -479,11 +476,14 @@ def _caller_states(drafter, cache, ctx_caches, reuse_len: int, tokens: int):
 def _spec_loop(target, tokenizer, drafter, ids, cap, max_new_tokens, sampling, seed, use_graph,
                draft_override, verbose, penalties=(0.0, 0.0), lookup_max_draft=0, cache=None,
                ctx_caches=None, reuse_len: int = 0, cap_controller=None,
-               logprobs: int | None = None, confidence_threshold: float = 0.0) -> GenResult:
+               logprobs: int | None = None, confidence_threshold: float = 0.0, stop=None,
+               on_text=None) -> GenResult:
     """The decode loop of speculative_generate / dflash_generate. `cap` is the ceiling; with a
     cap_controller each drafter round uses min(controller.cap, cap) and feeds the outcome back
-    (generate.py:846-847,924-925); lookup rounds neither use nor update it."""
+    (generate.py:846-847,924-925); lookup rounds neither use nor update it. Text streams to
+    on_text and stop strings end the decode at a round boundary (TextStream)."""
     eos_ids = eos_token_ids(tokenizer)
+    st = TextStream(tokenizer, eos_ids, on_text, stop)
     budget = len(ids) + max_new_tokens + cap + 1
     sampling = sampling if (sampling is not None and sampling.active) else None
     states = None
@@ -525,9 +525,10 @@ def _spec_loop(target, tokenizer, drafter, ids, cap, max_new_tokens, sampling, s
         torch.cuda.synchronize()
         t1 = time.time()
         out = [pending]
+        st.update(out)
         accept = []
         rounds = lookup_rounds = 0
-        while len(out) < max_new_tokens and pending not in eos_ids:
+        while len(out) < max_new_tokens and pending not in eos_ids and not st.stopped:
             lk = index.propose() if index is not None else []
             if lk:
                 lookup_rounds += 1
@@ -559,17 +560,20 @@ def _spec_loop(target, tokenizer, drafter, ids, cap, max_new_tokens, sampling, s
             if index is not None:
                 index.extend(appended)
             pending = out[-1]
+            st.update(out)
             rounds += 1
             if verbose:
                 src = "lookup" if lk else "drafter"
                 print(f"  round {rounds:3d}: {src} drafted {len(lk) if lk else drafted}, accepted {n}, "
                       f"committed {len(committed)}")
+        st.flush()
         t2 = time.time()
-        text = _decode(tokenizer, [t for t in out if t not in eos_ids])
+        text = st.final_text(tokenizer, out, _decode)
         return GenResult(text=text, token_ids=out, num_tokens=len(out), num_rounds=len(accept),
                          accept_lengths=accept, target_forwards=len(accept) + 1,
                          seconds=t2 - t0, decode_seconds=t2 - t1, lookup_rounds=lookup_rounds,
-                         finish_reason=_finish_reason(out, max_new_tokens, pending, eos_ids),
+                         finish_reason=_finish_reason(out, max_new_tokens, pending, eos_ids,
+                                                      st.stopped),
                          logprobs=lp_list)
     finally:
         sess.release()
@@ -607,7 +611,8 @@ def speculative_generate(target, tokenizer, drafter, prompt: str = "", *,
                       Sampling(temperature, top_p, top_k), seed, use_graph, draft_override,
                       verbose, (presence_penalty, frequency_penalty),
                       max(1, int(lookup_max_draft)) if lookup_drafts else 0, cache, ctx_caches,
-                      reuse_len, cap_controller, logprobs, float(confidence_threshold))
+                      reuse_len, cap_controller, logprobs, float(confidence_threshold), stop,
+                      on_text)
 
 
 def dflash_generate(target_model, tokenizer, drafter, prompt: str = "", *,
@@ -626,7 +631,7 @@ def dflash_generate(target_model, tokenizer, drafter, prompt: str = "", *,
         prompt_ids = encode_prompt(tokenizer, prompt, apply_chat_template)
     return _spec_loop(target_model, tokenizer, drafter, list(prompt_ids), cap, max_new_tokens,
                       Sampling(temperature, top_p, top_k), seed, use_graph, None, verbose,
-                      cap_controller=cap_controller)
+                      cap_controller=cap_controller, stop=stop, on_text=on_text)
 
 
 class GreedySession:
@@ -719,6 +724,7 @@ def greedy_generate(target, tokenizer, prompt: str = "", *, prompt_ids: list[int
     """Plain decoding of the target (the baseline the speedup is measured against): greedy, or
     sampled with temperature / top-p / top-k from a Philox stream seeded by `seed`."""
     eos_ids = eos_token_ids(tokenizer)
+    st = TextStream(tokenizer, eos_ids, on_text, stop)
     if prompt_ids is None:
         prompt_ids = encode_prompt(tokenizer, prompt, apply_chat_template)
     ids = list(prompt_ids)
@@ -743,7 +749,8 @@ def greedy_generate(target, tokenizer, prompt: str = "", *, prompt_ids: list[int
             lp_list = sess.lp.entries([nxt])
         t1 = time.time()
         out = [nxt]
-        while len(out) < max_new_tokens and nxt not in eos_ids:
+        st.update(out)
+        while len(out) < max_new_tokens and nxt not in eos_ids and not st.stopped:
             plan = sess.step(use_graph)[0]
             if use_graph and sess.graph is None:
                 sess.capture()
@@ -751,12 +758,15 @@ def greedy_generate(target, tokenizer, prompt: str = "", *, prompt_ids: list[int
             out.append(nxt)
             if lp_list is not None:
                 lp_list.extend(sess.lp.entries([nxt]))
+            st.update(out)
+        st.flush()
         t2 = time.time()
-        text = _decode(tokenizer, [t for t in out if t not in eos_ids])
+        text = st.final_text(tokenizer, out, _decode)
         return GenResult(text=text, token_ids=out, num_tokens=len(out), num_rounds=len(out),
                          accept_lengths=[1] * len(out), target_forwards=len(out),
                          seconds=t2 - t0, decode_seconds=t2 - t1,
-                         finish_reason=_finish_reason(out, max_new_tokens, nxt, eos_ids),
+                         finish_reason=_finish_reason(out, max_new_tokens, nxt, eos_ids,
+                                                      st.stopped),
                          logprobs=lp_list)
     finally:
         sess.release()

@@ -21,6 +21,7 @@ from .generate import (GenResult, _decode, _finish_reason, _pick_first, eos_toke
                        prefill_rows)
 from .kvcache import CacheState
 from .model import Sampling
+from .streaming import TextStream
 
 
 class NGramIndex:
@@ -138,6 +139,7 @@ def lookup_generate(target_model, tokenizer, prompt: str = "", *,
                     stop: list[str] | None = None, on_text=None) -> GenResult:
     """Prompt-lookup speculative decoding, batch 1, no drafter model (lookup.py:92-202)."""
     eos_ids = eos_token_ids(tokenizer)
+    st = TextStream(tokenizer, eos_ids, on_text, stop)
     if prompt_ids is None:
         prompt_ids = list(tokenizer.encode(prompt))
     ids = list(prompt_ids)
@@ -156,8 +158,9 @@ def lookup_generate(target_model, tokenizer, prompt: str = "", *,
         pending = _pick_first(t, last, ver.sampling, rng)
         out = [pending]
         index.extend([pending])
+        st.update(out)
         accept = []
-        while len(out) < max_new_tokens and pending not in eos_ids:
+        while len(out) < max_new_tokens and pending not in eos_ids and not st.stopped:
             draft = index.propose()
             plan = ver.run(pending, draft)
             n = plan[0]
@@ -171,11 +174,14 @@ def lookup_generate(target_model, tokenizer, prompt: str = "", *,
                     break
             index.extend(appended)
             pending = out[-1]
+            st.update(out)
+        st.flush()
         secs = time.time() - t0
-        return GenResult(text=_decode(tokenizer, [x for x in out if x not in eos_ids]),
+        return GenResult(text=st.final_text(tokenizer, out, _decode),
                          token_ids=out, num_tokens=len(out), num_rounds=len(accept),
                          accept_lengths=accept, target_forwards=len(accept) + 1, seconds=secs,
-                         finish_reason=_finish_reason(out, max_new_tokens, pending, eos_ids))
+                         finish_reason=_finish_reason(out, max_new_tokens, pending, eos_ids,
+                                                      st.stopped))
     finally:
         tstate.release()
 

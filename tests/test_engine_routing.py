@@ -33,9 +33,11 @@ class _StubEngine:
         self.stats = {"requests": 0, "prompt_tokens": 0, "completion_tokens": 0,
                       "generation_seconds": 0.0, "sum_accept_len": 0.0}
         self.solo = []
+        self.on_text = []
 
     def run_request(self, prompt_ids, p, on_text=None):
         self.solo.append(prompt_ids[0])
+        self.on_text.append(on_text)
         return _res(prompt_ids)
 
     def _count(self, *a):
@@ -111,6 +113,8 @@ def test_classification():
     assert not be.fits_slot([1] * 10, eng_mod._params(16, 0.0, presence_penalty=0.5))
     assert not be.fits_slot([1] * 10, eng_mod._params(16, 0.0, logprobs=2))
     assert not be.fits_slot([1] * 5000, ok)                                       # too long
+    assert not be.fits_slot([1] * 10, eng_mod._params(16, 0.0, stop=["\n"]))     # stop strings
+    assert not be.fits_slot([1] * 10, ok, on_text=print)                         # streaming
     e.mode = "lookup"
     assert not be.fits_slot([1] * 10, ok)
 
@@ -125,8 +129,9 @@ def test_loop_batches_greedy_and_runs_solo_requests(batch_engine):
     assert sorted(tables[0].admitted) == [0, 1, 2, 3, 4] and sorted(e.solo) == [9, 10]
     st = be.metrics()["batching"]
     assert st["slot_requests"] == 5 and st["solo_requests"] == 2 and st["max_active"] == 2
-    with pytest.raises(NotImplementedError):
-        be.generate([1], max_tokens=4, temperature=0.0, stop=["x"])
+    # stop strings and streaming callbacks run alone, with the callback handed to the engine
+    r = be.generate([11], max_tokens=4, temperature=0.0, stop=["x"], on_text=print)
+    assert r.token_ids == [11] and e.solo[-1] == 11 and e.on_text[-1] is print
 
 
 def test_failed_round_fails_only_its_rows(batch_engine):
@@ -175,3 +180,10 @@ def test_replica_pool_least_loaded_dispatch():
     finally:
         pool.close()
     assert set(pool.replica_metrics) == {0, 1}
+
+
+def test_replica_pool_refuses_callbacks():
+    """Callbacks cannot be sent to worker processes; stop strings can."""
+    pool = eng_mod.ReplicaPool.__new__(eng_mod.ReplicaPool)
+    with pytest.raises(ValueError, match="on_text"):
+        pool.submit([1], max_tokens=4, temperature=0.0, on_text=print)
