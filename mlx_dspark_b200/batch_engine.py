@@ -30,6 +30,7 @@ from .generate import (GenResult, GreedySession, SpecSession, _decode, eos_token
                        prefill_rows)
 from .kvcache import PAGE, CacheState, RowView
 from .prefix_cache import PrefixBlocks
+from .streaming import TextStream
 
 
 def batchable(target) -> bool:
@@ -38,21 +39,25 @@ def batchable(target) -> bool:
 
 
 class _RowTracker:
-    """One row's committed tokens, eos / length stop and result (batch_engine.py:254-319)."""
+    """One row's committed tokens, its text stream (on_text, stop strings), its eos / length /
+    stop-string end and its result (batch_engine.py:254-319)."""
 
-    def __init__(self, tokenizer, first: int, max_new_tokens: int):
+    def __init__(self, tokenizer, first: int, max_new_tokens: int, on_text=None, stop=None):
         self.tok = tokenizer
         self.eos = eos_token_ids(tokenizer)
         self.mnt = int(max_new_tokens)
+        self.stream = TextStream(tokenizer, self.eos, on_text, stop)
         self.out_ids = [int(first)]
         self.accept_lengths: list[int] = []
         self.finished = False
+        self.stream.update(self.out_ids)
         self._check()
 
     def _check(self):
         ids = self.out_ids
-        if ids[-1] in self.eos or len(ids) >= self.mnt:
+        if ids[-1] in self.eos or len(ids) >= self.mnt or self.stream.stopped:
             self.finished = True
+            self.stream.flush()   # the rest of the text goes out as the row finishes
 
     def commit(self, tokens, accept_len=None):
         if self.finished:
@@ -63,14 +68,15 @@ class _RowTracker:
             self.out_ids.append(int(t))
             if t in self.eos:
                 break
+        self.stream.update(self.out_ids)
         self._check()
 
     def result(self, secs: float) -> GenResult:
         ids = self.out_ids
-        reason = "stop" if ids[-1] in self.eos else "length"
+        reason = "stop" if (ids[-1] in self.eos or self.stream.stopped) else "length"
         spec = bool(self.accept_lengths)
         al = self.accept_lengths if spec else [1] * len(ids)
-        return GenResult(text=_decode(self.tok, [t for t in ids if t not in self.eos]),
+        return GenResult(text=self.stream.final_text(self.tok, ids, _decode),
                          token_ids=ids, num_tokens=len(ids), num_rounds=len(al),
                          accept_lengths=al, target_forwards=(len(al) + 1) if spec else len(ids),
                          seconds=secs, finish_reason=reason)
@@ -136,8 +142,6 @@ class SpecSlots:
         """Prefill one request into the next free slot (reusing a stored prefix's pages)."""
         if not self.has_free_slot:
             raise RuntimeError("SpecSlots.admit: no free slot")
-        if on_text is not None or stop:
-            raise NotImplementedError("streaming callbacks and stop strings are not built")
         ids = list(prompt_ids)
         need = len(ids) + int(max_new_tokens) + self.cap + self.k + 2
         if need > self.max_tokens:
@@ -156,7 +160,7 @@ class SpecSlots:
         if self.blocks is not None:
             self.blocks.store_row(b, ids)
         self.pending[b] = first
-        self.trk[b] = _RowTracker(self.tokenizer, first, max_new_tokens)
+        self.trk[b] = _RowTracker(self.tokenizer, first, max_new_tokens, on_text, stop)
         self.meta[b] = meta
         self.t0[b] = time.time()
         self.n_active += 1
@@ -236,8 +240,10 @@ def batch_spec_generate(target, tokenizer, drafter, prompts_ids: list[list[int]]
     slots = SpecSlots(target, tokenizer, drafter, capacity=B, max_draft_tokens=max_draft_tokens,
                       batched_drafter=batched_drafter, max_tokens=mt, prefix_reuse=prefix_reuse)
     try:
+        ot = list(on_texts) if on_texts is not None else [None] * B
+        sp = list(stops) if stops is not None else [None] * B
         for i, ids in enumerate(prompts_ids):
-            slots.admit(ids, max_new_tokens=mnt[i], meta=i)
+            slots.admit(ids, max_new_tokens=mnt[i], on_text=ot[i], stop=sp[i], meta=i)
         results: list[GenResult | None] = [None] * B
         while slots.n_active:
             for meta, res in slots.step():
@@ -265,7 +271,9 @@ def batch_generate_baseline(target, tokenizer, prompts_ids: list[list[int]], *,
             last = prefill_rows(target, list(ids), RowView(sess.tstate, b), ())
             first.append(int(last.float().argmax()))
         sess.buf.ids.copy_(torch.tensor(first, dtype=torch.int32))
-        trk = [_RowTracker(tokenizer, first[b], mnt[b]) for b in range(B)]
+        ot = list(on_texts) if on_texts is not None else [None] * B
+        sp = list(stops) if stops is not None else [None] * B
+        trk = [_RowTracker(tokenizer, first[b], mnt[b], ot[b], sp[b]) for b in range(B)]
         while not all(t.finished for t in trk):
             plans = sess.step(use_graph)
             if use_graph and sess.graph is None:

@@ -22,8 +22,8 @@ How work reaches the GPU is this build's own:
   * ReplicaPool runs one worker process per GPU, each with its own model replica and
     BatchEngine, and no collective between them. The host sends each request to the replica
     with the least outstanding work (prompt plus max new tokens of its unfinished requests).
-Requests with stop strings or an on_text streaming callback take the solo path (the slot
-table keeps no per-row text state). A ReplicaPool takes stop strings but not callbacks, which
+Stop strings and on_text streaming callbacks work in the slot table (each row keeps its own
+text stream) and on the solo path. A ReplicaPool takes stop strings but not callbacks, which
 cannot be sent to its worker processes.
 """
 from __future__ import annotations
@@ -246,15 +246,16 @@ class BatchEngine:
     # ---------------------------------------------------------------- submission
     def fits_slot(self, prompt_ids, p: dict, on_text=None) -> bool:
         """A request runs in the slot table when it decodes greedily with no per-request
-        state the batched round lacks (penalties, logprobs, stop strings, callbacks; those run
-        alone) and its prompt plus output fits one slot."""
+        state the batched round lacks (penalties, logprobs; those run alone) and its prompt
+        plus output fits one slot. Stop strings and streaming callbacks are per-row host state
+        of the table (server.py:488-500)."""
         if self.engine.mode not in ("dspark", "baseline"):
             return False
         block = self.engine.drafter.block_size if self.engine.drafter is not None else 0
         need = len(prompt_ids) + p["max_tokens"] + 2 * block + 2
         return (p["temperature"] == 0.0 and not p["presence_penalty"]
-                and not p["frequency_penalty"] and p["logprobs"] is None and not p["stop"]
-                and on_text is None and need <= self.slot_tokens)
+                and not p["frequency_penalty"] and p["logprobs"] is None
+                and need <= self.slot_tokens)
 
     def submit(self, prompt_ids, *, max_tokens: int, temperature: float, top_p: float = 1.0,
                top_k: int = 0, presence_penalty: float = 0.0, frequency_penalty: float = 0.0,
@@ -339,7 +340,8 @@ class BatchEngine:
 
     def _admit(self, r: _Request) -> None:
         try:
-            self._table().admit(r.prompt_ids, max_new_tokens=r.params["max_tokens"], meta=r)
+            self._table().admit(r.prompt_ids, max_new_tokens=r.params["max_tokens"],
+                                on_text=r.on_text, stop=r.params["stop"] or None, meta=r)
             self.batch_stats["slot_requests"] += 1
         except BaseException as e:  # noqa: BLE001 - one bad request must not stop the table
             r.future.set_exception(e)

@@ -65,9 +65,10 @@ class _FakeTable:
     def meta(self):
         return [r for r, _ in self.rows]
 
-    def admit(self, ids, *, max_new_tokens, meta):
+    def admit(self, ids, *, max_new_tokens, meta, on_text=None, stop=None):
         assert len(self.rows) < self.capacity
         self.admitted.append(ids[0])
+        self.text_args = (on_text, stop)
         self.rows.append([meta, self.rounds])
 
     def step(self):
@@ -113,8 +114,8 @@ def test_classification():
     assert not be.fits_slot([1] * 10, eng_mod._params(16, 0.0, presence_penalty=0.5))
     assert not be.fits_slot([1] * 10, eng_mod._params(16, 0.0, logprobs=2))
     assert not be.fits_slot([1] * 5000, ok)                                       # too long
-    assert not be.fits_slot([1] * 10, eng_mod._params(16, 0.0, stop=["\n"]))     # stop strings
-    assert not be.fits_slot([1] * 10, ok, on_text=print)                         # streaming
+    assert be.fits_slot([1] * 10, eng_mod._params(16, 0.0, stop=["\n"]))         # per-row text
+    assert be.fits_slot([1] * 10, ok, on_text=print)
     e.mode = "lookup"
     assert not be.fits_slot([1] * 10, ok)
 
@@ -129,9 +130,13 @@ def test_loop_batches_greedy_and_runs_solo_requests(batch_engine):
     assert sorted(tables[0].admitted) == [0, 1, 2, 3, 4] and sorted(e.solo) == [9, 10]
     st = be.metrics()["batching"]
     assert st["slot_requests"] == 5 and st["solo_requests"] == 2 and st["max_active"] == 2
-    # stop strings and streaming callbacks run alone, with the callback handed to the engine
+    # stop strings and streaming callbacks go to the table with the row
     r = be.generate([11], max_tokens=4, temperature=0.0, stop=["x"], on_text=print)
-    assert r.token_ids == [11] and e.solo[-1] == 11 and e.on_text[-1] is print
+    assert r.token_ids == [11] and tables[0].admitted[-1] == 11
+    assert tables[0].text_args == (print, ["x"])
+    # and to the engine with a solo request
+    r = be.generate([12], max_tokens=4, temperature=0.5, stop=["y"], on_text=print)
+    assert e.solo[-1] == 12 and e.on_text[-1] is print
 
 
 def test_failed_round_fails_only_its_rows(batch_engine):
@@ -187,3 +192,31 @@ def test_replica_pool_refuses_callbacks():
     pool = eng_mod.ReplicaPool.__new__(eng_mod.ReplicaPool)
     with pytest.raises(ValueError, match="on_text"):
         pool.submit([1], max_tokens=4, temperature=0.0, on_text=print)
+
+
+def test_row_tracker_text_stream():
+    """The slot table's per-row state: a stop string ends the row, its text is cut, the
+    callback gets exactly that text, and a row without one decodes every id (fake tokenizer,
+    no GPU)."""
+    from mlx_dspark_b200.batch_engine import _RowTracker
+
+    class Tok:
+        eos_token_id = 99
+
+        def decode(self, ids):
+            return "".join(chr(97 + i) for i in ids)
+
+    got = []
+    t = _RowTracker(Tok(), 0, 50, on_text=got.append, stop=["de"])
+    t.commit([1, 2], accept_len=3)
+    assert not t.finished
+    t.commit([3, 4, 5], accept_len=4)
+    assert t.finished
+    t.commit([6])                              # ignored once finished
+    r = t.result(0.0)
+    assert r.text == "abc" and "".join(got) == "abc" and r.finish_reason == "stop"
+    assert r.token_ids == [0, 1, 2, 3, 4, 5] and r.accept_lengths == [3, 4]
+    plain = _RowTracker(Tok(), 0, 4)
+    plain.commit([1, 99, 7])
+    r = plain.result(0.0)
+    assert r.text == "ab" and r.token_ids == [0, 1, 99] and r.finish_reason == "stop"
