@@ -26,8 +26,9 @@ from collections import deque
 
 import torch
 
-from .generate import (GenResult, GreedySession, SpecSession, _decode, eos_token_ids,
-                       prefill_rows)
+from .generate import (GenResult, GreedySession, SpecSession, _decode, _pick_first,
+                       eos_token_ids, prefill_rows)
+from .model import Sampling
 from .kvcache import PAGE, CacheState, RowView
 from .prefix_cache import PrefixBlocks
 from .streaming import TextStream
@@ -257,19 +258,21 @@ def batch_generate_baseline(target, tokenizer, prompts_ids: list[list[int]], *,
                             max_new_tokens=128, temperature: float = 0.0, top_p: float = 1.0,
                             top_k: int = 0, seed: int | None = None, use_graph: bool = True,
                             on_texts=None, stops=None) -> list[GenResult]:
-    """Batched plain greedy decode (batch_engine.py:322-362): per-row prefill, then one
-    batched target forward per token until every row is done."""
-    if temperature > 0.0:
-        raise NotImplementedError("the sampled batched baseline is not built")
+    """Batched plain decode (batch_engine.py:322-362): per-row prefill, then one batched target
+    forward per token until every row is done; greedy, or with temperature > 0 a draw from
+    top-p/top-k(softmax(logits / T)) per row, row b on its own Philox stream seeded with
+    seed + b (seed 0 when None)."""
     B = len(prompts_ids)
     mnt = list(max_new_tokens) if isinstance(max_new_tokens, (list, tuple)) else [max_new_tokens] * B
-    sess = GreedySession(target, B, max(len(p) for p in prompts_ids) + max(mnt) + 2)
+    base_seed = 0 if seed is None else int(seed)
+    sess = GreedySession(target, B, max(len(p) for p in prompts_ids) + max(mnt) + 2,
+                         Sampling(temperature, top_p, top_k), [base_seed + b for b in range(B)])
     try:
         t0 = time.time()
         first = []
         for b, ids in enumerate(prompts_ids):
             last = prefill_rows(target, list(ids), RowView(sess.tstate, b), ())
-            first.append(int(last.float().argmax()))
+            first.append(_pick_first(target, last, sess.sampling, sess.rng[b:b + 1]))
         sess.buf.ids.copy_(torch.tensor(first, dtype=torch.int32))
         ot = list(on_texts) if on_texts is not None else [None] * B
         sp = list(stops) if stops is not None else [None] * B
