@@ -47,7 +47,8 @@ def _gemv_lib():
 def linear_kind() -> str:
     """How the timed decode computes its W8 linears (for the baseline's sample description)."""
     if _gemv_lib() is not None:
-        return "int8 weights read once per step by the threaded C group-64 GEMV of oracle/cpu_gemv.c"
+        return ("int8 weights read once per step by the threaded AVX2 C group-64 GEMV of "
+                "oracle/cpu_gemv.c; the small ops between products in torch on one thread")
     return "int8 weights dequantized per step in torch (oracle/cpu_gemv.c not built)"
 
 
@@ -57,7 +58,11 @@ class StreamingDecoder:
     def __init__(self, w, max_ctx: int, threads: int | None = None, chunk_rows: int = 2048):
         self.w, self.cfg = w, w.cfg
         self.threads = threads or os.cpu_count() or 1
-        torch.set_num_threads(self.threads)
+        # the C GEMV runs its own pool of self.threads threads, which spin between the
+        # products; torch's thread pool beside it would fight them for the cores during the
+        # small ops in between (on an 8-core host, 2.6 tok/s with one torch thread against
+        # 1.0 with eight), so torch gets one thread when the C GEMV is there
+        torch.set_num_threads(1 if _gemv_lib() is not None else self.threads)
         c = self.cfg
         self.freqs = inv_freq(c.head_dim, c.rope_theta)
         self.chunk = chunk_rows
@@ -112,10 +117,12 @@ class StreamingDecoder:
             k = rope(rms_norm(k, L.k_norm, c.rms_norm_eps), p, self.freqs)
             self.K[i, :, pos] = k[:, 0]
             self.V[i, :, pos] = v[:, 0]
+            # GQA as a batched product per kv head: query heads j*rep .. j*rep+rep-1 read kv
+            # head j (no repeated copy of the context)
             rep = c.num_attention_heads // c.num_key_value_heads
-            Kc = self.K[i, :, :pos + 1].repeat_interleave(rep, 0)
-            Vc = self.V[i, :, :pos + 1].repeat_interleave(rep, 0)
-            s = (q @ Kc.transpose(1, 2)) * c.head_dim ** -0.5
+            qg = q.reshape(c.num_key_value_heads, rep, c.head_dim)
+            Kc, Vc = self.K[i, :, :pos + 1], self.V[i, :, :pos + 1]
+            s = (qg @ Kc.transpose(1, 2)) * c.head_dim ** -0.5
             a = bf(torch.softmax(s, -1) @ Vc).reshape(-1)
             h = bf(h + self._lin(a, L.wo))
             x = rms_norm(h, L.post_ln, c.rms_norm_eps)
@@ -130,14 +137,18 @@ class StreamingDecoder:
 def time_greedy_decode(w, context: int, budget_s: float = 20.0, min_steps: int = 1,
                        max_steps: int = 64, threads: int | None = None):
     """Decode until the time budget is spent; returns (tokens_per_s, steps, seconds, threads)."""
-    dec = StreamingDecoder(w, context + max_steps + 1, threads)
-    dec.fill_random_context(context)
-    tok = 1
-    tok = dec.step(tok)  # untimed warm-up (allocator, thread pool)
-    t0 = time.perf_counter()
-    n = 0
-    while n < max_steps and (n < min_steps or time.perf_counter() - t0 < budget_s):
-        tok = dec.step(tok)
-        n += 1
-    dt = time.perf_counter() - t0
-    return n / dt, n, dt, dec.threads
+    prev_threads = torch.get_num_threads()
+    try:
+        dec = StreamingDecoder(w, context + max_steps + 1, threads)
+        dec.fill_random_context(context)
+        tok = 1
+        tok = dec.step(tok)  # untimed warm-up (allocator, thread pool)
+        t0 = time.perf_counter()
+        n = 0
+        while n < max_steps and (n < min_steps or time.perf_counter() - t0 < budget_s):
+            tok = dec.step(tok)
+            n += 1
+        dt = time.perf_counter() - t0
+        return n / dt, n, dt, dec.threads
+    finally:
+        torch.set_num_threads(prev_threads)
