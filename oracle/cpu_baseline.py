@@ -57,7 +57,9 @@ class StreamingDecoder:
 
     def __init__(self, w, max_ctx: int, threads: int | None = None, chunk_rows: int = 2048):
         self.w, self.cfg = w, w.cfg
-        self.threads = threads or os.cpu_count() or 1
+        # the cores this process may run on (an affinity mask can hold fewer than the host has)
+        usable = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else None
+        self.threads = threads or usable or os.cpu_count() or 1
         # the C GEMV runs its own pool of self.threads threads, which spin between the
         # products; torch's thread pool beside it would fight them for the cores during the
         # small ops in between (on an 8-core host, 2.6 tok/s with one torch thread against
